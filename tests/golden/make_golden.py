@@ -1,0 +1,225 @@
+"""Generate golden fixtures from the reference's own torch implementation.
+
+Run once in a container where the reference project is available:
+
+    python tests/golden/make_golden.py --reference /path/to/YANchor
+
+It extracts the pinned transformers wheel (``wheels/transformers-*.whl``, pure
+Python) to a scratch directory, puts it and the reference root first on
+``sys.path`` and calls:
+
+* ``torch_chunk_gated_delta_rule`` / ``torch_recurrent_gated_delta_rule`` /
+  ``l2norm`` / ``Qwen3_5RMSNormGated``
+  (transformers/models/qwen3_5/modeling_qwen3_5.py:175-353)
+* the gate expression of ``Qwen3_5GatedDeltaNet.forward`` (same file :500-502)
+* ``select_topk``, ``merge_topk``, ``exclusive_prefix_topk``,
+  ``indexed_gqa_torch`` and ``IndependentGQAMemory._decode`` with the torch
+  backend (modeling_yanchor.py:22-313)
+* ``counter_uniform`` and ``sample_top_k_top_p_counter``
+  (runtime/model/inference_kernels.py:24-88)
+
+on seeded inputs and writes the inputs and outputs as ``.npz`` files next to
+this script.  The GPU box never needs the reference: tests only read the
+``.npz`` files.
+"""
+from __future__ import annotations
+
+import argparse
+import math
+import os
+import sys
+import tempfile
+import zipfile
+from types import SimpleNamespace
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _import_reference(root):
+    wheel = [f for f in os.listdir(os.path.join(root, 'wheels')) if f.startswith('transformers') and f.endswith('.whl')][0]
+    scratch = tempfile.mkdtemp(prefix='yb_golden_whl_')
+    zipfile.ZipFile(os.path.join(root, 'wheels', wheel)).extractall(scratch)
+    sys.path[:0] = [scratch, root, os.path.join(root, 'runtime')]
+    import torch  # noqa: F401
+    from transformers.models.qwen3_5 import modeling_qwen3_5 as qwen
+    import modeling_yanchor as my
+    import model.inference_kernels as ik
+    return qwen, my, ik
+
+
+def gdn_fixtures(qwen, torch):
+    F = torch.nn.functional
+    out = {}
+    # --- config-0 style, T=160 (two full chunks + a partial one), fp32 ---------
+    g0 = torch.Generator().manual_seed(0)
+    B, T, H, D = 2, 160, 2, 64
+    q = torch.randn(B, T, H, D, generator=g0)
+    k = torch.randn(B, T, H, D, generator=g0)
+    v = torch.randn(B, T, H, D, generator=g0)
+    g = F.logsigmoid(torch.randn(B, T, H, generator=g0))
+    beta = torch.sigmoid(torch.randn(B, T, H, generator=g0))
+    h0 = 0.02 * torch.randn(B, H, D, D, generator=g0)
+    out.update(small_q=q, small_k=k, small_v=v, small_g=g, small_beta=beta, small_h0=h0)
+    o, s = qwen.torch_chunk_gated_delta_rule(q, k, v, g, beta, chunk_size=64, initial_state=h0,
+                                             output_final_state=True, use_qk_l2norm_in_kernel=True)
+    out.update(small_chunk_o=o, small_chunk_s=s)
+    o, s = qwen.torch_recurrent_gated_delta_rule(q, k, v, g, beta, initial_state=h0,
+                                                 output_final_state=True, use_qk_l2norm_in_kernel=True)
+    out.update(small_rec_o=o, small_rec_s=s)
+    # the exact config-0 recipe: pre-normalised q, k; zero initial state
+    qn, kn = qwen.l2norm(q), qwen.l2norm(k)
+    out.update(small_l2q_head=qn[:, :8])
+    o, s = qwen.torch_chunk_gated_delta_rule(qn, kn, v, g, beta, chunk_size=64, initial_state=None,
+                                             output_final_state=True)
+    out.update(small_chunk0_o=o, small_chunk0_s=s)
+    # --- grouped value heads (H=2, HV=4) and varlen packing ------------------
+    g1 = torch.Generator().manual_seed(1)
+    cu = [0, 37, 100, 165]
+    Tt, Hk, HV, Dk = cu[-1], 2, 4, 32
+    q = torch.randn(1, Tt, Hk, Dk, generator=g1)
+    k = torch.randn(1, Tt, Hk, Dk, generator=g1)
+    v = torch.randn(1, Tt, HV, Dk, generator=g1)
+    g = F.logsigmoid(torch.randn(1, Tt, HV, generator=g1))
+    beta = torch.sigmoid(torch.randn(1, Tt, HV, generator=g1))
+    h0 = 0.02 * torch.randn(len(cu) - 1, HV, Dk, Dk, generator=g1)
+    out.update(var_q=q, var_k=k, var_v=v, var_g=g, var_beta=beta, var_h0=h0, var_cu=torch.tensor(cu))
+    for name, fn in (('chunk', qwen.torch_chunk_gated_delta_rule), ('rec', qwen.torch_recurrent_gated_delta_rule)):
+        os_, ss = [], []
+        for n in range(len(cu) - 1):
+            sl = slice(cu[n], cu[n + 1])
+            qq = q[:, sl].repeat_interleave(HV // Hk, dim=2)
+            kk = k[:, sl].repeat_interleave(HV // Hk, dim=2)
+            kw = dict(initial_state=h0[n:n + 1], output_final_state=True, use_qk_l2norm_in_kernel=True)
+            if name == 'chunk':
+                kw['chunk_size'] = 64
+            o, s = fn(qq, kk, v[:, sl], g[:, sl], beta[:, sl], **kw)
+            os_.append(o)
+            ss.append(s)
+        out[f'var_{name}_o'] = torch.cat(os_, 1)
+        out[f'var_{name}_s'] = torch.cat(ss, 0)
+    # --- gates and the gated RMSNorm epilogue --------------------------------
+    g2 = torch.Generator().manual_seed(2)
+    a = 3.0 * torch.randn(5, 3, 8, generator=g2)
+    a[0, 0, :4] = torch.tensor([25.0, 21.0, 19.0, -30.0])     # both softplus branches
+    b = torch.randn(5, 3, 8, generator=g2)
+    A_log = torch.empty(8).uniform_(0, 16, generator=g2).log()
+    dt_bias = torch.randn(8, generator=g2)
+    beta_ref = b.sigmoid()
+    g_ref = -A_log.float().exp() * F.softplus(a.float() + dt_bias)     # modeling_qwen3_5.py:500-502
+    out.update(gate_a=a, gate_b=b, gate_A_log=A_log, gate_dt_bias=dt_bias, gate_g=g_ref, gate_beta=beta_ref)
+    norm = qwen.Qwen3_5RMSNormGated(64, eps=1e-6)
+    with torch.no_grad():
+        norm.weight.copy_(1.0 + 0.1 * torch.randn(64, generator=g2))
+    x = torch.randn(12, 64, generator=g2)
+    z = torch.randn(12, 64, generator=g2)
+    with torch.no_grad():
+        out.update(norm_x=x, norm_z=z, norm_w=norm.weight.detach().clone(), norm_out=norm(x, z))
+    return out
+
+
+def memory_fixtures(my, torch):
+    out = {}
+    g = torch.Generator().manual_seed(3)
+    # --- select_topk / merge_topk with ties, -0.0 and invalid references ------
+    n, cap = 24, 10
+    scores = torch.randint(-3, 4, (4, 3, n), generator=g).float() * 0.5
+    scores[0, 0, :3] = torch.tensor([0.0, -0.0, 0.0])
+    positions = torch.stack([torch.randperm(100, generator=g)[:n] for _ in range(12)]).reshape(4, 3, n)
+    refs = torch.arange(n).expand(4, 3, n).clone()
+    refs[torch.rand(4, 3, n, generator=g) < 0.25] = -1
+    scores = scores.masked_fill(refs < 0, -math.inf)
+    sel = my.select_topk(scores, positions, refs, cap)
+    out.update(sel_scores_in=scores, sel_pos_in=positions, sel_refs_in=refs,
+               sel_scores=sel[0], sel_pos=sel[1], sel_refs=sel[2])
+    sel = my.select_topk(scores, positions, refs, n + 4)      # capacity above n pads
+    out.update(selpad_scores=sel[0], selpad_pos=sel[1], selpad_refs=sel[2])
+    # --- exclusive prefix top-k over blocks ----------------------------------
+    B, blocks, G, chunk, cap = 2, 5, 2, 8, 6
+    ps = torch.randn(B, blocks, G, chunk, generator=g)
+    pp = torch.arange(blocks * chunk).reshape(1, blocks, 1, chunk).expand(B, blocks, G, chunk).clone()
+    pr = pp.clone()
+    pr[:, -1, :, 5:] = -1
+    ps = ps.masked_fill(pr < 0, -math.inf)
+    pre = my.exclusive_prefix_topk(ps, pp, pr, cap)
+    out.update(pre_scores_in=ps, pre_pos_in=pp, pre_refs_in=pr,
+               pre_scores=pre[0], pre_pos=pre[1], pre_refs=pre[2])
+    # --- indexed_gqa_torch (prefill read) ------------------------------------
+    B, blocks, chunk, H, G, D, S, cap = 2, 3, 8, 4, 2, 32, 20, 6
+    q = torch.randn(B, blocks, chunk, H, D, generator=g)
+    kk = torch.randn(B, S, G, D, generator=g)
+    vv = torch.randn(B, S, G, D, generator=g)
+    rr = torch.randint(0, S, (B, blocks, G, cap), generator=g)
+    rr[torch.rand(B, blocks, G, cap, generator=g) < 0.3] = -1
+    rr[0, 0, 0] = -1                                            # a group with no anchors
+    out.update(idx_q=q, idx_k=kk, idx_v=vv, idx_refs=rr, idx_out=my.indexed_gqa_torch(q, kk, vv, rr))
+    # --- decode read + commit, many steps, torch backend ----------------------
+    B, H, G, D, CAP, CHUNK, STEPS = 3, 4, 2, 32, 6, 8, 41
+    cfg = SimpleNamespace(backend='torch', hidden_size=16, num_attention_heads=H, num_key_value_heads=G,
+                          head_dim=D, rms_norm_eps=1e-6, initializer_range=0.02, fixed_memory_swa_window=64,
+                          independent_memory=dict(capacity=CAP, max_commit_chunk=CHUNK, admission_rank=4,
+                                                  writer_intermediate_size=8))
+    mem = my.IndependentGQAMemory(cfg)
+    state = my.IndependentMemoryState.empty(B, G, CAP, CHUNK, D, 'cpu', torch.float32)
+    qs = torch.randn(STEPS, B, 1, H, D, generator=g)
+    ks = torch.randn(STEPS, B, 1, G, D, generator=g)
+    vs = torch.randn(STEPS, B, 1, G, D, generator=g)
+    sc = torch.randint(-4, 5, (STEPS, B, 1, G), generator=g).float() * 0.25   # ties on purpose
+    valid = torch.rand(STEPS, B, 1, generator=g) > 0.15
+    reads = []
+    snapshots = {}
+    for t in range(STEPS):
+        with torch.no_grad():
+            r = mem._decode(qs[t], ks[t], vs[t], sc[t], valid[t], CHUNK, state)
+        reads.append(r)
+        if t in (7, 20):
+            for f in ('keys', 'values', 'scores', 'positions', 'pending_keys', 'pending_values',
+                      'pending_scores', 'count', 'total'):
+                snapshots[f'dec_t{t}_{f}'] = getattr(state, f).clone()
+    out.update(dec_q=qs, dec_k=ks, dec_v=vs, dec_scores=sc, dec_valid=valid, dec_reads=torch.stack(reads))
+    out.update(snapshots)
+    for f in ('keys', 'values', 'scores', 'positions', 'pending_keys', 'pending_values',
+              'pending_scores', 'count', 'total'):
+        out[f'dec_final_{f}'] = getattr(state, f).clone()
+    return out
+
+
+def sampling_fixtures(ik, torch):
+    out = {}
+    g = torch.Generator().manual_seed(4)
+    ids = torch.cat([torch.arange(64), torch.tensor([2**31 - 1, 2**32 - 1, 2**40 + 5, -1, -7])])
+    steps = torch.randint(0, 2**33, ids.shape, generator=g)
+    out.update(cu_ids=ids, cu_steps=steps)
+    for seed, stream in ((0, 0), (1234, 0), (2**32 + 99, 3)):
+        out[f'cu_u_{seed}_{stream}'] = ik.counter_uniform(ids, steps, seed=seed, stream=stream)
+    B, V = 16, 1000
+    scores = torch.randn(B, V, generator=g) * 3.0
+    attempt = torch.arange(B) * 7 + 3
+    step = torch.randint(0, 10000, (B,), generator=g)
+    out.update(samp_scores=scores, samp_attempt=attempt, samp_steps=step)
+    cases = [(1.0, 1, 1.0), (1.0, 20, 0.95), (0.7, 20, 0.9), (1.3, 50, 1.0), (1.0, 5, 0.3), (0.8, 0, 1.0)]
+    for i, (temp, tk, tp) in enumerate(cases):
+        out[f'samp_case{i}'] = torch.tensor([temp, tk, tp])
+        out[f'samp_out{i}'] = ik.sample_top_k_top_p_counter(scores, attempt, step, seed=77, temperature=temp,
+                                                             top_k=tk, top_p=tp)
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--reference', required=True)
+    args = ap.parse_args()
+    qwen, my, ik = _import_reference(os.path.abspath(args.reference))
+    import torch
+    torch.manual_seed(0)
+    for name, fn in (('gdn', lambda: gdn_fixtures(qwen, torch)), ('memory', lambda: memory_fixtures(my, torch)),
+                     ('sampling', lambda: sampling_fixtures(ik, torch))):
+        data = {k: (v.detach().cpu().numpy() if hasattr(v, 'detach') else np.asarray(v)) for k, v in fn().items()}
+        path = os.path.join(HERE, f'{name}.npz')
+        np.savez_compressed(path, **data)
+        print(path, sum(x.nbytes for x in data.values()), 'bytes raw')
+
+
+if __name__ == '__main__':
+    main()

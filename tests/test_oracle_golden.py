@@ -1,0 +1,153 @@
+"""Pin the numpy oracle to fixtures produced by the reference's own torch code
+(tests/golden/make_golden.py).  CPU only."""
+import numpy as np
+import pytest
+
+from oracle import gdn, memory, sampling
+
+
+def close(a, b, atol, rtol=0.0):
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    assert a.shape == b.shape, (a.shape, b.shape)
+    err = np.abs(a - b).max() if a.size else 0.0
+    assert np.allclose(a, b, atol=atol, rtol=rtol), f'max abs err {err}'
+
+
+# ---------------------------------------------------------------- GDN ------
+def test_l2norm(golden):
+    d = golden('gdn')
+    close(gdn.l2norm(d['small_q'])[:, :8], d['small_l2q_head'], 1e-6)
+
+
+@pytest.mark.parametrize('form', ['chunk', 'rec'])
+def test_gdn_small(golden, form):
+    d = golden('gdn')
+    fn = gdn.chunk_gated_delta_rule if form == 'chunk' else gdn.recurrent_gated_delta_rule
+    o, s = fn(d['small_q'], d['small_k'], d['small_v'], d['small_g'], d['small_beta'],
+              initial_state=d['small_h0'], use_qk_l2norm=True)
+    close(o, d[f'small_{form}_o'], 2e-5)
+    close(s, d[f'small_{form}_s'], 2e-5)
+
+
+def test_gdn_config0_recipe(golden):
+    """Config-0 recipe: q, k normalised up front, zero initial state."""
+    d = golden('gdn')
+    q, k = gdn.l2norm(d['small_q']), gdn.l2norm(d['small_k'])
+    o, s = gdn.chunk_gated_delta_rule(q, k, d['small_v'], d['small_g'], d['small_beta'])
+    close(o, d['small_chunk0_o'], 2e-5)
+    close(s, d['small_chunk0_s'], 2e-5)
+
+
+@pytest.mark.parametrize('form', ['chunk', 'rec'])
+def test_gdn_gva_varlen(golden, form):
+    d = golden('gdn')
+    fn = gdn.chunk_gated_delta_rule if form == 'chunk' else gdn.recurrent_gated_delta_rule
+    o, s = fn(d['var_q'], d['var_k'], d['var_v'], d['var_g'], d['var_beta'], initial_state=d['var_h0'],
+              use_qk_l2norm=True, cu_seqlens=d['var_cu'])
+    close(o, d[f'var_{form}_o'], 2e-5)
+    close(s, d[f'var_{form}_s'], 2e-5)
+
+
+def test_chunk_equals_recurrent_float64(golden):
+    d = golden('gdn')
+    args = (d['var_q'], d['var_k'], d['var_v'], d['var_g'], d['var_beta'])
+    kw = dict(initial_state=d['var_h0'], use_qk_l2norm=True, cu_seqlens=d['var_cu'], dtype=np.float64)
+    o1, s1 = gdn.chunk_gated_delta_rule(*args, **kw)
+    o2, s2 = gdn.recurrent_gated_delta_rule(*args, **kw)
+    close(o1, o2, 1e-10)
+    close(s1, s2, 1e-10)
+
+
+def test_transposed_state_layout(golden):
+    d = golden('gdn')
+    args = (d['var_q'], d['var_k'], d['var_v'], d['var_g'], d['var_beta'])
+    h0t = d['var_h0'].swapaxes(-1, -2)
+    o, s = gdn.recurrent_gated_delta_rule(*args, initial_state=h0t, use_qk_l2norm=True,
+                                          cu_seqlens=d['var_cu'], transpose_state=True)
+    close(o, d['var_rec_o'], 2e-5)
+    close(s.swapaxes(-1, -2), d['var_rec_s'], 2e-5)
+
+
+def test_gates(golden):
+    d = golden('gdn')
+    g, beta = gdn.gdn_gates(d['gate_a'], d['gate_b'], d['gate_A_log'], d['gate_dt_bias'])
+    close(g, d['gate_g'], 1e-5, 1e-6)
+    close(beta, d['gate_beta'], 1e-6)
+
+
+def test_rmsnorm_gated(golden):
+    d = golden('gdn')
+    close(gdn.rmsnorm_gated(d['norm_x'], d['norm_z'], d['norm_w']), d['norm_out'], 1e-5)
+
+
+# ------------------------------------------------------------- memory ------
+def test_select_topk(golden):
+    d = golden('memory')
+    s, p, r = memory.select_topk(d['sel_scores_in'], d['sel_pos_in'], d['sel_refs_in'], 10)
+    np.testing.assert_array_equal(s, d['sel_scores'])
+    np.testing.assert_array_equal(p, d['sel_pos'])
+    np.testing.assert_array_equal(r, d['sel_refs'])
+    s, p, r = memory.select_topk(d['sel_scores_in'], d['sel_pos_in'], d['sel_refs_in'], 28)
+    np.testing.assert_array_equal(s, d['selpad_scores'])
+    np.testing.assert_array_equal(p, d['selpad_pos'])
+    np.testing.assert_array_equal(r, d['selpad_refs'])
+
+
+def test_exclusive_prefix_topk(golden):
+    d = golden('memory')
+    s, p, r = memory.exclusive_prefix_topk(d['pre_scores_in'], d['pre_pos_in'], d['pre_refs_in'], 6)
+    np.testing.assert_array_equal(s, d['pre_scores'])
+    np.testing.assert_array_equal(p, d['pre_pos'])
+    np.testing.assert_array_equal(r, d['pre_refs'])
+
+
+def test_indexed_gqa(golden):
+    d = golden('memory')
+    out = memory.indexed_gqa(d['idx_q'], d['idx_k'], d['idx_v'], d['idx_refs'])
+    close(out, d['idx_out'], 2e-5)
+
+
+def _replay_decode(d, upto):
+    B, G, D = d['dec_k'].shape[1], d['dec_k'].shape[3], d['dec_k'].shape[4]
+    CAP = d['dec_final_keys'].shape[2]
+    PC = d['dec_final_pending_keys'].shape[2]
+    st = memory.empty_state(B, G, CAP, PC, D)
+    reads = []
+    for t in range(upto):
+        k0 = st['keys'].copy()
+        reads.append(memory.decode_read(d['dec_q'][t], st['keys'], st['values'], st['positions'])
+                     * d['dec_valid'][t][..., None, None])
+        memory.commit_decode(d['dec_k'][t], d['dec_v'][t], d['dec_scores'][t], d['dec_valid'][t][:, 0], 8, st)
+        del k0
+    return st, np.stack(reads)
+
+
+def test_decode_read_commit_sequence(golden):
+    d = golden('memory')
+    steps = d['dec_q'].shape[0]
+    for t in (7, 20):
+        st, _ = _replay_decode(d, t + 1)
+        for f in st:
+            np.testing.assert_allclose(st[f], d[f'dec_t{t}_{f}'], atol=0, err_msg=f)
+    st, reads = _replay_decode(d, steps)
+    close(reads, d['dec_reads'], 2e-5)
+    for f in st:
+        np.testing.assert_allclose(st[f], d[f'dec_final_{f}'], atol=0, err_msg=f)
+
+
+# ----------------------------------------------------------- sampling ------
+def test_counter_uniform(golden):
+    d = golden('sampling')
+    for seed, stream in ((0, 0), (1234, 0), (2**32 + 99, 3)):
+        u = sampling.counter_uniform(d['cu_ids'], d['cu_steps'], seed, stream)
+        np.testing.assert_array_equal(u, d[f'cu_u_{seed}_{stream}'])
+
+
+def test_sampler(golden):
+    d = golden('sampling')
+    for i in range(6):
+        temp, tk, tp = d[f'samp_case{i}']
+        got = sampling.sample_top_k_top_p_counter(d['samp_scores'], d['samp_attempt'], d['samp_steps'], 77,
+                                                  float(temp), int(tk), float(tp))
+        np.testing.assert_array_equal(got, d[f'samp_out{i}'], err_msg=f'case {i}')
