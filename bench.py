@@ -1,0 +1,441 @@
+"""Benchmark of the YANchor hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl yanchor_b200|reference]
+
+One step = one decode step of the hot path at the YANchor-4B shape for the
+batch on this GPU (weak scaling: every rank owns its own sequences):
+
+  * 24 GDN layers: fused recurrent update (q/k L2 norm, gates from raw a / b,
+    fp32 state 32 x 128 x 128 per sequence updated in place, gated RMSNorm
+    epilogue) — ``fused_recurrent_gated_delta_rule``
+  * 8 anchor-memory layers: decode read + commit (G=4, H=16, D=256,
+    CAP=64, chunk=64) — ``committed_gqa`` / ``commit_decode``
+  * greedy sampling over the 248,320-token vocabulary — ``greedy``
+
+``value`` is whole-job decode tokens/s (N x batch / step time) with inputs
+resident in HBM; the GDN state (3.2 GB per GPU at batch 64) is far larger than
+L2, so no L2 flush is needed between steps.  ``e2e`` repeats the step with
+the step's activations copied from pinned host memory before it and the
+sampled token ids copied back after it.  ``prefill`` reports config 1
+(chunked prefill B=8, T=8192, H=HV=32, K=V=128, plus the anchor read over 64
+slots) on rank 0.  ``--impl reference`` times the reference algorithm's CPU
+restatement (the numpy oracle) on the host cores instead.
+
+The step runs as a captured CUDA graph (the reference's decode loop replays a
+graph of the whole model forward too).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+METRIC = 'decode tok/s/GPU at B=64, 32K gen; chunked-prefill tok/s; % of roofline'
+
+# YANchor-4B hot-path shape (configuration_yanchor.py over Qwen3_5TextConfig
+# defaults: 32 layers, every 4th is SWA + anchor memory)
+L_GDN, L_MEM = 24, 8
+H_K, H_V, DK, DV = 16, 32, 128, 128
+MEM_G, MEM_H, MEM_D, MEM_CAP, MEM_CHUNK = 4, 16, 256, 64, 64
+VOCAB = 248320
+
+
+def peaks():
+    path = os.path.join(ROOT, 'MEASURED_PEAKS.json')
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p['hbm_gbs']), float(p['bf16_tflops']), float(p.get('bf16_tflops_sustained', p['bf16_tflops'])), \
+            'measured'
+    except Exception:  # noqa: BLE001
+        return 6650.0, 1590.0, 1400.0, 'fallback'
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', f'--id={self.index}', f'--query-gpu={self.FIELDS}',
+                                          '--format=csv,noheader,nounits', '-lms', '200'],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:  # noqa: BLE001
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:  # noqa: BLE001
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ('hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap')
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(',')]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == 'active':
+                    reasons.add(name)
+        if not sm:
+            return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['unsampled'], 'samples': 0}
+        return {'sm_mhz': statistics.median(sm), 'sm_max_mhz': max(mx), 'reasons': sorted(reasons),
+                'samples': len(sm)}
+
+
+# ----------------------------------------------------------------- GPU arm --
+def build_decode(torch, yb, B, device, n_inputs=4, seed=0):
+    """Allocate the model-shaped state and `n_inputs` sets of step inputs."""
+    gen = torch.Generator(device=device).manual_seed(seed)
+    bf = torch.bfloat16
+
+    def rnd(*shape, dtype=bf, scale=1.0):
+        return (torch.randn(*shape, generator=gen, device=device) * scale).to(dtype)
+
+    layers = []
+    for _ in range(L_GDN):
+        layers.append(dict(state=0.02 * torch.randn(B, H_V, DK, DV, generator=gen, device=device),
+                           A_log=torch.empty(H_V, device=device).uniform_(1, 16, generator=gen).log(),
+                           dt_bias=torch.ones(H_V, device=device),
+                           norm_w=rnd(DV, scale=0.1) + 1.0))
+    mems = [yb.MemoryState.empty(B, MEM_G, MEM_CAP, MEM_CHUNK, MEM_D, device, bf) for _ in range(L_MEM)]
+    inputs = []
+    for _ in range(n_inputs):
+        inputs.append(dict(
+            q=rnd(L_GDN, B, 1, H_K, DK), k=rnd(L_GDN, B, 1, H_K, DK), v=rnd(L_GDN, B, 1, H_V, DV),
+            z=rnd(L_GDN, B, 1, H_V, DV), a=rnd(L_GDN, B, 1, H_V), b=rnd(L_GDN, B, 1, H_V),
+            mq=rnd(L_MEM, B, 1, MEM_H, MEM_D), mk=rnd(L_MEM, B, 1, MEM_G, MEM_D), mv=rnd(L_MEM, B, 1, MEM_G, MEM_D),
+            ms=rnd(L_MEM, B, 1, MEM_G, dtype=torch.float32), logits=rnd(B, VOCAB, scale=3.0)))
+    active = torch.ones(B, dtype=torch.bool, device=device)
+    ws = torch.empty(yb.sampling.workspace_bytes(B, VOCAB, 1), dtype=torch.uint8, device=device)
+    return layers, mems, inputs, active, ws
+
+
+def decode_step(yb, layers, mems, x, active, ws):
+    """One decode step of the hot path; returns the sampled token ids."""
+    for i, L in enumerate(layers):
+        yb.fused_recurrent_gated_delta_rule(
+            x['q'][i], x['k'][i], x['v'][i], g=x['a'][i], beta=x['b'][i], initial_state=L['state'],
+            output_final_state=True, use_qk_l2norm_in_kernel=True, use_gate_in_kernel=True, A_log=L['A_log'],
+            dt_bias=L['dt_bias'], use_beta_sigmoid_in_kernel=True, z=x['z'][i], norm_weight=L['norm_w'],
+            inplace=True)
+    for i, st in enumerate(mems):
+        yb.committed_gqa(x['mq'][i], st)
+        yb.commit_decode(x['mk'][i], x['mv'][i], x['ms'][i], active, MEM_CHUNK, st)
+    return yb.greedy(x['logits'], workspace=ws)
+
+
+LAUNCHES_PER_STEP = L_GDN + 2 * L_MEM + 2
+
+
+def gdn_bytes_per_launch(B):
+    state = B * H_V * DK * DV * 4 * 2                      # fp32 state read + write
+    acts = B * (2 * H_K * DK + 3 * H_V * DV) * 2 + B * H_V * 2 * 2   # q, k, v, z, o (bf16) + a, b
+    return state + acts
+
+
+def time_events(torch, fn, iters, stream):
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(iters):
+        fn()
+    end.record(stream)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / iters
+
+
+def run_gpu(args, rank, world, local_rank, dist):
+    import torch
+    import yanchor_b200 as yb
+    device = torch.device('cuda', local_rank)
+    torch.cuda.set_device(device)
+    B = args.batch
+    layers, mems, inputs, active, ws = build_decode(torch, yb, B, device, seed=1234 + rank)
+    stream = torch.cuda.current_stream(device)
+
+    # eager warm-up (also loads the library and sets kernel attributes)
+    for w in range(max(args.warmup, 3)):
+        decode_step(yb, layers, mems, inputs[w % len(inputs)], active, ws)
+    torch.cuda.synchronize()
+    graphs, outs = [], []
+    for x in inputs:
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(device)
+        s.wait_stream(stream)
+        with torch.cuda.stream(s):
+            decode_step(yb, layers, mems, x, active, ws)   # pre-capture run on the side stream
+        stream.wait_stream(s)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g):
+            outs.append(decode_step(yb, layers, mems, x, active, ws))
+        graphs.append(g)
+    for w in range(args.warmup):
+        graphs[w % len(graphs)].replay()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # ---- device-resident timed region ----
+    barrier()
+    with ClockSampler(local_rank) as clocks:
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for i in range(args.steps):
+            graphs[i % len(graphs)].replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms = start.elapsed_time(end) / args.steps
+    if dist is not None:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * B / (ms / 1e3)
+
+    # ---- dominant kernel alone: GDN recurrent update, CUDA events on its stream ----
+    x0 = inputs[0]
+    L0 = layers[0]
+
+    def one_gdn():
+        yb.fused_recurrent_gated_delta_rule(
+            x0['q'][0], x0['k'][0], x0['v'][0], g=x0['a'][0], beta=x0['b'][0], initial_state=L0['state'],
+            output_final_state=True, use_qk_l2norm_in_kernel=True, use_gate_in_kernel=True, A_log=L0['A_log'],
+            dt_bias=L0['dt_bias'], use_beta_sigmoid_in_kernel=True, z=x0['z'][0], norm_weight=L0['norm_w'],
+            inplace=True)
+    gg = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gg):
+        for _ in range(L_GDN):
+            one_gdn()
+    gg.replay()
+    gdn_ms = time_events(torch, gg.replay, 5, stream) / L_GDN
+    hbm, tf_burst, tf_sust, peak_kind = peaks()
+    gbytes = gdn_bytes_per_launch(B)
+    achieved = gbytes / (gdn_ms / 1e3) / 1e9
+
+    # ---- end to end: pinned host inputs -> step -> token ids back to host ----
+    host_in = {k: v.cpu().pin_memory() for k, v in inputs[0].items()}
+    host_out = torch.empty((B, 1), dtype=torch.int64).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host_in.values())
+    d2h = host_out.numel() * host_out.element_size()
+
+    def e2e_step():
+        for k_, t in host_in.items():
+            inputs[0][k_].copy_(t, non_blocking=True)
+        graphs[0].replay()
+        host_out.copy_(outs[0], non_blocking=True)
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    e2e_ms = time_events(torch, e2e_step, max(3, args.steps // 2), stream)
+    if dist is not None:
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    result = {
+        'metric': METRIC, 'value': round(value, 1), 'unit': 'tok/s', 'n_gpus': world, 'steps': args.steps,
+        'warmup': args.warmup, 'ms_per_step': round(ms, 4), 'higher_is_better': True, 'scaling': 'weak',
+        'vs_baseline': None, 'dtype': 'fp32 state, bf16 activations', 'data': 'synthetic (random init, seeded)',
+        'config': {
+            'workload': 'decode hot path (config 3 shape): 24 GDN layers + 8 anchor-memory layers + greedy '
+                        'sampler, one token per sequence per step, CUDA-graph replay',
+            'batch_per_gpu': B, 'global_batch': B * world,
+            'gdn': {'layers': L_GDN, 'H': H_K, 'HV': H_V, 'K': DK, 'V': DV, 'state': 'fp32, in place'},
+            'memory': {'layers': L_MEM, 'G': MEM_G, 'H': MEM_H, 'D': MEM_D, 'CAP': MEM_CAP, 'chunk': MEM_CHUNK},
+            'vocab': VOCAB, 'parallelism': f'sequence-sharded x{world}, no collective',
+            'l2': 'no flush: 3.2 GB of GDN state per GPU streams through each step (> 126 MB L2)'},
+        'roofline': {'bound': 'hbm', 'kernel': 'gdn_recurrent_kernel', 'achieved': round(achieved, 1),
+                     'peak': hbm, 'unit': 'GB/s', 'frac': round(achieved / hbm, 4), 'peak_kind': peak_kind,
+                     'bytes_per_launch': gbytes, 'launch_ms': round(gdn_ms, 5), 'traffic': traffic_per_launch()},
+        'e2e': {'value': round(world * B / (e2e_ms / 1e3), 1), 'unit': 'tok/s', 'h2d_bytes_per_step': h2d,
+                'd2h_bytes_per_step': d2h, 'ms_per_step': round(e2e_ms, 4),
+                'how': 'pinned host activations + logits copied in, graph replay, token ids copied out, '
+                       'all on one stream, CUDA events'},
+        'gpu_launches': LAUNCHES_PER_STEP * args.steps,
+        'clocks': clocks.summary(),
+    }
+    return result, (layers, mems, inputs)
+
+
+def traffic_per_launch():
+    """DRAM bytes (read + write) of one gdn_recurrent_kernel launch from the
+    committed ncu summary, or None when no capture has been summarised."""
+    path = os.path.join(ROOT, 'profiles', 'gdn_recurrent_decode_b64.json')
+    try:
+        with open(path) as f:
+            return json.load(f).get('dram_bytes_per_launch')
+    except Exception:  # noqa: BLE001
+        return None
+
+
+def run_prefill(torch, yb, device, hbm, tf_burst, peak_kind):
+    """Config 1: chunked prefill B=8, T=8192, H=HV=32, K=V=128 (bf16 in, fp32
+    state), and the anchor read over 64 slots per head at the memory shape."""
+    gen = torch.Generator(device=device).manual_seed(7)
+    bf = torch.bfloat16
+    B, T, H, K = 8, 8192, 32, 128
+    q = torch.randn(B, T, H, K, generator=gen, device=device).to(bf)
+    k = torch.randn(B, T, H, K, generator=gen, device=device).to(bf)
+    v = torch.randn(B, T, H, K, generator=gen, device=device).to(bf)
+    g = torch.nn.functional.logsigmoid(torch.randn(B, T, H, generator=gen, device=device))
+    beta = torch.randn(B, T, H, generator=gen, device=device).sigmoid().to(bf)
+    h0 = 0.02 * torch.randn(B, H, K, K, generator=gen, device=device)
+
+    def chunk():
+        yb.chunk_gated_delta_rule(q, k, v, g, beta, initial_state=h0, output_final_state=True,
+                                  use_qk_l2norm_in_kernel=True)
+    for _ in range(2):
+        chunk()
+    stream = torch.cuda.current_stream(device)
+    ms = time_events(torch, chunk, 3, stream)
+    flops = B * T * H * (6 * K * K + 2 * 64 * (3 * K + 2 * K))
+    # anchor read: blocks of 64 tokens, 16 query heads over 4 groups, D=256, 64 anchors
+    blocks = T // 64
+    mq = torch.randn(B, blocks, 64, MEM_H, MEM_D, generator=gen, device=device).to(bf)
+    mk = torch.randn(1, 4096, MEM_G, MEM_D, generator=gen, device=device).to(bf)
+    mv = torch.randn(1, 4096, MEM_G, MEM_D, generator=gen, device=device).to(bf)
+    refs = torch.randint(0, 4096, (B, blocks, MEM_G, 64), generator=gen, device=device)
+    for _ in range(2):
+        yb.indexed_gqa(mq, mk, mv, refs)
+    mem_ms = time_events(torch, lambda: yb.indexed_gqa(mq, mk, mv, refs), 3, stream)
+    achieved = flops / (ms / 1e3) / 1e12
+    return {'workload': 'config 1: chunked prefill B=8 T=8192 H=HV=32 K=V=128 bf16, fp32 state; '
+                        'plus anchor read (indexed_gqa) over 64 slots, G=4 H=16 D=256',
+            'tok_s': round(B * T / (ms / 1e3), 1), 'gdn_ms': round(ms, 3), 'anchor_read_ms': round(mem_ms, 3),
+            'tok_s_with_anchor_read': round(B * T / ((ms + mem_ms) / 1e3), 1),
+            'roofline': {'bound': 'tensor', 'kernel': 'gdn chunk', 'achieved': round(achieved, 2), 'peak': tf_burst,
+                         'unit': 'TFLOP/s', 'frac': round(achieved / tf_burst, 4), 'peak_kind': peak_kind,
+                         'flops_per_launch': flops}}
+
+
+# ------------------------------------------------------------- CPU arm ------
+def cpu_decode_sample(steps=2, B=64, seed=0):
+    """Time the numpy restatement of the same decode step on the host."""
+    from oracle import gdn as ogdn, memory as omem, sampling as osamp
+    rng = np.random.default_rng(seed)
+    f32 = np.float32
+    states = [(0.02 * rng.standard_normal((B, H_V, DK, DV))).astype(f32) for _ in range(L_GDN)]
+    A_log = np.log(rng.uniform(1, 16, H_V)).astype(f32)
+    mem = [omem.empty_state(B, MEM_G, MEM_CAP, MEM_CHUNK, MEM_D) for _ in range(L_MEM)]
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        for i in range(L_GDN):
+            q = rng.standard_normal((B, 1, H_K, DK)).astype(f32)
+            k = rng.standard_normal((B, 1, H_K, DK)).astype(f32)
+            v = rng.standard_normal((B, 1, H_V, DV)).astype(f32)
+            a = rng.standard_normal((B, 1, H_V)).astype(f32)
+            b = rng.standard_normal((B, 1, H_V)).astype(f32)
+            z = rng.standard_normal((B, 1, H_V, DV)).astype(f32)
+            g, beta = ogdn.gdn_gates(a, b, A_log, np.ones(H_V, f32))
+            o, states[i] = ogdn.recurrent_gated_delta_rule(q, k, v, g, beta, initial_state=states[i],
+                                                           use_qk_l2norm=True)
+            ogdn.rmsnorm_gated(o, z, np.ones(DV, f32))
+        for st in mem:
+            mq = rng.standard_normal((B, 1, MEM_H, MEM_D)).astype(f32)
+            omem.decode_read(mq, st['keys'], st['values'], st['positions'])
+            omem.commit_decode(rng.standard_normal((B, 1, MEM_G, MEM_D)).astype(f32),
+                               rng.standard_normal((B, 1, MEM_G, MEM_D)).astype(f32),
+                               rng.standard_normal((B, 1, MEM_G)).astype(f32), np.ones(B, bool), MEM_CHUNK, st)
+        osamp.greedy(rng.standard_normal((B, VOCAB)).astype(f32))
+    dt = time.perf_counter() - t0
+    return B * steps / dt, dt
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=20)
+    ap.add_argument('--warmup', type=int, default=5)
+    ap.add_argument('--batch', type=int, default=64)
+    ap.add_argument('--impl', default='yanchor_b200', choices=['yanchor_b200', 'reference'])
+    ap.add_argument('--no-prefill', action='store_true')
+    ap.add_argument('--no-cpu', action='store_true')
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local_rank = int(os.environ.get('LOCAL_RANK', '0'))
+    sys.path.insert(0, ROOT)
+
+    if args.impl == 'reference':
+        if rank != 0:
+            return
+        cores = 1
+        steps = max(1, min(args.steps, 3))
+        value, dt = cpu_decode_sample(steps=steps, B=args.batch)
+        line = {'metric': METRIC, 'value': round(value, 3), 'unit': 'tok/s', 'n_gpus': args.gpus, 'steps': steps,
+                'warmup': 0, 'ms_per_step': round(dt / steps * 1e3, 1), 'higher_is_better': True,
+                'scaling': 'weak', 'vs_baseline': None, 'dtype': 'fp32', 'data': 'synthetic (random init, seeded)',
+                'impl': 'reference',
+                'config': {'workload': 'decode hot path (config 3 shape): 24 GDN layers + 8 anchor-memory layers '
+                                       '+ greedy sampler', 'batch_per_gpu': args.batch},
+                'cpu_baseline': {'value': round(value, 3), 'unit': 'tok/s', 'cores': cores, 'kind': 'port',
+                                 'sample': f'{steps} full decode steps at B={args.batch} through the numpy '
+                                           f'restatement of the reference algorithm (oracle/), single thread'},
+                'e2e': {'value': round(value, 3), 'unit': 'tok/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    dist = None
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as tdist
+        torch.cuda.set_device(local_rank)
+        tdist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120))
+        dist = tdist
+    result, _ = run_gpu(args, rank, world, local_rank, dist)
+    if rank == 0:
+        import torch
+        import yanchor_b200 as yb
+        hbm, tf_burst, tf_sust, peak_kind = peaks()
+        if not args.no_prefill:
+            result['prefill'] = run_prefill(torch, yb, torch.device('cuda', local_rank), hbm, tf_burst, peak_kind)
+        if world == 1 and not args.no_cpu:
+            value, dt = cpu_decode_sample(steps=2, B=args.batch)
+            result['cpu_baseline'] = {'value': round(value, 3), 'unit': 'tok/s', 'cores': 1, 'kind': 'port',
+                                      'sample': f'2 full decode steps at B={args.batch} through the numpy '
+                                                f'restatement (oracle/), single thread, {dt:.1f} s'}
+        print(json.dumps(result), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == '__main__':
+    main()

@@ -1,0 +1,188 @@
+/*
+ * yanchor_b200 — C ABI of the B200 (sm_100a) kernels for YANchor's
+ * data-parallel hot path: the gated delta rule (GDN) recurrence (chunked
+ * prefill and per-token decode), the fixed-capacity anchor memory read/write,
+ * and final-logit sampling.
+ *
+ * Conventions
+ *   - Every pointer is a device pointer unless stated otherwise; the caller
+ *     owns all memory.  Sizes and strides are int64 element counts.
+ *   - `stream` is a cudaStream_t passed as void*.  Nothing here synchronises
+ *     the stream or allocates device memory, so every call may be captured in
+ *     a CUDA graph.
+ *   - Every entry point returns YB_OK (0) or an error code; argument errors
+ *     are detected on the host before any launch.  yb_last_error() gives a
+ *     message for the calling thread's last failure.
+ *   - dtype codes: YB_F32, YB_F16, YB_BF16.
+ *
+ * The reference binds these operations as Python callables; the comment above
+ * each entry point names the reference interface it replaces (paths inside
+ * the reference project; "fla:" is flash-linear-attention 0.5.1, the
+ * third-party package the reference pins in requirements.txt:20).
+ */
+#ifndef YANCHOR_B200_H
+#define YANCHOR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum yb_dtype { YB_F32 = 0, YB_F16 = 1, YB_BF16 = 2 };
+
+enum yb_status {
+  YB_OK = 0,
+  YB_ERR_ARGUMENT = 1,     /* bad shape, stride, dtype or pointer */
+  YB_ERR_UNSUPPORTED = 2,  /* valid request this build does not implement */
+  YB_ERR_CUDA = 3,         /* a CUDA launch failed */
+  YB_ERR_WORKSPACE = 4     /* workspace missing or too small */
+};
+
+/* GDN flags */
+#define YB_GDN_QK_L2NORM 1u        /* use_qk_l2norm_in_kernel */
+#define YB_GDN_GATE_IN_KERNEL 2u   /* g holds raw `a`; decay = -exp(A_log) * softplus(a + dt_bias) */
+#define YB_GDN_BETA_SIGMOID 4u     /* beta holds logits; beta = sigmoid(beta) */
+#define YB_GDN_TRANSPOSE_STATE 8u  /* state layout [N, HV, V, K] instead of [N, HV, K, V] */
+
+/* Message of the calling thread's last failed call ("" if none). */
+const char *yb_last_error(void);
+/* ABI version of this library. */
+int yb_abi_version(void);
+
+/*
+ * Per-token gated delta rule over T steps (T = 1 is batched decode).
+ * Replaces fla: ops/gated_delta_rule/fused_recurrent.py:291
+ * `fused_recurrent_gated_delta_rule`, as bound by modeling_yanchor.py:398-406
+ * and by the in-place decode override runtime/model/inference_kernels.py:147-173
+ * (h0 == ht: the state is updated in place).
+ *
+ *   q, k  [B, T, H, K]    v, o  [B, T, HV, V]    g, beta  [B, T, HV]
+ *   h0, ht [N, HV, K, V] fp32 (or [N, HV, V, K] with YB_GDN_TRANSPOSE_STATE);
+ *   either may be NULL; they may alias.
+ *   *_tok_stride: elements between consecutive tokens of the flattened
+ *   (B*T) token axis; heads and features are contiguous inside a token.
+ *   cu_seqlens: NULL, or [N+1] int64 with B == 1 (varlen packing).
+ *   A_log, dt_bias: [HV] fp32, used with YB_GDN_GATE_IN_KERNEL.
+ *   z, norm_weight: optional fused gated RMSNorm epilogue
+ *   (transformers qwen3_5 Qwen3_5RMSNormGated, modeling_qwen3_5.py:175-190):
+ *   o = norm_weight * rmsnorm(o) * silu(z); z [B, T, HV, V] contiguous,
+ *   norm_weight [V], both in io_dtype.  Pass NULL to skip.
+ */
+int yb_gdn_recurrent_fwd(const void *q, const void *k, const void *v, int64_t q_tok_stride,
+                         int64_t k_tok_stride, int64_t v_tok_stride, const void *g, const void *beta,
+                         int64_t g_tok_stride, int64_t beta_tok_stride, const float *A_log,
+                         const float *dt_bias, const float *h0, float *ht, void *o, const void *z,
+                         const void *norm_weight, float norm_eps, const int64_t *cu_seqlens, int64_t B,
+                         int64_t T, int64_t H, int64_t HV, int64_t K, int64_t V, int64_t N, float scale,
+                         int io_dtype, int g_dtype, int beta_dtype, uint32_t flags, void *stream);
+
+/*
+ * Chunked (64-token WY/UT transform) gated delta rule for prefill.
+ * Replaces fla: ops/gated_delta_rule/chunk.py:365 `chunk_gated_delta_rule`
+ * (bound at modeling_yanchor.py:397-405; the torch restatement is
+ * transformers qwen3_5 modeling_qwen3_5.py:234-311).
+ * Same tensor conventions as yb_gdn_recurrent_fwd (no fused norm epilogue).
+ * workspace: device scratch of at least yb_gdn_chunk_workspace_bytes(...)
+ * bytes (may be NULL when that is 0).
+ */
+int64_t yb_gdn_chunk_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t HV, int64_t K, int64_t V,
+                                     int64_t N, int io_dtype);
+int yb_gdn_chunk_fwd(const void *q, const void *k, const void *v, int64_t q_tok_stride,
+                     int64_t k_tok_stride, int64_t v_tok_stride, const void *g, const void *beta,
+                     int64_t g_tok_stride, int64_t beta_tok_stride, const float *A_log, const float *dt_bias,
+                     const float *h0, float *ht, void *o, const int64_t *cu_seqlens, int64_t B, int64_t T,
+                     int64_t H, int64_t HV, int64_t K, int64_t V, int64_t N, float scale, int io_dtype,
+                     int g_dtype, int beta_dtype, uint32_t flags, void *workspace, int64_t workspace_bytes,
+                     void *stream);
+
+/*
+ * GDN gates: beta = sigmoid(b) (io_dtype) and g = -exp(A_log) * softplus(a + dt_bias)
+ * (fp32, linear above 20).  b, a: [rows, heads] with row strides; A_log, dt_bias [heads] fp32.
+ * Replaces runtime/model/inference_kernels.py:683-691 `triton_qwen35_fused_gdn_gates`
+ * (the expression of transformers qwen3_5 modeling_qwen3_5.py:500-502).
+ */
+int yb_gdn_gates(const void *b, const void *a, int64_t b_row_stride, int64_t a_row_stride,
+                 const float *A_log, const float *dt_bias, void *beta_out, float *g_out, int64_t rows,
+                 int64_t heads, int io_dtype, void *stream);
+
+/*
+ * Anchor memory, decode read: softmax over the CAP committed slots plus a
+ * null slot (logit 0, value 0); empty slots have position < 0.
+ * Replaces runtime/model/independent_memory.py:177 `committed_gqa`
+ * (torch: modeling_yanchor.py:283-290).
+ *   query, out [B, 1, H, D] contiguous; keys, values [*, G, CAP, D] with batch
+ *   stride kv_stride0; positions [*, G, CAP] int32 with batch stride
+ *   pos_stride0; indices NULL or [B] int64 (state row per request, -1 = skip,
+ *   output zeros).
+ */
+int yb_mem_decode_read(const void *query, const void *keys, const void *values, const int32_t *positions,
+                       const int64_t *indices, void *out, int64_t B, int64_t H, int64_t G, int64_t CAP,
+                       int64_t D, int64_t kv_stride0, int64_t pos_stride0, int dtype, void *stream);
+
+/*
+ * Anchor memory, decode write/commit (state mutated in place).
+ * Replaces runtime/model/independent_memory.py:190 `commit_decode`
+ * (torch: modeling_yanchor.py:291-312).
+ *   key, value [B, 1, G, D] contiguous; scores [B, 1, G] fp32; active [B] bool.
+ *   Bank: keys/values [*, G, CAP, D] (batch stride kv_stride0), scores fp32 and
+ *   positions int32 [*, G, CAP] (batch stride meta_stride0).  Pending:
+ *   pending_keys/values [*, G, PC, D] (pkv_stride0), pending_scores [*, G, PC]
+ *   (pmeta_stride0).  count/total int64 [*] (count_stride0).  chunk <= PC.
+ */
+int yb_mem_decode_commit(const void *key, const void *value, const float *scores, const uint8_t *active,
+                         int64_t chunk, void *keys, void *values, float *bank_scores, int32_t *positions,
+                         void *pending_keys, void *pending_values, float *pending_scores, int64_t *count,
+                         int64_t *total, const int64_t *indices, int64_t B, int64_t G, int64_t CAP,
+                         int64_t PC, int64_t D, int64_t kv_stride0, int64_t meta_stride0,
+                         int64_t pkv_stride0, int64_t pmeta_stride0, int64_t count_stride0, int dtype,
+                         void *stream);
+
+/*
+ * Anchor memory, prefill read: each block's queries attend to their group's
+ * referenced rows plus the null slot.
+ * Replaces runtime/model/independent_memory.py:38 `indexed_gqa`
+ * (torch: modeling_yanchor.py:22-42 `indexed_gqa_torch`).
+ *   query, out [B, blocks, chunk, H, D]; key, value [KB, S, G, D] (KB = 1 or B);
+ *   references [B, blocks, G, CAP] int64, -1 = empty.  All contiguous.
+ */
+int yb_mem_indexed_read(const void *query, const void *key, const void *value, const int64_t *references,
+                        void *out, int64_t B, int64_t blocks, int64_t chunk, int64_t H, int64_t G,
+                        int64_t D, int64_t S, int64_t KB, int64_t CAP, int dtype, void *stream);
+
+/*
+ * Sampling.  scores [B, vocab] (row stride in elements) in dtype; out [B] int64.
+ * Workspace: device scratch of at least yb_sample_workspace_bytes(B, vocab, top_k).
+ *
+ * yb_sample_greedy: index of the first maximum per row (argmax).
+ * Replaces the top_k == 1 branch of runtime/model/inference_kernels.py:73-88
+ * `sample_top_k_top_p_counter` (scores.argmax(-1)).
+ *
+ * yb_sample_top_k_top_p_counter: top-k (k <= 256; top_k <= 0 means the whole
+ * vocabulary, allowed only with top_p == 1) → softmax(values / temperature) →
+ * top-p truncation → inverse-CDF pick with the stateless counter uniform of
+ * (attempt id, step, seed, stream).  steps NULL means every row uses
+ * scalar_step.  Replaces inference_kernels.py:73-88 and the fused top-20
+ * sampler inference_kernels.py:1119-1167.
+ */
+int64_t yb_sample_workspace_bytes(int64_t B, int64_t vocab, int64_t top_k);
+int yb_sample_greedy(const void *scores, int64_t row_stride, int64_t B, int64_t vocab, int dtype, int64_t *out,
+                     void *workspace, int64_t workspace_bytes, void *stream);
+int yb_sample_top_k_top_p_counter(const void *scores, int64_t row_stride, int64_t B, int64_t vocab, int dtype,
+                                  const int64_t *attempt_ids, const int64_t *steps, int64_t scalar_step,
+                                  int64_t seed, int64_t stream_id, float temperature, int64_t top_k,
+                                  float top_p, int64_t *out, void *workspace, int64_t workspace_bytes,
+                                  void *stream);
+
+/*
+ * scores[i] -= penalty * seen[i] over n elements (seen: bool bytes).
+ * Replaces runtime/model/inference_kernels.py:1104-1114 `_apply_dense_presence_penalty_`.
+ */
+int yb_presence_penalty(void *scores, const uint8_t *seen, int64_t n, float penalty, int dtype, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* YANCHOR_B200_H */

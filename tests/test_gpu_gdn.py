@@ -1,0 +1,233 @@
+"""GPU parity of the gated-delta-rule kernels against the CPU oracle and the
+reference-generated fixtures.
+
+Tolerances: fp32 inputs compare at 1e-4 (chunk, recurrent) against the fp32
+reference outputs; bf16 inputs use the north-star bar — max abs error
+<= 2e-2 on outputs and <= 1e-3 relative (Frobenius) on the fp32 state —
+against a float64 oracle."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import gdn as ogdn
+
+pytestmark = pytest.mark.gpu
+
+BF16_ATOL = 2e-2
+STATE_RTOL = 1e-3
+
+
+@pytest.fixture(scope='module')
+def yb():
+    import yanchor_b200
+    assert torch.cuda.is_available()
+    return yanchor_b200
+
+
+def cuda(x, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(x)).cuda()
+    return t if dtype is None else t.to(dtype)
+
+
+def host(t):
+    return t.detach().float().cpu().numpy()
+
+
+def rel(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30)
+
+
+def make_inputs(rng, B, T, H, HV, K, V, h0_std=0.02, N=None):
+    q = rng.standard_normal((B, T, H, K)).astype(np.float32)
+    k = rng.standard_normal((B, T, H, K)).astype(np.float32)
+    v = rng.standard_normal((B, T, HV, V)).astype(np.float32)
+    g = np.log(1 / (1 + np.exp(-rng.standard_normal((B, T, HV))))).astype(np.float32)   # logsigmoid
+    beta = (1 / (1 + np.exp(-rng.standard_normal((B, T, HV))))).astype(np.float32)
+    h0 = (h0_std * rng.standard_normal((N or B, HV, K, V))).astype(np.float32)
+    return q, k, v, g, beta, h0
+
+
+# ---------------------------------------------------------------- golden ----
+@pytest.mark.parametrize('form', ['chunk', 'rec'])
+def test_golden_small_fp32(yb, golden, form):
+    d = golden('gdn')
+    fn = yb.chunk_gated_delta_rule if form == 'chunk' else yb.fused_recurrent_gated_delta_rule
+    o, s = fn(cuda(d['small_q']), cuda(d['small_k']), cuda(d['small_v']), g=cuda(d['small_g']),
+              beta=cuda(d['small_beta']), initial_state=cuda(d['small_h0']), output_final_state=True,
+              use_qk_l2norm_in_kernel=True)
+    np.testing.assert_allclose(host(o), d[f'small_{form}_o'], atol=1e-4)
+    np.testing.assert_allclose(host(s), d[f'small_{form}_s'], atol=1e-4)
+
+
+@pytest.mark.parametrize('form', ['chunk', 'rec'])
+def test_golden_gva_varlen_fp32(yb, golden, form):
+    d = golden('gdn')
+    fn = yb.chunk_gated_delta_rule if form == 'chunk' else yb.fused_recurrent_gated_delta_rule
+    o, s = fn(cuda(d['var_q']), cuda(d['var_k']), cuda(d['var_v']), g=cuda(d['var_g']), beta=cuda(d['var_beta']),
+              initial_state=cuda(d['var_h0']), output_final_state=True, use_qk_l2norm_in_kernel=True,
+              cu_seqlens=cuda(d['var_cu']))
+    np.testing.assert_allclose(host(o), d[f'var_{form}_o'], atol=1e-4)
+    np.testing.assert_allclose(host(s), d[f'var_{form}_s'], atol=1e-4)
+
+
+def test_golden_config0_recipe(yb, golden):
+    d = golden('gdn')
+    q, k = ogdn.l2norm(d['small_q']), ogdn.l2norm(d['small_k'])
+    o, s = yb.chunk_gated_delta_rule(cuda(q), cuda(k), cuda(d['small_v']), cuda(d['small_g']),
+                                     cuda(d['small_beta']), output_final_state=True)
+    np.testing.assert_allclose(host(o), d['small_chunk0_o'], atol=1e-4)
+    np.testing.assert_allclose(host(s), d['small_chunk0_s'], atol=1e-4)
+
+
+# ------------------------------------------------------------ decode bf16 ---
+@pytest.mark.parametrize('trans', [False, True])
+def test_decode_bf16_yanchor_shape(yb, trans):
+    """One decode step at the YANchor-4B GDN shape (H=16, HV=32, K=V=128)."""
+    rng = np.random.default_rng(10)
+    q, k, v, g, beta, h0 = make_inputs(rng, 16, 1, 16, 32, 128, 128, h0_std=0.05)
+    qb, kb, vb = (cuda(x, torch.bfloat16) for x in (q, k, v))
+    h0d = cuda(h0.swapaxes(-1, -2).copy() if trans else h0)
+    o, s = yb.fused_recurrent_gated_delta_rule(qb, kb, vb, g=cuda(g), beta=cuda(beta, torch.bfloat16),
+                                               initial_state=h0d, output_final_state=True,
+                                               use_qk_l2norm_in_kernel=True, transpose_state_layout=trans)
+    eo, es = ogdn.recurrent_gated_delta_rule(host(qb), host(kb), host(vb), g, host(cuda(beta, torch.bfloat16)),
+                                             initial_state=h0, use_qk_l2norm=True, dtype=np.float64)
+    sd = host(s)
+    if trans:
+        sd = sd.swapaxes(-1, -2)
+    assert np.abs(host(o) - eo).max() <= BF16_ATOL
+    assert rel(sd, es) <= STATE_RTOL
+
+
+def test_decode_inplace_state_and_steps(yb):
+    """In-place state (h0 is ht) over 24 decode steps equals the oracle run."""
+    rng = np.random.default_rng(11)
+    B, H, HV, K, V, steps = 8, 16, 32, 128, 128, 24
+    q, k, v, g, beta, h0 = make_inputs(rng, B, steps, H, HV, K, V, h0_std=0.05)
+    state = cuda(h0)
+    outs = []
+    for t in range(steps):
+        o, s = yb.fused_recurrent_gated_delta_rule(
+            cuda(q[:, t:t + 1], torch.bfloat16), cuda(k[:, t:t + 1], torch.bfloat16),
+            cuda(v[:, t:t + 1], torch.bfloat16), g=cuda(g[:, t:t + 1]), beta=cuda(beta[:, t:t + 1]),
+            initial_state=state, output_final_state=True, use_qk_l2norm_in_kernel=True, inplace=True)
+        assert s is state
+        outs.append(host(o))
+    rb = lambda x: host(cuda(x, torch.bfloat16))  # noqa: E731
+    eo, es = ogdn.recurrent_gated_delta_rule(rb(q), rb(k), rb(v), g, beta, initial_state=h0, use_qk_l2norm=True,
+                                             dtype=np.float64)
+    assert np.abs(np.concatenate(outs, 1) - eo).max() <= BF16_ATOL
+    assert rel(host(state), es) <= STATE_RTOL
+
+
+def test_decode_gates_and_norm_in_kernel(yb):
+    """use_gate_in_kernel + beta logits + the fused gated RMSNorm epilogue."""
+    rng = np.random.default_rng(12)
+    B, H, HV, K, V = 8, 16, 32, 128, 128
+    q, k, v, _, _, h0 = make_inputs(rng, B, 1, H, HV, K, V, h0_std=0.05)
+    a = (2 * rng.standard_normal((B, 1, HV))).astype(np.float32)
+    blog = rng.standard_normal((B, 1, HV)).astype(np.float32)
+    A_log = np.log(rng.uniform(1, 16, HV)).astype(np.float32)
+    dt_bias = rng.standard_normal(HV).astype(np.float32)
+    z = rng.standard_normal((B, 1, HV, V)).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(V)).astype(np.float32)
+    bf = torch.bfloat16
+    o, s = yb.fused_recurrent_gated_delta_rule(
+        cuda(q, bf), cuda(k, bf), cuda(v, bf), g=cuda(a), beta=cuda(blog, bf), initial_state=cuda(h0),
+        output_final_state=True, use_qk_l2norm_in_kernel=True, use_gate_in_kernel=True, A_log=cuda(A_log),
+        dt_bias=cuda(dt_bias), use_beta_sigmoid_in_kernel=True, z=cuda(z, bf), norm_weight=cuda(w, bf))
+    g, beta = ogdn.gdn_gates(a, host(cuda(blog, bf)), A_log, dt_bias, dtype=np.float64)
+    rb = lambda x: host(cuda(x, bf))  # noqa: E731
+    eo, es = ogdn.recurrent_gated_delta_rule(rb(q), rb(k), rb(v), g, beta, initial_state=h0, use_qk_l2norm=True,
+                                             dtype=np.float64)
+    en = ogdn.rmsnorm_gated(eo, rb(z), rb(w), dtype=np.float64)
+    assert np.abs(host(o) - en).max() <= BF16_ATOL * 2
+    assert rel(host(s), es) <= STATE_RTOL
+
+
+def test_gdn_gates_kernel(yb, golden):
+    d = golden('gdn')
+    beta, g = yb.gdn_gates(cuda(d['gate_b']), cuda(d['gate_a']), cuda(d['gate_A_log']), cuda(d['gate_dt_bias']))
+    np.testing.assert_allclose(host(g), d['gate_g'], rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(host(beta), d['gate_beta'], atol=1e-6)
+
+
+# ------------------------------------------------------------ prefill bf16 --
+@pytest.mark.parametrize('H', [16, 32])
+def test_chunk_bf16_vs_oracle(yb, H):
+    """bf16 chunked prefill with a ragged tail and a nonzero initial state."""
+    rng = np.random.default_rng(20 + H)
+    B, T, HV, K, V = 2, 300, 32, 128, 128
+    q, k, v, g, beta, h0 = make_inputs(rng, B, T, H, HV, K, V)
+    bf = torch.bfloat16
+    o, s = yb.chunk_gated_delta_rule(cuda(q, bf), cuda(k, bf), cuda(v, bf), cuda(g), cuda(beta, bf),
+                                     initial_state=cuda(h0), output_final_state=True, use_qk_l2norm_in_kernel=True)
+    rb = lambda x: host(cuda(x, bf))  # noqa: E731
+    eo, es = ogdn.chunk_gated_delta_rule(rb(q), rb(k), rb(v), g, rb(beta), initial_state=h0, use_qk_l2norm=True,
+                                         dtype=np.float64)
+    assert np.abs(host(o) - eo).max() <= BF16_ATOL
+    assert rel(host(s), es) <= STATE_RTOL
+
+
+def test_chunk_varlen_bf16_vs_oracle(yb):
+    rng = np.random.default_rng(30)
+    cu = np.array([0, 1, 64, 65, 200, 333, 512], dtype=np.int64)
+    H, HV, K, V = 16, 32, 128, 128
+    q, k, v, g, beta, h0 = make_inputs(rng, 1, int(cu[-1]), H, HV, K, V, N=len(cu) - 1)
+    bf = torch.bfloat16
+    o, s = yb.chunk_gated_delta_rule(cuda(q, bf), cuda(k, bf), cuda(v, bf), cuda(g), cuda(beta, bf),
+                                     initial_state=cuda(h0), output_final_state=True, use_qk_l2norm_in_kernel=True,
+                                     cu_seqlens=cuda(cu))
+    rb = lambda x: host(cuda(x, bf))  # noqa: E731
+    eo, es = ogdn.chunk_gated_delta_rule(rb(q), rb(k), rb(v), g, rb(beta), initial_state=h0, use_qk_l2norm=True,
+                                         cu_seqlens=cu, dtype=np.float64)
+    assert np.abs(host(o) - eo).max() <= BF16_ATOL
+    assert rel(host(s), es) <= STATE_RTOL
+
+
+def test_empty_and_zero_length(yb):
+    bf = torch.bfloat16
+    q = torch.zeros(1, 0, 16, 128, device='cuda', dtype=bf)
+    v = torch.zeros(1, 0, 32, 128, device='cuda', dtype=bf)
+    g = torch.zeros(1, 0, 32, device='cuda')
+    o, s = yb.chunk_gated_delta_rule(q, q, v, g, g.to(bf), output_final_state=True)
+    assert o.shape == (1, 0, 32, 128) and s.shape == (1, 32, 128, 128) and not s.abs().any()
+    # a zero-length sequence in a varlen batch keeps its initial state
+    cu = torch.tensor([0, 0, 5], device='cuda')
+    qq = torch.randn(1, 5, 16, 128, device='cuda', dtype=bf)
+    vv = torch.randn(1, 5, 32, 128, device='cuda', dtype=bf)
+    gg = -torch.rand(1, 5, 32, device='cuda')
+    h0 = torch.randn(2, 32, 128, 128, device='cuda')
+    for fn in (yb.chunk_gated_delta_rule, yb.fused_recurrent_gated_delta_rule):
+        _, s = fn(qq, qq, vv, gg, gg.sigmoid().to(bf), initial_state=h0, output_final_state=True, cu_seqlens=cu,
+                  use_qk_l2norm_in_kernel=True)
+        torch.testing.assert_close(s[0], h0[0], rtol=0, atol=0)
+
+
+# ------------------------------------------------- full-size properties -----
+def test_config1_chunk_equals_recurrent_and_split(yb):
+    """At the config-1 shape (B=8, T=8192, H=HV=32, K=V=128, bf16), the
+    chunked prefill agrees with the token recurrence, and splitting the
+    sequence in two with state passing gives the same final state."""
+    torch.manual_seed(0)
+    B, T, H, K = 8, 8192, 32, 128
+    bf = torch.bfloat16
+    q = torch.randn(B, T, H, K, device='cuda', dtype=bf)
+    k = torch.randn(B, T, H, K, device='cuda', dtype=bf)
+    v = torch.randn(B, T, H, K, device='cuda', dtype=bf)
+    g = torch.nn.functional.logsigmoid(torch.randn(B, T, H, device='cuda'))
+    beta = torch.randn(B, T, H, device='cuda').sigmoid().to(bf)
+    h0 = 0.02 * torch.randn(B, H, K, K, device='cuda')
+    kw = dict(output_final_state=True, use_qk_l2norm_in_kernel=True)
+    o1, s1 = yb.chunk_gated_delta_rule(q, k, v, g, beta, initial_state=h0, **kw)
+    o2, s2 = yb.fused_recurrent_gated_delta_rule(q, k, v, g=g, beta=beta, initial_state=h0, **kw)
+    assert (o1.float() - o2.float()).abs().max().item() <= BF16_ATOL
+    assert ((s1 - s2).norm() / s2.norm()).item() <= STATE_RTOL
+    cut = 3000   # not a chunk multiple
+    oa, sa = yb.chunk_gated_delta_rule(q[:, :cut], k[:, :cut], v[:, :cut], g[:, :cut], beta[:, :cut],
+                                       initial_state=h0, **kw)
+    ob, sb = yb.chunk_gated_delta_rule(q[:, cut:], k[:, cut:], v[:, cut:], g[:, cut:], beta[:, cut:],
+                                       initial_state=sa, **kw)
+    assert (torch.cat([oa, ob], 1).float() - o1.float()).abs().max().item() <= BF16_ATOL
+    assert ((sb - s1).norm() / s1.norm()).item() <= STATE_RTOL

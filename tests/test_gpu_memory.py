@@ -1,0 +1,131 @@
+"""GPU parity of the anchor-memory kernels against the reference fixtures and
+the CPU oracle.  Integer state (positions, count, total) and copied rows
+(bank keys / values, scores) must match exactly; reads are float and compare
+at 1e-5 (fp32) or 2e-2 (bf16)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import memory as omem
+
+pytestmark = pytest.mark.gpu
+
+FIELDS = ('keys', 'values', 'scores', 'positions', 'pending_keys', 'pending_values', 'pending_scores', 'count',
+          'total')
+
+
+@pytest.fixture(scope='module')
+def yb():
+    import yanchor_b200
+    return yanchor_b200
+
+
+def cuda(x, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(x)).cuda()
+    return t if dtype is None else t.to(dtype)
+
+
+def host(t):
+    return t.detach().cpu().numpy() if t.dtype in (torch.int32, torch.int64, torch.bool) else \
+        t.detach().float().cpu().numpy()
+
+
+def to_device_state(yb, st, dtype):
+    return yb.MemoryState(*(cuda(st[f], dtype if st[f].dtype == np.float32 and 'score' not in f else None)
+                            for f in FIELDS))
+
+
+def test_decode_sequence_matches_reference(yb, golden):
+    """Replay the reference's 41-step decode (fixed ties, inactive rows,
+    several commits) on the GPU."""
+    d = golden('memory')
+    B, G, D = d['dec_k'].shape[1], d['dec_k'].shape[3], d['dec_k'].shape[4]
+    CAP, PC = d['dec_final_keys'].shape[2], d['dec_final_pending_keys'].shape[2]
+    st = yb.MemoryState.empty(B, G, CAP, PC, D, 'cuda', torch.float32)
+    for t in range(d['dec_q'].shape[0]):
+        read = yb.committed_gqa(cuda(d['dec_q'][t]), st) * cuda(d['dec_valid'][t])[..., None, None]
+        np.testing.assert_allclose(host(read), d['dec_reads'][t], atol=1e-5, err_msg=f'step {t}')
+        yb.commit_decode(cuda(d['dec_k'][t]), cuda(d['dec_v'][t]), cuda(d['dec_scores'][t]),
+                         cuda(d['dec_valid'][t][:, 0]), 8, st)
+        if t in (7, 20):
+            for f in FIELDS:
+                np.testing.assert_array_equal(host(getattr(st, f)), d[f'dec_t{t}_{f}'], err_msg=f'{f} @ {t}')
+    for f in FIELDS:
+        np.testing.assert_array_equal(host(getattr(st, f)), d[f'dec_final_{f}'], err_msg=f)
+
+
+def test_decode_yanchor_shape_bf16_with_pool_indices(yb):
+    """YANchor-4B memory shape (G=4, H=16, D=256, CAP=64, chunk=64), bf16,
+    requests mapped into a larger slot pool through indices (-1 = skip)."""
+    rng = np.random.default_rng(40)
+    B, POOL, G, H, D, CAP, CH, STEPS = 6, 9, 4, 16, 256, 64, 64, 150
+    indices = np.array([3, 0, -1, 8, 5, 1], dtype=np.int64)
+    st_np = omem.empty_state(POOL, G, CAP, CH, D)
+    bf = torch.bfloat16
+    st = to_device_state(yb, st_np, bf)
+    for t in range(STEPS):
+        q = rng.standard_normal((B, 1, H, D)).astype(np.float32)
+        k = rng.standard_normal((B, 1, G, D)).astype(np.float32)
+        v = rng.standard_normal((B, 1, G, D)).astype(np.float32)
+        sc = np.round(rng.standard_normal((B, 1, G)) * 4).astype(np.float32) / 4   # frequent ties
+        act = rng.random(B) > 0.1
+        qb, kb, vb = cuda(q, bf), cuda(k, bf), cuda(v, bf)
+        read = yb.committed_gqa(qb, st, cuda(indices))
+        ref_read = omem.decode_read(host(qb), st_np['keys'], st_np['values'], st_np['positions'], indices)
+        assert np.abs(host(read) - ref_read).max() <= 2e-2, t
+        yb.commit_decode(kb, vb, cuda(sc), cuda(act), CH, st, cuda(indices))
+        omem.commit_decode(host(kb), host(vb), sc, act, CH, st_np, indices)
+    for f in FIELDS:
+        np.testing.assert_array_equal(host(getattr(st, f)), st_np[f].astype(host(getattr(st, f)).dtype),
+                                      err_msg=f)
+
+
+def test_decode_strided_pool_view(yb):
+    """State fields that are views into a wider page (batch stride larger than
+    the row), as the vLLM adapter passes."""
+    rng = np.random.default_rng(41)
+    B, G, H, D, CAP, CH = 4, 2, 4, 64, 16, 8
+    st_np = omem.empty_state(B, G, CAP, CH, D)
+    pad = lambda x, extra: torch.cat([x, torch.zeros((x.shape[0], extra) + x.shape[2:], dtype=x.dtype,  # noqa: E731
+                                                                 device=x.device)], 1)[:, :x.shape[1]]
+    base = to_device_state(yb, st_np, torch.float32)
+    st = yb.MemoryState(*(pad(getattr(base, f), 3) if getattr(base, f).dim() > 1 else getattr(base, f)
+                          for f in FIELDS))
+    assert st.keys.stride(0) != G * CAP * D
+    for t in range(20):
+        q = rng.standard_normal((B, 1, H, D)).astype(np.float32)
+        k = rng.standard_normal((B, 1, G, D)).astype(np.float32)
+        v = rng.standard_normal((B, 1, G, D)).astype(np.float32)
+        sc = rng.standard_normal((B, 1, G)).astype(np.float32)
+        act = np.ones(B, bool)
+        read = yb.committed_gqa(cuda(q), st)
+        np.testing.assert_allclose(host(read), omem.decode_read(q, st_np['keys'], st_np['values'],
+                                                                st_np['positions']), atol=1e-5)
+        yb.commit_decode(cuda(k), cuda(v), cuda(sc), cuda(act), CH, st)
+        omem.commit_decode(k, v, sc, act, CH, st_np)
+    for f in FIELDS:
+        np.testing.assert_array_equal(host(getattr(st, f)), st_np[f].astype(host(getattr(st, f)).dtype))
+
+
+def test_indexed_read_golden(yb, golden):
+    d = golden('memory')
+    out = yb.indexed_gqa(cuda(d['idx_q']), cuda(d['idx_k']), cuda(d['idx_v']), cuda(d['idx_refs']))
+    np.testing.assert_allclose(host(out), d['idx_out'], atol=1e-5)
+
+
+@pytest.mark.parametrize('kb', [1, 2])
+def test_indexed_read_bf16_yanchor_shape(yb, kb):
+    rng = np.random.default_rng(42 + kb)
+    B, blocks, chunk, H, G, D, S, CAP = 2, 3, 64, 16, 4, 256, 300, 64
+    q = rng.standard_normal((B, blocks, chunk, H, D)).astype(np.float32)
+    k = rng.standard_normal((kb, S, G, D)).astype(np.float32)
+    v = rng.standard_normal((kb, S, G, D)).astype(np.float32)
+    refs = rng.integers(0, S, (B, blocks, G, CAP)).astype(np.int64)
+    refs[rng.random(refs.shape) < 0.2] = -1
+    refs[1, 2, 3] = -1
+    bf = torch.bfloat16
+    qb, kb_, vb = cuda(q, bf), cuda(k, bf), cuda(v, bf)
+    out = yb.indexed_gqa(qb, kb_, vb, cuda(refs))
+    ref = omem.indexed_gqa(host(qb), host(kb_), host(vb), refs)
+    assert np.abs(host(out) - ref).max() <= 2e-2
+    assert not host(out)[1, 2, :, 12:16].any()      # no anchors: only the null slot

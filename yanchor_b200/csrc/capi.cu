@@ -1,0 +1,238 @@
+// extern "C" entry points: validate arguments on the host, then dispatch to
+// the kernel launchers.  Errors never reach the device: a bad call returns a
+// status code and a message (yb_last_error) before any launch.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace yb {
+
+static thread_local char g_err[512] = "";
+
+int set_error(int code, const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char *what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return YB_OK;
+}
+
+static bool dtype_ok(int d) { return d == YB_F32 || d == YB_F16 || d == YB_BF16; }
+static int dtype_size(int d) { return d == YB_F32 ? 4 : 2; }
+static bool aligned(const void *p, int bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; }
+
+#define YB_REQUIRE(cond, ...)                                 \
+  do {                                                        \
+    if (!(cond)) return set_error(YB_ERR_ARGUMENT, __VA_ARGS__); \
+  } while (0)
+
+static int check_gdn(const GdnArgs &a, const char *op) {
+  YB_REQUIRE(dtype_ok(a.io_dtype) && dtype_ok(a.g_dtype) && dtype_ok(a.beta_dtype), "%s: bad dtype code", op);
+  YB_REQUIRE(a.B >= 0 && a.T >= 0 && a.H > 0 && a.HV > 0 && a.K > 0 && a.V > 0, "%s: bad sizes", op);
+  YB_REQUIRE(a.HV % a.H == 0, "%s: HV=%lld must be a multiple of H=%lld", op, (long long)a.HV, (long long)a.H);
+  YB_REQUIRE(a.B * a.T == 0 || (a.q && a.k && a.v && a.g && a.beta && a.o), "%s: null tensor", op);
+  if (a.cu_seqlens) {
+    YB_REQUIRE(a.B == 1, "%s: cu_seqlens requires B == 1 (got %lld)", op, (long long)a.B);
+    YB_REQUIRE(a.N >= 0, "%s: bad N", op);
+  } else {
+    YB_REQUIRE(a.N == a.B, "%s: N (%lld) must equal B (%lld) without cu_seqlens", op, (long long)a.N,
+               (long long)a.B);
+  }
+  const int es = dtype_size(a.io_dtype);
+  YB_REQUIRE(a.q_ts >= a.H * a.K && a.k_ts >= a.H * a.K && a.v_ts >= a.HV * a.V, "%s: token stride too small", op);
+  YB_REQUIRE((a.q_ts * es) % 16 == 0 && (a.k_ts * es) % 16 == 0 && (a.v_ts * es) % 16 == 0,
+             "%s: token strides must be multiples of 16 bytes", op);
+  YB_REQUIRE(aligned(a.q, 16) && aligned(a.k, 16) && aligned(a.v, 16) && aligned(a.o, 16),
+             "%s: q, k, v, o must be 16-byte aligned", op);
+  YB_REQUIRE(!a.h0 || aligned(a.h0, 16), "%s: h0 must be 16-byte aligned", op);
+  YB_REQUIRE(!a.ht || aligned(a.ht, 16), "%s: ht must be 16-byte aligned", op);
+  if (a.flags & YB_GDN_GATE_IN_KERNEL) YB_REQUIRE(a.A_log != nullptr, "%s: A_log required with gate-in-kernel", op);
+  YB_REQUIRE(!(a.flags & ~15u), "%s: unknown flag bits 0x%x", op, a.flags);
+  return YB_OK;
+}
+
+}  // namespace yb
+
+using namespace yb;
+
+extern "C" {
+
+const char *yb_last_error(void) { return g_err; }
+int yb_abi_version(void) { return 1; }
+
+int yb_gdn_recurrent_fwd(const void *q, const void *k, const void *v, int64_t q_tok_stride, int64_t k_tok_stride,
+                         int64_t v_tok_stride, const void *g, const void *beta, int64_t g_tok_stride,
+                         int64_t beta_tok_stride, const float *A_log, const float *dt_bias, const float *h0,
+                         float *ht, void *o, const void *z, const void *norm_weight, float norm_eps,
+                         const int64_t *cu_seqlens, int64_t B, int64_t T, int64_t H, int64_t HV, int64_t K,
+                         int64_t V, int64_t N, float scale, int io_dtype, int g_dtype, int beta_dtype, uint32_t flags,
+                         void *stream) {
+  GdnArgs a{};
+  a.q = q; a.k = k; a.v = v; a.q_ts = q_tok_stride; a.k_ts = k_tok_stride; a.v_ts = v_tok_stride;
+  a.g = g; a.beta = beta; a.g_ts = g_tok_stride; a.beta_ts = beta_tok_stride;
+  a.A_log = A_log; a.dt_bias = dt_bias; a.h0 = h0; a.ht = ht; a.o = o;
+  a.z = z; a.norm_w = norm_weight; a.norm_eps = norm_eps; a.cu_seqlens = cu_seqlens;
+  a.B = B; a.T = T; a.H = H; a.HV = HV; a.K = K; a.V = V; a.N = N; a.scale = scale;
+  a.io_dtype = io_dtype; a.g_dtype = g_dtype; a.beta_dtype = beta_dtype; a.flags = flags;
+  a.stream = static_cast<cudaStream_t>(stream);
+  int rc = check_gdn(a, "gdn_recurrent");
+  if (rc) return rc;
+  if ((z == nullptr) != (norm_weight == nullptr))
+    return set_error(YB_ERR_ARGUMENT, "gdn_recurrent: z and norm_weight go together");
+  if (z && !(aligned(z, 16) && aligned(norm_weight, 16)))
+    return set_error(YB_ERR_ARGUMENT, "gdn_recurrent: z and norm_weight must be 16-byte aligned");
+  return launch_gdn_recurrent(a);
+}
+
+int64_t yb_gdn_chunk_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t HV, int64_t K, int64_t V, int64_t N,
+                                     int io_dtype) {
+  return gdn_chunk_workspace_bytes(B, T, H, HV, K, V, N, io_dtype);
+}
+
+int yb_gdn_chunk_fwd(const void *q, const void *k, const void *v, int64_t q_tok_stride, int64_t k_tok_stride,
+                     int64_t v_tok_stride, const void *g, const void *beta, int64_t g_tok_stride,
+                     int64_t beta_tok_stride, const float *A_log, const float *dt_bias, const float *h0, float *ht,
+                     void *o, const int64_t *cu_seqlens, int64_t B, int64_t T, int64_t H, int64_t HV, int64_t K,
+                     int64_t V, int64_t N, float scale, int io_dtype, int g_dtype, int beta_dtype, uint32_t flags,
+                     void *workspace, int64_t workspace_bytes, void *stream) {
+  GdnArgs a{};
+  a.q = q; a.k = k; a.v = v; a.q_ts = q_tok_stride; a.k_ts = k_tok_stride; a.v_ts = v_tok_stride;
+  a.g = g; a.beta = beta; a.g_ts = g_tok_stride; a.beta_ts = beta_tok_stride;
+  a.A_log = A_log; a.dt_bias = dt_bias; a.h0 = h0; a.ht = ht; a.o = o; a.cu_seqlens = cu_seqlens;
+  a.B = B; a.T = T; a.H = H; a.HV = HV; a.K = K; a.V = V; a.N = N; a.scale = scale;
+  a.io_dtype = io_dtype; a.g_dtype = g_dtype; a.beta_dtype = beta_dtype; a.flags = flags;
+  a.workspace = workspace; a.workspace_bytes = workspace_bytes;
+  a.stream = static_cast<cudaStream_t>(stream);
+  int rc = check_gdn(a, "gdn_chunk");
+  if (rc) return rc;
+  const int64_t need = gdn_chunk_workspace_bytes(B, T, H, HV, K, V, N, io_dtype);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need))
+    return set_error(YB_ERR_WORKSPACE, "gdn_chunk: workspace of %lld bytes required", (long long)need);
+  return launch_gdn_chunk(a);
+}
+
+int yb_gdn_gates(const void *b, const void *a, int64_t b_row_stride, int64_t a_row_stride, const float *A_log,
+                 const float *dt_bias, void *beta_out, float *g_out, int64_t rows, int64_t heads, int io_dtype,
+                 void *stream) {
+  YB_REQUIRE(dtype_ok(io_dtype), "gdn_gates: bad dtype");
+  YB_REQUIRE(rows >= 0 && heads > 0, "gdn_gates: bad sizes");
+  YB_REQUIRE(b && a && A_log && beta_out && g_out, "gdn_gates: null tensor");
+  YB_REQUIRE(b_row_stride >= heads && a_row_stride >= heads, "gdn_gates: row stride too small");
+  return launch_gdn_gates(b, a, b_row_stride, a_row_stride, A_log, dt_bias, beta_out, g_out, rows, heads, io_dtype,
+                          static_cast<cudaStream_t>(stream));
+}
+
+int yb_mem_decode_read(const void *query, const void *keys, const void *values, const int32_t *positions,
+                       const int64_t *indices, void *out, int64_t B, int64_t H, int64_t G, int64_t CAP, int64_t D,
+                       int64_t kv_stride0, int64_t pos_stride0, int dtype, void *stream) {
+  YB_REQUIRE(dtype_ok(dtype), "mem_decode_read: bad dtype");
+  YB_REQUIRE(B >= 0 && H > 0 && G > 0 && CAP > 0 && D > 0 && H % G == 0, "mem_decode_read: bad sizes");
+  YB_REQUIRE(query && keys && values && positions && out, "mem_decode_read: null tensor");
+  YB_REQUIRE(kv_stride0 >= G * CAP * D && pos_stride0 >= G * CAP, "mem_decode_read: batch stride too small");
+  YB_REQUIRE((kv_stride0 * dtype_size(dtype)) % 16 == 0, "mem_decode_read: key batch stride must be 16-byte multiple");
+  YB_REQUIRE(aligned(query, 16) && aligned(keys, 16) && aligned(values, 16) && aligned(out, 16),
+             "mem_decode_read: tensors must be 16-byte aligned");
+  MemReadArgs a{query, keys, values, positions, indices, out, B, H, G, CAP, D, kv_stride0, pos_stride0, dtype,
+                static_cast<cudaStream_t>(stream)};
+  return launch_mem_decode_read(a);
+}
+
+int yb_mem_decode_commit(const void *key, const void *value, const float *scores, const uint8_t *active, int64_t chunk,
+                         void *keys, void *values, float *bank_scores, int32_t *positions, void *pending_keys,
+                         void *pending_values, float *pending_scores, int64_t *count, int64_t *total,
+                         const int64_t *indices, int64_t B, int64_t G, int64_t CAP, int64_t PC, int64_t D,
+                         int64_t kv_stride0, int64_t meta_stride0, int64_t pkv_stride0, int64_t pmeta_stride0,
+                         int64_t count_stride0, int dtype, void *stream) {
+  YB_REQUIRE(dtype_ok(dtype), "mem_decode_commit: bad dtype");
+  YB_REQUIRE(B >= 0 && G > 0 && CAP > 0 && PC > 0 && D > 0, "mem_decode_commit: bad sizes");
+  YB_REQUIRE(chunk >= 1 && chunk <= PC, "mem_decode_commit: chunk=%lld must be in [1, PC=%lld]", (long long)chunk,
+             (long long)PC);
+  YB_REQUIRE(key && value && scores && active && keys && values && bank_scores && positions && pending_keys &&
+                 pending_values && pending_scores && count && total,
+             "mem_decode_commit: null tensor");
+  YB_REQUIRE(kv_stride0 >= G * CAP * D && meta_stride0 >= G * CAP && pkv_stride0 >= G * PC * D &&
+                 pmeta_stride0 >= G * PC && count_stride0 >= 1,
+             "mem_decode_commit: batch stride too small");
+  MemCommitArgs a{key, value, scores, active, chunk, keys, values, bank_scores, positions, pending_keys,
+                  pending_values, pending_scores, count, total, indices, B, G, CAP, PC, D, kv_stride0,
+                  meta_stride0, pkv_stride0, pmeta_stride0, count_stride0, dtype, static_cast<cudaStream_t>(stream)};
+  return launch_mem_decode_commit(a);
+}
+
+int yb_mem_indexed_read(const void *query, const void *key, const void *value, const int64_t *references, void *out,
+                        int64_t B, int64_t blocks, int64_t chunk, int64_t H, int64_t G, int64_t D, int64_t S,
+                        int64_t KB, int64_t CAP, int dtype, void *stream) {
+  YB_REQUIRE(dtype_ok(dtype), "mem_indexed_read: bad dtype");
+  YB_REQUIRE(B >= 0 && blocks >= 0 && chunk > 0 && H > 0 && G > 0 && D > 0 && S >= 0 && CAP > 0 && H % G == 0,
+             "mem_indexed_read: bad sizes");
+  YB_REQUIRE(KB == 1 || KB == B, "mem_indexed_read: key batch must be 1 or B");
+  YB_REQUIRE(query && key && value && references && out, "mem_indexed_read: null tensor");
+  YB_REQUIRE(aligned(query, 16) && aligned(key, 16) && aligned(value, 16) && aligned(out, 16),
+             "mem_indexed_read: tensors must be 16-byte aligned");
+  MemIndexedArgs a{query, key, value, references, out, B, blocks, chunk, H, G, D, S, KB, CAP, dtype,
+                   static_cast<cudaStream_t>(stream)};
+  return launch_mem_indexed_read(a);
+}
+
+int64_t yb_sample_workspace_bytes(int64_t B, int64_t vocab, int64_t top_k) {
+  return sample_workspace_bytes(B, vocab, top_k);
+}
+
+int yb_sample_greedy(const void *scores, int64_t row_stride, int64_t B, int64_t vocab, int dtype, int64_t *out,
+                     void *workspace, int64_t workspace_bytes, void *stream) {
+  YB_REQUIRE(dtype_ok(dtype), "sample_greedy: bad dtype");
+  YB_REQUIRE(B >= 0 && vocab > 0 && row_stride >= vocab, "sample_greedy: bad sizes");
+  YB_REQUIRE(scores && out, "sample_greedy: null tensor");
+  const int64_t need = sample_workspace_bytes(B, vocab, 1);
+  if (workspace == nullptr || workspace_bytes < need)
+    return set_error(YB_ERR_WORKSPACE, "sample_greedy: workspace of %lld bytes required", (long long)need);
+  SampleArgs a{};
+  a.scores = scores; a.row_stride = row_stride; a.B = B; a.vocab = vocab; a.dtype = dtype; a.out = out;
+  a.workspace = workspace; a.workspace_bytes = workspace_bytes; a.stream = static_cast<cudaStream_t>(stream);
+  return launch_sample_greedy(a);
+}
+
+int yb_sample_top_k_top_p_counter(const void *scores, int64_t row_stride, int64_t B, int64_t vocab, int dtype,
+                                  const int64_t *attempt_ids, const int64_t *steps, int64_t scalar_step, int64_t seed,
+                                  int64_t stream_id, float temperature, int64_t top_k, float top_p, int64_t *out,
+                                  void *workspace, int64_t workspace_bytes, void *stream) {
+  YB_REQUIRE(dtype_ok(dtype), "sample_top_k_top_p_counter: bad dtype");
+  YB_REQUIRE(B >= 0 && vocab > 0 && row_stride >= vocab, "sample_top_k_top_p_counter: bad sizes");
+  YB_REQUIRE(scores && out && attempt_ids, "sample_top_k_top_p_counter: null tensor");
+  YB_REQUIRE(temperature > 0.f && top_p > 0.f && top_p <= 1.f, "invalid top-k/top-p sampling parameters");
+  YB_REQUIRE(top_k <= vocab, "top-k exceeds the vocabulary");
+  SampleArgs a{};
+  a.scores = scores; a.row_stride = row_stride; a.B = B; a.vocab = vocab; a.dtype = dtype;
+  a.attempt_ids = attempt_ids; a.steps = steps; a.scalar_step = scalar_step; a.seed = seed; a.stream_id = stream_id;
+  a.temperature = temperature; a.top_k = top_k; a.top_p = top_p; a.out = out;
+  a.workspace = workspace; a.workspace_bytes = workspace_bytes; a.stream = static_cast<cudaStream_t>(stream);
+  if (top_k == 1) {
+    const int64_t need = sample_workspace_bytes(B, vocab, 1);
+    if (workspace == nullptr || workspace_bytes < need)
+      return set_error(YB_ERR_WORKSPACE, "sample: workspace of %lld bytes required", (long long)need);
+    return launch_sample_greedy(a);
+  }
+  if (top_k <= 0)
+    return set_error(YB_ERR_UNSUPPORTED, "sample: top_k <= 0 (whole-vocabulary sampling) is not built");
+  const int64_t need = sample_workspace_bytes(B, vocab, top_k);
+  if (workspace == nullptr || workspace_bytes < need)
+    return set_error(YB_ERR_WORKSPACE, "sample: workspace of %lld bytes required", (long long)need);
+  return launch_sample_topk_topp(a);
+}
+
+int yb_presence_penalty(void *scores, const uint8_t *seen, int64_t n, float penalty, int dtype, void *stream) {
+  YB_REQUIRE(dtype_ok(dtype), "presence_penalty: bad dtype");
+  YB_REQUIRE(n >= 0 && (n == 0 || (scores && seen)), "presence_penalty: bad arguments");
+  return launch_presence_penalty(scores, seen, n, penalty, dtype, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

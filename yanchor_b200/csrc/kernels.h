@@ -1,0 +1,99 @@
+// Internal launcher interface between the C ABI (capi.cu) and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace yb {
+
+struct GdnArgs {
+  const void *q, *k, *v;
+  int64_t q_ts, k_ts, v_ts;  // token strides (elements)
+  const void *g, *beta;
+  int64_t g_ts, beta_ts;
+  const float *A_log, *dt_bias;
+  const float *h0;
+  float *ht;
+  void *o;
+  const void *z, *norm_w;
+  float norm_eps;
+  const int64_t *cu_seqlens;
+  int64_t B, T, H, HV, K, V, N;
+  float scale;
+  int io_dtype, g_dtype, beta_dtype;
+  uint32_t flags;
+  void *workspace;
+  int64_t workspace_bytes;
+  cudaStream_t stream;
+};
+
+int launch_gdn_recurrent(const GdnArgs &a);
+int launch_gdn_chunk(const GdnArgs &a);
+int launch_gdn_chunk_simt(const GdnArgs &a);
+int64_t gdn_chunk_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t HV, int64_t K, int64_t V,
+                                  int64_t N, int io_dtype);
+
+int launch_gdn_gates(const void *b, const void *a, int64_t b_rs, int64_t a_rs, const float *A_log,
+                     const float *dt_bias, void *beta_out, float *g_out, int64_t rows, int64_t heads,
+                     int io_dtype, cudaStream_t stream);
+
+struct MemReadArgs {
+  const void *query, *keys, *values;
+  const int32_t *positions;
+  const int64_t *indices;
+  void *out;
+  int64_t B, H, G, CAP, D, kv_s0, pos_s0;
+  int dtype;
+  cudaStream_t stream;
+};
+int launch_mem_decode_read(const MemReadArgs &a);
+
+struct MemCommitArgs {
+  const void *key, *value;
+  const float *scores;
+  const uint8_t *active;
+  int64_t chunk;
+  void *keys, *values;
+  float *bank_scores;
+  int32_t *positions;
+  void *pkeys, *pvalues;
+  float *pscores;
+  int64_t *count, *total;
+  const int64_t *indices;
+  int64_t B, G, CAP, PC, D, kv_s0, meta_s0, pkv_s0, pmeta_s0, count_s0;
+  int dtype;
+  cudaStream_t stream;
+};
+int launch_mem_decode_commit(const MemCommitArgs &a);
+
+struct MemIndexedArgs {
+  const void *query, *key, *value;
+  const int64_t *refs;
+  void *out;
+  int64_t B, blocks, chunk, H, G, D, S, KB, CAP;
+  int dtype;
+  cudaStream_t stream;
+};
+int launch_mem_indexed_read(const MemIndexedArgs &a);
+
+struct SampleArgs {
+  const void *scores;
+  int64_t row_stride, B, vocab;
+  int dtype;
+  const int64_t *attempt_ids, *steps;
+  int64_t scalar_step, seed, stream_id;
+  float temperature;
+  int64_t top_k;
+  float top_p;
+  int64_t *out;
+  void *workspace;
+  int64_t workspace_bytes;
+  cudaStream_t stream;
+};
+int64_t sample_workspace_bytes(int64_t B, int64_t vocab, int64_t top_k);
+int launch_sample_greedy(const SampleArgs &a);
+int launch_sample_topk_topp(const SampleArgs &a);
+int launch_presence_penalty(void *scores, const uint8_t *seen, int64_t n, float penalty, int dtype,
+                            cudaStream_t stream);
+
+}  // namespace yb

@@ -1,0 +1,453 @@
+// Anchor memory ("independent GQA memory") kernels: decode read, decode
+// write/commit and the prefill indexed read.
+//
+// Semantics follow modeling_yanchor.py:22-42 (indexed read), :51-63 (top-k
+// selection order) and :277-313 (decode read / commit), and the Triton
+// kernels of runtime/model/independent_memory.py.  Every softmax includes
+// the null slot: one extra logit 0 whose value row is zero.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace yb {
+namespace {
+
+// ---------------------------------------------------------------------------
+// Decode read: one CTA per (request row, group).  R = H / G query rows read
+// the CAP committed slots of their group.
+// ---------------------------------------------------------------------------
+constexpr int kReadThreads = 128;
+
+template <typename T, int R, int D>
+__global__ void __launch_bounds__(kReadThreads) mem_decode_read_kernel(const MemReadArgs a) {
+  constexpr int NW = kReadThreads / 32;
+  constexpr int DL = D / 8;  // lanes covering one row (8 elements each)
+  static_assert(D % 8 == 0 && DL <= 32, "D must be a multiple of 8, at most 256");
+  extern __shared__ __align__(16) float rsm[];
+  const int CAP = int(a.CAP);
+  float *sq = rsm;                // [R][D]
+  float *sw = sq + R * D;         // [R][CAP] logits -> weights
+  float *part = sw + R * CAP;     // [NW][R][D] partial outputs
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t row = blockIdx.x / a.G;
+  const int g = int(blockIdx.x % a.G);
+  const int64_t s = a.indices ? a.indices[row] : row;
+  const T *qp = static_cast<const T *>(a.query) + (row * a.H + int64_t(g) * R) * D;
+  T *outp = static_cast<T *>(a.out) + (row * a.H + int64_t(g) * R) * D;
+  if (s < 0) {  // skipped request: zeros
+    for (int e = tid; e < R * D; e += kReadThreads) outp[e] = from_f<T>(0.f);
+    return;
+  }
+  const T *kp = static_cast<const T *>(a.keys) + s * a.kv_s0 + int64_t(g) * CAP * D;
+  const T *vp = static_cast<const T *>(a.values) + s * a.kv_s0 + int64_t(g) * CAP * D;
+  const int32_t *pp = a.positions + s * a.pos_s0 + int64_t(g) * CAP;
+  for (int e = tid; e < R * D; e += kReadThreads) sq[e] = to_f(qp[e]);
+  __syncthreads();
+  const float scale = rsqrtf(float(D));
+  // logits: a warp per slot, lanes split D
+  for (int slot = warp; slot < CAP; slot += NW) {
+    float kv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (lane < DL) load8(kp + int64_t(slot) * D + lane * 8, kv);
+    const bool valid = pp[slot] >= 0;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      float acc = 0.f;
+      if (lane < DL) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc = fmaf(sq[r * D + lane * 8 + j], kv[j], acc);
+      }
+      acc = warp_sum(acc);
+      if (lane == 0) sw[r * CAP + slot] = valid ? acc * scale : -INFINITY;
+    }
+  }
+  __syncthreads();
+  // softmax with the null logit 0: a warp per query row
+  for (int r = warp; r < R; r += NW) {
+    float m = 0.f;
+    for (int j = lane; j < CAP; j += 32) m = fmaxf(m, sw[r * CAP + j]);
+    m = warp_max(m);
+    float den = 0.f;
+    for (int j = lane; j < CAP; j += 32) {
+      const float e = expf(sw[r * CAP + j] - m);
+      sw[r * CAP + j] = e;
+      den += e;
+    }
+    den = warp_sum(den) + expf(-m);
+    const float inv = 1.f / den;
+    for (int j = lane; j < CAP; j += 32) sw[r * CAP + j] *= inv;
+  }
+  __syncthreads();
+  // weighted values: each warp takes a strided subset of slots; lanes split D
+  if (lane < DL) {
+    float acc[R][8];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[r][j] = 0.f;
+    for (int slot = warp; slot < CAP; slot += NW) {
+      float vv[8];
+      load8(vp + int64_t(slot) * D + lane * 8, vv);
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const float w = sw[r * CAP + slot];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[r][j] = fmaf(w, vv[j], acc[r][j]);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) part[(warp * R + r) * D + lane * 8 + j] = acc[r][j];
+  }
+  __syncthreads();
+  for (int e = tid; e < R * D; e += kReadThreads) {
+    float x = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) x += part[w * R * D + e];
+    outp[e] = from_f<T>(x);
+  }
+}
+
+template <typename T, int R>
+int launch_read_r(const MemReadArgs &a) {
+  const size_t smem = sizeof(float) * (R * a.D + R * a.CAP + (kReadThreads / 32) * R * a.D);
+  dim3 grid(unsigned(a.B * a.G));
+  switch (a.D) {
+#define YB_READ_CASE(DD)                                                                           \
+  case DD: {                                                                                       \
+    auto kern = mem_decode_read_kernel<T, R, DD>;                                                  \
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)); \
+    kern<<<grid, kReadThreads, smem, a.stream>>>(a);                                               \
+    return check_launch("mem_decode_read_kernel");                                                 \
+  }
+    YB_READ_CASE(64)
+    YB_READ_CASE(128)
+    YB_READ_CASE(256)
+#undef YB_READ_CASE
+  }
+  return set_error(YB_ERR_UNSUPPORTED, "memory read: D=%lld not built (64/128/256)", (long long)a.D);
+}
+
+template <typename T>
+int launch_read_t(const MemReadArgs &a) {
+  switch (a.H / a.G) {
+    case 1: return launch_read_r<T, 1>(a);
+    case 2: return launch_read_r<T, 2>(a);
+    case 4: return launch_read_r<T, 4>(a);
+    case 8: return launch_read_r<T, 8>(a);
+  }
+  return set_error(YB_ERR_UNSUPPORTED, "memory read: H/G=%lld not built (1/2/4/8)", (long long)(a.H / a.G));
+}
+
+// ---------------------------------------------------------------------------
+// Decode commit: one CTA per request row, looping over groups.
+// Candidates are the CAP bank slots followed by the `chunk` pending slots.
+// Order: score descending, then position ascending (invalid last), then
+// candidate index — the stable double argsort of select_topk.  Invalid
+// winners get position -1 and copy bank slot 0, as the reference's
+// gather with references clamped at 0 does.
+// ---------------------------------------------------------------------------
+constexpr int kCommitThreads = 256;
+constexpr int kMaxCand = 512;
+
+__device__ __forceinline__ bool cand_before(float sa, int64_t pa, int ia, float sb, int64_t pb, int ib) {
+  if (sa != sb) return sa > sb;  // -0.0 == 0.0, as in a float sort
+  if (pa != pb) return pa < pb;
+  return ia < ib;
+}
+
+template <typename T>
+__device__ void commit_gather(T *bank, const T *pend, T *stage, const int *sel, const int64_t *pkey, int g,
+                              int CAP, int PC, int D) {
+  const int tid = threadIdx.x;
+  for (int e = tid; e < CAP * D; e += kCommitThreads) {
+    const int r = e / D, d = e % D;
+    const int c = sel[r];
+    const int src = pkey[c] == INT64_MAX ? 0 : c;
+    stage[e] = src < CAP ? bank[(int64_t(g) * CAP + src) * D + d] : pend[(int64_t(g) * PC + src - CAP) * D + d];
+  }
+  __syncthreads();
+  for (int e = tid; e < CAP * D; e += kCommitThreads) bank[int64_t(g) * CAP * D + e] = stage[e];
+  __syncthreads();
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kCommitThreads) mem_decode_commit_kernel(const MemCommitArgs a) {
+  __shared__ float c_score[kMaxCand];
+  __shared__ int64_t c_pkey[kMaxCand];  // position, INT64_MAX for an invalid slot
+  __shared__ int sel[kMaxCand];         // new slot -> winning candidate
+  extern __shared__ __align__(16) unsigned char cm_raw[];
+  T *stage = reinterpret_cast<T *>(cm_raw);  // [CAP][D]
+  const int tid = threadIdx.x;
+  const int64_t row = blockIdx.x;
+  const int64_t s = a.indices ? a.indices[row] : row;
+  if (s < 0 || !a.active[row]) return;
+  const int CAP = int(a.CAP), D = int(a.D), chunk = int(a.chunk), G = int(a.G), PC = int(a.PC);
+  const int64_t count = a.count[s * a.count_s0];
+  const int64_t total = a.total[s * a.count_s0];
+  const bool commit = count + 1 == chunk;
+  const T *key = static_cast<const T *>(a.key) + row * G * D;
+  const T *val = static_cast<const T *>(a.value) + row * G * D;
+  T *bank_k = static_cast<T *>(a.keys) + s * a.kv_s0;
+  T *bank_v = static_cast<T *>(a.values) + s * a.kv_s0;
+  T *pend_k = static_cast<T *>(a.pkeys) + s * a.pkv_s0;
+  T *pend_v = static_cast<T *>(a.pvalues) + s * a.pkv_s0;
+  float *bscore = a.bank_scores + s * a.meta_s0;
+  int32_t *bpos = a.positions + s * a.meta_s0;
+  float *pscore = a.pscores + s * a.pmeta_s0;
+
+  // push into pending slot `count`
+  for (int e = tid; e < G * D; e += kCommitThreads) {
+    const int g = e / D, d = e % D;
+    pend_k[(int64_t(g) * PC + count) * D + d] = key[e];
+    pend_v[(int64_t(g) * PC + count) * D + d] = val[e];
+  }
+  if (tid < G) pscore[int64_t(tid) * PC + count] = a.scores[row * G + tid];
+  if (commit) {
+    const int n = CAP + chunk;
+    for (int g = 0; g < G; ++g) {
+      __syncthreads();  // pushes visible; previous group finished
+      for (int c = tid; c < n; c += kCommitThreads) {
+        if (c < CAP) {
+          const int32_t pos = bpos[int64_t(g) * CAP + c];
+          c_score[c] = bscore[int64_t(g) * CAP + c];
+          c_pkey[c] = pos < 0 ? INT64_MAX : int64_t(pos);
+        } else {
+          const int i = c - CAP;  // every pending slot is filled when committing
+          c_score[c] = pscore[int64_t(g) * PC + i];
+          c_pkey[c] = total - count + i;
+        }
+      }
+      __syncthreads();
+      for (int c = tid; c < n; c += kCommitThreads) {
+        const float sc = c_score[c];
+        const int64_t pk = c_pkey[c];
+        int rank = 0;
+        for (int o = 0; o < n; ++o) rank += cand_before(c_score[o], c_pkey[o], o, sc, pk, c);
+        if (rank < CAP) sel[rank] = c;
+      }
+      __syncthreads();
+      commit_gather(bank_k, pend_k, stage, sel, c_pkey, g, CAP, PC, D);
+      commit_gather(bank_v, pend_v, stage, sel, c_pkey, g, CAP, PC, D);
+      for (int r = tid; r < CAP; r += kCommitThreads) {
+        const int c = sel[r];
+        bscore[int64_t(g) * CAP + r] = c_score[c];
+        bpos[int64_t(g) * CAP + r] = c_pkey[c] == INT64_MAX ? -1 : int32_t(c_pkey[c]);
+      }
+    }
+  }
+  __syncthreads();  // every thread has read count / total
+  if (tid == 0) {
+    a.count[s * a.count_s0] = commit ? 0 : count + 1;
+    a.total[s * a.count_s0] = total + 1;
+  }
+}
+
+template <typename T>
+int launch_commit_t(const MemCommitArgs &a) {
+  const size_t smem = sizeof(T) * a.CAP * a.D;
+  auto kern = mem_decode_commit_kernel<T>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "memory commit: smem attribute: %s", cudaGetErrorString(e));
+  }
+  kern<<<unsigned(a.B), kCommitThreads, smem, a.stream>>>(a);
+  return check_launch("mem_decode_commit_kernel");
+}
+
+// ---------------------------------------------------------------------------
+// Prefill indexed read: one CTA per (row, block, group).  The referenced key
+// and value rows are gathered once into shared memory; each warp then takes
+// one chunk position at a time and computes the R heads of the group.
+// ---------------------------------------------------------------------------
+constexpr int kIdxThreads = 256;
+constexpr int kIdxMaxCap = 128;
+
+template <typename T, int R, int D>
+__global__ void __launch_bounds__(kIdxThreads) mem_indexed_read_kernel(const MemIndexedArgs a) {
+  constexpr int PITCH = D + 16 / int(sizeof(T));  // pad each row by 16 bytes (bank spread)
+  constexpr int NW = kIdxThreads / 32;
+  constexpr int DL = D / 8;
+  constexpr int SL = kIdxMaxCap / 32;  // slots per lane (max)
+  extern __shared__ __align__(16) unsigned char ir_raw[];
+  const int CAP = int(a.CAP);
+  T *sk = reinterpret_cast<T *>(ir_raw);     // [CAP][PITCH]
+  T *sv = sk + CAP * PITCH;                  // [CAP][PITCH]
+  float *sq = reinterpret_cast<float *>(sv + CAP * PITCH);  // [NW][R][D]
+  __shared__ int svalid[kIdxMaxCap];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t gid = blockIdx.x;
+  const int g = int(gid % a.G);
+  const int64_t blk = (gid / a.G) % a.blocks;
+  const int64_t b = gid / (a.G * a.blocks);
+  const int64_t kb = a.KB == 1 ? 0 : b;
+  const int64_t *refs = a.refs + gid * CAP;
+  const T *kbase = static_cast<const T *>(a.key);
+  const T *vbase = static_cast<const T *>(a.value);
+  // gather referenced rows (16-byte vectors)
+  for (int e = tid; e < CAP * (D / 8); e += kIdxThreads) {
+    const int slot = e / (D / 8), d8 = (e % (D / 8)) * 8;
+    const int64_t ref = refs[slot];
+    float kx[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, vx[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (ref >= 0) {
+      const int64_t off = ((kb * a.S + ref) * a.G + g) * D + d8;
+      load8(kbase + off, kx);
+      load8(vbase + off, vx);
+    }
+    store8(sk + slot * PITCH + d8, kx);
+    store8(sv + slot * PITCH + d8, vx);
+    if (d8 == 0) svalid[slot] = ref >= 0;
+  }
+  __syncthreads();
+  const float scale = rsqrtf(float(D));
+  const T *qbase = static_cast<const T *>(a.query);
+  T *obase = static_cast<T *>(a.out);
+  float *myq = sq + warp * R * D;
+  for (int c = warp; c < a.chunk; c += NW) {
+    const int64_t qrow = ((b * a.blocks + blk) * a.chunk + c) * a.H + int64_t(g) * R;  // first head row
+    for (int e = lane; e < R * D; e += 32) myq[e] = to_f(qbase[qrow * D + e]);
+    __syncwarp();
+    // logits: lane owns slots lane, lane + 32, ...
+    float lg[R][SL];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int j = 0; j < SL; ++j) lg[r][j] = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < SL; ++j) {
+      const int slot = lane + 32 * j;
+      if (slot < CAP && svalid[slot]) {
+        float acc[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) acc[r] = 0.f;
+        for (int d = 0; d < D; d += 8) {
+          float kx[8];
+          load8(sk + slot * PITCH + d, kx);
+#pragma unroll
+          for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int t = 0; t < 8; ++t) acc[r] = fmaf(myq[r * D + d + t], kx[t], acc[r]);
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) lg[r][j] = acc[r] * scale;
+      }
+    }
+    // softmax with the null logit 0
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      float m = 0.f;
+#pragma unroll
+      for (int j = 0; j < SL; ++j) m = fmaxf(m, lg[r][j]);
+      m = warp_max(m);
+      float den = 0.f;
+#pragma unroll
+      for (int j = 0; j < SL; ++j) {
+        lg[r][j] = expf(lg[r][j] - m);
+        den += lg[r][j];
+      }
+      const float inv = 1.f / (warp_sum(den) + expf(-m));
+#pragma unroll
+      for (int j = 0; j < SL; ++j) lg[r][j] *= inv;
+    }
+    // weighted values: lanes split D
+    float acc[R][8];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int t = 0; t < 8; ++t) acc[r][t] = 0.f;
+#pragma unroll
+    for (int j = 0; j < SL; ++j) {
+      for (int src = 0; src < 32; ++src) {
+        const int slot = src + 32 * j;
+        if (slot >= CAP) break;
+        float w[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) w[r] = __shfl_sync(0xffffffffu, lg[r][j], src);
+        if (lane < DL) {
+          float vx[8];
+          load8(sv + slot * PITCH + lane * 8, vx);
+#pragma unroll
+          for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int t = 0; t < 8; ++t) acc[r][t] = fmaf(w[r], vx[t], acc[r][t]);
+        }
+      }
+    }
+    if (lane < DL) {
+#pragma unroll
+      for (int r = 0; r < R; ++r) store8(obase + (qrow + r) * D + lane * 8, acc[r]);
+    }
+    __syncwarp();
+  }
+}
+
+template <typename T, int R>
+int launch_indexed_r(const MemIndexedArgs &a) {
+  dim3 grid(unsigned(a.B * a.blocks * a.G));
+  switch (a.D) {
+#define YB_IDX_CASE(DD)                                                                                 \
+  case DD: {                                                                                            \
+    constexpr int PITCH = DD + 16 / int(sizeof(T));                                                     \
+    const size_t smem = 2 * sizeof(T) * a.CAP * PITCH + sizeof(float) * (kIdxThreads / 32) * R * DD;    \
+    auto kern = mem_indexed_read_kernel<T, R, DD>;                                                      \
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)); \
+    if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "indexed read: smem attribute: %s", cudaGetErrorString(e)); \
+    kern<<<grid, kIdxThreads, smem, a.stream>>>(a);                                                     \
+    return check_launch("mem_indexed_read_kernel");                                                     \
+  }
+    YB_IDX_CASE(64)
+    YB_IDX_CASE(128)
+    YB_IDX_CASE(256)
+#undef YB_IDX_CASE
+  }
+  return set_error(YB_ERR_UNSUPPORTED, "indexed read: D=%lld not built (64/128/256)", (long long)a.D);
+}
+
+template <typename T>
+int launch_indexed_t(const MemIndexedArgs &a) {
+  switch (a.H / a.G) {
+    case 1: return launch_indexed_r<T, 1>(a);
+    case 2: return launch_indexed_r<T, 2>(a);
+    case 4: return launch_indexed_r<T, 4>(a);
+    case 8: return launch_indexed_r<T, 8>(a);
+  }
+  return set_error(YB_ERR_UNSUPPORTED, "indexed read: H/G=%lld not built (1/2/4/8)", (long long)(a.H / a.G));
+}
+
+}  // namespace
+
+int launch_mem_decode_read(const MemReadArgs &a) {
+  if (a.B * a.G == 0) return YB_OK;
+  switch (a.dtype) {
+    case YB_F32: return launch_read_t<float>(a);
+    case YB_BF16: return launch_read_t<__nv_bfloat16>(a);
+    case YB_F16: return launch_read_t<__half>(a);
+  }
+  return set_error(YB_ERR_ARGUMENT, "memory read: bad dtype %d", a.dtype);
+}
+
+int launch_mem_decode_commit(const MemCommitArgs &a) {
+  if (a.B == 0) return YB_OK;
+  if (a.CAP + a.chunk > kMaxCand)
+    return set_error(YB_ERR_UNSUPPORTED, "memory commit: CAP + chunk = %lld exceeds %d",
+                     (long long)(a.CAP + a.chunk), kMaxCand);
+  switch (a.dtype) {
+    case YB_F32: return launch_commit_t<float>(a);
+    case YB_BF16: return launch_commit_t<__nv_bfloat16>(a);
+    case YB_F16: return launch_commit_t<__half>(a);
+  }
+  return set_error(YB_ERR_ARGUMENT, "memory commit: bad dtype %d", a.dtype);
+}
+
+int launch_mem_indexed_read(const MemIndexedArgs &a) {
+  if (a.B * a.blocks * a.G == 0) return YB_OK;
+  if (a.CAP > kIdxMaxCap)
+    return set_error(YB_ERR_UNSUPPORTED, "indexed read: CAP=%lld exceeds %d", (long long)a.CAP, kIdxMaxCap);
+  switch (a.dtype) {
+    case YB_F32: return launch_indexed_t<float>(a);
+    case YB_BF16: return launch_indexed_t<__nv_bfloat16>(a);
+    case YB_F16: return launch_indexed_t<__half>(a);
+  }
+  return set_error(YB_ERR_ARGUMENT, "indexed read: bad dtype %d", a.dtype);
+}
+
+}  // namespace yb

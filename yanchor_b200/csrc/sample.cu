@@ -1,0 +1,489 @@
+// Final-logit sampling: greedy argmax and the top-k / top-p counter sampler,
+// plus the dense presence penalty and the GDN gate kernel.
+//
+// Sampling follows runtime/model/inference_kernels.py:24-88: top-k of the
+// (temperature-scaled) scores, softmax, top-p truncation (keep while the
+// running sum before an entry is below top_p), renormalise, then the inverse
+// CDF with the stateless counter uniform of (attempt id, step, seed, stream).
+// Ties inside the top-k are ordered by ascending vocabulary index.
+//
+// Both samplers split each row over several CTAs: the first pass writes
+// per-split candidates to the caller's workspace and the second reduces them
+// per row, so a batch of 64 rows still fills the GPU.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace yb {
+namespace {
+
+constexpr int kNT = 256;
+constexpr int kMaxTopK = 256;
+constexpr int kTopkSpan = 16384;  // elements per CTA in the top-k first pass
+
+struct Cand {
+  float v;
+  int32_t pad;
+  int64_t i;
+};
+static_assert(sizeof(Cand) == 16, "candidate record is 16 bytes");
+
+// Order-preserving map float -> uint32 (larger float, larger key).
+__device__ __forceinline__ uint32_t fkey(float x) {
+  const uint32_t b = __float_as_uint(x);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+__device__ __forceinline__ bool better(float v, int64_t i, float bv, int64_t bi) {
+  return v > bv || (v == bv && i < bi);
+}
+
+int greedy_splits(int64_t B, int64_t vocab) {
+  int64_t s = (296 + B - 1) / B;
+  const int64_t cap = (vocab + 2047) / 2048;
+  if (s > cap) s = cap;
+  return int(s < 1 ? 1 : s);
+}
+int topk_splits(int64_t vocab, int64_t k) {
+  int64_t s = (vocab + kTopkSpan - 1) / kTopkSpan;
+  while (s > 1 && vocab / s < k) --s;  // every split holds at least k entries
+  return int(s < 1 ? 1 : s);
+}
+
+// Range [lo, hi) of split `split` out of `splits` over n elements.
+__host__ __device__ __forceinline__ void split_range(int64_t n, int splits, int split, int64_t &lo, int64_t &hi) {
+  lo = n * split / splits;
+  hi = n * (split + 1) / splits;
+}
+
+// ---------------------------------------------------------------- greedy ----
+template <typename T>
+__global__ void __launch_bounds__(kNT) greedy_partial_kernel(const T *scores, int64_t row_stride, int64_t vocab,
+                                                             int splits, Cand *ws) {
+  const int split = blockIdx.x;
+  const int64_t b = blockIdx.y;
+  int64_t lo, hi;
+  split_range(vocab, splits, split, lo, hi);
+  const T *row = scores + b * row_stride;
+  float best = -INFINITY;
+  int64_t bi = INT64_MAX;
+  constexpr int VEC = 16 / sizeof(T);
+  // align the vector part to 16 bytes
+  int64_t head = lo;
+  while (head < hi && (reinterpret_cast<uintptr_t>(row + head) & 15)) ++head;
+  for (int64_t j = lo + threadIdx.x; j < head; j += kNT) {
+    const float x = to_f(row[j]);
+    if (better(x, j, best, bi)) { best = x; bi = j; }
+  }
+  const int64_t nvec = (hi - head) / VEC;
+  for (int64_t u = threadIdx.x; u < nvec; u += kNT) {
+    const int64_t i = head + u * VEC;
+    float x[VEC];
+    if constexpr (VEC == 4) load4(reinterpret_cast<const float *>(row + i), x);
+    else load8(row + i, x);
+#pragma unroll
+    for (int t = 0; t < VEC; ++t)
+      if (better(x[t], i + t, best, bi)) { best = x[t]; bi = i + t; }
+  }
+  for (int64_t j = head + nvec * VEC + threadIdx.x; j < hi; j += kNT) {
+    const float x = to_f(row[j]);
+    if (better(x, j, best, bi)) { best = x; bi = j; }
+  }
+  __shared__ float sv[kNT / 32];
+  __shared__ int64_t si[kNT / 32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (better(ov, oi, best, bi)) { best = ov; bi = oi; }
+  }
+  if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = best; si[threadIdx.x >> 5] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kNT / 32; ++w)
+      if (better(sv[w], si[w], best, bi)) { best = sv[w]; bi = si[w]; }
+    Cand c;
+    c.v = best; c.pad = 0; c.i = bi;
+    ws[b * splits + split] = c;
+  }
+}
+
+__global__ void greedy_final_kernel(const Cand *ws, int splits, int64_t B, int64_t *out) {
+  const int64_t b = int64_t(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (b >= B) return;
+  float best = -INFINITY;
+  int64_t bi = INT64_MAX;
+  for (int s = lane; s < splits; s += 32) {
+    const Cand c = ws[b * splits + s];
+    if (better(c.v, c.i, best, bi)) { best = c.v; bi = c.i; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (better(ov, oi, best, bi)) { best = ov; bi = oi; }
+  }
+  if (lane == 0) out[b] = bi == INT64_MAX ? 0 : bi;
+}
+
+// ------------------------------------------------------ block radix select ---
+// Among the n keys in shared memory find the K-th largest key `thr` (1 <= K
+// <= n) and the number `gt` of keys strictly above it.  Four 8-bit passes;
+// warp-aggregated shared-memory histograms.
+__device__ void radix_select(const uint32_t *keys, int n, int K, int *hist, uint32_t &thr, int &gt) {
+  __shared__ int s_digit, s_above;
+  uint32_t prefix = 0, mask = 0;
+  int remaining = K, above = 0;
+  const int lane = threadIdx.x & 31;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = threadIdx.x; i < 256; i += kNT) hist[i] = 0;
+    __syncthreads();
+    for (int base = 0; base < n; base += kNT) {
+      const int i = base + threadIdx.x;
+      int digit = -1;
+      if (i < n) {
+        const uint32_t k = keys[i];
+        if ((k & mask) == prefix) digit = int((k >> shift) & 255u);
+      }
+      const unsigned peers = __match_any_sync(0xffffffffu, digit);
+      if (digit >= 0 && lane == __ffs(peers) - 1) atomicAdd(&hist[digit], __popc(peers));
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int acc = 0, d = 255;
+      for (; d > 0; --d) {
+        if (acc + hist[d] >= remaining) break;
+        acc += hist[d];
+      }
+      s_digit = d;
+      s_above = acc;
+    }
+    __syncthreads();
+    prefix |= uint32_t(s_digit) << shift;
+    mask |= 255u << shift;
+    remaining -= s_above;
+    above += s_above;
+    __syncthreads();
+  }
+  thr = prefix;
+  gt = above;
+}
+
+// Exclusive block scan of one int per thread; returns the block total.
+__device__ int block_exclusive_scan(int x, int &total) {
+  __shared__ int warp_tot[kNT / 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int inc = x;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += y;
+  }
+  if (lane == 31) warp_tot[warp] = inc;
+  __syncthreads();
+  int offset = 0, tot = 0;
+#pragma unroll
+  for (int w = 0; w < kNT / 32; ++w) {
+    if (w < warp) offset += warp_tot[w];
+    tot += warp_tot[w];
+  }
+  __syncthreads();
+  total = tot;
+  return offset + inc - x;
+}
+
+// Select the K largest of n (value, index) entries held in shared memory
+// (keys = fkey(value)); ties at the threshold go to the smallest indices.
+// Entries are scanned in the given order; when `index_ordered` is true the
+// storage order is ascending index, so the first `need` ties in storage order
+// are the smallest indices.  Writes K candidates to `outc` (any order).
+__device__ void select_k(const uint32_t *keys, const float *vals, const int64_t *idx, int n, int K,
+                         bool index_ordered, int *hist, Cand *outc) {
+  uint32_t thr;
+  int gt;
+  radix_select(keys, n, K, hist, thr, gt);
+  const int need = K - gt;  // ties to take
+  const int per = (n + kNT - 1) / kNT;
+  const int lo = min(n, int(threadIdx.x) * per), hi = min(n, lo + per);
+  int cg = 0, ce = 0;
+  for (int i = lo; i < hi; ++i) {
+    cg += keys[i] > thr;
+    ce += keys[i] == thr;
+  }
+  int tg, te;
+  int og = block_exclusive_scan(cg, tg);
+  int oe = block_exclusive_scan(ce, te);
+  for (int i = lo; i < hi; ++i) {
+    const uint32_t k = keys[i];
+    if (k > thr) {
+      Cand c;
+      c.v = vals[i]; c.pad = 0; c.i = idx[i];
+      outc[og++] = c;
+    } else if (k == thr) {
+      int rank = oe;
+      if (!index_ordered) {  // rank among ties by index
+        rank = 0;
+        for (int j = 0; j < n; ++j) rank += keys[j] == thr && idx[j] < idx[i];
+      }
+      if (rank < need) {
+        Cand c;
+        c.v = vals[i]; c.pad = 0; c.i = idx[i];
+        outc[gt + rank] = c;
+      }
+      ++oe;
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kNT) topk_partial_kernel(const T *scores, int64_t row_stride, int64_t vocab,
+                                                           int splits, int K, Cand *ws) {
+  extern __shared__ __align__(16) unsigned char tk_raw[];
+  uint32_t *keys = reinterpret_cast<uint32_t *>(tk_raw);       // [span]
+  float *vals = reinterpret_cast<float *>(keys + kTopkSpan);   // [span]
+  __shared__ int hist[256];
+  const int split = blockIdx.x;
+  const int64_t b = blockIdx.y;
+  int64_t lo, hi;
+  split_range(vocab, splits, split, lo, hi);
+  const int n = int(hi - lo);
+  const T *row = scores + b * row_stride;
+  for (int i = threadIdx.x; i < n; i += kNT) {
+    const float x = to_f(row[lo + i]);
+    vals[i] = x;
+    keys[i] = fkey(x);
+  }
+  __syncthreads();
+  // indices are implicit (lo + i): pass a null index array through a lambda-free path
+  uint32_t thr;
+  int gt;
+  radix_select(keys, n, K, hist, thr, gt);
+  const int need = K - gt;
+  const int per = (n + kNT - 1) / kNT;
+  const int a0 = min(n, int(threadIdx.x) * per), a1 = min(n, a0 + per);
+  int cg = 0, ce = 0;
+  for (int i = a0; i < a1; ++i) {
+    cg += keys[i] > thr;
+    ce += keys[i] == thr;
+  }
+  int tg, te;
+  int og = block_exclusive_scan(cg, tg);
+  int oe = block_exclusive_scan(ce, te);
+  Cand *outc = ws + (b * splits + split) * int64_t(K);
+  for (int i = a0; i < a1; ++i) {
+    const uint32_t k = keys[i];
+    if (k > thr || (k == thr && oe < need)) {
+      Cand c;
+      c.v = vals[i]; c.pad = 0; c.i = lo + i;
+      outc[k > thr ? og : gt + oe] = c;
+    }
+    og += k > thr;
+    oe += k == thr;
+  }
+}
+
+// counter uniform of (attempt id, step, seed, stream): uint32 hash -> (w + 0.5) / 2^32
+__device__ __forceinline__ float counter_uniform(int64_t attempt, int64_t step, int64_t seed, int64_t stream) {
+  const uint32_t id = uint32_t(attempt), st = uint32_t(step);
+  uint32_t state = id * 747796405u + st * 289133645u + uint32_t(seed) * 277803737u + uint32_t(stream) * 144269504u;
+  const uint32_t shift = (state >> 28) + 4u;
+  uint32_t word = ((state >> shift) ^ state) * 277803737u;
+  word = (word >> 22) ^ word;
+  const float u = float((double(word) + 0.5) / 4294967296.0);
+  const float limit = 1.0f - 5.9604645e-08f;  // 1 - eps(float32) / 2
+  return fminf(u, limit);
+}
+
+__global__ void __launch_bounds__(kNT) topk_final_kernel(const Cand *ws, int splits, int K, const int64_t *attempt,
+                                                         const int64_t *steps, int64_t scalar_step, int64_t seed,
+                                                         int64_t stream_id, float temperature, float top_p,
+                                                         int64_t *out) {
+  extern __shared__ __align__(16) unsigned char tf_raw[];
+  const int M = splits * K;
+  uint32_t *keys = reinterpret_cast<uint32_t *>(tf_raw);  // [M]
+  float *vals = reinterpret_cast<float *>(keys + M);      // [M]
+  int64_t *idx = reinterpret_cast<int64_t *>(vals + M + (M & 1));  // [M] (8-byte aligned)
+  __shared__ int hist[256];
+  __shared__ Cand sel[kMaxTopK];
+  __shared__ float sv[kMaxTopK];
+  __shared__ int64_t si[kMaxTopK];
+  const int64_t b = blockIdx.x;
+  for (int i = threadIdx.x; i < M; i += kNT) {
+    const Cand c = ws[b * M + i];
+    vals[i] = c.v;
+    idx[i] = c.i;
+    keys[i] = fkey(c.v);
+  }
+  __syncthreads();
+  select_k(keys, vals, idx, M, K, false, hist, sel);
+  __syncthreads();
+  // sort the K winners: value descending, index ascending
+  for (int i = threadIdx.x; i < K; i += kNT) {
+    const float v = sel[i].v;
+    const int64_t ix = sel[i].i;
+    int rank = 0;
+    for (int j = 0; j < K; ++j) rank += better(sel[j].v, sel[j].i, v, ix);
+    sv[rank] = v;
+    si[rank] = ix;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // softmax of values / temperature (the division is monotone, so top-k is unchanged)
+    const float m = sv[0] / temperature;
+    float tot = 0.f;
+    for (int i = 0; i < K; ++i) {
+      const float e = expf(sv[i] / temperature - m);
+      sv[i] = e;
+      tot += e;
+    }
+    for (int i = 0; i < K; ++i) sv[i] /= tot;
+    // top-p: keep while the running sum before the entry is below top_p
+    double run = 0.0;
+    float kept = 0.f;
+    for (int i = 0; i < K; ++i) {
+      const float p = sv[i];
+      const bool keep = float(float(run + p) - p) < top_p;
+      run += p;
+      sv[i] = keep ? p : 0.f;
+      kept += sv[i];
+    }
+    for (int i = 0; i < K; ++i) sv[i] /= kept;
+    float tot2 = 0.f;
+    for (int i = 0; i < K; ++i) tot2 += sv[i];
+    for (int i = 0; i < K; ++i) sv[i] /= tot2;
+    // inverse CDF with the counter uniform
+    double cum = 0.0;
+    float last = 0.f;
+    for (int i = 0; i < K; ++i) {
+      cum += sv[i];
+      sv[i] = float(cum);
+      last = sv[i];
+    }
+    const float u = counter_uniform(attempt[b], steps ? steps[b] : scalar_step, seed, stream_id);
+    const float thr = fminf(u * last, nextafterf(last, 0.f));
+    int rank = 0;
+    while (rank < K - 1 && sv[rank] < thr) ++rank;
+    out[b] = si[rank];
+  }
+}
+
+// ---------------------------------------------------------------- misc ------
+template <typename T>
+__global__ void presence_kernel(T *scores, const uint8_t *seen, int64_t n, float penalty) {
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
+    if (seen[i]) scores[i] = from_f<T>(to_f(scores[i]) - penalty);
+}
+
+template <typename T>
+__global__ void gates_kernel(const T *b, const T *a, int64_t b_rs, int64_t a_rs, const float *A_log,
+                             const float *dt_bias, T *beta, float *g, int64_t rows, int64_t heads) {
+  const int64_t n = rows * heads;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = i / heads, h = i % heads;
+    const float bb = to_f(b[r * b_rs + h]);
+    const float aa = to_f(a[r * a_rs + h]);
+    beta[i] = from_f<T>(sigmoidf_(bb));
+    g[i] = -expf(A_log[h]) * softplus20(aa + (dt_bias ? dt_bias[h] : 0.f));
+  }
+}
+
+template <typename T>
+int greedy_t(const SampleArgs &a) {
+  const int splits = greedy_splits(a.B, a.vocab);
+  Cand *ws = static_cast<Cand *>(a.workspace);
+  greedy_partial_kernel<T><<<dim3(splits, unsigned(a.B)), kNT, 0, a.stream>>>(static_cast<const T *>(a.scores),
+                                                                               a.row_stride, a.vocab, splits, ws);
+  int rc = check_launch("greedy_partial_kernel");
+  if (rc) return rc;
+  greedy_final_kernel<<<unsigned((a.B + 7) / 8), 256, 0, a.stream>>>(ws, splits, a.B, a.out);
+  return check_launch("greedy_final_kernel");
+}
+
+template <typename T>
+int topk_t(const SampleArgs &a) {
+  const int K = int(a.top_k);
+  const int splits = topk_splits(a.vocab, K);
+  Cand *ws = static_cast<Cand *>(a.workspace);
+  const size_t smem1 = size_t(kTopkSpan) * 8;
+  auto k1 = topk_partial_kernel<T>;
+  cudaError_t e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem1));
+  if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "topk: smem attribute: %s", cudaGetErrorString(e));
+  k1<<<dim3(splits, unsigned(a.B)), kNT, smem1, a.stream>>>(static_cast<const T *>(a.scores), a.row_stride, a.vocab,
+                                                           splits, K, ws);
+  int rc = check_launch("topk_partial_kernel");
+  if (rc) return rc;
+  const int M = splits * K;
+  const size_t smem2 = size_t(M) * 8 + size_t(M + 1) * 8;
+  e = cudaFuncSetAttribute(topk_final_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem2));
+  if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "topk: smem attribute: %s", cudaGetErrorString(e));
+  topk_final_kernel<<<unsigned(a.B), kNT, smem2, a.stream>>>(ws, splits, K, a.attempt_ids, a.steps, a.scalar_step,
+                                                            a.seed, a.stream_id, a.temperature, a.top_p, a.out);
+  return check_launch("topk_final_kernel");
+}
+
+}  // namespace
+
+int64_t sample_workspace_bytes(int64_t B, int64_t vocab, int64_t top_k) {
+  const int64_t g = int64_t(greedy_splits(B, vocab)) * B * int64_t(sizeof(Cand));
+  int64_t t = 0;
+  if (top_k > 1) t = int64_t(topk_splits(vocab, top_k)) * top_k * B * int64_t(sizeof(Cand));
+  return g > t ? g : t;
+}
+
+int launch_sample_greedy(const SampleArgs &a) {
+  if (a.B == 0) return YB_OK;
+  switch (a.dtype) {
+    case YB_F32: return greedy_t<float>(a);
+    case YB_BF16: return greedy_t<__nv_bfloat16>(a);
+    case YB_F16: return greedy_t<__half>(a);
+  }
+  return set_error(YB_ERR_ARGUMENT, "sample: bad dtype %d", a.dtype);
+}
+
+int launch_sample_topk_topp(const SampleArgs &a) {
+  if (a.B == 0) return YB_OK;
+  if (a.top_k < 2 || a.top_k > kMaxTopK)
+    return set_error(YB_ERR_UNSUPPORTED, "sample: top_k=%lld outside [2, %d]", (long long)a.top_k, kMaxTopK);
+  const int M = topk_splits(a.vocab, a.top_k) * int(a.top_k);
+  if (size_t(M) * 16 + 8 > 200 * 1024)
+    return set_error(YB_ERR_UNSUPPORTED, "sample: %d candidates exceed the merge buffer", M);
+  switch (a.dtype) {
+    case YB_F32: return topk_t<float>(a);
+    case YB_BF16: return topk_t<__nv_bfloat16>(a);
+    case YB_F16: return topk_t<__half>(a);
+  }
+  return set_error(YB_ERR_ARGUMENT, "sample: bad dtype %d", a.dtype);
+}
+
+int launch_presence_penalty(void *scores, const uint8_t *seen, int64_t n, float penalty, int dtype,
+                            cudaStream_t stream) {
+  if (n == 0 || penalty == 0.f) return YB_OK;
+  const unsigned grid = unsigned(((n + 255) / 256 < 148 * 16 ? (n + 255) / 256 : 148 * 16));
+  switch (dtype) {
+    case YB_F32: presence_kernel<float><<<grid, 256, 0, stream>>>(static_cast<float *>(scores), seen, n, penalty); break;
+    case YB_BF16: presence_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(static_cast<__nv_bfloat16 *>(scores), seen, n, penalty); break;
+    case YB_F16: presence_kernel<__half><<<grid, 256, 0, stream>>>(static_cast<__half *>(scores), seen, n, penalty); break;
+    default: return set_error(YB_ERR_ARGUMENT, "presence penalty: bad dtype %d", dtype);
+  }
+  return check_launch("presence_kernel");
+}
+
+int launch_gdn_gates(const void *b, const void *a, int64_t b_rs, int64_t a_rs, const float *A_log,
+                     const float *dt_bias, void *beta_out, float *g_out, int64_t rows, int64_t heads, int io_dtype,
+                     cudaStream_t stream) {
+  const int64_t n = rows * heads;
+  if (n == 0) return YB_OK;
+  const unsigned grid = unsigned(((n + 255) / 256 < 148 * 16 ? (n + 255) / 256 : 148 * 16));
+  switch (io_dtype) {
+#define YB_GATES(T) \
+  gates_kernel<T><<<grid, 256, 0, stream>>>(static_cast<const T *>(b), static_cast<const T *>(a), b_rs, a_rs, A_log, dt_bias, static_cast<T *>(beta_out), g_out, rows, heads)
+    case YB_F32: YB_GATES(float); break;
+    case YB_BF16: YB_GATES(__nv_bfloat16); break;
+    case YB_F16: YB_GATES(__half); break;
+#undef YB_GATES
+    default: return set_error(YB_ERR_ARGUMENT, "gates: bad dtype %d", io_dtype);
+  }
+  return check_launch("gates_kernel");
+}
+
+}  // namespace yb

@@ -1,0 +1,206 @@
+"""Gated delta rule operators with the fla call signatures.
+
+``chunk_gated_delta_rule`` and ``fused_recurrent_gated_delta_rule`` accept the
+arguments of fla 0.5.1 (``fla/ops/gated_delta_rule/chunk.py:365`` and
+``fused_recurrent.py:291``, the third-party package the reference pins), which
+is what ``modeling_yanchor.py:397-406`` binds onto every
+``Qwen3_5GatedDeltaNet`` and what ``runtime/model/inference_kernels.py:716``
+calls for decode.  They also accept the positional torch-path convention of
+``transformers`` qwen3_5 (``modeling_qwen3_5.py:508-529``).  Shapes:
+
+    q, k  [B, T, H, K]      v  [B, T, HV, V]      g, beta  [B, T, HV]
+    initial_state / final_state  [N, HV, K, V] float32  ([N, HV, V, K] with
+    transpose_state_layout);  N = B, or len(cu_seqlens) - 1 with B == 1.
+
+Returns ``(o [B, T, HV, V] in q.dtype, final_state or None)``.  With
+``inplace=True`` (recurrent operator only) a contiguous float32
+``initial_state`` is updated in place and returned as the final state, the
+contract of the reference's in-place decode override
+(``inference_kernels.py:147-173``).
+
+Everything runs on the CUDA kernels of libyanchor_b200.so; there is no CPU
+path.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._torch import dtype_code, ptr, require_cuda, scalar_token_view, stream_ptr, token_view
+
+
+def _validate(q, k, v, g, beta, initial_state, cu_seqlens):
+    if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
+        raise ValueError('q, k, v must be [B, T, H, K] / [B, T, HV, V]')
+    if q.shape[2] != k.shape[2]:
+        raise ValueError(f'q and k must have the same number of heads, but got q.shape[2]={q.shape[2]} '
+                         f'and k.shape[2]={k.shape[2]}')
+    H, HV = q.shape[2], v.shape[2]
+    if HV % H != 0:
+        raise ValueError(f'For GVA, num_v_heads (HV={HV}) must be evenly divisible by num_heads (H={H}), '
+                         f'but got HV % H = {HV % H}')
+    if q.shape != k.shape or q.shape[:2] != v.shape[:2]:
+        raise ValueError('q, k, v batch/time/feature shapes disagree')
+    if g is None or beta is None:
+        raise ValueError('g and beta are required')
+    if g.shape != v.shape[:3] or beta.shape != v.shape[:3]:
+        raise ValueError('g and beta must be [B, T, HV] (head-wise beta)')
+    if cu_seqlens is not None:
+        if q.shape[0] != 1:
+            raise ValueError(f'The batch size is expected to be 1 rather than {q.shape[0]} when using '
+                             f'`cu_seqlens`.Please flatten variable-length inputs before processing.')
+        if initial_state is not None and initial_state.shape[0] != len(cu_seqlens) - 1:
+            raise ValueError(f'The number of initial states is expected to be equal to the number of input '
+                             f'sequences, i.e., {len(cu_seqlens) - 1} rather than {initial_state.shape[0]}.')
+
+
+def _common(q, k, v, g, beta, scale, initial_state, output_final_state, use_qk_l2norm_in_kernel, cu_seqlens,
+            transpose_state_layout, use_gate_in_kernel, A_log, dt_bias, beta_logits, inplace):
+    require_cuda(q, k, v, g, beta, initial_state, cu_seqlens, A_log, dt_bias)
+    _validate(q, k, v, g, beta, initial_state, cu_seqlens)
+    B, T, H, K = q.shape
+    HV, V = v.shape[2], v.shape[3]
+    if k.dtype != q.dtype or v.dtype != q.dtype:
+        raise TypeError('q, k and v must share a dtype')
+    if cu_seqlens is not None:
+        cu = cu_seqlens.to(device=q.device, dtype=torch.int64).contiguous()
+        N = cu.numel() - 1
+    else:
+        cu = None
+        N = B
+    if scale is None:
+        scale = K ** -0.5
+    flags = 0
+    if use_qk_l2norm_in_kernel:
+        flags |= _lib.GDN_QK_L2NORM
+    if transpose_state_layout:
+        flags |= _lib.GDN_TRANSPOSE_STATE
+    if use_gate_in_kernel:
+        if A_log is None:
+            raise ValueError('`A_log` must be provided when `use_gate_in_kernel=True`.')
+        flags |= _lib.GDN_GATE_IN_KERNEL
+        A_log = A_log.to(torch.float32).contiguous()
+        dt_bias = None if dt_bias is None else dt_bias.to(torch.float32).contiguous()
+    else:
+        A_log = dt_bias = None
+    if beta_logits:
+        flags |= _lib.GDN_BETA_SIGMOID
+    q, qs = token_view(q)
+    k, ks = token_view(k)
+    v, vs = token_view(v)
+    g, gs = scalar_token_view(g)
+    beta, bs = scalar_token_view(beta)
+    state_shape = (N, HV, V, K) if transpose_state_layout else (N, HV, K, V)
+    h0 = None
+    if initial_state is not None:
+        if tuple(initial_state.shape) != state_shape:
+            raise ValueError(f'initial_state must have shape {state_shape}, got {tuple(initial_state.shape)}')
+        h0 = initial_state
+        if h0.dtype != torch.float32 or not h0.is_contiguous() or h0.data_ptr() % 16:
+            h0 = h0.to(torch.float32).contiguous()
+            if h0.data_ptr() % 16:
+                h0 = h0.clone()
+    ht = None
+    if output_final_state:
+        if inplace and h0 is not None and h0 is initial_state:
+            ht = h0
+        else:
+            ht = torch.empty(state_shape, device=q.device, dtype=torch.float32)
+    o = torch.empty((B, T, HV, V), device=q.device, dtype=q.dtype)
+    return dict(q=q, k=k, v=v, qs=qs, ks=ks, vs=vs, g=g, gs=gs, beta=beta, bs=bs, A_log=A_log, dt_bias=dt_bias,
+                h0=h0, ht=ht, o=o, cu=cu, B=B, T=T, H=H, HV=HV, K=K, V=V, N=N, scale=float(scale), flags=flags)
+
+
+def fused_recurrent_gated_delta_rule(q, k, v, g=None, gk=None, gv=None, beta=None, scale=None, initial_state=None,
+                                     output_final_state=False, use_qk_l2norm_in_kernel=False,
+                                     use_gate_in_kernel=False, A_log=None, dt_bias=None, cu_seqlens=None,
+                                     transpose_state_layout=False, *, use_beta_sigmoid_in_kernel=False,
+                                     z=None, norm_weight=None, norm_eps=1e-6, inplace=False):
+    """Per-token gated delta rule (fla ``fused_recurrent_gated_delta_rule``).
+
+    Extra keyword-only arguments: ``use_beta_sigmoid_in_kernel`` (beta holds
+    logits); ``z`` / ``norm_weight`` / ``norm_eps`` to fuse the gated RMSNorm
+    epilogue (``Qwen3_5RMSNormGated``) into the output; ``inplace`` to write
+    the final state into ``initial_state`` (when it is a contiguous float32
+    tensor) and return that tensor, as the reference's in-place decode
+    override does.  By default a new final-state tensor is returned, as fla
+    does.
+    """
+    if gk is not None or gv is not None:
+        raise NotImplementedError('per-key / per-value decays (gk, gv) are not part of the YANchor path')
+    if beta is None:
+        beta = torch.ones(v.shape[:3], device=v.device, dtype=q.dtype)
+    a = _common(q, k, v, g, beta, scale, initial_state, output_final_state, use_qk_l2norm_in_kernel, cu_seqlens,
+                transpose_state_layout, use_gate_in_kernel, A_log, dt_bias, use_beta_sigmoid_in_kernel, inplace)
+    if (z is None) != (norm_weight is None):
+        raise ValueError('z and norm_weight go together')
+    if z is not None:
+        require_cuda(z, norm_weight)
+        if z.shape != a['o'].shape:
+            raise ValueError('z must be [B, T, HV, V]')
+        z = z.to(q.dtype).contiguous()
+        norm_weight = norm_weight.to(q.dtype).contiguous()
+    rc = _lib.lib().yb_gdn_recurrent_fwd(
+        a['q'].data_ptr(), a['k'].data_ptr(), a['v'].data_ptr(), a['qs'], a['ks'], a['vs'],
+        a['g'].data_ptr(), a['beta'].data_ptr(), a['gs'], a['bs'], ptr(a['A_log']), ptr(a['dt_bias']),
+        ptr(a['h0']), ptr(a['ht']), a['o'].data_ptr(), ptr(z), ptr(norm_weight), float(norm_eps), ptr(a['cu']),
+        a['B'], a['T'], a['H'], a['HV'], a['K'], a['V'], a['N'], a['scale'], dtype_code(a['q']),
+        dtype_code(a['g']), dtype_code(a['beta']), a['flags'], stream_ptr(q.device))
+    _lib.check(rc, 'fused_recurrent_gated_delta_rule')
+    return a['o'], (a['ht'] if output_final_state else None)
+
+
+def chunk_gated_delta_rule(q, k, v, g, beta, scale=None, initial_state=None, output_final_state=False,
+                           use_qk_l2norm_in_kernel=False, cu_seqlens=None, cu_seqlens_cpu=None, cp_context=None,
+                           transpose_state_layout=False, **kwargs):
+    """Chunked (64-token) gated delta rule (fla ``chunk_gated_delta_rule``)."""
+    if 'head_first' in kwargs:
+        raise DeprecationWarning('head_first has been removed. Inputs must be in `[B, T, H, ...]` format.')
+    if cp_context is not None:
+        raise NotImplementedError('context parallelism is not part of the YANchor path')
+    if 'chunk_size' in kwargs and kwargs['chunk_size'] != 64:
+        raise NotImplementedError('only chunk_size=64 is built')
+    use_gate_in_kernel = kwargs.get('use_gate_in_kernel', False)
+    a = _common(q, k, v, g, beta, scale, initial_state, output_final_state, use_qk_l2norm_in_kernel, cu_seqlens,
+                transpose_state_layout, use_gate_in_kernel, kwargs.get('A_log'), kwargs.get('dt_bias'),
+                kwargs.get('use_beta_sigmoid_in_kernel', False), inplace=False)
+    L = _lib.lib()
+    need = L.yb_gdn_chunk_workspace_bytes(a['B'], a['T'], a['H'], a['HV'], a['K'], a['V'], a['N'],
+                                          dtype_code(a['q']))
+    ws = torch.empty(max(need, 1), device=q.device, dtype=torch.uint8) if need > 0 else None
+    rc = L.yb_gdn_chunk_fwd(
+        a['q'].data_ptr(), a['k'].data_ptr(), a['v'].data_ptr(), a['qs'], a['ks'], a['vs'],
+        a['g'].data_ptr(), a['beta'].data_ptr(), a['gs'], a['bs'], ptr(a['A_log']), ptr(a['dt_bias']),
+        ptr(a['h0']), ptr(a['ht']), a['o'].data_ptr(), ptr(a['cu']),
+        a['B'], a['T'], a['H'], a['HV'], a['K'], a['V'], a['N'], a['scale'], dtype_code(a['q']),
+        dtype_code(a['g']), dtype_code(a['beta']), a['flags'], ptr(ws), need, stream_ptr(q.device))
+    _lib.check(rc, 'chunk_gated_delta_rule')
+    return a['o'], (a['ht'] if output_final_state else None)
+
+
+def gdn_gates(b, a, A_log, dt_bias):
+    """beta = sigmoid(b), g = -exp(A_log) * softplus(a + dt_bias) for one
+    decode token: b, a ``[B, 1, HV]`` (any row stride) -> (beta in b.dtype,
+    g float32), as ``runtime/model/inference_kernels.py:683-691``."""
+    require_cuda(b, a, A_log, dt_bias)
+    if b.shape != a.shape or b.shape[-1] != A_log.numel():
+        raise ValueError('fused GDN gates require matching [.., HV] head logits')
+    if b.stride(-1) != 1 or a.stride(-1) != 1:
+        b, a = b.contiguous(), a.contiguous()
+    heads = b.shape[-1]
+    rows = b.numel() // heads
+    b2, a2 = b.reshape(rows, heads), a.reshape(rows, heads)
+    beta = torch.empty(b.shape, device=b.device, dtype=b.dtype)
+    g = torch.empty(b.shape, device=b.device, dtype=torch.float32)
+    A = A_log.to(torch.float32).contiguous()
+    dtb = None if dt_bias is None else dt_bias.to(torch.float32).contiguous()
+    rc = _lib.lib().yb_gdn_gates(b2.data_ptr(), a2.data_ptr(), b2.stride(0), a2.stride(0), A.data_ptr(), ptr(dtb),
+                                 beta.data_ptr(), g.data_ptr(), rows, heads, dtype_code(b), stream_ptr(b.device))
+    _lib.check(rc, 'gdn_gates')
+    return beta, g
+
+
+# names used by fla and by the transformers torch path
+fused_recurrent_gdn = fused_recurrent_gated_delta_rule
+chunk_gdn = chunk_gated_delta_rule
+recurrent_gated_delta_rule = fused_recurrent_gated_delta_rule
