@@ -30,7 +30,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -60,58 +59,72 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
-    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
-              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
-              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+    """Samples SM clocks and clock-event (throttle) reasons through NVML from a
+    background thread every few milliseconds while the timed region runs.
+    Reading clocks changes nothing on the GPU."""
+    REASONS = (('hw_slowdown', 'nvmlClocksEventReasonHwSlowdown'),
+               ('hw_thermal_slowdown', 'nvmlClocksEventReasonHwThermalSlowdown'),
+               ('sw_thermal_slowdown', 'nvmlClocksEventReasonSwThermalSlowdown'),
+               ('sw_power_cap', 'nvmlClocksEventReasonSwPowerCap'),
+               ('hw_power_brake', 'nvmlClocksEventReasonHwPowerBrakeSlowdown'))
 
-    def __init__(self, index):
+    def __init__(self, index, interval_s=0.002):
         self.index = index
-        self.proc = None
-        self.lines = []
+        self.interval = interval_s
+        self.samples = []
+        self.max_mhz = None
+        self.error = None
+        self._stop = threading.Event()
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(['nvidia-smi', f'--id={self.index}', f'--query-gpu={self.FIELDS}',
-                                          '--format=csv,noheader,nounits', '-lms', '200'],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+            import pynvml as nv
+            nv.nvmlInit()
+            visible = os.environ.get('CUDA_VISIBLE_DEVICES')
+            idx = self.index
+            if visible:
+                ids = [x for x in visible.split(',') if x.strip()]
+                if ids and ids[self.index].strip().isdigit():
+                    idx = int(ids[self.index])
+            self.nv = nv
+            self.handle = nv.nvmlDeviceGetHandleByIndex(idx)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(self.handle, nv.NVML_CLOCK_SM)
+            self.thread = threading.Thread(target=self._run, daemon=True)
             self.thread.start()
-        except Exception:  # noqa: BLE001
-            self.proc = None
+        except Exception as e:  # noqa: BLE001
+            self.error = repr(e)
+            self.nv = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _run(self):
+        nv = self.nv
+        getr = getattr(nv, 'nvmlDeviceGetCurrentClocksEventReasons', None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self._stop.is_set():
+            try:
+                self.samples.append((nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM),
+                                     int(getr(self.handle))))
+            except Exception as e:  # noqa: BLE001
+                self.error = repr(e)
+                return
+            time.sleep(self.interval)
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:  # noqa: BLE001
-                self.proc.kill()
+        self._stop.set()
+        if self.nv is not None:
+            self.thread.join(timeout=5)
 
     def summary(self):
-        sm, mx, reasons = [], [], set()
-        names = ('hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap')
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(',')]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower() == 'active':
+        if not self.samples:
+            return {'sm_mhz': None, 'sm_max_mhz': self.max_mhz, 'reasons': ['unsampled'], 'samples': 0,
+                    'error': self.error}
+        reasons = set()
+        for _, bits in self.samples:
+            for name, const in self.REASONS:
+                if bits & int(getattr(self.nv, const, 0)):
                     reasons.add(name)
-        if not sm:
-            return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['unsampled'], 'samples': 0}
-        return {'sm_mhz': statistics.median(sm), 'sm_max_mhz': max(mx), 'reasons': sorted(reasons),
-                'samples': len(sm)}
+        return {'sm_mhz': statistics.median(m for m, _ in self.samples), 'sm_max_mhz': self.max_mhz,
+                'reasons': sorted(reasons), 'samples': len(self.samples), 'source': 'NVML, 2 ms polling'}
 
 
 # ----------------------------------------------------------------- GPU arm --
@@ -343,6 +356,50 @@ def run_prefill(torch, yb, device, hbm, tf_burst, peak_kind):
                          'flops_per_launch': flops}}
 
 
+def run_only(args):
+    """Run one kernel family `--steps` times at the bench shapes (for ncu
+    captures of a small case); prints its mean CUDA-event time."""
+    import torch
+    import yanchor_b200 as yb
+    dev = torch.device('cuda', 0)
+    B = args.batch
+    layers, mems, inputs, active, ws = build_decode(torch, yb, B, dev, n_inputs=1)
+    x, L0, st = inputs[0], layers[0], mems[0]
+    gen = torch.Generator(device=dev).manual_seed(3)
+    bf = torch.bfloat16
+    if args.only == 'gdn_chunk':
+        Bp, T, H, K = args.prefill_batch, 8192, 32, 128
+        q, k, v = (torch.randn(Bp, T, H, K, generator=gen, device=dev).to(bf) for _ in range(3))
+        g = torch.nn.functional.logsigmoid(torch.randn(Bp, T, H, generator=gen, device=dev))
+        beta = torch.randn(Bp, T, H, generator=gen, device=dev).sigmoid().to(bf)
+        fn = lambda: yb.chunk_gated_delta_rule(q, k, v, g, beta, output_final_state=True,  # noqa: E731
+                                               use_qk_l2norm_in_kernel=True)
+    elif args.only == 'mem_indexed':
+        blocks = 128
+        mq = torch.randn(8, blocks, 64, MEM_H, MEM_D, generator=gen, device=dev).to(bf)
+        mk = torch.randn(1, 4096, MEM_G, MEM_D, generator=gen, device=dev).to(bf)
+        refs = torch.randint(0, 4096, (8, blocks, MEM_G, 64), generator=gen, device=dev)
+        fn = lambda: yb.indexed_gqa(mq, mk, mk, refs)  # noqa: E731
+    else:
+        fns = {
+            'gdn_decode': lambda: yb.fused_recurrent_gated_delta_rule(
+                x['q'][0], x['k'][0], x['v'][0], g=x['a'][0], beta=x['b'][0], initial_state=L0['state'],
+                output_final_state=True, use_qk_l2norm_in_kernel=True, use_gate_in_kernel=True,
+                A_log=L0['A_log'], dt_bias=L0['dt_bias'], use_beta_sigmoid_in_kernel=True, z=x['z'][0],
+                norm_weight=L0['norm_w'], inplace=True),
+            'mem_read': lambda: yb.committed_gqa(x['mq'][0], st),
+            'mem_commit': lambda: yb.commit_decode(x['mk'][0], x['mv'][0], x['ms'][0], active, MEM_CHUNK, st),
+            'greedy': lambda: yb.greedy(x['logits'], workspace=ws),
+            'topk': lambda: yb.sample_top_k_top_p_counter(x['logits'], torch.arange(B, device=dev), 1, seed=0,
+                                                          temperature=1.0, top_k=20, top_p=0.95),
+        }
+        fn = fns[args.only]
+    for _ in range(args.warmup):
+        fn()
+    ms = time_events(torch, fn, args.steps, torch.cuda.current_stream(dev))
+    print(json.dumps({'only': args.only, 'ms': round(ms, 5), 'steps': args.steps}), flush=True)
+
+
 # ------------------------------------------------------------- CPU arm ------
 def cpu_decode_sample(steps=2, B=64, seed=0):
     """Time the numpy restatement of the same decode step on the host."""
@@ -379,12 +436,15 @@ def cpu_decode_sample(steps=2, B=64, seed=0):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
-    ap.add_argument('--steps', type=int, default=20)
+    ap.add_argument('--steps', type=int, default=200)
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--batch', type=int, default=64)
     ap.add_argument('--impl', default='yanchor_b200', choices=['yanchor_b200', 'reference'])
     ap.add_argument('--no-prefill', action='store_true')
     ap.add_argument('--no-cpu', action='store_true')
+    ap.add_argument('--only', choices=['gdn_decode', 'gdn_chunk', 'mem_read', 'mem_commit', 'mem_indexed', 'greedy',
+                                       'topk'], help='run one kernel family (small ncu captures)')
+    ap.add_argument('--prefill-batch', type=int, default=8)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get('WORLD_SIZE', '1'))
@@ -392,6 +452,9 @@ def main():
     local_rank = int(os.environ.get('LOCAL_RANK', '0'))
     sys.path.insert(0, ROOT)
 
+    if args.only:
+        run_only(args)
+        return
     if args.impl == 'reference':
         if rank != 0:
             return

@@ -50,6 +50,14 @@ enum yb_status {
 const char *yb_last_error(void);
 /* ABI version of this library. */
 int yb_abi_version(void);
+/*
+ * Error word of the kernels that synchronise through time-bounded waits (the
+ * tensor-core chunk kernel): 0 when every wait completed, else the code of
+ * the first wait that gave up (that launch's outputs are then invalid).
+ * Synchronises the current device; `clear` resets the word.  No reference
+ * counterpart: the reference's Triton kernels have no such waits.
+ */
+int yb_device_error(int clear);
 
 /*
  * Per-token gated delta rule over T steps (T = 1 is batched decode).

@@ -142,7 +142,11 @@ def test_decode_gates_and_norm_in_kernel(yb):
     eo, es = ogdn.recurrent_gated_delta_rule(rb(q), rb(k), rb(v), g, beta, initial_state=h0, use_qk_l2norm=True,
                                              dtype=np.float64)
     en = ogdn.rmsnorm_gated(eo, rb(z), rb(w), dtype=np.float64)
-    assert np.abs(host(o) - en).max() <= BF16_ATOL * 2
+    # The norm divides by rms(o) per head (o is small here), so compare
+    # relative to the output scale: the kernel rounds o, the normalised value
+    # and weight * value to bf16 exactly where Qwen3_5RMSNormGated does.
+    assert rel(host(o), en) <= 1e-2
+    assert np.abs(host(o) - en).max() <= 0.1
     assert rel(host(s), es) <= STATE_RTOL
 
 
@@ -200,8 +204,8 @@ def test_empty_and_zero_length(yb):
     gg = -torch.rand(1, 5, 32, device='cuda')
     h0 = torch.randn(2, 32, 128, 128, device='cuda')
     for fn in (yb.chunk_gated_delta_rule, yb.fused_recurrent_gated_delta_rule):
-        _, s = fn(qq, qq, vv, gg, gg.sigmoid().to(bf), initial_state=h0, output_final_state=True, cu_seqlens=cu,
-                  use_qk_l2norm_in_kernel=True)
+        _, s = fn(qq, qq, vv, g=gg, beta=gg.sigmoid().to(bf), initial_state=h0, output_final_state=True,
+                  cu_seqlens=cu, use_qk_l2norm_in_kernel=True)
         torch.testing.assert_close(s[0], h0[0], rtol=0, atol=0)
 
 

@@ -30,6 +30,7 @@ _U32 = ctypes.c_uint32
 SIGNATURES = {
     'yb_last_error': (ctypes.c_char_p, []),
     'yb_abi_version': (_I, []),
+    'yb_device_error': (_I, [_I]),
     'yb_gdn_recurrent_fwd': (_I, [_P, _P, _P, _I64, _I64, _I64, _P, _P, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _F,
                                   _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _F, _I, _I, _I, _U32, _P]),
     'yb_gdn_chunk_workspace_bytes': (_I64, [_I64, _I64, _I64, _I64, _I64, _I64, _I64, _I]),

@@ -70,5 +70,24 @@ def build(verbose: bool = False, force: bool = False) -> str:
     return LIB
 
 
+TEST_CSRC = os.path.join(os.path.dirname(HERE), 'tests', 'csrc')
+TEST_LIB = os.path.join(os.path.dirname(HERE), 'tests', '_build', 'libyb_tc_debug.so')
+
+
+def build_test_lib(force: bool = False) -> str:
+    """Test-only library: the tensor-core chunk kernel with its stage dumps
+    enabled (tests/csrc/tc_debug.cu).  Never loaded by the package."""
+    src = os.path.join(TEST_CSRC, 'tc_debug.cu')
+    deps = [src, os.path.join(CSRC, 'gdn_chunk_tc.cu')] + _headers()
+    os.makedirs(os.path.dirname(TEST_LIB), exist_ok=True)
+    if force or not os.path.exists(TEST_LIB) or os.path.getmtime(TEST_LIB) < max(os.path.getmtime(d) for d in deps):
+        cmd = [nvcc(), *ARCH, *FLAGS, '-shared', src, '-o', TEST_LIB, '-lcudart']
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError(f'nvcc failed on tc_debug.cu:\n{res.stderr}')
+    return TEST_LIB
+
+
 if __name__ == '__main__':
     print(build(verbose='-v' in sys.argv, force='-f' in sys.argv))
+    print(build_test_lib(force='-f' in sys.argv))

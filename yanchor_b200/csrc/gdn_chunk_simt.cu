@@ -19,7 +19,6 @@ namespace yb {
 namespace {
 
 constexpr int C = 64;    // chunk length
-constexpr int BV = 64;   // value slice per CTA
 constexpr int NT = 256;  // threads
 
 struct ChunkParams {
@@ -45,7 +44,7 @@ __device__ __forceinline__ float load_scalar(const void *p, int64_t idx, int dty
   return __half2float(static_cast<const __half *>(p)[idx]);
 }
 
-template <int K>
+template <int K, int BV>
 struct Smem {
   static constexpr int KP = K + 1;  // padded row pitch for q / k
   static constexpr int CP = C + 1;
@@ -59,10 +58,14 @@ struct Smem {
   float G[C], eG[C], bet[C], tail[C];
 };
 
-template <typename TIO, int K>
+template <typename TIO, int K, int BV>
 __global__ void __launch_bounds__(NT) gdn_chunk_simt_kernel(const ChunkParams p) {
+  constexpr int TXN = BV / 4;             // threads across a C x BV tile row (4 columns each)
+  constexpr int RT = C * BV / (4 * NT);   // tile rows per thread
+  constexpr int RD = K * BV / (4 * NT);   // state rows per thread
+  static_assert(RT >= 1 && RD >= 1, "tile must cover the block");
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  Smem<K> &sm = *reinterpret_cast<Smem<K> *>(smem_raw);
+  Smem<K, BV> &sm = *reinterpret_cast<Smem<K, BV> *>(smem_raw);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n = blockIdx.x / p.HV, hv = blockIdx.x % p.HV;
   const int v0 = blockIdx.y * BV;
@@ -93,8 +96,9 @@ __global__ void __launch_bounds__(NT) gdn_chunk_simt_kernel(const ChunkParams p)
   const TIO *kp = static_cast<const TIO *>(p.k);
   const TIO *vp = static_cast<const TIO *>(p.v);
   TIO *op = static_cast<TIO *>(p.o);
-  // output tile of this thread for the C x BV products: rows 4*ty.., cols 4*tx..
-  const int tx = tid % 16, ty = tid / 16;
+  // C x BV products: rows RT*ty.., cols 4*tx..;  C x C products: 4x4 at (4*py, 4*px)
+  const int tx = tid % TXN, ty = tid / TXN;
+  const int px = tid % 16, py = tid / 16;
 
   for (int64_t c0 = 0; c0 < len; c0 += C) {
     const int m = int(len - c0 < C ? len - c0 : C);
@@ -167,9 +171,9 @@ __global__ void __launch_bounds__(NT) gdn_chunk_simt_kernel(const ChunkParams p)
         float ki[4], qi[4], kj[4];
 #pragma unroll
         for (int a = 0; a < 4; ++a) {
-          ki[a] = sm.k[ty * 4 + a][d];
-          qi[a] = sm.q[ty * 4 + a][d];
-          kj[a] = sm.k[tx * 4 + a][d];
+          ki[a] = sm.k[py * 4 + a][d];
+          qi[a] = sm.q[py * 4 + a][d];
+          kj[a] = sm.k[px * 4 + a][d];
         }
 #pragma unroll
         for (int a = 0; a < 4; ++a)
@@ -183,7 +187,7 @@ __global__ void __launch_bounds__(NT) gdn_chunk_simt_kernel(const ChunkParams p)
       for (int a = 0; a < 4; ++a)
 #pragma unroll
         for (int b = 0; b < 4; ++b) {
-          const int i = ty * 4 + a, j = tx * 4 + b;
+          const int i = py * 4 + a, j = px * 4 + b;
           const float dec = j <= i ? expf(sm.G[i] - sm.G[j]) : 0.f;
           sm.L[i][j] = j < i ? sm.bet[i] * kk[a][b] * dec : 0.f;
           sm.P[i][j] = qk[a][b] * dec;
@@ -203,20 +207,20 @@ __global__ void __launch_bounds__(NT) gdn_chunk_simt_kernel(const ChunkParams p)
       }
     }
     // ---- Y = beta (v - e^G (k S));  QS = q S kept in registers ----
-    float qs[4][4] = {};
+    float qs[RT][4] = {};
     {
-      float ks[4][4] = {};
+      float ks[RT][4] = {};
       for (int d = 0; d < K; ++d) {
         float4 sv = *reinterpret_cast<const float4 *>(&sm.S[d][tx * 4]);
         const float s4[4] = {sv.x, sv.y, sv.z, sv.w};
-        float ki[4], qi[4];
+        float ki[RT], qi[RT];
 #pragma unroll
-        for (int a = 0; a < 4; ++a) {
-          ki[a] = sm.k[ty * 4 + a][d];
-          qi[a] = sm.q[ty * 4 + a][d];
+        for (int a = 0; a < RT; ++a) {
+          ki[a] = sm.k[ty * RT + a][d];
+          qi[a] = sm.q[ty * RT + a][d];
         }
 #pragma unroll
-        for (int a = 0; a < 4; ++a)
+        for (int a = 0; a < RT; ++a)
 #pragma unroll
           for (int b = 0; b < 4; ++b) {
             ks[a][b] = fmaf(ki[a], s4[b], ks[a][b]);
@@ -224,8 +228,8 @@ __global__ void __launch_bounds__(NT) gdn_chunk_simt_kernel(const ChunkParams p)
           }
       }
 #pragma unroll
-      for (int a = 0; a < 4; ++a) {
-        const int i = ty * 4 + a;
+      for (int a = 0; a < RT; ++a) {
+        const int i = ty * RT + a;
 #pragma unroll
         for (int b = 0; b < 4; ++b) {
           const int c = tx * 4 + b;
@@ -235,51 +239,50 @@ __global__ void __launch_bounds__(NT) gdn_chunk_simt_kernel(const ChunkParams p)
     }
     __syncthreads();
     // ---- v_new = Tm Y ----
-    float vn[4][4] = {};
+    float vn[RT][4] = {};
     for (int j = 0; j < C; ++j) {
       float4 yv = *reinterpret_cast<const float4 *>(&sm.vv[j][tx * 4]);
       const float y4[4] = {yv.x, yv.y, yv.z, yv.w};
 #pragma unroll
-      for (int a = 0; a < 4; ++a) {
-        const float t = sm.Tm[ty * 4 + a][j];
+      for (int a = 0; a < RT; ++a) {
+        const float t = sm.Tm[ty * RT + a][j];
 #pragma unroll
         for (int b = 0; b < 4; ++b) vn[a][b] = fmaf(t, y4[b], vn[a][b]);
       }
     }
     __syncthreads();
 #pragma unroll
-    for (int a = 0; a < 4; ++a)
-      *reinterpret_cast<float4 *>(&sm.vv[ty * 4 + a][tx * 4]) = make_float4(vn[a][0], vn[a][1], vn[a][2], vn[a][3]);
+    for (int a = 0; a < RT; ++a)
+      *reinterpret_cast<float4 *>(&sm.vv[ty * RT + a][tx * 4]) = make_float4(vn[a][0], vn[a][1], vn[a][2], vn[a][3]);
     __syncthreads();
     // ---- o = e^G QS + P v_new ----
     {
-      float ov[4][4];
+      float ov[RT][4];
 #pragma unroll
-      for (int a = 0; a < 4; ++a)
+      for (int a = 0; a < RT; ++a)
 #pragma unroll
-        for (int b = 0; b < 4; ++b) ov[a][b] = sm.eG[ty * 4 + a] * qs[a][b];
+        for (int b = 0; b < 4; ++b) ov[a][b] = sm.eG[ty * RT + a] * qs[a][b];
       for (int j = 0; j < C; ++j) {
         float4 xv = *reinterpret_cast<const float4 *>(&sm.vv[j][tx * 4]);
         const float x4[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
-        for (int a = 0; a < 4; ++a) {
-          const float pp = sm.P[ty * 4 + a][j];
+        for (int a = 0; a < RT; ++a) {
+          const float pp = sm.P[ty * RT + a][j];
 #pragma unroll
           for (int b = 0; b < 4; ++b) ov[a][b] = fmaf(pp, x4[b], ov[a][b]);
         }
       }
 #pragma unroll
-      for (int a = 0; a < 4; ++a) {
-        const int i = ty * 4 + a;
+      for (int a = 0; a < RT; ++a) {
+        const int i = ty * RT + a;
         if (i < m) {
           TIO *dst = op + (bos + c0 + i) * int64_t(p.HV) * p.V + int64_t(hv) * p.V + v0 + tx * 4;
           store4(dst, ov[a]);
         }
       }
     }
-    // ---- S <- e^{G_last} S + (k e^{G_last - G})^T v_new : K x BV, (K/16) x 4 per thread ----
+    // ---- S <- e^{G_last} S + (k e^{G_last - G})^T v_new : K x BV, RD x 4 per thread ----
     {
-      constexpr int RD = K / 16;
       const float gl = expf(sm.G[C - 1]);
       float acc[RD][4];
 #pragma unroll
@@ -316,19 +319,27 @@ __global__ void __launch_bounds__(NT) gdn_chunk_simt_kernel(const ChunkParams p)
   }
 }
 
-template <typename TIO, int K>
-int launch_k(const GdnArgs &a, const ChunkParams &p) {
-  const size_t smem = sizeof(Smem<K>);
-  auto kern = gdn_chunk_simt_kernel<TIO, K>;
-  static bool configured = false;  // per template instance
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "gdn chunk simt: smem attribute: %s", cudaGetErrorString(e));
-    configured = true;
-  }
+template <typename TIO, int K, int BV>
+int launch_kb(const GdnArgs &a, const ChunkParams &p) {
+  const size_t smem = sizeof(Smem<K, BV>);
+  auto kern = gdn_chunk_simt_kernel<TIO, K, BV>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "gdn chunk simt: smem attribute: %s", cudaGetErrorString(e));
   dim3 grid(unsigned(a.N * a.HV), unsigned(a.V / BV));
   kern<<<grid, NT, smem, a.stream>>>(p);
   return check_launch("gdn_chunk_simt_kernel");
+}
+
+template <typename TIO, int K>
+int launch_k(const GdnArgs &a, const ChunkParams &p) {
+  return a.V % 64 == 0 ? launch_kb<TIO, K, 64>(a, p) : launch_kb<TIO, K, 32>(a, p);
+}
+
+template <typename TIO>
+int launch_io(const GdnArgs &a, const ChunkParams &p) {
+  if (a.K == 32) return launch_k<TIO, 32>(a, p);
+  if (a.K == 64) return launch_k<TIO, 64>(a, p);
+  return launch_k<TIO, 128>(a, p);
 }
 
 }  // namespace
@@ -345,13 +356,13 @@ int launch_gdn_chunk_simt(const GdnArgs &a) {
   p.H = int(a.H); p.HV = int(a.HV); p.V = int(a.V);
   p.scale = a.scale; p.flags = a.flags;
   if (a.N * a.HV == 0) return YB_OK;
-  if (a.V % BV) return set_error(YB_ERR_UNSUPPORTED, "gdn chunk: V=%lld must be a multiple of 64", (long long)a.V);
-  if (a.K != 64 && a.K != 128)
-    return set_error(YB_ERR_UNSUPPORTED, "gdn chunk: K=%lld not built; supported 64/128", (long long)a.K);
+  if (a.V % 32) return set_error(YB_ERR_UNSUPPORTED, "gdn chunk: V=%lld must be a multiple of 32", (long long)a.V);
+  if (a.K != 32 && a.K != 64 && a.K != 128)
+    return set_error(YB_ERR_UNSUPPORTED, "gdn chunk: K=%lld not built; supported 32/64/128", (long long)a.K);
   switch (a.io_dtype) {
-    case YB_F32: return a.K == 64 ? launch_k<float, 64>(a, p) : launch_k<float, 128>(a, p);
-    case YB_BF16: return a.K == 64 ? launch_k<__nv_bfloat16, 64>(a, p) : launch_k<__nv_bfloat16, 128>(a, p);
-    case YB_F16: return a.K == 64 ? launch_k<__half, 64>(a, p) : launch_k<__half, 128>(a, p);
+    case YB_F32: return launch_io<float>(a, p);
+    case YB_BF16: return launch_io<__nv_bfloat16>(a, p);
+    case YB_F16: return launch_io<__half>(a, p);
   }
   return set_error(YB_ERR_ARGUMENT, "gdn chunk: bad io dtype %d", a.io_dtype);
 }

@@ -1,0 +1,705 @@
+// Chunked gated delta rule on the 5th-generation tensor cores (tcgen05 +
+// TMEM + TMA), bf16 inputs, K = V = 128, chunk C = 64, fp32 state.
+//
+// One CTA owns one (sequence, value head) and walks the sequence chunk by
+// chunk.  Per chunk, with raw (unnormalised) bf16 q, k, v tiles straight
+// from TMA and the L2 norms folded into fp32 scale factors (kn_j = 1/|k_j|,
+// qn_i = scale/|q_i|), G the in-chunk cumulative log decay:
+//
+//   MMA1  [K;Q] K^T              -> k_i.k_j and q_i.k_j            (TMEM)
+//   epi   L_ij = beta_i e^{G_i-G_j} kn_i kn_j k_i.k_j   (j < i),
+//         P_ij = qn_i kn_j e^{G_i-G_j} q_i.k_j           (j <= i)
+//   SIMT  T = (I + L)^-1 in fp32 (16x16 blocked forward substitution)
+//   MMA2  W^T = k^T Tw^T, U^T = v^T Tu^T   with Tw_ij = T_ij beta_j e^{G_j} kn_j,
+//                                                Tu_ij = T_ij beta_j
+//   MMA3  X^T = S^T W^T, Y^T = S^T q^T                          (state bf16)
+//   epi   v_new^T = U^T - X^T
+//   MMA4  O^T = v_new^T P^T
+//   MMA5  D^T = (v_new^T * e^{G_last-G} kn) k
+//   epi   o = e^{G} qn Y + O ;  S^T <- e^{G_last} S^T + D^T    (fp32 in TMEM)
+//
+// (the chunk form of transformers qwen3_5 modeling_qwen3_5.py:234-311 and
+// of fla's chunk_gated_delta_rule_fwd).  Every state-dependent product is
+// computed transposed ("value lanes"): TMEM lane v holds value column v, so
+// each epilogue thread owns one column of the state, of v_new and of o, and
+// all element-wise work stays in registers.  The state lives in TMEM as
+// fp32 for the whole sequence and enters the MMAs as a bf16 copy.
+//
+// Roles: warp 0 = TMA producer (+ gates, cumulative decay), warp 1 = TMEM
+// allocator and single-thread MMA issuer, warps 2..5 = epilogue (thread row
+// r = 32*(warp%4) + lane, the TMEM lane it may access).  Every wait is
+// bounded in time; a CTA that gives up records an error code, drains its
+// in-flight copies and MMAs, frees TMEM and exits.
+#include "common.cuh"
+#include "kernels.h"
+#include "tc.cuh"
+
+namespace yb {
+namespace {
+
+using namespace tc;
+
+constexpr int C = 64;       // chunk length
+constexpr int KD = 128;     // key dim
+constexpr int VD = 128;     // value dim
+constexpr int NTHREADS = 192;
+constexpr int EPI_THREADS = 128;
+
+// ---- shared memory map (bytes) ----
+constexpr uint32_t OFF_KQ0 = 0;            // [K;Q] stage 0: 128 rows x 128 cols, 2 column blocks
+constexpr uint32_t OFF_KQ1 = 32768;
+constexpr uint32_t OFF_V0 = 65536;         // V stage 0: 64 rows x 128 cols
+constexpr uint32_t OFF_V1 = 81920;
+constexpr uint32_t OFF_LF = 98304;         // L fp32 64x64 / o staging bf16 64x128
+constexpr uint32_t OFF_TF = 114688;        // T fp32 64x64
+constexpr uint32_t OFF_P = 131072;         // P bf16 64x64 (SW128)
+constexpr uint32_t OFF_TW = 139264;        // Tw bf16 64x64 (SW128); solve scratch before that
+constexpr uint32_t OFF_TU = 147456;        // Tu bf16 64x64 (SW128)
+constexpr uint32_t OFF_WT = 155648;        // W^T bf16 128x64 (SW128) / v~ (v_new scaled) 128x64
+constexpr uint32_t OFF_VN = 172032;        // v_new^T bf16 128x64
+constexpr uint32_t OFF_ST = 188416;        // S^T bf16 128x128 (2 column blocks)
+constexpr uint32_t OFF_GST = 221184;       // per stage: G, beta, e^G, e^{G_last-G} (4 x 64 floats)
+constexpr uint32_t OFF_NORM = OFF_GST + 2 * 1024;   // kn[64], qn[64]
+constexpr uint32_t OFF_BAR = OFF_NORM + 512;        // mbarriers
+constexpr uint32_t OFF_MISC = OFF_BAR + 64;         // tmem base, abort flag
+constexpr uint32_t SMEM_BYTES = OFF_MISC + 16;
+
+// ---- TMEM columns ----
+constexpr uint32_t T_D1 = 0;     // [KK^T; QK^T] 128x64, later O^T
+constexpr uint32_t T_W = 64;     // W^T, later X^T
+constexpr uint32_t T_U = 128;    // U^T
+constexpr uint32_t T_Y = 192;    // Y^T
+constexpr uint32_t T_DS = 256;   // D^T (128 columns)
+constexpr uint32_t T_S = 384;    // S^T fp32 state (128 columns)
+
+constexpr uint32_t ID_N64_KK = idesc_bf16(128, 64, false, false);
+constexpr uint32_t ID_N64_MK = idesc_bf16(128, 64, true, false);
+constexpr uint32_t ID_N64_KM = idesc_bf16(128, 64, false, true);
+constexpr uint32_t ID_N128_KM = idesc_bf16(128, 128, false, true);
+
+// error codes recorded in g_device_error
+constexpr int ERR_WAIT_FULL = 0x101, ERR_WAIT_EMPTY = 0x102, ERR_WAIT_MMA = 0x103, ERR_WAIT_EPI = 0x104,
+              ERR_ALIGN = 0x105, ERR_WAIT_DONE = 0x106;
+
+struct TcParams {
+  const void *g, *beta;
+  int64_t g_ts, beta_ts;
+  int g_dtype, beta_dtype;
+  const float *A_log, *dt_bias;
+  const float *h0;
+  float *ht;
+  __nv_bfloat16 *o;
+#ifdef YB_TC_DEBUG
+  float *dbg;  // test-only build: intermediates of CTA 0, chunk 0
+#endif
+  const int64_t *cu;
+  int64_t T;
+  int H, HV;
+  float scale;
+  uint32_t flags;
+};
+
+__device__ __forceinline__ float load_scalar(const void *p, int64_t idx, int dtype) {
+  if (dtype == YB_F32) return static_cast<const float *>(p)[idx];
+  if (dtype == YB_BF16) return __bfloat162float(static_cast<const __nv_bfloat16 *>(p)[idx]);
+  return __half2float(static_cast<const __half *>(p)[idx]);
+}
+
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+#ifdef YB_TC_DEBUG
+// Test-only: copy `n` values of TMEM row r (already in registers) into the
+// debug buffer at tile offset `off` (row-major, `n` columns).
+#define YB_DBG_ROW(off, n, vals)                                                       \
+  do {                                                                                 \
+    if (p.dbg && blockIdx.x == 0 && c == 0)                                            \
+      for (int _i = 0; _i < (n); ++_i) p.dbg[(off) + r * (n) + _i] = (vals)[_i];       \
+  } while (0)
+#else
+#define YB_DBG_ROW(off, n, vals) \
+  do {                           \
+  } while (0)
+#endif
+constexpr int DBG_D1 = 0, DBG_W = 8192, DBG_U = 16384, DBG_X = 24576, DBG_Y = 32768, DBG_O = 40960,
+              DBG_DS = 49152, DBG_T = 65536, DBG_NORM = 69632, DBG_TS = 70000;
+#ifdef YB_TC_DEBUG
+// Test-only: phase timestamps (ns since the thread started) of epilogue
+// thread 0 of CTA 0 for the first 32 chunks, 16 events per chunk.
+#define YB_DBG_TS(ev)                                                                   \
+  do {                                                                                  \
+    if (p.dbg && blockIdx.x == 0 && r == 0 && c < 32)                                   \
+      p.dbg[DBG_TS + c * 16 + (ev)] = float(globaltimer_ns() - dbg_t0);                 \
+  } while (0)
+#else
+#define YB_DBG_TS(ev) \
+  do {                \
+  } while (0)
+#endif
+
+__global__ void __launch_bounds__(NTHREADS, 1)
+    gdn_chunk_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                        const __grid_constant__ CUtensorMap map_v, const TcParams p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + OFF_BAR);  // [2]
+  uint64_t *empty = full + 2;                                      // [2]
+  uint64_t *mma_bar = full + 4;
+  uint64_t *epi_bar = full + 5;
+  uint64_t *done_bar = full + 6;
+  uint32_t *tmem_base_smem = reinterpret_cast<uint32_t *>(smem + OFF_MISC);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OFF_MISC + 4);
+  float *kn = reinterpret_cast<float *>(smem + OFF_NORM);
+  float *qn = kn + 64;
+
+  const int n = blockIdx.x / p.HV, hv = blockIdx.x % p.HV;
+  const int h = hv / (p.HV / p.H);
+  int64_t bos, len;
+  if (p.cu) {
+    bos = p.cu[n];
+    len = p.cu[n + 1] - bos;
+  } else {
+    bos = int64_t(n) * p.T;
+    len = p.T;
+  }
+  const int nchunks = int((len + C - 1) / C);
+  const int64_t head = (int64_t(n) * p.HV + hv) * int64_t(KD) * VD;
+  const bool trans = p.flags & YB_GDN_TRANSPOSE_STATE;
+
+  if (tid == 0) {
+    *abort_flag = (smem_u32(smem) & 1023u) ? 1 : 0;  // SW128 tiles need a 1024-byte aligned base
+    if (*abort_flag) atomicCAS(&g_device_error, 0, ERR_ALIGN);
+    mbar_init(&full[0], 32);
+    mbar_init(&full[1], 32);
+    mbar_init(&empty[0], 2);
+    mbar_init(&empty[1], 2);
+    mbar_init(mma_bar, 1);
+    mbar_init(epi_bar, EPI_THREADS);
+    mbar_init(done_bar, 1);
+    mbar_fence_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_base_smem, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_base_smem;
+
+  if (warp == 0) {
+    // ===================== producer =====================
+    if (lane == 0) {
+      prefetch_tensormap(&map_q);
+      prefetch_tensormap(&map_k);
+      prefetch_tensormap(&map_v);
+    }
+    const bool gate_in = p.flags & YB_GDN_GATE_IN_KERNEL;
+    const bool beta_sig = p.flags & YB_GDN_BETA_SIGMOID;
+    const float a_coef = gate_in ? -expf(p.A_log[hv]) : 0.f;
+    const float dtb = (gate_in && p.dt_bias) ? p.dt_bias[hv] : 0.f;
+    int issued = 0;
+    for (int c = 0; c < nchunks && !*abort_flag; ++c) {
+      const int s = c & 1;
+      if (c >= 2 && !mbar_wait(&empty[s], ((c >> 1) - 1) & 1, abort_flag, ERR_WAIT_EMPTY)) break;
+      // gates, masked beyond the sequence, and the cumulative decay
+      float gv[2], bv[2];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int i = lane + 32 * half;
+        const int64_t t = int64_t(c) * C + i;
+        float gl = 0.f, b = 0.f;
+        if (t < len) {
+          const int64_t tok = bos + t;
+          gl = load_scalar(p.g, tok * p.g_ts + hv, p.g_dtype);
+          if (gate_in) gl = a_coef * softplus20(gl + dtb);
+          b = load_scalar(p.beta, tok * p.beta_ts + hv, p.beta_dtype);
+          if (beta_sig) b = sigmoidf_(b);
+        }
+        gv[half] = gl;
+        bv[half] = b;
+      }
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const float y0 = __shfl_up_sync(0xffffffffu, gv[0], off), y1 = __shfl_up_sync(0xffffffffu, gv[1], off);
+        if (lane >= off) {
+          gv[0] += y0;
+          gv[1] += y1;
+        }
+      }
+      gv[1] += __shfl_sync(0xffffffffu, gv[0], 31);
+      const float glast = __shfl_sync(0xffffffffu, gv[1], 31);
+      float *gst = reinterpret_cast<float *>(smem + OFF_GST + s * 1024);
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int i = lane + 32 * half;
+        gst[i] = gv[half];
+        gst[64 + i] = bv[half];
+        gst[128 + i] = expf(gv[half]);
+        gst[192 + i] = expf(glast - gv[half]);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        uint8_t *kq = smem + (s ? OFF_KQ1 : OFF_KQ0);
+        uint8_t *vt = smem + (s ? OFF_V1 : OFF_V0);
+        const int tok0 = int(bos + int64_t(c) * C);
+        mbar_arrive_expect_tx(&full[s], 6 * 8192);
+#pragma unroll
+        for (int cb = 0; cb < 2; ++cb) {
+          tma_load_3d(kq + cb * 16384, &map_k, &full[s], cb * 64, h, tok0);
+          tma_load_3d(kq + cb * 16384 + 8192, &map_q, &full[s], cb * 64, h, tok0);
+          tma_load_3d(vt + cb * 8192, &map_v, &full[s], cb * 64, hv, tok0);
+        }
+      } else {
+        mbar_arrive(&full[s]);
+      }
+      issued = c + 1;
+    }
+    // drain: every issued stage must have landed before the CTA may exit
+    for (int c = (issued > 2 ? issued - 2 : 0); c < issued; ++c) {
+      mbar_wait(&full[c & 1], (c >> 1) & 1, abort_flag, ERR_WAIT_FULL);
+    }
+  } else if (warp == 1) {
+    // ===================== MMA issuer =====================
+    int epi_phase = 0, ok = 1;
+    auto wait_epi = [&]() {
+      ok = ok && mbar_wait(epi_bar, epi_phase & 1, abort_flag, ERR_WAIT_EPI);
+      ++epi_phase;
+      tc_fence_after();
+      return ok;
+    };
+    if (lane == 0) {
+      wait_epi();  // initial state staged
+      for (int c = 0; c < nchunks && ok; ++c) {
+        const int s = c & 1;
+        const uint32_t kq = smem_u32(smem + (s ? OFF_KQ1 : OFF_KQ0));
+        const uint32_t vt = smem_u32(smem + (s ? OFF_V1 : OFF_V0));
+        if (!mbar_wait(&full[s], (c >> 1) & 1, abort_flag, ERR_WAIT_FULL)) break;
+        tc_fence_after();
+        // MMA1: [K;Q] K^T  (M=128, N=64, K=128)
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          mma_bf16(tmem + T_D1, sdesc(kq + off, 16, 1024), sdesc(kq + off, 16, 1024), ID_N64_KK, kk > 0);
+        }
+        mma_commit(mma_bar);
+        if (!wait_epi()) break;
+        // MMA2: W^T = k^T Tw^T ;  U^T = v^T Tu^T   (M=128, N=64, K=64)
+        const uint32_t tw = smem_u32(smem + OFF_TW), tu = smem_u32(smem + OFF_TU);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          mma_bf16(tmem + T_W, sdesc(kq + kk * 2048, 16384, 1024), sdesc(tw + kk * 32, 16, 1024), ID_N64_MK, kk > 0);
+          mma_bf16(tmem + T_U, sdesc(vt + kk * 2048, 8192, 1024), sdesc(tu + kk * 32, 16, 1024), ID_N64_MK, kk > 0);
+        }
+        mma_commit(mma_bar);
+        if (!wait_epi()) break;
+        // MMA3: X^T = S^T W^T ;  Y^T = S^T q^T   (M=128, N=64, K=128)
+        const uint32_t st = smem_u32(smem + OFF_ST), wt = smem_u32(smem + OFF_WT);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t a = sdesc(st + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+          mma_bf16(tmem + T_W, a, sdesc(wt + kk * 2048, 16384, 1024), ID_N64_KM, kk > 0);
+          mma_bf16(tmem + T_Y, a, sdesc(kq + 8192 + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024), ID_N64_KK,
+                   kk > 0);
+        }
+        mma_commit(mma_bar);
+        if (!wait_epi()) break;
+        // MMA4: O^T = v_new^T P^T (N=64, K=64) ;  MMA5: D^T = (v~_hi + v~_lo)^T k (N=128, K=64)
+        const uint32_t vn = smem_u32(smem + OFF_VN), pp = smem_u32(smem + OFF_P);
+        const uint32_t vlo = smem_u32(smem + OFF_TF);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          mma_bf16(tmem + T_D1, sdesc(vn + kk * 32, 16, 1024), sdesc(pp + kk * 32, 16, 1024), ID_N64_KK, kk > 0);
+          mma_bf16(tmem + T_DS, sdesc(wt + kk * 32, 16, 1024), sdesc(kq + kk * 2048, 16384, 1024), ID_N128_KM,
+                   kk > 0);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_bf16(tmem + T_DS, sdesc(vlo + kk * 32, 16, 1024), sdesc(kq + kk * 2048, 16384, 1024), ID_N128_KM,
+                   true);
+        mma_commit(mma_bar);
+        mma_commit(&empty[s]);
+        if (!wait_epi()) break;
+      }
+      // all issued MMAs finished before TMEM is released
+      mma_commit(done_bar);
+      mbar_wait(done_bar, 0, abort_flag, ERR_WAIT_DONE);
+    }
+    __syncwarp();
+  } else {
+    // ===================== epilogue (128 threads) =====================
+    const int r = (warp & 3) * 32 + lane;            // TMEM lane == tile row
+#ifdef YB_TC_DEBUG
+    const uint64_t dbg_t0 = globaltimer_ns();
+#endif
+    const uint32_t lane_base = tmem + (uint32_t((warp & 3) * 32) << 16);
+    const bool l2 = p.flags & YB_GDN_QK_L2NORM;
+    uint8_t *st_tile = smem + OFF_ST;
+    float *LF = reinterpret_cast<float *>(smem + OFF_LF);
+    float *TF = reinterpret_cast<float *>(smem + OFF_TF);
+    float *scr = reinterpret_cast<float *>(smem + OFF_TW);
+    int mma_phase = 0;
+    bool ok = true;
+    auto wait_mma = [&]() {
+      ok = ok && mbar_wait(mma_bar, mma_phase & 1, abort_flag, ERR_WAIT_MMA);
+      ++mma_phase;
+      tc_fence_after();
+      return ok;
+    };
+    auto signal_mma = [&]() {
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(epi_bar);
+    };
+
+    // ---- initial state: thread r owns value column v = r ----
+    {
+      float row[32];
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+#pragma unroll
+        for (int d = 0; d < 32; ++d) {
+          const int dd = q4 * 32 + d;
+          row[d] = p.h0 ? (trans ? p.h0[head + int64_t(r) * KD + dd] : p.h0[head + int64_t(dd) * VD + r]) : 0.f;
+        }
+        tmem_st32(lane_base + T_S + q4 * 32, row);
+        if (nchunks == 0 && p.ht) {
+#pragma unroll
+          for (int d = 0; d < 32; ++d) {
+            const int dd = q4 * 32 + d;
+            if (trans) p.ht[head + int64_t(r) * KD + dd] = row[d];
+            else p.ht[head + int64_t(dd) * VD + r] = row[d];
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint4 w;
+          w.x = pack_bf16x2(row[8 * j + 0], row[8 * j + 1]);
+          w.y = pack_bf16x2(row[8 * j + 2], row[8 * j + 3]);
+          w.z = pack_bf16x2(row[8 * j + 4], row[8 * j + 5]);
+          w.w = pack_bf16x2(row[8 * j + 6], row[8 * j + 7]);
+          *reinterpret_cast<uint4 *>(st_tile + sw128_off(128, q4 >> 1, r, (q4 & 1) * 4 + j)) = w;
+        }
+      }
+      tmem_wait_st();
+      signal_mma();
+    }
+
+    for (int c = 0; c < nchunks && ok; ++c) {
+      const int s = c & 1;
+      const uint8_t *kq = smem + (s ? OFF_KQ1 : OFF_KQ0);
+      const float *gst = reinterpret_cast<const float *>(smem + OFF_GST + s * 1024);
+      const float *G = gst, *BT = gst + 64, *EG = gst + 128, *TAIL = gst + 192;
+      const int m = int(len - int64_t(c) * C < C ? len - int64_t(c) * C : C);
+      YB_DBG_TS(0);
+      if (!mbar_wait(&full[s], (c >> 1) & 1, abort_flag, ERR_WAIT_FULL)) break;
+      YB_DBG_TS(1);
+      if (!wait_mma()) break;   // MMA1 done
+      YB_DBG_TS(2);
+      // ---------- step 2: norms, L, P ----------
+      float d1[64];
+      tmem_ld32(lane_base + T_D1, d1);
+      tmem_ld32(lane_base + T_D1 + 32, d1 + 32);
+      tmem_wait_ld();
+      YB_DBG_ROW(DBG_D1, 64, d1);
+      if (r < 64) {
+        float diag = 0.f;
+#pragma unroll
+        for (int j = 0; j < 64; ++j) diag = (j == r) ? d1[j] : diag;
+        kn[r] = l2 ? rsqrtf(diag + 1e-6f) : 1.f;
+      } else {
+        const int i = r - 64;
+        float ss = 0.f;
+#pragma unroll
+        for (int cb = 0; cb < 2; ++cb)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float x[8];
+            ld_chunk_bf16(kq, 128, cb, 64 + i, j, x);
+#pragma unroll
+            for (int t = 0; t < 8; ++t) ss += x[t] * x[t];
+          }
+        qn[i] = (l2 ? rsqrtf(ss + 1e-6f) : 1.f) * p.scale;
+      }
+      epi_sync();
+      if (r < 64) {
+        const int i = r;
+        const float ci = BT[i] * kn[i], gi = G[i];
+#pragma unroll
+        for (int j4 = 0; j4 < 16; ++j4) {
+          float4 v4;
+          float *vv = reinterpret_cast<float *>(&v4);
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const int j = 4 * j4 + t;
+            vv[t] = j < i ? ci * kn[j] * __expf(gi - G[j]) * d1[j] : 0.f;
+          }
+          *reinterpret_cast<float4 *>(LF + i * 64 + 4 * j4) = v4;
+        }
+      } else {
+        const int i = r - 64;
+        const float ci = qn[i], gi = G[i];
+        float pr[64];
+#pragma unroll
+        for (int j = 0; j < 64; ++j) pr[j] = j <= i ? ci * kn[j] * __expf(gi - G[j]) * d1[j] : 0.f;
+        st_row64_bf16(smem + OFF_P, 64, 0, i, pr);
+      }
+      epi_sync();
+      YB_DBG_TS(3);
+      // ---------- T = (I + L)^-1, 16x16 blocks ----------
+      if (r < 64) {
+        const int j = r, b = j >> 4, jj = j & 15;
+        float x[16];
+#pragma unroll
+        for (int ii = 0; ii < 16; ++ii) {
+          const float *Lrow = LF + (b * 16 + ii) * 64 + b * 16;
+          float acc = 0.f;
+#pragma unroll
+          for (int mm = 0; mm < ii; ++mm) acc = fmaf(Lrow[mm], x[mm], acc);
+          x[ii] = ii < jj ? 0.f : (ii == jj ? 1.f : -acc);
+        }
+        for (int row = 0; row < 64; ++row) {
+          const int rb = row >> 4;
+          TF[row * 64 + j] = rb == b ? x[row & 15] : 0.f;  // blocks below the diagonal are filled next
+        }
+      }
+      epi_sync();
+      for (int dlev = 1; dlev < 4; ++dlev) {
+        const int nb = 4 - dlev;
+        // Y_(bi,bj) = sum_{m in blocks bj..bi-1} L[bi-rows][m] T[m][bj-cols]
+        for (int e = r; e < nb * 256; e += EPI_THREADS) {
+          const int blk = e >> 8, rr = (e >> 4) & 15, cc = e & 15;
+          const int bi = dlev + blk, bj = blk;
+          const float *Lrow = LF + (bi * 16 + rr) * 64;
+          float acc = 0.f;
+          for (int mcol = bj * 16; mcol < bi * 16; ++mcol) acc = fmaf(Lrow[mcol], TF[mcol * 64 + bj * 16 + cc], acc);
+          scr[e] = acc;
+        }
+        epi_sync();
+        // T_(bi,bj) = -T_(bi,bi) Y
+        for (int e = r; e < nb * 256; e += EPI_THREADS) {
+          const int blk = e >> 8, rr = (e >> 4) & 15, cc = e & 15;
+          const int bi = dlev + blk, bj = blk;
+          const float *Trow = TF + (bi * 16 + rr) * 64 + bi * 16;
+          float acc = 0.f;
+#pragma unroll
+          for (int t = 0; t < 16; ++t) acc = fmaf(Trow[t], scr[(blk << 8) + t * 16 + cc], acc);
+          TF[(bi * 16 + rr) * 64 + bj * 16 + cc] = -acc;
+        }
+        epi_sync();
+      }
+      YB_DBG_TS(4);
+      // Tw (rows 0..63 by threads 0..63), Tu (threads 64..127)
+      {
+        const int i = r & 63;
+        float rowv[64];
+        if (r < 64) {
+#pragma unroll
+          for (int j = 0; j < 64; ++j) rowv[j] = TF[i * 64 + j] * BT[j] * EG[j] * kn[j];
+          st_row64_bf16(smem + OFF_TW, 64, 0, i, rowv);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 64; ++j) rowv[j] = TF[i * 64 + j] * BT[j];
+          st_row64_bf16(smem + OFF_TU, 64, 0, i, rowv);
+        }
+      }
+#ifdef YB_TC_DEBUG
+      if (p.dbg && blockIdx.x == 0 && c == 0) {
+        if (r < 64)
+          for (int j = 0; j < 64; ++j) p.dbg[DBG_T + r * 64 + j] = TF[r * 64 + j];
+        p.dbg[DBG_NORM + r] = r < 64 ? kn[r] : qn[r - 64];
+      }
+#endif
+      tc_fence_before();
+      signal_mma();
+      YB_DBG_TS(5);
+      // ---------- step 4: W^T -> smem (MN-major B operand of MMA3) ----------
+      if (!wait_mma()) break;
+      YB_DBG_TS(6);
+      {
+        float w[64];
+        tmem_ld32(lane_base + T_W, w);
+        tmem_ld32(lane_base + T_W + 32, w + 32);
+        tmem_wait_ld();
+        YB_DBG_ROW(DBG_W, 64, w);
+        st_row64_bf16(smem + OFF_WT, 128, 0, r, w);
+      }
+      signal_mma();
+      YB_DBG_TS(7);
+      // ---------- step 6: v_new = U - X ----------
+      if (!wait_mma()) break;
+      YB_DBG_TS(8);
+      {
+        float u[64], x[64];
+        tmem_ld32(lane_base + T_U, u);
+        tmem_ld32(lane_base + T_U + 32, u + 32);
+        tmem_ld32(lane_base + T_W, x);
+        tmem_ld32(lane_base + T_W + 32, x + 32);
+        tmem_wait_ld();
+        YB_DBG_ROW(DBG_U, 64, u);
+        YB_DBG_ROW(DBG_X, 64, x);
+#pragma unroll
+        for (int i = 0; i < 64; ++i) u[i] -= x[i];
+        st_row64_bf16(smem + OFF_VN, 128, 0, r, u);
+        // v~ = v_new e^{G_last-G} kn enters the state update as bf16 hi + lo
+        // parts (its rounding is what limits the fp32 state's accuracy)
+#pragma unroll
+        for (int i = 0; i < 64; ++i) u[i] *= TAIL[i] * kn[i];
+        st_row64_bf16(smem + OFF_WT, 128, 0, r, u);
+#pragma unroll
+        for (int i = 0; i < 64; ++i) u[i] -= __bfloat162float(__float2bfloat16_rn(u[i]));
+        st_row64_bf16(smem + OFF_TF, 128, 0, r, u);
+      }
+      signal_mma();
+      YB_DBG_TS(9);
+      // ---------- step 8: outputs and the state update ----------
+      if (!wait_mma()) break;
+      YB_DBG_TS(10);
+      {
+        float y[64], oo[64];
+        tmem_ld32(lane_base + T_Y, y);
+        tmem_ld32(lane_base + T_Y + 32, y + 32);
+        tmem_ld32(lane_base + T_D1, oo);
+        tmem_ld32(lane_base + T_D1 + 32, oo + 32);
+        tmem_wait_ld();
+        YB_DBG_ROW(DBG_Y, 64, y);
+        YB_DBG_ROW(DBG_O, 64, oo);
+        __nv_bfloat16 *ostage = reinterpret_cast<__nv_bfloat16 *>(smem + OFF_LF);  // [64][128]
+#pragma unroll
+        for (int i = 0; i < 64; ++i) ostage[i * 128 + r] = __float2bfloat16_rn(EG[i] * qn[i] * y[i] + oo[i]);
+      }
+      {
+        const float decay = EG[63];   // e^{G_last}
+        const bool last = c == nchunks - 1;
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          float sv[32], dv[32];
+          tmem_ld32(lane_base + T_S + q4 * 32, sv);
+          tmem_ld32(lane_base + T_DS + q4 * 32, dv);
+          tmem_wait_ld();
+#ifdef YB_TC_DEBUG
+          if (p.dbg && blockIdx.x == 0 && c == 0)
+            for (int d = 0; d < 32; ++d) p.dbg[DBG_DS + r * 128 + q4 * 32 + d] = dv[d];
+#endif
+#pragma unroll
+          for (int d = 0; d < 32; ++d) sv[d] = fmaf(decay, sv[d], dv[d]);
+          tmem_st32(lane_base + T_S + q4 * 32, sv);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint4 w;
+            w.x = pack_bf16x2(sv[8 * j + 0], sv[8 * j + 1]);
+            w.y = pack_bf16x2(sv[8 * j + 2], sv[8 * j + 3]);
+            w.z = pack_bf16x2(sv[8 * j + 4], sv[8 * j + 5]);
+            w.w = pack_bf16x2(sv[8 * j + 6], sv[8 * j + 7]);
+            *reinterpret_cast<uint4 *>(st_tile + sw128_off(128, q4 >> 1, r, (q4 & 1) * 4 + j)) = w;
+          }
+          if (last && p.ht) {
+#pragma unroll
+            for (int d = 0; d < 32; ++d) {
+              const int dd = q4 * 32 + d;
+              if (trans) p.ht[head + int64_t(r) * KD + dd] = sv[d];
+              else p.ht[head + int64_t(dd) * VD + r] = sv[d];
+            }
+          }
+        }
+        tmem_wait_st();
+      }
+      YB_DBG_TS(11);
+      epi_sync();
+      {
+        // coalesced store of the o tile: row i = r / 2, half = r % 2 (128 bytes each)
+        const int i = r >> 1, half = r & 1;
+        if (i < m) {
+          const uint4 *src = reinterpret_cast<const uint4 *>(smem + OFF_LF + i * 256 + half * 128);
+          uint4 *dst = reinterpret_cast<uint4 *>(p.o + ((bos + int64_t(c) * C + i) * p.HV + hv) * VD + half * 64);
+#pragma unroll
+          for (int t = 0; t < 8; ++t) dst[t] = src[t];
+        }
+      }
+      epi_sync();
+      if (r == 0) mbar_arrive(&empty[s]);   // stage's gates / tiles no longer read
+      signal_mma();
+      YB_DBG_TS(12);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+// ---- host side ----------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// [tokens, heads, 128] bf16 -> boxes of 64 tokens x 1 head x 64 features, 128-byte swizzle
+int make_map(CUtensorMap *map, const void *base, int64_t ntok, int64_t heads, int64_t tok_stride) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return set_error(YB_ERR_CUDA, "gdn chunk tc: cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[3] = {128, cuuint64_t(heads), cuuint64_t(ntok)};
+  const cuuint64_t strides[2] = {128 * 2, cuuint64_t(tok_stride) * 2};
+  const cuuint32_t box[3] = {64, 1, 64};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(YB_ERR_CUDA, "gdn chunk tc: tensor map encode failed (%d)", int(r));
+  return YB_OK;
+}
+
+}  // namespace
+
+bool gdn_chunk_tc_supported(const GdnArgs &a) {
+  return a.io_dtype == YB_BF16 && a.K == KD && a.V == VD && a.B * a.T > 0;
+}
+
+int launch_gdn_chunk_tc_impl(const GdnArgs &a, float *dbg) {
+  const int64_t ntok = a.B * a.T;
+  CUtensorMap mq, mk, mv;
+  int rc = make_map(&mq, a.q, ntok, a.H, a.q_ts);
+  if (!rc) rc = make_map(&mk, a.k, ntok, a.H, a.k_ts);
+  if (!rc) rc = make_map(&mv, a.v, ntok, a.HV, a.v_ts);
+  if (rc) return rc;
+  TcParams p;
+  p.g = a.g; p.beta = a.beta; p.g_ts = a.g_ts; p.beta_ts = a.beta_ts;
+  p.g_dtype = a.g_dtype; p.beta_dtype = a.beta_dtype;
+  p.A_log = a.A_log; p.dt_bias = a.dt_bias;
+  p.h0 = a.h0; p.ht = a.ht; p.o = static_cast<__nv_bfloat16 *>(a.o);
+  p.cu = a.cu_seqlens; p.T = a.T; p.H = int(a.H); p.HV = int(a.HV);
+  p.scale = a.scale; p.flags = a.flags;
+#ifdef YB_TC_DEBUG
+  p.dbg = dbg;
+#else
+  (void)dbg;
+#endif
+  cudaError_t e = cudaFuncSetAttribute(gdn_chunk_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(SMEM_BYTES));
+  if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "gdn chunk tc: smem attribute: %s", cudaGetErrorString(e));
+  gdn_chunk_tc_kernel<<<unsigned(a.N * a.HV), NTHREADS, SMEM_BYTES, a.stream>>>(mq, mk, mv, p);
+  return check_launch("gdn_chunk_tc_kernel");
+}
+
+int launch_gdn_chunk_tc(const GdnArgs &a) { return launch_gdn_chunk_tc_impl(a, nullptr); }
+
+int read_device_error(int clear) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, tc::g_device_error, sizeof(int));
+  if (e != cudaSuccess) return -1;
+  if (clear && v) {
+    const int z = 0;
+    cudaMemcpyToSymbol(tc::g_device_error, &z, sizeof(int));
+  }
+  return v;
+}
+
+}  // namespace yb

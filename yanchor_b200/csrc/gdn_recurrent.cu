@@ -276,7 +276,8 @@ int launch_io(const GdnArgs &a, const RecParams &p) {
   if (a.K == 64 && a.V == 64) return launch_kv<TIO, 64, 64>(a, p);
   if (a.K == 128 && a.V == 64) return launch_kv<TIO, 128, 64>(a, p);
   if (a.K == 64 && a.V == 128) return launch_kv<TIO, 64, 128>(a, p);
-  return set_error(YB_ERR_UNSUPPORTED, "gdn recurrent: (K, V) = (%lld, %lld) not built; supported 64/128",
+  if (a.K == 32 && a.V == 32) return launch_kv<TIO, 32, 32>(a, p);
+  return set_error(YB_ERR_UNSUPPORTED, "gdn recurrent: (K, V) = (%lld, %lld) not built; supported 32/64/128",
                    (long long)a.K, (long long)a.V);
 }
 

@@ -30,6 +30,9 @@ struct GdnArgs {
 int launch_gdn_recurrent(const GdnArgs &a);
 int launch_gdn_chunk(const GdnArgs &a);
 int launch_gdn_chunk_simt(const GdnArgs &a);
+bool gdn_chunk_tc_supported(const GdnArgs &a);
+int launch_gdn_chunk_tc(const GdnArgs &a);
+int read_device_error(int clear);
 int64_t gdn_chunk_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t HV, int64_t K, int64_t V,
                                   int64_t N, int io_dtype);
 

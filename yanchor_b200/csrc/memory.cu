@@ -119,12 +119,13 @@ int launch_read_r(const MemReadArgs &a) {
     kern<<<grid, kReadThreads, smem, a.stream>>>(a);                                               \
     return check_launch("mem_decode_read_kernel");                                                 \
   }
+    YB_READ_CASE(32)
     YB_READ_CASE(64)
     YB_READ_CASE(128)
     YB_READ_CASE(256)
 #undef YB_READ_CASE
   }
-  return set_error(YB_ERR_UNSUPPORTED, "memory read: D=%lld not built (64/128/256)", (long long)a.D);
+  return set_error(YB_ERR_UNSUPPORTED, "memory read: D=%lld not built (32/64/128/256)", (long long)a.D);
 }
 
 template <typename T>
@@ -394,12 +395,13 @@ int launch_indexed_r(const MemIndexedArgs &a) {
     kern<<<grid, kIdxThreads, smem, a.stream>>>(a);                                                     \
     return check_launch("mem_indexed_read_kernel");                                                     \
   }
+    YB_IDX_CASE(32)
     YB_IDX_CASE(64)
     YB_IDX_CASE(128)
     YB_IDX_CASE(256)
 #undef YB_IDX_CASE
   }
-  return set_error(YB_ERR_UNSUPPORTED, "indexed read: D=%lld not built (64/128/256)", (long long)a.D);
+  return set_error(YB_ERR_UNSUPPORTED, "indexed read: D=%lld not built (32/64/128/256)", (long long)a.D);
 }
 
 template <typename T>

@@ -300,9 +300,9 @@ __global__ void __launch_bounds__(kNT) topk_final_kernel(const Cand *ws, int spl
                                                          int64_t *out) {
   extern __shared__ __align__(16) unsigned char tf_raw[];
   const int M = splits * K;
-  uint32_t *keys = reinterpret_cast<uint32_t *>(tf_raw);  // [M]
-  float *vals = reinterpret_cast<float *>(keys + M);      // [M]
-  int64_t *idx = reinterpret_cast<int64_t *>(vals + M + (M & 1));  // [M] (8-byte aligned)
+  uint32_t *keys = reinterpret_cast<uint32_t *>(tf_raw);      // [M] at byte 0
+  float *vals = reinterpret_cast<float *>(tf_raw + 4 * M);      // [M] at byte 4M
+  int64_t *idx = reinterpret_cast<int64_t *>(tf_raw + 8 * M);   // [M] at byte 8M (8-byte aligned)
   __shared__ int hist[256];
   __shared__ Cand sel[kMaxTopK];
   __shared__ float sv[kMaxTopK];
