@@ -177,6 +177,22 @@ int yb_mem_indexed_read(const void *query, const void *key, const void *value, c
 int64_t yb_sample_workspace_bytes(int64_t B, int64_t vocab, int64_t top_k);
 int yb_sample_greedy(const void *scores, int64_t row_stride, int64_t B, int64_t vocab, int dtype, int64_t *out,
                      void *workspace, int64_t workspace_bytes, void *stream);
+/*
+ * yb_sample_greedy_noalloc: the same argmax as yb_sample_greedy, for callers
+ * that cannot allocate device memory where they sample — a host runtime
+ * binding this ABI without a device allocator of its own, or a decode loop
+ * that must not allocate while its stream is being captured.  It takes no
+ * workspace: its partial results go to a fixed 64 KiB device array inside
+ * this library, which covers at most 4096 rows (larger batches get
+ * YB_ERR_UNSUPPORTED).  It allocates nothing and frees nothing.  The first
+ * call on a device looks the array's device address up once for that device,
+ * so make that first call before any stream capture.  All calls on a device
+ * share the array: calls that may run at the same time on the GPU (different
+ * streams with no ordering between them) race on it.  No counterpart in the
+ * reference, which always lets torch allocate.
+ */
+int yb_sample_greedy_noalloc(const void *scores, int64_t row_stride, int64_t B, int64_t vocab, int dtype,
+                             int64_t *out, void *stream);
 int yb_sample_top_k_top_p_counter(const void *scores, int64_t row_stride, int64_t B, int64_t vocab, int dtype,
                                   const int64_t *attempt_ids, const int64_t *steps, int64_t scalar_step,
                                   int64_t seed, int64_t stream_id, float temperature, int64_t top_k,

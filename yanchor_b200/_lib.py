@@ -43,6 +43,7 @@ SIGNATURES = {
     'yb_mem_indexed_read': (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I, _P]),
     'yb_sample_workspace_bytes': (_I64, [_I64, _I64, _I64]),
     'yb_sample_greedy': (_I, [_P, _I64, _I64, _I64, _I, _P, _P, _I64, _P]),
+    'yb_sample_greedy_noalloc': (_I, [_P, _I64, _I64, _I64, _I, _P, _P]),
     'yb_sample_top_k_top_p_counter': (_I, [_P, _I64, _I64, _I64, _I, _P, _P, _I64, _I64, _I64, _F, _I64, _F, _P, _P,
                                            _I64, _P]),
     'yb_presence_penalty': (_I, [_P, _P, _I64, _F, _I, _P]),

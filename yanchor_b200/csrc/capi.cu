@@ -188,6 +188,17 @@ int64_t yb_sample_workspace_bytes(int64_t B, int64_t vocab, int64_t top_k) {
   return sample_workspace_bytes(B, vocab, top_k);
 }
 
+int yb_sample_greedy_noalloc(const void *scores, int64_t row_stride, int64_t B, int64_t vocab, int dtype,
+                             int64_t *out, void *stream) {
+  YB_REQUIRE(dtype_ok(dtype), "sample_greedy_noalloc: bad dtype");
+  YB_REQUIRE(B >= 0 && vocab > 0 && row_stride >= vocab, "sample_greedy_noalloc: bad sizes");
+  YB_REQUIRE(B == 0 || (scores && out), "sample_greedy_noalloc: null tensor");
+  SampleArgs a{};
+  a.scores = scores; a.row_stride = row_stride; a.B = B; a.vocab = vocab; a.dtype = dtype; a.out = out;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return launch_sample_greedy_noalloc(a);
+}
+
 int yb_sample_greedy(const void *scores, int64_t row_stride, int64_t B, int64_t vocab, int dtype, int64_t *out,
                      void *workspace, int64_t workspace_bytes, void *stream) {
   YB_REQUIRE(dtype_ok(dtype), "sample_greedy: bad dtype");

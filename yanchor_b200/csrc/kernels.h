@@ -95,6 +95,8 @@ struct SampleArgs {
 };
 int64_t sample_workspace_bytes(int64_t B, int64_t vocab, int64_t top_k);
 int launch_sample_greedy(const SampleArgs &a);
+int launch_sample_greedy_noalloc(const SampleArgs &a);
+int64_t greedy_builtin_scratch_bytes();
 int launch_sample_topk_topp(const SampleArgs &a);
 int launch_presence_penalty(void *scores, const uint8_t *seen, int64_t n, float penalty, int dtype,
                             cudaStream_t stream);

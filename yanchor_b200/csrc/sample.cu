@@ -10,8 +10,18 @@
 // Both samplers split each row over several CTAs: the first pass writes
 // per-split candidates to the caller's workspace and the second reduces them
 // per row, so a batch of 64 rows still fills the GPU.
+#include <mutex>
+
 #include "common.cuh"
 #include "kernels.h"
+
+namespace yb {
+// Built-in scratch of the no-allocation greedy entry point: 16 bytes per
+// (row, split) partial; 64 KiB covers up to 4096 rows.
+constexpr int64_t kGreedyScratchBytes = 64 * 1024;
+constexpr int kMaxDevices = 64;
+static __device__ __align__(256) unsigned char g_greedy_scratch[kGreedyScratchBytes];
+}  // namespace yb
 
 namespace yb {
 namespace {
@@ -438,6 +448,52 @@ int launch_sample_greedy(const SampleArgs &a) {
     case YB_F16: return greedy_t<__half>(a);
   }
   return set_error(YB_ERR_ARGUMENT, "sample: bad dtype %d", a.dtype);
+}
+
+// ---- greedy argmax for callers that cannot allocate device memory ----------
+// The per-split partial maxima live in this fixed array instead of a
+// caller-provided workspace.  Every GPU that loads the library holds it until
+// the process exits; all calls on a device share it, so calls that overlap on
+// the GPU (different streams, no ordering between them) race on it.  Nothing
+// in it needs to start at zero: every call writes each partial it reads.
+int64_t greedy_builtin_scratch_bytes() { return kGreedyScratchBytes; }
+
+namespace {
+// Host code may not use g_greedy_scratch's address directly (the host-side
+// name is only a stand-in); the device address comes from
+// cudaGetSymbolAddress, looked up once per device with that device current.
+std::mutex g_scratch_mu;
+void *g_scratch_addr[kMaxDevices] = {};
+}  // namespace
+
+int launch_sample_greedy_noalloc(const SampleArgs &a) {
+  const int64_t need = sample_workspace_bytes(a.B, a.vocab, 1);
+  if (need > kGreedyScratchBytes)
+    return set_error(YB_ERR_UNSUPPORTED,
+                     "sample_greedy_noalloc: %lld rows need %lld bytes of scratch; the built-in scratch holds %lld "
+                     "(use yb_sample_greedy with a workspace)",
+                     (long long)a.B, (long long)need, (long long)kGreedyScratchBytes);
+  if (a.B == 0) return YB_OK;
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "sample_greedy_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return set_error(YB_ERR_UNSUPPORTED, "sample_greedy_noalloc: device %d", dev);
+  void *scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (!g_scratch_addr[dev]) {
+      void *p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_greedy_scratch);
+      if (e != cudaSuccess)
+        return set_error(YB_ERR_CUDA, "sample_greedy_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      g_scratch_addr[dev] = p;
+    }
+    scratch = g_scratch_addr[dev];
+  }
+  SampleArgs b = a;
+  b.workspace = scratch;
+  b.workspace_bytes = kGreedyScratchBytes;
+  return launch_sample_greedy(b);
 }
 
 int launch_sample_topk_topp(const SampleArgs &a) {

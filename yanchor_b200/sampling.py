@@ -46,6 +46,24 @@ def greedy(scores, workspace=None):
     return out
 
 
+def greedy_noalloc(scores, out=None):
+    """argmax like ``greedy``, for callers that cannot allocate device memory
+    when they sample: it needs no workspace (the library keeps a fixed 64 KiB
+    device array for the partial results, enough for 4096 rows).  Pass a
+    preallocated ``out`` ([B, 1] int64) to allocate nothing at all.  Calls that
+    may run concurrently on the GPU share that array and race; make the first
+    call on each device before capturing a CUDA graph."""
+    require_cuda(scores)
+    scores = _rows(scores)
+    B, V = scores.shape
+    if out is None:
+        out = torch.empty((B, 1), device=scores.device, dtype=torch.int64)
+    rc = _lib.lib().yb_sample_greedy_noalloc(scores.data_ptr(), scores.stride(0), B, V, dtype_code(scores),
+                                             out.data_ptr(), stream_ptr(scores.device))
+    _lib.check(rc, 'greedy_noalloc')
+    return out
+
+
 def sample_top_k_top_p_counter(scores, attempt_ids, steps, *, seed, temperature, top_k, top_p, stream=0,
                                workspace=None):
     require_cuda(scores)
