@@ -14,7 +14,7 @@ from conftest import ROOT
 pytestmark = pytest.mark.gpu
 
 LIB = os.path.join(ROOT, 'tests', '_build', 'libyb_tc_debug.so')
-DBG = dict(D1=0, W=8192, U=16384, X=24576, Y=32768, O=40960, DS=49152, T=65536, NORM=69632)
+DBG = dict(D1=0, W=16384, U=24576, X=32768, Y=40960, O=49152, DS=57344, T=73728, NORM=77824)
 
 
 def bf(x):
@@ -47,7 +47,7 @@ def run():
     gd, h0d = dev(g, torch.float32), dev(h0, torch.float32)
     ht = torch.zeros_like(h0d)
     o = torch.zeros(B, T, HV, K, device='cuda', dtype=torch.bfloat16)
-    dbg = torch.full((71000,), float("nan"), device="cuda")
+    dbg = torch.full((80000,), float("nan"), device="cuda")
     scale = K ** -0.5
     rc = f(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), H * K, H * K, HV * K, gd.data_ptr(), bd.data_ptr(), HV, HV,
            h0d.data_ptr(), ht.data_ptr(), o.data_ptr(), B, T, H, HV, scale, 0, 2, 1, dbg.data_ptr(),
@@ -66,7 +66,8 @@ def expected(d):
     G = np.cumsum(d['g'][0, :64, 0].astype(np.float64))
     bt = d['beta'][0, :64, 0].astype(np.float64)
     e = {}
-    e['D1'] = np.concatenate([K_ @ K_.T, Q_ @ K_.T], 0)
+    KQ = np.concatenate([K_, Q_], 0)
+    e['D1'] = KQ @ KQ.T
     kn = 1 / np.sqrt(np.diag(K_ @ K_.T) + 1e-6)
     qn = d['scale'] / np.sqrt((Q_ * Q_).sum(1) + 1e-6)
     e['NORM'] = np.concatenate([kn, qn])
@@ -89,7 +90,7 @@ def expected(d):
     return e
 
 
-SHAPES = dict(D1=(128, 64), W=(128, 64), U=(128, 64), X=(128, 64), Y=(128, 64), O=(128, 64), DS=(128, 128),
+SHAPES = dict(D1=(128, 128), W=(128, 64), U=(128, 64), X=(128, 64), Y=(128, 64), O=(128, 64), DS=(128, 128),
               T=(64, 64), NORM=(128,))
 ORDER = ['D1', 'NORM', 'T', 'W', 'U', 'X', 'Y', 'O', 'DS']
 TOL = dict(D1=2e-3, NORM=2e-3, T=2e-3, W=1e-2, U=1e-2, X=2e-2, Y=1e-2, O=2e-2, DS=2e-2)

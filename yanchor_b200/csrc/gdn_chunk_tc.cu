@@ -6,7 +6,7 @@
 // from TMA and the L2 norms folded into fp32 scale factors (kn_j = 1/|k_j|,
 // qn_i = scale/|q_i|), G the in-chunk cumulative log decay:
 //
-//   MMA1  [K;Q] K^T              -> k_i.k_j and q_i.k_j            (TMEM)
+//   MMA1  [K;Q][K;Q]^T            -> k_i.k_j, q_i.k_j, and |k|^2, |q|^2 on the diagonal
 //   epi   L_ij = beta_i e^{G_i-G_j} kn_i kn_j k_i.k_j   (j < i),
 //         P_ij = qn_i kn_j e^{G_i-G_j} q_i.k_j           (j <= i)
 //   SIMT  T = (I + L)^-1 in fp32 (16x16 blocked forward substitution)
@@ -15,8 +15,8 @@
 //   MMA3  X^T = S^T W^T, Y^T = S^T q^T                          (state bf16)
 //   epi   v_new^T = U^T - X^T
 //   MMA4  O^T = v_new^T P^T
-//   MMA5  D^T = (v_new^T * e^{G_last-G} kn) k
-//   epi   o = e^{G} qn Y + O ;  S^T <- e^{G_last} S^T + D^T    (fp32 in TMEM)
+//   MMA5  D^T = (v_new^T * e^{G_last-G} kn) k     (that operand as bf16 hi + lo)
+//   epi   S^T <- e^{G_last} S^T + D^T   (fp32 in TMEM);   o = e^{G} qn Y + O
 //
 // (the chunk form of transformers qwen3_5 modeling_qwen3_5.py:234-311 and
 // of fla's chunk_gated_delta_rule_fwd).  Every state-dependent product is
@@ -44,35 +44,39 @@ constexpr int KD = 128;     // key dim
 constexpr int VD = 128;     // value dim
 constexpr int NTHREADS = 192;
 constexpr int EPI_THREADS = 128;
+constexpr int LP = 68;      // row pitch (floats) of the fp32 L matrix: 16-byte aligned rows
 
-// ---- shared memory map (bytes) ----
+// ---- shared memory map (bytes); SW128 tiles on 1024-byte boundaries ----
 constexpr uint32_t OFF_KQ0 = 0;            // [K;Q] stage 0: 128 rows x 128 cols, 2 column blocks
 constexpr uint32_t OFF_KQ1 = 32768;
 constexpr uint32_t OFF_V0 = 65536;         // V stage 0: 64 rows x 128 cols
 constexpr uint32_t OFF_V1 = 81920;
-constexpr uint32_t OFF_LF = 98304;         // L fp32 64x64 / o staging bf16 64x128
-constexpr uint32_t OFF_TF = 114688;        // T fp32 64x64
-constexpr uint32_t OFF_P = 131072;         // P bf16 64x64 (SW128)
-constexpr uint32_t OFF_TW = 139264;        // Tw bf16 64x64 (SW128); solve scratch before that
-constexpr uint32_t OFF_TU = 147456;        // Tu bf16 64x64 (SW128)
-constexpr uint32_t OFF_WT = 155648;        // W^T bf16 128x64 (SW128) / v~ (v_new scaled) 128x64
-constexpr uint32_t OFF_VN = 172032;        // v_new^T bf16 128x64
-constexpr uint32_t OFF_ST = 188416;        // S^T bf16 128x128 (2 column blocks)
-constexpr uint32_t OFF_GST = 221184;       // per stage: G, beta, e^G, e^{G_last-G} (4 x 64 floats)
+constexpr uint32_t OFF_LF = 98304;         // L fp32 64 x LP, later the o staging tile bf16 64x128
+constexpr uint32_t OFF_TF = 115712;        // v~_lo bf16 128x64 (SW128)
+constexpr uint32_t OFF_P = 133120;         // P bf16 64x64 (SW128)
+constexpr uint32_t OFF_TW = 141312;        // Tw bf16 64x64 (SW128); solve scratch before that
+constexpr uint32_t OFF_TU = 149504;        // Tu bf16 64x64 (SW128)
+constexpr uint32_t OFF_WT = 157696;        // W^T bf16 128x64 (SW128), later v~_hi
+constexpr uint32_t OFF_VN = 174080;        // v_new^T bf16 128x64
+constexpr uint32_t OFF_ST = 190464;        // S^T bf16 128x128 (2 column blocks)
+constexpr uint32_t OFF_GST = 223232;       // per stage: G, beta, e^G, e^{G_last-G} (4 x 64 floats)
 constexpr uint32_t OFF_NORM = OFF_GST + 2 * 1024;   // kn[64], qn[64]
 constexpr uint32_t OFF_BAR = OFF_NORM + 512;        // mbarriers
 constexpr uint32_t OFF_MISC = OFF_BAR + 64;         // tmem base, abort flag
 constexpr uint32_t SMEM_BYTES = OFF_MISC + 16;
+static_assert(OFF_LF + 64 * LP * 4 <= OFF_TF && OFF_TF + 16384 <= OFF_P, "L / v~_lo overlap");
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
 // ---- TMEM columns ----
-constexpr uint32_t T_D1 = 0;     // [KK^T; QK^T] 128x64, later O^T
-constexpr uint32_t T_W = 64;     // W^T, later X^T
+constexpr uint32_t T_D1 = 0;     // [K;Q][K;Q]^T 128x128 (cols 0..127); later O^T (cols 0..63)
+constexpr uint32_t T_W = 64;     // W^T, later X^T (inside D1's columns: D1 is dead by then)
 constexpr uint32_t T_U = 128;    // U^T
 constexpr uint32_t T_Y = 192;    // Y^T
 constexpr uint32_t T_DS = 256;   // D^T (128 columns)
 constexpr uint32_t T_S = 384;    // S^T fp32 state (128 columns)
 
 constexpr uint32_t ID_N64_KK = idesc_bf16(128, 64, false, false);
+constexpr uint32_t ID_N128_KK = idesc_bf16(128, 128, false, false);
 constexpr uint32_t ID_N64_MK = idesc_bf16(128, 64, true, false);
 constexpr uint32_t ID_N64_KM = idesc_bf16(128, 64, false, true);
 constexpr uint32_t ID_N128_KM = idesc_bf16(128, 128, false, true);
@@ -106,7 +110,50 @@ __device__ __forceinline__ float load_scalar(const void *p, int64_t idx, int dty
 }
 
 __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// epilogue threads 0..63 (warps 4 and 5) only: the phases of the triangular solve
+__device__ __forceinline__ void solve_sync() { asm volatile("bar.sync 2, 64;" ::: "memory"); }
 
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+// acc (16x16 as two 16x8 tiles, m16n8 accumulator fragments) += A (16x16) B (16x16),
+// both fp32 row-major in shared memory (pitches lda, ldb), on the warp-level tf32
+// tensor-core path (these 16x16 blocks are far below tcgen05's 128-row tiles).
+__device__ __forceinline__ void block_mma16_tf32(float acc[2][4], const float *pa, int lda, const float *pb, int ldb) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int k0 = 0; k0 < 16; k0 += 8) {
+    const uint32_t a0 = to_tf32(pa[g * lda + k0 + t]), a1 = to_tf32(pa[(g + 8) * lda + k0 + t]);
+    const uint32_t a2 = to_tf32(pa[g * lda + k0 + t + 4]), a3 = to_tf32(pa[(g + 8) * lda + k0 + t + 4]);
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const uint32_t b0 = to_tf32(pb[(k0 + t) * ldb + nt * 8 + g]), b1 = to_tf32(pb[(k0 + t + 4) * ldb + nt * 8 + g]);
+      asm volatile(
+          "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+          "{%0,%1,%2,%3};"
+          : "+f"(acc[nt][0]), "+f"(acc[nt][1]), "+f"(acc[nt][2]), "+f"(acc[nt][3])
+          : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    }
+  }
+}
+
+// dst (16x16 fp32, pitch ld) = sign * acc
+__device__ __forceinline__ void store_block16(float *dst, int ld, const float acc[2][4], float sign) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    dst[g * ld + nt * 8 + 2 * t] = sign * acc[nt][0];
+    dst[g * ld + nt * 8 + 2 * t + 1] = sign * acc[nt][1];
+    dst[(g + 8) * ld + nt * 8 + 2 * t] = sign * acc[nt][2];
+    dst[(g + 8) * ld + nt * 8 + 2 * t + 1] = sign * acc[nt][3];
+  }
+}
+
+constexpr int DBG_D1 = 0, DBG_W = 16384, DBG_U = 24576, DBG_X = 32768, DBG_Y = 40960, DBG_O = 49152,
+              DBG_DS = 57344, DBG_T = 73728, DBG_NORM = 77824, DBG_TS = 78000;
 #ifdef YB_TC_DEBUG
 // Test-only: copy `n` values of TMEM row r (already in registers) into the
 // debug buffer at tile offset `off` (row-major, `n` columns).
@@ -115,14 +162,6 @@ __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" :::
     if (p.dbg && blockIdx.x == 0 && c == 0)                                            \
       for (int _i = 0; _i < (n); ++_i) p.dbg[(off) + r * (n) + _i] = (vals)[_i];       \
   } while (0)
-#else
-#define YB_DBG_ROW(off, n, vals) \
-  do {                           \
-  } while (0)
-#endif
-constexpr int DBG_D1 = 0, DBG_W = 8192, DBG_U = 16384, DBG_X = 24576, DBG_Y = 32768, DBG_O = 40960,
-              DBG_DS = 49152, DBG_T = 65536, DBG_NORM = 69632, DBG_TS = 70000;
-#ifdef YB_TC_DEBUG
 // Test-only: phase timestamps (ns since the thread started) of epilogue
 // thread 0 of CTA 0 for the first 32 chunks, 16 events per chunk.
 #define YB_DBG_TS(ev)                                                                   \
@@ -131,10 +170,27 @@ constexpr int DBG_D1 = 0, DBG_W = 8192, DBG_U = 16384, DBG_X = 24576, DBG_Y = 32
       p.dbg[DBG_TS + c * 16 + (ev)] = float(globaltimer_ns() - dbg_t0);                 \
   } while (0)
 #else
+#define YB_DBG_ROW(off, n, vals) \
+  do {                           \
+  } while (0)
 #define YB_DBG_TS(ev) \
   do {                \
   } while (0)
 #endif
+
+// 64 values -> one SW128 row of bf16 (8 x 16-byte stores), and as two
+// 32-value halves (one per TMEM load) for the state copy.
+__device__ __forceinline__ void st_half_bf16(uint8_t *tile, int rows, int cb, int r, int jbase, const float *v) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 w;
+    w.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+    w.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+    w.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+    w.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+    *reinterpret_cast<uint4 *>(tile + sw128_off(rows, cb, r, jbase + j)) = w;
+  }
+}
 
 __global__ void __launch_bounds__(NTHREADS, 1)
     gdn_chunk_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
@@ -272,11 +328,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const uint32_t vt = smem_u32(smem + (s ? OFF_V1 : OFF_V0));
         if (!mbar_wait(&full[s], (c >> 1) & 1, abort_flag, ERR_WAIT_FULL)) break;
         tc_fence_after();
-        // MMA1: [K;Q] K^T  (M=128, N=64, K=128)
+        // MMA1: [K;Q] [K;Q]^T  (M=128, N=128, K=128)
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          mma_bf16(tmem + T_D1, sdesc(kq + off, 16, 1024), sdesc(kq + off, 16, 1024), ID_N64_KK, kk > 0);
+          mma_bf16(tmem + T_D1, sdesc(kq + off, 16, 1024), sdesc(kq + off, 16, 1024), ID_N128_KK, kk > 0);
         }
         mma_commit(mma_bar);
         if (!wait_epi()) break;
@@ -332,8 +388,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const bool l2 = p.flags & YB_GDN_QK_L2NORM;
     uint8_t *st_tile = smem + OFF_ST;
     float *LF = reinterpret_cast<float *>(smem + OFF_LF);
-    float *TF = reinterpret_cast<float *>(smem + OFF_TF);
-    float *scr = reinterpret_cast<float *>(smem + OFF_TW);
     int mma_phase = 0;
     bool ok = true;
     auto wait_mma = [&]() {
@@ -367,15 +421,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             else p.ht[head + int64_t(dd) * VD + r] = row[d];
           }
         }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint4 w;
-          w.x = pack_bf16x2(row[8 * j + 0], row[8 * j + 1]);
-          w.y = pack_bf16x2(row[8 * j + 2], row[8 * j + 3]);
-          w.z = pack_bf16x2(row[8 * j + 4], row[8 * j + 5]);
-          w.w = pack_bf16x2(row[8 * j + 6], row[8 * j + 7]);
-          *reinterpret_cast<uint4 *>(st_tile + sw128_off(128, q4 >> 1, r, (q4 & 1) * 4 + j)) = w;
-        }
+        st_half_bf16(st_tile, 128, q4 >> 1, r, (q4 & 1) * 4, row);
       }
       tmem_wait_st();
       signal_mma();
@@ -383,7 +429,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
     for (int c = 0; c < nchunks && ok; ++c) {
       const int s = c & 1;
-      const uint8_t *kq = smem + (s ? OFF_KQ1 : OFF_KQ0);
       const float *gst = reinterpret_cast<const float *>(smem + OFF_GST + s * 1024);
       const float *G = gst, *BT = gst + 64, *EG = gst + 128, *TAIL = gst + 192;
       const int m = int(len - int64_t(c) * C < C ? len - int64_t(c) * C : C);
@@ -392,121 +437,154 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       YB_DBG_TS(1);
       if (!wait_mma()) break;   // MMA1 done
       YB_DBG_TS(2);
-      // ---------- step 2: norms, L, P ----------
+      // ---------- step 2: norms (diagonal of D1), L, P ----------
       float d1[64];
       tmem_ld32(lane_base + T_D1, d1);
       tmem_ld32(lane_base + T_D1 + 32, d1 + 32);
-      tmem_wait_ld();
-      YB_DBG_ROW(DBG_D1, 64, d1);
-      if (r < 64) {
+      {
+        float dg[32];   // the 32 columns holding this thread's own diagonal entry
+        tmem_ld32(lane_base + T_D1 + uint32_t(r & ~31), dg);
+        tmem_wait_ld();
+        YB_DBG_TS(13);
+#ifdef YB_TC_DEBUG
+        if (p.dbg && blockIdx.x == 0 && c == 0) {
+          float full_row[32];
+          for (int q4 = 0; q4 < 4; ++q4) {
+            tmem_ld32(lane_base + T_D1 + q4 * 32, full_row);
+            tmem_wait_ld();
+            for (int t = 0; t < 32; ++t) p.dbg[DBG_D1 + r * 128 + q4 * 32 + t] = full_row[t];
+          }
+        }
+#endif
         float diag = 0.f;
 #pragma unroll
-        for (int j = 0; j < 64; ++j) diag = (j == r) ? d1[j] : diag;
-        kn[r] = l2 ? rsqrtf(diag + 1e-6f) : 1.f;
-      } else {
-        const int i = r - 64;
-        float ss = 0.f;
-#pragma unroll
-        for (int cb = 0; cb < 2; ++cb)
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float x[8];
-            ld_chunk_bf16(kq, 128, cb, 64 + i, j, x);
-#pragma unroll
-            for (int t = 0; t < 8; ++t) ss += x[t] * x[t];
-          }
-        qn[i] = (l2 ? rsqrtf(ss + 1e-6f) : 1.f) * p.scale;
+        for (int t = 0; t < 32; ++t) diag = (t == lane) ? dg[t] : diag;
+        const float nrm = l2 ? rsqrtf(diag + 1e-6f) : 1.f;
+        if (r < 64) kn[r] = nrm;
+        else qn[r - 64] = nrm * p.scale;
       }
       epi_sync();
+      YB_DBG_TS(14);
       if (r < 64) {
-        const int i = r;
-        const float ci = BT[i] * kn[i], gi = G[i];
+        // threads 0..63: row r of L, then column r of T = (I + L)^-1 ...
+        {
+          const int i = r;
+          const float ci = BT[i] * kn[i], gi = G[i];
 #pragma unroll
-        for (int j4 = 0; j4 < 16; ++j4) {
-          float4 v4;
-          float *vv = reinterpret_cast<float *>(&v4);
+          for (int j4 = 0; j4 < 16; ++j4) {
+            float4 v4;
+            float *vv = reinterpret_cast<float *>(&v4);
 #pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const int j = 4 * j4 + t;
-            vv[t] = j < i ? ci * kn[j] * __expf(gi - G[j]) * d1[j] : 0.f;
+            for (int t = 0; t < 4; ++t) {
+              // branch-free mask (the exponent is clamped so masked lanes stay finite)
+              const int j = 4 * j4 + t;
+              vv[t] = ci * kn[j] * __expf(fminf(gi - G[j], 0.f)) * d1[j] * float(j < i);
+            }
+            *reinterpret_cast<float4 *>(LF + i * LP + 4 * j4) = v4;
           }
-          *reinterpret_cast<float4 *>(LF + i * 64 + 4 * j4) = v4;
+        }
+        YB_DBG_TS(15);
+        solve_sync();
+        YB_DBG_TS(3);
+        // ---- T = (I + L)^-1 by 16x16 blocks: T_ii = D_i (diagonal inverses),
+        //      T_ij = -sum_{m=j}^{i-1} M_im T_mj with M_im = D_i L_im ----
+        float *TF = reinterpret_cast<float *>(smem + OFF_TF);   // T fp32, pitch LP
+        float *MB = reinterpret_cast<float *>(smem + OFF_TW);   // six M blocks, pitch 20
+        {
+          // diagonal blocks: thread j solves column j of its block in registers
+          const int j = r, b = j >> 4, jj = j & 15;
+          float x[16];
+#pragma unroll
+          for (int ii = 0; ii < 16; ++ii) {
+            const float *Lrow = LF + (b * 16 + ii) * LP + b * 16;
+            float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+            for (int mm = 0; mm + 1 < ii; mm += 2) {
+              a0 = fmaf(Lrow[mm], x[mm], a0);
+              a1 = fmaf(Lrow[mm + 1], x[mm + 1], a1);
+            }
+            if (ii & 1) a0 = fmaf(Lrow[ii - 1], x[ii - 1], a0);
+            x[ii] = ii < jj ? 0.f : (ii == jj ? 1.f : -(a0 + a1));
+          }
+#pragma unroll
+          for (int ii = 0; ii < 16; ++ii) TF[(b * 16 + ii) * LP + j] = x[ii];
+          for (int row = 0; row < b * 16; ++row) TF[row * LP + j] = 0.f;   // upper blocks
+        }
+        solve_sync();
+        // M blocks, list order (1,0) (2,1) (3,2) (2,0) (3,1) (3,0); warp w of the two takes k = w, w+2, w+4
+        const int sw = r >> 5;
+        for (int k = sw; k < 6; k += 2) {
+          const int bi = k < 3 ? k + 1 : (k == 5 ? 3 : k - 1), bm = k < 3 ? k : (k == 3 ? 0 : (k == 4 ? 1 : 0));
+          float acc[2][4] = {};
+          block_mma16_tf32(acc, TF + bi * 16 * LP + bi * 16, LP, LF + bi * 16 * LP + bm * 16, LP);
+          store_block16(MB + k * 320, 20, acc, 1.f);
+        }
+        solve_sync();
+        // distance 1: T_(i,i-1) = -M_(i,i-1) D_(i-1),  i = 1..3
+        for (int i = 1 + sw; i < 4; i += 2) {
+          float acc[2][4] = {};
+          block_mma16_tf32(acc, MB + (i - 1) * 320, 20, TF + (i - 1) * 16 * LP + (i - 1) * 16, LP);
+          store_block16(TF + i * 16 * LP + (i - 1) * 16, LP, acc, -1.f);
+        }
+        solve_sync();
+        // distance 2: T_(i,i-2) = -(M_(i,i-2) D_(i-2) + M_(i,i-1) T_(i-1,i-2)),  i = 2 (warp 0), 3 (warp 1)
+        {
+          const int i = 2 + sw;
+          float acc[2][4] = {};
+          block_mma16_tf32(acc, MB + (i + 1) * 320, 20, TF + (i - 2) * 16 * LP + (i - 2) * 16, LP);
+          block_mma16_tf32(acc, MB + (i - 1) * 320, 20, TF + (i - 1) * 16 * LP + (i - 2) * 16, LP);
+          store_block16(TF + i * 16 * LP + (i - 2) * 16, LP, acc, -1.f);
+        }
+        solve_sync();
+        // distance 3: T_(3,0) = -(M_30 D_0 + M_31 T_10 + M_32 T_20)
+        if (sw == 0) {
+          float acc[2][4] = {};
+          block_mma16_tf32(acc, MB + 5 * 320, 20, TF, LP);
+          block_mma16_tf32(acc, MB + 4 * 320, 20, TF + 16 * LP, LP);
+          block_mma16_tf32(acc, MB + 2 * 320, 20, TF + 32 * LP, LP);
+          store_block16(TF + 48 * LP, LP, acc, -1.f);
         }
       } else {
+        // threads 64..127: row r-64 of P, concurrently
         const int i = r - 64;
         const float ci = qn[i], gi = G[i];
         float pr[64];
 #pragma unroll
-        for (int j = 0; j < 64; ++j) pr[j] = j <= i ? ci * kn[j] * __expf(gi - G[j]) * d1[j] : 0.f;
+        for (int j = 0; j < 64; ++j) pr[j] = ci * kn[j] * __expf(fminf(gi - G[j], 0.f)) * d1[j] * float(j <= i);
         st_row64_bf16(smem + OFF_P, 64, 0, i, pr);
       }
       epi_sync();
-      YB_DBG_TS(3);
-      // ---------- T = (I + L)^-1, 16x16 blocks ----------
-      if (r < 64) {
-        const int j = r, b = j >> 4, jj = j & 15;
-        float x[16];
-#pragma unroll
-        for (int ii = 0; ii < 16; ++ii) {
-          const float *Lrow = LF + (b * 16 + ii) * 64 + b * 16;
-          float acc = 0.f;
-#pragma unroll
-          for (int mm = 0; mm < ii; ++mm) acc = fmaf(Lrow[mm], x[mm], acc);
-          x[ii] = ii < jj ? 0.f : (ii == jj ? 1.f : -acc);
-        }
-        for (int row = 0; row < 64; ++row) {
-          const int rb = row >> 4;
-          TF[row * 64 + j] = rb == b ? x[row & 15] : 0.f;  // blocks below the diagonal are filled next
-        }
-      }
-      epi_sync();
-      for (int dlev = 1; dlev < 4; ++dlev) {
-        const int nb = 4 - dlev;
-        // Y_(bi,bj) = sum_{m in blocks bj..bi-1} L[bi-rows][m] T[m][bj-cols]
-        for (int e = r; e < nb * 256; e += EPI_THREADS) {
-          const int blk = e >> 8, rr = (e >> 4) & 15, cc = e & 15;
-          const int bi = dlev + blk, bj = blk;
-          const float *Lrow = LF + (bi * 16 + rr) * 64;
-          float acc = 0.f;
-          for (int mcol = bj * 16; mcol < bi * 16; ++mcol) acc = fmaf(Lrow[mcol], TF[mcol * 64 + bj * 16 + cc], acc);
-          scr[e] = acc;
-        }
-        epi_sync();
-        // T_(bi,bj) = -T_(bi,bi) Y
-        for (int e = r; e < nb * 256; e += EPI_THREADS) {
-          const int blk = e >> 8, rr = (e >> 4) & 15, cc = e & 15;
-          const int bi = dlev + blk, bj = blk;
-          const float *Trow = TF + (bi * 16 + rr) * 64 + bi * 16;
-          float acc = 0.f;
-#pragma unroll
-          for (int t = 0; t < 16; ++t) acc = fmaf(Trow[t], scr[(blk << 8) + t * 16 + cc], acc);
-          TF[(bi * 16 + rr) * 64 + bj * 16 + cc] = -acc;
-        }
-        epi_sync();
-      }
       YB_DBG_TS(4);
-      // Tw (rows 0..63 by threads 0..63), Tu (threads 64..127)
+      // Tw (rows by threads 0..63) and Tu (threads 64..127) from T, as bf16 tiles
       {
+        const float *TF = reinterpret_cast<const float *>(smem + OFF_TF);
         const int i = r & 63;
         float rowv[64];
+#pragma unroll
+        for (int j4 = 0; j4 < 16; ++j4) {
+          const float4 t4 = *reinterpret_cast<const float4 *>(TF + i * LP + 4 * j4);
+          rowv[4 * j4] = t4.x;
+          rowv[4 * j4 + 1] = t4.y;
+          rowv[4 * j4 + 2] = t4.z;
+          rowv[4 * j4 + 3] = t4.w;
+        }
+#ifdef YB_TC_DEBUG
+        if (p.dbg && blockIdx.x == 0 && c == 0) {
+          if (r < 64)
+            for (int j = 0; j < 64; ++j) p.dbg[DBG_T + r * 64 + j] = rowv[j];
+          p.dbg[DBG_NORM + r] = r < 64 ? kn[r] : qn[r - 64];
+        }
+#endif
         if (r < 64) {
 #pragma unroll
-          for (int j = 0; j < 64; ++j) rowv[j] = TF[i * 64 + j] * BT[j] * EG[j] * kn[j];
+          for (int j = 0; j < 64; ++j) rowv[j] *= BT[j] * EG[j] * kn[j];
           st_row64_bf16(smem + OFF_TW, 64, 0, i, rowv);
         } else {
 #pragma unroll
-          for (int j = 0; j < 64; ++j) rowv[j] = TF[i * 64 + j] * BT[j];
+          for (int j = 0; j < 64; ++j) rowv[j] *= BT[j];
           st_row64_bf16(smem + OFF_TU, 64, 0, i, rowv);
         }
       }
-#ifdef YB_TC_DEBUG
-      if (p.dbg && blockIdx.x == 0 && c == 0) {
-        if (r < 64)
-          for (int j = 0; j < 64; ++j) p.dbg[DBG_T + r * 64 + j] = TF[r * 64 + j];
-        p.dbg[DBG_NORM + r] = r < 64 ? kn[r] : qn[r - 64];
-      }
-#endif
-      tc_fence_before();
       signal_mma();
       YB_DBG_TS(5);
       // ---------- step 4: W^T -> smem (MN-major B operand of MMA3) ----------
@@ -548,9 +626,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
       signal_mma();
       YB_DBG_TS(9);
-      // ---------- step 8: outputs and the state update ----------
+      // ---------- step 8: state update first (it gates the next chunk), then o ----------
       if (!wait_mma()) break;
       YB_DBG_TS(10);
+      uint32_t opk[32];   // this thread's o column as packed bf16 pairs (tokens 2t, 2t+1)
       {
         float y[64], oo[64];
         tmem_ld32(lane_base + T_Y, y);
@@ -560,9 +639,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         tmem_wait_ld();
         YB_DBG_ROW(DBG_Y, 64, y);
         YB_DBG_ROW(DBG_O, 64, oo);
-        __nv_bfloat16 *ostage = reinterpret_cast<__nv_bfloat16 *>(smem + OFF_LF);  // [64][128]
 #pragma unroll
-        for (int i = 0; i < 64; ++i) ostage[i * 128 + r] = __float2bfloat16_rn(EG[i] * qn[i] * y[i] + oo[i]);
+        for (int t = 0; t < 32; ++t)
+          opk[t] = pack_bf16x2(EG[2 * t] * qn[2 * t] * y[2 * t] + oo[2 * t],
+                               EG[2 * t + 1] * qn[2 * t + 1] * y[2 * t + 1] + oo[2 * t + 1]);
       }
       {
         const float decay = EG[63];   // e^{G_last}
@@ -580,15 +660,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
           for (int d = 0; d < 32; ++d) sv[d] = fmaf(decay, sv[d], dv[d]);
           tmem_st32(lane_base + T_S + q4 * 32, sv);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint4 w;
-            w.x = pack_bf16x2(sv[8 * j + 0], sv[8 * j + 1]);
-            w.y = pack_bf16x2(sv[8 * j + 2], sv[8 * j + 3]);
-            w.z = pack_bf16x2(sv[8 * j + 4], sv[8 * j + 5]);
-            w.w = pack_bf16x2(sv[8 * j + 6], sv[8 * j + 7]);
-            *reinterpret_cast<uint4 *>(st_tile + sw128_off(128, q4 >> 1, r, (q4 & 1) * 4 + j)) = w;
-          }
+          st_half_bf16(st_tile, 128, q4 >> 1, r, (q4 & 1) * 4, sv);
           if (last && p.ht) {
 #pragma unroll
             for (int d = 0; d < 32; ++d) {
@@ -601,20 +673,32 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         tmem_wait_st();
       }
       YB_DBG_TS(11);
-      epi_sync();
+      // release the MMA warp (next chunk's MMA1 overlaps the output store below)
+      // and the stage's gates / tiles (everything read from them is in registers)
+      signal_mma();
+      if (r == 0) mbar_arrive(&empty[s]);
       {
-        // coalesced store of the o tile: row i = r / 2, half = r % 2 (128 bytes each)
-        const int i = r >> 1, half = r & 1;
-        if (i < m) {
-          const uint4 *src = reinterpret_cast<const uint4 *>(smem + OFF_LF + i * 256 + half * 128);
-          uint4 *dst = reinterpret_cast<uint4 *>(p.o + ((bos + int64_t(c) * C + i) * p.HV + hv) * VD + half * 64);
+        __nv_bfloat16 *ostage = reinterpret_cast<__nv_bfloat16 *>(smem + OFF_LF);  // [64][128]
 #pragma unroll
-          for (int t = 0; t < 8; ++t) dst[t] = src[t];
+        for (int t = 0; t < 32; ++t) {
+          const __nv_bfloat162 pr2 = *reinterpret_cast<const __nv_bfloat162 *>(&opk[t]);
+          ostage[(2 * t) * 128 + r] = pr2.x;
+          ostage[(2 * t + 1) * 128 + r] = pr2.y;
         }
       }
       epi_sync();
-      if (r == 0) mbar_arrive(&empty[s]);   // stage's gates / tiles no longer read
-      signal_mma();
+      {
+        // copy the o tile out: 16-byte piece q = r + 128 t covers row q / 16, bytes 16 (q % 16);
+        // consecutive threads touch consecutive pieces (conflict-free, coalesced)
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          const int q = r + 128 * t, i = q >> 4, piece = q & 15;
+          if (i < m) {
+            const uint4 v = *reinterpret_cast<const uint4 *>(smem + OFF_LF + q * 16);
+            *reinterpret_cast<uint4 *>(p.o + ((bos + int64_t(c) * C + i) * p.HV + hv) * VD + piece * 8) = v;
+          }
+        }
+      }
       YB_DBG_TS(12);
     }
   }
