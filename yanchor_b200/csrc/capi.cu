@@ -68,7 +68,10 @@ extern "C" {
 
 const char *yb_last_error(void) { return g_err; }
 int yb_abi_version(void) { return 1; }
-int yb_device_error(int clear) { return read_device_error(clear); }
+int yb_device_error(int clear) {
+  const int a = read_device_error(clear), b = read_device_error_idx(clear);
+  return a ? a : b;
+}
 
 int yb_gdn_recurrent_fwd(const void *q, const void *k, const void *v, int64_t q_tok_stride, int64_t k_tok_stride,
                          int64_t v_tok_stride, const void *g, const void *beta, int64_t g_tok_stride,

@@ -78,6 +78,9 @@ struct MemIndexedArgs {
   cudaStream_t stream;
 };
 int launch_mem_indexed_read(const MemIndexedArgs &a);
+bool mem_indexed_tc_supported(const MemIndexedArgs &a);
+int launch_mem_indexed_tc(const MemIndexedArgs &a);
+int read_device_error_idx(int clear);
 
 struct SampleArgs {
   const void *scores;

@@ -289,14 +289,15 @@ __global__ void __launch_bounds__(kIdxThreads) mem_indexed_read_kernel(const Mem
     const int slot = e / (D / 8), d8 = (e % (D / 8)) * 8;
     const int64_t ref = refs[slot];
     float kx[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, vx[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (ref >= 0) {
+    const bool ok_ref = ref >= 0 && ref < a.S;  // out-of-range references read as empty
+    if (ok_ref) {
       const int64_t off = ((kb * a.S + ref) * a.G + g) * D + d8;
       load8(kbase + off, kx);
       load8(vbase + off, vx);
     }
     store8(sk + slot * PITCH + d8, kx);
     store8(sv + slot * PITCH + d8, vx);
-    if (d8 == 0) svalid[slot] = ref >= 0;
+    if (d8 == 0) svalid[slot] = ok_ref;
   }
   __syncthreads();
   const float scale = rsqrtf(float(D));
@@ -442,6 +443,7 @@ int launch_mem_decode_commit(const MemCommitArgs &a) {
 
 int launch_mem_indexed_read(const MemIndexedArgs &a) {
   if (a.B * a.blocks * a.G == 0) return YB_OK;
+  if (mem_indexed_tc_supported(a)) return launch_mem_indexed_tc(a);
   if (a.CAP > kIdxMaxCap)
     return set_error(YB_ERR_UNSUPPORTED, "indexed read: CAP=%lld exceeds %d", (long long)a.CAP, kIdxMaxCap);
   switch (a.dtype) {
