@@ -21,6 +21,12 @@ def bf(x):
     return torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).to(torch.bfloat16).float().numpy()
 
 
+def hilo(x):
+    """x as the kernel feeds it to the tensor cores: bf16 hi + bf16 lo."""
+    h = bf(x)
+    return h + bf(np.asarray(x, np.float32) - h)
+
+
 def relerr(a, b):
     return float(np.linalg.norm(np.asarray(a, np.float64) - b) / max(np.linalg.norm(b), 1e-30))
 
@@ -75,8 +81,8 @@ def expected(d):
     L = np.tril(bt[:, None] * kn[:, None] * kn[None, :] * dec * (K_ @ K_.T), -1)
     Tm = np.linalg.inv(np.eye(64) + L)
     e['T'] = Tm
-    Tw = bf(Tm * (bt * np.exp(G) * kn)[None, :])
-    Tu = bf(Tm * bt[None, :])
+    Tw = hilo(Tm * (bt * np.exp(G) * kn)[None, :])
+    Tu = hilo(Tm * bt[None, :])
     e['W'] = K_.T @ Tw.T
     e['U'] = V_.T @ Tu.T
     ST = bf(d['h0'][0, 0].T)
@@ -85,7 +91,7 @@ def expected(d):
     vn = e['U'] - e['X']
     P = bf(np.tril(qn[:, None] * kn[None, :] * dec * (Q_ @ K_.T)))
     e['O'] = bf(vn) @ P.T
-    vt = bf(vn * (np.exp(G[-1] - G) * kn)[None, :])
+    vt = hilo(vn * (np.exp(G[-1] - G) * kn)[None, :])
     e['DS'] = vt @ K_
     return e
 
@@ -93,7 +99,7 @@ def expected(d):
 SHAPES = dict(D1=(128, 128), W=(128, 64), U=(128, 64), X=(128, 64), Y=(128, 64), O=(128, 64), DS=(128, 128),
               T=(64, 64), NORM=(128,))
 ORDER = ['D1', 'NORM', 'T', 'W', 'U', 'X', 'Y', 'O', 'DS']
-TOL = dict(D1=2e-3, NORM=2e-3, T=2e-3, W=1e-2, U=1e-2, X=2e-2, Y=1e-2, O=2e-2, DS=2e-2)
+TOL = dict(D1=2e-3, NORM=2e-3, T=2e-3, W=2e-3, U=2e-3, X=2e-2, Y=1e-2, O=2e-2, DS=2e-2)
 
 
 @pytest.mark.parametrize('stage', ORDER)

@@ -11,7 +11,7 @@
 //         P_ij = qn_i kn_j e^{G_i-G_j} q_i.k_j           (j <= i)
 //   SIMT  T = (I + L)^-1 in fp32 (16x16 blocked forward substitution)
 //   MMA2  W^T = k^T Tw^T, U^T = v^T Tu^T   with Tw_ij = T_ij beta_j e^{G_j} kn_j,
-//                                                Tu_ij = T_ij beta_j
+//                                                Tu_ij = T_ij beta_j   (bf16 hi + lo)
 //   MMA3  X^T = S^T W^T, Y^T = S^T q^T                          (state bf16)
 //   epi   v_new^T = U^T - X^T
 //   MMA4  O^T = v_new^T P^T
@@ -51,7 +51,9 @@ constexpr uint32_t OFF_KQ0 = 0;            // [K;Q] stage 0: 128 rows x 128 cols
 constexpr uint32_t OFF_KQ1 = 32768;
 constexpr uint32_t OFF_V0 = 65536;         // V stage 0: 64 rows x 128 cols
 constexpr uint32_t OFF_V1 = 81920;
-constexpr uint32_t OFF_LF = 98304;         // L fp32 64 x LP, later the o staging tile bf16 64x128
+constexpr uint32_t OFF_LF = 98304;         // L fp32 64 x LP, then Tw_lo / Tu_lo, later the o staging tile
+constexpr uint32_t OFF_TWLO = OFF_LF;      // Tw_lo bf16 64x64 (SW128), once L is solved
+constexpr uint32_t OFF_TULO = OFF_LF + 8192;
 constexpr uint32_t OFF_TF = 115712;        // v~_lo bf16 128x64 (SW128)
 constexpr uint32_t OFF_P = 133120;         // P bf16 64x64 (SW128)
 constexpr uint32_t OFF_TW = 141312;        // Tw bf16 64x64 (SW128); solve scratch before that
@@ -65,6 +67,7 @@ constexpr uint32_t OFF_BAR = OFF_NORM + 512;        // mbarriers
 constexpr uint32_t OFF_MISC = OFF_BAR + 64;         // tmem base, abort flag
 constexpr uint32_t SMEM_BYTES = OFF_MISC + 16;
 static_assert(OFF_LF + 64 * LP * 4 <= OFF_TF && OFF_TF + 16384 <= OFF_P, "L / v~_lo overlap");
+static_assert(OFF_TULO + 8192 <= OFF_TF && OFF_TWLO % 1024 == 0 && OFF_TULO % 1024 == 0, "T lo tiles");
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
 // ---- TMEM columns ----
@@ -336,12 +339,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         mma_commit(mma_bar);
         if (!wait_epi()) break;
-        // MMA2: W^T = k^T Tw^T ;  U^T = v^T Tu^T   (M=128, N=64, K=64)
+        // MMA2: W^T = k^T (Tw_hi + Tw_lo)^T ;  U^T = v^T (Tu_hi + Tu_lo)^T   (M=128, N=64, K=64)
         const uint32_t tw = smem_u32(smem + OFF_TW), tu = smem_u32(smem + OFF_TU);
+        const uint32_t twl = smem_u32(smem + OFF_TWLO), tul = smem_u32(smem + OFF_TULO);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           mma_bf16(tmem + T_W, sdesc(kq + kk * 2048, 16384, 1024), sdesc(tw + kk * 32, 16, 1024), ID_N64_MK, kk > 0);
           mma_bf16(tmem + T_U, sdesc(vt + kk * 2048, 8192, 1024), sdesc(tu + kk * 32, 16, 1024), ID_N64_MK, kk > 0);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          mma_bf16(tmem + T_W, sdesc(kq + kk * 2048, 16384, 1024), sdesc(twl + kk * 32, 16, 1024), ID_N64_MK, true);
+          mma_bf16(tmem + T_U, sdesc(vt + kk * 2048, 8192, 1024), sdesc(tul + kk * 32, 16, 1024), ID_N64_MK, true);
         }
         mma_commit(mma_bar);
         if (!wait_epi()) break;
@@ -575,15 +584,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           p.dbg[DBG_NORM + r] = r < 64 ? kn[r] : qn[r - 64];
         }
 #endif
+        // both factors enter MMA2 as bf16 hi + lo: a single bf16 rounding of T
+        // alone costs ~2e-3 relative on the state
         if (r < 64) {
 #pragma unroll
           for (int j = 0; j < 64; ++j) rowv[j] *= BT[j] * EG[j] * kn[j];
-          st_row64_bf16(smem + OFF_TW, 64, 0, i, rowv);
         } else {
 #pragma unroll
           for (int j = 0; j < 64; ++j) rowv[j] *= BT[j];
-          st_row64_bf16(smem + OFF_TU, 64, 0, i, rowv);
         }
+        st_row64_bf16(smem + (r < 64 ? OFF_TW : OFF_TU), 64, 0, i, rowv);
+#pragma unroll
+        for (int j = 0; j < 64; ++j) rowv[j] -= __bfloat162float(__float2bfloat16_rn(rowv[j]));
+        st_row64_bf16(smem + (r < 64 ? OFF_TWLO : OFF_TULO), 64, 0, i, rowv);
       }
       signal_mma();
       YB_DBG_TS(5);
