@@ -10,6 +10,7 @@ Reference algorithms restated here (paths inside the reference project):
                                      runtime/model/independent_memory.py:47-88,177-188
 * ``commit_decode``                  modeling_yanchor.py:291-312 (torch) and
                                      runtime/model/independent_memory.py:90-201
+* ``sequence`` (prefill read + write) modeling_yanchor.py:178-275
 
 The memory state is a dict with the fields of ``IndependentMemoryState``
 (modeling_yanchor.py:80-120): keys/values ``[B, G, CAP, D]``, scores
@@ -17,8 +18,9 @@ The memory state is a dict with the fields of ``IndependentMemoryState``
 pending_values ``[B, G, PC, D]``, pending_scores ``[B, G, PC]`` float32,
 count / total ``[B]`` int64.
 
-Ordering used for every top-CAP selection: score descending, then position
-ascending with invalid entries (reference < 0) last, then candidate order.
+Ordering used for every top-CAP selection: score descending (NaN first),
+then position ascending with invalid entries (reference < 0) last, then
+candidate order.
 Invalid entries come out as (score -inf, position -1, reference -1).
 """
 from __future__ import annotations
@@ -48,9 +50,12 @@ def select_topk(scores, positions, references, capacity):
     idx = np.arange(n)
     take = min(capacity, n)
     for row in range(flat_s.shape[0]):
-        # np.lexsort: last key is primary.  -score puts larger scores first;
-        # -0.0 and 0.0 compare equal, as in a stable float sort.
-        order = np.lexsort((idx, flat_p[row], -flat_s[row]))[:take]
+        # np.lexsort: last key is primary.  NaN scores rank first and tie with
+        # each other (torch's descending sort treats NaN as the largest value);
+        # -score puts larger scores first; -0.0 and 0.0 compare equal, as in a
+        # stable float sort.
+        nan = np.isnan(flat_s[row])
+        order = np.lexsort((idx, flat_p[row], np.where(nan, 0.0, -flat_s[row]), ~nan))[:take]
         out_s[row, :take] = flat_s[row, order]
         out_p[row, :take] = flat_pos[row, order]
         out_r[row, :take] = flat_ref[row, order]
@@ -200,3 +205,138 @@ def empty_state(batch, groups, capacity, pending, dim, dtype=np.float32):
         'count': np.zeros((batch,), np.int64),
         'total': np.zeros((batch,), np.int64),
     }
+
+
+def sequence(query, scores, key_all, value_all, valid, chunk, state=None, capacity=None):
+    """Prefill anchor read and write, ``IndependentGQAMemory._sequence``
+    (modeling_yanchor.py:178-275), restated step by step.
+
+    query ``[B, T, H, D]``; scores ``[B, T, G]`` float32; ``key_all`` /
+    ``value_all`` ``[B, T, G, D]``: the writer's key / value for every token
+    (the reference evaluates the writer only on the tokens it keeps; the
+    writer works row by row, so those rows are the same); ``valid`` ``[B, T]``
+    bool or None; ``state``: a state dict (mutated in place) or None, in which
+    case ``capacity`` gives CAP and nothing is written.  Returns the read
+    ``[B, T, H, D]``.
+
+    The prompt is laid on a timeline of ``extent`` slots: with a state, the
+    first ``count`` slots are the state's pending tokens and the new tokens
+    follow.  Each chunk-sized block of the timeline reads the top-CAP of the
+    blocks before it (plus the state's bank); only tokens that some block can
+    read, or that stay pending afterwards, get a key / value row.
+    """
+    q_in = np.asarray(query, np.float32)
+    s_in = np.asarray(scores, np.float32)
+    B, T, H, D = q_in.shape
+    G = s_in.shape[-1]
+    CAP = state['keys'].shape[2] if state is not None else int(capacity)
+    bi = np.arange(B)[:, None]
+    if valid is None:
+        order = None
+        q, s = q_in, s_in
+        counts = np.full(B, T, np.int64)
+    else:
+        valid = np.asarray(valid, bool)
+        order = np.argsort(~valid, axis=1, kind='stable')          # valid tokens first, stable
+        q, s = q_in[bi, order], s_in[bi, order]
+        counts = valid.sum(1).astype(np.int64)
+    old_count = np.zeros(B, np.int64) if state is None else state['count'].astype(np.int64)
+    old_total = np.zeros(B, np.int64) if state is None else state['total'].astype(np.int64)
+    prefix_length = 0 if state is None else chunk
+    extent = -(-(T + prefix_length) // chunk) * chunk
+    at = np.arange(extent)[None, :].repeat(B, 0)
+    limit = old_count + counts
+    valid_extent = at < limit[:, None]
+    if state is None:
+        q = np.concatenate((q, np.zeros((B, extent - T, H, D), np.float32)), 1)
+        s = np.concatenate((s, np.full((B, extent - T, G), -np.inf, np.float32)), 1)
+        shift = 0
+    else:
+        select = np.where(at < old_count[:, None], at, chunk + at - old_count[:, None])
+        select = np.minimum(select, chunk + T - 1)
+        q = np.concatenate((np.zeros((B, chunk, H, D), np.float32), q), 1)[bi, select]
+        pend = np.asarray(state['pending_scores'], np.float32).transpose(0, 2, 1)[:, :chunk]
+        s = np.concatenate((pend, s), 1)[bi, select]
+        shift = CAP
+    s = np.where(valid_extent[..., None], s, -np.inf).astype(np.float32)
+    positions = (old_total - old_count)[:, None] + at
+    refs = np.where(valid_extent, at + shift, -1)
+    blocks = extent // chunk
+
+    def blocked(x):
+        x = x if x.ndim == 3 else np.repeat(x[..., None], G, -1)
+        return x.reshape(B, blocks, chunk, G).transpose(0, 1, 3, 2)
+
+    prefix = exclusive_prefix_topk(blocked(s), blocked(positions), blocked(refs), CAP)
+    if state is not None:
+        bank_ref = np.where(state['positions'] < 0, -1, np.arange(CAP)[None, None])
+        initial = (state['scores'], state['positions'], bank_ref)
+        prefix = merge_topk(prefix, tuple(np.repeat(x[:, None], blocks + 1, 1) for x in initial), CAP)
+    boundary = (np.arange(1, blocks + 1) * chunk)[None, :, None, None]
+    entrant = prefix[2][:, 1:] - shift
+    if state is None:
+        used = boundary < limit[:, None, None, None]
+    else:
+        used = boundary <= limit[:, None, None, None]
+    take = (entrant >= boundary - chunk) & (entrant < boundary) & used
+    needed = np.zeros((B, extent + 1), bool)
+    target = np.where(take, entrant, extent).reshape(B, -1)
+    needed[np.repeat(np.arange(B), target.shape[1]), target.ravel()] = True
+    if state is not None:
+        full = limit // chunk
+        needed[:, :extent] |= valid_extent & (at >= full[:, None] * chunk)
+    needed = needed[:, :extent] & valid_extent & (at >= old_count[:, None])
+    sel_b, sel_pos = np.nonzero(needed)
+    original = sel_pos - old_count[sel_b]
+    if order is not None:
+        original = order[sel_b, original]
+    k = np.asarray(key_all)[sel_b, original]
+    v = np.asarray(value_all)[sel_b, original]
+    references = np.full((B, shift + extent), -1, np.int64)
+    source_k, source_v = k, v
+    offset = 0
+    if state is not None:
+        offset = B * (CAP + chunk)
+        old_k = np.concatenate((state['keys'], state['pending_keys'][:, :, :chunk]), 2).transpose(0, 2, 1, 3)
+        old_v = np.concatenate((state['values'], state['pending_values'][:, :, :chunk]), 2).transpose(0, 2, 1, 3)
+        source_k = np.concatenate((old_k.reshape(-1, G, D), k), 0)
+        source_v = np.concatenate((old_v.reshape(-1, G, D), v), 0)
+        base = np.arange(B)[:, None] * (CAP + chunk)
+        references[:, :shift] = base + np.arange(shift)[None]
+        references[:, shift:] = np.where(at < old_count[:, None], base + CAP + at, -1)
+    references[sel_b, shift + sel_pos] = offset + np.arange(len(k))
+    zero = np.zeros((1, G, D), source_k.dtype)
+    source_k = np.concatenate((source_k, zero), 0)
+    source_v = np.concatenate((source_v, zero), 0)
+    pre_refs = prefix[2][:, :-1]
+    read_refs = np.where(pre_refs < 0, -1, references[np.arange(B)[:, None, None, None], np.maximum(pre_refs, 0)])
+    read = indexed_gqa(q.reshape(B, blocks, chunk, H, D), source_k[None], source_v[None], read_refs)
+    read = read.reshape(B, extent, H, D)
+    if state is None:
+        output = read[:, :T]
+    else:
+        output = read[bi, np.minimum(old_count[:, None] + np.arange(T)[None], extent - 1)]
+    if order is not None:
+        output = output[bi, np.argsort(order, axis=1)] * valid[..., None, None]
+    if state is not None:
+        rows = np.arange(B)
+        score, position, reference = (x[rows, full] for x in prefix)       # [B, G, CAP]
+        g = np.arange(G)[None, :, None]
+        compact = references[rows[:, None, None], np.maximum(reference, 0)]
+        empty = (reference < 0)[..., None]
+        state['keys'][...] = np.where(empty, 0, source_k[np.maximum(compact, 0), g])
+        state['values'][...] = np.where(empty, 0, source_v[np.maximum(compact, 0), g])
+        state['scores'][...] = score
+        state['positions'][...] = position
+        pc = state['pending_keys'].shape[2]
+        pending = full[:, None] * chunk + np.arange(pc)[None]
+        remaining = limit % chunk
+        mask = np.arange(pc)[None] < remaining[:, None]
+        pending = np.minimum(pending, extent - 1)
+        compact = np.maximum(references[bi, pending + shift], 0)
+        state['pending_keys'][...] = np.where(mask[..., None, None], source_k[compact], 0).transpose(0, 2, 1, 3)
+        state['pending_values'][...] = np.where(mask[..., None, None], source_v[compact], 0).transpose(0, 2, 1, 3)
+        state['pending_scores'][...] = np.where(mask[..., None], s[bi, pending], -np.inf).transpose(0, 2, 1)
+        state['count'][...] = remaining
+        state['total'][...] = old_total + counts
+    return output.astype(np.float32)

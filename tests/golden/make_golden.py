@@ -13,8 +13,8 @@ Python) to a scratch directory, puts it and the reference root first on
   (transformers/models/qwen3_5/modeling_qwen3_5.py:175-353)
 * the gate expression of ``Qwen3_5GatedDeltaNet.forward`` (same file :500-502)
 * ``select_topk``, ``merge_topk``, ``exclusive_prefix_topk``,
-  ``indexed_gqa_torch`` and ``IndependentGQAMemory._decode`` with the torch
-  backend (modeling_yanchor.py:22-313)
+  ``indexed_gqa_torch``, ``IndependentGQAMemory._write_kv`` / ``_sequence`` /
+  ``_decode`` with the torch backend (modeling_yanchor.py:22-313)
 * ``counter_uniform`` and ``sample_top_k_top_p_counter``
   (runtime/model/inference_kernels.py:24-88)
 
@@ -145,6 +145,32 @@ def memory_fixtures(my, torch):
     pre = my.exclusive_prefix_topk(ps, pp, pr, cap)
     out.update(pre_scores_in=ps, pre_pos_in=pp, pre_refs_in=pr,
                pre_scores=pre[0], pre_pos=pre[1], pre_refs=pre[2])
+    # --- select_topk edge cases: NaN scores (rank first, as torch's descending
+    # sort puts them), invalid references with finite scores, int32 positions
+    es = torch.randint(-2, 3, (5, 17), generator=g).float()
+    es[0, [2, 9]] = float('nan')
+    es[1, :4] = torch.tensor([-0.0, 0.0, float('inf'), float('-inf')])
+    ep = torch.stack([torch.randperm(50, generator=g)[:17] for _ in range(5)]).int()
+    er = torch.arange(17).expand(5, 17).clone()
+    er[torch.rand(5, 17, generator=g) < 0.3] = -1          # invalid, but scores stay finite
+    sel = my.select_topk(es, ep, er, 9)
+    out.update(seledge_scores_in=es, seledge_pos_in=ep, seledge_refs_in=er,
+               seledge_scores=sel[0], seledge_pos=sel[1], seledge_refs=sel[2])
+    # --- exclusive prefix top-k: odd block count, chunk = capacity, ties -------
+    B, blocks, G, chunk, cap = 2, 7, 3, 16, 16
+    ps = (torch.randn(B, blocks, G, chunk, generator=g) * 4).round() / 4
+    pp = torch.arange(blocks * chunk).reshape(1, blocks, 1, chunk).expand(B, blocks, G, chunk).clone() + 5
+    pr = pp.clone()
+    pr[1, -1, :, 9:] = -1
+    ps = ps.masked_fill(pr < 0, -math.inf)
+    pre = my.exclusive_prefix_topk(ps, pp, pr, cap)
+    out.update(pre2_scores_in=ps, pre2_pos_in=pp, pre2_refs_in=pr,
+               pre2_scores=pre[0], pre2_pos=pre[1], pre2_refs=pre[2])
+    # --- prefill orchestration (_sequence): fresh state with a left-padded
+    # mask, a continuation from that state, and the stateless form.  The
+    # writer's k / v are recorded for every token (the writer is row-wise), so
+    # a restatement can gather the rows the reference computes on demand.
+    out.update(sequence_fixtures(my, torch, g))
     # --- indexed_gqa_torch (prefill read) ------------------------------------
     B, blocks, chunk, H, G, D, S, cap = 2, 3, 8, 4, 2, 32, 20, 6
     q = torch.randn(B, blocks, chunk, H, D, generator=g)
@@ -182,6 +208,42 @@ def memory_fixtures(my, torch):
     for f in ('keys', 'values', 'scores', 'positions', 'pending_keys', 'pending_values',
               'pending_scores', 'count', 'total'):
         out[f'dec_final_{f}'] = getattr(state, f).clone()
+    return out
+
+
+def sequence_fixtures(my, torch, g):
+    B, H, G, D, CAP, CHUNK, ROT, HID = 3, 4, 2, 32, 6, 8, 8, 16
+    cfg = SimpleNamespace(backend='torch', hidden_size=HID, num_attention_heads=H, num_key_value_heads=G,
+                          head_dim=D, rms_norm_eps=1e-6, initializer_range=0.2, fixed_memory_swa_window=64,
+                          independent_memory=dict(capacity=CAP, max_commit_chunk=CHUNK, admission_rank=4,
+                                                  writer_intermediate_size=8))
+    mem = my.IndependentGQAMemory(cfg)
+    out = {}
+    state = my.IndependentMemoryState.empty(B, G, CAP, CHUNK, D, 'cpu', torch.float32)
+    fields = ('keys', 'values', 'scores', 'positions', 'pending_keys', 'pending_values', 'pending_scores',
+              'count', 'total')
+    calls = [('seq1', 29, True, True), ('seq2', 13, False, True), ('seq3', 21, False, False)]
+    for name, T, masked, stateful in calls:
+        u = torch.randn(B, T, HID, generator=g)
+        query = torch.randn(B, T, H, D, generator=g)
+        scores = (torch.randn(B, T, G, generator=g) * 2).round() / 2       # ties on purpose
+        theta = torch.randn(B, T, ROT // 2, generator=g)
+        pe = (torch.cat((theta.cos(), theta.cos()), -1), torch.cat((theta.sin(), theta.sin()), -1))
+        valid = None
+        if masked:
+            valid = torch.ones(B, T, dtype=torch.bool)
+            valid[1, :5] = False                                           # left padding
+            valid[2, :T - 3] = False                                       # a short prompt
+        with torch.no_grad():
+            k_all, v_all = mem._write_kv(u.reshape(-1, HID), tuple(x.reshape(-1, ROT) for x in pe))
+            o = mem._sequence(u, query, scores, pe, valid, CHUNK, state if stateful else None)
+        out.update({f'{name}_q': query, f'{name}_scores': scores, f'{name}_o': o,
+                    f'{name}_k': k_all.reshape(B, T, G, D), f'{name}_v': v_all.reshape(B, T, G, D)})
+        if valid is not None:
+            out[f'{name}_valid'] = valid
+        if stateful:
+            for f in fields:
+                out[f'{name}_state_{f}'] = getattr(state, f).clone()
     return out
 
 

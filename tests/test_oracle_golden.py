@@ -10,7 +10,8 @@ def close(a, b, atol, rtol=0.0):
     a = np.asarray(a, dtype=np.float64)
     b = np.asarray(b, dtype=np.float64)
     assert a.shape == b.shape, (a.shape, b.shape)
-    err = np.abs(a - b).max() if a.size else 0.0
+    fin = np.isfinite(a) & np.isfinite(b)
+    err = np.abs(a - b)[fin].max() if fin.any() else 0.0
     assert np.allclose(a, b, atol=atol, rtol=rtol), f'max abs err {err}'
 
 
@@ -100,6 +101,47 @@ def test_exclusive_prefix_topk(golden):
     np.testing.assert_array_equal(s, d['pre_scores'])
     np.testing.assert_array_equal(p, d['pre_pos'])
     np.testing.assert_array_equal(r, d['pre_refs'])
+
+
+def test_select_topk_edges(golden):
+    """NaN scores rank first, invalid references keep finite scores, int32 positions."""
+    d = golden('memory')
+    s, p, r = memory.select_topk(d['seledge_scores_in'], d['seledge_pos_in'], d['seledge_refs_in'], 9)
+    np.testing.assert_array_equal(s, d['seledge_scores'])
+    np.testing.assert_array_equal(p, d['seledge_pos'])
+    np.testing.assert_array_equal(r, d['seledge_refs'])
+
+
+def test_exclusive_prefix_topk_odd_blocks(golden):
+    d = golden('memory')
+    s, p, r = memory.exclusive_prefix_topk(d['pre2_scores_in'], d['pre2_pos_in'], d['pre2_refs_in'], 16)
+    np.testing.assert_array_equal(s, d['pre2_scores'])
+    np.testing.assert_array_equal(p, d['pre2_pos'])
+    np.testing.assert_array_equal(r, d['pre2_refs'])
+
+
+SEQ_FIELDS = ('keys', 'values', 'scores', 'positions', 'pending_keys', 'pending_values', 'pending_scores',
+              'count', 'total')
+
+
+def test_sequence_prefill(golden):
+    """Prefill read + write against the reference's _sequence: a fresh state
+    with a left-padded mask, a continuation, and the stateless form."""
+    d = golden('memory')
+    B, G, D = d['seq1_k'].shape[0], d['seq1_k'].shape[2], d['seq1_k'].shape[3]
+    CAP, CHUNK = d['seq1_state_keys'].shape[2], d['seq1_state_pending_keys'].shape[2]
+    state = memory.empty_state(B, G, CAP, CHUNK, D)
+    for name, stateful in (('seq1', True), ('seq2', True), ('seq3', False)):
+        valid = d.get(f'{name}_valid')
+        o = memory.sequence(d[f'{name}_q'], d[f'{name}_scores'], d[f'{name}_k'], d[f'{name}_v'], valid, CHUNK,
+                            state if stateful else None, capacity=CAP)
+        close(o, d[f'{name}_o'], 2e-5)
+        if stateful:
+            for f in SEQ_FIELDS:
+                if state[f].dtype.kind == 'f':
+                    close(state[f], d[f'{name}_state_{f}'], 2e-5)
+                else:
+                    np.testing.assert_array_equal(state[f], d[f'{name}_state_{f}'], err_msg=f'{name} {f}')
 
 
 def test_indexed_gqa(golden):
