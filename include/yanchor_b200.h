@@ -13,7 +13,7 @@
  *   - Every entry point returns YB_OK (0) or an error code; argument errors
  *     are detected on the host before any launch.  yb_last_error() gives a
  *     message for the calling thread's last failure.
- *   - dtype codes: YB_F32, YB_F16, YB_BF16.
+ *   - dtype codes: YB_F32, YB_F16, YB_BF16 (values), YB_I32, YB_I64 (positions).
  *
  * The reference binds these operations as Python callables; the comment above
  * each entry point names the reference interface it replaces (paths inside
@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-enum yb_dtype { YB_F32 = 0, YB_F16 = 1, YB_BF16 = 2 };
+enum yb_dtype { YB_F32 = 0, YB_F16 = 1, YB_BF16 = 2, YB_I32 = 3, YB_I64 = 4 };
 
 enum yb_status {
   YB_OK = 0,
@@ -158,6 +158,39 @@ int yb_mem_decode_commit(const void *key, const void *value, const float *scores
 int yb_mem_indexed_read(const void *query, const void *key, const void *value, const int64_t *references,
                         void *out, int64_t B, int64_t blocks, int64_t chunk, int64_t H, int64_t G,
                         int64_t D, int64_t S, int64_t KB, int64_t CAP, int dtype, void *stream);
+
+/*
+ * Top-CAP selection of anchor candidates.  Order: score descending (NaN
+ * first, -0.0 equal to 0.0), then position ascending with invalid entries
+ * (reference < 0) last, then candidate index.  Outputs: scores float32,
+ * positions int64 (-1 where the reference is < 0), references int64; rows
+ * with fewer candidates than `capacity` are padded with (-inf, -1, -1).
+ * positions_dtype is YB_I32 or YB_I64.  All arrays contiguous.
+ *
+ * yb_mem_select_topk: per row of `n` candidates (n <= 4096).
+ * Replaces modeling_yanchor.py:51-60 `select_topk` (and `merge_topk`,
+ * :62-63, which is select_topk of the concatenation).
+ *
+ * yb_mem_exclusive_prefix_topk: inputs [B, blocks, G, chunk] (chunk <= 4096);
+ * outputs [B, blocks + 1, G, capacity] (capacity <= 512): entry i is the
+ * top-capacity over blocks 0 .. i-1, entry `blocks` over all of them.  With
+ * initial_scores non-NULL, a bank [B, G, capacity] (scores, positions and
+ * references; initial_references NULL means "slot index where the position
+ * is >= 0, else -1") joins every entry, as the reference's merge of each
+ * prefix with the state's bank.  Equal to the reference when valid
+ * positions are distinct within a (row, group) and invalid references are
+ * -1, which holds for the prefill orchestration.  Replaces
+ * modeling_yanchor.py:65-78 `exclusive_prefix_topk` and :206-208.
+ */
+int yb_mem_select_topk(const float *scores, const void *positions, int positions_dtype, const int64_t *references,
+                       int64_t rows, int64_t n, int64_t capacity, float *out_scores, int64_t *out_positions,
+                       int64_t *out_references, void *stream);
+int yb_mem_exclusive_prefix_topk(const float *scores, const void *positions, int positions_dtype,
+                                 const int64_t *references, int64_t B, int64_t blocks, int64_t G, int64_t chunk,
+                                 int64_t capacity, const float *initial_scores, const void *initial_positions,
+                                 int initial_positions_dtype, const int64_t *initial_references,
+                                 float *out_scores, int64_t *out_positions, int64_t *out_references,
+                                 void *stream);
 
 /*
  * Sampling.  scores [B, vocab] (row stride in elements) in dtype; out [B] int64.

@@ -5,16 +5,19 @@ Operators (all CUDA, via the C ABI library libyanchor_b200.so):
 * gated delta rule: ``chunk_gated_delta_rule`` (prefill),
   ``fused_recurrent_gated_delta_rule`` (decode), ``gdn_gates``
 * anchor memory: ``indexed_gqa`` (prefill read), ``committed_gqa`` (decode
-  read), ``commit_decode`` (decode write)
+  read), ``commit_decode`` (decode write), ``select_topk`` / ``merge_topk`` /
+  ``exclusive_prefix_topk`` (top-CAP selection) and ``sequence`` (the
+  prefill read / write orchestration)
 * sampling: ``greedy``, ``sample_top_k_top_p_counter``,
   ``apply_dense_presence_penalty_``
-* ``bind_gdn_kernels`` / ``install_memory_module`` put them where the
-  reference model code looks them up.
+* ``bind_gdn_kernels`` / ``install_memory_module`` / ``bind_memory_prefill``
+  put them where the reference model code looks them up.
 """
 from .gated_delta_rule import chunk_gated_delta_rule, fused_recurrent_gated_delta_rule, gdn_gates  # noqa: F401
 from .independent_memory import MemoryState, commit_decode, committed_gqa, indexed_gqa  # noqa: F401
+from .memory_prefill import exclusive_prefix_topk, merge_topk, select_topk, sequence  # noqa: F401
 from .sampling import apply_dense_presence_penalty_, greedy, sample_top_k_top_p_counter  # noqa: F401
-from .bind import bind_gdn_kernels, install_memory_module  # noqa: F401
+from .bind import bind_gdn_kernels, bind_memory_prefill, install_memory_module  # noqa: F401
 from ._lib import LIB_PATH, YanchorError, lib  # noqa: F401
 
 __version__ = '0.1.0'

@@ -9,6 +9,10 @@
 * ``install_memory_module()`` makes ``importlib.import_module(
   "model.independent_memory")`` — the lookup of ``_cuda_module``
   (``modeling_yanchor.py:19-20``) — return ``yanchor_b200.independent_memory``.
+* ``bind_memory_prefill(modeling)`` replaces the module-level ``select_topk``
+  / ``merge_topk`` / ``exclusive_prefix_topk`` of the given
+  ``modeling_yanchor`` module and ``IndependentGQAMemory._sequence``
+  (modeling_yanchor.py:51-78, 178-275) with ``yanchor_b200.memory_prefill``.
 """
 from __future__ import annotations
 
@@ -16,7 +20,7 @@ import functools
 import sys
 import types
 
-from . import gated_delta_rule, independent_memory
+from . import gated_delta_rule, independent_memory, memory_prefill
 
 
 def bind_gdn_kernels(model, *, inplace_decode: bool = True) -> dict:
@@ -41,3 +45,18 @@ def install_memory_module() -> types.ModuleType:
     sys.modules['model.independent_memory'] = independent_memory
     pkg.independent_memory = independent_memory
     return independent_memory
+
+
+def bind_memory_prefill(modeling) -> dict:
+    for name in ('select_topk', 'merge_topk', 'exclusive_prefix_topk'):
+        setattr(modeling, name, getattr(memory_prefill, name))
+
+    def _sequence(self, u, query, scores, position_embeddings, valid, chunk, state=None):
+        def write_kv(batch_index, token_index):
+            angles = tuple(x.expand(query.shape[0], -1, -1)[batch_index, token_index] for x in position_embeddings)
+            return self._write_kv(u[batch_index, token_index], angles)
+        return memory_prefill.sequence(query, scores, write_kv, valid, chunk, state, capacity=self.capacity)
+
+    modeling.IndependentGQAMemory._sequence = _sequence
+    return {'backend': 'yanchor_b200', 'memory_prefill': ['select_topk', 'merge_topk', 'exclusive_prefix_topk',
+                                                          'IndependentGQAMemory._sequence']}

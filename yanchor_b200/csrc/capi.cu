@@ -187,6 +187,41 @@ int yb_mem_indexed_read(const void *query, const void *key, const void *value, c
   return launch_mem_indexed_read(a);
 }
 
+static bool pos_dtype_ok(int d) { return d == YB_I32 || d == YB_I64; }
+
+int yb_mem_select_topk(const float *scores, const void *positions, int positions_dtype, const int64_t *references,
+                       int64_t rows, int64_t n, int64_t capacity, float *out_scores, int64_t *out_positions,
+                       int64_t *out_references, void *stream) {
+  YB_REQUIRE(pos_dtype_ok(positions_dtype), "select_topk: positions must be YB_I32 or YB_I64");
+  YB_REQUIRE(rows >= 0 && n >= 0 && capacity >= 0 && rows <= 0x7fffffffLL, "select_topk: bad sizes");
+  YB_REQUIRE(rows * n == 0 || (scores && positions && references), "select_topk: null input");
+  YB_REQUIRE(rows * capacity == 0 || (out_scores && out_positions && out_references), "select_topk: null output");
+  TopkArgs a{scores, positions, references, positions_dtype, rows, n, capacity, out_scores, out_positions,
+             out_references, static_cast<cudaStream_t>(stream)};
+  return launch_select_topk(a);
+}
+
+int yb_mem_exclusive_prefix_topk(const float *scores, const void *positions, int positions_dtype,
+                                 const int64_t *references, int64_t B, int64_t blocks, int64_t G, int64_t chunk,
+                                 int64_t capacity, const float *initial_scores, const void *initial_positions,
+                                 int initial_positions_dtype, const int64_t *initial_references,
+                                 float *out_scores, int64_t *out_positions, int64_t *out_references,
+                                 void *stream) {
+  YB_REQUIRE(pos_dtype_ok(positions_dtype), "exclusive_prefix_topk: positions must be YB_I32 or YB_I64");
+  YB_REQUIRE(B >= 0 && blocks >= 0 && G > 0 && chunk >= 0 && capacity >= 0 && B * G <= 0x7fffffffLL &&
+                 B * blocks * G <= 0x7fffffffLL,
+             "exclusive_prefix_topk: bad sizes");
+  YB_REQUIRE(B * blocks * chunk == 0 || (scores && positions && references), "exclusive_prefix_topk: null input");
+  YB_REQUIRE(B * capacity == 0 || (out_scores && out_positions && out_references),
+             "exclusive_prefix_topk: null output");
+  YB_REQUIRE(!initial_scores || (initial_positions && pos_dtype_ok(initial_positions_dtype)),
+             "exclusive_prefix_topk: initial bank needs positions (YB_I32 or YB_I64)");
+  PrefixTopkArgs a{scores, positions, references, positions_dtype, B, blocks, G, chunk, capacity,
+                   initial_scores, initial_positions, initial_references, initial_positions_dtype,
+                   out_scores, out_positions, out_references, static_cast<cudaStream_t>(stream)};
+  return launch_exclusive_prefix_topk(a);
+}
+
 int64_t yb_sample_workspace_bytes(int64_t B, int64_t vocab, int64_t top_k) {
   return sample_workspace_bytes(B, vocab, top_k);
 }

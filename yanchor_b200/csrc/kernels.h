@@ -82,6 +82,34 @@ bool mem_indexed_tc_supported(const MemIndexedArgs &a);
 int launch_mem_indexed_tc(const MemIndexedArgs &a);
 int read_device_error_idx(int clear);
 
+struct TopkArgs {
+  const float *scores;
+  const void *positions;
+  const int64_t *refs;
+  int pos_dtype;
+  int64_t rows, n, cap;
+  float *out_s;
+  int64_t *out_p, *out_r;
+  cudaStream_t stream;
+};
+int launch_select_topk(const TopkArgs &a);
+
+struct PrefixTopkArgs {
+  const float *scores;
+  const void *positions;
+  const int64_t *refs;
+  int pos_dtype;
+  int64_t B, blocks, G, chunk, cap;
+  const float *init_s;
+  const void *init_p;
+  const int64_t *init_r;
+  int init_pos_dtype;
+  float *out_s;
+  int64_t *out_p, *out_r;
+  cudaStream_t stream;
+};
+int launch_exclusive_prefix_topk(const PrefixTopkArgs &a);
+
 struct SampleArgs {
   const void *scores;
   int64_t row_stride, B, vocab;

@@ -1,0 +1,242 @@
+"""Prefill side of the anchor memory: top-CAP selection and the prefill
+read / write orchestration, with the reference's call signatures.
+
+    select_topk(scores, positions, references, capacity)       modeling_yanchor.py:51-60
+    merge_topk(left, right, capacity)                           modeling_yanchor.py:62-63
+    exclusive_prefix_topk(scores, positions, references, capacity, initial=None)
+                                                                modeling_yanchor.py:65-78
+    sequence(query, scores, write_kv, valid, chunk, state=None, capacity=None)
+                                                                modeling_yanchor.py:178-275
+
+The selections run on libyanchor_b200.so's sort / merge kernels and the read
+on its indexed-read kernel; the orchestration between them is device-side
+torch indexing.  There is no CPU path.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+from ._torch import require_cuda, stream_ptr
+from .independent_memory import indexed_gqa
+
+_I32, _I64 = 3, 4   # yb_dtype codes for positions
+
+
+def _positions(p: torch.Tensor):
+    if p.dtype == torch.int32:
+        return p.contiguous(), _I32
+    return p.to(torch.int64).contiguous(), _I64
+
+
+def select_topk(scores, positions, references, capacity):
+    """Top-``capacity`` along the last axis: score descending (NaN first),
+    then position ascending with invalid references (< 0) last, then index.
+    Returns (scores, positions int64 with -1 where the reference is < 0,
+    references), each ``lead + (capacity,)``; short rows are padded with
+    (-inf, -1, -1)."""
+    require_cuda(scores, positions, references)
+    if not (scores.shape == positions.shape == references.shape):
+        raise ValueError('scores, positions and references must share a shape')
+    capacity = int(capacity)
+    lead, n = scores.shape[:-1], scores.shape[-1]
+    s32 = scores.to(torch.float32).contiguous()
+    pos, pcode = _positions(positions)
+    refs = references.to(torch.int64).contiguous()
+    rows = math.prod(lead)
+    out_s = torch.empty(lead + (capacity,), device=scores.device, dtype=torch.float32)
+    out_p = torch.empty(lead + (capacity,), device=scores.device, dtype=torch.int64)
+    out_r = torch.empty(lead + (capacity,), device=scores.device, dtype=torch.int64)
+    rc = _lib.lib().yb_mem_select_topk(s32.data_ptr(), pos.data_ptr(), pcode, refs.data_ptr(), rows, n, capacity,
+                                       out_s.data_ptr(), out_p.data_ptr(), out_r.data_ptr(),
+                                       stream_ptr(scores.device))
+    _lib.check(rc, 'select_topk')
+    return out_s.to(scores.dtype), out_p, out_r.to(references.dtype)
+
+
+def merge_topk(left, right, capacity):
+    """Top-``capacity`` of two candidate sets (the concatenation along the
+    last axis, ``left`` first)."""
+    return select_topk(*(torch.cat((a, b), -1) for a, b in zip(left, right)), capacity)
+
+
+def exclusive_prefix_topk(scores, positions, references, capacity, initial=None):
+    """Inputs ``[B, blocks, G, chunk]``; returns (scores, positions,
+    references), each ``[B, blocks + 1, G, capacity]``: entry ``i`` is the
+    top-``capacity`` over blocks ``0 .. i-1`` and entry ``blocks`` over all.
+
+    ``initial`` (an extension): a bank ``(scores, positions[, references])``
+    of ``[B, G, capacity]`` that joins every entry, equal to the reference's
+    ``merge_topk(prefix, bank expanded over the entries)`` in ``_sequence``
+    (references default to the slot index where the position is >= 0).
+    Matches the reference whenever valid positions are distinct within a
+    (row, group) and invalid references are -1, as in the prefill
+    orchestration."""
+    require_cuda(scores, positions, references)
+    if scores.dim() != 4 or not (scores.shape == positions.shape == references.shape):
+        raise ValueError('scores, positions and references must be [B, blocks, G, chunk]')
+    B, blocks, G, chunk = scores.shape
+    capacity = int(capacity)
+    s32 = scores.to(torch.float32).contiguous()
+    pos, pcode = _positions(positions)
+    refs = references.to(torch.int64).contiguous()
+    shape = (B, blocks + 1, G, capacity)
+    out_s = torch.empty(shape, device=scores.device, dtype=torch.float32)
+    out_p = torch.empty(shape, device=scores.device, dtype=torch.int64)
+    out_r = torch.empty(shape, device=scores.device, dtype=torch.int64)
+    init_s = init_p = init_r = None
+    icode = _I64
+    if initial is not None:
+        init_s = initial[0].to(torch.float32).contiguous()
+        init_p, icode = _positions(initial[1])
+        if len(initial) > 2 and initial[2] is not None:
+            init_r = initial[2].to(torch.int64).contiguous()
+        for t in (init_s, init_p) + ((init_r,) if init_r is not None else ()):
+            if t.shape != (B, G, capacity):
+                raise ValueError('initial bank must be [B, G, capacity]')
+    ptr = lambda t: 0 if t is None else t.data_ptr()  # noqa: E731
+    rc = _lib.lib().yb_mem_exclusive_prefix_topk(
+        s32.data_ptr(), pos.data_ptr(), pcode, refs.data_ptr(), B, blocks, G, chunk, capacity,
+        ptr(init_s), ptr(init_p), icode, ptr(init_r), out_s.data_ptr(), out_p.data_ptr(), out_r.data_ptr(),
+        stream_ptr(scores.device))
+    _lib.check(rc, 'exclusive_prefix_topk')
+    return out_s.to(scores.dtype), out_p, out_r.to(references.dtype)
+
+
+def sequence(query, scores, write_kv, valid, chunk, state=None, capacity=None):
+    """Prefill anchor read and write (``IndependentGQAMemory._sequence``,
+    modeling_yanchor.py:178-275).
+
+    query ``[B, T, H, D]``; scores ``[B, T, G]`` (admission scores);
+    ``write_kv(batch_index, token_index) -> (key, value)`` gives the writer's
+    ``[N, G, D]`` rows for the listed tokens (called once, only for the tokens
+    that some block reads or that stay pending); ``valid`` ``[B, T]`` bool or
+    None; ``state`` an ``IndependentMemoryState``-like object, updated in
+    place, or None (then ``capacity`` gives CAP and nothing is kept).  Returns
+    the read ``[B, T, H, D]`` (zero on invalid tokens).
+
+    Each row's tokens (valid ones first, in order) are laid on a timeline
+    after the state's ``count`` pending tokens and padded to whole blocks of
+    ``chunk``.  Block ``i`` reads the top-CAP over the state's bank and
+    blocks ``0 .. i-1``; afterwards the bank becomes the top-CAP over all
+    complete blocks and the incomplete tail becomes the pending chunk.
+    """
+    require_cuda(query, scores)
+    B, T, H, D = query.shape
+    G = scores.shape[-1]
+    dev = query.device
+    cap = int(state.keys.shape[2]) if state is not None else int(capacity)
+    if T == 0:
+        return query.new_zeros(query.shape)                   # nothing to read or add
+    i64 = dict(device=dev, dtype=torch.int64)
+    rows = torch.arange(B, **i64)[:, None]
+
+    # ---- timeline: [the state's pending tokens | new tokens, valid first] ----
+    if valid is None:
+        order = None
+        n_new = torch.full((B,), T, **i64)
+    else:
+        valid = valid.to(device=dev, dtype=torch.bool)
+        order = torch.argsort((~valid).to(torch.int8), dim=1, stable=True)   # valid first, stable
+        n_new = valid.sum(1)
+    c0 = torch.zeros(B, **i64) if state is None else state.count.to(torch.int64).clone()
+    t0 = torch.zeros(B, **i64) if state is None else state.total.to(torch.int64).clone()
+    lead = 0 if state is None else chunk
+    extent = -(-(T + lead) // chunk) * chunk
+    blocks = extent // chunk
+    slot = torch.arange(extent, **i64)[None]
+    fill = c0 + n_new
+    live = slot < fill[:, None]
+    is_new = slot >= c0[:, None]
+    j = (slot - c0[:, None]).clamp(0, T - 1)                 # new-token rank of each slot
+    tok = j if order is None else order.gather(1, j)          # its token index
+    s_slot = scores.to(torch.float32)[rows, tok]             # [B, extent, G]
+    shift = 0
+    if state is not None:
+        pend = state.pending_scores[:, :, :chunk].transpose(1, 2).to(torch.float32)
+        s_slot = torch.where(is_new[..., None], s_slot, pend[rows, slot.clamp(max=chunk - 1)])
+        shift = cap
+    s_slot = s_slot.masked_fill(~live[..., None], float('-inf'))
+    pos_slot = (t0 - c0)[:, None] + slot
+    ref_slot = torch.where(live, slot + shift, -1)
+
+    def blocked(x):
+        if x.dim() == 2:
+            x = x[..., None].expand(B, extent, G)
+        return x.reshape(B, blocks, chunk, G).transpose(2, 3)
+
+    initial = None if state is None else (state.scores, state.positions)
+    pre_s, pre_p, pre_r = exclusive_prefix_topk(blocked(s_slot), blocked(pos_slot), blocked(ref_slot), cap,
+                                                initial=initial)
+
+    # ---- which new tokens get a key / value row ----
+    bound = (torch.arange(1, blocks + 1, **i64) * chunk)[None, :, None, None]
+    ent = pre_r[:, 1:] - shift                                # entrant slot of each block-end top-CAP
+    used = bound <= fill[:, None, None, None] if state is not None else bound < fill[:, None, None, None]
+    own = (ent >= bound - chunk) & (ent < bound) & used
+    needed = torch.zeros(B, extent + 1, device=dev, dtype=torch.bool)
+    needed.scatter_(1, torch.where(own, ent, extent).flatten(1), True)
+    needed = needed[:, :extent]
+    if state is not None:
+        full = fill // chunk
+        needed |= live & (slot >= (full * chunk)[:, None])    # the tail that stays pending
+    needed &= live & is_new
+    sel_b, sel_slot = needed.nonzero(as_tuple=True)
+    k_new, v_new = write_kv(sel_b, tok[sel_b, sel_slot])
+    k_new = k_new.to(query.dtype).reshape(-1, G, D)
+    v_new = v_new.to(query.dtype).reshape(-1, G, D)
+
+    # ---- source rows [old bank + pending rows | new rows | zero row] and the slot -> row table ----
+    table = torch.full((B, shift + extent), -1, **i64)
+    zero = query.new_zeros(1, G, D)
+    if state is not None:
+        per = cap + chunk
+        old_k = torch.cat((state.keys, state.pending_keys[:, :, :chunk]), 2).transpose(1, 2)
+        old_v = torch.cat((state.values, state.pending_values[:, :, :chunk]), 2).transpose(1, 2)
+        src_k = torch.cat((old_k.reshape(-1, G, D).to(query.dtype), k_new, zero), 0)
+        src_v = torch.cat((old_v.reshape(-1, G, D).to(query.dtype), v_new, zero), 0)
+        base = rows * per
+        table[:, :shift] = base + torch.arange(shift, **i64)[None]
+        table[:, shift:] = torch.where(~is_new, base + cap + slot, -1)
+        offset = B * per
+    else:
+        src_k = torch.cat((k_new, zero), 0)
+        src_v = torch.cat((v_new, zero), 0)
+        offset = 0
+    table[sel_b, shift + sel_slot] = offset + torch.arange(sel_b.numel(), **i64)
+
+    # ---- read: block i attends to prefix entry i ----
+    reads = pre_r[:, :-1]
+    read_refs = torch.where(reads < 0, -1, table[rows[:, :, None, None], reads.clamp(min=0)])
+    q_slot = query[rows, tok]                                  # [B, extent, H, D]
+    read = indexed_gqa(q_slot.reshape(B, blocks, chunk, H, D), src_k[None].contiguous(), src_v[None].contiguous(),
+                       read_refs).reshape(B, extent, H, D)
+    if order is None:
+        out = read[rows, (c0[:, None] + torch.arange(T, **i64)[None]).clamp(max=extent - 1)]
+    else:
+        rank = torch.argsort(order, dim=1)                    # token -> its rank among the reordered tokens
+        out = read[rows, (c0[:, None] + rank).clamp(max=extent - 1)] * valid[..., None, None]
+
+    # ---- new state: bank = top-CAP over all complete blocks, tail = pending ----
+    if state is not None:
+        bank_s, bank_p, bank_r = (x[torch.arange(B, device=dev), full] for x in (pre_s, pre_p, pre_r))
+        gi = torch.arange(G, **i64)[None, :, None]
+        src_row = table[rows[:, :, None], bank_r.clamp(min=0)].clamp(min=0)
+        hole = (bank_r < 0)[..., None]
+        state.keys.copy_(src_k[src_row, gi].masked_fill(hole, 0))
+        state.values.copy_(src_v[src_row, gi].masked_fill(hole, 0))
+        state.scores.copy_(bank_s)
+        state.positions.copy_(bank_p)
+        pc = state.pending_keys.shape[2]
+        tail = (full[:, None] * chunk + torch.arange(pc, **i64)[None]).clamp(max=extent - 1)
+        remaining = fill % chunk
+        keep = torch.arange(pc, **i64)[None] < remaining[:, None]
+        tail_row = table[rows, tail + shift].clamp(min=0)
+        state.pending_keys.copy_(src_k[tail_row].masked_fill(~keep[..., None, None], 0).transpose(1, 2))
+        state.pending_values.copy_(src_v[tail_row].masked_fill(~keep[..., None, None], 0).transpose(1, 2))
+        state.pending_scores.copy_(s_slot[rows, tail].masked_fill(~keep[..., None], float('-inf')).transpose(1, 2))
+        state.count.copy_(remaining)
+        state.total.copy_(t0 + n_new)
+    return out
