@@ -346,11 +346,38 @@ def run_prefill(torch, yb, device, hbm, tf_burst, peak_kind):
     for _ in range(2):
         yb.indexed_gqa(mq, mk, mv, refs)
     mem_ms = time_events(torch, lambda: yb.indexed_gqa(mq, mk, mv, refs), 3, stream)
+    # prefix top-64 over the 128 blocks of each (row, group)
+    psc = (torch.randn(B, blocks, MEM_G, 64, generator=gen, device=device) * 2).round() / 2
+    ppos = torch.arange(T, device=device).reshape(1, blocks, 1, 64).expand(B, blocks, MEM_G, 64).contiguous()
+    for _ in range(2):
+        yb.exclusive_prefix_topk(psc, ppos, ppos, 64)
+    topk_ms = time_events(torch, lambda: yb.exclusive_prefix_topk(psc, ppos, ppos, 64), 3, stream)
+    # the whole prefill write + read of one memory layer on a fresh state; the
+    # writer's rows come from per-token keys / values made beforehand (the
+    # writer's projections are model GEMMs, outside this path)
+    msc = (torch.randn(B, T, MEM_G, generator=gen, device=device) * 2).round() / 2
+    mq2 = mq.reshape(B, T, MEM_H, MEM_D)
+    wk = torch.randn(B, T, MEM_G, MEM_D, generator=gen, device=device).to(bf)
+    wv = torch.randn(B, T, MEM_G, MEM_D, generator=gen, device=device).to(bf)
+
+    def writer(b, t):            # stands in for the writer: N (token, group) rows
+        rows = b * T + t
+        return (wk.view(B * T, -1).index_select(0, rows).view(-1, MEM_G, MEM_D),
+                wv.view(B * T, -1).index_select(0, rows).view(-1, MEM_G, MEM_D))
+
+    def seq():
+        st = yb.MemoryState.empty(B, MEM_G, 64, MEM_CHUNK, MEM_D, device, bf)
+        yb.sequence(mq2, msc, writer, None, MEM_CHUNK, st)
+    for _ in range(2):
+        seq()
+    seq_ms = time_events(torch, seq, 3, stream)
     achieved = flops / (ms / 1e3) / 1e12
     return {'workload': 'config 1: chunked prefill B=8 T=8192 H=HV=32 K=V=128 bf16, fp32 state; '
-                        'plus anchor read (indexed_gqa) over 64 slots, G=4 H=16 D=256',
+                        'plus the anchor prefill of one memory layer (64 slots, G=4 H=16 D=256, chunk 64)',
             'tok_s': round(B * T / (ms / 1e3), 1), 'gdn_ms': round(ms, 3), 'anchor_read_ms': round(mem_ms, 3),
+            'anchor_prefix_topk_ms': round(topk_ms, 3), 'anchor_sequence_ms': round(seq_ms, 3),
             'tok_s_with_anchor_read': round(B * T / ((ms + mem_ms) / 1e3), 1),
+            'tok_s_with_anchor_prefill': round(B * T / ((ms + seq_ms) / 1e3), 1),
             'roofline': {'bound': 'tensor', 'kernel': 'gdn chunk', 'achieved': round(achieved, 2), 'peak': tf_burst,
                          'unit': 'TFLOP/s', 'frac': round(achieved / tf_burst, 4), 'peak_kind': peak_kind,
                          'flops_per_launch': flops}}
@@ -380,6 +407,22 @@ def run_only(args):
         mk = torch.randn(1, 4096, MEM_G, MEM_D, generator=gen, device=dev).to(bf)
         refs = torch.randint(0, 4096, (8, blocks, MEM_G, 64), generator=gen, device=dev)
         fn = lambda: yb.indexed_gqa(mq, mk, mk, refs)  # noqa: E731
+    elif args.only in ('mem_topk', 'mem_sequence'):
+        blocks, T = 128, 8192
+        psc = (torch.randn(8, blocks, MEM_G, 64, generator=gen, device=dev) * 2).round() / 2
+        ppos = torch.arange(T, device=dev).reshape(1, blocks, 1, 64).expand(8, blocks, MEM_G, 64).contiguous()
+        msc = (torch.randn(8, T, MEM_G, generator=gen, device=dev) * 2).round() / 2
+        mq = torch.randn(8, T, MEM_H, MEM_D, generator=gen, device=dev).to(bf)
+        wk = torch.randn(8, T, MEM_G, MEM_D, generator=gen, device=dev).to(bf)
+
+        def writer(b, t):
+            rows = wk.view(8 * T, -1).index_select(0, b * T + t).view(-1, MEM_G, MEM_D)
+            return rows, rows
+
+        def seq():
+            st = yb.MemoryState.empty(8, MEM_G, MEM_CAP, MEM_CHUNK, MEM_D, dev, bf)
+            yb.sequence(mq, msc, writer, None, MEM_CHUNK, st)
+        fn = (lambda: yb.exclusive_prefix_topk(psc, ppos, ppos, 64)) if args.only == 'mem_topk' else seq
     else:
         fns = {
             'gdn_decode': lambda: yb.fused_recurrent_gated_delta_rule(
@@ -442,7 +485,8 @@ def main():
     ap.add_argument('--impl', default='yanchor_b200', choices=['yanchor_b200', 'reference'])
     ap.add_argument('--no-prefill', action='store_true')
     ap.add_argument('--no-cpu', action='store_true')
-    ap.add_argument('--only', choices=['gdn_decode', 'gdn_chunk', 'mem_read', 'mem_commit', 'mem_indexed', 'greedy',
+    ap.add_argument('--only', choices=['gdn_decode', 'gdn_chunk', 'mem_read', 'mem_commit', 'mem_indexed', 'mem_topk',
+                                       'mem_sequence', 'greedy',
                                        'topk'], help='run one kernel family (small ncu captures)')
     ap.add_argument('--prefill-batch', type=int, default=8)
     args = ap.parse_args()

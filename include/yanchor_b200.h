@@ -158,6 +158,21 @@ int yb_mem_decode_commit(const void *key, const void *value, const float *scores
 int yb_mem_indexed_read(const void *query, const void *key, const void *value, const int64_t *references,
                         void *out, int64_t B, int64_t blocks, int64_t chunk, int64_t H, int64_t G,
                         int64_t D, int64_t S, int64_t KB, int64_t CAP, int dtype, void *stream);
+/*
+ * yb_mem_indexed_read_timeline: the same read for the prefill orchestration,
+ * addressing the prompt's own tensors: query / out [B, T, H, D]; block slot
+ * s (0 <= s < blocks * chunk) of row b is token s + token_shift[b]; only
+ * slots in [write_lo[b], write_hi[b]) whose token lies in [0, T) are
+ * computed and written — every other output row is left untouched.
+ * token_shift / write_lo / write_hi: device int64 [B].  Replaces the
+ * reference's gather of the query onto the timeline and of the read back
+ * (modeling_yanchor.py:196-198, 260-265) around `indexed_gqa`.
+ */
+int yb_mem_indexed_read_timeline(const void *query, const void *key, const void *value, const int64_t *references,
+                                 void *out, int64_t B, int64_t T, int64_t blocks, int64_t chunk, int64_t H,
+                                 int64_t G, int64_t D, int64_t S, int64_t KB, int64_t CAP,
+                                 const int64_t *token_shift, const int64_t *write_lo, const int64_t *write_hi,
+                                 int dtype, void *stream);
 
 /*
  * Top-CAP selection of anchor candidates.  Order: score descending (NaN

@@ -137,28 +137,34 @@ def test_sequence_golden(yb, golden):
 
 
 def test_sequence_bf16_yanchor_shape(yb):
-    """YANchor memory shape (H=16, G=4, D=256, CAP=64, chunk 64), bf16: a
-    masked first prefill, a continuation, against the oracle."""
+    """YANchor memory shape (H=16, G=4, D=256, CAP=64, chunk 64), bf16,
+    against the oracle: a left-padded first prefill, a left-padded
+    continuation (pending tokens and padding in the same block), unmasked
+    continuations, and a mask with holes (the gather path)."""
     rng = np.random.default_rng(77)
     B, H, G, D, CAP, CH = 3, 16, 4, 256, 64, 64
     bf = torch.bfloat16
     state = _state(yb, B, G, CAP, CH, D, bf)
     st = omem.empty_state(B, G, CAP, CH, D)
-    calls = [(300, True), (150, False), (64, False)]
-    for T, masked in calls:
+    calls = [(300, 'left'), (150, 'left'), (64, None), (77, 'holes'), (129, None)]
+    for T, mask in calls:
         q = cuda(rng.standard_normal((B, T, H, D)).astype(np.float32), bf)
         sc = cuda((rng.standard_normal((B, T, G)) * 2).round().astype(np.float32) / 2)
         K = cuda(rng.standard_normal((B, T, G, D)).astype(np.float32), bf)
         V = cuda(rng.standard_normal((B, T, G, D)).astype(np.float32), bf)
         valid = None
-        if masked:
+        if mask == 'left':
             vm = np.ones((B, T), bool)
             vm[1, :37] = False
             vm[2, :T - 70] = False
             valid = cuda(vm)
+        elif mask == 'holes':
+            vm = rng.random((B, T)) > 0.3
+            vm[0] = False                                   # a row with nothing new
+            valid = cuda(vm)
         o = yb.sequence(q, sc, lambda b, t: (K[b, t], V[b, t]), valid, CH, state)
         want = omem.sequence(host(q), host(sc), host(K), host(V), None if valid is None else host(valid), CH, st)
-        assert np.abs(host(o) - want).max() <= 2e-2
+        assert np.abs(host(o) - want).max() <= 2e-2, f'T={T} {mask}'
         for f in FIELDS:
             np.testing.assert_array_equal(host(getattr(state, f)), st[f].astype(host(getattr(state, f)).dtype),
-                                          err_msg=f'T={T} {f}')
+                                          err_msg=f'T={T} {mask} {f}')

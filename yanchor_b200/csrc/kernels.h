@@ -76,6 +76,10 @@ struct MemIndexedArgs {
   int64_t B, blocks, chunk, H, G, D, S, KB, CAP;
   int dtype;
   cudaStream_t stream;
+  // timeline mode: query / out are [B, T, H, D]; slot s of row b is token
+  // s + tok_shift[b]; only slots in [w_lo[b], w_hi[b]) are written
+  const int64_t *tok_shift = nullptr, *w_lo = nullptr, *w_hi = nullptr;
+  int64_t T = 0;
 };
 int launch_mem_indexed_read(const MemIndexedArgs &a);
 bool mem_indexed_tc_supported(const MemIndexedArgs &a);

@@ -15,6 +15,14 @@
 // (modeling_yanchor.py:22-42 indexed_gqa_torch; runtime/model/
 // independent_memory.py:6-45 indexed_gqa, which also splits p into bf16
 // hi + lo.)
+//
+// Timeline mode (the prefill orchestration): query and output are the
+// prompt's own [B, T, H, D] tensors and block slot s of row b is token
+// s + token_shift[b]; a 4-D tensor map loads the block's rows straight from
+// there (tokens outside [0, T) read as zeros) and only slots in
+// [write_lo[b], write_hi[b]) are written — whole 32-position halves by TMA
+// store, ragged halves by each thread's own predicated stores.  This
+// replaces two gathers of the whole query / output through a timeline copy.
 #include "common.cuh"
 #include "kernels.h"
 #include "tc.cuh"
@@ -42,6 +50,10 @@ struct IdxParams {
   const int64_t *refs;
   int64_t blocks, chunk, H, G, S, KB;
   float scale;
+  // timeline mode (tok_shift != nullptr)
+  const int64_t *tok_shift, *w_lo, *w_hi;
+  int64_t T;
+  __nv_bfloat16 *out;
 };
 
 __device__ __forceinline__ void cp_async16(void *dst, const void *src, bool valid) {
@@ -53,6 +65,31 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, const void 
   asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];"
                ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
                : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y, int z,
+                                            int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+      "[%2];" ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y),
+      "r"(z), "r"(w)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap *map, const void *src, int x, int y, int z, int w) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];"
+               ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z), "r"(w)
+               : "memory");
+}
+// 64 floats -> 64 bf16 (128 contiguous bytes) in global memory
+__device__ __forceinline__ void st_global_row64_bf16(__nv_bfloat16 *dst, const float *v) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    uint4 w;
+    w.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+    w.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+    w.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+    w.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+    reinterpret_cast<uint4 *>(dst)[j] = w;
+  }
 }
 
 __global__ void __launch_bounds__(NT, 1)
@@ -74,6 +111,10 @@ __global__ void __launch_bounds__(NT, 1)
   const int R = int(p.H / p.G);
   const int tok0 = int((b * p.blocks + blk) * p.chunk);
   const int64_t *refs = p.refs + unit * CAPS;
+  const bool timeline = p.tok_shift != nullptr;
+  const int64_t shift = timeline ? p.tok_shift[b] : 0;
+  const int64_t w_lo = timeline ? p.w_lo[b] : 0, w_hi = timeline ? p.w_hi[b] : 0;
+  const int ttok0 = int(blk * CAPS + shift);        // timeline: token of the block's first slot
 
   if (tid == 0) {
     *abort_flag = (smem_u32(smem) & 1023u) ? 1 : 0;
@@ -93,7 +134,12 @@ __global__ void __launch_bounds__(NT, 1)
     prefetch_tensormap(&map_q);
     mbar_arrive_expect_tx(qbar, 4 * 32768);
 #pragma unroll
-    for (int cb = 0; cb < 4; ++cb) tma_load_3d(smem + OFF_QO + cb * 32768, &map_q, qbar, cb * 64, g * R, tok0);
+    for (int cb = 0; cb < 4; ++cb) {
+      if (timeline)
+        tma_load_4d(smem + OFF_QO + cb * 32768, &map_q, qbar, cb * 64, g * R, ttok0, int(b));
+      else
+        tma_load_3d(smem + OFF_QO + cb * 32768, &map_q, qbar, cb * 64, g * R, tok0);
+    }
   }
   // gather the referenced key / value rows (16-byte pieces, swizzled rows)
   for (int e = tid; e < CAPS * 32; e += NT) {
@@ -179,6 +225,15 @@ __global__ void __launch_bounds__(NT, 1)
     wait_mma(ERR_WAIT_O);
     if (!ok) break;
     // ---- O / den -> bf16 staging (rows of half h, 4 column blocks) -> TMA store ----
+    // (timeline halves that are not wholly inside the write range: each
+    // thread stores its own row if its slot is in range)
+    // (a TMA store never starts at a negative or out-of-range token)
+    const int64_t s0 = blk * CAPS + h * 32;
+    const bool direct = timeline && (s0 < w_lo || s0 + 32 > w_hi || s0 + shift < 0 || s0 + shift + 32 > p.T);
+    const int64_t my_slot = s0 + (tid >> 2);
+    const bool mine = direct && my_slot >= w_lo && my_slot < w_hi && my_slot + shift >= 0 && my_slot + shift < p.T;
+    __nv_bfloat16 *my_out =
+        mine ? p.out + (((b * p.T + my_slot + shift) * p.H) + g * R + (tid & 3)) * D : nullptr;
 #pragma unroll
     for (int cb = 0; cb < 4; ++cb) {
       float o[64];
@@ -187,15 +242,23 @@ __global__ void __launch_bounds__(NT, 1)
       tmem_wait_ld();
 #pragma unroll
       for (int t = 0; t < 64; ++t) o[t] *= inv_den;
-      st_row64_bf16(smem + OFF_QO + cb * 32768 + h * 16384, 128, 0, tid, o);
+      if (direct) {
+        if (mine) st_global_row64_bf16(my_out + cb * 64, o);
+      } else {
+        st_row64_bf16(smem + OFF_QO + cb * 32768 + h * 16384, 128, 0, tid, o);
+      }
     }
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
-    if (tid == 0) {
+    if (tid == 0 && !direct) {
 #pragma unroll
-      for (int cb = 0; cb < 4; ++cb)
-        tma_store_3d(&map_o, smem + OFF_QO + cb * 32768 + h * 16384, cb * 64, g * R, tok0 + h * 32);
+      for (int cb = 0; cb < 4; ++cb) {
+        if (timeline)
+          tma_store_4d(&map_o, smem + OFF_QO + cb * 32768 + h * 16384, cb * 64, g * R, ttok0 + h * 32, int(b));
+        else
+          tma_store_3d(&map_o, smem + OFF_QO + cb * 32768 + h * 16384, cb * 64, g * R, tok0 + h * 32);
+      }
       asm volatile("cp.async.bulk.commit_group;" ::: "memory");
     }
   }
@@ -237,6 +300,21 @@ int make_map(CUtensorMap *map, const void *base, int64_t ntok, int64_t H, int R,
   return YB_OK;
 }
 
+// [B, T, H, 256] bf16 with boxes of `pos` positions x R heads x 64 features of one row
+int make_map_4d(CUtensorMap *map, const void *base, int64_t B, int64_t T, int64_t H, int R, int pos) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return set_error(YB_ERR_CUDA, "indexed read tc: cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[4] = {cuuint64_t(D), cuuint64_t(H), cuuint64_t(T), cuuint64_t(B)};
+  const cuuint64_t strides[3] = {cuuint64_t(D) * 2, cuuint64_t(H) * D * 2, cuuint64_t(T) * H * D * 2};
+  const cuuint32_t box[4] = {64, cuuint32_t(R), cuuint32_t(pos), 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(YB_ERR_CUDA, "indexed read tc: tensor map encode failed (%d)", int(r));
+  return YB_OK;
+}
+
 }  // namespace
 
 bool mem_indexed_tc_supported(const MemIndexedArgs &a) {
@@ -251,8 +329,14 @@ int launch_mem_indexed_tc(const MemIndexedArgs &a) {
   const int64_t ntok = a.B * a.blocks * a.chunk;
   const int R = int(a.H / a.G);
   CUtensorMap mq, mo;
-  int rc = make_map(&mq, a.query, ntok, a.H, R, 64);
-  if (!rc) rc = make_map(&mo, a.out, ntok, a.H, R, 32);
+  int rc;
+  if (a.tok_shift) {
+    rc = make_map_4d(&mq, a.query, a.B, a.T, a.H, R, 64);
+    if (!rc) rc = make_map_4d(&mo, a.out, a.B, a.T, a.H, R, 32);
+  } else {
+    rc = make_map(&mq, a.query, ntok, a.H, R, 64);
+    if (!rc) rc = make_map(&mo, a.out, ntok, a.H, R, 32);
+  }
   if (rc) return rc;
   IdxParams p;
   p.key = static_cast<const __nv_bfloat16 *>(a.key);
@@ -260,6 +344,8 @@ int launch_mem_indexed_tc(const MemIndexedArgs &a) {
   p.refs = a.refs;
   p.blocks = a.blocks; p.chunk = a.chunk; p.H = a.H; p.G = a.G; p.S = a.S; p.KB = a.KB;
   p.scale = 1.0f / sqrtf(float(D));
+  p.tok_shift = a.tok_shift; p.w_lo = a.w_lo; p.w_hi = a.w_hi; p.T = a.T;
+  p.out = static_cast<__nv_bfloat16 *>(a.out);
   cudaError_t e = cudaFuncSetAttribute(mem_indexed_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        int(SMEM_BYTES));
   if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "indexed read tc: smem attribute: %s", cudaGetErrorString(e));

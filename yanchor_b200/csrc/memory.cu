@@ -305,7 +305,12 @@ __global__ void __launch_bounds__(kIdxThreads) mem_indexed_read_kernel(const Mem
   T *obase = static_cast<T *>(a.out);
   float *myq = sq + warp * R * D;
   for (int c = warp; c < a.chunk; c += NW) {
-    const int64_t qrow = ((b * a.blocks + blk) * a.chunk + c) * a.H + int64_t(g) * R;  // first head row
+    int64_t qrow = ((b * a.blocks + blk) * a.chunk + c) * a.H + int64_t(g) * R;  // first head row
+    if (a.tok_shift) {           // timeline mode: slot -> token; only the write range is computed
+      const int64_t s = blk * a.chunk + c, tok = s + a.tok_shift[b];
+      if (s < a.w_lo[b] || s >= a.w_hi[b] || tok < 0 || tok >= a.T) continue;
+      qrow = (b * a.T + tok) * a.H + int64_t(g) * R;
+    }
     for (int e = lane; e < R * D; e += 32) myq[e] = to_f(qbase[qrow * D + e]);
     __syncwarp();
     // logits: lane owns slots lane, lane + 32, ...

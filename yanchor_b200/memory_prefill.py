@@ -9,8 +9,9 @@ read / write orchestration, with the reference's call signatures.
                                                                 modeling_yanchor.py:178-275
 
 The selections run on libyanchor_b200.so's sort / merge kernels and the read
-on its indexed-read kernel; the orchestration between them is device-side
-torch indexing.  There is no CPU path.
+on its indexed-read kernel, which addresses the prompt's own query and output
+through the timeline; the orchestration between them is device-side torch
+indexing.  There is no CPU path.
 """
 from __future__ import annotations
 
@@ -19,7 +20,7 @@ import math
 import torch
 
 from . import _lib
-from ._torch import require_cuda, stream_ptr
+from ._torch import dtype_code, require_cuda, stream_ptr
 from .independent_memory import indexed_gqa
 
 _I32, _I64 = 3, 4   # yb_dtype codes for positions
@@ -105,6 +106,24 @@ def exclusive_prefix_topk(scores, positions, references, capacity, initial=None)
     return out_s.to(scores.dtype), out_p, out_r.to(references.dtype)
 
 
+def _read_timeline(query, src_k, src_v, refs, shift, lo, hi, blocks, chunk, zero_fill):
+    """indexed read of the prompt's ``[B, T, H, D]`` query through the
+    timeline (slot s of row b = token s + shift[b]), writing slots [lo, hi)."""
+    query = query.contiguous()
+    B, T, H, D = query.shape
+    G, CAP = refs.shape[-2:]
+    out = torch.zeros_like(query) if zero_fill else torch.empty_like(query)
+    key, value = src_k[None].contiguous(), src_v[None].contiguous()
+    refs = refs.contiguous()
+    shift, lo, hi = (x.to(torch.int64).contiguous() for x in (shift, lo, hi))
+    rc = _lib.lib().yb_mem_indexed_read_timeline(
+        query.data_ptr(), key.data_ptr(), value.data_ptr(), refs.data_ptr(), out.data_ptr(), B, T, blocks, chunk, H,
+        G, D, key.shape[1], 1, CAP, shift.data_ptr(), lo.data_ptr(), hi.data_ptr(), dtype_code(query),
+        stream_ptr(query.device))
+    _lib.check(rc, 'indexed_gqa (timeline)')
+    return out
+
+
 def sequence(query, scores, write_kv, valid, chunk, state=None, capacity=None):
     """Prefill anchor read and write (``IndependentGQAMemory._sequence``,
     modeling_yanchor.py:178-275).
@@ -152,7 +171,7 @@ def sequence(query, scores, write_kv, valid, chunk, state=None, capacity=None):
     is_new = slot >= c0[:, None]
     j = (slot - c0[:, None]).clamp(0, T - 1)                 # new-token rank of each slot
     tok = j if order is None else order.gather(1, j)          # its token index
-    s_slot = scores.to(torch.float32)[rows, tok]             # [B, extent, G]
+    s_slot = scores.to(torch.float32).reshape(B * T, G).index_select(0, (rows * T + tok).flatten()).view(B, extent, G)
     shift = 0
     if state is not None:
         pend = state.pending_scores[:, :, :chunk].transpose(1, 2).to(torch.float32)
@@ -210,14 +229,24 @@ def sequence(query, scores, write_kv, valid, chunk, state=None, capacity=None):
     # ---- read: block i attends to prefix entry i ----
     reads = pre_r[:, :-1]
     read_refs = torch.where(reads < 0, -1, table[rows[:, :, None, None], reads.clamp(min=0)])
-    q_slot = query[rows, tok]                                  # [B, extent, H, D]
-    read = indexed_gqa(q_slot.reshape(B, blocks, chunk, H, D), src_k[None].contiguous(), src_v[None].contiguous(),
-                       read_refs).reshape(B, extent, H, D)
-    if order is None:
-        out = read[rows, (c0[:, None] + torch.arange(T, **i64)[None]).clamp(max=extent - 1)]
+    run = True                                                # each row's valid tokens are one run
+    if order is not None:
+        v8 = valid.to(torch.int8)
+        run = bool((((v8[:, 1:] > v8[:, :-1]).sum(1) + v8[:, 0]) <= 1).all())
+    if run:
+        # the read kernel addresses the prompt's own rows: slot s of row b is
+        # token s - count + first valid token; only new, live slots are written
+        first = torch.zeros(B, **i64) if order is None else valid.to(torch.int8).argmax(1)
+        out = _read_timeline(query, src_k, src_v, read_refs, first - c0, c0, fill, blocks, chunk, zero_fill=order
+                             is not None)
     else:
+        # whole (token, all heads) rows move with index_select on flattened views
+        q_slot = query.reshape(B * T, H * D).index_select(0, (rows * T + tok).flatten())
+        read = indexed_gqa(q_slot.view(B, blocks, chunk, H, D), src_k[None], src_v[None], read_refs)
         rank = torch.argsort(order, dim=1)                    # token -> its rank among the reordered tokens
-        out = read[rows, (c0[:, None] + rank).clamp(max=extent - 1)] * valid[..., None, None]
+        at = (c0[:, None] + rank).clamp(max=extent - 1)
+        out = read.view(B * extent, H * D).index_select(0, (rows * extent + at).flatten()).view(B, T, H, D)
+        out.masked_fill_(~valid[..., None, None], 0)
 
     # ---- new state: bank = top-CAP over all complete blocks, tail = pending ----
     if state is not None:
