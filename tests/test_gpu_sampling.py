@@ -24,20 +24,49 @@ def cuda(x, dtype=None):
 
 def test_sampler_matches_reference_fixtures(yb, golden):
     d = golden('sampling')
-    for i in range(6):
+    for i in range(6):                  # case 5 is the whole-vocabulary path (top_k 0, top_p 1)
         temp, tk, tp = (float(x) for x in d[f'samp_case{i}'])
-        if int(tk) <= 0:
-            continue   # whole-vocabulary sampling is not built (NotImplementedError, below)
         out = yb.sample_top_k_top_p_counter(cuda(d['samp_scores']), cuda(d['samp_attempt']), cuda(d['samp_steps']),
                                             seed=77, temperature=temp, top_k=int(tk), top_p=tp)
         np.testing.assert_array_equal(out.cpu().numpy(), d[f'samp_out{i}'], err_msg=f'case {i}')
 
 
-def test_whole_vocabulary_sampling_is_refused(yb):
+def test_whole_vocabulary_with_top_p_is_refused(yb):
+    """top_k <= 0 with top_p < 1 needs a whole-vocabulary sort: not built."""
     s = torch.randn(2, 100, device='cuda')
     with pytest.raises(NotImplementedError):
         yb.sample_top_k_top_p_counter(s, torch.arange(2, device='cuda'), 0, seed=1, temperature=1.0, top_k=0,
-                                      top_p=1.0)
+                                      top_p=0.9)
+
+
+@pytest.mark.parametrize('dtype,temp', [(torch.float32, 1.0), (torch.bfloat16, 0.7), (torch.float32, 1.6)])
+def test_whole_vocabulary_sampling_vs_exact_cdf(yb, dtype, temp):
+    """top_k 0, top_p 1 over the YANchor vocabulary (with a masked -inf tail)
+    against the exact (float64) CDF of the same fp32 probabilities: ids must
+    match except where the threshold lies within 2e-6 of a CDF step.  (At
+    this size a float32 cumsum, the reference's, drifts by ~1e-5 from the
+    exact CDF in a summation-order-dependent way, so the exact CDF is the
+    pin; the 1000-token reference fixture above matches id for id.)"""
+    rng = np.random.default_rng(int(temp * 10))
+    B, V = 64, 248_320
+    scores = (rng.standard_normal((B, V)) * 3).astype(np.float32)
+    scores[:, -320:] = -np.inf
+    st = cuda(scores, dtype)
+    scores = st.float().cpu().numpy()
+    attempt = rng.integers(0, 2**40, B).astype(np.int64)
+    steps = rng.integers(0, 5000, B).astype(np.int64)
+    out = yb.sample_top_k_top_p_counter(st, cuda(attempt), cuda(steps), seed=11, temperature=temp, top_k=0,
+                                        top_p=1.0).cpu().numpy()[:, 0]
+    z = (scores / np.float32(temp)).astype(np.float64)
+    p = np.exp(z - z.max(-1, keepdims=True))
+    cum = np.cumsum(p, -1) / p.sum(-1, keepdims=True)
+    thr = osamp.counter_uniform(attempt, steps, 11).astype(np.float64)
+    exact = np.array([np.searchsorted(cum[r], thr[r], side='left') for r in range(B)])
+    near = np.array([min(abs(cum[r, exact[r]] - thr[r]), abs(cum[r, max(exact[r] - 1, 0)] - thr[r])) < 2e-6
+                     for r in range(B)])
+    bad = (out != exact) & ~near
+    assert not bad.any(), (np.nonzero(bad)[0], out[bad], exact[bad])
+    assert (out != exact).sum() <= 2
 
 
 @pytest.mark.parametrize('dtype', [torch.float32, torch.bfloat16])

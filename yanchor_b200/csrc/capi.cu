@@ -294,8 +294,14 @@ int yb_sample_top_k_top_p_counter(const void *scores, int64_t row_stride, int64_
       return set_error(YB_ERR_WORKSPACE, "sample: workspace of %lld bytes required", (long long)need);
     return launch_sample_greedy(a);
   }
-  if (top_k <= 0)
-    return set_error(YB_ERR_UNSUPPORTED, "sample: top_k <= 0 (whole-vocabulary sampling) is not built");
+  if (top_k <= 0) {
+    if (top_p != 1.0f)
+      return set_error(YB_ERR_UNSUPPORTED, "sample: top_k <= 0 with top_p < 1 (a whole-vocabulary sort) is not built");
+    const int64_t need = sample_workspace_bytes(B, vocab, top_k);
+    if (workspace == nullptr || workspace_bytes < need)
+      return set_error(YB_ERR_WORKSPACE, "sample: workspace of %lld bytes required", (long long)need);
+    return launch_sample_cdf(a);
+  }
   const int64_t need = sample_workspace_bytes(B, vocab, top_k);
   if (workspace == nullptr || workspace_bytes < need)
     return set_error(YB_ERR_WORKSPACE, "sample: workspace of %lld bytes required", (long long)need);

@@ -133,6 +133,7 @@ int launch_sample_greedy(const SampleArgs &a);
 int launch_sample_greedy_noalloc(const SampleArgs &a);
 int64_t greedy_builtin_scratch_bytes();
 int launch_sample_topk_topp(const SampleArgs &a);
+int launch_sample_cdf(const SampleArgs &a);
 int launch_presence_penalty(void *scores, const uint8_t *seen, int64_t n, float penalty, int dtype,
                             cudaStream_t stream);
 

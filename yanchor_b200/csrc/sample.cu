@@ -397,6 +397,167 @@ __global__ void gates_kernel(const T *b, const T *a, int64_t b_rs, int64_t a_rs,
   }
 }
 
+// ------------------------------------------------ whole-vocabulary CDF ------
+// top_k <= 0 with top_p == 1 (runtime/model/inference_kernels.py:77-80):
+// softmax(scores / temperature) over the whole vocabulary in index order,
+// then the first index whose running sum reaches min(u * total,
+// nextafter(total, 0)).  Pass 1: per (row, span) the max of x / T and the
+// exp-sum relative to it (online, one read).  Pass 2, one CTA per row: join
+// the spans, find the span where the running sum crosses the threshold, and
+// scan that span in index order (block-wide prefix sums) for the index.
+// The running sums are fp32 in a different order than a sequential cumsum;
+// ids can differ only where the threshold lies within rounding distance of a
+// CDF step.
+struct SoftPart {
+  float m, z;
+};
+
+__device__ __forceinline__ void join_soft(float &m, float &z, float m2, float z2) {
+  const float mm = fmaxf(m, m2);
+  z = (mm == -INFINITY) ? 0.f : z * __expf(m - mm) + z2 * __expf(m2 - mm);
+  m = mm;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kNT) cdf_partial_kernel(const T *scores, int64_t row_stride, int64_t vocab,
+                                                          int splits, float temperature, SoftPart *ws) {
+  __shared__ float red_m[kNT / 32], red_z[kNT / 32];
+  const int64_t b = blockIdx.y;
+  const int64_t lo = int64_t(blockIdx.x) * kTopkSpan;
+  const int64_t hi = lo + kTopkSpan < vocab ? lo + kTopkSpan : vocab;
+  const T *row = scores + b * row_stride;
+  float m = -INFINITY, z = 0.f;
+  for (int64_t i = lo + threadIdx.x; i < hi; i += kNT) {
+    const float x = to_f(row[i]) / temperature;
+    if (x == -INFINITY) continue;              // masked logits add nothing (and -inf - -inf is NaN)
+    if (x > m) {
+      z = z * __expf(m - x) + 1.f;
+      m = x;
+    } else {
+      z += __expf(x - m);
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o), z2 = __shfl_xor_sync(0xffffffffu, z, o);
+    join_soft(m, z, m2, z2);
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    red_m[warp] = m;
+    red_z[warp] = z;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float M = -INFINITY, Z = 0.f;
+    for (int w = 0; w < kNT / 32; ++w) join_soft(M, Z, red_m[w], red_z[w]);
+    ws[b * splits + blockIdx.x] = SoftPart{M, Z};
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kNT) cdf_final_kernel(const T *scores, int64_t row_stride, int64_t vocab,
+                                                        int splits, float temperature, const SoftPart *ws,
+                                                        const int64_t *attempt, const int64_t *steps,
+                                                        int64_t scalar_step, int64_t seed, int64_t stream_id,
+                                                        int64_t *out) {
+  constexpr int PER = 8;                      // consecutive elements per thread per tile
+  constexpr int TILE = kNT * PER;
+  __shared__ float s_base, s_thr, s_M;
+  __shared__ int s_split;
+  __shared__ float warp_tot[kNT / 32];
+  __shared__ int s_found;
+  const int64_t b = blockIdx.x;
+  const T *row = scores + b * row_stride;
+  if (threadIdx.x == 0) {
+    float M = -INFINITY;
+    for (int s = 0; s < splits; ++s) M = fmaxf(M, ws[b * splits + s].m);
+    float Z = 0.f;
+    for (int s = 0; s < splits; ++s) {
+      const SoftPart p = ws[b * splits + s];
+      Z += p.m == -INFINITY ? 0.f : p.z * __expf(p.m - M);
+    }
+    const float u = counter_uniform(attempt[b], steps ? steps[b] : scalar_step, seed, stream_id);
+    const float thr = fminf(u * Z, nextafterf(Z, 0.f));
+    // the span whose running sum first reaches the threshold
+    float base = 0.f;
+    int split = splits - 1;
+    for (int s = 0; s < splits; ++s) {
+      const SoftPart p = ws[b * splits + s];
+      const float zs = p.m == -INFINITY ? 0.f : p.z * __expf(p.m - M);
+      if (base + zs >= thr) {
+        split = s;
+        break;
+      }
+      base += zs;
+    }
+    s_base = base;
+    s_thr = thr;
+    s_M = M;
+    s_split = split;
+    s_found = 0x7fffffff;
+  }
+  __syncthreads();
+  const float M = s_M, thr = s_thr;
+  float base = s_base;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // scan from the chosen span onward (later spans only if rounding moved the crossing)
+  for (int64_t t0 = int64_t(s_split) * kTopkSpan; t0 < vocab; t0 += TILE) {
+    const int64_t i0 = t0 + int64_t(threadIdx.x) * PER;
+    float e[PER], mine = 0.f;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      e[j] = (i0 + j < vocab) ? __expf(to_f(row[i0 + j]) / temperature - M) : 0.f;
+      mine += e[j];
+    }
+    // exclusive prefix of `mine` over the block
+    float incl = mine;
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    float before = 0.f, tile_tot = 0.f;
+    for (int w = 0; w < kNT / 32; ++w) {
+      if (w < warp) before += warp_tot[w];
+      tile_tot += warp_tot[w];
+    }
+    float run = base + before + (incl - mine);
+    if (i0 < vocab && run + mine >= thr) {     // the crossing is in this thread's elements
+      int hit = PER - 1;
+#pragma unroll
+      for (int j = 0; j < PER; ++j) {
+        run += e[j];
+        if (run >= thr) {
+          hit = j;
+          break;
+        }
+      }
+      const int64_t idx = i0 + hit < vocab ? i0 + hit : vocab - 1;
+      atomicMin(&s_found, int(idx));
+    }
+    __syncthreads();
+    if (s_found != 0x7fffffff) break;
+    base += tile_tot;
+    __syncthreads();                           // warp_tot is rewritten by the next tile
+  }
+  if (threadIdx.x == 0) out[b] = s_found != 0x7fffffff ? int64_t(s_found) : vocab - 1;
+}
+
+template <typename T>
+int cdf_t(const SampleArgs &a) {
+  const int splits = int((a.vocab + kTopkSpan - 1) / kTopkSpan);
+  SoftPart *ws = static_cast<SoftPart *>(a.workspace);
+  cdf_partial_kernel<T><<<dim3(splits, unsigned(a.B)), kNT, 0, a.stream>>>(
+      static_cast<const T *>(a.scores), a.row_stride, a.vocab, splits, a.temperature, ws);
+  int rc = check_launch("cdf_partial_kernel");
+  if (rc) return rc;
+  cdf_final_kernel<T><<<unsigned(a.B), kNT, 0, a.stream>>>(static_cast<const T *>(a.scores), a.row_stride, a.vocab,
+                                                          splits, a.temperature, ws, a.attempt_ids, a.steps,
+                                                          a.scalar_step, a.seed, a.stream_id, a.out);
+  return check_launch("cdf_final_kernel");
+}
+
 template <typename T>
 int greedy_t(const SampleArgs &a) {
   const int splits = greedy_splits(a.B, a.vocab);
@@ -437,7 +598,19 @@ int64_t sample_workspace_bytes(int64_t B, int64_t vocab, int64_t top_k) {
   const int64_t g = int64_t(greedy_splits(B, vocab)) * B * int64_t(sizeof(Cand));
   int64_t t = 0;
   if (top_k > 1) t = int64_t(topk_splits(vocab, top_k)) * top_k * B * int64_t(sizeof(Cand));
+  if (top_k <= 0) t = (vocab + kTopkSpan - 1) / kTopkSpan * B * int64_t(sizeof(SoftPart));
   return g > t ? g : t;
+}
+
+int launch_sample_cdf(const SampleArgs &a) {
+  if (a.B == 0) return YB_OK;
+  if (a.vocab >= 0x7fffffffLL) return set_error(YB_ERR_UNSUPPORTED, "sample: vocabulary too large");
+  switch (a.dtype) {
+    case YB_F32: return cdf_t<float>(a);
+    case YB_BF16: return cdf_t<__nv_bfloat16>(a);
+    case YB_F16: return cdf_t<__half>(a);
+  }
+  return set_error(YB_ERR_ARGUMENT, "sample: bad dtype %d", a.dtype);
 }
 
 int launch_sample_greedy(const SampleArgs &a) {

@@ -68,7 +68,7 @@ def sample_top_k_top_p_counter(scores, attempt_ids, steps, *, seed, temperature,
                                workspace=None):
     require_cuda(scores)
     scores = _rows(scores)
-    if temperature <= 0.0 or top_k <= 0 and top_p != 1.0 or not 0.0 < top_p <= 1.0:
+    if temperature <= 0.0 or not 0.0 < top_p <= 1.0:
         raise ValueError('invalid top-k/top-p sampling parameters')
     B, V = scores.shape
     if top_k > V:
@@ -88,7 +88,7 @@ def sample_top_k_top_p_counter(scores, attempt_ids, steps, *, seed, temperature,
     else:
         steps_t, scalar = None, int(steps)
     out = torch.empty((B, 1), device=scores.device, dtype=torch.int64)
-    need = workspace_bytes(B, V, max(int(top_k), 1))
+    need = workspace_bytes(B, V, int(top_k))
     if workspace is None or workspace.numel() < need:
         workspace = torch.empty(need, device=scores.device, dtype=torch.uint8)
     rc = _lib.lib().yb_sample_top_k_top_p_counter(
