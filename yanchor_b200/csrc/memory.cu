@@ -107,13 +107,125 @@ __global__ void __launch_bounds__(kReadThreads) mem_decode_read_kernel(const Mem
   }
 }
 
+// ---------------------------------------------------------------------------
+// Decode read, staged: the same read with the whole bank of a (row, group)
+// (CAP key rows and CAP value rows) put in flight at once by cp.async into
+// padded shared-memory rows, so one CTA's 2*CAP*D*sizeof(T) bytes stream at
+// once instead of one dependent row load per warp iteration.  Logits: one
+// (slot, head) pair per thread (the 16-byte row padding makes the 8 slots a
+// warp touches hit different banks); softmax: a warp per head; weighted
+// values: one feature column per thread for all R heads.  Used whenever the
+// staged bank fits in shared memory.
+// ---------------------------------------------------------------------------
+constexpr int kStageThreads = 256;
+
+__device__ __forceinline__ void cp_async16_mem(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
+
+template <typename T, int R, int D>
+__global__ void __launch_bounds__(kStageThreads) mem_decode_read_staged_kernel(const MemReadArgs a) {
+  constexpr int ROWB = D * int(sizeof(T)) + 16;   // padded row bytes
+  constexpr int PIECES = D * int(sizeof(T)) / 16;
+  constexpr int QP = D + 4;                       // padded q row (floats)
+  extern __shared__ __align__(16) unsigned char st_raw[];
+  const int CAP = int(a.CAP);
+  unsigned char *sk = st_raw;                                     // [CAP][ROWB]
+  unsigned char *sv = sk + size_t(CAP) * ROWB;                    // [CAP][ROWB]
+  float *sq = reinterpret_cast<float *>(sv + size_t(CAP) * ROWB); // [R][QP]
+  float *sw = sq + R * QP;                                        // [R][CAP]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t row = blockIdx.x / a.G;
+  const int g = int(blockIdx.x % a.G);
+  const int64_t s = a.indices ? a.indices[row] : row;
+  const T *qp = static_cast<const T *>(a.query) + (row * a.H + int64_t(g) * R) * D;
+  T *outp = static_cast<T *>(a.out) + (row * a.H + int64_t(g) * R) * D;
+  if (s < 0) {  // skipped request: zeros
+    for (int e = tid; e < R * D; e += kStageThreads) outp[e] = from_f<T>(0.f);
+    return;
+  }
+  const unsigned char *kp =
+      reinterpret_cast<const unsigned char *>(static_cast<const T *>(a.keys) + s * a.kv_s0 + int64_t(g) * CAP * D);
+  const unsigned char *vp =
+      reinterpret_cast<const unsigned char *>(static_cast<const T *>(a.values) + s * a.kv_s0 + int64_t(g) * CAP * D);
+  const int32_t *pp = a.positions + s * a.pos_s0 + int64_t(g) * CAP;
+  for (int e = tid; e < CAP * PIECES; e += kStageThreads) {
+    const int slot = e / PIECES, pc = e % PIECES;
+    cp_async16_mem(sk + slot * ROWB + pc * 16, kp + (size_t(slot) * D * sizeof(T) + pc * 16));
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  for (int e = tid; e < CAP * PIECES; e += kStageThreads) {
+    const int slot = e / PIECES, pc = e % PIECES;
+    cp_async16_mem(sv + slot * ROWB + pc * 16, vp + (size_t(slot) * D * sizeof(T) + pc * 16));
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  for (int e = tid; e < R * D; e += kStageThreads) sq[(e / D) * QP + e % D] = to_f(qp[e]);
+  asm volatile("cp.async.wait_group 1;" ::: "memory");   // keys are in
+  __syncthreads();
+  const float scale = rsqrtf(float(D));
+  for (int e = tid; e < CAP * R; e += kStageThreads) {
+    const int slot = e / R, r = e % R;
+    const T *krow = reinterpret_cast<const T *>(sk + slot * ROWB);
+    const float *qr = sq + r * QP;
+    float acc = 0.f;
+#pragma unroll 4
+    for (int d = 0; d < D; d += 8) {
+      float kx[8];
+      load8(krow + d, kx);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc = fmaf(qr[d + j], kx[j], acc);
+    }
+    sw[r * CAP + slot] = pp[slot] >= 0 ? acc * scale : -INFINITY;
+  }
+  __syncthreads();
+  // softmax with the null logit 0: a warp per head
+  for (int r = warp; r < R; r += kStageThreads / 32) {
+    float m = 0.f;
+    for (int j = lane; j < CAP; j += 32) m = fmaxf(m, sw[r * CAP + j]);
+    m = warp_max(m);
+    float den = 0.f;
+    for (int j = lane; j < CAP; j += 32) {
+      const float e = expf(sw[r * CAP + j] - m);
+      sw[r * CAP + j] = e;
+      den += e;
+    }
+    den = warp_sum(den) + expf(-m);
+    const float inv = 1.f / den;
+    for (int j = lane; j < CAP; j += 32) sw[r * CAP + j] *= inv;
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");   // values are in
+  __syncthreads();
+  for (int d = tid; d < D; d += kStageThreads) {
+    float acc[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = 0.f;
+    for (int slot = 0; slot < CAP; ++slot) {
+      const float x = to_f(reinterpret_cast<const T *>(sv + slot * ROWB)[d]);
+#pragma unroll
+      for (int r = 0; r < R; ++r) acc[r] = fmaf(sw[r * CAP + slot], x, acc[r]);
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) outp[r * D + d] = from_f<T>(acc[r]);
+  }
+}
+
 template <typename T, int R>
 int launch_read_r(const MemReadArgs &a) {
   const size_t smem = sizeof(float) * (R * a.D + R * a.CAP + (kReadThreads / 32) * R * a.D);
+  const size_t staged = size_t(a.CAP) * 2 * (a.D * sizeof(T) + 16) + sizeof(float) * (R * (a.D + 4) + R * a.CAP);
   dim3 grid(unsigned(a.B * a.G));
   switch (a.D) {
 #define YB_READ_CASE(DD)                                                                           \
   case DD: {                                                                                       \
+    if (staged <= 160 * 1024) {                                                                    \
+      auto sk = mem_decode_read_staged_kernel<T, R, DD>;                                           \
+      cudaError_t e = cudaFuncSetAttribute(sk, cudaFuncAttributeMaxDynamicSharedMemorySize, int(staged)); \
+      if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "memory read: smem attribute: %s", cudaGetErrorString(e)); \
+      sk<<<grid, kStageThreads, staged, a.stream>>>(a);                                            \
+      return check_launch("mem_decode_read_staged_kernel");                                        \
+    }                                                                                              \
     auto kern = mem_decode_read_kernel<T, R, DD>;                                                  \
     if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)); \
     kern<<<grid, kReadThreads, smem, a.stream>>>(a);                                               \
