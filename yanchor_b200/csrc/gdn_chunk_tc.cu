@@ -42,8 +42,8 @@ using namespace tc;
 constexpr int C = 64;       // chunk length
 constexpr int KD = 128;     // key dim
 constexpr int VD = 128;     // value dim
-constexpr int NTHREADS = 192;
-constexpr int EPI_THREADS = 128;
+constexpr int NTHREADS = 320;   // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
+constexpr int EPI_THREADS = 256;
 constexpr int LP = 68;      // row pitch (floats) of the fp32 L matrix: 16-byte aligned rows
 
 // ---- shared memory map (bytes); SW128 tiles on 1024-byte boundaries ----
@@ -112,7 +112,7 @@ __device__ __forceinline__ float load_scalar(const void *p, int64_t idx, int dty
   return __half2float(static_cast<const __half *>(p)[idx]);
 }
 
-__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }   // all 8 epilogue warps
 // epilogue threads 0..63 (warps 4 and 5) only: the phases of the triangular solve
 __device__ __forceinline__ void solve_sync() { asm volatile("bar.sync 2, 64;" ::: "memory"); }
 
@@ -160,21 +160,21 @@ constexpr int DBG_D1 = 0, DBG_W = 16384, DBG_U = 24576, DBG_X = 32768, DBG_Y = 4
 #ifdef YB_TC_DEBUG
 // Test-only: copy `n` values of TMEM row r (already in registers) into the
 // debug buffer at tile offset `off` (row-major, `n` columns).
-#define YB_DBG_ROW(off, n, vals)                                                       \
+#define YB_DBG_ROW(off, width, base, n, vals)                                          \
   do {                                                                                 \
     if (p.dbg && blockIdx.x == 0 && c == 0)                                            \
-      for (int _i = 0; _i < (n); ++_i) p.dbg[(off) + r * (n) + _i] = (vals)[_i];       \
+      for (int _i = 0; _i < (n); ++_i) p.dbg[(off) + r * (width) + (base) + _i] = (vals)[_i]; \
   } while (0)
 // Test-only: phase timestamps (ns since the thread started) of epilogue
 // thread 0 of CTA 0 for the first 32 chunks, 16 events per chunk.
 #define YB_DBG_TS(ev)                                                                   \
   do {                                                                                  \
-    if (p.dbg && blockIdx.x == 0 && r == 0 && c < 32)                                   \
+    if (p.dbg && blockIdx.x == 0 && et == 0 && c < 32)                                  \
       p.dbg[DBG_TS + c * 16 + (ev)] = float(globaltimer_ns() - dbg_t0);                 \
   } while (0)
 #else
-#define YB_DBG_ROW(off, n, vals) \
-  do {                           \
+#define YB_DBG_ROW(off, width, base, n, vals) \
+  do {                                        \
   } while (0)
 #define YB_DBG_TS(ev) \
   do {                \
@@ -388,8 +388,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     __syncwarp();
   } else {
-    // ===================== epilogue (128 threads) =====================
+    // ===================== epilogue (256 threads, 8 warps) =====================
+    // Warps 2..5 (half 0) and 6..9 (half 1) each cover the four TMEM lane
+    // quarters, so thread (r, half) owns tile row r and, of every row, the
+    // column half `half`: 32 of 64 columns, or 64 of the state's 128.
     const int r = (warp & 3) * 32 + lane;            // TMEM lane == tile row
+    const int half = (warp - 2) >> 2;
+    const int et = half * 128 + r;                   // 0..255
+    const int j0 = 32 * half;                        // first of this thread's 32 columns
 #ifdef YB_TC_DEBUG
     const uint64_t dbg_t0 = globaltimer_ns();
 #endif
@@ -411,11 +417,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_arrive(epi_bar);
     };
 
-    // ---- initial state: thread r owns value column v = r ----
+    // ---- initial state: thread r owns value column v = r; half h the key rows 64h .. 64h+63 ----
     {
       float row[32];
 #pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
+      for (int qq = 0; qq < 2; ++qq) {
+        const int q4 = 2 * half + qq;
 #pragma unroll
         for (int d = 0; d < 32; ++d) {
           const int dd = q4 * 32 + d;
@@ -447,10 +454,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       if (!wait_mma()) break;   // MMA1 done
       YB_DBG_TS(2);
       // ---------- step 2: norms (diagonal of D1), L, P ----------
-      float d1[64];
-      tmem_ld32(lane_base + T_D1, d1);
-      tmem_ld32(lane_base + T_D1 + 32, d1 + 32);
-      {
+      float d1[32];   // row r of D1, columns j0 .. j0+31
+      tmem_ld32(lane_base + T_D1 + uint32_t(j0), d1);
+      if (half == 0) {
         float dg[32];   // the 32 columns holding this thread's own diagonal entry
         tmem_ld32(lane_base + T_D1 + uint32_t(r & ~31), dg);
         tmem_wait_ld();
@@ -471,30 +477,44 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const float nrm = l2 ? rsqrtf(diag + 1e-6f) : 1.f;
         if (r < 64) kn[r] = nrm;
         else qn[r - 64] = nrm * p.scale;
+      } else {
+        tmem_wait_ld();
       }
       epi_sync();
       YB_DBG_TS(14);
       if (r < 64) {
-        // threads 0..63: row r of L, then column r of T = (I + L)^-1 ...
-        {
-          const int i = r;
-          const float ci = BT[i] * kn[i], gi = G[i];
+        // row r of L, columns j0 .. j0+31 (branch-free mask; the exponent is
+        // clamped so masked entries stay finite)
+        const int i = r;
+        const float ci = BT[i] * kn[i], gi = G[i];
 #pragma unroll
-          for (int j4 = 0; j4 < 16; ++j4) {
-            float4 v4;
-            float *vv = reinterpret_cast<float *>(&v4);
+        for (int j4 = 0; j4 < 8; ++j4) {
+          float4 v4;
+          float *vv = reinterpret_cast<float *>(&v4);
 #pragma unroll
-            for (int t = 0; t < 4; ++t) {
-              // branch-free mask (the exponent is clamped so masked lanes stay finite)
-              const int j = 4 * j4 + t;
-              vv[t] = ci * kn[j] * __expf(fminf(gi - G[j], 0.f)) * d1[j] * float(j < i);
-            }
-            *reinterpret_cast<float4 *>(LF + i * LP + 4 * j4) = v4;
+          for (int t = 0; t < 4; ++t) {
+            const int jj = 4 * j4 + t, j = j0 + jj;
+            vv[t] = ci * kn[j] * __expf(fminf(gi - G[j], 0.f)) * d1[jj] * float(j < i);
           }
+          *reinterpret_cast<float4 *>(LF + i * LP + j0 + 4 * j4) = v4;
         }
-        YB_DBG_TS(15);
-        solve_sync();
-        YB_DBG_TS(3);
+      } else {
+        // row r-64 of P, columns j0 .. j0+31
+        const int i = r - 64;
+        const float ci = qn[i], gi = G[i];
+        float pr[32];
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) {
+          const int j = j0 + jj;
+          pr[jj] = ci * kn[j] * __expf(fminf(gi - G[j], 0.f)) * d1[jj] * float(j <= i);
+        }
+        st_half_bf16(smem + OFF_P, 64, 0, i, 4 * half, pr);
+      }
+      YB_DBG_TS(15);
+      epi_sync();
+      YB_DBG_TS(3);
+      if (r < 64 && half == 0) {
+        // warps 4 and 5: T = (I + L)^-1 (solve_sync spans exactly these 64 threads)
         // ---- T = (I + L)^-1 by 16x16 blocks: T_ii = D_i (diagonal inverses),
         //      T_ij = -sum_{m=j}^{i-1} M_im T_mj with M_im = D_i L_im ----
         float *TF = reinterpret_cast<float *>(smem + OFF_TF);   // T fp32, pitch LP
@@ -553,25 +573,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           block_mma16_tf32(acc, MB + 2 * 320, 20, TF + 32 * LP, LP);
           store_block16(TF + 48 * LP, LP, acc, -1.f);
         }
-      } else {
-        // threads 64..127: row r-64 of P, concurrently
-        const int i = r - 64;
-        const float ci = qn[i], gi = G[i];
-        float pr[64];
-#pragma unroll
-        for (int j = 0; j < 64; ++j) pr[j] = ci * kn[j] * __expf(fminf(gi - G[j], 0.f)) * d1[j] * float(j <= i);
-        st_row64_bf16(smem + OFF_P, 64, 0, i, pr);
       }
       epi_sync();
       YB_DBG_TS(4);
-      // Tw (rows by threads 0..63) and Tu (threads 64..127) from T, as bf16 tiles
+      // Tw (rows 0..63 of threads r < 64) and Tu (threads r >= 64) from T, as bf16 tiles
       {
         const float *TF = reinterpret_cast<const float *>(smem + OFF_TF);
         const int i = r & 63;
-        float rowv[64];
+        float rowv[32];
 #pragma unroll
-        for (int j4 = 0; j4 < 16; ++j4) {
-          const float4 t4 = *reinterpret_cast<const float4 *>(TF + i * LP + 4 * j4);
+        for (int j4 = 0; j4 < 8; ++j4) {
+          const float4 t4 = *reinterpret_cast<const float4 *>(TF + i * LP + j0 + 4 * j4);
           rowv[4 * j4] = t4.x;
           rowv[4 * j4 + 1] = t4.y;
           rowv[4 * j4 + 2] = t4.z;
@@ -580,23 +592,23 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #ifdef YB_TC_DEBUG
         if (p.dbg && blockIdx.x == 0 && c == 0) {
           if (r < 64)
-            for (int j = 0; j < 64; ++j) p.dbg[DBG_T + r * 64 + j] = rowv[j];
-          p.dbg[DBG_NORM + r] = r < 64 ? kn[r] : qn[r - 64];
+            for (int jj = 0; jj < 32; ++jj) p.dbg[DBG_T + r * 64 + j0 + jj] = rowv[jj];
+          if (half == 0) p.dbg[DBG_NORM + r] = r < 64 ? kn[r] : qn[r - 64];
         }
 #endif
         // both factors enter MMA2 as bf16 hi + lo: a single bf16 rounding of T
         // alone costs ~2e-3 relative on the state
         if (r < 64) {
 #pragma unroll
-          for (int j = 0; j < 64; ++j) rowv[j] *= BT[j] * EG[j] * kn[j];
+          for (int jj = 0; jj < 32; ++jj) rowv[jj] *= BT[j0 + jj] * EG[j0 + jj] * kn[j0 + jj];
         } else {
 #pragma unroll
-          for (int j = 0; j < 64; ++j) rowv[j] *= BT[j];
+          for (int jj = 0; jj < 32; ++jj) rowv[jj] *= BT[j0 + jj];
         }
-        st_row64_bf16(smem + (r < 64 ? OFF_TW : OFF_TU), 64, 0, i, rowv);
+        st_half_bf16(smem + (r < 64 ? OFF_TW : OFF_TU), 64, 0, i, 4 * half, rowv);
 #pragma unroll
-        for (int j = 0; j < 64; ++j) rowv[j] -= __bfloat162float(__float2bfloat16_rn(rowv[j]));
-        st_row64_bf16(smem + (r < 64 ? OFF_TWLO : OFF_TULO), 64, 0, i, rowv);
+        for (int jj = 0; jj < 32; ++jj) rowv[jj] -= __bfloat162float(__float2bfloat16_rn(rowv[jj]));
+        st_half_bf16(smem + (r < 64 ? OFF_TWLO : OFF_TULO), 64, 0, i, 4 * half, rowv);
       }
       signal_mma();
       YB_DBG_TS(5);
@@ -604,12 +616,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       if (!wait_mma()) break;
       YB_DBG_TS(6);
       {
-        float w[64];
-        tmem_ld32(lane_base + T_W, w);
-        tmem_ld32(lane_base + T_W + 32, w + 32);
+        float w[32];
+        tmem_ld32(lane_base + T_W + uint32_t(j0), w);
         tmem_wait_ld();
-        YB_DBG_ROW(DBG_W, 64, w);
-        st_row64_bf16(smem + OFF_WT, 128, 0, r, w);
+        YB_DBG_ROW(DBG_W, 64, j0, 32, w);
+        st_half_bf16(smem + OFF_WT, 128, 0, r, 4 * half, w);
       }
       signal_mma();
       YB_DBG_TS(7);
@@ -617,51 +628,49 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       if (!wait_mma()) break;
       YB_DBG_TS(8);
       {
-        float u[64], x[64];
-        tmem_ld32(lane_base + T_U, u);
-        tmem_ld32(lane_base + T_U + 32, u + 32);
-        tmem_ld32(lane_base + T_W, x);
-        tmem_ld32(lane_base + T_W + 32, x + 32);
+        float u[32], x[32];
+        tmem_ld32(lane_base + T_U + uint32_t(j0), u);
+        tmem_ld32(lane_base + T_W + uint32_t(j0), x);
         tmem_wait_ld();
-        YB_DBG_ROW(DBG_U, 64, u);
-        YB_DBG_ROW(DBG_X, 64, x);
+        YB_DBG_ROW(DBG_U, 64, j0, 32, u);
+        YB_DBG_ROW(DBG_X, 64, j0, 32, x);
 #pragma unroll
-        for (int i = 0; i < 64; ++i) u[i] -= x[i];
-        st_row64_bf16(smem + OFF_VN, 128, 0, r, u);
+        for (int i = 0; i < 32; ++i) u[i] -= x[i];
+        st_half_bf16(smem + OFF_VN, 128, 0, r, 4 * half, u);
         // v~ = v_new e^{G_last-G} kn enters the state update as bf16 hi + lo
         // parts (its rounding is what limits the fp32 state's accuracy)
 #pragma unroll
-        for (int i = 0; i < 64; ++i) u[i] *= TAIL[i] * kn[i];
-        st_row64_bf16(smem + OFF_WT, 128, 0, r, u);
+        for (int i = 0; i < 32; ++i) u[i] *= TAIL[j0 + i] * kn[j0 + i];
+        st_half_bf16(smem + OFF_WT, 128, 0, r, 4 * half, u);
 #pragma unroll
-        for (int i = 0; i < 64; ++i) u[i] -= __bfloat162float(__float2bfloat16_rn(u[i]));
-        st_row64_bf16(smem + OFF_TF, 128, 0, r, u);
+        for (int i = 0; i < 32; ++i) u[i] -= __bfloat162float(__float2bfloat16_rn(u[i]));
+        st_half_bf16(smem + OFF_TF, 128, 0, r, 4 * half, u);
       }
       signal_mma();
       YB_DBG_TS(9);
       // ---------- step 8: state update first (it gates the next chunk), then o ----------
       if (!wait_mma()) break;
       YB_DBG_TS(10);
-      uint32_t opk[32];   // this thread's o column as packed bf16 pairs (tokens 2t, 2t+1)
+      uint32_t opk[16];   // this thread's o column, tokens j0 + 2t and j0 + 2t + 1, as packed bf16 pairs
       {
-        float y[64], oo[64];
-        tmem_ld32(lane_base + T_Y, y);
-        tmem_ld32(lane_base + T_Y + 32, y + 32);
-        tmem_ld32(lane_base + T_D1, oo);
-        tmem_ld32(lane_base + T_D1 + 32, oo + 32);
+        float y[32], oo[32];
+        tmem_ld32(lane_base + T_Y + uint32_t(j0), y);
+        tmem_ld32(lane_base + T_D1 + uint32_t(j0), oo);
         tmem_wait_ld();
-        YB_DBG_ROW(DBG_Y, 64, y);
-        YB_DBG_ROW(DBG_O, 64, oo);
+        YB_DBG_ROW(DBG_Y, 64, j0, 32, y);
+        YB_DBG_ROW(DBG_O, 64, j0, 32, oo);
 #pragma unroll
-        for (int t = 0; t < 32; ++t)
-          opk[t] = pack_bf16x2(EG[2 * t] * qn[2 * t] * y[2 * t] + oo[2 * t],
-                               EG[2 * t + 1] * qn[2 * t + 1] * y[2 * t + 1] + oo[2 * t + 1]);
+        for (int t = 0; t < 16; ++t) {
+          const int a = j0 + 2 * t;
+          opk[t] = pack_bf16x2(EG[a] * qn[a] * y[2 * t] + oo[2 * t], EG[a + 1] * qn[a + 1] * y[2 * t + 1] + oo[2 * t + 1]);
+        }
       }
       {
         const float decay = EG[63];   // e^{G_last}
         const bool last = c == nchunks - 1;
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
+        for (int qq = 0; qq < 2; ++qq) {
+          const int q4 = 2 * half + qq;
           float sv[32], dv[32];
           tmem_ld32(lane_base + T_S + q4 * 32, sv);
           tmem_ld32(lane_base + T_DS + q4 * 32, dv);
@@ -689,23 +698,23 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       // release the MMA warp (next chunk's MMA1 overlaps the output store below)
       // and the stage's gates / tiles (everything read from them is in registers)
       signal_mma();
-      if (r == 0) mbar_arrive(&empty[s]);
+      if (et == 0) mbar_arrive(&empty[s]);
       {
         __nv_bfloat16 *ostage = reinterpret_cast<__nv_bfloat16 *>(smem + OFF_LF);  // [64][128]
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
+        for (int t = 0; t < 16; ++t) {
           const __nv_bfloat162 pr2 = *reinterpret_cast<const __nv_bfloat162 *>(&opk[t]);
-          ostage[(2 * t) * 128 + r] = pr2.x;
-          ostage[(2 * t + 1) * 128 + r] = pr2.y;
+          ostage[(j0 + 2 * t) * 128 + r] = pr2.x;
+          ostage[(j0 + 2 * t + 1) * 128 + r] = pr2.y;
         }
       }
       epi_sync();
       {
-        // copy the o tile out: 16-byte piece q = r + 128 t covers row q / 16, bytes 16 (q % 16);
+        // copy the o tile out: 16-byte piece q = et + 256 t covers row q / 16, bytes 16 (q % 16);
         // consecutive threads touch consecutive pieces (conflict-free, coalesced)
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          const int q = r + 128 * t, i = q >> 4, piece = q & 15;
+        for (int t = 0; t < 4; ++t) {
+          const int q = et + 256 * t, i = q >> 4, piece = q & 15;
           if (i < m) {
             const uint4 v = *reinterpret_cast<const uint4 *>(smem + OFF_LF + q * 16);
             *reinterpret_cast<uint4 *>(p.o + ((bos + int64_t(c) * C + i) * p.HV + hv) * VD + piece * 8) = v;
