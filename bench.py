@@ -130,7 +130,7 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------- GPU arm --
-def build_decode(torch, yb, B, device, n_inputs=4, seed=0):
+def build_decode(torch, yb, B, device, n_inputs=4, seed=0, state_dtype=None):
     """Allocate the model-shaped state and `n_inputs` sets of step inputs."""
     gen = torch.Generator(device=device).manual_seed(seed)
     bf = torch.bfloat16
@@ -140,7 +140,8 @@ def build_decode(torch, yb, B, device, n_inputs=4, seed=0):
 
     layers = []
     for _ in range(L_GDN):
-        layers.append(dict(state=0.02 * torch.randn(B, H_V, DK, DV, generator=gen, device=device),
+        layers.append(dict(state=(0.02 * torch.randn(B, H_V, DK, DV, generator=gen, device=device)).to(
+                               state_dtype or torch.float32),
                            A_log=torch.empty(H_V, device=device).uniform_(1, 16, generator=gen).log(),
                            dt_bias=torch.ones(H_V, device=device),
                            norm_w=rnd(DV, scale=0.1) + 1.0))
@@ -174,8 +175,8 @@ def decode_step(yb, layers, mems, x, active, ws):
 LAUNCHES_PER_STEP = L_GDN + 2 * L_MEM + 2
 
 
-def gdn_bytes_per_launch(B):
-    state = B * H_V * DK * DV * 4 * 2                      # fp32 state read + write
+def gdn_bytes_per_launch(B, state_bytes=4):
+    state = B * H_V * DK * DV * state_bytes * 2            # state read + write (fp32, or a 16-bit storage)
     acts = B * (2 * H_K * DK + 3 * H_V * DV) * 2 + B * H_V * 2 * 2   # q, k, v, z, o (bf16) + a, b
     return state + acts
 
@@ -336,6 +337,37 @@ def run_gpu(args, rank, world, local_rank, dist):
         e2e_ms = shard.max_over_ranks(e2e_ms, device=device)
         e2e_serial_ms = shard.max_over_ranks(e2e_serial_ms, device=device)
 
+    # ---- the reference's opt-in fp16 recurrent-state storage (install_inference(fp16_state=True)) ----
+    layers16, mems16, inputs16, _, ws16 = build_decode(torch, yb, B, device, n_inputs=1, seed=99 + rank,
+                                                       state_dtype=torch.float16)
+    for _ in range(3):
+        decode_step(yb, layers16, mems16, inputs16[0], active, ws16)
+    torch.cuda.synchronize()
+    g16 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g16):
+        decode_step(yb, layers16, mems16, inputs16[0], active, ws16)
+    for _ in range(3):
+        g16.replay()
+    ms16 = time_events(torch, g16.replay, max(3, args.steps // 2), stream)
+    L16 = layers16[0]
+
+    def one_gdn16():
+        yb.fused_recurrent_gated_delta_rule(
+            inputs16[0]['q'][0], inputs16[0]['k'][0], inputs16[0]['v'][0], g=inputs16[0]['a'][0],
+            beta=inputs16[0]['b'][0], initial_state=L16['state'], output_final_state=True,
+            use_qk_l2norm_in_kernel=True, use_gate_in_kernel=True, A_log=L16['A_log'], dt_bias=L16['dt_bias'],
+            use_beta_sigmoid_in_kernel=True, z=inputs16[0]['z'][0], norm_weight=L16['norm_w'], inplace=True)
+    gg16 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gg16):
+        for _ in range(L_GDN):
+            one_gdn16()
+    gg16.replay()
+    gdn16_ms = time_events(torch, gg16.replay, 5, stream) / L_GDN
+    gbytes16 = gdn_bytes_per_launch(B, state_bytes=2)
+    del g16, gg16
+    if dist is not None:
+        ms16 = shard.max_over_ranks(ms16, device=device)
+
     result = {
         'metric': METRIC, 'value': round(value, 1), 'unit': 'tok/s', 'n_gpus': world, 'steps': args.steps,
         'warmup': args.warmup, 'ms_per_step': round(ms, 4), 'higher_is_better': True, 'scaling': 'weak',
@@ -352,6 +384,13 @@ def run_gpu(args, rank, world, local_rank, dist):
                        'activations + logits in on a copy stream (overlapping the other group\'s step), replays '
                        'its graph and copies its token ids out; serial_*: one group, copy then step, one stream; '
                        'CUDA events on the compute stream'},
+        'decode_fp16_state': {
+            'value': round(world * B / (ms16 / 1e3), 1), 'unit': 'tok/s', 'ms_per_step': round(ms16, 4),
+            'how': 'the same step with the GDN state stored as fp16 (the reference\'s opt-in fp16_non_anchor '
+                   'storage): widened to fp32 per step, rounded to nearest on store',
+            'gdn_kernel': {'achieved': round(gbytes16 / (gdn16_ms / 1e3) / 1e9, 1), 'peak': hbm, 'unit': 'GB/s',
+                           'frac': round(gbytes16 / (gdn16_ms / 1e3) / 1e9 / hbm, 4), 'bytes_per_launch': gbytes16,
+                           'launch_ms': round(gdn16_ms, 5)}},
         'gpu_launches': LAUNCHES_PER_STEP * args.steps,
         'clocks': clocks.summary(),
     }

@@ -45,6 +45,8 @@ enum yb_status {
 #define YB_GDN_GATE_IN_KERNEL 2u   /* g holds raw `a`; decay = -exp(A_log) * softplus(a + dt_bias) */
 #define YB_GDN_BETA_SIGMOID 4u     /* beta holds logits; beta = sigmoid(beta) */
 #define YB_GDN_TRANSPOSE_STATE 8u  /* state layout [N, HV, V, K] instead of [N, HV, K, V] */
+#define YB_GDN_STATE_F16 16u       /* yb_gdn_recurrent_fwd: h0 / ht are float16 (else float32) */
+#define YB_GDN_STATE_BF16 32u      /* yb_gdn_recurrent_fwd: h0 / ht are bfloat16 */
 
 /* Message of the calling thread's last failed call ("" if none). */
 const char *yb_last_error(void);
@@ -68,7 +70,12 @@ int yb_device_error(int clear);
  *
  *   q, k  [B, T, H, K]    v, o  [B, T, HV, V]    g, beta  [B, T, HV]
  *   h0, ht [N, HV, K, V] fp32 (or [N, HV, V, K] with YB_GDN_TRANSPOSE_STATE);
- *   either may be NULL; they may alias.
+ *   either may be NULL; they may alias.  With YB_GDN_STATE_F16 or
+ *   YB_GDN_STATE_BF16 (K = V = 128) both are float16 / bfloat16: the
+ *   reference's reduced-precision state storage for decode
+ *   (runtime/model/inference_kernels.py:437-457, modeling_yanchor.py:733-750);
+ *   the state is widened to fp32 for the step and rounded to nearest when
+ *   stored.
  *   *_tok_stride: elements between consecutive tokens of the flattened
  *   (B*T) token axis; heads and features are contiguous inside a token.
  *   cu_seqlens: NULL, or [N+1] int64 with B == 1 (varlen packing).
@@ -81,7 +88,7 @@ int yb_device_error(int clear);
 int yb_gdn_recurrent_fwd(const void *q, const void *k, const void *v, int64_t q_tok_stride,
                          int64_t k_tok_stride, int64_t v_tok_stride, const void *g, const void *beta,
                          int64_t g_tok_stride, int64_t beta_tok_stride, const float *A_log,
-                         const float *dt_bias, const float *h0, float *ht, void *o, const void *z,
+                         const float *dt_bias, const void *h0, void *ht, void *o, const void *z,
                          const void *norm_weight, float norm_eps, const int64_t *cu_seqlens, int64_t B,
                          int64_t T, int64_t H, int64_t HV, int64_t K, int64_t V, int64_t N, float scale,
                          int io_dtype, int g_dtype, int beta_dtype, uint32_t flags, void *stream);

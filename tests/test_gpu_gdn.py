@@ -121,6 +121,57 @@ def test_decode_inplace_state_and_steps(yb):
     assert rel(host(state), es) <= STATE_RTOL
 
 
+@pytest.mark.parametrize('sdtype', [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize('trans', [False, True])
+def test_decode_16bit_state_storage(yb, sdtype, trans):
+    """The reference's reduced-precision state storage: a bf16 / fp16 state
+    updated in place over 8 decode calls (fp32 inside a call, rounded to
+    nearest on store) against the oracle with the same rounding after every
+    call."""
+    rng = np.random.default_rng(40 + trans)
+    B, H, HV, K, V, steps = 4, 16, 32, 128, 128, 8
+    q, k, v, g, beta, h0 = make_inputs(rng, B, steps, H, HV, K, V, h0_std=0.05)
+    if trans:
+        h0 = np.ascontiguousarray(h0.transpose(0, 1, 3, 2))
+    store = lambda x: torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(sdtype).float().numpy()  # noqa: E731
+    state = cuda(h0).to(sdtype)
+    es = store(h0)
+    outs, eouts = [], []
+    rb = lambda x: host(cuda(x, torch.bfloat16))  # noqa: E731
+    for t in range(steps):
+        sl = slice(t, t + 1)
+        o, s = yb.fused_recurrent_gated_delta_rule(
+            cuda(q[:, sl], torch.bfloat16), cuda(k[:, sl], torch.bfloat16), cuda(v[:, sl], torch.bfloat16),
+            g=cuda(g[:, sl]), beta=cuda(beta[:, sl]), initial_state=state, output_final_state=True,
+            use_qk_l2norm_in_kernel=True, transpose_state_layout=trans, inplace=True)
+        assert s is state and s.dtype == sdtype
+        outs.append(host(o))
+        eo, es = ogdn.recurrent_gated_delta_rule(rb(q[:, sl]), rb(k[:, sl]), rb(v[:, sl]), g[:, sl], beta[:, sl],
+                                                 initial_state=es, use_qk_l2norm=True, transpose_state=trans,
+                                                 dtype=np.float64)
+        es = store(es)
+        eouts.append(eo)
+    assert np.abs(np.concatenate(outs, 1) - np.concatenate(eouts, 1)).max() <= BF16_ATOL
+    assert rel(host(state), es) <= STATE_RTOL
+
+
+def test_decode_16bit_state_not_inplace_returns_fp32(yb):
+    """Without ``inplace`` a 16-bit initial state is read and a new float32
+    final state returned, as fla does."""
+    rng = np.random.default_rng(3)
+    q, k, v, g, beta, h0 = make_inputs(rng, 2, 1, 16, 32, 128, 128, h0_std=0.05)
+    st16 = cuda(h0).half()
+    o, s = yb.fused_recurrent_gated_delta_rule(cuda(q, torch.bfloat16), cuda(k, torch.bfloat16),
+                                               cuda(v, torch.bfloat16), g=cuda(g), beta=cuda(beta),
+                                               initial_state=st16, output_final_state=True,
+                                               use_qk_l2norm_in_kernel=True)
+    assert s.dtype == torch.float32 and s is not st16
+    rb = lambda x: host(cuda(x, torch.bfloat16))  # noqa: E731
+    eo, es = ogdn.recurrent_gated_delta_rule(rb(q), rb(k), rb(v), g, beta, initial_state=host(st16),
+                                             use_qk_l2norm=True, dtype=np.float64)
+    assert rel(host(s), es) <= STATE_RTOL
+
+
 def test_decode_gates_and_norm_in_kernel(yb):
     """use_gate_in_kernel + beta logits + the fused gated RMSNorm epilogue."""
     rng = np.random.default_rng(12)

@@ -19,6 +19,8 @@ GDN_QK_L2NORM = 1
 GDN_GATE_IN_KERNEL = 2
 GDN_BETA_SIGMOID = 4
 GDN_TRANSPOSE_STATE = 8
+GDN_STATE_F16 = 16
+GDN_STATE_BF16 = 32
 
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64

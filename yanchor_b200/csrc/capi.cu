@@ -56,7 +56,9 @@ static int check_gdn(const GdnArgs &a, const char *op) {
   YB_REQUIRE(!a.h0 || aligned(a.h0, 16), "%s: h0 must be 16-byte aligned", op);
   YB_REQUIRE(!a.ht || aligned(a.ht, 16), "%s: ht must be 16-byte aligned", op);
   if (a.flags & YB_GDN_GATE_IN_KERNEL) YB_REQUIRE(a.A_log != nullptr, "%s: A_log required with gate-in-kernel", op);
-  YB_REQUIRE(!(a.flags & ~15u), "%s: unknown flag bits 0x%x", op, a.flags);
+  YB_REQUIRE(!(a.flags & ~63u), "%s: unknown flag bits 0x%x", op, a.flags);
+  YB_REQUIRE((a.flags & (YB_GDN_STATE_F16 | YB_GDN_STATE_BF16)) != (YB_GDN_STATE_F16 | YB_GDN_STATE_BF16),
+             "%s: at most one state storage flag", op);
   return YB_OK;
 }
 
@@ -75,15 +77,18 @@ int yb_device_error(int clear) {
 
 int yb_gdn_recurrent_fwd(const void *q, const void *k, const void *v, int64_t q_tok_stride, int64_t k_tok_stride,
                          int64_t v_tok_stride, const void *g, const void *beta, int64_t g_tok_stride,
-                         int64_t beta_tok_stride, const float *A_log, const float *dt_bias, const float *h0,
-                         float *ht, void *o, const void *z, const void *norm_weight, float norm_eps,
+                         int64_t beta_tok_stride, const float *A_log, const float *dt_bias, const void *h0,
+                         void *ht, void *o, const void *z, const void *norm_weight, float norm_eps,
                          const int64_t *cu_seqlens, int64_t B, int64_t T, int64_t H, int64_t HV, int64_t K,
                          int64_t V, int64_t N, float scale, int io_dtype, int g_dtype, int beta_dtype, uint32_t flags,
                          void *stream) {
   GdnArgs a{};
   a.q = q; a.k = k; a.v = v; a.q_ts = q_tok_stride; a.k_ts = k_tok_stride; a.v_ts = v_tok_stride;
   a.g = g; a.beta = beta; a.g_ts = g_tok_stride; a.beta_ts = beta_tok_stride;
-  a.A_log = A_log; a.dt_bias = dt_bias; a.h0 = h0; a.ht = ht; a.o = o;
+  // a 16-bit state (YB_GDN_STATE_F16 / _BF16) travels through the float-typed
+  // fields untouched; the decode kernel reads them with the flagged type
+  a.A_log = A_log; a.dt_bias = dt_bias; a.h0 = static_cast<const float *>(h0); a.ht = static_cast<float *>(ht);
+  a.o = o;
   a.z = z; a.norm_w = norm_weight; a.norm_eps = norm_eps; a.cu_seqlens = cu_seqlens;
   a.B = B; a.T = T; a.H = H; a.HV = HV; a.K = K; a.V = V; a.N = N; a.scale = scale;
   a.io_dtype = io_dtype; a.g_dtype = g_dtype; a.beta_dtype = beta_dtype; a.flags = flags;
@@ -118,6 +123,8 @@ int yb_gdn_chunk_fwd(const void *q, const void *k, const void *v, int64_t q_tok_
   a.stream = static_cast<cudaStream_t>(stream);
   int rc = check_gdn(a, "gdn_chunk");
   if (rc) return rc;
+  if (flags & (YB_GDN_STATE_F16 | YB_GDN_STATE_BF16))
+    return set_error(YB_ERR_UNSUPPORTED, "gdn_chunk: 16-bit state storage is a decode feature (prefill keeps fp32)");
   const int64_t need = gdn_chunk_workspace_bytes(B, T, H, HV, K, V, N, io_dtype);
   if (need > 0 && (workspace == nullptr || workspace_bytes < need))
     return set_error(YB_ERR_WORKSPACE, "gdn_chunk: workspace of %lld bytes required", (long long)need);

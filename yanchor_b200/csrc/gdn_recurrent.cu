@@ -13,8 +13,14 @@
 //
 // Thread layout: the state tile is ROWS x COLS with COLS the contiguous axis
 // of the stored layout (V for [K,V], K for [V,K]).  Each thread owns 4
-// contiguous columns (one 16-byte vector) of RPT consecutive rows; a warp
-// covers whole 512-byte rows, so every state access is fully coalesced.
+// contiguous columns (one 16- or 8-byte vector) of RPT consecutive rows; a
+// warp covers whole rows, so every state access is fully coalesced.
+//
+// State storage: fp32, or bf16 / fp16 (the reference's reduced-precision
+// recurrent-state storage for decode, runtime/model/inference_kernels.py:
+// 437-457 and modeling_yanchor.py:733-750).  A 16-bit state is widened to
+// fp32 on load, all arithmetic is fp32, and it is rounded to nearest on the
+// final store — as fla's fused recurrent kernel does with a 16-bit h0 / ht.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -30,8 +36,8 @@ struct RecParams {
   int64_t g_ts, beta_ts;
   int g_dtype, beta_dtype;
   const float *A_log, *dt_bias;
-  const float *h0;
-  float *ht;
+  const void *h0;
+  void *ht;
   void *o;
   const void *z, *norm_w;
   float norm_eps;
@@ -48,7 +54,31 @@ __device__ __forceinline__ float load_scalar(const void *p, int64_t idx, int dty
   return __half2float(static_cast<const __half *>(p)[idx]);
 }
 
-template <typename TIO, int K, int V, bool TRANS, bool NORM>
+// four consecutive state values: streaming load / store in the storage type
+__device__ __forceinline__ void ld_state4(const float *src, float *x) {
+  const float4 v = __ldcs(reinterpret_cast<const float4 *>(src));
+  x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+}
+template <typename T16>
+__device__ __forceinline__ void ld_state4(const T16 *src, float *x) {
+  const uint2 v = __ldcs(reinterpret_cast<const uint2 *>(src));
+  const T16 *h = reinterpret_cast<const T16 *>(&v);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) x[j] = to_f(h[j]);
+}
+__device__ __forceinline__ void st_state4(float *dst, const float *x) {
+  __stcs(reinterpret_cast<float4 *>(dst), make_float4(x[0], x[1], x[2], x[3]));
+}
+template <typename T16>
+__device__ __forceinline__ void st_state4(T16 *dst, const float *x) {
+  uint2 v;
+  T16 *h = reinterpret_cast<T16 *>(&v);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) h[j] = from_f<T16>(x[j]);
+  __stcs(reinterpret_cast<uint2 *>(dst), v);
+}
+
+template <typename TIO, typename TS, int K, int V, bool TRANS, bool NORM>
 __global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(const RecParams p) {
   constexpr int ROWS = TRANS ? V : K;
   constexpr int COLS = TRANS ? K : V;
@@ -83,12 +113,9 @@ __global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(const RecParams
   const int64_t head = (int64_t(n) * p.HV + hv) * K * V;
   float s[RPT][4];
   if (p.h0) {
-    const float *src = p.h0 + head;
+    const TS *src = static_cast<const TS *>(p.h0) + head;
 #pragma unroll
-    for (int i = 0; i < RPT; ++i) {
-      float4 x = __ldcs(reinterpret_cast<const float4 *>(src + (rg * RPT + i) * COLS + c0));
-      s[i][0] = x.x; s[i][1] = x.y; s[i][2] = x.z; s[i][3] = x.w;
-    }
+    for (int i = 0; i < RPT; ++i) ld_state4(src + (rg * RPT + i) * COLS + c0, s[i]);
   } else {
 #pragma unroll
     for (int i = 0; i < RPT; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
@@ -250,28 +277,32 @@ __global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(const RecParams
   }
 
   if (p.ht) {
-    float *dst = p.ht + head;
+    TS *dst = static_cast<TS *>(p.ht) + head;
 #pragma unroll
-    for (int i = 0; i < RPT; ++i)
-      __stcs(reinterpret_cast<float4 *>(dst + (rg * RPT + i) * COLS + c0),
-             make_float4(s[i][0], s[i][1], s[i][2], s[i][3]));
+    for (int i = 0; i < RPT; ++i) st_state4(dst + (rg * RPT + i) * COLS + c0, s[i]);
   }
 }
 
-template <typename TIO, int K, int V>
+template <typename TIO, int K, int V, typename TS = float>
 int launch_kv(const GdnArgs &a, const RecParams &p) {
   const bool trans = a.flags & YB_GDN_TRANSPOSE_STATE;
   const bool norm = a.z != nullptr;
   dim3 grid(unsigned(a.N * a.HV));
-  if (!trans && !norm) gdn_recurrent_kernel<TIO, K, V, false, false><<<grid, kThreads, 0, a.stream>>>(p);
-  if (!trans && norm) gdn_recurrent_kernel<TIO, K, V, false, true><<<grid, kThreads, 0, a.stream>>>(p);
-  if (trans && !norm) gdn_recurrent_kernel<TIO, K, V, true, false><<<grid, kThreads, 0, a.stream>>>(p);
-  if (trans && norm) gdn_recurrent_kernel<TIO, K, V, true, true><<<grid, kThreads, 0, a.stream>>>(p);
+  if (!trans && !norm) gdn_recurrent_kernel<TIO, TS, K, V, false, false><<<grid, kThreads, 0, a.stream>>>(p);
+  if (!trans && norm) gdn_recurrent_kernel<TIO, TS, K, V, false, true><<<grid, kThreads, 0, a.stream>>>(p);
+  if (trans && !norm) gdn_recurrent_kernel<TIO, TS, K, V, true, false><<<grid, kThreads, 0, a.stream>>>(p);
+  if (trans && norm) gdn_recurrent_kernel<TIO, TS, K, V, true, true><<<grid, kThreads, 0, a.stream>>>(p);
   return check_launch("gdn_recurrent_kernel");
 }
 
 template <typename TIO>
 int launch_io(const GdnArgs &a, const RecParams &p) {
+  if (a.flags & (YB_GDN_STATE_F16 | YB_GDN_STATE_BF16)) {   // 16-bit state storage: the YANchor head shape
+    if (a.K != 128 || a.V != 128)
+      return set_error(YB_ERR_UNSUPPORTED, "gdn recurrent: 16-bit state storage is built for K = V = 128");
+    if (a.flags & YB_GDN_STATE_F16) return launch_kv<TIO, 128, 128, __half>(a, p);
+    return launch_kv<TIO, 128, 128, __nv_bfloat16>(a, p);
+  }
   if (a.K == 128 && a.V == 128) return launch_kv<TIO, 128, 128>(a, p);
   if (a.K == 64 && a.V == 64) return launch_kv<TIO, 64, 64>(a, p);
   if (a.K == 128 && a.V == 64) return launch_kv<TIO, 128, 64>(a, p);

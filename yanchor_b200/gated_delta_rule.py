@@ -96,7 +96,11 @@ def _common(q, k, v, g, beta, scale, initial_state, output_final_state, use_qk_l
         if tuple(initial_state.shape) != state_shape:
             raise ValueError(f'initial_state must have shape {state_shape}, got {tuple(initial_state.shape)}')
         h0 = initial_state
-        if h0.dtype != torch.float32 or not h0.is_contiguous() or h0.data_ptr() % 16:
+        half_state = h0.dtype in (torch.float16, torch.bfloat16)
+        if inplace and half_state and h0.is_contiguous() and h0.data_ptr() % 16 == 0:
+            # 16-bit state storage, updated in place in its own dtype
+            flags |= _lib.GDN_STATE_F16 if h0.dtype == torch.float16 else _lib.GDN_STATE_BF16
+        elif h0.dtype != torch.float32 or not h0.is_contiguous() or h0.data_ptr() % 16:
             h0 = h0.to(torch.float32).contiguous()
             if h0.data_ptr() % 16:
                 h0 = h0.clone()
@@ -121,10 +125,13 @@ def fused_recurrent_gated_delta_rule(q, k, v, g=None, gk=None, gv=None, beta=Non
     Extra keyword-only arguments: ``use_beta_sigmoid_in_kernel`` (beta holds
     logits); ``z`` / ``norm_weight`` / ``norm_eps`` to fuse the gated RMSNorm
     epilogue (``Qwen3_5RMSNormGated``) into the output; ``inplace`` to write
-    the final state into ``initial_state`` (when it is a contiguous float32
-    tensor) and return that tensor, as the reference's in-place decode
-    override does.  By default a new final-state tensor is returned, as fla
-    does.
+    the final state into ``initial_state`` (when it is a contiguous float32,
+    bfloat16 or float16 tensor) and return that tensor, as the reference's
+    in-place decode override does.  A 16-bit state stays 16-bit: it is the
+    reference's reduced-precision state storage (``fp16_non_anchor`` /
+    ``bf16_non_anchor``), widened to fp32 for the step and rounded to nearest
+    when stored.  By default a new float32 final-state tensor is returned, as
+    fla does.
     """
     if gk is not None or gv is not None:
         raise NotImplementedError('per-key / per-value decays (gk, gv) are not part of the YANchor path')
