@@ -94,6 +94,38 @@ int yb_gdn_recurrent_fwd(const void *q, const void *k, const void *v, int64_t q_
                          int io_dtype, int g_dtype, int beta_dtype, uint32_t flags, void *stream);
 
 /*
+ * Causal depthwise conv1d in front of the recurrence (the GDN layer's short
+ * convolution over the fused q/k/v projection):
+ *   y[t, c] = act(sum_{j < KS} weight[c, j] * x[t - (KS - 1) + j, c] + bias[c]),
+ * act = SiLU when silu != 0, fp32 arithmetic, one rounding to dtype.
+ * Activations are token-major with channels contiguous: x, out [B, T, C]
+ * (the memory of the reference's [B, C, T] transposed view), given by batch
+ * and token strides in elements.  State [B, C, W], W = KS (the cache's
+ * convention) or KS - 1 (`initial_states` of the causal-conv1d package);
+ * its last KS - 1 entries are the inputs before t = 0.  weight [C, KS] and
+ * bias [C] (or NULL) are fp32.  KS in {2, 3, 4}.
+ *
+ * yb_conv1d_update: one token (T = 1); the state is shifted left and the
+ * input appended, in place.  Replaces runtime/model/inference_kernels.py:
+ * 339-376 `triton_graph_safe_causal_conv1d_update` and modeling_yanchor.py:
+ * 349-353 `torch_causal_conv1d_update`.
+ *
+ * yb_conv1d_fwd: a segment of T tokens; inputs before it come from
+ * initial_state (NULL: zeros); final_state (NULL: not written, may alias
+ * initial_state) receives the last W inputs of [initial_state | x], zeros
+ * where there are none.  Replaces the prefill convolution of transformers
+ * qwen3_5 modeling_qwen3_5.py:462-480 (`causal_conv1d_fn` / `conv1d`).
+ */
+int yb_conv1d_update(const void *x, int64_t x_batch_stride, void *conv_state, int64_t state_batch_stride,
+                     int64_t state_width, const float *weight, const float *bias, void *out,
+                     int64_t out_batch_stride, int64_t B, int64_t C, int64_t KS, int silu, int dtype,
+                     void *stream);
+int yb_conv1d_fwd(const void *x, int64_t x_batch_stride, int64_t x_token_stride, const void *initial_state,
+                  void *final_state, int64_t state_batch_stride, int64_t state_width, const float *weight,
+                  const float *bias, void *out, int64_t out_batch_stride, int64_t out_token_stride, int64_t B,
+                  int64_t T, int64_t C, int64_t KS, int silu, int dtype, void *stream);
+
+/*
  * Chunked (64-token WY/UT transform) gated delta rule for prefill.
  * Replaces fla: ops/gated_delta_rule/chunk.py:365 `chunk_gated_delta_rule`
  * (bound at modeling_yanchor.py:397-405; the torch restatement is

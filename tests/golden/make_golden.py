@@ -17,6 +17,8 @@ Python) to a scratch directory, puts it and the reference root first on
   ``_decode`` with the torch backend (modeling_yanchor.py:22-313)
 * ``counter_uniform`` and ``sample_top_k_top_p_counter``
   (runtime/model/inference_kernels.py:24-88)
+* ``torch_causal_conv1d_update`` and the causal ``nn.Conv1d`` of the GDN
+  layer (modeling_yanchor.py:349-370)
 
 on seeded inputs and writes the inputs and outputs as ``.npz`` files next to
 this script.  The GPU box never needs the reference: tests only read the
@@ -247,6 +249,38 @@ def sequence_fixtures(my, torch, g):
     return out
 
 
+def conv_fixtures(my, torch):
+    """Causal depthwise conv1d: the decode update through the reference's
+    ``torch_causal_conv1d_update`` (modeling_yanchor.py:349-353), and
+    prefill segments through an ``nn.Conv1d`` built as the reference layer
+    builds it (modeling_yanchor.py:369-370) and applied as the qwen3_5
+    forward applies it (modeling_qwen3_5.py:462-480): fresh, with a cached
+    state prepended, and shorter than the kernel."""
+    import torch.nn.functional as F
+    g = torch.Generator().manual_seed(11)
+    B, C, KS = 3, 40, 4
+    w = torch.randn(C, KS, generator=g) * 0.5
+    out = {'conv_w': w}
+    x = torch.randn(B, C, 1, generator=g)
+    st = torch.randn(B, C, KS, generator=g)
+    st_after = st.clone()
+    y = my.torch_causal_conv1d_update(x, st_after, w, None, 'silu')
+    out.update(conv_upd_x=x, conv_upd_state=st, conv_upd_y=y, conv_upd_state_after=st_after)
+    layer = torch.nn.Conv1d(C, C, KS, groups=C, padding=KS - 1, bias=False)
+    with torch.no_grad():
+        layer.weight.copy_(w[:, None])
+        for name, T, cached in (('conv_pre', 11, False), ('conv_prec', 9, True), ('conv_pres', 2, False)):
+            xs = torch.randn(B, C, T, generator=g)
+            mixed = torch.cat([st, xs], -1) if cached else xs
+            new_state = F.pad(mixed, (KS - mixed.shape[-1], 0))
+            ys = F.silu(layer(mixed)[:, :, :mixed.shape[-1]])
+            if cached:
+                ys = ys[:, :, -T:]
+            out.update({f'{name}_x': xs, f'{name}_y': ys, f'{name}_state': new_state})
+    out['conv_prec_state_in'] = st
+    return out
+
+
 def sampling_fixtures(ik, torch):
     out = {}
     g = torch.Generator().manual_seed(4)
@@ -276,7 +310,7 @@ def main():
     import torch
     torch.manual_seed(0)
     for name, fn in (('gdn', lambda: gdn_fixtures(qwen, torch)), ('memory', lambda: memory_fixtures(my, torch)),
-                     ('sampling', lambda: sampling_fixtures(ik, torch))):
+                     ('sampling', lambda: sampling_fixtures(ik, torch)), ('conv', lambda: conv_fixtures(my, torch))):
         data = {k: (v.detach().cpu().numpy() if hasattr(v, 'detach') else np.asarray(v)) for k, v in fn().items()}
         path = os.path.join(HERE, f'{name}.npz')
         np.savez_compressed(path, **data)

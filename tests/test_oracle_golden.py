@@ -193,3 +193,21 @@ def test_sampler(golden):
         got = sampling.sample_top_k_top_p_counter(d['samp_scores'], d['samp_attempt'], d['samp_steps'], 77,
                                                   float(temp), int(tk), float(tp))
         np.testing.assert_array_equal(got, d[f'samp_out{i}'], err_msg=f'case {i}')
+
+
+# --------------------------------------------------------------- conv1d ------
+def test_conv_update(golden):
+    from oracle import conv
+    d = golden('conv')
+    y, st = conv.conv_update(d['conv_upd_x'], d['conv_upd_state'], d['conv_w'])
+    close(y, d['conv_upd_y'], 1e-5)
+    close(st, d['conv_upd_state_after'], 0.0)
+
+
+@pytest.mark.parametrize('name,cached', [('conv_pre', False), ('conv_prec', True), ('conv_pres', False)])
+def test_conv_prefill(golden, name, cached):
+    from oracle import conv
+    d = golden('conv')
+    y, st = conv.conv_fwd(d[f'{name}_x'], d['conv_w'], initial_state=d['conv_prec_state_in'] if cached else None)
+    close(y, d[f'{name}_y'], 1e-5)
+    close(st, d[f'{name}_state'], 0.0)

@@ -3,7 +3,9 @@
 Operators (all CUDA, via the C ABI library libyanchor_b200.so):
 
 * gated delta rule: ``chunk_gated_delta_rule`` (prefill),
-  ``fused_recurrent_gated_delta_rule`` (decode), ``gdn_gates``
+  ``fused_recurrent_gated_delta_rule`` (decode), ``gdn_gates``, and the
+  short convolution before it: ``causal_conv1d_update`` /
+  ``causal_conv1d_fn``
 * anchor memory: ``indexed_gqa`` (prefill read), ``committed_gqa`` (decode
   read), ``commit_decode`` (decode write), ``select_topk`` / ``merge_topk`` /
   ``exclusive_prefix_topk`` (top-CAP selection) and ``sequence`` (the
@@ -14,6 +16,7 @@ Operators (all CUDA, via the C ABI library libyanchor_b200.so):
   put them where the reference model code looks them up.
 """
 from .gated_delta_rule import chunk_gated_delta_rule, fused_recurrent_gated_delta_rule, gdn_gates  # noqa: F401
+from .conv import causal_conv1d_fn, causal_conv1d_update  # noqa: F401
 from .independent_memory import MemoryState, commit_decode, committed_gqa, indexed_gqa  # noqa: F401
 from .memory_prefill import exclusive_prefix_topk, merge_topk, select_topk, sequence  # noqa: F401
 from .sampling import apply_dense_presence_penalty_, greedy, sample_top_k_top_p_counter  # noqa: F401

@@ -3,7 +3,8 @@
 * ``bind_gdn_kernels(model)`` sets ``chunk_gated_delta_rule`` and
   ``recurrent_gated_delta_rule`` on every module that has them (the
   ``Qwen3_5GatedDeltaNet`` layers), as ``bind_native_qwen_gdn_kernels`` does
-  for fla (``modeling_yanchor.py:392-410``).  With ``inplace_decode`` the
+  for fla (``modeling_yanchor.py:392-410``), and their
+  ``causal_conv1d_update`` / ``causal_conv1d_fn``.  With ``inplace_decode`` the
   recurrent operator updates the cached state in place, as the reference's
   decode override (``runtime/model/inference_kernels.py:147-184``).
 * ``install_memory_module()`` makes ``importlib.import_module(
@@ -20,20 +21,24 @@ import functools
 import sys
 import types
 
-from . import gated_delta_rule, independent_memory, memory_prefill
+from . import conv as conv1d, gated_delta_rule, independent_memory, memory_prefill
 
 
-def bind_gdn_kernels(model, *, inplace_decode: bool = True) -> dict:
+def bind_gdn_kernels(model, *, inplace_decode: bool = True, conv: bool = True) -> dict:
     recurrent = functools.partial(gated_delta_rule.fused_recurrent_gated_delta_rule, inplace=inplace_decode)
     names = []
     for name, module in model.named_modules():
         if hasattr(module, 'chunk_gated_delta_rule') and hasattr(module, 'recurrent_gated_delta_rule'):
             module.chunk_gated_delta_rule = gated_delta_rule.chunk_gated_delta_rule
             module.recurrent_gated_delta_rule = recurrent
+            if conv and hasattr(module, 'causal_conv1d_update'):
+                # the layer's short convolution (transformers qwen3_5 modeling_qwen3_5.py:453-476)
+                module.causal_conv1d_update = conv1d.causal_conv1d_update
+                module.causal_conv1d_fn = conv1d.causal_conv1d_fn
             names.append(name)
     if not names:
         raise RuntimeError('no GDN layers were found')
-    return {'backend': 'yanchor_b200', 'native_gdn_layers': names, 'inplace_decode': inplace_decode}
+    return {'backend': 'yanchor_b200', 'native_gdn_layers': names, 'inplace_decode': inplace_decode, 'conv': conv}
 
 
 def install_memory_module() -> types.ModuleType:

@@ -1,0 +1,136 @@
+// Causal depthwise conv1d in front of the GDN recurrence (the short
+// convolution over the fused q/k/v projection), decode update and prefill.
+//
+//   y[t, c] = act(sum_{j < KS} w[c, j] * x[t - (KS - 1) + j, c] + bias[c])
+//
+// with inputs before the segment taken from the conv state (zeros without
+// one).  Decode: runtime/model/inference_kernels.py:339-355 (the graph-safe
+// Triton update: fp32 arithmetic, one rounding, state shifted left and the
+// new input appended) and modeling_yanchor.py:349-353.  Prefill: transformers
+// qwen3_5 modeling_qwen3_5.py:462-480 (the cached state prepended, the new
+// state = the last inputs, zero-padded on the left).
+//
+// Layout: activations token-major with channels contiguous ([B, T, C], the
+// memory behind the reference's [B, C, T] transposed view); state [B, C, W]
+// with W = KS (the cache's convention) or KS - 1 (the causal-conv1d
+// package's `initial_states`), only its last KS - 1 entries feed outputs.
+// One thread per channel: a warp reads 32 consecutive channels of a token.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace yb {
+namespace {
+
+constexpr int kConvThreads = 128;
+constexpr int kConvTile = 32;   // tokens per thread in prefill
+
+__device__ __forceinline__ float conv_act(float y, bool silu) { return silu ? y * sigmoidf_(y) : y; }
+
+template <typename T, int KS>
+__global__ void __launch_bounds__(kConvThreads) conv_update_kernel(const ConvArgs a) {
+  const int64_t b = blockIdx.y;
+  const int64_t c = int64_t(blockIdx.x) * kConvThreads + threadIdx.x;
+  if (c >= a.C) return;
+  const T *x = static_cast<const T *>(a.x) + b * a.x_bs;
+  T *st = static_cast<T *>(a.state) + b * a.state_bs + c * a.W;
+  float win[KS];
+#pragma unroll
+  for (int j = 0; j < KS - 1; ++j) win[j] = to_f(st[a.W - (KS - 1) + j]);
+  const T xin = x[c];
+  win[KS - 1] = to_f(xin);
+  float y = a.bias ? a.bias[c] : 0.f;
+#pragma unroll
+  for (int j = 0; j < KS; ++j) y = fmaf(a.weight[c * KS + j], win[j], y);
+  // shift the state left by one and append the input (stored values are inputs: no rounding)
+  for (int j = 0; j + 1 < a.W; ++j) st[j] = st[j + 1];
+  st[a.W - 1] = xin;
+  static_cast<T *>(a.out)[b * a.out_bs + c] = from_f<T>(conv_act(y, a.silu));
+}
+
+template <typename T, int KS>
+__global__ void __launch_bounds__(kConvThreads) conv_fwd_kernel(const ConvArgs a) {
+  const int64_t b = blockIdx.z;
+  const int64_t c = int64_t(blockIdx.x) * kConvThreads + threadIdx.x;
+  const int64_t t0 = int64_t(blockIdx.y) * kConvTile;
+  if (c >= a.C) return;
+  const T *x = static_cast<const T *>(a.x) + b * a.x_bs + c;
+  const T *st_in = a.state_in ? static_cast<const T *>(a.state_in) + b * a.state_bs + c * a.W : nullptr;
+  float w[KS];
+#pragma unroll
+  for (int j = 0; j < KS; ++j) w[j] = a.weight[c * KS + j];
+  const float bias = a.bias ? a.bias[c] : 0.f;
+  // the KS - 1 inputs before t0
+  auto input = [&](int64_t t) -> float {
+    if (t >= 0) return to_f(x[t * a.x_ts]);
+    const int64_t back = -t;   // 1 .. KS - 1 (or more, before the state: zero)
+    if (st_in && back <= a.W) return to_f(st_in[a.W - back]);
+    return 0.f;
+  };
+  float win[KS];
+#pragma unroll
+  for (int j = 0; j < KS - 1; ++j) win[j] = input(t0 - (KS - 1) + j);
+  const int64_t t1 = t0 + kConvTile < a.T ? t0 + kConvTile : a.T;
+  T *out = static_cast<T *>(a.out) + b * a.out_bs + c;
+  for (int64_t t = t0; t < t1; ++t) {
+    win[KS - 1] = to_f(x[t * a.x_ts]);
+    float y = bias;
+#pragma unroll
+    for (int j = 0; j < KS; ++j) y = fmaf(w[j], win[j], y);
+    out[t * a.out_ts] = from_f<T>(conv_act(y, a.silu));
+#pragma unroll
+    for (int j = 0; j < KS - 1; ++j) win[j] = win[j + 1];
+  }
+  // final state: the last W inputs of [state | x] (zeros before both); tile 0
+  // is the only reader of the initial state, so the two may alias
+  if (blockIdx.y == 0 && a.state_out) {
+    T *so = static_cast<T *>(a.state_out) + b * a.state_bs + c * a.W;
+    T vals[8];
+    for (int j = 0; j < a.W; ++j) {
+      const int64_t t = a.T - a.W + j;
+      if (t >= 0) vals[j] = x[t * a.x_ts];
+      else if (st_in && -t <= a.W) vals[j] = st_in[a.W + t];
+      else vals[j] = from_f<T>(0.f);
+    }
+    for (int j = 0; j < a.W; ++j) so[j] = vals[j];
+  }
+}
+
+template <typename T>
+int conv_dispatch(const ConvArgs &a, bool update) {
+  switch (a.KS) {
+#define YB_CONV_CASE(K)                                                                                 \
+  case K:                                                                                               \
+    if (update) {                                                                                       \
+      conv_update_kernel<T, K><<<dim3(unsigned((a.C + kConvThreads - 1) / kConvThreads), unsigned(a.B)), \
+                                 kConvThreads, 0, a.stream>>>(a);                                       \
+      return check_launch("conv_update_kernel");                                                        \
+    }                                                                                                   \
+    conv_fwd_kernel<T, K><<<dim3(unsigned((a.C + kConvThreads - 1) / kConvThreads),                     \
+                                 unsigned((a.T + kConvTile - 1) / kConvTile), unsigned(a.B)),           \
+                            kConvThreads, 0, a.stream>>>(a);                                            \
+    return check_launch("conv_fwd_kernel");
+    YB_CONV_CASE(2)
+    YB_CONV_CASE(3)
+    YB_CONV_CASE(4)
+#undef YB_CONV_CASE
+  }
+  return set_error(YB_ERR_UNSUPPORTED, "conv1d: kernel width %lld not built (2, 3, 4)", (long long)a.KS);
+}
+
+}  // namespace
+
+int launch_conv1d(const ConvArgs &a, bool update) {
+  if (a.B == 0 || a.C == 0 || (!update && a.T == 0 && !a.state_out)) return YB_OK;
+  if (!update && a.T == 0) {
+    // nothing to convolve; the state is unchanged
+    return YB_OK;
+  }
+  switch (a.dtype) {
+    case YB_F32: return conv_dispatch<float>(a, update);
+    case YB_BF16: return conv_dispatch<__nv_bfloat16>(a, update);
+    case YB_F16: return conv_dispatch<__half>(a, update);
+  }
+  return set_error(YB_ERR_ARGUMENT, "conv1d: bad dtype %d", a.dtype);
+}
+
+}  // namespace yb

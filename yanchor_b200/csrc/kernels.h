@@ -114,6 +114,23 @@ struct PrefixTopkArgs {
 };
 int launch_exclusive_prefix_topk(const PrefixTopkArgs &a);
 
+struct ConvArgs {
+  const void *x;
+  int64_t x_bs, x_ts;             // batch / token strides (elements); channels contiguous
+  void *state;                    // update: [B, C, W], in place
+  const void *state_in;           // prefill: optional initial state
+  void *state_out;                // prefill: optional final state (may alias state_in)
+  int64_t state_bs, W;            // state batch stride (elements), width (KS or KS - 1)
+  const float *weight, *bias;     // [C, KS] fp32, [C] fp32 or null
+  void *out;
+  int64_t out_bs, out_ts;
+  int64_t B, T, C, KS;
+  bool silu;
+  int dtype;
+  cudaStream_t stream;
+};
+int launch_conv1d(const ConvArgs &a, bool update);
+
 struct SampleArgs {
   const void *scores;
   int64_t row_stride, B, vocab;
