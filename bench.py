@@ -45,6 +45,7 @@ METRIC = 'decode tok/s/GPU at B=64, 32K gen; chunked-prefill tok/s; % of rooflin
 # defaults: 32 layers, every 4th is SWA + anchor memory)
 L_GDN, L_MEM = 24, 8
 H_K, H_V, DK, DV = 16, 32, 128, 128
+CONV_C, CONV_KS = 2 * H_K * DK + H_V * DV, 4     # the short convolution over the fused q/k/v projection
 MEM_G, MEM_H, MEM_D, MEM_CAP, MEM_CHUNK = 4, 16, 256, 64, 64
 VOCAB = 248320
 
@@ -142,6 +143,8 @@ def build_decode(torch, yb, B, device, n_inputs=4, seed=0, state_dtype=None):
     for _ in range(L_GDN):
         layers.append(dict(state=(0.02 * torch.randn(B, H_V, DK, DV, generator=gen, device=device)).to(
                                state_dtype or torch.float32),
+                           conv_state=rnd(B, CONV_C, CONV_KS),
+                           conv_w=torch.randn(CONV_C, CONV_KS, generator=gen, device=device) * 0.5,
                            A_log=torch.empty(H_V, device=device).uniform_(1, 16, generator=gen).log(),
                            dt_bias=torch.ones(H_V, device=device),
                            norm_w=rnd(DV, scale=0.1) + 1.0))
@@ -149,7 +152,7 @@ def build_decode(torch, yb, B, device, n_inputs=4, seed=0, state_dtype=None):
     inputs = []
     for _ in range(n_inputs):
         inputs.append(dict(
-            q=rnd(L_GDN, B, 1, H_K, DK), k=rnd(L_GDN, B, 1, H_K, DK), v=rnd(L_GDN, B, 1, H_V, DV),
+            mixed=rnd(L_GDN, B, 1, CONV_C),
             z=rnd(L_GDN, B, 1, H_V, DV), a=rnd(L_GDN, B, 1, H_V), b=rnd(L_GDN, B, 1, H_V),
             mq=rnd(L_MEM, B, 1, MEM_H, MEM_D), mk=rnd(L_MEM, B, 1, MEM_G, MEM_D), mv=rnd(L_MEM, B, 1, MEM_G, MEM_D),
             ms=rnd(L_MEM, B, 1, MEM_G, dtype=torch.float32), logits=rnd(B, VOCAB, scale=3.0)))
@@ -158,11 +161,22 @@ def build_decode(torch, yb, B, device, n_inputs=4, seed=0, state_dtype=None):
     return layers, mems, inputs, active, ws
 
 
+def conv_qkv(yb, L, mixed):
+    """The layer's short convolution (in place on its conv state), then q, k, v
+    as views of its output, as the reference layer splits them."""
+    mix = yb.causal_conv1d_update(mixed.transpose(1, 2), L['conv_state'], L['conv_w'], None, 'silu').transpose(1, 2)
+    q = mix[..., :H_K * DK].unflatten(-1, (H_K, DK))
+    k = mix[..., H_K * DK:2 * H_K * DK].unflatten(-1, (H_K, DK))
+    v = mix[..., 2 * H_K * DK:].unflatten(-1, (H_V, DV))
+    return q, k, v
+
+
 def decode_step(yb, layers, mems, x, active, ws):
     """One decode step of the hot path; returns the sampled token ids."""
     for i, L in enumerate(layers):
+        q, k, v = conv_qkv(yb, L, x['mixed'][i])
         yb.fused_recurrent_gated_delta_rule(
-            x['q'][i], x['k'][i], x['v'][i], g=x['a'][i], beta=x['b'][i], initial_state=L['state'],
+            q, k, v, g=x['a'][i], beta=x['b'][i], initial_state=L['state'],
             output_final_state=True, use_qk_l2norm_in_kernel=True, use_gate_in_kernel=True, A_log=L['A_log'],
             dt_bias=L['dt_bias'], use_beta_sigmoid_in_kernel=True, z=x['z'][i], norm_weight=L['norm_w'],
             inplace=True)
@@ -172,7 +186,7 @@ def decode_step(yb, layers, mems, x, active, ws):
     return yb.greedy(x['logits'], workspace=ws)
 
 
-LAUNCHES_PER_STEP = L_GDN + 2 * L_MEM + 2
+LAUNCHES_PER_STEP = 2 * L_GDN + 2 * L_MEM + 2     # conv + GDN per GDN layer, read + commit, greedy (2)
 
 
 def gdn_bytes_per_launch(B, state_bytes=4):
@@ -195,8 +209,9 @@ def time_events(torch, fn, iters, stream):
 def decode_config(B, world):
     """The workload both arms report (the reference arm runs the same step on the host)."""
     return {
-        'workload': 'decode hot path (config 3 shape): 24 GDN layers + 8 anchor-memory layers + greedy '
-                    'sampler, one token per sequence per step, CUDA-graph replay',
+        'workload': 'decode hot path (config 3 shape): 24 GDN layers (short conv update + fused recurrence) + '
+                    '8 anchor-memory layers + greedy sampler, one token per sequence per step, CUDA-graph replay',
+        'conv': {'channels': CONV_C, 'kernel': CONV_KS, 'state': 'bf16, in place'},
         'batch_per_gpu': B, 'global_batch': B * world,
         'gdn': {'layers': L_GDN, 'H': H_K, 'HV': H_V, 'K': DK, 'V': DV, 'state': 'fp32, in place'},
         'memory': {'layers': L_MEM, 'G': MEM_G, 'H': MEM_H, 'D': MEM_D, 'CAP': MEM_CAP, 'chunk': MEM_CHUNK},
@@ -257,10 +272,11 @@ def run_gpu(args, rank, world, local_rank, dist):
     # ---- dominant kernel alone: GDN recurrent update, CUDA events on its stream ----
     x0 = inputs[0]
     L0 = layers[0]
+    q0, k0, v0 = conv_qkv(yb, L0, x0['mixed'][0])
 
     def one_gdn():
         yb.fused_recurrent_gated_delta_rule(
-            x0['q'][0], x0['k'][0], x0['v'][0], g=x0['a'][0], beta=x0['b'][0], initial_state=L0['state'],
+            q0, k0, v0, g=x0['a'][0], beta=x0['b'][0], initial_state=L0['state'],
             output_final_state=True, use_qk_l2norm_in_kernel=True, use_gate_in_kernel=True, A_log=L0['A_log'],
             dt_bias=L0['dt_bias'], use_beta_sigmoid_in_kernel=True, z=x0['z'][0], norm_weight=L0['norm_w'],
             inplace=True)
@@ -350,10 +366,11 @@ def run_gpu(args, rank, world, local_rank, dist):
         g16.replay()
     ms16 = time_events(torch, g16.replay, max(3, args.steps // 2), stream)
     L16 = layers16[0]
+    q16, k16, v16 = conv_qkv(yb, L16, inputs16[0]['mixed'][0])
 
     def one_gdn16():
         yb.fused_recurrent_gated_delta_rule(
-            inputs16[0]['q'][0], inputs16[0]['k'][0], inputs16[0]['v'][0], g=inputs16[0]['a'][0],
+            q16, k16, v16, g=inputs16[0]['a'][0],
             beta=inputs16[0]['b'][0], initial_state=L16['state'], output_final_state=True,
             use_qk_l2norm_in_kernel=True, use_gate_in_kernel=True, A_log=L16['A_log'], dt_bias=L16['dt_bias'],
             use_beta_sigmoid_in_kernel=True, z=inputs16[0]['z'][0], norm_weight=L16['norm_w'], inplace=True)
@@ -516,9 +533,11 @@ def run_only(args):
             yb.sequence(mq, msc, writer, None, MEM_CHUNK, st)
         fn = (lambda: yb.exclusive_prefix_topk(psc, ppos, ppos, 64)) if args.only == 'mem_topk' else seq
     else:
+        q0, k0, v0 = conv_qkv(yb, L0, x['mixed'][0])
         fns = {
+            'conv_update': lambda: conv_qkv(yb, L0, x['mixed'][0]),
             'gdn_decode': lambda: yb.fused_recurrent_gated_delta_rule(
-                x['q'][0], x['k'][0], x['v'][0], g=x['a'][0], beta=x['b'][0], initial_state=L0['state'],
+                q0, k0, v0, g=x['a'][0], beta=x['b'][0], initial_state=L0['state'],
                 output_final_state=True, use_qk_l2norm_in_kernel=True, use_gate_in_kernel=True,
                 A_log=L0['A_log'], dt_bias=L0['dt_bias'], use_beta_sigmoid_in_kernel=True, z=x['z'][0],
                 norm_weight=L0['norm_w'], inplace=True),
@@ -538,18 +557,23 @@ def run_only(args):
 # ------------------------------------------------------------- CPU arm ------
 def cpu_decode_sample(steps=2, B=64, seed=0):
     """Time the numpy restatement of the same decode step on the host."""
-    from oracle import gdn as ogdn, memory as omem, sampling as osamp
+    from oracle import conv as oconv, gdn as ogdn, memory as omem, sampling as osamp
     rng = np.random.default_rng(seed)
     f32 = np.float32
     states = [(0.02 * rng.standard_normal((B, H_V, DK, DV))).astype(f32) for _ in range(L_GDN)]
+    conv_states = [rng.standard_normal((B, CONV_C, CONV_KS)).astype(f32) for _ in range(L_GDN)]
+    conv_w = (rng.standard_normal((CONV_C, CONV_KS)) * 0.5).astype(f32)
     A_log = np.log(rng.uniform(1, 16, H_V)).astype(f32)
     mem = [omem.empty_state(B, MEM_G, MEM_CAP, MEM_CHUNK, MEM_D) for _ in range(L_MEM)]
     t0 = time.perf_counter()
     for _ in range(steps):
         for i in range(L_GDN):
-            q = rng.standard_normal((B, 1, H_K, DK)).astype(f32)
-            k = rng.standard_normal((B, 1, H_K, DK)).astype(f32)
-            v = rng.standard_normal((B, 1, H_V, DV)).astype(f32)
+            mixed = rng.standard_normal((B, CONV_C, 1)).astype(f32)
+            y, conv_states[i] = oconv.conv_update(mixed, conv_states[i], conv_w)
+            y = y[:, :, 0].astype(f32)
+            q = y[:, None, :H_K * DK].reshape(B, 1, H_K, DK)
+            k = y[:, None, H_K * DK:2 * H_K * DK].reshape(B, 1, H_K, DK)
+            v = y[:, None, 2 * H_K * DK:].reshape(B, 1, H_V, DV)
             a = rng.standard_normal((B, 1, H_V)).astype(f32)
             b = rng.standard_normal((B, 1, H_V)).astype(f32)
             z = rng.standard_normal((B, 1, H_V, DV)).astype(f32)
@@ -608,7 +632,7 @@ def main():
     ap.add_argument('--impl', default='yanchor_b200', choices=['yanchor_b200', 'reference'])
     ap.add_argument('--no-prefill', action='store_true')
     ap.add_argument('--no-cpu', action='store_true')
-    ap.add_argument('--only', choices=['gdn_decode', 'gdn_chunk', 'mem_read', 'mem_commit', 'mem_indexed', 'mem_topk',
+    ap.add_argument('--only', choices=['conv_update', 'gdn_decode', 'gdn_chunk', 'mem_read', 'mem_commit', 'mem_indexed', 'mem_topk',
                                        'mem_sequence', 'greedy',
                                        'topk'], help='run one kernel family (small ncu captures)')
     ap.add_argument('--prefill-batch', type=int, default=8)

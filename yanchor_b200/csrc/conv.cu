@@ -15,6 +15,8 @@
 // with W = KS (the cache's convention) or KS - 1 (the causal-conv1d
 // package's `initial_states`), only its last KS - 1 entries feed outputs.
 // One thread per channel: a warp reads 32 consecutive channels of a token.
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -33,6 +35,30 @@ __global__ void __launch_bounds__(kConvThreads) conv_update_kernel(const ConvArg
   if (c >= a.C) return;
   const T *x = static_cast<const T *>(a.x) + b * a.x_bs;
   T *st = static_cast<T *>(a.state) + b * a.state_bs + c * a.W;
+  if constexpr (KS == 4) {
+    // the common case (width-4 cache state): the channel's state and weights
+    // move as single vectors
+    using V = typename std::conditional<sizeof(T) == 4, float4, uint2>::type;
+    if (a.W == 4 && (reinterpret_cast<uintptr_t>(st) % sizeof(V)) == 0 &&
+        (reinterpret_cast<uintptr_t>(a.weight + c * 4) % 16) == 0) {
+      V sv = *reinterpret_cast<const V *>(st);
+      T *h = reinterpret_cast<T *>(&sv);
+      const T xin = x[c];
+      const float4 w4 = *reinterpret_cast<const float4 *>(a.weight + c * 4);
+      float y = a.bias ? a.bias[c] : 0.f;
+      y = fmaf(w4.x, to_f(h[1]), y);
+      y = fmaf(w4.y, to_f(h[2]), y);
+      y = fmaf(w4.z, to_f(h[3]), y);
+      y = fmaf(w4.w, to_f(xin), y);
+      h[0] = h[1];
+      h[1] = h[2];
+      h[2] = h[3];
+      h[3] = xin;
+      *reinterpret_cast<V *>(st) = sv;
+      static_cast<T *>(a.out)[b * a.out_bs + c] = from_f<T>(conv_act(y, a.silu));
+      return;
+    }
+  }
   float win[KS];
 #pragma unroll
   for (int j = 0; j < KS - 1; ++j) win[j] = to_f(st[a.W - (KS - 1) + j]);
