@@ -129,3 +129,34 @@ def test_indexed_read_bf16_yanchor_shape(yb, kb):
     ref = omem.indexed_gqa(host(qb), host(kb_), host(vb), refs)
     assert np.abs(host(out) - ref).max() <= 2e-2
     assert not host(out)[1, 2, :, 12:16].any()      # no anchors: only the null slot
+
+
+def test_vllm_page_pool_decode(yb):
+    """The decode read + commit on a pool of vLLM memory pages (views, no
+    copies) with state indices (one request skipped) equal the oracle."""
+    from yanchor_b200 import independent_memory as im
+    rng = np.random.default_rng(8)
+    B, H, G, D, CAP, CH, P, steps = 4, 16, 4, 256, 64, 64, 6, 70
+    vs, ms = im.vllm_page_shapes(G, CAP, CH, D)
+    values = torch.empty((P,) + vs, device='cuda', dtype=torch.bfloat16)
+    meta = torch.empty((P,) + ms, device='cuda')
+    st = im.state_from_vllm_page(values, meta, G, CAP, CH, D)
+    im.reset_vllm_page_(st)
+    idx = np.array([3, 0, -1, 5], np.int64)
+    pool_np = omem.empty_state(P, G, CAP, CH, D)
+    for t in range(steps):
+        q = rng.standard_normal((B, 1, H, D)).astype(np.float32)
+        k = rng.standard_normal((B, 1, G, D)).astype(np.float32)
+        v = rng.standard_normal((B, 1, G, D)).astype(np.float32)
+        sc = (rng.standard_normal((B, 1, G)) * 2).round().astype(np.float32) / 2
+        act = rng.random(B) > 0.1
+        bf = torch.bfloat16
+        qb, kb, vb = cuda(q, bf), cuda(k, bf), cuda(v, bf)
+        r = yb.committed_gqa(qb, st, cuda(idx))
+        er = omem.decode_read(host(qb), pool_np['keys'], pool_np['values'], pool_np['positions'], idx)
+        assert np.abs(host(r) - er).max() <= 2e-2
+        yb.commit_decode(kb, vb, cuda(sc), cuda(act), CH, st, cuda(idx))
+        omem.commit_decode(host(kb), host(vb), sc, act, CH, pool_np, idx)
+    for f in FIELDS:
+        np.testing.assert_array_equal(host(getattr(st, f)), pool_np[f].astype(host(getattr(st, f)).dtype),
+                                      err_msg=f)

@@ -58,6 +58,54 @@ class MemoryState:
                    torch.zeros(batch, device=device, dtype=torch.int64))
 
 
+def vllm_page_shapes(groups, capacity, chunk, dim):
+    """Per-slot shapes of the vLLM plugin's memory page: (values, meta)
+    (vllm_yanchor.py:19-22).  values hold keys, values, pending keys and
+    pending values in the model dtype; meta holds float32 scores, int32
+    positions, float32 pending scores and int64 count / total."""
+    return (2 * groups * (capacity + chunk) * dim,), (groups * (2 * capacity + chunk) + 4,)
+
+
+def state_from_vllm_page(values, meta, groups, capacity, chunk, dim):
+    """A ``MemoryState`` of views into a pool of vLLM memory pages
+    ``values [P, 2*G*(CAP+chunk)*D]`` and ``meta [P, G*(2*CAP+chunk)+4]``
+    float32, laid out as the plugin's ``YANchorMemory.state``
+    (vllm_yanchor.py:47-62): no copy — every operator here reads and writes
+    the pages in place (each field is batch-strided by the page size), and
+    ``indices`` pick the page of each request."""
+    P = values.shape[0]
+    if tuple(values.shape[1:]) != vllm_page_shapes(groups, capacity, chunk, dim)[0] or \
+            tuple(meta.shape[1:]) != vllm_page_shapes(groups, capacity, chunk, dim)[1] or meta.shape[0] != P:
+        raise ValueError('pages do not match the memory shape')
+    if meta.dtype != torch.float32:
+        raise TypeError('the meta page is float32')
+    fields, off = [], 0
+    for width in (capacity, capacity, chunk, chunk):
+        size = groups * width * dim
+        fields.append(values[:, off:off + size].view(P, groups, width, dim))
+        off += size
+    w = groups * capacity
+    scores = meta[:, :w].view(P, groups, capacity)
+    positions = meta[:, w:2 * w].view(torch.int32).view(P, groups, capacity)
+    pending_scores = meta[:, 2 * w:-4].view(P, groups, chunk)
+    count = meta[:, -4:-2].view(torch.int64).squeeze(-1)
+    total = meta[:, -2:].view(torch.int64).squeeze(-1)
+    return MemoryState(fields[0], fields[1], scores, positions, fields[2], fields[3], pending_scores, count, total)
+
+
+def reset_vllm_page_(state, pages=None):
+    """Empty the given pages (all when None), as ``IndependentMemoryState.reset_``
+    (modeling_yanchor.py:110-118) does for a state."""
+    for name in ('keys', 'values', 'scores', 'positions', 'pending_keys', 'pending_values', 'pending_scores',
+                 'count', 'total'):
+        t = getattr(state, name)
+        fill = float('-inf') if 'scores' in name else -1 if name == 'positions' else 0
+        if pages is None:
+            t.fill_(fill)
+        else:
+            t.index_fill_(0, pages.to(t.device), fill)
+
+
 def _inner_contiguous(t: torch.Tensor, ndim_inner: int) -> bool:
     expected = 1
     for d in range(t.dim() - 1, t.dim() - 1 - ndim_inner, -1):
