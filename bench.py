@@ -171,9 +171,19 @@ def conv_qkv(yb, L, mixed):
     return q, k, v
 
 
-def decode_step(yb, layers, mems, x, active, ws):
+def gdn_layer(yb, L, x, i):
+    """One GDN layer's decode core in one launch: conv update, gates, L2 norm,
+    recurrence (state in place), gated RMSNorm."""
+    return yb.fused_gdn_decode(x['mixed'][i], x['z'][i], x['a'][i], x['b'][i], L['conv_state'], L['conv_w'], None,
+                               L['state'], L['A_log'], L['dt_bias'], L['norm_w'], num_k_heads=H_K)
+
+
+def decode_step(yb, layers, mems, x, active, ws, fused=False):
     """One decode step of the hot path; returns the sampled token ids."""
     for i, L in enumerate(layers):
+        if fused:
+            gdn_layer(yb, L, x, i)
+            continue
         q, k, v = conv_qkv(yb, L, x['mixed'][i])
         yb.fused_recurrent_gated_delta_rule(
             q, k, v, g=x['a'][i], beta=x['b'][i], initial_state=L['state'],
@@ -186,10 +196,11 @@ def decode_step(yb, layers, mems, x, active, ws):
     return yb.greedy(x['logits'], workspace=ws)
 
 
-LAUNCHES_PER_STEP = 2 * L_GDN + 2 * L_MEM + 2     # conv + GDN per GDN layer, read + commit, greedy (2)
+LAUNCHES_PER_STEP = 2 * L_GDN + 2 * L_MEM + 2     # conv + recurrence per GDN layer, read + commit, greedy (2)
 
 
 def gdn_bytes_per_launch(B, state_bytes=4):
+    """Algorithmic HBM bytes of one recurrence launch (after the conv)."""
     state = B * H_V * DK * DV * state_bytes * 2            # state read + write (fp32, or a 16-bit storage)
     acts = B * (2 * H_K * DK + 3 * H_V * DV) * 2 + B * H_V * 2 * 2   # q, k, v, z, o (bf16) + a, b
     return state + acts
@@ -209,8 +220,9 @@ def time_events(torch, fn, iters, stream):
 def decode_config(B, world):
     """The workload both arms report (the reference arm runs the same step on the host)."""
     return {
-        'workload': 'decode hot path (config 3 shape): 24 GDN layers (short conv update + fused recurrence) + '
-                    '8 anchor-memory layers + greedy sampler, one token per sequence per step, CUDA-graph replay',
+        'workload': 'decode hot path (config 3 shape): 24 GDN layers (short conv update, then the recurrence with '
+                    'gates, L2 norm and gated RMSNorm) + 8 anchor-memory layers + greedy sampler, one token per '
+                    'sequence per step, CUDA-graph replay',
         'conv': {'channels': CONV_C, 'kernel': CONV_KS, 'state': 'bf16, in place'},
         'batch_per_gpu': B, 'global_batch': B * world,
         'gdn': {'layers': L_GDN, 'H': H_K, 'HV': H_V, 'K': DK, 'V': DV, 'state': 'fp32, in place'},
@@ -269,7 +281,7 @@ def run_gpu(args, rank, world, local_rank, dist):
         ms = shard.max_over_ranks(ms, device=device)
     value = world * B / (ms / 1e3)
 
-    # ---- dominant kernel alone: GDN recurrent update, CUDA events on its stream ----
+    # ---- dominant kernel alone: the recurrence, CUDA events on its stream ----
     x0 = inputs[0]
     L0 = layers[0]
     q0, k0, v0 = conv_qkv(yb, L0, x0['mixed'][0])
@@ -536,6 +548,9 @@ def run_only(args):
         q0, k0, v0 = conv_qkv(yb, L0, x['mixed'][0])
         fns = {
             'conv_update': lambda: conv_qkv(yb, L0, x['mixed'][0]),
+            'gdn_fused': lambda: yb.fused_gdn_decode(x['mixed'][0], x['z'][0], x['a'][0], x['b'][0], L0['conv_state'],
+                                                     L0['conv_w'], None, L0['state'], L0['A_log'], L0['dt_bias'],
+                                                     L0['norm_w'], num_k_heads=H_K),
             'gdn_decode': lambda: yb.fused_recurrent_gated_delta_rule(
                 q0, k0, v0, g=x['a'][0], beta=x['b'][0], initial_state=L0['state'],
                 output_final_state=True, use_qk_l2norm_in_kernel=True, use_gate_in_kernel=True,
@@ -632,7 +647,7 @@ def main():
     ap.add_argument('--impl', default='yanchor_b200', choices=['yanchor_b200', 'reference'])
     ap.add_argument('--no-prefill', action='store_true')
     ap.add_argument('--no-cpu', action='store_true')
-    ap.add_argument('--only', choices=['conv_update', 'gdn_decode', 'gdn_chunk', 'mem_read', 'mem_commit', 'mem_indexed', 'mem_topk',
+    ap.add_argument('--only', choices=['conv_update', 'gdn_decode', 'gdn_fused', 'gdn_chunk', 'mem_read', 'mem_commit', 'mem_indexed', 'mem_topk',
                                        'mem_sequence', 'greedy',
                                        'topk'], help='run one kernel family (small ncu captures)')
     ap.add_argument('--prefill-batch', type=int, default=8)

@@ -94,6 +94,33 @@ int yb_gdn_recurrent_fwd(const void *q, const void *k, const void *v, int64_t q_
                          int io_dtype, int g_dtype, int beta_dtype, uint32_t flags, void *stream);
 
 /*
+ * One GDN layer's decode core in one launch: the short conv update over the
+ * fused q/k/v projection (kernel width 4, SiLU), the gates
+ * (decay = exp(-exp(A_log) * softplus(a + dt_bias)), beta = sigmoid(b)), the
+ * q/k L2 norm, the gated delta rule with the state updated in place, and
+ * the gated RMSNorm of the output with z and norm_weight.  Replaces the
+ * sequence of runtime/model/inference_kernels.py:693-721
+ * `_fused_gdn_gate_native_decode_forward` between in_proj and out_proj
+ * (fused gates :668-691, causal_conv1d_update :339-376, the in-place
+ * recurrence :147-173, Qwen3_5RMSNormGated), with the same roundings.
+ *
+ *   mixed [N*T, 2*H*K + HV*V] (channels q | k | v), z [N*T, HV, V],
+ *   a, b [N*T, HV] (logits) — bf16 or fp16 (io_dtype), token strides in
+ *   elements; conv_state [N, 2*H*K + HV*V, 4] in io_dtype, updated in place;
+ *   conv_weight [C, 4], conv_bias [C] (or NULL) fp32; state [N, HV, K, V]
+ *   (or [N, HV, V, K] with YB_GDN_TRANSPOSE_STATE) in state_dtype (YB_F32,
+ *   YB_BF16 or YB_F16), updated in place; A_log, dt_bias [HV] fp32;
+ *   norm_weight [V] io_dtype; o [N*T, HV, V] io_dtype.  K = V = 128.
+ */
+int yb_gdn_decode_fused(const void *mixed, int64_t mixed_tok_stride, const void *z, int64_t z_tok_stride,
+                        const void *a, const void *b, int64_t ab_tok_stride, void *conv_state,
+                        int64_t conv_batch_stride, int64_t conv_width, const float *conv_weight,
+                        const float *conv_bias, int64_t conv_ks, void *state, int state_dtype,
+                        const float *A_log, const float *dt_bias, const void *norm_weight, float norm_eps,
+                        void *o, int64_t N, int64_t T, int64_t H, int64_t HV, int64_t K, int64_t V, float scale,
+                        int io_dtype, uint32_t flags, void *stream);
+
+/*
  * Causal depthwise conv1d in front of the recurrence (the GDN layer's short
  * convolution over the fused q/k/v projection):
  *   y[t, c] = act(sum_{j < KS} weight[c, j] * x[t - (KS - 1) + j, c] + bias[c]),

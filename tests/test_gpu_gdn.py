@@ -201,6 +201,59 @@ def test_decode_gates_and_norm_in_kernel(yb):
     assert rel(host(s), es) <= STATE_RTOL
 
 
+@pytest.mark.parametrize('sdtype,trans,T', [(torch.float32, False, 1), (torch.float16, False, 1),
+                                            (torch.float32, True, 1), (torch.float32, False, 3)])
+def test_fused_decode_layer_vs_oracle(yb, sdtype, trans, T):
+    """The one-launch GDN decode core (conv -> gates -> L2 norm -> recurrence
+    -> gated RMSNorm), 4 calls, against the reference chain in the oracle:
+    conv outputs and beta rounded to bf16 as the reference stores them, the
+    state rounded to its storage dtype after every call."""
+    from oracle import conv as oconv
+    rng = np.random.default_rng(70 + T + trans)
+    B, H, HV, K, V, calls = 4, 16, 32, 128, 128, 4
+    C = 2 * H * K + HV * V
+    bf = torch.bfloat16
+    rb = lambda x: host(cuda(np.ascontiguousarray(x, np.float32), bf))  # noqa: E731
+    store = lambda x: torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(sdtype).float().numpy()  # noqa: E731
+    w_conv = (0.5 * rng.standard_normal((C, 4))).astype(np.float32)
+    cst = rb(rng.standard_normal((B, C, 4)))
+    A_log = np.log(rng.uniform(1, 16, HV)).astype(np.float32)
+    dt_bias = rng.standard_normal(HV).astype(np.float32)
+    wn = rb(1 + 0.1 * rng.standard_normal(V))
+    h0 = (0.05 * rng.standard_normal((B, HV, K, V))).astype(np.float32)
+    if trans:
+        h0 = np.ascontiguousarray(h0.transpose(0, 1, 3, 2))
+    conv_state = cuda(cst, bf)
+    state = cuda(h0).to(sdtype)
+    es, ecs = store(h0), cst
+    for _ in range(calls):
+        mixed = rb(rng.standard_normal((B, T, C)))
+        z = rb(rng.standard_normal((B, T, HV, V)))
+        a = rb(2 * rng.standard_normal((B, T, HV)))
+        blog = rb(rng.standard_normal((B, T, HV)))
+        o = yb.fused_gdn_decode(cuda(mixed, bf), cuda(z, bf), cuda(a, bf), cuda(blog, bf), conv_state, cuda(w_conv),
+                                None, state, cuda(A_log), cuda(dt_bias), cuda(wn, bf), num_k_heads=H,
+                                transpose_state_layout=trans)
+        outs = []
+        for t in range(T):
+            y, ecs = oconv.conv_update(mixed[:, t, :, None], ecs, w_conv)
+            y = rb(y[:, :, 0])[:, None]                               # stored as bf16 by the conv update
+            q = y[..., :H * K].reshape(B, 1, H, K)
+            k = y[..., H * K:2 * H * K].reshape(B, 1, H, K)
+            v = y[..., 2 * H * K:].reshape(B, 1, HV, V)
+            g, beta = ogdn.gdn_gates(a[:, t:t + 1], blog[:, t:t + 1], A_log, dt_bias, dtype=np.float64)
+            beta = rb(beta)                                           # stored in b's dtype
+            eo, es = ogdn.recurrent_gated_delta_rule(q, k, v, g, beta, initial_state=es, use_qk_l2norm=True,
+                                                     transpose_state=trans, dtype=np.float64)
+            outs.append(ogdn.rmsnorm_gated(eo, z[:, t:t + 1], wn, dtype=np.float64))
+        es = store(es)
+        en = np.concatenate(outs, 1)
+        assert rel(host(o), en) <= 1e-2
+        assert np.abs(host(o) - en).max() <= 0.1
+    np.testing.assert_array_equal(host(conv_state), rb(ecs))
+    assert rel(host(state), es) <= STATE_RTOL
+
+
 def test_gdn_gates_kernel(yb, golden):
     d = golden('gdn')
     beta, g = yb.gdn_gates(cuda(d['gate_b']), cuda(d['gate_a']), cuda(d['gate_A_log']), cuda(d['gate_dt_bias']))

@@ -15,7 +15,8 @@ Operators (all CUDA, via the C ABI library libyanchor_b200.so):
 * ``bind_gdn_kernels`` / ``install_memory_module`` / ``bind_memory_prefill``
   put them where the reference model code looks them up.
 """
-from .gated_delta_rule import chunk_gated_delta_rule, fused_recurrent_gated_delta_rule, gdn_gates  # noqa: F401
+from .gated_delta_rule import (chunk_gated_delta_rule, fused_gdn_decode, fused_recurrent_gated_delta_rule,  # noqa: F401
+                               gdn_gates)
 from .conv import causal_conv1d_fn, causal_conv1d_update  # noqa: F401
 from .independent_memory import MemoryState, commit_decode, committed_gqa, indexed_gqa  # noqa: F401
 from .memory_prefill import exclusive_prefix_topk, merge_topk, select_topk, sequence  # noqa: F401

@@ -71,8 +71,8 @@ extern "C" {
 const char *yb_last_error(void) { return g_err; }
 int yb_abi_version(void) { return 1; }
 int yb_device_error(int clear) {
-  const int a = read_device_error(clear), b = read_device_error_idx(clear);
-  return a ? a : b;
+  const int a = read_device_error(clear), b = read_device_error_idx(clear), c = read_device_error_fused(clear);
+  return a ? a : (b ? b : c);
 }
 
 int yb_gdn_recurrent_fwd(const void *q, const void *k, const void *v, int64_t q_tok_stride, int64_t k_tok_stride,
@@ -215,6 +215,39 @@ int yb_mem_indexed_read_timeline(const void *query, const void *key, const void 
   a.w_hi = write_hi;
   a.T = T;
   return launch_mem_indexed_read(a);
+}
+
+int yb_gdn_decode_fused(const void *mixed, int64_t mixed_tok_stride, const void *z, int64_t z_tok_stride,
+                        const void *a, const void *b, int64_t ab_tok_stride, void *conv_state,
+                        int64_t conv_batch_stride, int64_t conv_width, const float *conv_weight,
+                        const float *conv_bias, int64_t conv_ks, void *state, int state_dtype,
+                        const float *A_log, const float *dt_bias, const void *norm_weight, float norm_eps,
+                        void *o, int64_t N, int64_t T, int64_t H, int64_t HV, int64_t K, int64_t V, float scale,
+                        int io_dtype, uint32_t flags, void *stream) {
+  YB_REQUIRE(io_dtype == YB_BF16 || io_dtype == YB_F16, "gdn_decode_fused: activations must be bf16 or fp16");
+  YB_REQUIRE(state_dtype == YB_F32 || state_dtype == YB_BF16 || state_dtype == YB_F16,
+             "gdn_decode_fused: bad state dtype");
+  YB_REQUIRE(N >= 0 && T >= 0 && H > 0 && HV > 0 && HV % H == 0 && K > 0 && V > 0, "gdn_decode_fused: bad sizes");
+  YB_REQUIRE(!(flags & ~uint32_t(YB_GDN_TRANSPOSE_STATE)), "gdn_decode_fused: only YB_GDN_TRANSPOSE_STATE may be set");
+  const int64_t C = 2 * H * K + HV * V;
+  YB_REQUIRE(mixed_tok_stride >= C && z_tok_stride >= HV * V && ab_tok_stride >= HV,
+             "gdn_decode_fused: token strides too small");
+  YB_REQUIRE(N == 0 || conv_batch_stride >= C * conv_width, "gdn_decode_fused: conv state batch stride too small");
+  YB_REQUIRE(N * T == 0 || (mixed && z && a && b && conv_state && conv_weight && state && A_log && norm_weight && o),
+             "gdn_decode_fused: null tensor");
+  YB_REQUIRE(aligned(mixed, 16) && aligned(z, 16) && aligned(conv_state, 16) && aligned(conv_weight, 16) &&
+                 aligned(state, 16) && aligned(o, 16) && aligned(norm_weight, 16),
+             "gdn_decode_fused: tensors must be 16-byte aligned");
+  YB_REQUIRE((mixed_tok_stride * dtype_size(io_dtype)) % 16 == 0 && (z_tok_stride * dtype_size(io_dtype)) % 16 == 0,
+             "gdn_decode_fused: token strides must be multiples of 16 bytes");
+  FusedArgs f{};
+  f.mixed = mixed; f.mixed_ts = mixed_tok_stride; f.z = z; f.z_ts = z_tok_stride; f.a = a; f.b = b;
+  f.ab_ts = ab_tok_stride; f.conv_state = conv_state; f.conv_bs = conv_batch_stride; f.conv_width = conv_width;
+  f.conv_ks = conv_ks; f.conv_w = conv_weight; f.conv_b = conv_bias; f.state = state; f.state_dtype = state_dtype;
+  f.trans = flags & YB_GDN_TRANSPOSE_STATE; f.A_log = A_log; f.dt_bias = dt_bias; f.norm_w = norm_weight;
+  f.norm_eps = norm_eps; f.scale = scale; f.o = o; f.N = N; f.T = T; f.H = H; f.HV = HV; f.K = K; f.V = V;
+  f.io_dtype = io_dtype; f.stream = static_cast<cudaStream_t>(stream);
+  return launch_gdn_decode_fused(f);
 }
 
 int yb_conv1d_update(const void *x, int64_t x_batch_stride, void *conv_state, int64_t state_batch_stride,

@@ -114,6 +114,30 @@ struct PrefixTopkArgs {
 };
 int launch_exclusive_prefix_topk(const PrefixTopkArgs &a);
 
+struct FusedArgs {
+  const void *mixed;
+  int64_t mixed_ts;
+  const void *z;
+  int64_t z_ts;
+  const void *a, *b;
+  int64_t ab_ts;
+  void *conv_state;
+  int64_t conv_bs, conv_width, conv_ks;
+  const float *conv_w, *conv_b;
+  void *state;
+  int state_dtype;
+  bool trans;
+  const float *A_log, *dt_bias;
+  const void *norm_w;
+  float norm_eps, scale;
+  void *o;
+  int64_t N, T, H, HV, K, V;
+  int io_dtype;
+  cudaStream_t stream;
+};
+int launch_gdn_decode_fused(const FusedArgs &a);
+int read_device_error_fused(int clear);
+
 struct ConvArgs {
   const void *x;
   int64_t x_bs, x_ts;             // batch / token strides (elements); channels contiguous

@@ -211,3 +211,62 @@ def gdn_gates(b, a, A_log, dt_bias):
 fused_recurrent_gdn = fused_recurrent_gated_delta_rule
 chunk_gdn = chunk_gated_delta_rule
 recurrent_gated_delta_rule = fused_recurrent_gated_delta_rule
+
+
+def fused_gdn_decode(mixed_qkv, z, a, b, conv_state, conv_weight, conv_bias, recurrent_state, A_log, dt_bias,
+                     norm_weight, *, num_k_heads, norm_eps=1e-6, scale=None, transpose_state_layout=False):
+    """One GDN layer's decode core, everything between ``in_proj_*`` and
+    ``out_proj`` of ``_fused_gdn_gate_native_decode_forward``
+    (runtime/model/inference_kernels.py:693-721), in one launch:
+    short conv update (SiLU) -> split q | k | v -> gates -> L2 norm -> gated
+    delta rule (state in place) -> gated RMSNorm with z.
+
+    mixed_qkv ``[B, T, 2*H*K + HV*V]`` (the in_proj_qkv output, token-major);
+    z ``[B, T, HV, V]`` (or ``[B, T, HV*V]``); a, b ``[B, T, HV]`` logits;
+    conv_state ``[B, C, 4]`` (activation dtype) and recurrent_state
+    ``[B, HV, K, V]`` (float32, bfloat16 or float16) are updated in place;
+    conv_weight ``[C, 4]`` (or ``[C, 1, 4]``); returns ``[B, T, HV, V]``.
+    K = V = 128, HV / H in {1, 2}.
+    """
+    require_cuda(mixed_qkv, z, a, b, conv_state, conv_weight, conv_bias, recurrent_state, A_log, dt_bias,
+                 norm_weight)
+    B, T, C = mixed_qkv.shape
+    N, HV = recurrent_state.shape[0], recurrent_state.shape[1]
+    K = recurrent_state.shape[3] if transpose_state_layout else recurrent_state.shape[2]
+    V = recurrent_state.shape[2] if transpose_state_layout else recurrent_state.shape[3]
+    H = int(num_k_heads)
+    if N != B or C != 2 * H * K + HV * V:
+        raise ValueError('mixed_qkv must be [B, T, 2*H*K + HV*V] for the recurrent state [B, HV, K, V]')
+    if mixed_qkv.dtype not in (torch.bfloat16, torch.float16):
+        raise TypeError('activations must be bfloat16 or float16')
+    for name, t in (('z', z), ('a', a), ('b', b), ('conv_state', conv_state), ('norm_weight', norm_weight)):
+        if t.dtype != mixed_qkv.dtype:
+            raise TypeError(f'{name} must share the activation dtype')
+    if not recurrent_state.is_contiguous() or recurrent_state.data_ptr() % 16:
+        raise ValueError('recurrent_state must be contiguous and 16-byte aligned (it is updated in place)')
+    if conv_state.shape != (B, C, 4) or conv_state.stride(2) != 1 or conv_state.stride(1) != 4:
+        raise ValueError('conv_state must be [B, C, 4], contiguous inside each batch row')
+    mixed, ms = token_view(mixed_qkv)
+    z = z.reshape(B, T, HV, V)
+    z, zs = token_view(z)
+    a, abs_ = scalar_token_view(a)
+    b, bs_ = scalar_token_view(b)
+    if abs_ != bs_:
+        b = b.reshape(B, T, HV).contiguous()
+        a = a.reshape(B, T, HV).contiguous()
+        abs_ = HV
+    w = conv_weight.reshape(C, -1).to(torch.float32).contiguous()
+    cb = None if conv_bias is None else conv_bias.to(torch.float32).contiguous()
+    A_log = A_log.to(torch.float32).contiguous()
+    dt_bias = None if dt_bias is None else dt_bias.to(torch.float32).contiguous()
+    norm_weight = norm_weight.contiguous()
+    o = torch.empty((B, T, HV, V), device=mixed_qkv.device, dtype=mixed_qkv.dtype)
+    sd = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}[recurrent_state.dtype]
+    rc = _lib.lib().yb_gdn_decode_fused(
+        mixed.data_ptr(), ms, z.data_ptr(), zs, a.data_ptr(), b.data_ptr(), abs_, conv_state.data_ptr(),
+        conv_state.stride(0), 4, w.data_ptr(), ptr(cb), w.shape[1], recurrent_state.data_ptr(), sd, A_log.data_ptr(),
+        ptr(dt_bias), norm_weight.data_ptr(), float(norm_eps), o.data_ptr(), B, T, H, HV, K, V,
+        float(K ** -0.5 if scale is None else scale), dtype_code(mixed_qkv),
+        _lib.GDN_TRANSPOSE_STATE if transpose_state_layout else 0, stream_ptr(mixed_qkv.device))
+    _lib.check(rc, 'fused_gdn_decode')
+    return o
