@@ -397,6 +397,31 @@ def run_gpu(args, rank, world, local_rank, dist):
     if dist is not None:
         ms16 = shard.max_over_ranks(ms16, device=device)
 
+    # ---- sliding-window attention decode over the physical ring (the 8 SWA layers, an (f) row) ----
+    SW_QH, SW_KVH, SW_W, SW_D = 16, 4, 1024, 256
+    bf = torch.bfloat16
+    rings = [(torch.randn(B, SW_KVH, SW_W, SW_D, device=device).to(bf),
+              torch.randn(B, SW_KVH, SW_W, SW_D, device=device).to(bf),
+              torch.ones(B, SW_W, device=device, dtype=torch.bool),
+              torch.zeros((), device=device, dtype=torch.int64)) for _ in range(L_MEM)]
+    swq = torch.randn(L_MEM, B, 1, SW_QH, SW_D, device=device).to(bf)
+    swk = torch.randn(L_MEM, B, SW_KVH, 1, SW_D, device=device).to(bf)
+    sw_ws = torch.empty(yb.swa.workspace_bytes(B, SW_KVH, SW_QH, SW_W, SW_D), device=device, dtype=torch.uint8)
+
+    def swa_layers():
+        for i, (rk, rv, rval, ridx) in enumerate(rings):
+            yb.physical_ring_update_(rk, rv, rval, ridx, swk[i], swk[i], active[:, None])
+            yb.physical_ring_decode_attention(swq[i], rk, rv, rval, workspace=sw_ws)
+    swa_layers()
+    torch.cuda.synchronize()
+    gsw = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gsw):
+        swa_layers()
+    gsw.replay()
+    swa_ms = time_events(torch, gsw.replay, 20, stream) / L_MEM
+    swa_bytes = B * SW_KVH * SW_W * SW_D * 2 * 2 + B * SW_QH * SW_D * 2 * 2
+    del gsw, rings
+
     result = {
         'metric': METRIC, 'value': round(value, 1), 'unit': 'tok/s', 'n_gpus': world, 'steps': args.steps,
         'warmup': args.warmup, 'ms_per_step': round(ms, 4), 'higher_is_better': True, 'scaling': 'weak',
@@ -420,6 +445,10 @@ def run_gpu(args, rank, world, local_rank, dist):
             'gdn_kernel': {'achieved': round(gbytes16 / (gdn16_ms / 1e3) / 1e9, 1), 'peak': hbm, 'unit': 'GB/s',
                            'frac': round(gbytes16 / (gdn16_ms / 1e3) / 1e9 / hbm, 4), 'bytes_per_launch': gbytes16,
                            'launch_ms': round(gdn16_ms, 5)}},
+        'swa_decode': {'layer_ms': round(swa_ms, 5), 'how': 'ring write + attention over W=1024 positions, '
+                       '16 query heads over 4 KV heads, D=256, B per GPU, CUDA graph over 8 layers',
+                       'achieved_gbs': round(swa_bytes / (swa_ms / 1e3) / 1e9, 1), 'peak': hbm,
+                       'frac': round(swa_bytes / (swa_ms / 1e3) / 1e9 / hbm, 4), 'bytes_per_layer': swa_bytes},
         'gpu_launches': LAUNCHES_PER_STEP * args.steps,
         'clocks': clocks.summary(),
     }
@@ -528,6 +557,13 @@ def run_only(args):
         mk = torch.randn(1, 4096, MEM_G, MEM_D, generator=gen, device=dev).to(bf)
         refs = torch.randint(0, 4096, (8, blocks, MEM_G, 64), generator=gen, device=dev)
         fn = lambda: yb.indexed_gqa(mq, mk, mk, refs)  # noqa: E731
+    elif args.only == 'swa':
+        rk = torch.randn(B, 4, 1024, 256, generator=gen, device=dev).to(bf)
+        rv = torch.randn(B, 4, 1024, 256, generator=gen, device=dev).to(bf)
+        rval = torch.ones(B, 1024, device=dev, dtype=torch.bool)
+        sq = torch.randn(B, 1, 16, 256, generator=gen, device=dev).to(bf)
+        sw = torch.empty(yb.swa.workspace_bytes(B, 4, 16, 1024, 256), device=dev, dtype=torch.uint8)
+        fn = lambda: yb.physical_ring_decode_attention(sq, rk, rv, rval, workspace=sw)  # noqa: E731
     elif args.only in ('mem_topk', 'mem_sequence'):
         blocks, T = 128, 8192
         psc = (torch.randn(8, blocks, MEM_G, 64, generator=gen, device=dev) * 2).round() / 2
@@ -648,7 +684,7 @@ def main():
     ap.add_argument('--no-prefill', action='store_true')
     ap.add_argument('--no-cpu', action='store_true')
     ap.add_argument('--only', choices=['conv_update', 'gdn_decode', 'gdn_fused', 'gdn_chunk', 'mem_read', 'mem_commit', 'mem_indexed', 'mem_topk',
-                                       'mem_sequence', 'greedy',
+                                       'mem_sequence', 'swa', 'greedy',
                                        'topk'], help='run one kernel family (small ncu captures)')
     ap.add_argument('--prefill-batch', type=int, default=8)
     args = ap.parse_args()

@@ -121,6 +121,36 @@ int yb_gdn_decode_fused(const void *mixed, int64_t mixed_tok_stride, const void 
                         int io_dtype, uint32_t flags, void *stream);
 
 /*
+ * Sliding-window attention decode over the physical ring cache.  Ring key /
+ * value [B, KVH, W, D] (each head's W positions are contiguous rows of D;
+ * batch / head strides in elements), ring valid [B, W] (bool bytes), one
+ * device int64 write index for the whole batch.
+ *
+ * yb_swa_ring_write: the new token's key / value [B, KVH, 1, D] (strides in
+ * elements, D contiguous) and valid [B] go to ring position *ring_index,
+ * then *ring_index advances modulo W.  Replaces
+ * runtime/model/inference_kernels.py:1828-1879
+ * `triton_fixed_memory_swa_physical_ring_update`.
+ *
+ * yb_swa_decode_attention: query [B, 1, QH, D] -> out [B, 1, QH, D]; each
+ * query head h attends to the valid positions of KV head h / (QH / KVH),
+ * scale D^-1/2 (a row with no valid position gives zeros).  D in
+ * {32, 64, 128, 256}, QH / KVH in {1, 2, 4, 8}.  Workspace:
+ * yb_swa_decode_workspace_bytes(B, KVH, QH, W, D).  Replaces
+ * runtime/model/inference_kernels.py:1881-1897
+ * `fixed_memory_physical_ring_decode_attention`.
+ */
+int yb_swa_ring_write(const void *key, const void *value, int64_t kv_batch_stride, int64_t kv_head_stride,
+                      const uint8_t *valid, void *ring_key, void *ring_value, int64_t ring_batch_stride,
+                      int64_t ring_head_stride, uint8_t *ring_valid, int64_t ring_valid_batch_stride,
+                      int64_t *ring_index, int64_t B, int64_t KVH, int64_t W, int64_t D, int dtype, void *stream);
+int64_t yb_swa_decode_workspace_bytes(int64_t B, int64_t KVH, int64_t QH, int64_t W, int64_t D);
+int yb_swa_decode_attention(const void *query, const void *ring_key, const void *ring_value,
+                            int64_t ring_batch_stride, int64_t ring_head_stride, const uint8_t *valid,
+                            int64_t valid_batch_stride, void *out, int64_t B, int64_t QH, int64_t KVH, int64_t W,
+                            int64_t D, int dtype, void *workspace, int64_t workspace_bytes, void *stream);
+
+/*
  * Causal depthwise conv1d in front of the recurrence (the GDN layer's short
  * convolution over the fused q/k/v projection):
  *   y[t, c] = act(sum_{j < KS} weight[c, j] * x[t - (KS - 1) + j, c] + bias[c]),

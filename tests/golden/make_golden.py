@@ -19,6 +19,8 @@ Python) to a scratch directory, puts it and the reference root first on
   (runtime/model/inference_kernels.py:24-88)
 * ``torch_causal_conv1d_update`` and the causal ``nn.Conv1d`` of the GDN
   layer (modeling_yanchor.py:349-370)
+* ``fixed_memory_physical_ring_decode_attention`` (runtime/model/
+  inference_kernels.py:1881-1897)
 
 on seeded inputs and writes the inputs and outputs as ``.npz`` files next to
 this script.  The GPU box never needs the reference: tests only read the
@@ -281,6 +283,22 @@ def conv_fixtures(my, torch):
     return out
 
 
+def swa_fixtures(ik, torch):
+    """The physical-ring decode attention (runtime/model/inference_kernels.py:
+    1881-1897) through its reproducible (math SDPA) path: grouped-query, a
+    validity mask with holes and a row with a single valid position."""
+    g = torch.Generator().manual_seed(13)
+    B, QH, KVH, W, D = 3, 8, 2, 24, 32
+    q = torch.randn(B, 1, QH, D, generator=g)
+    rk = torch.randn(B, KVH, W, D, generator=g)
+    rv = torch.randn(B, KVH, W, D, generator=g)
+    valid = torch.rand(B, W, generator=g) > 0.3
+    valid[2] = False
+    valid[2, 5] = True
+    out = ik.fixed_memory_physical_ring_decode_attention(q, rk, rv, valid, reproducible=True)
+    return {'swa_q': q, 'swa_k': rk, 'swa_v': rv, 'swa_valid': valid, 'swa_out': out}
+
+
 def sampling_fixtures(ik, torch):
     out = {}
     g = torch.Generator().manual_seed(4)
@@ -310,7 +328,8 @@ def main():
     import torch
     torch.manual_seed(0)
     for name, fn in (('gdn', lambda: gdn_fixtures(qwen, torch)), ('memory', lambda: memory_fixtures(my, torch)),
-                     ('sampling', lambda: sampling_fixtures(ik, torch)), ('conv', lambda: conv_fixtures(my, torch))):
+                     ('sampling', lambda: sampling_fixtures(ik, torch)), ('conv', lambda: conv_fixtures(my, torch)),
+                     ('swa', lambda: swa_fixtures(ik, torch))):
         data = {k: (v.detach().cpu().numpy() if hasattr(v, 'detach') else np.asarray(v)) for k, v in fn().items()}
         path = os.path.join(HERE, f'{name}.npz')
         np.savez_compressed(path, **data)

@@ -1,0 +1,77 @@
+"""GPU parity of the sliding-window attention decode over the physical ring:
+the attention against the reference fixture (fp32) and the oracle (bf16,
+the YANchor shape: 16 query heads over 4 KV heads, D=256, W=1024), and the
+ring update (write position, wrap-around, validity) against the oracle."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import swa as oswa
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope='module')
+def yb():
+    import yanchor_b200
+    return yanchor_b200
+
+
+def cuda(x, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(x)).cuda()
+    return t if dtype is None else t.to(dtype)
+
+
+def host(t):
+    return t.detach().cpu().numpy() if t.dtype == torch.bool else t.detach().float().cpu().numpy()
+
+
+def test_attention_golden(yb, golden):
+    d = golden('swa')
+    out = yb.physical_ring_decode_attention(cuda(d['swa_q']), cuda(d['swa_k']), cuda(d['swa_v']),
+                                            cuda(d['swa_valid']))
+    np.testing.assert_allclose(host(out), d['swa_out'], atol=2e-5)
+
+
+@pytest.mark.parametrize('W', [1024, 100, 1])
+def test_attention_bf16_yanchor_shape(yb, W):
+    rng = np.random.default_rng(W)
+    B, QH, KVH, D = 8, 16, 4, 256
+    bf = torch.bfloat16
+    q = cuda(rng.standard_normal((B, 1, QH, D)).astype(np.float32), bf)
+    k = cuda(rng.standard_normal((B, KVH, W, D)).astype(np.float32), bf)
+    v = cuda(rng.standard_normal((B, KVH, W, D)).astype(np.float32), bf)
+    valid = rng.random((B, W)) > 0.25
+    valid[:, 0] = True                                  # the token just written
+    valid[3] = False                                    # a row with nothing valid: zeros
+    out = yb.physical_ring_decode_attention(q, k, v, cuda(valid))
+    ref = oswa.decode_attention(host(q), host(k), host(v), valid)
+    ref[3] = 0.0
+    assert np.abs(host(out) - ref).max() <= 2e-2
+
+
+def test_ring_update_wraps_and_feeds_attention(yb):
+    """Nine writes into a 4-wide ring (two wrap-arounds) with inactive rows,
+    each followed by an attention read, against the oracle."""
+    rng = np.random.default_rng(5)
+    B, QH, KVH, W, D = 3, 8, 2, 4, 64
+    rk = np.zeros((B, KVH, W, D), np.float32)
+    rv = np.zeros((B, KVH, W, D), np.float32)
+    rval = np.zeros((B, W), bool)
+    idx = 0
+    ring_k, ring_v, ring_valid = cuda(rk), cuda(rv), cuda(rval)
+    ring_index = torch.zeros((), dtype=torch.int64, device='cuda')
+    for step in range(9):
+        k = rng.standard_normal((B, KVH, 1, D)).astype(np.float32)
+        v = rng.standard_normal((B, KVH, 1, D)).astype(np.float32)
+        val = rng.random((B, 1)) > 0.2
+        q = rng.standard_normal((B, 1, QH, D)).astype(np.float32)
+        yb.physical_ring_update_(ring_k, ring_v, ring_valid, ring_index, cuda(k), cuda(v), cuda(val))
+        rk, rv, rval, idx = oswa.ring_update(rk, rv, rval, idx, k, v, val)
+        assert int(ring_index.item()) == idx
+        np.testing.assert_array_equal(host(ring_k), rk)
+        np.testing.assert_array_equal(host(ring_valid), rval)
+        out = yb.physical_ring_decode_attention(cuda(q), ring_k, ring_v, ring_valid)
+        ref = oswa.decode_attention(q, rk, rv, rval)
+        ref[~rval.any(1)] = 0.0
+        np.testing.assert_allclose(host(out), ref, atol=2e-5)

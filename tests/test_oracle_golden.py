@@ -211,3 +211,10 @@ def test_conv_prefill(golden, name, cached):
     y, st = conv.conv_fwd(d[f'{name}_x'], d['conv_w'], initial_state=d['conv_prec_state_in'] if cached else None)
     close(y, d[f'{name}_y'], 1e-5)
     close(st, d[f'{name}_state'], 0.0)
+
+
+# ------------------------------------------------------------------ SWA ------
+def test_swa_decode_attention(golden):
+    from oracle import swa
+    d = golden('swa')
+    close(swa.decode_attention(d['swa_q'], d['swa_k'], d['swa_v'], d['swa_valid']), d['swa_out'], 2e-6)

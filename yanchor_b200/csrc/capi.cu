@@ -250,6 +250,58 @@ int yb_gdn_decode_fused(const void *mixed, int64_t mixed_tok_stride, const void 
   return launch_gdn_decode_fused(f);
 }
 
+int yb_swa_ring_write(const void *key, const void *value, int64_t kv_batch_stride, int64_t kv_head_stride,
+                      const uint8_t *valid, void *ring_key, void *ring_value, int64_t ring_batch_stride,
+                      int64_t ring_head_stride, uint8_t *ring_valid, int64_t ring_valid_batch_stride,
+                      int64_t *ring_index, int64_t B, int64_t KVH, int64_t W, int64_t D, int dtype, void *stream) {
+  YB_REQUIRE(dtype_ok(dtype), "swa_ring_write: bad dtype");
+  YB_REQUIRE(B >= 0 && KVH > 0 && W > 0 && (D == 32 || D == 64 || D == 128 || D == 256),
+             "swa_ring_write: bad sizes (D in 32/64/128/256)");
+  YB_REQUIRE(B == 0 || (key && value && valid && ring_key && ring_value && ring_valid && ring_index),
+             "swa_ring_write: null tensor");
+  YB_REQUIRE(ring_head_stride >= W * D && (B <= 1 || ring_batch_stride >= KVH * ring_head_stride) &&
+                 kv_head_stride >= D && (B <= 1 || kv_batch_stride >= KVH * kv_head_stride) &&
+                 (B <= 1 || ring_valid_batch_stride >= W),
+             "swa_ring_write: strides too small");
+  YB_REQUIRE(aligned(key, 16) && aligned(value, 16) && aligned(ring_key, 16) && aligned(ring_value, 16) &&
+                 ((kv_batch_stride | kv_head_stride | ring_batch_stride | ring_head_stride) * dtype_size(dtype)) % 16 == 0,
+             "swa_ring_write: tensors and strides must be 16-byte aligned");
+  SwaArgs a{};
+  a.new_k = key; a.new_v = value; a.new_bs = kv_batch_stride; a.new_hs = kv_head_stride; a.new_valid = valid;
+  a.ring_k = ring_key; a.ring_v = ring_value; a.ring_bs = ring_batch_stride; a.ring_hs = ring_head_stride;
+  a.ring_valid = ring_valid; a.valid_bs = ring_valid_batch_stride; a.ring_index = ring_index;
+  a.B = B; a.KVH = KVH; a.W = W; a.D = D; a.dtype = dtype; a.stream = static_cast<cudaStream_t>(stream);
+  return launch_swa_ring_write(a);
+}
+
+int64_t yb_swa_decode_workspace_bytes(int64_t B, int64_t KVH, int64_t QH, int64_t W, int64_t D) {
+  return swa_workspace_bytes(B, KVH, QH, W, D);
+}
+
+int yb_swa_decode_attention(const void *query, const void *ring_key, const void *ring_value,
+                            int64_t ring_batch_stride, int64_t ring_head_stride, const uint8_t *valid,
+                            int64_t valid_batch_stride, void *out, int64_t B, int64_t QH, int64_t KVH, int64_t W,
+                            int64_t D, int dtype, void *workspace, int64_t workspace_bytes, void *stream) {
+  YB_REQUIRE(dtype_ok(dtype), "swa_decode_attention: bad dtype");
+  YB_REQUIRE(B >= 0 && KVH > 0 && QH % KVH == 0 && W > 0 && D > 0, "swa_decode_attention: bad sizes");
+  YB_REQUIRE(B == 0 || (query && ring_key && ring_value && valid && out), "swa_decode_attention: null tensor");
+  YB_REQUIRE(ring_head_stride >= W * D && (B <= 1 || ring_batch_stride >= KVH * ring_head_stride) &&
+                 (B <= 1 || valid_batch_stride >= W),
+             "swa_decode_attention: strides too small");
+  YB_REQUIRE(aligned(query, 16) && aligned(ring_key, 16) && aligned(ring_value, 16) && aligned(out, 16) &&
+                 ((ring_batch_stride | ring_head_stride) * dtype_size(dtype)) % 16 == 0,
+             "swa_decode_attention: tensors and strides must be 16-byte aligned");
+  const int64_t need = swa_workspace_bytes(B, KVH, QH, W, D);
+  if (workspace == nullptr || workspace_bytes < need)
+    return set_error(YB_ERR_WORKSPACE, "swa_decode_attention: workspace of %lld bytes required", (long long)need);
+  SwaArgs a{};
+  a.query = query; a.ring_k = const_cast<void *>(ring_key); a.ring_v = const_cast<void *>(ring_value);
+  a.ring_bs = ring_batch_stride; a.ring_hs = ring_head_stride; a.ring_valid = const_cast<uint8_t *>(valid);
+  a.valid_bs = valid_batch_stride; a.out = out; a.B = B; a.QH = QH; a.KVH = KVH; a.W = W; a.D = D;
+  a.dtype = dtype; a.stream = static_cast<cudaStream_t>(stream);
+  return launch_swa_decode_attention(a, workspace);
+}
+
 int yb_conv1d_update(const void *x, int64_t x_batch_stride, void *conv_state, int64_t state_batch_stride,
                      int64_t state_width, const float *weight, const float *bias, void *out,
                      int64_t out_batch_stride, int64_t B, int64_t C, int64_t KS, int silu, int dtype,

@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/yanchor_b200.h"
 
 namespace yb {
@@ -100,6 +102,34 @@ __device__ __forceinline__ float softplus20(float x) { return x > 20.f ? x : log
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + expf(-x)); }
 
 }  // namespace yb
+
+// ---- programmatic dependent launch -------------------------------------------
+// A kernel launched with launch_pdl may start while the previous kernel in
+// its stream is still running.  Before pdl_wait() it must read nothing that
+// kernel may write (an L2 prefetch is always safe: a later write lands in L2
+// first); pdl_release() lets the next kernel begin launching.  Both are no-ops
+// for a normal launch.  A kernel releases only after its own wait, so when it
+// runs its pre-wait part every kernel before its predecessor has finished,
+// and a dependent can only be scheduled once every CTA of its predecessor is.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void prefetch_l2(const void *p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // ---- host-side error plumbing (defined in capi.cu) ---------------------------
 namespace yb {

@@ -32,6 +32,8 @@ template <typename T, int KS>
 __global__ void __launch_bounds__(kConvThreads) conv_update_kernel(const ConvArgs a) {
   const int64_t b = blockIdx.y;
   const int64_t c = int64_t(blockIdx.x) * kConvThreads + threadIdx.x;
+  pdl_wait();
+  pdl_release();
   if (c >= a.C) return;
   const T *x = static_cast<const T *>(a.x) + b * a.x_bs;
   T *st = static_cast<T *>(a.state) + b * a.state_bs + c * a.W;
@@ -127,8 +129,10 @@ int conv_dispatch(const ConvArgs &a, bool update) {
 #define YB_CONV_CASE(K)                                                                                 \
   case K:                                                                                               \
     if (update) {                                                                                       \
-      conv_update_kernel<T, K><<<dim3(unsigned((a.C + kConvThreads - 1) / kConvThreads), unsigned(a.B)), \
-                                 kConvThreads, 0, a.stream>>>(a);                                       \
+      const cudaError_t e = launch_pdl(conv_update_kernel<T, K>,                                        \
+                                       dim3(unsigned((a.C + kConvThreads - 1) / kConvThreads), unsigned(a.B)), \
+                                       dim3(kConvThreads), 0, a.stream, a);                             \
+      if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "conv_update_kernel: %s", cudaGetErrorString(e)); \
       return check_launch("conv_update_kernel");                                                        \
     }                                                                                                   \
     conv_fwd_kernel<T, K><<<dim3(unsigned((a.C + kConvThreads - 1) / kConvThreads),                     \

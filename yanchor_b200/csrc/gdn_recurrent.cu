@@ -110,7 +110,16 @@ __global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(const RecParams
   __shared__ float s_decay, s_beta, s_kq;
 
   // State tile into registers (issued first: it is the long-latency stream).
+  // Under a dependent launch it is only prefetched into L2 before the wait:
+  // the previous kernel may be the one that wrote it.
   const int64_t head = (int64_t(n) * p.HV + hv) * K * V;
+  if (p.h0) {
+    const TS *src = static_cast<const TS *>(p.h0) + head;
+#pragma unroll
+    for (int i = 0; i < RPT; i += (sizeof(TS) == 4 ? 1 : 2)) prefetch_l2(src + (rg * RPT + i) * COLS + c0);
+  }
+  pdl_wait();
+  pdl_release();
   float s[RPT][4];
   if (p.h0) {
     const TS *src = static_cast<const TS *>(p.h0) + head;
@@ -288,10 +297,10 @@ int launch_kv(const GdnArgs &a, const RecParams &p) {
   const bool trans = a.flags & YB_GDN_TRANSPOSE_STATE;
   const bool norm = a.z != nullptr;
   dim3 grid(unsigned(a.N * a.HV));
-  if (!trans && !norm) gdn_recurrent_kernel<TIO, TS, K, V, false, false><<<grid, kThreads, 0, a.stream>>>(p);
-  if (!trans && norm) gdn_recurrent_kernel<TIO, TS, K, V, false, true><<<grid, kThreads, 0, a.stream>>>(p);
-  if (trans && !norm) gdn_recurrent_kernel<TIO, TS, K, V, true, false><<<grid, kThreads, 0, a.stream>>>(p);
-  if (trans && norm) gdn_recurrent_kernel<TIO, TS, K, V, true, true><<<grid, kThreads, 0, a.stream>>>(p);
+  auto kern = trans ? (norm ? gdn_recurrent_kernel<TIO, TS, K, V, true, true> : gdn_recurrent_kernel<TIO, TS, K, V, true, false>)
+                    : (norm ? gdn_recurrent_kernel<TIO, TS, K, V, false, true> : gdn_recurrent_kernel<TIO, TS, K, V, false, false>);
+  const cudaError_t e = launch_pdl(kern, grid, dim3(kThreads), 0, a.stream, p);
+  if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "gdn_recurrent_kernel: %s", cudaGetErrorString(e));
   return check_launch("gdn_recurrent_kernel");
 }
 

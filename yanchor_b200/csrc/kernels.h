@@ -138,6 +138,25 @@ struct FusedArgs {
 int launch_gdn_decode_fused(const FusedArgs &a);
 int read_device_error_fused(int clear);
 
+struct SwaArgs {
+  const void *new_k, *new_v;      // ring write: the new token [B, KVH, 1, D]
+  int64_t new_bs, new_hs;
+  const uint8_t *new_valid;       // [B]
+  void *ring_k, *ring_v;          // [B, KVH, W, D]
+  int64_t ring_bs, ring_hs;
+  uint8_t *ring_valid;            // [B, W]
+  int64_t valid_bs;
+  int64_t *ring_index;            // device scalar
+  const void *query;              // attention: [B, 1, QH, D]
+  void *out;                      // [B, 1, QH, D]
+  int64_t B, QH, KVH, W, D;
+  int dtype;
+  cudaStream_t stream;
+};
+int launch_swa_ring_write(const SwaArgs &a);
+int launch_swa_decode_attention(const SwaArgs &a, void *workspace);
+int64_t swa_workspace_bytes(int64_t B, int64_t KVH, int64_t QH, int64_t W, int64_t D);
+
 struct ConvArgs {
   const void *x;
   int64_t x_bs, x_ts;             // batch / token strides (elements); channels contiguous

@@ -139,6 +139,18 @@ __global__ void __launch_bounds__(kStageThreads) mem_decode_read_staged_kernel(c
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t row = blockIdx.x / a.G;
   const int g = int(blockIdx.x % a.G);
+  if (!a.indices) {   // the bank's rows are known before the wait: warm L2 with them
+    const unsigned char *k0 = reinterpret_cast<const unsigned char *>(static_cast<const T *>(a.keys) + row * a.kv_s0 +
+                                                                       int64_t(g) * a.CAP * D);
+    const unsigned char *v0 = reinterpret_cast<const unsigned char *>(static_cast<const T *>(a.values) + row * a.kv_s0 +
+                                                                       int64_t(g) * a.CAP * D);
+    for (int64_t off = int64_t(tid) * 128; off < a.CAP * D * int64_t(sizeof(T)); off += kStageThreads * 128) {
+      prefetch_l2(k0 + off);
+      prefetch_l2(v0 + off);
+    }
+  }
+  pdl_wait();
+  pdl_release();
   const int64_t s = a.indices ? a.indices[row] : row;
   const T *qp = static_cast<const T *>(a.query) + (row * a.H + int64_t(g) * R) * D;
   T *outp = static_cast<T *>(a.out) + (row * a.H + int64_t(g) * R) * D;
@@ -223,7 +235,8 @@ int launch_read_r(const MemReadArgs &a) {
       auto sk = mem_decode_read_staged_kernel<T, R, DD>;                                           \
       cudaError_t e = cudaFuncSetAttribute(sk, cudaFuncAttributeMaxDynamicSharedMemorySize, int(staged)); \
       if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "memory read: smem attribute: %s", cudaGetErrorString(e)); \
-      sk<<<grid, kStageThreads, staged, a.stream>>>(a);                                            \
+      e = launch_pdl(sk, grid, dim3(kStageThreads), staged, a.stream, a);                           \
+      if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "memory read: %s", cudaGetErrorString(e)); \
       return check_launch("mem_decode_read_staged_kernel");                                        \
     }                                                                                              \
     auto kern = mem_decode_read_kernel<T, R, DD>;                                                  \
@@ -285,6 +298,8 @@ __device__ void commit_gather(T *bank, const T *pend, T *stage, const int *sel, 
 
 template <typename T>
 __global__ void __launch_bounds__(kCommitThreads) mem_decode_commit_kernel(const MemCommitArgs a) {
+  pdl_wait();
+  pdl_release();
   __shared__ float c_score[kMaxCand];
   __shared__ int64_t c_pkey[kMaxCand];  // position, INT64_MAX for an invalid slot
   __shared__ int sel[kMaxCand];         // new slot -> winning candidate
@@ -363,7 +378,8 @@ int launch_commit_t(const MemCommitArgs &a) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "memory commit: smem attribute: %s", cudaGetErrorString(e));
   }
-  kern<<<unsigned(a.B), kCommitThreads, smem, a.stream>>>(a);
+  const cudaError_t le = launch_pdl(kern, dim3(unsigned(a.B)), dim3(kCommitThreads), smem, a.stream, a);
+  if (le != cudaSuccess) return set_error(YB_ERR_CUDA, "memory commit: %s", cudaGetErrorString(le));
   return check_launch("mem_decode_commit_kernel");
 }
 

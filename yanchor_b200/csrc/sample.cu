@@ -69,6 +69,8 @@ __host__ __device__ __forceinline__ void split_range(int64_t n, int splits, int 
 template <typename T>
 __global__ void __launch_bounds__(kNT) greedy_partial_kernel(const T *scores, int64_t row_stride, int64_t vocab,
                                                              int splits, Cand *ws) {
+  pdl_wait();
+  pdl_release();
   const int split = blockIdx.x;
   const int64_t b = blockIdx.y;
   int64_t lo, hi;
@@ -118,6 +120,8 @@ __global__ void __launch_bounds__(kNT) greedy_partial_kernel(const T *scores, in
 }
 
 __global__ void greedy_final_kernel(const Cand *ws, int splits, int64_t B, int64_t *out) {
+  pdl_wait();
+  pdl_release();
   const int64_t b = int64_t(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (b >= B) return;
@@ -562,11 +566,14 @@ template <typename T>
 int greedy_t(const SampleArgs &a) {
   const int splits = greedy_splits(a.B, a.vocab);
   Cand *ws = static_cast<Cand *>(a.workspace);
-  greedy_partial_kernel<T><<<dim3(splits, unsigned(a.B)), kNT, 0, a.stream>>>(static_cast<const T *>(a.scores),
-                                                                               a.row_stride, a.vocab, splits, ws);
+  cudaError_t e = launch_pdl(greedy_partial_kernel<T>, dim3(splits, unsigned(a.B)), dim3(kNT), 0, a.stream,
+                             static_cast<const T *>(a.scores), a.row_stride, a.vocab, splits, ws);
+  if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "greedy_partial_kernel: %s", cudaGetErrorString(e));
   int rc = check_launch("greedy_partial_kernel");
   if (rc) return rc;
-  greedy_final_kernel<<<unsigned((a.B + 7) / 8), 256, 0, a.stream>>>(ws, splits, a.B, a.out);
+  e = launch_pdl(greedy_final_kernel, dim3(unsigned((a.B + 7) / 8)), dim3(256), 0, a.stream,
+                 static_cast<const Cand *>(ws), splits, a.B, a.out);
+  if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "greedy_final_kernel: %s", cudaGetErrorString(e));
   return check_launch("greedy_final_kernel");
 }
 

@@ -1,0 +1,249 @@
+// Sliding-window attention decode over the physical ring cache
+// (runtime/model/inference_kernels.py:1828-1897).
+//
+// Ring: key / value [B, KVH, W, D] (positions contiguous rows of D), valid
+// [B, W], one device-resident write index for the batch.  Update: the new
+// token's key / value / valid go to position `index`, then the index
+// advances modulo W (a second one-thread launch, so no block of the write
+// sees a moved index).
+//
+// Attention: each query head attends to every ring position whose valid
+// flag is set (order does not matter to a softmax), scale D^-1/2, query head
+// h reading KV head h / R (R = QH / KVH).  Split over the window: one CTA per
+// (row, KV head, 64-position slice) stages the slice's K and V rows by
+// cp.async into padded shared rows, computes the R heads' logits (one
+// (position, head) pair per thread), their slice max and exp-sum, and the
+// exp-weighted value sums (one feature column per thread); a combine kernel
+// rescales the slices to the global max and normalises.  Memory-bound: every
+// K / V byte is read once.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace yb {
+namespace {
+
+constexpr int kSwaThreads = 256;
+constexpr int kSwaSlice = 64;
+
+__device__ __forceinline__ void cp_async16_swa(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
+
+template <typename T>
+__global__ void swa_ring_write_kernel(const SwaArgs a) {
+  constexpr int VEC = 16 / int(sizeof(T));
+  const int64_t idx = *a.ring_index;
+  if (idx < 0 || idx >= a.W) return;   // a corrupt index writes nothing (the advance restarts it at 0)
+  const int64_t pieces = a.B * a.KVH * (a.D / VEC);
+  const int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (e < 2 * pieces) {
+    const bool is_v = e >= pieces;
+    const int64_t f = is_v ? e - pieces : e;
+    const int64_t d = (f % (a.D / VEC)) * VEC, bh = f / (a.D / VEC), b = bh / a.KVH, h = bh % a.KVH;
+    const T *src = static_cast<const T *>(is_v ? a.new_v : a.new_k) + b * a.new_bs + h * a.new_hs + d;
+    T *dst = static_cast<T *>(is_v ? a.ring_v : a.ring_k) + b * a.ring_bs + h * a.ring_hs + idx * a.D + d;
+    *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(src);
+  } else if (e < 2 * pieces + a.B) {
+    const int64_t b = e - 2 * pieces;
+    a.ring_valid[b * a.valid_bs + idx] = a.new_valid[b];
+  }
+}
+
+__global__ void swa_ring_advance_kernel(int64_t *index, int64_t W) {
+  const int64_t i = *index;
+  *index = (i < 0 || i + 1 >= W) ? 0 : i + 1;
+}
+
+template <typename T, int R, int D>
+__global__ void __launch_bounds__(kSwaThreads) swa_partial_kernel(const SwaArgs a, float *part) {
+  constexpr int ROWB = D * int(sizeof(T)) + 16;   // padded shared row (bank spread)
+  constexpr int PIECES = D * int(sizeof(T)) / 16;
+  constexpr int QP = D + 4;
+  extern __shared__ __align__(16) unsigned char swa_raw[];
+  unsigned char *sk = swa_raw;                                        // [slice][ROWB]
+  unsigned char *sv = sk + kSwaSlice * ROWB;                          // [slice][ROWB]
+  float *sq = reinterpret_cast<float *>(sv + kSwaSlice * ROWB);       // [R][QP]
+  float *sp = sq + R * QP;                                            // [R][slice] logits -> weights
+  float *sm = sp + R * kSwaSlice;                                     // [R] max, [R] sum
+  const int tid = threadIdx.x;
+  const int64_t bh = blockIdx.x, b = bh / a.KVH, kvh = bh % a.KVH;
+  const int64_t slice = blockIdx.y, p0 = slice * kSwaSlice;
+  const int np = int(a.W - p0 < kSwaSlice ? a.W - p0 : kSwaSlice);
+  const unsigned char *kb = reinterpret_cast<const unsigned char *>(static_cast<const T *>(a.ring_k) + b * a.ring_bs +
+                                                                      kvh * a.ring_hs + p0 * D);
+  const unsigned char *vb = reinterpret_cast<const unsigned char *>(static_cast<const T *>(a.ring_v) + b * a.ring_bs +
+                                                                      kvh * a.ring_hs + p0 * D);
+  for (int e = tid; e < np * PIECES; e += kSwaThreads)
+    cp_async16_swa(sk + (e / PIECES) * ROWB + (e % PIECES) * 16, kb + size_t(e / PIECES) * D * sizeof(T) +
+                                                                     (e % PIECES) * 16);
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  for (int e = tid; e < np * PIECES; e += kSwaThreads)
+    cp_async16_swa(sv + (e / PIECES) * ROWB + (e % PIECES) * 16, vb + size_t(e / PIECES) * D * sizeof(T) +
+                                                                     (e % PIECES) * 16);
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  const T *q = static_cast<const T *>(a.query) + (b * a.QH + kvh * R) * D;
+  for (int e = tid; e < R * D; e += kSwaThreads) sq[(e / D) * QP + e % D] = to_f(q[e]);
+  asm volatile("cp.async.wait_group 1;" ::: "memory");
+  __syncthreads();
+  const float scale = rsqrtf(float(D));
+  for (int e = tid; e < kSwaSlice * R; e += kSwaThreads) {
+    const int pos = e / R, r = e % R;
+    float acc = -INFINITY;
+    if (pos < np && a.ring_valid[b * a.valid_bs + p0 + pos]) {
+      const T *krow = reinterpret_cast<const T *>(sk + pos * ROWB);
+      const float *qr = sq + r * QP;
+      acc = 0.f;
+#pragma unroll 4
+      for (int d = 0; d < D; d += 8) {
+        float kx[8];
+        load8(krow + d, kx);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc = fmaf(qr[d + j], kx[j], acc);
+      }
+      acc *= scale;
+    }
+    sp[r * kSwaSlice + pos] = acc;
+  }
+  __syncthreads();
+  // per head: slice max and exp-sum (a warp per head)
+  const int warp = tid >> 5, lane = tid & 31;
+  for (int r = warp; r < R; r += kSwaThreads / 32) {
+    float m = -INFINITY;
+    for (int j = lane; j < kSwaSlice; j += 32) m = fmaxf(m, sp[r * kSwaSlice + j]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (int j = lane; j < kSwaSlice; j += 32) {
+      const float x = sp[r * kSwaSlice + j];
+      const float w = x == -INFINITY ? 0.f : __expf(x - m);
+      sp[r * kSwaSlice + j] = w;
+      l += w;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      sm[r] = m;
+      sm[R + r] = l;
+    }
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+  // exp-weighted value sums: one feature column per thread, all R heads
+  float *out = part + (bh * gridDim.y + slice) * (R * (D + 2));
+  for (int d = tid; d < D; d += kSwaThreads) {
+    float acc[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = 0.f;
+    for (int pos = 0; pos < np; ++pos) {
+      const float x = to_f(reinterpret_cast<const T *>(sv + pos * ROWB)[d]);
+#pragma unroll
+      for (int r = 0; r < R; ++r) acc[r] = fmaf(sp[r * kSwaSlice + pos], x, acc[r]);
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) out[r * (D + 2) + d] = acc[r];
+  }
+  if (tid < R) {
+    out[tid * (D + 2) + D] = sm[tid];
+    out[tid * (D + 2) + D + 1] = sm[R + tid];
+  }
+}
+
+template <typename T>
+__global__ void swa_combine_kernel(const SwaArgs a, const float *part, int R, int slices) {
+  const int64_t bh = blockIdx.x, b = bh / a.KVH, kvh = bh % a.KVH;
+  const int r = blockIdx.y;
+  const int D = int(a.D);
+  const float *pb = part + bh * slices * (R * (D + 2)) + r * (D + 2);
+  float M = -INFINITY;
+  for (int s = 0; s < slices; ++s) M = fmaxf(M, pb[s * R * (D + 2) + D]);
+  T *o = static_cast<T *>(a.out) + (b * a.QH + kvh * R + r) * D;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float num = 0.f, den = 0.f;
+    if (M != -INFINITY) {
+      for (int s = 0; s < slices; ++s) {
+        const float *ps = pb + s * R * (D + 2);
+        const float m = ps[D];
+        if (m == -INFINITY) continue;
+        const float f = __expf(m - M);
+        num = fmaf(ps[d], f, num);
+        den = fmaf(ps[D + 1], f, den);
+      }
+    }
+    o[d] = from_f<T>(den > 0.f ? num / den : 0.f);
+  }
+}
+
+template <typename T, int R, int D>
+int attn_launch(const SwaArgs &a, float *part, int slices) {
+  const size_t smem = size_t(2) * kSwaSlice * (D * sizeof(T) + 16) + sizeof(float) * (R * (D + 4) + R * kSwaSlice + 2 * R);
+  auto k = swa_partial_kernel<T, R, D>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "swa attention: smem attribute: %s", cudaGetErrorString(e));
+  k<<<dim3(unsigned(a.B * a.KVH), unsigned(slices)), kSwaThreads, smem, a.stream>>>(a, part);
+  int rc = check_launch("swa_partial_kernel");
+  if (rc) return rc;
+  swa_combine_kernel<T><<<dim3(unsigned(a.B * a.KVH), unsigned(R)), D < 256 ? D : 256, 0, a.stream>>>(a, part, R,
+                                                                                                      slices);
+  return check_launch("swa_combine_kernel");
+}
+
+template <typename T, int R>
+int attn_r(const SwaArgs &a, float *part, int slices) {
+  switch (a.D) {
+    case 32: return attn_launch<T, R, 32>(a, part, slices);
+    case 64: return attn_launch<T, R, 64>(a, part, slices);
+    case 128: return attn_launch<T, R, 128>(a, part, slices);
+    case 256: return attn_launch<T, R, 256>(a, part, slices);
+  }
+  return set_error(YB_ERR_UNSUPPORTED, "swa attention: head dim %lld not built (32/64/128/256)", (long long)a.D);
+}
+
+template <typename T>
+int attn_t(const SwaArgs &a, float *part, int slices) {
+  switch (a.QH / a.KVH) {
+    case 1: return attn_r<T, 1>(a, part, slices);
+    case 2: return attn_r<T, 2>(a, part, slices);
+    case 4: return attn_r<T, 4>(a, part, slices);
+    case 8: return attn_r<T, 8>(a, part, slices);
+  }
+  return set_error(YB_ERR_UNSUPPORTED, "swa attention: QH / KVH = %lld not built (1/2/4/8)",
+                   (long long)(a.QH / a.KVH));
+}
+
+}  // namespace
+
+int64_t swa_workspace_bytes(int64_t B, int64_t KVH, int64_t QH, int64_t W, int64_t D) {
+  const int64_t slices = (W + kSwaSlice - 1) / kSwaSlice;
+  return B * KVH * slices * (QH / (KVH > 0 ? KVH : 1)) * (D + 2) * int64_t(sizeof(float));
+}
+
+int launch_swa_ring_write(const SwaArgs &a) {
+  if (a.B == 0) return YB_OK;
+  const int64_t elem = a.dtype == YB_F32 ? 4 : 2;
+  const int64_t n = 2 * a.B * a.KVH * (a.D * elem / 16) + a.B;
+  const unsigned blocks = unsigned((n + 255) / 256);
+  switch (a.dtype) {
+    case YB_F32: swa_ring_write_kernel<float><<<blocks, 256, 0, a.stream>>>(a); break;
+    case YB_BF16: swa_ring_write_kernel<__nv_bfloat16><<<blocks, 256, 0, a.stream>>>(a); break;
+    case YB_F16: swa_ring_write_kernel<__half><<<blocks, 256, 0, a.stream>>>(a); break;
+    default: return set_error(YB_ERR_ARGUMENT, "swa ring: bad dtype %d", a.dtype);
+  }
+  int rc = check_launch("swa_ring_write_kernel");
+  if (rc) return rc;
+  swa_ring_advance_kernel<<<1, 1, 0, a.stream>>>(a.ring_index, a.W);
+  return check_launch("swa_ring_advance_kernel");
+}
+
+int launch_swa_decode_attention(const SwaArgs &a, void *workspace) {
+  if (a.B * a.KVH == 0) return YB_OK;
+  const int slices = int((a.W + kSwaSlice - 1) / kSwaSlice);
+  float *part = static_cast<float *>(workspace);
+  switch (a.dtype) {
+    case YB_F32: return attn_t<float>(a, part, slices);
+    case YB_BF16: return attn_t<__nv_bfloat16>(a, part, slices);
+    case YB_F16: return attn_t<__half>(a, part, slices);
+  }
+  return set_error(YB_ERR_ARGUMENT, "swa attention: bad dtype %d", a.dtype);
+}
+
+}  // namespace yb
