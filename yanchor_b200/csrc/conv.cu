@@ -28,6 +28,60 @@ constexpr int kConvTile = 32;   // tokens per thread in prefill
 
 __device__ __forceinline__ float conv_act(float y, bool silu) { return silu ? y * sigmoidf_(y) : y; }
 
+// The common decode case (width-4 cache state, 16-bit activations, C a
+// multiple of 4): a thread owns 4 consecutive channels of kConvRows batch
+// rows, so the weights stay in registers and each row's loads are all issued
+// before its stores.
+constexpr int kConvRows = 1;
+
+template <typename T>
+__global__ void __launch_bounds__(kConvThreads) conv_update4_kernel(const ConvArgs a) {
+  const int64_t c = (int64_t(blockIdx.x) * kConvThreads + threadIdx.x) * 4;
+  const int64_t b0 = int64_t(blockIdx.y) * kConvRows;
+  pdl_wait();
+  pdl_release();
+  if (c >= a.C) return;
+  float4 w[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) w[j] = __ldg(reinterpret_cast<const float4 *>(a.weight + (c + j) * 4));
+  float bias[4] = {0.f, 0.f, 0.f, 0.f};
+  if (a.bias) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) bias[j] = a.bias[c + j];
+  }
+#pragma unroll
+  for (int rr = 0; rr < kConvRows; ++rr) {
+    const int64_t b = b0 + rr;
+    if (b >= a.B) break;
+    const T *x = static_cast<const T *>(a.x) + b * a.x_bs + c;
+    T *st = static_cast<T *>(a.state) + b * a.state_bs + c * 4;
+    const uint2 xv = *reinterpret_cast<const uint2 *>(x);                 // 4 inputs
+    uint4 sv[2];                                                          // 4 channels x 4 taps
+    sv[0] = *reinterpret_cast<const uint4 *>(st);
+    sv[1] = *reinterpret_cast<const uint4 *>(st + 8);
+    const T *xin = reinterpret_cast<const T *>(&xv);
+    T *h = reinterpret_cast<T *>(sv);
+    T yo[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      T *s4 = h + 4 * j;
+      float y = bias[j];
+      y = fmaf(w[j].x, to_f(s4[1]), y);
+      y = fmaf(w[j].y, to_f(s4[2]), y);
+      y = fmaf(w[j].z, to_f(s4[3]), y);
+      y = fmaf(w[j].w, to_f(xin[j]), y);
+      s4[0] = s4[1];
+      s4[1] = s4[2];
+      s4[2] = s4[3];
+      s4[3] = xin[j];
+      yo[j] = from_f<T>(conv_act(y, a.silu));
+    }
+    *reinterpret_cast<uint4 *>(st) = sv[0];
+    *reinterpret_cast<uint4 *>(st + 8) = sv[1];
+    *reinterpret_cast<uint2 *>(static_cast<T *>(a.out) + b * a.out_bs + c) = *reinterpret_cast<const uint2 *>(yo);
+  }
+}
+
 template <typename T, int KS>
 __global__ void __launch_bounds__(kConvThreads) conv_update_kernel(const ConvArgs a) {
   const int64_t b = blockIdx.y;
@@ -125,6 +179,17 @@ __global__ void __launch_bounds__(kConvThreads) conv_fwd_kernel(const ConvArgs a
 
 template <typename T>
 int conv_dispatch(const ConvArgs &a, bool update) {
+  if constexpr (sizeof(T) == 2) {
+    const uintptr_t al = reinterpret_cast<uintptr_t>(a.x) | reinterpret_cast<uintptr_t>(a.state) |
+                         reinterpret_cast<uintptr_t>(a.out) | reinterpret_cast<uintptr_t>(a.weight);
+    if (update && a.KS == 4 && a.W == 4 && a.C % 4 == 0 && (al % 16) == 0 && (a.x_bs % 4) == 0 &&
+        (a.out_bs % 4) == 0 && (a.state_bs % 8) == 0) {
+      const dim3 grid(unsigned((a.C / 4 + kConvThreads - 1) / kConvThreads), unsigned((a.B + kConvRows - 1) / kConvRows));
+      const cudaError_t e = launch_pdl(conv_update4_kernel<T>, grid, dim3(kConvThreads), 0, a.stream, a);
+      if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "conv_update4_kernel: %s", cudaGetErrorString(e));
+      return check_launch("conv_update4_kernel");
+    }
+  }
   switch (a.KS) {
 #define YB_CONV_CASE(K)                                                                                 \
   case K:                                                                                               \

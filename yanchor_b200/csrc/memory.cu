@@ -323,11 +323,25 @@ __global__ void __launch_bounds__(kCommitThreads) mem_decode_commit_kernel(const
   int32_t *bpos = a.positions + s * a.meta_s0;
   float *pscore = a.pscores + s * a.pmeta_s0;
 
-  // push into pending slot `count`
-  for (int e = tid; e < G * D; e += kCommitThreads) {
-    const int g = e / D, d = e % D;
-    pend_k[(int64_t(g) * PC + count) * D + d] = key[e];
-    pend_v[(int64_t(g) * PC + count) * D + d] = val[e];
+  // push into pending slot `count` (16-byte pieces when every row start is aligned)
+  constexpr int VEC = 16 / int(sizeof(T));
+  const bool vec = (D % VEC) == 0 && (reinterpret_cast<uintptr_t>(key) % 16) == 0 &&
+                   (reinterpret_cast<uintptr_t>(val) % 16) == 0 && (reinterpret_cast<uintptr_t>(pend_k) % 16) == 0 &&
+                   (reinterpret_cast<uintptr_t>(pend_v) % 16) == 0;
+  if (vec) {
+    for (int e = tid * VEC; e < G * D; e += kCommitThreads * VEC) {
+      const int g = e / D, d = e % D;
+      const int64_t dst = (int64_t(g) * PC + count) * D + d;
+      const uint4 kv = *reinterpret_cast<const uint4 *>(key + e), vv = *reinterpret_cast<const uint4 *>(val + e);
+      *reinterpret_cast<uint4 *>(pend_k + dst) = kv;
+      *reinterpret_cast<uint4 *>(pend_v + dst) = vv;
+    }
+  } else {
+    for (int e = tid; e < G * D; e += kCommitThreads) {
+      const int g = e / D, d = e % D;
+      pend_k[(int64_t(g) * PC + count) * D + d] = key[e];
+      pend_v[(int64_t(g) * PC + count) * D + d] = val[e];
+    }
   }
   if (tid < G) pscore[int64_t(tid) * PC + count] = a.scores[row * G + tid];
   if (commit) {
