@@ -160,3 +160,28 @@ def test_vllm_page_pool_decode(yb):
     for f in FIELDS:
         np.testing.assert_array_equal(host(getattr(st, f)), pool_np[f].astype(host(getattr(st, f)).dtype),
                                       err_msg=f)
+
+
+@pytest.mark.parametrize('R,D,CAP', [(1, 64, 16), (2, 128, 40), (4, 256, 64), (8, 128, 64), (4, 64, 1)])
+@pytest.mark.parametrize('dt', [torch.bfloat16, torch.float16])
+def test_decode_read_16bit_shapes(yb, R, D, CAP, dt):
+    """The 16-bit decode read (tensor-core path for banks of <= 64 slots):
+    head groups of 1-8, head dims 64-256, partly empty banks, a bank with no
+    entry (only the null slot), pool indices with a skipped request."""
+    rng = np.random.default_rng(R * 1000 + D + CAP)
+    B, G, POOL = 5, 3, 7
+    H = G * R
+    st = omem.empty_state(POOL, G, CAP, 4, D)
+    st['keys'][:] = rng.standard_normal(st['keys'].shape) * 2
+    st['values'][:] = rng.standard_normal(st['values'].shape)
+    st['positions'][:] = np.where(rng.random(st['positions'].shape) < 0.7,
+                                  rng.integers(0, 1000, st['positions'].shape), -1)
+    st['positions'][2, 1] = -1                          # nothing stored: the null slot only
+    dev = to_device_state(yb, st, dt)
+    q = rng.standard_normal((B, 1, H, D)).astype(np.float32)
+    idx = np.array([2, 0, -1, 6, 3], np.int64)
+    qd = cuda(q, dt)
+    out = yb.committed_gqa(qd, dev, cuda(idx))
+    ref = omem.decode_read(host(qd), host(dev.keys), host(dev.values), st['positions'], idx)
+    assert np.abs(host(out) - ref).max() <= 2e-2
+    assert not host(out)[2].any()

@@ -75,3 +75,22 @@ def test_ring_update_wraps_and_feeds_attention(yb):
         ref = oswa.decode_attention(q, rk, rv, rval)
         ref[~rval.any(1)] = 0.0
         np.testing.assert_allclose(host(out), ref, atol=2e-5)
+
+
+@pytest.mark.parametrize('R,D,W', [(1, 64, 65), (2, 128, 200), (8, 64, 64), (4, 256, 37)])
+@pytest.mark.parametrize('dt', [torch.bfloat16, torch.float16])
+def test_attention_16bit_shapes(yb, R, D, W, dt):
+    """Head groups of 1-8, head dims 64-256, windows that end mid-slice, a row
+    with nothing valid."""
+    rng = np.random.default_rng(R * 7 + D + W)
+    B, KVH = 3, 2
+    QH = KVH * R
+    q = cuda(rng.standard_normal((B, 1, QH, D)).astype(np.float32), dt)
+    k = cuda(rng.standard_normal((B, KVH, W, D)).astype(np.float32), dt)
+    v = cuda(rng.standard_normal((B, KVH, W, D)).astype(np.float32), dt)
+    valid = rng.random((B, W)) > 0.3
+    valid[1] = False
+    out = yb.physical_ring_decode_attention(q, k, v, cuda(valid))
+    ref = oswa.decode_attention(host(q), host(k), host(v), valid)
+    ref[1] = 0.0
+    assert np.abs(host(out) - ref).max() <= 2e-2

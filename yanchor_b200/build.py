@@ -62,7 +62,7 @@ def build(verbose: bool = False, force: bool = False) -> str:
             jobs.append((src, obj))
     with ThreadPoolExecutor(max_workers=min(8, max(1, len(jobs)))) as ex:
         list(ex.map(lambda j: _compile(*j, verbose), jobs))
-    if jobs or not os.path.exists(LIB):
+    if jobs or not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):
         cmd = [nvcc(), *ARCH, '-shared', '-o', LIB, *objs, '-lcudart']
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:

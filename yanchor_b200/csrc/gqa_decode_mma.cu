@@ -1,0 +1,298 @@
+// Grouped-query decode attention on warp-level tensor cores (mma.sync
+// m16n8k16, bf16 / fp16 in, fp32 accumulate): the R query heads of one KV
+// group attend to a slice of up to 64 stored positions.  Shared by the
+// anchor-memory decode read (one 64-slot slice per (row, group), the null
+// slot folded into the softmax, output written directly; semantics of
+// modeling_yanchor.py:283-290 and runtime/model/independent_memory.py:47-88)
+// and the sliding-window ring decode (64-position slices, partial results
+// merged by swa_combine_kernel; runtime/model/inference_kernels.py:1881-1897).
+//
+// Per CTA (4 warps): K, V slice rows arrive by cp.async in padded shared rows
+// (row stride D*2+16 bytes: every ldmatrix phase touches 8 distinct banks
+// groups).  Warp w computes S^T = K Q^T for positions 16w..16w+15 (A = K rows,
+// B = Q padded to 8 heads), the CTA takes the per-head max and exp-sum, P goes
+// to shared memory as bf16 hi + lo, and O^T = V^T P^T (A = V rows through
+// ldmatrix.trans, B = P) gives each warp a quarter of the D columns.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace yb {
+
+namespace {
+
+constexpr int kGqaThreads = 128;
+constexpr int kGqaSlice = 64;
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t *r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t *r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t *r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(addr));
+}
+template <typename T>
+__device__ __forceinline__ void mma16816(float *c, const uint32_t *a, const uint32_t *b);
+template <>
+__device__ __forceinline__ void mma16816<__nv_bfloat16>(float *c, const uint32_t *a, const uint32_t *b) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+template <>
+__device__ __forceinline__ void mma16816<__half>(float *c, const uint32_t *a, const uint32_t *b) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+__device__ __forceinline__ void cp16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+
+template <typename T, int R, int D>
+__global__ void __launch_bounds__(kGqaThreads) gqa_decode_mma_kernel(const GqaDecodeArgs a) {
+  static_assert(R <= 8 && D % 64 == 0, "R <= 8 heads, D a multiple of 64");
+  constexpr int ROW = D + 8;          // padded K / V / Q row (elements)
+  constexpr int PROW = kGqaSlice + 8; // padded P row
+  extern __shared__ __align__(16) unsigned char gqa_raw[];
+  T *sk = reinterpret_cast<T *>(gqa_raw);                 // [64][ROW]
+  T *sv = sk + kGqaSlice * ROW;                           // [64][ROW]
+  T *sq = sv + kGqaSlice * ROW;                           // [8][ROW]
+  T *sp = sq + 8 * ROW;                                   // [2][8][PROW]  P hi, P lo
+  float *red = reinterpret_cast<float *>(sp + 2 * 8 * PROW);   // [4 warps][8] max, then [4][8] sums
+  float *fin = red + 2 * 4 * 8;                                // [8] max, [8] 1 / denominator
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g8 = lane >> 2, t4 = lane & 3;
+  const int64_t unit = blockIdx.x;                        // (row, group)
+  const int64_t slice = blockIdx.y, p0 = slice * kGqaSlice;
+  const int64_t b = unit / a.G, g = unit % a.G;
+  if (!a.indices) {   // the slice's rows are known before the wait: warm L2 with them
+    const char *k0 = reinterpret_cast<const char *>(static_cast<const T *>(a.keys) + b * a.kv_bs + g * a.kv_gs + p0 * D);
+    const char *v0 = reinterpret_cast<const char *>(static_cast<const T *>(a.values) + b * a.kv_bs + g * a.kv_gs + p0 * D);
+    const int64_t nb = (a.P - p0 < kGqaSlice ? a.P - p0 : kGqaSlice) * D * int64_t(sizeof(T));
+    for (int64_t off = int64_t(tid) * 128; off < nb; off += kGqaThreads * 128) {
+      prefetch_l2(k0 + off);
+      prefetch_l2(v0 + off);
+    }
+  }
+  // the stored row this CTA reads; a memory row may be skipped (index -1)
+  pdl_wait();
+  pdl_release();
+  const int64_t s = a.indices ? a.indices[b] : b;
+  const int np = int(a.P - p0 < kGqaSlice ? a.P - p0 : kGqaSlice);
+  if (s < 0) {   // skipped request (memory read): zero output
+    T *o = static_cast<T *>(a.out) + (b * a.QH + g * R) * D;
+    for (int e = tid; e < R * D; e += kGqaThreads) o[e] = from_f<T>(0.f);
+    return;
+  }
+  const T *kb = static_cast<const T *>(a.keys) + s * a.kv_bs + g * a.kv_gs + p0 * D;
+  const T *vb = static_cast<const T *>(a.values) + s * a.kv_bs + g * a.kv_gs + p0 * D;
+  constexpr int PIECES = D / 8;
+  for (int e = tid; e < np * PIECES; e += kGqaThreads) cp16(sk + (e / PIECES) * ROW + (e % PIECES) * 8, kb + e * 8);
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  for (int e = tid; e < np * PIECES; e += kGqaThreads) cp16(sv + (e / PIECES) * ROW + (e % PIECES) * 8, vb + e * 8);
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  // zero the rows a short slice leaves empty (their logits are masked; V must not hold NaNs)
+  for (int e = np * PIECES + tid; e < kGqaSlice * PIECES; e += kGqaThreads) {
+    *reinterpret_cast<uint4 *>(sk + (e / PIECES) * ROW + (e % PIECES) * 8) = make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<uint4 *>(sv + (e / PIECES) * ROW + (e % PIECES) * 8) = make_uint4(0, 0, 0, 0);
+  }
+  const T *qg = static_cast<const T *>(a.query) + (b * a.QH + g * R) * D;
+  for (int e = tid; e < 8 * PIECES; e += kGqaThreads) {
+    const int h = e / PIECES, c = (e % PIECES) * 8;
+    *reinterpret_cast<uint4 *>(sq + h * ROW + c) =
+        h < R ? *reinterpret_cast<const uint4 *>(qg + h * D + c) : make_uint4(0, 0, 0, 0);
+  }
+  asm volatile("cp.async.wait_group 1;" ::: "memory");
+  __syncthreads();
+
+  // ---- S^T (16 positions x 8 heads per warp) ----
+  float sc[4] = {0.f, 0.f, 0.f, 0.f};
+  {
+    const int pr = warp * 16 + (lane & 7) + 8 * ((lane >> 3) & 1), kc = 8 * (lane >> 4);
+    const int qr = lane & 7, qc = 8 * ((lane >> 3) & 1);
+#pragma unroll
+    for (int k = 0; k < D; k += 16) {
+      uint32_t af[4], bfr[2];
+      ldsm_x4(smem_addr(sk + pr * ROW + k + kc), af);
+      ldsm_x2(smem_addr(sq + qr * ROW + k + qc), bfr);
+      mma16816<T>(sc, af, bfr);
+    }
+  }
+  // this thread's entries: positions warp*16 + g8 (+8), heads 2 t4, 2 t4 + 1
+  const float scale = rsqrtf(float(D));
+  float m2[2];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int pos = warp * 16 + g8 + (j >> 1) * 8;
+    bool ok = pos < np;
+    if (ok) {
+      if (a.positions) ok = a.positions[s * a.pos_bs + g * a.pos_gs + p0 + pos] >= 0;
+      else ok = a.valid[b * a.valid_bs + p0 + pos] != 0;
+    }
+    sc[j] = ok ? sc[j] * scale : -INFINITY;
+  }
+  m2[0] = fmaxf(sc[0], sc[2]);
+  m2[1] = fmaxf(sc[1], sc[3]);
+#pragma unroll
+  for (int o = 4; o < 32; o <<= 1) {
+    m2[0] = fmaxf(m2[0], __shfl_xor_sync(0xffffffffu, m2[0], o));
+    m2[1] = fmaxf(m2[1], __shfl_xor_sync(0xffffffffu, m2[1], o));
+  }
+  if (g8 == 0) {
+    red[warp * 8 + 2 * t4] = m2[0];
+    red[warp * 8 + 2 * t4 + 1] = m2[1];
+  }
+  __syncthreads();
+  if (tid < 8) {
+    float m = fmaxf(fmaxf(red[tid], red[8 + tid]), fmaxf(red[16 + tid], red[24 + tid]));
+    if (a.null_slot) m = fmaxf(m, 0.f);
+    fin[tid] = m;
+  }
+  __syncthreads();
+  // ---- P = exp(S - m) as bf16 hi + lo, and the exp-sums ----
+  float l2[2] = {0.f, 0.f};
+  T *phi = sp, *plo = sp + 8 * PROW;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int pos = warp * 16 + g8 + (j >> 1) * 8, h = 2 * t4 + (j & 1);
+    const float m = fin[h];
+    const float p = (sc[j] == -INFINITY || m == -INFINITY) ? 0.f : expf(sc[j] - m);
+    l2[j & 1] += p;
+    const T hi = from_f<T>(p);
+    phi[h * PROW + pos] = hi;
+    plo[h * PROW + pos] = from_f<T>(p - to_f(hi));
+  }
+#pragma unroll
+  for (int o = 4; o < 32; o <<= 1) {
+    l2[0] += __shfl_xor_sync(0xffffffffu, l2[0], o);
+    l2[1] += __shfl_xor_sync(0xffffffffu, l2[1], o);
+  }
+  if (g8 == 0) {
+    red[32 + warp * 8 + 2 * t4] = l2[0];
+    red[32 + warp * 8 + 2 * t4 + 1] = l2[1];
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+  if (tid < 8) {
+    float l = red[32 + tid] + red[40 + tid] + red[48 + tid] + red[56 + tid];
+    if (a.null_slot) l += expf(-fin[tid]);         // the null slot: logit 0, value 0
+    fin[8 + tid] = l;
+  }
+  __syncthreads();
+
+  // ---- O^T = V^T P^T: warp w owns D columns [w D/4, (w+1) D/4) ----
+  constexpr int DW = D / 4, TILES = DW / 16;
+  float acc[TILES][4];
+#pragma unroll
+  for (int t = 0; t < TILES; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
+  {
+    const int vp = (lane & 7) + 8 * (lane >> 4), vd = 8 * ((lane >> 3) & 1);
+    const int pr = lane & 7, pc = 8 * ((lane >> 3) & 1);
+#pragma unroll
+    for (int k = 0; k < kGqaSlice; k += 16) {
+      uint32_t bh[2], bl[2];
+      ldsm_x2(smem_addr(phi + pr * PROW + k + pc), bh);
+      ldsm_x2(smem_addr(plo + pr * PROW + k + pc), bl);
+#pragma unroll
+      for (int t = 0; t < TILES; ++t) {
+        uint32_t af[4];
+        ldsm_x4_t(smem_addr(sv + (k + vp) * ROW + warp * DW + t * 16 + vd), af);
+        mma16816<T>(acc[t], af, bh);
+        mma16816<T>(acc[t], af, bl);
+      }
+    }
+  }
+  // acc[t]: rows (D columns) warp*DW + 16 t + g8 (+8), cols (heads) 2 t4, 2 t4 + 1
+  if (a.partial) {
+    // SWA slice: unnormalised sums + the slice's max and exp-sum, for the combine pass
+    float *part = a.partial + (unit * gridDim.y + slice) * (R * (D + 2));
+#pragma unroll
+    for (int t = 0; t < TILES; ++t)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int h = 2 * t4 + (j & 1), d = warp * DW + 16 * t + g8 + (j >> 1) * 8;
+        if (h < R) part[h * (D + 2) + d] = acc[t][j];
+      }
+    if (tid < R) {
+      part[tid * (D + 2) + D] = fin[tid];
+      part[tid * (D + 2) + D + 1] = fin[8 + tid];
+    }
+  } else {
+    T *o = static_cast<T *>(a.out) + (b * a.QH + g * R) * D;
+#pragma unroll
+    for (int t = 0; t < TILES; ++t)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int h = 2 * t4 + (j & 1), d = warp * DW + 16 * t + g8 + (j >> 1) * 8;
+        if (h < R) {
+          const float l = fin[8 + h];
+          o[h * D + d] = from_f<T>(l > 0.f ? acc[t][j] / l : 0.f);
+        }
+      }
+  }
+}
+
+template <typename T, int R, int D>
+int launch_gqa(const GqaDecodeArgs &a, unsigned slices) {
+  constexpr int ROW = D + 8, PROW = kGqaSlice + 8;
+  const size_t smem = sizeof(T) * (2 * kGqaSlice * ROW + 8 * ROW + 2 * 8 * PROW) + sizeof(float) * (64 + 16);
+  auto k = gqa_decode_mma_kernel<T, R, D>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "gqa decode: smem attribute: %s", cudaGetErrorString(e));
+  e = launch_pdl(k, dim3(unsigned(a.B * a.G), slices), dim3(kGqaThreads), smem, a.stream, a);
+  if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "gqa decode: %s", cudaGetErrorString(e));
+  return check_launch("gqa_decode_mma_kernel");
+}
+
+template <typename T, int R>
+int gqa_d(const GqaDecodeArgs &a, unsigned slices) {
+  switch (a.D) {
+    case 64: return launch_gqa<T, R, 64>(a, slices);
+    case 128: return launch_gqa<T, R, 128>(a, slices);
+    case 256: return launch_gqa<T, R, 256>(a, slices);
+  }
+  return -1;
+}
+
+template <typename T>
+int gqa_r(const GqaDecodeArgs &a, unsigned slices) {
+  switch (a.QH / a.G) {
+    case 1: return gqa_d<T, 1>(a, slices);
+    case 2: return gqa_d<T, 2>(a, slices);
+    case 4: return gqa_d<T, 4>(a, slices);
+    case 8: return gqa_d<T, 8>(a, slices);
+  }
+  return -1;
+}
+
+}  // namespace
+
+bool gqa_decode_mma_supported(int dtype, int64_t QH, int64_t G, int64_t D) {
+  const int64_t R = G > 0 ? QH / G : 0;
+  return (dtype == YB_BF16 || dtype == YB_F16) && (D == 64 || D == 128 || D == 256) &&
+         (R == 1 || R == 2 || R == 4 || R == 8) && QH % G == 0;
+}
+
+int launch_gqa_decode_mma(const GqaDecodeArgs &a) {
+  if (a.B * a.G == 0) return YB_OK;
+  const unsigned slices = unsigned((a.P + kGqaSlice - 1) / kGqaSlice);
+  if (!a.partial && slices != 1) return set_error(YB_ERR_UNSUPPORTED, "gqa decode: a direct read covers <= 64 slots");
+  const int rc = a.dtype == YB_BF16 ? gqa_r<__nv_bfloat16>(a, slices) : gqa_r<__half>(a, slices);
+  if (rc < 0) return set_error(YB_ERR_UNSUPPORTED, "gqa decode: shape not built");
+  return rc;
+}
+
+}  // namespace yb

@@ -153,6 +153,30 @@ struct SwaArgs {
   int dtype;
   cudaStream_t stream;
 };
+// Grouped-query decode attention on mma.sync: R = QH / G query heads of one
+// KV group attend to up to 64 stored positions per CTA.  Direct mode (the
+// anchor-memory read) writes normalised output with an optional null slot;
+// partial mode (the sliding-window ring) writes per-slice sums for
+// swa_combine_kernel.
+struct GqaDecodeArgs {
+  const void *query;              // [B, QH, D] contiguous
+  const void *keys, *values;      // row s, group g, position p at s*kv_bs + g*kv_gs + p*D
+  int64_t kv_bs, kv_gs;
+  const int32_t *positions;       // mask by position >= 0 (s*pos_bs + g*pos_gs + p), or
+  int64_t pos_bs, pos_gs;
+  const uint8_t *valid;           // mask by valid[b*valid_bs + p]
+  int64_t valid_bs;
+  const int64_t *indices;         // optional stored row per request (-1 skips it)
+  void *out;                      // direct mode: [B, QH, D]
+  float *partial;                 // partial mode: [B*G, slices, R, D + 2]
+  int null_slot;                  // add the null logit 0 (value 0) to the softmax
+  int64_t B, G, QH, D, P;
+  int dtype;
+  cudaStream_t stream;
+};
+bool gqa_decode_mma_supported(int dtype, int64_t QH, int64_t G, int64_t D);
+int launch_gqa_decode_mma(const GqaDecodeArgs &a);
+
 int launch_swa_ring_write(const SwaArgs &a);
 int launch_swa_decode_attention(const SwaArgs &a, void *workspace);
 int64_t swa_workspace_bytes(int64_t B, int64_t KVH, int64_t QH, int64_t W, int64_t D);

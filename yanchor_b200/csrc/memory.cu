@@ -567,6 +567,31 @@ int launch_indexed_t(const MemIndexedArgs &a) {
 
 int launch_mem_decode_read(const MemReadArgs &a) {
   if (a.B * a.G == 0) return YB_OK;
+  const auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (a.CAP <= 64 && gqa_decode_mma_supported(a.dtype, a.H, a.G, a.D) && a.kv_s0 % 8 == 0 && al16(a.query) &&
+      al16(a.keys) && al16(a.values) && al16(a.out)) {
+    // a bank of at most 64 slots: one tensor-core CTA per (row, group)
+    GqaDecodeArgs g{};
+    g.query = a.query;
+    g.keys = a.keys;
+    g.values = a.values;
+    g.kv_bs = a.kv_s0;
+    g.kv_gs = a.CAP * a.D;
+    g.positions = a.positions;
+    g.pos_bs = a.pos_s0;
+    g.pos_gs = a.CAP;
+    g.indices = a.indices;
+    g.out = a.out;
+    g.null_slot = 1;
+    g.B = a.B;
+    g.G = a.G;
+    g.QH = a.H;
+    g.D = a.D;
+    g.P = a.CAP;
+    g.dtype = a.dtype;
+    g.stream = a.stream;
+    return launch_gqa_decode_mma(g);
+  }
   switch (a.dtype) {
     case YB_F32: return launch_read_t<float>(a);
     case YB_BF16: return launch_read_t<__nv_bfloat16>(a);

@@ -238,6 +238,40 @@ int launch_swa_decode_attention(const SwaArgs &a, void *workspace) {
   if (a.B * a.KVH == 0) return YB_OK;
   const int slices = int((a.W + kSwaSlice - 1) / kSwaSlice);
   float *part = static_cast<float *>(workspace);
+  const auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (gqa_decode_mma_supported(a.dtype, a.QH, a.KVH, a.D) && a.ring_bs % 8 == 0 && a.ring_hs % 8 == 0 &&
+      al16(a.query) && al16(a.ring_k) && al16(a.ring_v)) {
+    // tensor-core slices, then the same combine pass
+    GqaDecodeArgs g{};
+    g.query = a.query;
+    g.keys = a.ring_k;
+    g.values = a.ring_v;
+    g.kv_bs = a.ring_bs;
+    g.kv_gs = a.ring_hs;
+    g.valid = a.ring_valid;
+    g.valid_bs = a.valid_bs;
+    g.partial = part;
+    g.B = a.B;
+    g.G = a.KVH;
+    g.QH = a.QH;
+    g.D = a.D;
+    g.P = a.W;
+    g.dtype = a.dtype;
+    g.stream = a.stream;
+    int rc = launch_gqa_decode_mma(g);
+    if (rc) return rc;
+    const int R = int(a.QH / a.KVH);
+    switch (a.dtype) {
+      case YB_BF16:
+        swa_combine_kernel<__nv_bfloat16><<<dim3(unsigned(a.B * a.KVH), unsigned(R)), a.D < 256 ? a.D : 256, 0,
+                                            a.stream>>>(a, part, R, slices);
+        break;
+      default:
+        swa_combine_kernel<__half><<<dim3(unsigned(a.B * a.KVH), unsigned(R)), a.D < 256 ? a.D : 256, 0, a.stream>>>(
+            a, part, R, slices);
+    }
+    return check_launch("swa_combine_kernel");
+  }
   switch (a.dtype) {
     case YB_F32: return attn_t<float>(a, part, slices);
     case YB_BF16: return attn_t<__nv_bfloat16>(a, part, slices);
