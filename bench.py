@@ -48,6 +48,8 @@ H_K, H_V, DK, DV = 16, 32, 128, 128
 CONV_C, CONV_KS = 2 * H_K * DK + H_V * DV, 4     # the short convolution over the fused q/k/v projection
 MEM_G, MEM_H, MEM_D, MEM_CAP, MEM_CHUNK = 4, 16, 256, 64, 64
 VOCAB = 248320
+GEN_TOKENS = 32768                                # config 3: 32K generated tokens per sequence
+PAD_ID, EOS_IDS = 248044, ()                      # fixed-length generation: no end ids (runtime/inference.py:94)
 
 
 def peaks():
@@ -158,7 +160,29 @@ def build_decode(torch, yb, B, device, n_inputs=4, seed=0, state_dtype=None):
             ms=rnd(L_MEM, B, 1, MEM_G, dtype=torch.float32), logits=rnd(B, VOCAB, scale=3.0)))
     active = torch.ones(B, dtype=torch.bool, device=device)
     ws = torch.empty(yb.sampling.workspace_bytes(B, VOCAB, 1), dtype=torch.uint8, device=device)
-    return layers, mems, inputs, active, ws
+    return layers, mems, inputs, active, ws, build_table(torch, B, device)
+
+
+def build_table(torch, B, device):
+    """The decode loop's slot table (runtime/model/inference_kernels.py:1451-1475
+    shapes): one slot per sequence, token storage for the 32K-token run,
+    the seen-token table over the vocabulary, sink rows for idle slots."""
+    i64 = torch.int64
+    return dict(storage=torch.zeros((2 * B, GEN_TOKENS + 1), dtype=torch.int32, device=device),
+                dense_seen=torch.zeros((B, VOCAB), dtype=torch.bool, device=device),
+                generated_lengths=torch.zeros(2 * B, dtype=i64, device=device),
+                finished_by_eos=torch.zeros(2 * B, dtype=torch.bool, device=device),
+                finished=torch.zeros(B, dtype=torch.bool, device=device),
+                slot_rows=torch.arange(B, device=device), sink_rows=B + torch.arange(B, device=device),
+                slot_caps=torch.full((B,), GEN_TOKENS, dtype=i64, device=device),
+                row_steps=torch.ones(B, dtype=i64, device=device),
+                row_positions=torch.full((B,), 1024, dtype=i64, device=device),
+                decode_ids=torch.zeros((B, 1), dtype=i64, device=device),
+                decode_useful_events=torch.zeros((), dtype=i64, device=device))
+
+
+TABLE_FIELDS = ('storage', 'dense_seen', 'generated_lengths', 'finished_by_eos', 'finished', 'slot_rows', 'sink_rows',
+                'slot_caps', 'row_steps', 'row_positions', 'decode_ids', 'decode_useful_events')
 
 
 def conv_qkv(yb, L, mixed):
@@ -178,8 +202,9 @@ def gdn_layer(yb, L, x, i):
                                L['state'], L['A_log'], L['dt_bias'], L['norm_w'], num_k_heads=H_K)
 
 
-def decode_step(yb, layers, mems, x, active, ws, fused=False):
-    """One decode step of the hot path; returns the sampled token ids."""
+def decode_step(yb, layers, mems, x, active, ws, table, fused=False):
+    """One decode step of the hot path, then the decode loop's bookkeeping
+    of the sampled token; returns the sampled token ids."""
     for i, L in enumerate(layers):
         if fused:
             gdn_layer(yb, L, x, i)
@@ -193,10 +218,14 @@ def decode_step(yb, layers, mems, x, active, ws, fused=False):
     for i, st in enumerate(mems):
         yb.committed_gqa(x['mq'][i], st)
         yb.commit_decode(x['mk'][i], x['mv'][i], x['ms'][i], active, MEM_CHUNK, st)
-    return yb.greedy(x['logits'], workspace=ws)
+    tok = yb.greedy(x['logits'], workspace=ws)
+    yb.update_fixed_decode_state_(tok, *(table[k] for k in TABLE_FIELDS), maximum_new_tokens=GEN_TOKENS,
+                                  pad_token_id=PAD_ID, eos_token_ids=EOS_IDS)
+    return tok
 
 
-LAUNCHES_PER_STEP = 2 * L_GDN + 2 * L_MEM + 2     # conv + recurrence per GDN layer, read + commit, greedy (2)
+# conv + recurrence per GDN layer, read + commit per memory layer, greedy (2), bookkeeping (1)
+LAUNCHES_PER_STEP = 2 * L_GDN + 2 * L_MEM + 3
 
 
 def gdn_bytes_per_launch(B, state_bytes=4):
@@ -238,12 +267,12 @@ def run_gpu(args, rank, world, local_rank, dist):
     device = torch.device('cuda', local_rank)
     torch.cuda.set_device(device)
     B = args.batch
-    layers, mems, inputs, active, ws = build_decode(torch, yb, B, device, seed=1234 + rank)
+    layers, mems, inputs, active, ws, table = build_decode(torch, yb, B, device, seed=1234 + rank)
     stream = torch.cuda.current_stream(device)
 
     # eager warm-up (also loads the library and sets kernel attributes)
     for w in range(max(args.warmup, 3)):
-        decode_step(yb, layers, mems, inputs[w % len(inputs)], active, ws)
+        decode_step(yb, layers, mems, inputs[w % len(inputs)], active, ws, table)
     torch.cuda.synchronize()
     graphs, outs = [], []
     for x in inputs:
@@ -251,11 +280,11 @@ def run_gpu(args, rank, world, local_rank, dist):
         s = torch.cuda.Stream(device)
         s.wait_stream(stream)
         with torch.cuda.stream(s):
-            decode_step(yb, layers, mems, x, active, ws)   # pre-capture run on the side stream
+            decode_step(yb, layers, mems, x, active, ws, table)   # pre-capture run on the side stream
         stream.wait_stream(s)
         torch.cuda.synchronize()
         with torch.cuda.graph(g):
-            outs.append(decode_step(yb, layers, mems, x, active, ws))
+            outs.append(decode_step(yb, layers, mems, x, active, ws, table))
         graphs.append(g)
     for w in range(args.warmup):
         graphs[w % len(graphs)].replay()
@@ -323,13 +352,13 @@ def run_gpu(args, rank, world, local_rank, dist):
     # group's inputs for its next step come in on a copy stream.  Every step
     # still copies its full inputs in and its token ids out inside the timed
     # region; no step's inputs depend on the other group.
-    layers_b, mems_b, inputs_b, _, ws_b = build_decode(torch, yb, B, device, n_inputs=1, seed=4321 + rank)
+    layers_b, mems_b, inputs_b, _, ws_b, table_b = build_decode(torch, yb, B, device, n_inputs=1, seed=4321 + rank)
     for _ in range(2):
-        decode_step(yb, layers_b, mems_b, inputs_b[0], active, ws_b)
+        decode_step(yb, layers_b, mems_b, inputs_b[0], active, ws_b, table_b)
     torch.cuda.synchronize()
     g_b = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_b):
-        out_b = decode_step(yb, layers_b, mems_b, inputs_b[0], active, ws_b)
+        out_b = decode_step(yb, layers_b, mems_b, inputs_b[0], active, ws_b, table_b)
     host_in_b = {k: v.cpu().pin_memory() for k, v in inputs_b[0].items()}
     host_out_b = torch.empty((B, 1), dtype=torch.int64).pin_memory()
     groups = [(inputs[0], graphs[0], outs[0], host_in, host_out), (inputs_b[0], g_b, out_b, host_in_b, host_out_b)]
@@ -366,14 +395,14 @@ def run_gpu(args, rank, world, local_rank, dist):
         e2e_serial_ms = shard.max_over_ranks(e2e_serial_ms, device=device)
 
     # ---- the reference's opt-in fp16 recurrent-state storage (install_inference(fp16_state=True)) ----
-    layers16, mems16, inputs16, _, ws16 = build_decode(torch, yb, B, device, n_inputs=1, seed=99 + rank,
+    layers16, mems16, inputs16, _, ws16, table16 = build_decode(torch, yb, B, device, n_inputs=1, seed=99 + rank,
                                                        state_dtype=torch.float16)
     for _ in range(3):
-        decode_step(yb, layers16, mems16, inputs16[0], active, ws16)
+        decode_step(yb, layers16, mems16, inputs16[0], active, ws16, table16)
     torch.cuda.synchronize()
     g16 = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g16):
-        decode_step(yb, layers16, mems16, inputs16[0], active, ws16)
+        decode_step(yb, layers16, mems16, inputs16[0], active, ws16, table16)
     for _ in range(3):
         g16.replay()
     ms16 = time_events(torch, g16.replay, max(3, args.steps // 2), stream)
@@ -540,7 +569,7 @@ def run_only(args):
     import yanchor_b200 as yb
     dev = torch.device('cuda', 0)
     B = args.batch
-    layers, mems, inputs, active, ws = build_decode(torch, yb, B, dev, n_inputs=1)
+    layers, mems, inputs, active, ws, table = build_decode(torch, yb, B, dev, n_inputs=1)
     x, L0, st = inputs[0], layers[0], mems[0]
     gen = torch.Generator(device=dev).manual_seed(3)
     bf = torch.bfloat16
@@ -608,8 +637,14 @@ def run_only(args):
 # ------------------------------------------------------------- CPU arm ------
 def cpu_decode_sample(steps=2, B=64, seed=0):
     """Time the numpy restatement of the same decode step on the host."""
-    from oracle import conv as oconv, gdn as ogdn, memory as omem, sampling as osamp
+    from oracle import conv as oconv, decode_state as ods, gdn as ogdn, memory as omem, sampling as osamp
     rng = np.random.default_rng(seed)
+    i64 = np.int64
+    table = dict(storage=np.zeros((2 * B, GEN_TOKENS + 1), np.int32), dense_seen=np.zeros((B, VOCAB), bool),
+                 generated_lengths=np.zeros(2 * B, i64), finished_by_eos=np.zeros(2 * B, bool),
+                 finished=np.zeros(B, bool), slot_rows=np.arange(B, dtype=i64), sink_rows=B + np.arange(B, dtype=i64),
+                 slot_caps=np.full(B, GEN_TOKENS, i64), row_steps=np.ones(B, i64), row_positions=np.full(B, 1024, i64),
+                 decode_ids=np.zeros((B, 1), i64), decode_useful_events=np.zeros((), i64))
     f32 = np.float32
     states = [(0.02 * rng.standard_normal((B, H_V, DK, DV))).astype(f32) for _ in range(L_GDN)]
     conv_states = [rng.standard_normal((B, CONV_C, CONV_KS)).astype(f32) for _ in range(L_GDN)]
@@ -638,7 +673,9 @@ def cpu_decode_sample(steps=2, B=64, seed=0):
             omem.commit_decode(rng.standard_normal((B, 1, MEM_G, MEM_D)).astype(f32),
                                rng.standard_normal((B, 1, MEM_G, MEM_D)).astype(f32),
                                rng.standard_normal((B, 1, MEM_G)).astype(f32), np.ones(B, bool), MEM_CHUNK, st)
-        osamp.greedy(rng.standard_normal((B, VOCAB)).astype(f32))
+        tok = osamp.greedy(rng.standard_normal((B, VOCAB)).astype(f32))
+        ods.update_decode_state(np.asarray(tok, i64).reshape(B, 1), *(table[k] for k in TABLE_FIELDS),
+                                maximum_new_tokens=GEN_TOKENS, pad_token_id=PAD_ID, eos_token_ids=EOS_IDS)
     dt = time.perf_counter() - t0
     return B * steps / dt, dt
 

@@ -349,6 +349,40 @@ int yb_sample_top_k_top_p_counter(const void *scores, int64_t row_stride, int64_
  */
 int yb_presence_penalty(void *scores, const uint8_t *seen, int64_t n, float penalty, int dtype, void *stream);
 
+/*
+ * Decode-loop bookkeeping after one sampled token per slot, in one launch.
+ * Replaces runtime/model/inference_kernels.py:1206-1208
+ * `_update_fixed_decode_state_` (Triton kernel :1169-1204) and the torch
+ * statements it stands for (:1701-1717).  Per slot r:
+ *   active = !finished[r] && slot_rows[r] >= 0; token = active ? sampled : pad
+ *   write row = active ? slot_rows[r] : sink_rows[r];
+ *   write column = active ? row_steps[r] : maximum_new_tokens
+ *   storage[row, column] = token; dense_seen[r, token] = 1
+ *   next = row_steps[r] + active; generated_lengths[row] = next (if active)
+ *   finished_by_eos[row] |= active && token in eos_tokens
+ *   finished[r] |= active && (eos || next >= slot_caps[r])
+ *   row_steps[r] = next; row_positions[r] += active
+ *   decode_ids[r] = finished[r] ? pad : token; *useful_events += #active
+ * storage: [storage_rows, storage_stride] of storage_dtype (YB_I32 as the
+ * reference allocates it, or YB_I64), storage_cols = maximum_new_tokens + 1
+ * usable columns; dense_seen: [slots, seen_stride] bool with vocab columns;
+ * generated_lengths / finished_by_eos: [storage_rows]; the slot vectors
+ * [slots] (sampled_token and decode_ids at their row strides);
+ * useful_events a device int64 scalar.  eos_tokens: host array of
+ * eos_count (<= 8) ids.  Row indices must be distinct across active slots
+ * and sink rows (the reference's slot table guarantees it).  A token outside
+ * [0, vocab) or a write outside storage skips that store and is reported by
+ * yb_device_error() (0x201).  Capture-safe; one kernel launch.
+ */
+int yb_decode_state_update(const int64_t *sampled_token, int64_t sampled_stride, void *storage, int storage_dtype,
+                           int64_t storage_rows, int64_t storage_cols, int64_t storage_stride, uint8_t *dense_seen,
+                           int64_t seen_stride, int64_t vocab, int64_t *generated_lengths, uint8_t *finished_by_eos,
+                           uint8_t *finished, const int64_t *slot_rows, const int64_t *sink_rows,
+                           const int64_t *slot_caps, int64_t *row_steps, int64_t *row_positions, int64_t *decode_ids,
+                           int64_t decode_ids_stride, int64_t *useful_events, int64_t slots,
+                           int64_t maximum_new_tokens, int64_t pad_token, const int64_t *eos_tokens, int eos_count,
+                           void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -21,6 +21,8 @@ Python) to a scratch directory, puts it and the reference root first on
   layer (modeling_yanchor.py:349-370)
 * ``fixed_memory_physical_ring_decode_attention`` (runtime/model/
   inference_kernels.py:1881-1897)
+* the torch statements of the fixed-memory decode loop's per-step
+  bookkeeping (runtime/model/inference_kernels.py:1700-1717)
 
 on seeded inputs and writes the inputs and outputs as ``.npz`` files next to
 this script.  The GPU box never needs the reference: tests only read the
@@ -320,16 +322,77 @@ def sampling_fixtures(ik, torch):
     return out
 
 
+def _decode_loop_update_block(ik):
+    """The torch statements of the reference's per-step decode bookkeeping
+    (runtime/model/inference_kernels.py:1700-1717): the ``else`` branch of the
+    ``if`` that otherwise launches ``_update_fixed_decode_state_``.  Found in the
+    module's own source by its syntax tree, compiled, and run as written."""
+    import ast
+    import inspect
+    tree = ast.parse(inspect.getsource(ik))
+    for node in ast.walk(tree):
+        if isinstance(node, ast.If) and node.orelse and any(
+                isinstance(c, ast.Call) and getattr(c.func, 'id', None) == '_update_fixed_decode_state_'
+                for st in node.body for c in ast.walk(st)):
+            mod = ast.Module(body=node.orelse, type_ignores=[])
+            return compile(ast.fix_missing_locations(mod), ik.__file__, 'exec'), node.orelse[0].lineno
+    raise RuntimeError('decode-loop update block not found')
+
+
+def decode_state_fixtures(ik, torch):
+    """Several decode steps of the bookkeeping block on a slot table with
+    empty slots, finished rows, caps reached mid-run, two EOS ids and a row
+    whose slot empties between steps."""
+    code, line = _decode_loop_update_block(ik)
+    g = torch.Generator().manual_seed(21)
+    slots, total, max_new, vocab, pad = 11, 17, 9, 50, 0
+    eos = (7, 3)
+    st = {
+        'storage': torch.full((total + slots, max_new + 1), pad, dtype=torch.int32),
+        'dense_seen': torch.zeros(slots, vocab, dtype=torch.bool),
+        'generated_lengths': torch.zeros(total + slots, dtype=torch.long),
+        'finished_by_eos': torch.zeros(total + slots, dtype=torch.bool),
+        'finished': torch.tensor([False] * 8 + [True, False, False]),
+        'slot_rows': torch.tensor([0, 4, 2, 9, 11, 5, -1, 16, 3, 7, 1]),
+        'sink_rows': total + torch.arange(slots),
+        'slot_caps': torch.tensor([9, 3, 9, 5, 9, 2, 0, 9, 9, 4, 9]),
+        'row_steps': torch.ones(slots, dtype=torch.long),
+        'row_positions': torch.randint(100, 900, (slots,), generator=g),
+        'decode_ids': torch.randint(0, vocab, (slots, 1), generator=g),
+        'decode_useful_events': torch.zeros((), dtype=torch.long),
+    }
+    out = {'ds_init_' + k: v.clone() for k, v in st.items()}
+    out['ds_meta'] = torch.tensor([max_new, pad, *eos, line])
+    steps = 7
+    tokens = torch.randint(0, vocab, (steps, slots, 1), generator=g)
+    tokens[1, 2, 0], tokens[2, 0, 0], tokens[3, 7, 0] = 7, 3, 7    # EOS hits
+    out['ds_tokens'] = tokens
+    for t in range(steps):
+        if t == 4:
+            st['slot_rows'][3] = -1                                      # a slot emptied between steps
+        ns = dict(st, torch=torch, next_token=tokens[t].clone(), max_new_tokens=max_new, pad_token_id=pad,
+                  eos_token_ids=eos, prefill_context=None)
+        exec(code, ns)
+        for k in st:
+            st[k] = ns[k]
+        for k, v in st.items():
+            out[f'ds_{t}_{k}'] = v.clone()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--reference', required=True)
+    ap.add_argument('--only', nargs='*', help='fixture files to rewrite (default: all)')
     args = ap.parse_args()
     qwen, my, ik = _import_reference(os.path.abspath(args.reference))
     import torch
     torch.manual_seed(0)
     for name, fn in (('gdn', lambda: gdn_fixtures(qwen, torch)), ('memory', lambda: memory_fixtures(my, torch)),
                      ('sampling', lambda: sampling_fixtures(ik, torch)), ('conv', lambda: conv_fixtures(my, torch)),
-                     ('swa', lambda: swa_fixtures(ik, torch))):
+                     ('swa', lambda: swa_fixtures(ik, torch)), ('decode_state', lambda: decode_state_fixtures(ik, torch))):
+        if args.only and name not in args.only:
+            continue
         data = {k: (v.detach().cpu().numpy() if hasattr(v, 'detach') else np.asarray(v)) for k, v in fn().items()}
         path = os.path.join(HERE, f'{name}.npz')
         np.savez_compressed(path, **data)

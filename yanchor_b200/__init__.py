@@ -14,6 +14,8 @@ Operators (all CUDA, via the C ABI library libyanchor_b200.so):
   ``physical_ring_update_``, ``physical_ring_decode_attention``
 * sampling: ``greedy``, ``sample_top_k_top_p_counter``,
   ``apply_dense_presence_penalty_``
+* decode loop: ``update_fixed_decode_state_`` (per-step bookkeeping in one
+  launch) and ``FixedMemoryDecodeGraph`` (the CUDA-graph decode driver)
 * ``bind_gdn_kernels`` / ``install_memory_module`` / ``bind_memory_prefill``
   put them where the reference model code looks them up.
 """
@@ -24,6 +26,8 @@ from .swa import physical_ring_decode_attention, physical_ring_update_  # noqa: 
 from .independent_memory import MemoryState, commit_decode, committed_gqa, indexed_gqa  # noqa: F401
 from .memory_prefill import exclusive_prefix_topk, merge_topk, select_topk, sequence  # noqa: F401
 from .sampling import apply_dense_presence_penalty_, greedy, sample_top_k_top_p_counter  # noqa: F401
+from .decode_loop import (FixedMemoryDecodeGraph, resolve_recurrent_state_storage,  # noqa: F401
+                          restore_cuda_graph_cache, snapshot_cuda_graph_cache, update_fixed_decode_state_)
 from .bind import bind_gdn_kernels, bind_memory_prefill, install_memory_module  # noqa: F401
 from ._lib import LIB_PATH, YanchorError, lib  # noqa: F401
 

@@ -71,8 +71,9 @@ extern "C" {
 const char *yb_last_error(void) { return g_err; }
 int yb_abi_version(void) { return 1; }
 int yb_device_error(int clear) {
-  const int a = read_device_error(clear), b = read_device_error_idx(clear), c = read_device_error_fused(clear);
-  return a ? a : (b ? b : c);
+  const int a = read_device_error(clear), b = read_device_error_idx(clear), c = read_device_error_fused(clear),
+            d = read_device_error_loop(clear);
+  return a ? a : (b ? b : (c ? c : d));
 }
 
 int yb_gdn_recurrent_fwd(const void *q, const void *k, const void *v, int64_t q_tok_stride, int64_t k_tok_stride,
@@ -443,6 +444,40 @@ int yb_presence_penalty(void *scores, const uint8_t *seen, int64_t n, float pena
   YB_REQUIRE(dtype_ok(dtype), "presence_penalty: bad dtype");
   YB_REQUIRE(n >= 0 && (n == 0 || (scores && seen)), "presence_penalty: bad arguments");
   return launch_presence_penalty(scores, seen, n, penalty, dtype, static_cast<cudaStream_t>(stream));
+}
+
+int yb_decode_state_update(const int64_t *sampled_token, int64_t sampled_stride, void *storage, int storage_dtype,
+                           int64_t storage_rows, int64_t storage_cols, int64_t storage_stride, uint8_t *dense_seen,
+                           int64_t seen_stride, int64_t vocab, int64_t *generated_lengths, uint8_t *finished_by_eos,
+                           uint8_t *finished, const int64_t *slot_rows, const int64_t *sink_rows,
+                           const int64_t *slot_caps, int64_t *row_steps, int64_t *row_positions, int64_t *decode_ids,
+                           int64_t decode_ids_stride, int64_t *useful_events, int64_t slots,
+                           int64_t maximum_new_tokens, int64_t pad_token, const int64_t *eos_tokens, int eos_count,
+                           void *stream) {
+  YB_REQUIRE(slots >= 0 && storage_rows >= 0 && storage_cols >= 0 && vocab >= 0, "decode state: negative size");
+  YB_REQUIRE(storage_dtype == YB_I32 || storage_dtype == YB_I64, "decode state: storage must be int32 or int64");
+  YB_REQUIRE(storage_stride >= storage_cols && seen_stride >= vocab, "decode state: row strides too small");
+  YB_REQUIRE(eos_count >= 0 && (eos_count == 0 || eos_tokens), "decode state: bad EOS list");
+  YB_REQUIRE(slots == 0 || (sampled_token && storage && dense_seen && generated_lengths && finished_by_eos &&
+                            finished && slot_rows && sink_rows && slot_caps && row_steps && row_positions &&
+                            decode_ids && useful_events),
+             "decode state: null pointer");
+  if (eos_count > kMaxEos)
+    return set_error(YB_ERR_UNSUPPORTED, "decode state: %d EOS ids (at most %d)", eos_count, kMaxEos);
+  DecodeStateArgs a{};
+  a.sampled = sampled_token; a.sampled_stride = sampled_stride;
+  a.storage = storage; a.storage_i64 = storage_dtype == YB_I64;
+  a.storage_rows = storage_rows; a.storage_cols = storage_cols; a.storage_stride = storage_stride;
+  a.dense_seen = dense_seen; a.seen_stride = seen_stride; a.vocab = vocab;
+  a.generated_lengths = generated_lengths; a.finished_by_eos = finished_by_eos; a.finished = finished;
+  a.slot_rows = slot_rows; a.sink_rows = sink_rows; a.slot_caps = slot_caps;
+  a.row_steps = row_steps; a.row_positions = row_positions;
+  a.decode_ids = decode_ids; a.decode_ids_stride = decode_ids_stride; a.useful_events = useful_events;
+  a.slots = slots; a.max_new = maximum_new_tokens; a.pad = pad_token;
+  for (int e = 0; e < eos_count; ++e) a.eos[e] = eos_tokens[e];
+  a.eos_count = eos_count;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return launch_decode_state_update(a);
 }
 
 }  // extern "C"

@@ -177,6 +177,32 @@ struct GqaDecodeArgs {
 bool gqa_decode_mma_supported(int dtype, int64_t QH, int64_t G, int64_t D);
 int launch_gqa_decode_mma(const GqaDecodeArgs &a);
 
+// Decode-loop bookkeeping after a sampled token (one launch per step).
+constexpr int kMaxEos = 8;
+struct DecodeStateArgs {
+  const int64_t *sampled;         // [slots] at sampled_stride
+  int64_t sampled_stride;
+  void *storage;                  // [storage_rows, storage_stride] int32 (or int64)
+  int storage_i64;
+  int64_t storage_rows, storage_cols, storage_stride;
+  uint8_t *dense_seen;            // [slots, seen_stride] bool
+  int64_t seen_stride, vocab;
+  int64_t *generated_lengths;     // [storage_rows]
+  uint8_t *finished_by_eos;       // [storage_rows]
+  uint8_t *finished;              // [slots]
+  const int64_t *slot_rows, *sink_rows, *slot_caps;
+  int64_t *row_steps, *row_positions;
+  int64_t *decode_ids;            // [slots] at decode_ids_stride
+  int64_t decode_ids_stride;
+  int64_t *useful_events;         // device scalar
+  int64_t slots, max_new, pad;
+  int64_t eos[kMaxEos];
+  int eos_count;
+  cudaStream_t stream;
+};
+int launch_decode_state_update(const DecodeStateArgs &a);
+int read_device_error_loop(int clear);
+
 int launch_swa_ring_write(const SwaArgs &a);
 int launch_swa_decode_attention(const SwaArgs &a, void *workspace);
 int64_t swa_workspace_bytes(int64_t B, int64_t KVH, int64_t QH, int64_t W, int64_t D);
