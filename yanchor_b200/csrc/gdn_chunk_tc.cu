@@ -7,29 +7,35 @@
 // qn_i = scale/|q_i|), G the in-chunk cumulative log decay:
 //
 //   MMA1  [K;Q][K;Q]^T            -> k_i.k_j, q_i.k_j, and |k|^2, |q|^2 on the diagonal
-//   epi   L_ij = beta_i e^{G_i-G_j} kn_i kn_j k_i.k_j   (j < i),
+//   A     L_ij = beta_i e^{G_i-G_j} kn_i kn_j k_i.k_j   (j < i),
 //         P_ij = qn_i kn_j e^{G_i-G_j} q_i.k_j           (j <= i)
-//   SIMT  T = (I + L)^-1 in fp32 (16x16 blocked forward substitution)
+//   A     T = (I + L)^-1 in fp32 (16x16 blocked forward substitution)
 //   MMA2  W^T = k^T Tw^T, U^T = v^T Tu^T   with Tw_ij = T_ij beta_j e^{G_j} kn_j,
 //                                                Tu_ij = T_ij beta_j   (bf16 hi + lo)
 //   MMA3  X^T = S^T W^T, Y^T = S^T q^T                          (state bf16)
-//   epi   v_new^T = U^T - X^T
+//   B     v_new^T = U^T - X^T  (S^T in TMEM already holds e^{G_last} S^T)
 //   MMA4  O^T = v_new^T P^T
-//   MMA5  D^T = (v_new^T * e^{G_last-G} kn) k     (that operand as bf16 hi + lo)
-//   epi   S^T <- e^{G_last} S^T + D^T   (fp32 in TMEM);   o = e^{G} qn Y + O
+//   MMA5  S^T += (v_new^T * e^{G_last-G} kn) k     (that operand as bf16 hi + lo)
+//   B     o = e^{G} qn Y + O
 //
 // (the chunk form of transformers qwen3_5 modeling_qwen3_5.py:234-311 and
 // of fla's chunk_gated_delta_rule_fwd).  Every state-dependent product is
 // computed transposed ("value lanes"): TMEM lane v holds value column v, so
-// each epilogue thread owns one column of the state, of v_new and of o, and
+// each thread of group B owns one column of the state, of v_new and of o, and
 // all element-wise work stays in registers.  The state lives in TMEM as
 // fp32 for the whole sequence and enters the MMAs as a bf16 copy.
 //
 // Roles: warp 0 = TMA producer (+ gates, cumulative decay), warp 1 = TMEM
-// allocator and single-thread MMA issuer, warps 2..5 = epilogue (thread row
-// r = 32*(warp%4) + lane, the TMEM lane it may access).  Every wait is
-// bounded in time; a CTA that gives up records an error code, drains its
-// in-flight copies and MMAs, frees TMEM and exits.
+// allocator and single-thread MMA issuer, warps 2..5 = group A (the
+// state-independent work of a chunk: norms, L, P, T, Tw / Tu, W), warps 6..9
+// = group B (the state chain: v_new, the state update, o).  Thread row
+// r = 32*(warp%4) + lane is the TMEM lane it may access.  Group A works on
+// chunk c + 1 while group B finishes chunk c: MMA1 of chunk c + 1 is issued
+// right after MMA2 of chunk c, into the other of two alternating TMEM
+// regions, and the shared tiles the two groups touch are distinct or ordered
+// by the MMA barriers.
+// Every wait is bounded in time; a CTA that gives up records an error code,
+// drains its in-flight copies and MMAs, frees TMEM and exits.
 #include "common.cuh"
 #include "kernels.h"
 #include "tc.cuh"
@@ -42,40 +48,43 @@ using namespace tc;
 constexpr int C = 64;       // chunk length
 constexpr int KD = 128;     // key dim
 constexpr int VD = 128;     // value dim
-constexpr int NTHREADS = 320;   // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
-constexpr int EPI_THREADS = 256;
-constexpr int LP = 68;      // row pitch (floats) of the fp32 L matrix: 16-byte aligned rows
+constexpr int NTHREADS = 320;   // warp 0 TMA, warp 1 MMA, warps 2..5 group A, warps 6..9 group B
+constexpr int LP = 68;      // row pitch (floats) of the fp32 L and T matrices: 16-byte aligned rows
 
-// ---- shared memory map (bytes); SW128 tiles on 1024-byte boundaries ----
-constexpr uint32_t OFF_KQ0 = 0;            // [K;Q] stage 0: 128 rows x 128 cols, 2 column blocks
-constexpr uint32_t OFF_KQ1 = 32768;
-constexpr uint32_t OFF_V0 = 65536;         // V stage 0: 64 rows x 128 cols
-constexpr uint32_t OFF_V1 = 81920;
-constexpr uint32_t OFF_LF = 98304;         // L fp32 64 x LP, then Tw_lo / Tu_lo, later the o staging tile
-constexpr uint32_t OFF_TWLO = OFF_LF;      // Tw_lo bf16 64x64 (SW128), once L is solved
+// shared memory (byte offsets; SW128 tiles start on 1024-byte boundaries)
+constexpr uint32_t OFF_KQ0 = 0;            // [K;Q] stage 0: 2 column blocks of (K 64 rows, Q 64 rows)
+constexpr uint32_t OFF_KQ1 = 32768;        // stage 1
+constexpr uint32_t OFF_V = 65536;          // V 64 x 128 (one buffer: only MMA2 reads it)
+constexpr uint32_t OFF_LF = 81920;         // L fp32 64 x LP; once solved: Tw_lo / Tu_lo
+constexpr uint32_t OFF_TWLO = OFF_LF;      // Tw_lo bf16 64x64 (SW128)
 constexpr uint32_t OFF_TULO = OFF_LF + 8192;
-constexpr uint32_t OFF_TF = 115712;        // v~_lo bf16 128x64 (SW128)
-constexpr uint32_t OFF_P = 133120;         // P bf16 64x64 (SW128)
-constexpr uint32_t OFF_TW = 141312;        // Tw bf16 64x64 (SW128); solve scratch before that
-constexpr uint32_t OFF_TU = 149504;        // Tu bf16 64x64 (SW128)
-constexpr uint32_t OFF_WT = 157696;        // W^T bf16 128x64 (SW128), later v~_hi
-constexpr uint32_t OFF_VN = 174080;        // v_new^T bf16 128x64
+constexpr uint32_t OFF_TF = 99328;         // T fp32 64 x LP
+constexpr uint32_t OFF_P = 116736;         // P bf16 64x64 (SW128)
+constexpr uint32_t OFF_TW = 124928;        // Tw bf16 64x64 (SW128); solve scratch before that
+constexpr uint32_t OFF_TU = 133120;        // Tu bf16 64x64 (SW128)
+constexpr uint32_t OFF_VN = 141312;        // W^T bf16 128x64 (MMA3), then v_new^T (MMA4) of the same chunk
+constexpr uint32_t OFF_WT = OFF_VN;
+constexpr uint32_t OFF_OST = 157696;       // v~^T hi (MMA5), then the o staging tile [64][128] bf16
+constexpr uint32_t OFF_VHI = OFF_OST;      // v~^T bf16 128x64, high part
+constexpr uint32_t OFF_VLO = 174080;       // v~^T, low part
 constexpr uint32_t OFF_ST = 190464;        // S^T bf16 128x128 (2 column blocks)
-constexpr uint32_t OFF_GST = 223232;       // per stage: G, beta, e^G, e^{G_last-G} (4 x 64 floats)
-constexpr uint32_t OFF_NORM = OFF_GST + 2 * 1024;   // kn[64], qn[64]
-constexpr uint32_t OFF_BAR = OFF_NORM + 512;        // mbarriers
-constexpr uint32_t OFF_MISC = OFF_BAR + 64;         // tmem base, abort flag
+constexpr uint32_t OFF_GST = 223232;       // 3 slots: G, beta, e^G, e^{G_last-G} (4 x 64 floats)
+constexpr uint32_t OFF_NORM = OFF_GST + 3 * 1024;   // 3 slots: kn[64], qn[64]
+constexpr uint32_t OFF_BAR = OFF_NORM + 3 * 512;    // 17 mbarriers
+constexpr uint32_t OFF_MISC = OFF_BAR + 20 * 8;     // tmem base, abort flag
 constexpr uint32_t SMEM_BYTES = OFF_MISC + 16;
-static_assert(OFF_LF + 64 * LP * 4 <= OFF_TF && OFF_TF + 16384 <= OFF_P, "L / v~_lo overlap");
-static_assert(OFF_TULO + 8192 <= OFF_TF && OFF_TWLO % 1024 == 0 && OFF_TULO % 1024 == 0, "T lo tiles");
+static_assert(OFF_LF + 64 * LP * 4 <= OFF_TF && OFF_TF + 64 * LP * 4 <= OFF_P, "L / T regions");
+static_assert(OFF_TULO + 8192 <= OFF_TF && OFF_TF % 1024 == 0, "tiles inside L");
+static_assert(OFF_P % 1024 == 0 && OFF_VN % 1024 == 0 && OFF_ST % 1024 == 0 && OFF_ST + 32768 <= OFF_GST, "tiles");
+static_assert(6 * 320 * 4 <= 8192, "solve scratch fits the Tw tile");
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
-// ---- TMEM columns ----
-constexpr uint32_t T_D1 = 0;     // [K;Q][K;Q]^T 128x128 (cols 0..127); later O^T (cols 0..63)
-constexpr uint32_t T_W = 64;     // W^T, later X^T (inside D1's columns: D1 is dead by then)
-constexpr uint32_t T_U = 128;    // U^T
-constexpr uint32_t T_Y = 192;    // Y^T
-constexpr uint32_t T_DS = 256;   // D^T (128 columns)
+// TMEM columns (fp32, 128 lanes).  Chunk c uses region R(c) = c even ? T_R0 : T_R1
+// for [K;Q][K;Q]^T, then U^T (first 64 columns) and W^T / X^T (last 64).
+constexpr uint32_t T_R0 = 0;
+constexpr uint32_t T_R1 = 128;
+constexpr uint32_t T_Y = 256;    // Y^T
+constexpr uint32_t T_O = 320;    // O^T
 constexpr uint32_t T_S = 384;    // S^T fp32 state (128 columns)
 
 constexpr uint32_t ID_N64_KK = idesc_bf16(128, 64, false, false);
@@ -112,9 +121,6 @@ __device__ __forceinline__ float load_scalar(const void *p, int64_t idx, int dty
   return __half2float(static_cast<const __half *>(p)[idx]);
 }
 
-__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }   // all 8 epilogue warps
-// epilogue threads 0..63 (warps 4 and 5) only: the phases of the triangular solve
-__device__ __forceinline__ void solve_sync() { asm volatile("bar.sync 2, 64;" ::: "memory"); }
 
 __device__ __forceinline__ uint32_t to_tf32(float x) {
   uint32_t r;
@@ -156,7 +162,7 @@ __device__ __forceinline__ void store_block16(float *dst, int ld, const float ac
 }
 
 constexpr int DBG_D1 = 0, DBG_W = 16384, DBG_U = 24576, DBG_X = 32768, DBG_Y = 40960, DBG_O = 49152,
-              DBG_DS = 57344, DBG_T = 73728, DBG_NORM = 77824, DBG_TS = 78000;
+              DBG_S1 = 57344, DBG_T = 73728, DBG_NORM = 77824, DBG_TS = 78000;
 #ifdef YB_TC_DEBUG
 // Test-only: copy `n` values of TMEM row r (already in registers) into the
 // debug buffer at tile offset `off` (row-major, `n` columns).
@@ -165,11 +171,12 @@ constexpr int DBG_D1 = 0, DBG_W = 16384, DBG_U = 24576, DBG_X = 32768, DBG_Y = 4
     if (p.dbg && blockIdx.x == 0 && c == 0)                                            \
       for (int _i = 0; _i < (n); ++_i) p.dbg[(off) + r * (width) + (base) + _i] = (vals)[_i]; \
   } while (0)
-// Test-only: phase timestamps (ns since the thread started) of epilogue
-// thread 0 of CTA 0 for the first 32 chunks, 16 events per chunk.
+// Test-only: phase timestamps (ns since the thread started) of thread 0 of
+// each epilogue group of CTA 0 for the first 32 chunks, 16 events per chunk
+// (group A events 0..7, group B events 8..13).
 #define YB_DBG_TS(ev)                                                                   \
   do {                                                                                  \
-    if (p.dbg && blockIdx.x == 0 && et == 0 && c < 32)                                  \
+    if (p.dbg && blockIdx.x == 0 && r == 0 && c < 32)                                   \
       p.dbg[DBG_TS + c * 16 + (ev)] = float(globaltimer_ns() - dbg_t0);                 \
   } while (0)
 #else
@@ -195,20 +202,75 @@ __device__ __forceinline__ void st_half_bf16(uint8_t *tile, int rows, int cb, in
   }
 }
 
+// 64 values of one row as packed bf16 pairs -> one SW128 row half (jbase 0) or
+// second half (jbase 4) from 16 packed words.
+__device__ __forceinline__ void st_half_packed(uint8_t *tile, int rows, int cb, int r, int jbase, const uint32_t *pk) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    *reinterpret_cast<uint4 *>(tile + sw128_off(rows, cb, r, jbase + j)) =
+        make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+}
+
+// Named barriers of group A (warps 2..5, barrier 1) and of its threads 0..63
+// (warps 4 and 5, barrier 2: L rows and the triangular solve).  The *_and forms
+// also AND a status across the group, so that a wait that gave up ends the
+// loop in every thread of the group together (none is left at a barrier).
+__device__ __forceinline__ bool a_sync_and(bool ok) {
+  uint32_t res;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\tbar.red.and.pred po, 1, 128, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(res)
+      : "r"(uint32_t(ok))
+      : "memory");
+  return res != 0;
+}
+__device__ __forceinline__ bool solve_sync_and(bool ok) {
+  uint32_t res;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\tbar.red.and.pred po, 2, 64, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(res)
+      : "r"(uint32_t(ok))
+      : "memory");
+  return res != 0;
+}
+__device__ __forceinline__ void solve_sync() { asm volatile("bar.sync 2, 64;" ::: "memory"); }
+// group B (warps 6..9, barrier 3)
+__device__ __forceinline__ bool b_sync_and(bool ok) {
+  uint32_t res;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\tbar.red.and.pred po, 3, 128, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(res)
+      : "r"(uint32_t(ok))
+      : "memory");
+  return res != 0;
+}
+
 __global__ void __launch_bounds__(NTHREADS, 1)
     gdn_chunk_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                         const __grid_constant__ CUtensorMap map_v, const TcParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + OFF_BAR);  // [2]
-  uint64_t *empty = full + 2;                                      // [2]
-  uint64_t *mma_bar = full + 4;
-  uint64_t *epi_bar = full + 5;
-  uint64_t *done_bar = full + 6;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
+  uint64_t *full_kq = bars + 0;    // [2] K, Q tiles of a stage landed + its gates written (32 + tx)
+  uint64_t *empty_kq = bars + 2;   // [2] the stage's last MMA (MMA5) finished (1)
+  uint64_t *full_v = bars + 4;     // V landed (1 + tx)
+  uint64_t *empty_v = bars + 5;    // MMA2 read V (1)
+  uint64_t *mma1_bar = bars + 6;   // [2] [K;Q][K;Q]^T of chunk c in TMEM (c & 1 selects)
+  uint64_t *mma2_bar = bars + 8;   // W, U in TMEM
+  uint64_t *mma3_bar = bars + 9;   // X, Y in TMEM
+  uint64_t *mma45_bar = bars + 10; // O in TMEM, state updated
+  uint64_t *a_wt = bars + 11;      // group A: P and W^T tiles written (128)
+  uint64_t *b_vn = bars + 12;      // group B: v_new, v~ tiles written (128)
+  uint64_t *b_done = bars + 13;    // group B: state copy for the next MMA3 written, Y / O consumed, the
+                                   //          state scaled by the next chunk's decay (128)
+  uint64_t *done_bar = bars + 14;
+  uint64_t *a_tw = bars + 15;      // [2] group A: Tw / Tu tiles and the norms written, [K;Q][K;Q]^T
+                                   //     consumed (128; c & 1 selects)
   uint32_t *tmem_base_smem = reinterpret_cast<uint32_t *>(smem + OFF_MISC);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OFF_MISC + 4);
-  float *kn = reinterpret_cast<float *>(smem + OFF_NORM);
-  float *qn = kn + 64;
 
   const int n = blockIdx.x / p.HV, hv = blockIdx.x % p.HV;
   const int h = hv / (p.HV / p.H);
@@ -227,12 +289,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   if (tid == 0) {
     *abort_flag = (smem_u32(smem) & 1023u) ? 1 : 0;  // SW128 tiles need a 1024-byte aligned base
     if (*abort_flag) atomicCAS(&g_device_error, 0, ERR_ALIGN);
-    mbar_init(&full[0], 32);
-    mbar_init(&full[1], 32);
-    mbar_init(&empty[0], 2);
-    mbar_init(&empty[1], 2);
-    mbar_init(mma_bar, 1);
-    mbar_init(epi_bar, EPI_THREADS);
+    mbar_init(&full_kq[0], 32);
+    mbar_init(&full_kq[1], 32);
+    mbar_init(&empty_kq[0], 1);
+    mbar_init(&empty_kq[1], 1);
+    mbar_init(full_v, 1);
+    mbar_init(empty_v, 1);
+    mbar_init(&mma1_bar[0], 1);
+    mbar_init(&mma1_bar[1], 1);
+    mbar_init(mma2_bar, 1);
+    mbar_init(mma3_bar, 1);
+    mbar_init(mma45_bar, 1);
+    mbar_init(&a_tw[0], 128);
+    mbar_init(&a_tw[1], 128);
+    mbar_init(a_wt, 128);
+    mbar_init(b_vn, 128);
+    mbar_init(b_done, 128);
     mbar_init(done_bar, 1);
     mbar_fence_init();
   }
@@ -243,7 +315,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const uint32_t tmem = *tmem_base_smem;
 
   if (warp == 0) {
-    // ===================== producer =====================
+    // ===================== producer: TMA and gates =====================
     if (lane == 0) {
       prefetch_tensormap(&map_q);
       prefetch_tensormap(&map_k);
@@ -253,11 +325,23 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const bool beta_sig = p.flags & YB_GDN_BETA_SIGMOID;
     const float a_coef = gate_in ? -expf(p.A_log[hv]) : 0.f;
     const float dtb = (gate_in && p.dt_bias) ? p.dt_bias[hv] : 0.f;
-    int issued = 0;
+    int issued_kq = 0, issued_v = 0;
     for (int c = 0; c < nchunks && !*abort_flag; ++c) {
       const int s = c & 1;
-      if (c >= 2 && !mbar_wait(&empty[s], ((c >> 1) - 1) & 1, abort_flag, ERR_WAIT_EMPTY)) break;
-      // gates, masked beyond the sequence, and the cumulative decay
+      const int tok0 = int(bos + int64_t(c) * C);
+      if (c >= 2 && !mbar_wait(&empty_kq[s], ((c >> 1) - 1) & 1, abort_flag, ERR_WAIT_EMPTY)) break;
+      if (lane == 0) {
+        uint8_t *kq = smem + (s ? OFF_KQ1 : OFF_KQ0);
+        mbar_expect_tx(&full_kq[s], 4 * 8192);
+#pragma unroll
+        for (int cb = 0; cb < 2; ++cb) {
+          tma_load_3d(kq + cb * 16384, &map_k, &full_kq[s], cb * 64, h, tok0);
+          tma_load_3d(kq + cb * 16384 + 8192, &map_q, &full_kq[s], cb * 64, h, tok0);
+        }
+      }
+      issued_kq = c + 1;
+      // gates, masked beyond the sequence, and the cumulative decay (slot c % 3:
+      // its previous user, chunk c - 3, finished before this stage came free)
       float gv[2], bv[2];
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
@@ -284,7 +368,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
       gv[1] += __shfl_sync(0xffffffffu, gv[0], 31);
       const float glast = __shfl_sync(0xffffffffu, gv[1], 31);
-      float *gst = reinterpret_cast<float *>(smem + OFF_GST + s * 1024);
+      float *gst = reinterpret_cast<float *>(smem + OFF_GST + (c % 3) * 1024);
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         const int i = lane + 32 * half;
@@ -294,178 +378,141 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         gst[192 + i] = expf(glast - gv[half]);
       }
       __syncwarp();
+      mbar_arrive(&full_kq[s]);
+      // V of chunk c once MMA2 of chunk c - 1 has read the buffer
+      if (c >= 1 && !mbar_wait(empty_v, (c - 1) & 1, abort_flag, ERR_WAIT_EMPTY)) break;
       if (lane == 0) {
-        uint8_t *kq = smem + (s ? OFF_KQ1 : OFF_KQ0);
-        uint8_t *vt = smem + (s ? OFF_V1 : OFF_V0);
-        const int tok0 = int(bos + int64_t(c) * C);
-        mbar_arrive_expect_tx(&full[s], 6 * 8192);
+        mbar_arrive_expect_tx(full_v, 2 * 8192);
 #pragma unroll
-        for (int cb = 0; cb < 2; ++cb) {
-          tma_load_3d(kq + cb * 16384, &map_k, &full[s], cb * 64, h, tok0);
-          tma_load_3d(kq + cb * 16384 + 8192, &map_q, &full[s], cb * 64, h, tok0);
-          tma_load_3d(vt + cb * 8192, &map_v, &full[s], cb * 64, hv, tok0);
-        }
-      } else {
-        mbar_arrive(&full[s]);
+        for (int cb = 0; cb < 2; ++cb) tma_load_3d(smem + OFF_V + cb * 8192, &map_v, full_v, cb * 64, hv, tok0);
       }
-      issued = c + 1;
+      issued_v = c + 1;
     }
-    // drain: every issued stage must have landed before the CTA may exit
-    for (int c = (issued > 2 ? issued - 2 : 0); c < issued; ++c) {
-      mbar_wait(&full[c & 1], (c >> 1) & 1, abort_flag, ERR_WAIT_FULL);
-    }
+    // drain: every issued copy must have landed before the CTA may exit (bounded
+    // in time, but not cut short by another role's abort)
+    volatile int drain_flag = 0;
+    for (int c = (issued_kq > 2 ? issued_kq - 2 : 0); c < issued_kq; ++c)
+      mbar_wait(&full_kq[c & 1], (c >> 1) & 1, &drain_flag, ERR_WAIT_FULL);
+    if (issued_v > 0) mbar_wait(full_v, (issued_v - 1) & 1, &drain_flag, ERR_WAIT_FULL);
   } else if (warp == 1) {
-    // ===================== MMA issuer =====================
-    int epi_phase = 0, ok = 1;
-    auto wait_epi = [&]() {
-      ok = ok && mbar_wait(epi_bar, epi_phase & 1, abort_flag, ERR_WAIT_EPI);
-      ++epi_phase;
-      tc_fence_after();
-      return ok;
-    };
+    // ===================== MMA issuer (one thread) =====================
     if (lane == 0) {
-      wait_epi();  // initial state staged
-      for (int c = 0; c < nchunks && ok; ++c) {
-        const int s = c & 1;
-        const uint32_t kq = smem_u32(smem + (s ? OFF_KQ1 : OFF_KQ0));
-        const uint32_t vt = smem_u32(smem + (s ? OFF_V1 : OFF_V0));
-        if (!mbar_wait(&full[s], (c >> 1) & 1, abort_flag, ERR_WAIT_FULL)) break;
+      bool ok = true;
+      auto wait = [&](uint64_t *bar, uint32_t parity, int code) {
+        ok = ok && mbar_wait(bar, parity, abort_flag, code);
         tc_fence_after();
-        // MMA1: [K;Q] [K;Q]^T  (M=128, N=128, K=128)
+        return ok;
+      };
+      auto mma1 = [&](int c) {   // [K;Q] [K;Q]^T  (M=128, N=128, K=128) into R(c)
+        const uint32_t kq = smem_u32(smem + ((c & 1) ? OFF_KQ1 : OFF_KQ0));
+        const uint32_t d = tmem + ((c & 1) ? T_R1 : T_R0);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          mma_bf16(tmem + T_D1, sdesc(kq + off, 16, 1024), sdesc(kq + off, 16, 1024), ID_N128_KK, kk > 0);
+          mma_bf16(d, sdesc(kq + off, 16, 1024), sdesc(kq + off, 16, 1024), ID_N128_KK, kk > 0);
         }
-        mma_commit(mma_bar);
-        if (!wait_epi()) break;
-        // MMA2: W^T = k^T (Tw_hi + Tw_lo)^T ;  U^T = v^T (Tu_hi + Tu_lo)^T   (M=128, N=64, K=64)
+        mma_commit(&mma1_bar[c & 1]);
+      };
+      if (nchunks > 0 && wait(&full_kq[0], 0, ERR_WAIT_FULL)) mma1(0);
+      for (int c = 0; c < nchunks && ok; ++c) {
+        const int s = c & 1;
+        const uint32_t kq = smem_u32(smem + (s ? OFF_KQ1 : OFF_KQ0));
+        const uint32_t R = tmem + (s ? T_R1 : T_R0);
+        // MMA2: U^T = v^T (Tu_hi + Tu_lo)^T -> R ;  W^T = k^T (Tw_hi + Tw_lo)^T -> R + 64   (M=128, N=64, K=64)
+        if (!wait(&a_tw[s], (c >> 1) & 1, ERR_WAIT_EPI) || !wait(full_v, c & 1, ERR_WAIT_FULL)) break;
+        const uint32_t vt = smem_u32(smem + OFF_V);
         const uint32_t tw = smem_u32(smem + OFF_TW), tu = smem_u32(smem + OFF_TU);
         const uint32_t twl = smem_u32(smem + OFF_TWLO), tul = smem_u32(smem + OFF_TULO);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          mma_bf16(tmem + T_W, sdesc(kq + kk * 2048, 16384, 1024), sdesc(tw + kk * 32, 16, 1024), ID_N64_MK, kk > 0);
-          mma_bf16(tmem + T_U, sdesc(vt + kk * 2048, 8192, 1024), sdesc(tu + kk * 32, 16, 1024), ID_N64_MK, kk > 0);
+          mma_bf16(R + 64, sdesc(kq + kk * 2048, 16384, 1024), sdesc(tw + kk * 32, 16, 1024), ID_N64_MK, kk > 0);
+          mma_bf16(R, sdesc(vt + kk * 2048, 8192, 1024), sdesc(tu + kk * 32, 16, 1024), ID_N64_MK, kk > 0);
         }
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          mma_bf16(tmem + T_W, sdesc(kq + kk * 2048, 16384, 1024), sdesc(twl + kk * 32, 16, 1024), ID_N64_MK, true);
-          mma_bf16(tmem + T_U, sdesc(vt + kk * 2048, 8192, 1024), sdesc(tul + kk * 32, 16, 1024), ID_N64_MK, true);
+          mma_bf16(R + 64, sdesc(kq + kk * 2048, 16384, 1024), sdesc(twl + kk * 32, 16, 1024), ID_N64_MK, true);
+          mma_bf16(R, sdesc(vt + kk * 2048, 8192, 1024), sdesc(tul + kk * 32, 16, 1024), ID_N64_MK, true);
         }
-        mma_commit(mma_bar);
-        if (!wait_epi()) break;
-        // MMA3: X^T = S^T W^T ;  Y^T = S^T q^T   (M=128, N=64, K=128)
+        mma_commit(mma2_bar);
+        mma_commit(empty_v);
+        // MMA1 of chunk c + 1 into R(c + 1): group B read U, X of chunk c - 1 there before its b_vn;
+        // the stage's copy was issued a whole group-A phase ago (after MMA5 of chunk c - 1)
+        if (c + 1 < nchunks) {
+          if (!wait(&full_kq[s ^ 1], ((c + 1) >> 1) & 1, ERR_WAIT_FULL)) break;
+          mma1(c + 1);
+        }
+        // MMA3: X^T = S^T W^T -> R + 64 ;  Y^T = S^T q^T -> T_Y   (M=128, N=64, K=128)
+        if (!wait(a_wt, c & 1, ERR_WAIT_EPI) || !wait(b_done, c & 1, ERR_WAIT_EPI)) break;
         const uint32_t st = smem_u32(smem + OFF_ST), wt = smem_u32(smem + OFF_WT);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint64_t a = sdesc(st + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
-          mma_bf16(tmem + T_W, a, sdesc(wt + kk * 2048, 16384, 1024), ID_N64_KM, kk > 0);
+          mma_bf16(R + 64, a, sdesc(wt + kk * 2048, 16384, 1024), ID_N64_KM, kk > 0);
           mma_bf16(tmem + T_Y, a, sdesc(kq + 8192 + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024), ID_N64_KK,
                    kk > 0);
         }
-        mma_commit(mma_bar);
-        if (!wait_epi()) break;
-        // MMA4: O^T = v_new^T P^T (N=64, K=64) ;  MMA5: D^T = (v~_hi + v~_lo)^T k (N=128, K=64)
+        mma_commit(mma3_bar);
+        // MMA4: O^T = v_new^T P^T (N=64, K=64) ;  MMA5: S^T += (v~_hi + v~_lo)^T k (N=128, K=64), the
+        // state already scaled by the chunk's decay (group B did it with the previous state copy)
+        if (!wait(b_vn, c & 1, ERR_WAIT_EPI)) break;
         const uint32_t vn = smem_u32(smem + OFF_VN), pp = smem_u32(smem + OFF_P);
-        const uint32_t vlo = smem_u32(smem + OFF_TF);
+        const uint32_t vhi = smem_u32(smem + OFF_VHI), vlo = smem_u32(smem + OFF_VLO);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          mma_bf16(tmem + T_D1, sdesc(vn + kk * 32, 16, 1024), sdesc(pp + kk * 32, 16, 1024), ID_N64_KK, kk > 0);
-          mma_bf16(tmem + T_DS, sdesc(wt + kk * 32, 16, 1024), sdesc(kq + kk * 2048, 16384, 1024), ID_N128_KM,
-                   kk > 0);
+          mma_bf16(tmem + T_O, sdesc(vn + kk * 32, 16, 1024), sdesc(pp + kk * 32, 16, 1024), ID_N64_KK, kk > 0);
+          mma_bf16(tmem + T_S, sdesc(vhi + kk * 32, 16, 1024), sdesc(kq + kk * 2048, 16384, 1024), ID_N128_KM,
+                   true);
         }
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          mma_bf16(tmem + T_DS, sdesc(vlo + kk * 32, 16, 1024), sdesc(kq + kk * 2048, 16384, 1024), ID_N128_KM,
+          mma_bf16(tmem + T_S, sdesc(vlo + kk * 32, 16, 1024), sdesc(kq + kk * 2048, 16384, 1024), ID_N128_KM,
                    true);
-        mma_commit(mma_bar);
-        mma_commit(&empty[s]);
-        if (!wait_epi()) break;
+        mma_commit(mma45_bar);
+        mma_commit(&empty_kq[s]);
       }
       // all issued MMAs finished before TMEM is released
       mma_commit(done_bar);
       mbar_wait(done_bar, 0, abort_flag, ERR_WAIT_DONE);
     }
     __syncwarp();
-  } else {
-    // ===================== epilogue (256 threads, 8 warps) =====================
-    // Warps 2..5 (half 0) and 6..9 (half 1) each cover the four TMEM lane
-    // quarters, so thread (r, half) owns tile row r and, of every row, the
-    // column half `half`: 32 of 64 columns, or 64 of the state's 128.
-    const int r = (warp & 3) * 32 + lane;            // TMEM lane == tile row
-    const int half = (warp - 2) >> 2;
-    const int et = half * 128 + r;                   // 0..255
-    const int j0 = 32 * half;                        // first of this thread's 32 columns
+  } else if (warp < 6) {
+    // ===================== group A: the state-independent work of a chunk =====================
+    // thread r = TMEM lane r: rows r < 64 are L rows (and the solve), rows 64..127 P rows
+    const int r = (warp & 3) * 32 + lane;
 #ifdef YB_TC_DEBUG
     const uint64_t dbg_t0 = globaltimer_ns();
 #endif
     const uint32_t lane_base = tmem + (uint32_t((warp & 3) * 32) << 16);
     const bool l2 = p.flags & YB_GDN_QK_L2NORM;
-    uint8_t *st_tile = smem + OFF_ST;
     float *LF = reinterpret_cast<float *>(smem + OFF_LF);
-    int mma_phase = 0;
     bool ok = true;
-    auto wait_mma = [&]() {
-      ok = ok && mbar_wait(mma_bar, mma_phase & 1, abort_flag, ERR_WAIT_MMA);
-      ++mma_phase;
-      tc_fence_after();
-      return ok;
-    };
-    auto signal_mma = [&]() {
+    auto signal = [&](uint64_t *bar) {
       fence_async_smem();
       tc_fence_before();
-      mbar_arrive(epi_bar);
+      mbar_arrive(bar);
     };
-
-    // ---- initial state: thread r owns value column v = r; half h the key rows 64h .. 64h+63 ----
-    {
-      float row[32];
-#pragma unroll
-      for (int qq = 0; qq < 2; ++qq) {
-        const int q4 = 2 * half + qq;
-#pragma unroll
-        for (int d = 0; d < 32; ++d) {
-          const int dd = q4 * 32 + d;
-          row[d] = p.h0 ? (trans ? p.h0[head + int64_t(r) * KD + dd] : p.h0[head + int64_t(dd) * VD + r]) : 0.f;
-        }
-        tmem_st32(lane_base + T_S + q4 * 32, row);
-        if (nchunks == 0 && p.ht) {
-#pragma unroll
-          for (int d = 0; d < 32; ++d) {
-            const int dd = q4 * 32 + d;
-            if (trans) p.ht[head + int64_t(r) * KD + dd] = row[d];
-            else p.ht[head + int64_t(dd) * VD + r] = row[d];
-          }
-        }
-        st_half_bf16(st_tile, 128, q4 >> 1, r, (q4 & 1) * 4, row);
-      }
-      tmem_wait_st();
-      signal_mma();
-    }
-
     for (int c = 0; c < nchunks && ok; ++c) {
       const int s = c & 1;
-      const float *gst = reinterpret_cast<const float *>(smem + OFF_GST + s * 1024);
-      const float *G = gst, *BT = gst + 64, *EG = gst + 128, *TAIL = gst + 192;
-      const int m = int(len - int64_t(c) * C < C ? len - int64_t(c) * C : C);
+      const uint32_t R = s ? T_R1 : T_R0;
+      const float *gst = reinterpret_cast<const float *>(smem + OFF_GST + (c % 3) * 1024);
+      const float *G = gst, *BT = gst + 64, *EG = gst + 128;
+      float *kn = reinterpret_cast<float *>(smem + OFF_NORM + (c % 3) * 512);
+      float *qn = kn + 64;
       YB_DBG_TS(0);
-      if (!mbar_wait(&full[s], (c >> 1) & 1, abort_flag, ERR_WAIT_FULL)) break;
+      ok = mbar_wait(&full_kq[s], (c >> 1) & 1, abort_flag, ERR_WAIT_FULL);
+      ok = ok && mbar_wait(&mma1_bar[s], (c >> 1) & 1, abort_flag, ERR_WAIT_MMA);
+      tc_fence_after();
       YB_DBG_TS(1);
-      if (!wait_mma()) break;   // MMA1 done
-      YB_DBG_TS(2);
-      // ---------- step 2: norms (diagonal of D1), L, P ----------
-      float d1[32];   // row r of D1, columns j0 .. j0+31
-      tmem_ld32(lane_base + T_D1 + uint32_t(j0), d1);
-      if (half == 0) {
-        float dg[32];   // the 32 columns holding this thread's own diagonal entry
-        tmem_ld32(lane_base + T_D1 + uint32_t(r & ~31), dg);
+      // ---------- norms from the diagonal of [K;Q][K;Q]^T ----------
+      if (ok) {
+        float dg[32];
+        tmem_ld32(lane_base + R + uint32_t(r & ~31), dg);
         tmem_wait_ld();
-        YB_DBG_TS(13);
 #ifdef YB_TC_DEBUG
         if (p.dbg && blockIdx.x == 0 && c == 0) {
           float full_row[32];
           for (int q4 = 0; q4 < 4; ++q4) {
-            tmem_ld32(lane_base + T_D1 + q4 * 32, full_row);
+            tmem_ld32(lane_base + R + q4 * 32, full_row);
             tmem_wait_ld();
             for (int t = 0; t < 32; ++t) p.dbg[DBG_D1 + r * 128 + q4 * 32 + t] = full_row[t];
           }
@@ -477,44 +524,34 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const float nrm = l2 ? rsqrtf(diag + 1e-6f) : 1.f;
         if (r < 64) kn[r] = nrm;
         else qn[r - 64] = nrm * p.scale;
-      } else {
-        tmem_wait_ld();
       }
-      epi_sync();
-      YB_DBG_TS(14);
+      if (!(ok = a_sync_and(ok))) break;
+      YB_DBG_TS(2);
+      uint32_t pk[32];   // threads r >= 64: P row r - 64 as packed bf16 pairs, stored after MMA2
       if (r < 64) {
-        // row r of L, columns j0 .. j0+31 (branch-free mask; the exponent is
-        // clamped so masked entries stay finite)
+        // ---------- L row r (branch-free mask; the exponent is clamped so masked entries stay finite) ----------
         const int i = r;
         const float ci = BT[i] * kn[i], gi = G[i];
+#pragma unroll 1
+        for (int hf = 0; hf < 2; ++hf) {
+          float d1[32];
+          tmem_ld32(lane_base + R + uint32_t(32 * hf), d1);
+          tmem_wait_ld();
 #pragma unroll
-        for (int j4 = 0; j4 < 8; ++j4) {
-          float4 v4;
-          float *vv = reinterpret_cast<float *>(&v4);
+          for (int j4 = 0; j4 < 8; ++j4) {
+            float4 v4;
+            float *vv = reinterpret_cast<float *>(&v4);
 #pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const int jj = 4 * j4 + t, j = j0 + jj;
-            vv[t] = ci * kn[j] * __expf(fminf(gi - G[j], 0.f)) * d1[jj] * float(j < i);
+            for (int t = 0; t < 4; ++t) {
+              const int jj = 4 * j4 + t, j = 32 * hf + jj;
+              vv[t] = ci * kn[j] * __expf(fminf(gi - G[j], 0.f)) * d1[jj] * float(j < i);
+            }
+            *reinterpret_cast<float4 *>(LF + i * LP + 32 * hf + 4 * j4) = v4;
           }
-          *reinterpret_cast<float4 *>(LF + i * LP + j0 + 4 * j4) = v4;
         }
-      } else {
-        // row r-64 of P, columns j0 .. j0+31
-        const int i = r - 64;
-        const float ci = qn[i], gi = G[i];
-        float pr[32];
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          const int j = j0 + jj;
-          pr[jj] = ci * kn[j] * __expf(fminf(gi - G[j], 0.f)) * d1[jj] * float(j <= i);
-        }
-        st_half_bf16(smem + OFF_P, 64, 0, i, 4 * half, pr);
-      }
-      YB_DBG_TS(15);
-      epi_sync();
-      YB_DBG_TS(3);
-      if (r < 64 && half == 0) {
-        // warps 4 and 5: T = (I + L)^-1 (solve_sync spans exactly these 64 threads)
+        solve_sync();
+        YB_DBG_TS(3);
+        {
         // ---- T = (I + L)^-1 by 16x16 blocks: T_ii = D_i (diagonal inverses),
         //      T_ij = -sum_{m=j}^{i-1} M_im T_mj with M_im = D_i L_im ----
         float *TF = reinterpret_cast<float *>(smem + OFF_TF);   // T fp32, pitch LP
@@ -550,19 +587,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         solve_sync();
         // distance 1: T_(i,i-1) = -M_(i,i-1) D_(i-1),  i = 1..3
-        for (int i = 1 + sw; i < 4; i += 2) {
+        for (int i1 = 1 + sw; i1 < 4; i1 += 2) {
           float acc[2][4] = {};
-          block_mma16_tf32(acc, MB + (i - 1) * 320, 20, TF + (i - 1) * 16 * LP + (i - 1) * 16, LP);
-          store_block16(TF + i * 16 * LP + (i - 1) * 16, LP, acc, -1.f);
+          block_mma16_tf32(acc, MB + (i1 - 1) * 320, 20, TF + (i1 - 1) * 16 * LP + (i1 - 1) * 16, LP);
+          store_block16(TF + i1 * 16 * LP + (i1 - 1) * 16, LP, acc, -1.f);
         }
         solve_sync();
         // distance 2: T_(i,i-2) = -(M_(i,i-2) D_(i-2) + M_(i,i-1) T_(i-1,i-2)),  i = 2 (warp 0), 3 (warp 1)
         {
-          const int i = 2 + sw;
+          const int i2 = 2 + sw;
           float acc[2][4] = {};
-          block_mma16_tf32(acc, MB + (i + 1) * 320, 20, TF + (i - 2) * 16 * LP + (i - 2) * 16, LP);
-          block_mma16_tf32(acc, MB + (i - 1) * 320, 20, TF + (i - 1) * 16 * LP + (i - 2) * 16, LP);
-          store_block16(TF + i * 16 * LP + (i - 2) * 16, LP, acc, -1.f);
+          block_mma16_tf32(acc, MB + (i2 + 1) * 320, 20, TF + (i2 - 2) * 16 * LP + (i2 - 2) * 16, LP);
+          block_mma16_tf32(acc, MB + (i2 - 1) * 320, 20, TF + (i2 - 1) * 16 * LP + (i2 - 2) * 16, LP);
+          store_block16(TF + i2 * 16 * LP + (i2 - 2) * 16, LP, acc, -1.f);
         }
         solve_sync();
         // distance 3: T_(3,0) = -(M_30 D_0 + M_31 T_10 + M_32 T_20)
@@ -573,155 +610,246 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           block_mma16_tf32(acc, MB + 2 * 320, 20, TF + 32 * LP, LP);
           store_block16(TF + 48 * LP, LP, acc, -1.f);
         }
+        }
+      } else {
+        // ---------- P row r - 64, held packed until MMA4 of chunk c - 1 has read the tile ----------
+        const int i = r - 64;
+        const float ci = qn[i], gi = G[i];
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          float d1[32];
+          tmem_ld32(lane_base + R + uint32_t(32 * hf), d1);
+          tmem_wait_ld();
+#pragma unroll
+          for (int t = 0; t < 16; ++t) {
+            const int j = 32 * hf + 2 * t;
+            const float p0 = ci * kn[j] * __expf(fminf(gi - G[j], 0.f)) * d1[2 * t] * float(j <= i);
+            const float p1 = ci * kn[j + 1] * __expf(fminf(gi - G[j + 1], 0.f)) * d1[2 * t + 1] * float(j + 1 <= i);
+            pk[16 * hf + t] = pack_bf16x2(p0, p1);
+          }
+        }
       }
-      epi_sync();
+      if (!(ok = a_sync_and(ok))) break;
       YB_DBG_TS(4);
-      // Tw (rows 0..63 of threads r < 64) and Tu (threads r >= 64) from T, as bf16 tiles
+      // ---------- Tw (rows of threads r < 64) and Tu (r >= 64) from T, as bf16 hi + lo tiles ----------
       {
         const float *TF = reinterpret_cast<const float *>(smem + OFF_TF);
         const int i = r & 63;
-        float rowv[32];
+#pragma unroll 1
+        for (int hf = 0; hf < 2; ++hf) {
+          float rowv[32];
 #pragma unroll
-        for (int j4 = 0; j4 < 8; ++j4) {
-          const float4 t4 = *reinterpret_cast<const float4 *>(TF + i * LP + j0 + 4 * j4);
-          rowv[4 * j4] = t4.x;
-          rowv[4 * j4 + 1] = t4.y;
-          rowv[4 * j4 + 2] = t4.z;
-          rowv[4 * j4 + 3] = t4.w;
+          for (int j4 = 0; j4 < 8; ++j4) {
+            const float4 t4 = *reinterpret_cast<const float4 *>(TF + i * LP + 32 * hf + 4 * j4);
+            rowv[4 * j4] = t4.x;
+            rowv[4 * j4 + 1] = t4.y;
+            rowv[4 * j4 + 2] = t4.z;
+            rowv[4 * j4 + 3] = t4.w;
+          }
+#ifdef YB_TC_DEBUG
+          if (p.dbg && blockIdx.x == 0 && c == 0 && r < 64)
+            for (int jj = 0; jj < 32; ++jj) p.dbg[DBG_T + r * 64 + 32 * hf + jj] = rowv[jj];
+#endif
+          // both factors enter MMA2 as bf16 hi + lo: a single bf16 rounding of T
+          // alone costs ~2e-3 relative on the state
+          if (r < 64) {
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) {
+              const int j = 32 * hf + jj;
+              rowv[jj] *= BT[j] * EG[j] * kn[j];
+            }
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) rowv[jj] *= BT[32 * hf + jj];
+          }
+          st_half_bf16(smem + (r < 64 ? OFF_TW : OFF_TU), 64, 0, i, 4 * hf, rowv);
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) rowv[jj] -= __bfloat162float(__float2bfloat16_rn(rowv[jj]));
+          st_half_bf16(smem + (r < 64 ? OFF_TWLO : OFF_TULO), 64, 0, i, 4 * hf, rowv);
         }
 #ifdef YB_TC_DEBUG
-        if (p.dbg && blockIdx.x == 0 && c == 0) {
-          if (r < 64)
-            for (int jj = 0; jj < 32; ++jj) p.dbg[DBG_T + r * 64 + j0 + jj] = rowv[jj];
-          if (half == 0) p.dbg[DBG_NORM + r] = r < 64 ? kn[r] : qn[r - 64];
-        }
+        if (p.dbg && blockIdx.x == 0 && c == 0) p.dbg[DBG_NORM + r] = r < 64 ? kn[r] : qn[r - 64];
 #endif
-        // both factors enter MMA2 as bf16 hi + lo: a single bf16 rounding of T
-        // alone costs ~2e-3 relative on the state
-        if (r < 64) {
-#pragma unroll
-          for (int jj = 0; jj < 32; ++jj) rowv[jj] *= BT[j0 + jj] * EG[j0 + jj] * kn[j0 + jj];
-        } else {
-#pragma unroll
-          for (int jj = 0; jj < 32; ++jj) rowv[jj] *= BT[j0 + jj];
-        }
-        st_half_bf16(smem + (r < 64 ? OFF_TW : OFF_TU), 64, 0, i, 4 * half, rowv);
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) rowv[jj] -= __bfloat162float(__float2bfloat16_rn(rowv[jj]));
-        st_half_bf16(smem + (r < 64 ? OFF_TWLO : OFF_TULO), 64, 0, i, 4 * half, rowv);
       }
-      signal_mma();
+      signal(&a_tw[s]);
       YB_DBG_TS(5);
-      // ---------- step 4: W^T -> smem (MN-major B operand of MMA3) ----------
-      if (!wait_mma()) break;
+      // ---------- P, and W^T (MN-major B operand of MMA3) over the v_new tile ----------
+      // MMA2 of this chunk was issued after MMA4 / MMA5 of the previous one, so
+      // once it is done the P and v_new tiles of chunk c - 1 have been read
+      ok = mbar_wait(mma2_bar, c & 1, abort_flag, ERR_WAIT_MMA);
+      tc_fence_after();
+      if (!(ok = a_sync_and(ok))) break;
       YB_DBG_TS(6);
-      {
+      if (r >= 64) {
+        st_half_packed(smem + OFF_P, 64, 0, r - 64, 0, pk);
+        st_half_packed(smem + OFF_P, 64, 0, r - 64, 4, pk + 16);
+      }
+#pragma unroll 1
+      for (int hf = 0; hf < 2; ++hf) {
         float w[32];
-        tmem_ld32(lane_base + T_W + uint32_t(j0), w);
+        tmem_ld32(lane_base + R + 64 + uint32_t(32 * hf), w);
         tmem_wait_ld();
-        YB_DBG_ROW(DBG_W, 64, j0, 32, w);
-        st_half_bf16(smem + OFF_WT, 128, 0, r, 4 * half, w);
+        YB_DBG_ROW(DBG_W, 64, 32 * hf, 32, w);
+        st_half_bf16(smem + OFF_WT, 128, 0, r, 4 * hf, w);
       }
-      signal_mma();
+      signal(a_wt);
       YB_DBG_TS(7);
-      // ---------- step 6: v_new = U - X ----------
-      if (!wait_mma()) break;
-      YB_DBG_TS(8);
-      {
-        float u[32], x[32];
-        tmem_ld32(lane_base + T_U + uint32_t(j0), u);
-        tmem_ld32(lane_base + T_W + uint32_t(j0), x);
-        tmem_wait_ld();
-        YB_DBG_ROW(DBG_U, 64, j0, 32, u);
-        YB_DBG_ROW(DBG_X, 64, j0, 32, x);
+    }
+  } else {
+    // ===================== group B: the state chain of a chunk =====================
+    // thread r = TMEM lane r = value column r of the state, of v_new and of o
+    const int r = (warp & 3) * 32 + lane;
+#ifdef YB_TC_DEBUG
+    const uint64_t dbg_t0 = globaltimer_ns();
+#endif
+    const uint32_t lane_base = tmem + (uint32_t((warp & 3) * 32) << 16);
+    uint8_t *st_tile = smem + OFF_ST;
+    bool ok = true;
+    auto signal = [&](uint64_t *bar) {
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(bar);
+    };
+    // ---- initial state: bf16 copy for the first MMA3, and fp32 into TMEM scaled by
+    //      the first chunk's decay (MMA5 of a chunk accumulates into e^{G_last} S) ----
+    float decay0 = 1.f;
+    if (nchunks > 0) {
+      ok = mbar_wait(&full_kq[0], 0, abort_flag, ERR_WAIT_FULL);   // gates of chunk 0
+      decay0 = reinterpret_cast<const float *>(smem + OFF_GST)[128 + 63];
+    }
+#pragma unroll 1
+    for (int q4 = 0; q4 < 4; ++q4) {
+      float row[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) u[i] -= x[i];
-        st_half_bf16(smem + OFF_VN, 128, 0, r, 4 * half, u);
-        // v~ = v_new e^{G_last-G} kn enters the state update as bf16 hi + lo
-        // parts (its rounding is what limits the fp32 state's accuracy)
-#pragma unroll
-        for (int i = 0; i < 32; ++i) u[i] *= TAIL[j0 + i] * kn[j0 + i];
-        st_half_bf16(smem + OFF_WT, 128, 0, r, 4 * half, u);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) u[i] -= __bfloat162float(__float2bfloat16_rn(u[i]));
-        st_half_bf16(smem + OFF_TF, 128, 0, r, 4 * half, u);
+      for (int d = 0; d < 32; ++d) {
+        const int dd = q4 * 32 + d;
+        row[d] = p.h0 ? (trans ? p.h0[head + int64_t(r) * KD + dd] : p.h0[head + int64_t(dd) * VD + r]) : 0.f;
       }
-      signal_mma();
-      YB_DBG_TS(9);
-      // ---------- step 8: state update first (it gates the next chunk), then o ----------
-      if (!wait_mma()) break;
-      YB_DBG_TS(10);
-      uint32_t opk[16];   // this thread's o column, tokens j0 + 2t and j0 + 2t + 1, as packed bf16 pairs
-      {
-        float y[32], oo[32];
-        tmem_ld32(lane_base + T_Y + uint32_t(j0), y);
-        tmem_ld32(lane_base + T_D1 + uint32_t(j0), oo);
-        tmem_wait_ld();
-        YB_DBG_ROW(DBG_Y, 64, j0, 32, y);
-        YB_DBG_ROW(DBG_O, 64, j0, 32, oo);
+      if (nchunks == 0 && p.ht) {
 #pragma unroll
-        for (int t = 0; t < 16; ++t) {
-          const int a = j0 + 2 * t;
-          opk[t] = pack_bf16x2(EG[a] * qn[a] * y[2 * t] + oo[2 * t], EG[a + 1] * qn[a + 1] * y[2 * t + 1] + oo[2 * t + 1]);
+        for (int d = 0; d < 32; ++d) {
+          const int dd = q4 * 32 + d;
+          if (trans) p.ht[head + int64_t(r) * KD + dd] = row[d];
+          else p.ht[head + int64_t(dd) * VD + r] = row[d];
         }
       }
-      {
-        const float decay = EG[63];   // e^{G_last}
-        const bool last = c == nchunks - 1;
+      st_half_bf16(st_tile, 128, q4 >> 1, r, (q4 & 1) * 4, row);
 #pragma unroll
-        for (int qq = 0; qq < 2; ++qq) {
-          const int q4 = 2 * half + qq;
-          float sv[32], dv[32];
+      for (int d = 0; d < 32; ++d) row[d] *= decay0;
+      tmem_st32(lane_base + T_S + q4 * 32, row);
+    }
+    tmem_wait_st();
+    if (ok) signal(b_done);
+
+    for (int c = 0; c < nchunks; ++c) {
+      // every thread of the group has finished the previous chunk (its reads of
+      // the o staging tile included); a wait that gave up ends the loop for all
+      if (!(ok = b_sync_and(ok))) break;
+      const int s = c & 1;
+      const uint32_t R = s ? T_R1 : T_R0;
+      const float *gst = reinterpret_cast<const float *>(smem + OFF_GST + (c % 3) * 1024);
+      const float *EG = gst + 128, *TAIL = gst + 192;
+      const float *kn = reinterpret_cast<const float *>(smem + OFF_NORM + (c % 3) * 512);
+      const float *qn = kn + 64;
+      const int m = int(len - int64_t(c) * C < C ? len - int64_t(c) * C : C);
+      const bool last = c == nchunks - 1;
+      YB_DBG_TS(8);
+      ok = mbar_wait(mma3_bar, c & 1, abort_flag, ERR_WAIT_MMA);
+      // the chunk's gates and norms: acquired from group A's release (it wrote the
+      // norms after acquiring the gates); that barrier's next phase is chunk c + 2
+      ok = ok && mbar_wait(&a_tw[s], (c >> 1) & 1, abort_flag, ERR_WAIT_EPI);
+      tc_fence_after();
+      YB_DBG_TS(9);
+      // ---------- v_new = U - X; v~ = v_new e^{G_last-G} kn as bf16 hi + lo ----------
+      if (ok) {
+#pragma unroll 1
+        for (int hf = 0; hf < 2; ++hf) {
+          float u[32], x[32];
+          tmem_ld32(lane_base + R + uint32_t(32 * hf), u);
+          tmem_ld32(lane_base + R + 64 + uint32_t(32 * hf), x);
+          tmem_wait_ld();
+          YB_DBG_ROW(DBG_U, 64, 32 * hf, 32, u);
+          YB_DBG_ROW(DBG_X, 64, 32 * hf, 32, x);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) u[i] -= x[i];
+          st_half_bf16(smem + OFF_VN, 128, 0, r, 4 * hf, u);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) u[i] *= TAIL[32 * hf + i] * kn[32 * hf + i];
+          st_half_bf16(smem + OFF_VHI, 128, 0, r, 4 * hf, u);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) u[i] -= __bfloat162float(__float2bfloat16_rn(u[i]));
+          st_half_bf16(smem + OFF_VLO, 128, 0, r, 4 * hf, u);
+        }
+        signal(b_vn);
+      }
+      YB_DBG_TS(10);
+      ok = ok && mbar_wait(mma45_bar, c & 1, abort_flag, ERR_WAIT_MMA);
+      // the next chunk's decay scales the state now (its gates were written two chunks ahead)
+      if (!last) ok = ok && mbar_wait(&full_kq[s ^ 1], ((c + 1) >> 1) & 1, abort_flag, ERR_WAIT_FULL);
+      tc_fence_after();
+      YB_DBG_TS(11);
+      if (ok) {
+        // ---------- o = e^{G} qn Y + O for this value column, staged as [token][value]
+        //            rows over the v~_hi tile (MMA5 has read it) ----------
+        __nv_bfloat16 *ostage = reinterpret_cast<__nv_bfloat16 *>(smem + OFF_OST);
+#pragma unroll 1
+        for (int hf = 0; hf < 2; ++hf) {
+          float y[32], oo[32];
+          tmem_ld32(lane_base + T_Y + uint32_t(32 * hf), y);
+          tmem_ld32(lane_base + T_O + uint32_t(32 * hf), oo);
+          tmem_wait_ld();
+          YB_DBG_ROW(DBG_Y, 64, 32 * hf, 32, y);
+          YB_DBG_ROW(DBG_O, 64, 32 * hf, 32, oo);
+#pragma unroll
+          for (int t = 0; t < 32; ++t) {
+            const int a = 32 * hf + t;
+            ostage[a * 128 + r] = __float2bfloat16_rn(EG[a] * qn[a] * y[t] + oo[t]);
+          }
+        }
+        // ---------- the updated state: bf16 copy for the next MMA3 (ht after the last chunk),
+        //            then fp32 scaled by the next chunk's decay back into TMEM ----------
+        const float dnext =
+            last ? 1.f : reinterpret_cast<const float *>(smem + OFF_GST + ((c + 1) % 3) * 1024)[128 + 63];
+#pragma unroll 1
+        for (int q4 = 0; q4 < 4; ++q4) {
+          float sv[32];
           tmem_ld32(lane_base + T_S + q4 * 32, sv);
-          tmem_ld32(lane_base + T_DS + q4 * 32, dv);
           tmem_wait_ld();
 #ifdef YB_TC_DEBUG
           if (p.dbg && blockIdx.x == 0 && c == 0)
-            for (int d = 0; d < 32; ++d) p.dbg[DBG_DS + r * 128 + q4 * 32 + d] = dv[d];
+            for (int d = 0; d < 32; ++d) p.dbg[DBG_S1 + r * 128 + q4 * 32 + d] = sv[d];
 #endif
-#pragma unroll
-          for (int d = 0; d < 32; ++d) sv[d] = fmaf(decay, sv[d], dv[d]);
-          tmem_st32(lane_base + T_S + q4 * 32, sv);
           st_half_bf16(st_tile, 128, q4 >> 1, r, (q4 & 1) * 4, sv);
-          if (last && p.ht) {
+          if (last) {
+            if (p.ht) {
 #pragma unroll
-            for (int d = 0; d < 32; ++d) {
-              const int dd = q4 * 32 + d;
-              if (trans) p.ht[head + int64_t(r) * KD + dd] = sv[d];
-              else p.ht[head + int64_t(dd) * VD + r] = sv[d];
+              for (int d = 0; d < 32; ++d) {
+                const int dd = q4 * 32 + d;
+                if (trans) p.ht[head + int64_t(r) * KD + dd] = sv[d];
+                else p.ht[head + int64_t(dd) * VD + r] = sv[d];
+              }
             }
+          } else {
+#pragma unroll
+            for (int d = 0; d < 32; ++d) sv[d] *= dnext;
+            tmem_st32(lane_base + T_S + q4 * 32, sv);
           }
         }
         tmem_wait_st();
+        signal(b_done);
+        YB_DBG_TS(12);
       }
-      YB_DBG_TS(11);
-      // release the MMA warp (next chunk's MMA1 overlaps the output store below)
-      // and the stage's gates / tiles (everything read from them is in registers)
-      signal_mma();
-      if (et == 0) mbar_arrive(&empty[s]);
-      {
-        __nv_bfloat16 *ostage = reinterpret_cast<__nv_bfloat16 *>(smem + OFF_LF);  // [64][128]
+      if (!(ok = b_sync_and(ok))) break;
+      // ---------- o out: 16-byte piece q = r + 128 t covers token q / 16, bytes 16 (q % 16) ----------
 #pragma unroll
-        for (int t = 0; t < 16; ++t) {
-          const __nv_bfloat162 pr2 = *reinterpret_cast<const __nv_bfloat162 *>(&opk[t]);
-          ostage[(j0 + 2 * t) * 128 + r] = pr2.x;
-          ostage[(j0 + 2 * t + 1) * 128 + r] = pr2.y;
+      for (int t = 0; t < 8; ++t) {
+        const int q = r + 128 * t, i = q >> 4, piece = q & 15;
+        if (i < m) {
+          const uint4 v = *reinterpret_cast<const uint4 *>(smem + OFF_OST + q * 16);
+          *reinterpret_cast<uint4 *>(p.o + ((bos + int64_t(c) * C + i) * p.HV + hv) * VD + piece * 8) = v;
         }
       }
-      epi_sync();
-      {
-        // copy the o tile out: 16-byte piece q = et + 256 t covers row q / 16, bytes 16 (q % 16);
-        // consecutive threads touch consecutive pieces (conflict-free, coalesced)
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const int q = et + 256 * t, i = q >> 4, piece = q & 15;
-          if (i < m) {
-            const uint4 v = *reinterpret_cast<const uint4 *>(smem + OFF_LF + q * 16);
-            *reinterpret_cast<uint4 *>(p.o + ((bos + int64_t(c) * C + i) * p.HV + hv) * VD + piece * 8) = v;
-          }
-        }
-      }
-      YB_DBG_TS(12);
+      YB_DBG_TS(13);
     }
   }
 

@@ -46,6 +46,10 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
       "mbarrier.arrive.release.cta.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
       : "memory");
 }
+// raise the expected transaction bytes of the current phase without arriving
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
   asm volatile(
       "{\n\t.reg .b64 st;\n\t"
