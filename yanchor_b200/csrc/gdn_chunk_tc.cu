@@ -70,7 +70,8 @@ constexpr uint32_t OFF_VLO = 174080;       // v~^T, low part
 constexpr uint32_t OFF_ST = 190464;        // S^T bf16 128x128 (2 column blocks)
 constexpr uint32_t OFF_GST = 223232;       // 3 slots: G, beta, e^G, e^{G_last-G} (4 x 64 floats)
 constexpr uint32_t OFF_NORM = OFF_GST + 3 * 1024;   // 3 slots: kn[64], qn[64]
-constexpr uint32_t OFF_BAR = OFF_NORM + 3 * 512;    // 17 mbarriers
+constexpr uint32_t OFF_FW = OFF_NORM + 3 * 512;     // Tw column factors beta e^G kn of group A's chunk
+constexpr uint32_t OFF_BAR = OFF_FW + 256;          // 17 mbarriers
 constexpr uint32_t OFF_MISC = OFF_BAR + 20 * 8;     // tmem base, abort flag
 constexpr uint32_t SMEM_BYTES = OFF_MISC + 16;
 static_assert(OFF_LF + 64 * LP * 4 <= OFF_TF && OFF_TF + 64 * LP * 4 <= OFF_P, "L / T regions");
@@ -498,6 +499,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const float *G = gst, *BT = gst + 64, *EG = gst + 128;
       float *kn = reinterpret_cast<float *>(smem + OFF_NORM + (c % 3) * 512);
       float *qn = kn + 64;
+      float *fw = reinterpret_cast<float *>(smem + OFF_FW);
       YB_DBG_TS(0);
       ok = mbar_wait(&full_kq[s], (c >> 1) & 1, abort_flag, ERR_WAIT_FULL);
       ok = ok && mbar_wait(&mma1_bar[s], (c >> 1) & 1, abort_flag, ERR_WAIT_MMA);
@@ -522,34 +524,49 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
         for (int t = 0; t < 32; ++t) diag = (t == lane) ? dg[t] : diag;
         const float nrm = l2 ? rsqrtf(diag + 1e-6f) : 1.f;
-        if (r < 64) kn[r] = nrm;
-        else qn[r - 64] = nrm * p.scale;
+        if (r < 64) {
+          kn[r] = nrm;
+          fw[r] = BT[r] * EG[r] * nrm;
+          // the raw k_i.k_j row into the L buffer, for all four warps to scale
+#pragma unroll 1
+          for (int hf = 0; hf < 2; ++hf) {
+            float d1[32];
+            tmem_ld32(lane_base + R + uint32_t(32 * hf), d1);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j4 = 0; j4 < 8; ++j4)
+              *reinterpret_cast<float4 *>(LF + r * LP + 32 * hf + 4 * j4) =
+                  make_float4(d1[4 * j4], d1[4 * j4 + 1], d1[4 * j4 + 2], d1[4 * j4 + 3]);
+          }
+        } else {
+          qn[r - 64] = nrm * p.scale;
+        }
       }
       if (!(ok = a_sync_and(ok))) break;
       YB_DBG_TS(2);
+      // ---------- L row r & 63, columns 32 (r >> 6) .. +31, in place (branch-free mask; the
+      //            exponent is clamped so masked entries stay finite) ----------
+      {
+        const int i = r & 63, jb = 32 * (r >> 6);
+        const float ci = BT[i] * kn[i], gi = G[i];
+        float4 *row4 = reinterpret_cast<float4 *>(LF + i * LP + jb);
+        const float4 *kn4 = reinterpret_cast<const float4 *>(kn + jb);
+        const float4 *g4 = reinterpret_cast<const float4 *>(G + jb);
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4) {
+          float4 d = row4[j4];
+          const float4 kk = kn4[j4], gg = g4[j4];
+          const int j = jb + 4 * j4;
+          d.x *= ci * kk.x * __expf(fminf(gi - gg.x, 0.f)) * float(j < i);
+          d.y *= ci * kk.y * __expf(fminf(gi - gg.y, 0.f)) * float(j + 1 < i);
+          d.z *= ci * kk.z * __expf(fminf(gi - gg.z, 0.f)) * float(j + 2 < i);
+          d.w *= ci * kk.w * __expf(fminf(gi - gg.w, 0.f)) * float(j + 3 < i);
+          row4[j4] = d;
+        }
+      }
+      if (!(ok = a_sync_and(ok))) break;
       uint32_t pk[32];   // threads r >= 64: P row r - 64 as packed bf16 pairs, stored after MMA2
       if (r < 64) {
-        // ---------- L row r (branch-free mask; the exponent is clamped so masked entries stay finite) ----------
-        const int i = r;
-        const float ci = BT[i] * kn[i], gi = G[i];
-#pragma unroll 1
-        for (int hf = 0; hf < 2; ++hf) {
-          float d1[32];
-          tmem_ld32(lane_base + R + uint32_t(32 * hf), d1);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j4 = 0; j4 < 8; ++j4) {
-            float4 v4;
-            float *vv = reinterpret_cast<float *>(&v4);
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-              const int jj = 4 * j4 + t, j = 32 * hf + jj;
-              vv[t] = ci * kn[j] * __expf(fminf(gi - G[j], 0.f)) * d1[jj] * float(j < i);
-            }
-            *reinterpret_cast<float4 *>(LF + i * LP + 32 * hf + 4 * j4) = v4;
-          }
-        }
-        solve_sync();
         YB_DBG_TS(3);
         {
         // ---- T = (I + L)^-1 by 16x16 blocks: T_ii = D_i (diagonal inverses),
@@ -654,10 +671,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           // alone costs ~2e-3 relative on the state
           if (r < 64) {
 #pragma unroll
-            for (int jj = 0; jj < 32; ++jj) {
-              const int j = 32 * hf + jj;
-              rowv[jj] *= BT[j] * EG[j] * kn[j];
-            }
+            for (int jj = 0; jj < 32; ++jj) rowv[jj] *= fw[32 * hf + jj];
           } else {
 #pragma unroll
             for (int jj = 0; jj < 32; ++jj) rowv[jj] *= BT[32 * hf + jj];
