@@ -54,8 +54,10 @@ const char *yb_last_error(void);
 int yb_abi_version(void);
 /*
  * Error word of the kernels that synchronise through time-bounded waits (the
- * tensor-core chunk kernel): 0 when every wait completed, else the code of
- * the first wait that gave up (that launch's outputs are then invalid).
+ * tensor-core kernels) or skip a store whose index leaves its table (the
+ * decode bookkeeping, 0x201): 0 when every wait completed and every index
+ * was in range, else the first code recorded (that launch's outputs are then
+ * invalid).
  * Synchronises the current device; `clear` resets the word.  No reference
  * counterpart: the reference's Triton kernels have no such waits.
  */
@@ -124,7 +126,8 @@ int yb_gdn_decode_fused(const void *mixed, int64_t mixed_tok_stride, const void 
  * Sliding-window attention decode over the physical ring cache.  Ring key /
  * value [B, KVH, W, D] (each head's W positions are contiguous rows of D;
  * batch / head strides in elements), ring valid [B, W] (bool bytes), one
- * device int64 write index for the whole batch.
+ * device write index for the whole batch (index_dtype YB_I32, as the
+ * reference's cache keeps it, or YB_I64).
  *
  * yb_swa_ring_write: the new token's key / value [B, KVH, 1, D] (strides in
  * elements, D contiguous) and valid [B] go to ring position *ring_index,
@@ -143,7 +146,8 @@ int yb_gdn_decode_fused(const void *mixed, int64_t mixed_tok_stride, const void 
 int yb_swa_ring_write(const void *key, const void *value, int64_t kv_batch_stride, int64_t kv_head_stride,
                       const uint8_t *valid, void *ring_key, void *ring_value, int64_t ring_batch_stride,
                       int64_t ring_head_stride, uint8_t *ring_valid, int64_t ring_valid_batch_stride,
-                      int64_t *ring_index, int64_t B, int64_t KVH, int64_t W, int64_t D, int dtype, void *stream);
+                      void *ring_index, int index_dtype, int64_t B, int64_t KVH, int64_t W, int64_t D, int dtype,
+                      void *stream);
 int64_t yb_swa_decode_workspace_bytes(int64_t B, int64_t KVH, int64_t QH, int64_t W, int64_t D);
 int yb_swa_decode_attention(const void *query, const void *ring_key, const void *ring_value,
                             int64_t ring_batch_stride, int64_t ring_head_stride, const uint8_t *valid,

@@ -94,3 +94,47 @@ def test_attention_16bit_shapes(yb, R, D, W, dt):
     ref = oswa.decode_attention(host(q), host(k), host(v), valid)
     ref[1] = 0.0
     assert np.abs(host(out) - ref).max() <= 2e-2
+
+
+@pytest.mark.parametrize('shared', [False, True])
+def test_layer_cache_ring_update_matches_reference_flow(yb, shared):
+    """The reference's layer-cache form: the ring is built on first use from
+    the chronological window cache (width keep + 1, the cache at 0 .. keep-1,
+    an int32 index at keep), then each decode token goes to the index, which
+    advances modulo the width; with shared storage the cache fields become
+    views into the ring."""
+    from types import SimpleNamespace
+    rng = np.random.default_rng(7 + shared)
+    B, KVH, keep, D, QH = 3, 2, 9, 64, 4
+    W = keep + 1
+    keys = rng.standard_normal((B, KVH, keep, D)).astype(np.float32)
+    values = rng.standard_normal((B, KVH, keep, D)).astype(np.float32)
+    valid = rng.random((B, keep)) > 0.2
+    cache = SimpleNamespace(keys=cuda(keys, torch.bfloat16), values=cuda(values, torch.bfloat16), valid=cuda(valid),
+                            _qwen35_swa_shared_ring_storage=shared)
+    rk = np.zeros((B, KVH, W, D), np.float32)
+    rv = np.zeros((B, KVH, W, D), np.float32)
+    rval = np.zeros((B, W), bool)
+    rk[:, :, :keep] = host(cache.keys)
+    rv[:, :, :keep] = host(cache.values)
+    rval[:, :keep] = valid
+    idx = keep
+    for step in range(13):
+        k = rng.standard_normal((B, KVH, 1, D)).astype(np.float32)
+        v = rng.standard_normal((B, KVH, 1, D)).astype(np.float32)
+        val = rng.random((B, 1)) > 0.3
+        kd, vd = cuda(k, torch.bfloat16), cuda(v, torch.bfloat16)
+        ring_k, ring_v, ring_valid = yb.layer_ring_update(cache, kd, vd, cuda(val))
+        rk, rv, rval, idx = oswa.ring_update(rk, rv, rval, idx, host(kd), host(vd), val)
+        assert cache._qwen35_swa_physical_ring_index.dtype == torch.int32
+        assert int(cache._qwen35_swa_physical_ring_index.item()) == idx, step
+        np.testing.assert_array_equal(host(ring_k), rk)
+        np.testing.assert_array_equal(host(ring_v), rv)
+        np.testing.assert_array_equal(host(ring_valid), rval)
+        q = cuda(rng.standard_normal((B, 1, QH, D)).astype(np.float32), torch.bfloat16)
+        out = yb.physical_ring_decode_attention(q, ring_k, ring_v, ring_valid)
+        ref = oswa.decode_attention(host(q), rk, rv, rval)
+        ref[~rval.any(1)] = 0.0
+        assert np.abs(host(out) - ref).max() <= 2e-2
+    if shared:
+        assert cache.keys.data_ptr() == cache._qwen35_swa_physical_ring_keys.data_ptr()

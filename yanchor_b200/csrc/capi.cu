@@ -254,8 +254,10 @@ int yb_gdn_decode_fused(const void *mixed, int64_t mixed_tok_stride, const void 
 int yb_swa_ring_write(const void *key, const void *value, int64_t kv_batch_stride, int64_t kv_head_stride,
                       const uint8_t *valid, void *ring_key, void *ring_value, int64_t ring_batch_stride,
                       int64_t ring_head_stride, uint8_t *ring_valid, int64_t ring_valid_batch_stride,
-                      int64_t *ring_index, int64_t B, int64_t KVH, int64_t W, int64_t D, int dtype, void *stream) {
+                      void *ring_index, int index_dtype, int64_t B, int64_t KVH, int64_t W, int64_t D, int dtype,
+                      void *stream) {
   YB_REQUIRE(dtype_ok(dtype), "swa_ring_write: bad dtype");
+  YB_REQUIRE(index_dtype == YB_I32 || index_dtype == YB_I64, "swa_ring_write: the index must be int32 or int64");
   YB_REQUIRE(B >= 0 && KVH > 0 && W > 0 && (D == 32 || D == 64 || D == 128 || D == 256),
              "swa_ring_write: bad sizes (D in 32/64/128/256)");
   YB_REQUIRE(B == 0 || (key && value && valid && ring_key && ring_value && ring_valid && ring_index),
@@ -271,6 +273,7 @@ int yb_swa_ring_write(const void *key, const void *value, int64_t kv_batch_strid
   a.new_k = key; a.new_v = value; a.new_bs = kv_batch_stride; a.new_hs = kv_head_stride; a.new_valid = valid;
   a.ring_k = ring_key; a.ring_v = ring_value; a.ring_bs = ring_batch_stride; a.ring_hs = ring_head_stride;
   a.ring_valid = ring_valid; a.valid_bs = ring_valid_batch_stride; a.ring_index = ring_index;
+  a.index_i64 = index_dtype == YB_I64;
   a.B = B; a.KVH = KVH; a.W = W; a.D = D; a.dtype = dtype; a.stream = static_cast<cudaStream_t>(stream);
   return launch_swa_ring_write(a);
 }

@@ -146,7 +146,8 @@ struct SwaArgs {
   int64_t ring_bs, ring_hs;
   uint8_t *ring_valid;            // [B, W]
   int64_t valid_bs;
-  int64_t *ring_index;            // device scalar
+  void *ring_index;               // device scalar, int32 (as the reference keeps it) or int64
+  int index_i64;
   const void *query;              // attention: [B, 1, QH, D]
   void *out;                      // [B, 1, QH, D]
   int64_t B, QH, KVH, W, D;

@@ -31,10 +31,14 @@ __device__ __forceinline__ void cp_async16_swa(void *dst, const void *src) {
                : "memory");
 }
 
+__device__ __forceinline__ int64_t ring_index_of(const SwaArgs &a) {
+  return a.index_i64 ? *static_cast<const int64_t *>(a.ring_index) : int64_t(*static_cast<const int32_t *>(a.ring_index));
+}
+
 template <typename T>
 __global__ void swa_ring_write_kernel(const SwaArgs a) {
   constexpr int VEC = 16 / int(sizeof(T));
-  const int64_t idx = *a.ring_index;
+  const int64_t idx = ring_index_of(a);
   if (idx < 0 || idx >= a.W) return;   // a corrupt index writes nothing (the advance restarts it at 0)
   const int64_t pieces = a.B * a.KVH * (a.D / VEC);
   const int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -51,9 +55,11 @@ __global__ void swa_ring_write_kernel(const SwaArgs a) {
   }
 }
 
-__global__ void swa_ring_advance_kernel(int64_t *index, int64_t W) {
-  const int64_t i = *index;
-  *index = (i < 0 || i + 1 >= W) ? 0 : i + 1;
+__global__ void swa_ring_advance_kernel(const SwaArgs a) {
+  const int64_t i = ring_index_of(a);
+  const int64_t next = (i < 0 || i + 1 >= a.W) ? 0 : i + 1;
+  if (a.index_i64) *static_cast<int64_t *>(a.ring_index) = next;
+  else *static_cast<int32_t *>(a.ring_index) = int32_t(next);
 }
 
 template <typename T, int R, int D>
@@ -230,7 +236,7 @@ int launch_swa_ring_write(const SwaArgs &a) {
   }
   int rc = check_launch("swa_ring_write_kernel");
   if (rc) return rc;
-  swa_ring_advance_kernel<<<1, 1, 0, a.stream>>>(a.ring_index, a.W);
+  swa_ring_advance_kernel<<<1, 1, 0, a.stream>>>(a);
   return check_launch("swa_ring_advance_kernel");
 }
 

@@ -8,9 +8,17 @@ reference's call shapes.
     physical_ring_decode_attention(query, ring_key, ring_value, valid)
         runtime/model/inference_kernels.py:1881-1897
         (`fixed_memory_physical_ring_decode_attention`)
+    layer_ring_update(layer_cache, key, value, valid)
+        the same update on a layer cache object, with the reference's
+        signature (runtime/model/inference_kernels.py:1861-1879,
+        `triton_fixed_memory_swa_physical_ring_update`): the ring lives in the
+        cache's ``_qwen35_swa_physical_ring_*`` attributes and is built on
+        first use as the reference builds it (`initialize_physical_ring`,
+        same file :555-598)
 
 Ring key / value ``[B, KVH, W, D]`` (positions contiguous inside each head),
-valid ``[B, W]`` bool, ring_index a device int64 scalar tensor.
+valid ``[B, W]`` bool, ring_index a device int32 (as the reference keeps it)
+or int64 scalar tensor.
 """
 from __future__ import annotations
 
@@ -40,13 +48,14 @@ def physical_ring_update_(ring_key, ring_value, ring_valid, ring_index, key, val
         raise ValueError('the new key / value must be [B, KVH, 1, D] in the ring dtype')
     if key.stride(3) != 1 or value.stride() != key.stride():
         key, value = key.contiguous(), value.contiguous()
-    if ring_index.dtype != torch.int64 or ring_index.numel() != 1:
-        raise TypeError('ring_index must be a one-element int64 tensor')
+    if ring_index.dtype not in (torch.int32, torch.int64) or ring_index.numel() != 1:
+        raise TypeError('ring_index must be a one-element int32 or int64 tensor')
     v = valid.reshape(B).to(torch.bool).contiguous()
     rc = _lib.lib().yb_swa_ring_write(key.data_ptr(), value.data_ptr(), key.stride(0), key.stride(1), v.data_ptr(),
                                       ring_key.data_ptr(), ring_value.data_ptr(), ring_key.stride(0),
                                       ring_key.stride(1), ring_valid.data_ptr(), ring_valid.stride(0),
-                                      ring_index.data_ptr(), B, KVH, W, D, dtype_code(ring_key),
+                                      ring_index.data_ptr(), 3 if ring_index.dtype == torch.int32 else 4,
+                                      B, KVH, W, D, dtype_code(ring_key),
                                       stream_ptr(ring_key.device))
     _lib.check(rc, 'physical_ring_update_')
     return ring_key, ring_value, ring_valid
@@ -81,3 +90,66 @@ def physical_ring_decode_attention(query, ring_key, ring_value, valid, *, reprod
                                             workspace.numel(), stream_ptr(q.device))
     _lib.check(rc, 'physical_ring_decode_attention')
     return out
+
+
+_RING = '_qwen35_swa_physical_ring_'
+
+
+def initialize_physical_ring(layer_cache):
+    """Build the ring from a chronological window cache (``keys`` / ``values``
+    ``[B, KVH, keep, D]``, ``valid [B, keep]``): ring width keep + 1, the
+    cached positions at 0 .. keep - 1, the write index at keep (int32).  With
+    ``_qwen35_swa_shared_ring_storage`` the cache's fields become views into
+    the ring.  Host-issued copies only (cache set-up, as the reference's)."""
+    tensors = (layer_cache.keys, layer_cache.values, layer_cache.valid)
+    if any(t is None or not t.is_cuda for t in tensors):
+        raise ValueError('physical SWA ring requires CUDA cache tensors')
+    keep = int(layer_cache.keys.shape[-2])
+    window = keep + 1
+    if getattr(layer_cache, '_qwen35_swa_shared_ring_storage', False):
+        for field, dim in (('keys', 2), ('values', 2), ('valid', 1)):
+            source = getattr(layer_cache, field)
+            shape = list(source.shape)
+            shape[dim] = window
+            target = getattr(layer_cache, _RING + field, None)
+            if target is not None and target.shape == tuple(shape) and source.data_ptr() == target.data_ptr():
+                target.narrow(dim, keep, 1).zero_()
+            else:
+                target = source.new_zeros(shape)
+                target.narrow(dim, 0, keep).copy_(source)
+            setattr(layer_cache, _RING + field, target)
+            setattr(layer_cache, field, target.narrow(dim, 0, keep))
+    else:
+        for field, source in (('keys', layer_cache.keys), ('values', layer_cache.values),
+                              ('valid', layer_cache.valid)):
+            shape = (*source.shape[:-2], window, source.shape[-1]) if field != 'valid' else (source.shape[0], window)
+            target = getattr(layer_cache, _RING + field, None)
+            if target is None or target.shape != shape or target.device != source.device:
+                target = source.new_zeros(shape)
+                setattr(layer_cache, _RING + field, target)
+            else:
+                target.zero_()
+            if field == 'valid':
+                target[:, :keep].copy_(source)
+            else:
+                target[:, :, :keep].copy_(source)
+    index = getattr(layer_cache, _RING + 'index', None)
+    if index is None or index.device != layer_cache.keys.device:
+        setattr(layer_cache, _RING + 'index', torch.tensor(keep, dtype=torch.int32, device=layer_cache.keys.device))
+    else:
+        index.fill_(keep)
+
+
+def layer_ring_update(layer_cache, key, value, valid):
+    """One decode token into the layer cache's ring (built on first use);
+    returns ``(ring_key, ring_value, ring_valid)`` as the reference does."""
+    require_cuda(key, value, valid)
+    if key.shape[-2] != 1 or value.shape[-2] != 1 or valid.shape[-1] != 1:
+        raise ValueError('physical SWA ring accepts one token')
+    if key.shape != value.shape or key.stride(-1) != 1 or value.stride(-1) != 1:
+        raise ValueError('physical SWA ring requires matching contiguous KV heads')
+    if not hasattr(layer_cache, _RING + 'index'):
+        initialize_physical_ring(layer_cache)
+    return physical_ring_update_(getattr(layer_cache, _RING + 'keys'), getattr(layer_cache, _RING + 'values'),
+                                 getattr(layer_cache, _RING + 'valid'), getattr(layer_cache, _RING + 'index'),
+                                 key, value, valid)
