@@ -55,7 +55,7 @@ int yb_abi_version(void);
 /*
  * Error word of the kernels that synchronise through time-bounded waits (the
  * tensor-core kernels) or skip a store whose index leaves its table (the
- * decode bookkeeping, 0x201): 0 when every wait completed and every index
+ * decode bookkeeping, 0x401): 0 when every wait completed and every index
  * was in range, else the first code recorded (that launch's outputs are then
  * invalid).
  * Synchronises the current device; `clear` resets the word.  No reference
@@ -354,6 +354,22 @@ int yb_sample_top_k_top_p_counter(const void *scores, int64_t row_stride, int64_
 int yb_presence_penalty(void *scores, const uint8_t *seen, int64_t n, float penalty, int dtype, void *stream);
 
 /*
+ * Sliding-window attention over a prompt (prefill), on the tcgen05 tensor
+ * cores.  Replaces modeling_yanchor.py:412-427 `reference_swa` (and the
+ * FlashAttention call of `flash_swa`, :429-449, on rows whose valid tokens
+ * form one run).  q / out [B, Tq, QH, D], k / v [B, Tk, KVH, D], contiguous
+ * bf16, D = 256, QH / KVH in {1, 2, 4, 8}.  Query i sits at absolute
+ * position query_start + i and key j at j; query i admits key j when
+ * i_abs - window < j <= i_abs and key_valid[b, j] (key_valid [B, Tk] bool
+ * bytes at valid_batch_stride, or NULL); scale D^-1/2.  A query whose own
+ * key_valid entry (at i_abs) is false, or that admits no key, gives zeros.
+ * Other shapes return YB_ERR_UNSUPPORTED.
+ */
+int yb_swa_prefill_attention(const void *q, const void *k, const void *v, const uint8_t *key_valid,
+                             int64_t valid_batch_stride, void *out, int64_t B, int64_t Tq, int64_t Tk, int64_t QH,
+                             int64_t KVH, int64_t D, int64_t window, int64_t query_start, int dtype, void *stream);
+
+/*
  * Decode-loop bookkeeping after one sampled token per slot, in one launch.
  * Replaces runtime/model/inference_kernels.py:1206-1208
  * `_update_fixed_decode_state_` (Triton kernel :1169-1204) and the torch
@@ -376,7 +392,7 @@ int yb_presence_penalty(void *scores, const uint8_t *seen, int64_t n, float pena
  * eos_count (<= 8) ids.  Row indices must be distinct across active slots
  * and sink rows (the reference's slot table guarantees it).  A token outside
  * [0, vocab) or a write outside storage skips that store and is reported by
- * yb_device_error() (0x201).  Capture-safe; one kernel launch.
+ * yb_device_error() (0x401).  Capture-safe; one kernel launch.
  */
 int yb_decode_state_update(const int64_t *sampled_token, int64_t sampled_stride, void *storage, int storage_dtype,
                            int64_t storage_rows, int64_t storage_cols, int64_t storage_stride, uint8_t *dense_seen,

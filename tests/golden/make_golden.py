@@ -22,7 +22,8 @@ Python) to a scratch directory, puts it and the reference root first on
 * ``fixed_memory_physical_ring_decode_attention`` (runtime/model/
   inference_kernels.py:1881-1897)
 * the torch statements of the fixed-memory decode loop's per-step
-  bookkeeping (runtime/model/inference_kernels.py:1700-1717)
+  bookkeeping (runtime/model/inference_kernels.py:1701-1717)
+* ``reference_swa`` (modeling_yanchor.py:412-427)
 
 on seeded inputs and writes the inputs and outputs as ``.npz`` files next to
 this script.  The GPU box never needs the reference: tests only read the
@@ -301,6 +302,37 @@ def swa_fixtures(ik, torch):
     return {'swa_q': q, 'swa_k': rk, 'swa_v': rv, 'swa_valid': valid, 'swa_out': out}
 
 
+def swa_prefill_fixtures(my, torch):
+    """``reference_swa`` (modeling_yanchor.py:412-427): a plain causal window,
+    left-padded rows through key validity, and a query block after a cached
+    window (``query_start``), grouped-query."""
+    g = torch.Generator().manual_seed(17)
+    out = {}
+    cases = [
+        ('a', 2, 40, 40, 4, 1, 16, 16, 0, None),
+        ('b', 3, 37, 37, 4, 2, 16, 50, 0, 'left'),
+        ('c', 2, 20, 45, 8, 2, 16, 24, 25, 'holes'),
+    ]
+    for name, B, Tq, Tk, QH, KVH, D, window, qs, mask in cases:
+        q = torch.randn(B, Tq, QH, D, generator=g)
+        k = torch.randn(B, Tk, KVH, D, generator=g)
+        v = torch.randn(B, Tk, KVH, D, generator=g)
+        kv = None
+        if mask == 'left':
+            kv = torch.ones(B, Tk, dtype=torch.bool)
+            kv[1, :5] = False
+            kv[2, :36] = False
+        elif mask == 'holes':
+            kv = torch.rand(B, Tk, generator=g) > 0.25
+            kv[:, qs:] |= torch.arange(Tq)[None, :] % 3 == 0
+        o = my.reference_swa(q, k, v, window=window, key_valid=kv, query_start=qs)
+        out.update({f'sp{name}_q': q, f'sp{name}_k': k, f'sp{name}_v': v, f'sp{name}_out': o,
+                    f'sp{name}_meta': torch.tensor([window, qs])})
+        if kv is not None:
+            out[f'sp{name}_valid'] = kv
+    return out
+
+
 def sampling_fixtures(ik, torch):
     out = {}
     g = torch.Generator().manual_seed(4)
@@ -390,7 +422,8 @@ def main():
     torch.manual_seed(0)
     for name, fn in (('gdn', lambda: gdn_fixtures(qwen, torch)), ('memory', lambda: memory_fixtures(my, torch)),
                      ('sampling', lambda: sampling_fixtures(ik, torch)), ('conv', lambda: conv_fixtures(my, torch)),
-                     ('swa', lambda: swa_fixtures(ik, torch)), ('decode_state', lambda: decode_state_fixtures(ik, torch))):
+                     ('swa', lambda: swa_fixtures(ik, torch)), ('decode_state', lambda: decode_state_fixtures(ik, torch)),
+                     ('swa_prefill', lambda: swa_prefill_fixtures(my, torch))):
         if args.only and name not in args.only:
             continue
         data = {k: (v.detach().cpu().numpy() if hasattr(v, 'detach') else np.asarray(v)) for k, v in fn().items()}

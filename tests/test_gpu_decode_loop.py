@@ -94,7 +94,7 @@ def test_state_update_out_of_vocabulary_token_is_reported(yb):
     yb.update_fixed_decode_state_(tok, *(dev[k] for k in FIELDS), maximum_new_tokens=4, pad_token_id=0,
                                   eos_token_ids=())
     torch.cuda.synchronize()
-    assert yb.lib().yb_device_error(1) == 0x201
+    assert yb.lib().yb_device_error(1) == 0x401
     assert dev['dense_seen'][1].sum().item() == 0 and dev['dense_seen'][0, 3].item()
     assert dev['storage'][1, 1].item() == vocab + 5 and int(dev['decode_useful_events']) == slots
 

@@ -218,3 +218,24 @@ def test_swa_decode_attention(golden):
     from oracle import swa
     d = golden('swa')
     close(swa.decode_attention(d['swa_q'], d['swa_k'], d['swa_v'], d['swa_valid']), d['swa_out'], 2e-6)
+
+
+@pytest.mark.parametrize('case', ['a', 'b', 'c'])
+def test_swa_prefill_attention(golden, case):
+    """reference_swa: plain causal window, left padding through key validity,
+    a query block after a cached window with holes."""
+    from oracle import swa
+    d = golden('swa_prefill')
+    window, qs = (int(x) for x in d[f'sp{case}_meta'])
+    kv = d[f'sp{case}_valid'] if f'sp{case}_valid' in d else None
+    close(swa.prefill_attention(d[f'sp{case}_q'], d[f'sp{case}_k'], d[f'sp{case}_v'], window, kv, qs),
+          d[f'sp{case}_out'], 2e-6)
+
+
+def test_flash_prefill_matches_reference_swa_on_contiguous_masks(golden):
+    """flash_swa counts valid tokens only; on left-padded rows (one contiguous
+    valid run per row) that is the same as reference_swa's absolute positions."""
+    from oracle import swa
+    d = golden('swa_prefill')
+    window, _ = (int(x) for x in d['spb_meta'])
+    close(swa.flash_prefill(d['spb_q'], d['spb_k'], d['spb_v'], window, d['spb_valid']), d['spb_out'], 2e-6)

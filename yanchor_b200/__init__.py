@@ -22,7 +22,8 @@ Operators (all CUDA, via the C ABI library libyanchor_b200.so):
 from .gated_delta_rule import (chunk_gated_delta_rule, fused_gdn_decode, fused_recurrent_gated_delta_rule,  # noqa: F401
                                gdn_gates)
 from .conv import causal_conv1d_fn, causal_conv1d_update  # noqa: F401
-from .swa import initialize_physical_ring, layer_ring_update, physical_ring_decode_attention, physical_ring_update_  # noqa: F401,E501
+from .swa import (flash_swa, initialize_physical_ring, layer_ring_update, physical_ring_decode_attention,  # noqa: F401
+                  physical_ring_update_, reference_swa)
 from .independent_memory import MemoryState, commit_decode, committed_gqa, indexed_gqa  # noqa: F401
 from .memory_prefill import exclusive_prefix_topk, merge_topk, select_topk, sequence  # noqa: F401
 from .sampling import apply_dense_presence_penalty_, greedy, sample_top_k_top_p_counter  # noqa: F401

@@ -64,6 +64,8 @@ SIGNATURES = {
     'yb_sample_top_k_top_p_counter': (_I, [_P, _I64, _I64, _I64, _I, _P, _P, _I64, _I64, _I64, _F, _I64, _F, _P, _P,
                                            _I64, _P]),
     'yb_presence_penalty': (_I, [_P, _P, _I64, _F, _I, _P]),
+    'yb_swa_prefill_attention': (_I, [_P, _P, _P, _P, _I64, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I,
+                                      _P]),
     'yb_decode_state_update': (_I, [_P, _I64, _P, _I, _I64, _I64, _I64, _P, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P,
                                     _P, _I64, _P, _I64, _I64, _I64, _P, _I, _P]),
 }

@@ -72,8 +72,8 @@ const char *yb_last_error(void) { return g_err; }
 int yb_abi_version(void) { return 1; }
 int yb_device_error(int clear) {
   const int a = read_device_error(clear), b = read_device_error_idx(clear), c = read_device_error_fused(clear),
-            d = read_device_error_loop(clear);
-  return a ? a : (b ? b : (c ? c : d));
+            d = read_device_error_loop(clear), e = read_device_error_swa(clear);
+  return a ? a : (b ? b : (c ? c : (d ? d : e)));
 }
 
 int yb_gdn_recurrent_fwd(const void *q, const void *k, const void *v, int64_t q_tok_stride, int64_t k_tok_stride,
@@ -481,6 +481,21 @@ int yb_decode_state_update(const int64_t *sampled_token, int64_t sampled_stride,
   a.eos_count = eos_count;
   a.stream = static_cast<cudaStream_t>(stream);
   return launch_decode_state_update(a);
+}
+
+int yb_swa_prefill_attention(const void *q, const void *k, const void *v, const uint8_t *key_valid,
+                             int64_t valid_batch_stride, void *out, int64_t B, int64_t Tq, int64_t Tk, int64_t QH,
+                             int64_t KVH, int64_t D, int64_t window, int64_t query_start, int dtype, void *stream) {
+  YB_REQUIRE(dtype_ok(dtype), "swa_prefill: bad dtype");
+  YB_REQUIRE(B >= 0 && Tq >= 0 && Tk >= 0 && QH > 0 && KVH > 0 && QH % KVH == 0 && window >= 1 && query_start >= 0,
+             "swa_prefill: bad sizes");
+  YB_REQUIRE(B * Tq == 0 || (q && k && v && out), "swa_prefill: null tensor");
+  YB_REQUIRE(key_valid == nullptr || B <= 1 || valid_batch_stride >= Tk, "swa_prefill: key_valid stride too small");
+  SwaPrefillArgs a{};
+  a.q = q; a.k = k; a.v = v; a.key_valid = key_valid; a.valid_bs = valid_batch_stride; a.out = out;
+  a.B = B; a.Tq = Tq; a.Tk = Tk; a.QH = QH; a.KVH = KVH; a.D = D; a.window = window; a.query_start = query_start;
+  a.dtype = dtype; a.stream = static_cast<cudaStream_t>(stream);
+  return launch_swa_prefill_tc(a);
 }
 
 }  // extern "C"

@@ -20,7 +20,7 @@ namespace yb {
 namespace {
 
 constexpr int kLoopThreads = 256;
-constexpr int ERR_DECODE_INDEX = 0x201;
+constexpr int ERR_DECODE_INDEX = 0x401;
 __device__ int g_loop_error = 0;
 
 template <typename TS>

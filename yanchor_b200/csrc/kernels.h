@@ -204,6 +204,21 @@ struct DecodeStateArgs {
 int launch_decode_state_update(const DecodeStateArgs &a);
 int read_device_error_loop(int clear);
 
+// Sliding-window prefill attention (tcgen05): q / out [B, Tq, QH, D], k / v
+// [B, Tk, KVH, D], contiguous; key_valid [B, Tk] bytes or null.
+struct SwaPrefillArgs {
+  const void *q, *k, *v;
+  const uint8_t *key_valid;
+  int64_t valid_bs;
+  void *out;
+  int64_t B, Tq, Tk, QH, KVH, D, window, query_start;
+  int dtype;
+  cudaStream_t stream;
+};
+bool swa_prefill_tc_supported(const SwaPrefillArgs &a);
+int launch_swa_prefill_tc(const SwaPrefillArgs &a);
+int read_device_error_swa(int clear);
+
 int launch_swa_ring_write(const SwaArgs &a);
 int launch_swa_decode_attention(const SwaArgs &a, void *workspace);
 int64_t swa_workspace_bytes(int64_t B, int64_t KVH, int64_t QH, int64_t W, int64_t D);

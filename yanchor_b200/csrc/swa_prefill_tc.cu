@@ -1,0 +1,400 @@
+// Sliding-window prefill attention on the tcgen05 tensor cores, bf16, D = 256
+// (the YANchor SWA layer): queries [B, Tq, QH, D] at absolute positions
+// query_start + i attend to keys [B, Tk, KVH, D] at positions j with
+// i_abs - window < j <= i_abs and key_valid[b, j]; scale D^-1/2; grouped
+// query heads (R = QH / KVH); a query whose own key_valid entry is false, or
+// that admits no key, gives zeros.  (modeling_yanchor.py:412-427
+// reference_swa; flash_swa :429-449 over each row's valid tokens.)
+//
+// One CTA per (row b, KV head, P = 128 / R query positions): its 128 query
+// rows are the (position, head) pairs of the group's R heads, brought in by
+// TMA in that order.  The keys the tile can see (at most window + P - 1)
+// stream through in 64-key tiles:
+//   warp 0   TMA producer: Q once; K / V tiles double-buffered, with each
+//            tile's key-validity flags
+//   warp 1   TMEM allocator and MMA issuer: S(t) = Q K(t)^T (M=128, N=64,
+//            K=256) into one of two TMEM buffers, then O += P(t-1) V(t-1)
+//            (N=256), so a tile's softmax overlaps the previous tile's PV
+//   warps 2-5  one query row per thread: mask, online softmax in base 2
+//            (O in TMEM is rescaled only when the row max grows by more than
+//            2^8), P as bf16 (as FlashAttention rounds it) into one of two
+//            shared buffers; at the end O / l staged over Q and TMA-stored.
+// Every barrier a role can lag on is indexed by tile parity, so no parity
+// wait can see a barrier two phases ahead.  Every wait is bounded in time; a
+// CTA that gives up records an error code, drains its copies and MMAs, frees
+// TMEM and exits.
+#include "common.cuh"
+#include "kernels.h"
+#include "tc.cuh"
+
+namespace yb {
+namespace {
+
+using namespace tc;
+
+constexpr int D = 256, NT = 192, KT = 64;
+constexpr uint32_t OFF_Q = 0;              // Q: 4 column blocks x 128 rows x 128 B (later the O staging)
+constexpr uint32_t OFF_K = 65536;          // K: 2 stages x 4 column blocks x 64 rows x 128 B
+constexpr uint32_t OFF_V = 131072;         // V: same
+constexpr uint32_t OFF_P = 196608;         // P: 2 buffers x 128 rows x 64 keys bf16 (SW128)
+constexpr uint32_t OFF_KF = 229376;        // key flags: 2 stages x 64 floats
+constexpr uint32_t OFF_BAR = OFF_KF + 512;
+constexpr uint32_t OFF_MISC = OFF_BAR + 16 * 8;
+constexpr uint32_t SMEM_BYTES = OFF_MISC + 16;
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+constexpr uint32_t T_S = 0;                // 2 x 64 columns
+constexpr uint32_t T_O = 256;              // 256 columns
+constexpr uint32_t ID_S = idesc_bf16(128, 64, false, false);
+constexpr uint32_t ID_O = idesc_bf16(128, 256, false, true);
+constexpr float kRescale = 8.f;            // log2 of the largest exp2 factor P may carry before O is rescaled
+constexpr int ERR_SP_Q = 0x501, ERR_SP_FULL = 0x502, ERR_SP_EMPTY = 0x503, ERR_SP_S = 0x504, ERR_SP_P = 0x505,
+              ERR_SP_O = 0x506, ERR_SP_DONE = 0x507, ERR_SP_FREE = 0x508;
+
+struct SpParams {
+  const uint8_t *key_valid;
+  int64_t valid_bs;
+  int64_t Tq, Tk, KVH, window, query_start, qtiles;
+  int R, P;
+  float scale_log2;
+};
+
+__device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y, int z,
+                                            int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+      "[%2];" ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y),
+      "r"(z), "r"(w)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap *map, const void *src, int x, int y, int z, int w) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];"
+               ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z), "r"(w)
+               : "memory");
+}
+// the softmax warps' named barrier (barrier 1, 128 threads), ANDing a status
+__device__ __forceinline__ bool epi_sync_and(bool ok) {
+  uint32_t res;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\tbar.red.and.pred po, 1, 128, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(res)
+      : "r"(uint32_t(ok))
+      : "memory");
+  return res != 0;
+}
+
+__global__ void __launch_bounds__(NT, 1)
+    swa_prefill_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                          const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_o,
+                          const SpParams p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
+  uint64_t *qbar = bars + 0;
+  uint64_t *full = bars + 1;       // [2] K / V tile and its flags landed (32 + tx)
+  uint64_t *empty = bars + 3;      // [2] the tile's O MMA finished (1)
+  uint64_t *s_full = bars + 5;     // [2] S of the tile in TMEM (1)
+  uint64_t *s_free = bars + 7;     // [2] the softmax warps have read that S buffer (128)
+  uint64_t *p_ready = bars + 9;    // [2] P of the tile written, O rescaled if needed (128)
+  uint64_t *o_done = bars + 11;    // [2] O += P V of the tile finished (1)
+  uint64_t *done_bar = bars + 13;
+  uint32_t *tmem_base_smem = reinterpret_cast<uint32_t *>(smem + OFF_MISC);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OFF_MISC + 4);
+
+  const int64_t unit = blockIdx.x;
+  const int64_t qt = unit % p.qtiles;
+  const int kvh = int((unit / p.qtiles) % p.KVH);
+  const int b = int(unit / (p.qtiles * p.KVH));
+  const int64_t qp0 = qt * p.P;                                     // first query of the tile
+  const int64_t qabs0 = p.query_start + qp0;
+  const int64_t qlast = p.query_start + (p.Tq < qp0 + p.P ? p.Tq : qp0 + p.P) - 1;
+  const int64_t lo = qabs0 - p.window + 1 > 0 ? qabs0 - p.window + 1 : 0;
+  const int64_t hi = qlast < p.Tk - 1 ? qlast : p.Tk - 1;
+  const int ntiles = hi >= lo ? int((hi - lo) / KT + 1) : 0;
+
+  if (tid == 0) {
+    *abort_flag = (smem_u32(smem) & 1023u) ? 1 : 0;  // SW128 tiles need a 1024-byte aligned base
+    if (*abort_flag) atomicCAS(&g_device_error, 0, ERR_SP_Q);
+    mbar_init(qbar, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&full[s], 32);
+      mbar_init(&empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_free[s], 128);
+      mbar_init(&p_ready[s], 128);
+      mbar_init(&o_done[s], 1);
+    }
+    mbar_init(done_bar, 1);
+    mbar_fence_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_base_smem, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_base_smem;
+
+  if (warp == 0) {
+    // ===================== producer =====================
+    if (lane == 0 && ntiles > 0 && !*abort_flag) {
+      prefetch_tensormap(&map_q);
+      prefetch_tensormap(&map_k);
+      prefetch_tensormap(&map_v);
+      mbar_arrive_expect_tx(qbar, 4 * 16384);
+#pragma unroll
+      for (int cb = 0; cb < 4; ++cb)
+        tma_load_4d(smem + OFF_Q + cb * 16384, &map_q, qbar, cb * 64, kvh * p.R, int(qp0), b);
+    }
+    int issued = 0;
+    for (int t = 0; t < ntiles && !*abort_flag; ++t) {
+      const int s = t & 1;
+      const int64_t kt0 = lo + int64_t(t) * KT;
+      if (t >= 2 && !mbar_wait(&empty[s], ((t >> 1) - 1) & 1, abort_flag, ERR_SP_EMPTY)) break;
+      if (lane == 0) {
+        mbar_expect_tx(&full[s], 8 * 8192);
+#pragma unroll
+        for (int cb = 0; cb < 4; ++cb) {
+          tma_load_4d(smem + OFF_K + s * 32768 + cb * 8192, &map_k, &full[s], cb * 64, kvh, int(kt0), b);
+          tma_load_4d(smem + OFF_V + s * 32768 + cb * 8192, &map_v, &full[s], cb * 64, kvh, int(kt0), b);
+        }
+      }
+      issued = t + 1;
+      float *kf = reinterpret_cast<float *>(smem + OFF_KF + s * 256);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int c = lane + 32 * h;
+        const int64_t j = kt0 + c;
+        bool ok = j < p.Tk;
+        if (ok && p.key_valid) ok = p.key_valid[int64_t(b) * p.valid_bs + j] != 0;
+        kf[c] = ok ? 1.f : 0.f;
+      }
+      __syncwarp();
+      mbar_arrive(&full[s]);
+    }
+    // drain: every issued copy must have landed before the CTA may exit
+    volatile int drain_flag = 0;
+    if (ntiles > 0 && lane == 0) mbar_wait(qbar, 0, &drain_flag, ERR_SP_Q);
+    for (int t = (issued > 2 ? issued - 2 : 0); t < issued; ++t)
+      mbar_wait(&full[t & 1], (t >> 1) & 1, &drain_flag, ERR_SP_FULL);
+  } else if (warp == 1) {
+    // ===================== MMA issuer (one thread) =====================
+    if (lane == 0 && ntiles > 0) {
+      bool ok = true;
+      auto wait = [&](uint64_t *bar, uint32_t parity, int code) {
+        ok = ok && mbar_wait(bar, parity, abort_flag, code);
+        tc_fence_after();
+        return ok;
+      };
+      wait(qbar, 0, ERR_SP_Q);
+      const uint32_t q = smem_u32(smem + OFF_Q);
+      for (int t = 0; t <= ntiles && ok; ++t) {
+        if (t < ntiles) {
+          const int s = t & 1;
+          if (!wait(&full[s], (t >> 1) & 1, ERR_SP_FULL)) break;
+          if (t >= 2 && !wait(&s_free[s], ((t >> 1) - 1) & 1, ERR_SP_FREE)) break;
+          const uint32_t k = smem_u32(smem + OFF_K + s * 32768);
+#pragma unroll
+          for (int kk = 0; kk < 16; ++kk)
+            mma_bf16(tmem + T_S + s * 64, sdesc(q + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+                     sdesc(k + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024), ID_S, kk > 0);
+          mma_commit(&s_full[s]);
+        }
+        if (t >= 1) {
+          const int u = t - 1, pb = u & 1;
+          if (!wait(&p_ready[pb], (u >> 1) & 1, ERR_SP_P)) break;
+          const uint32_t pp = smem_u32(smem + OFF_P + pb * 16384);
+          const uint32_t v = smem_u32(smem + OFF_V + pb * 32768);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_bf16(tmem + T_O, sdesc(pp + kk * 32, 16, 1024), sdesc(v + kk * 2048, 8192, 1024), ID_O,
+                     u > 0 || kk > 0);
+          mma_commit(&o_done[pb]);
+          mma_commit(&empty[pb]);
+        }
+      }
+      // all issued MMAs finished before TMEM is released
+      mma_commit(done_bar);
+      mbar_wait(done_bar, 0, abort_flag, ERR_SP_DONE);
+    }
+    __syncwarp();
+  } else {
+    // ===================== softmax and output (one query row per thread) =====================
+    const int r = (warp & 3) * 32 + lane;
+    const uint32_t lane_base = tmem + (uint32_t((warp & 3) * 32) << 16);
+    const int64_t qp = qp0 + r / p.R;
+    const int64_t qabs = p.query_start + qp;
+    bool ok = true;
+    float m_run = -INFINITY, l = 0.f;
+    for (int t = 0; t < ntiles; ++t) {
+      const int s = t & 1;
+      const int64_t kt0 = lo + int64_t(t) * KT;
+      // the tile's flags (acquired from the producer) and its S
+      ok = ok && mbar_wait(&full[s], (t >> 1) & 1, abort_flag, ERR_SP_FULL);
+      ok = ok && mbar_wait(&s_full[s], (t >> 1) & 1, abort_flag, ERR_SP_S);
+      tc_fence_after();
+      if (!ok) break;
+      float x[64];
+      tmem_ld32(lane_base + T_S + s * 64, x);
+      tmem_ld32(lane_base + T_S + s * 64 + 32, x + 32);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&s_free[s]);
+      const float *kf = reinterpret_cast<const float *>(smem + OFF_KF + s * 256);
+      float mt = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const int64_t j = kt0 + c;
+        const bool allowed = kf[c] != 0.f && j <= qabs && j > qabs - p.window;
+        x[c] = allowed ? x[c] * p.scale_log2 : -INFINITY;
+        mt = fmaxf(mt, x[c]);
+      }
+      const float m_new = fmaxf(m_run, mt);
+      if (m_new > m_run + kRescale) {
+        // the running max grows by more than 2^8: rescale O (once the previous
+        // tile's PV has landed) and l to the new max
+        if (m_run != -INFINITY) {
+          const float f = exp2f(m_run - m_new);
+          ok = mbar_wait(&o_done[(t - 1) & 1], ((t - 1) >> 1) & 1, abort_flag, ERR_SP_O);
+          tc_fence_after();
+          if (!ok) break;
+#pragma unroll 1
+          for (int q4 = 0; q4 < 8; ++q4) {
+            float o[32];
+            tmem_ld32(lane_base + T_O + q4 * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int d = 0; d < 32; ++d) o[d] *= f;
+            tmem_st32(lane_base + T_O + q4 * 32, o);
+          }
+          tmem_wait_st();
+          l *= f;
+        }
+        m_run = m_new;
+      }
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        x[c] = x[c] == -INFINITY ? 0.f : exp2f(x[c] - m_run);
+        l += x[c];
+      }
+      // P buffer t & 1 was last read by the PV MMA of tile t - 2
+      if (t >= 2) ok = mbar_wait(&o_done[s], ((t - 2) >> 1) & 1, abort_flag, ERR_SP_O);
+      if (!ok) break;
+      st_row64_bf16(smem + OFF_P + s * 16384, 128, 0, r, x);
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_ready[s]);
+    }
+    if (ok && ntiles > 0) {
+      ok = mbar_wait(&o_done[(ntiles - 1) & 1], ((ntiles - 1) >> 1) & 1, abort_flag, ERR_SP_O);
+      tc_fence_after();
+    }
+    // ---- O / l (zero for a query without admitted keys or marked invalid) staged over Q ----
+    bool row_valid = qp < p.Tq && l > 0.f;
+    if (row_valid && p.key_valid) row_valid = qabs < p.Tk && p.key_valid[int64_t(b) * p.valid_bs + qabs] != 0;
+    const float inv = row_valid ? 1.f / l : 0.f;
+    const bool use_o = ok && ntiles > 0;
+#pragma unroll 1
+    for (int cb = 0; cb < 4; ++cb) {
+      float o[64];
+      if (use_o) {
+        tmem_ld32(lane_base + T_O + cb * 64, o);
+        tmem_ld32(lane_base + T_O + cb * 64 + 32, o + 32);
+        tmem_wait_ld();
+      }
+#pragma unroll
+      for (int d = 0; d < 64; ++d) o[d] = use_o ? o[d] * inv : 0.f;
+      st_row64_bf16(smem + OFF_Q + cb * 16384, 128, 0, r, o);
+    }
+    fence_async_smem();
+    ok = epi_sync_and(ok);
+    if (r == 0 && ok) {
+#pragma unroll
+      for (int cb = 0; cb < 4; ++cb) tma_store_4d(&map_o, smem + OFF_Q + cb * 16384, cb * 64, kvh * p.R, int(qp0), b);
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// [B, T, H, 256] bf16, boxes of `pos` positions x `heads` heads x 64 features of one row
+int make_map(CUtensorMap *map, const void *base, int64_t B, int64_t T, int64_t H, int heads, int pos) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return set_error(YB_ERR_CUDA, "swa prefill: cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[4] = {cuuint64_t(D), cuuint64_t(H), cuuint64_t(T), cuuint64_t(B)};
+  const cuuint64_t strides[3] = {cuuint64_t(D) * 2, cuuint64_t(H) * D * 2, cuuint64_t(T) * H * D * 2};
+  const cuuint32_t box[4] = {64, cuuint32_t(heads), cuuint32_t(pos), 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(YB_ERR_CUDA, "swa prefill: tensor map encode failed (%d)", int(r));
+  return YB_OK;
+}
+
+}  // namespace
+
+bool swa_prefill_tc_supported(const SwaPrefillArgs &a) {
+  const int64_t R = a.KVH > 0 ? a.QH / a.KVH : 0;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.k) |
+                         reinterpret_cast<uintptr_t>(a.v) | reinterpret_cast<uintptr_t>(a.out)) & 15u) == 0;
+  return a.dtype == YB_BF16 && a.D == D && a.QH % a.KVH == 0 && (R == 1 || R == 2 || R == 4 || R == 8) &&
+         a.window >= 1 && aligned && a.Tq <= (int64_t(1) << 30) && a.Tk <= (int64_t(1) << 30);
+}
+
+int launch_swa_prefill_tc(const SwaPrefillArgs &a) {
+  if (a.B * a.Tq == 0) return YB_OK;
+  if (!swa_prefill_tc_supported(a))
+    return set_error(YB_ERR_UNSUPPORTED, "swa prefill: bf16, D = 256, QH / KVH in 1/2/4/8, 16-byte aligned only");
+  const int R = int(a.QH / a.KVH), P = 128 / R;
+  CUtensorMap mq, mk, mv, mo;
+  int rc = make_map(&mq, a.q, a.B, a.Tq, a.QH, R, P);
+  if (!rc) rc = make_map(&mo, a.out, a.B, a.Tq, a.QH, R, P);
+  if (!rc) rc = make_map(&mk, a.k, a.B, a.Tk, a.KVH, 1, KT);
+  if (!rc) rc = make_map(&mv, a.v, a.B, a.Tk, a.KVH, 1, KT);
+  if (rc) return rc;
+  SpParams p{};
+  p.key_valid = a.key_valid;
+  p.valid_bs = a.valid_bs;
+  p.Tq = a.Tq; p.Tk = a.Tk; p.KVH = a.KVH; p.window = a.window; p.query_start = a.query_start;
+  p.R = R; p.P = P;
+  p.qtiles = (a.Tq + P - 1) / P;
+  p.scale_log2 = float(1.4426950408889634 / sqrt(double(D)));
+  cudaError_t e = cudaFuncSetAttribute(swa_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(SMEM_BYTES));
+  if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "swa prefill: smem attribute: %s", cudaGetErrorString(e));
+  const int64_t grid = a.B * a.KVH * p.qtiles;
+  swa_prefill_tc_kernel<<<unsigned(grid), NT, SMEM_BYTES, a.stream>>>(mq, mk, mv, mo, p);
+  return check_launch("swa_prefill_tc_kernel");
+}
+
+int read_device_error_swa(int clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, tc::g_device_error, sizeof(int)) != cudaSuccess) return -1;
+  if (clear && v) {
+    const int z = 0;
+    cudaMemcpyToSymbol(tc::g_device_error, &z, sizeof(int));
+  }
+  return v;
+}
+
+}  // namespace yb

@@ -16,6 +16,12 @@ reference's call shapes.
         first use as the reference builds it (`initialize_physical_ring`,
         same file :555-598)
 
+    reference_swa(q, k, v, *, window, key_valid=None, query_start=0)
+        modeling_yanchor.py:412-427: sliding-window attention over a prompt
+        (tcgen05 kernel)
+    flash_swa(q, k, v, *, window, attention_mask)
+        modeling_yanchor.py:429-449: the same over each row's valid tokens
+
 Ring key / value ``[B, KVH, W, D]`` (positions contiguous inside each head),
 valid ``[B, W]`` bool, ring_index a device int32 (as the reference keeps it)
 or int64 scalar tensor.
@@ -153,3 +159,62 @@ def layer_ring_update(layer_cache, key, value, valid):
     return physical_ring_update_(getattr(layer_cache, _RING + 'keys'), getattr(layer_cache, _RING + 'values'),
                                  getattr(layer_cache, _RING + 'valid'), getattr(layer_cache, _RING + 'index'),
                                  key, value, valid)
+
+
+def reference_swa(q, k, v, *, window, key_valid=None, query_start=0):
+    """Sliding-window attention over a prompt, modeling_yanchor.py:412-427:
+    queries ``[B, Tq, QH, D]`` at positions ``query_start ..`` attend to keys
+    ``[B, Tk, KVH, D]`` at positions ``0 .. Tk - 1`` within ``window`` (causal),
+    masked by ``key_valid [B, Tk]``; a query whose own ``key_valid`` entry is
+    False gives zeros.  One tcgen05 kernel launch (bf16, D = 256)."""
+    require_cuda(q, k, v, key_valid)
+    if q.dim() != 4 or k.dim() != 4 or k.shape != v.shape or q.shape[0] != k.shape[0] or q.shape[3] != k.shape[3]:
+        raise ValueError('reference_swa expects q [B, Tq, QH, D] and k, v [B, Tk, KVH, D]')
+    if q.shape[2] % k.shape[2]:
+        raise ValueError('query heads must be a multiple of key heads')
+    if not (q.dtype == k.dtype == v.dtype):
+        raise TypeError('q, k, v must share a dtype')
+    B, Tq, QH, D = q.shape
+    Tk, KVH = k.shape[1], k.shape[2]
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    kv = None
+    if key_valid is not None:
+        if key_valid.shape != (B, Tk):
+            raise ValueError('key_valid must be [B, Tk]')
+        kv = key_valid.to(torch.bool).contiguous()
+    out = torch.empty_like(q)
+    rc = _lib.lib().yb_swa_prefill_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                             None if kv is None else kv.data_ptr(), Tk, out.data_ptr(), B, Tq, Tk,
+                                             QH, KVH, D, int(window), int(query_start), dtype_code(q),
+                                             stream_ptr(q.device))
+    _lib.check(rc, 'reference_swa')
+    return out
+
+
+def flash_swa(q, k, v, *, window, attention_mask):
+    """The prefill SWA of the CUDA path, modeling_yanchor.py:429-449: causal
+    window of ``window`` tokens; with ``attention_mask`` ([B, >= T], the last T
+    columns belong to this prompt) over each row's valid tokens in order, as
+    the reference's unpad / variable-length FlashAttention call does, padded
+    positions giving zeros.  Rows whose valid tokens form one run (left or
+    right padding) run in place; other rows are packed valid-first, run, and
+    scattered back."""
+    require_cuda(q, k, v)
+    if attention_mask is None:
+        return reference_swa(q, k, v, window=window)
+    B, T = q.shape[:2]
+    mask = attention_mask[:, -T:].to(device=q.device, dtype=torch.bool)
+    m8 = mask.to(torch.int8)
+    starts = (m8[:, 1:] > m8[:, :-1]).sum(1) + m8[:, 0]
+    if bool((starts <= 1).all()):
+        return reference_swa(q, k, v, window=window, key_valid=mask)
+    order = torch.argsort((~mask).to(torch.int8), dim=1, stable=True)          # valid tokens first, in order
+    n = mask.sum(1)
+    packed_valid = torch.arange(T, device=q.device)[None, :] < n[:, None]
+
+    def pack(x):
+        return torch.gather(x, 1, order[:, :, None, None].expand(x.shape))
+    out_packed = reference_swa(pack(q), pack(k), pack(v), window=window, key_valid=packed_valid)
+    out = torch.zeros_like(q)
+    out.scatter_(1, order[:, :, None, None].expand(out.shape), out_packed)
+    return out
