@@ -71,6 +71,12 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap *map, const void 
                ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z), "r"(w)
                : "memory");
 }
+// 2^x on the special-function unit (PTX ex2.approx.ftz; 2^-inf = +0)
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 // the softmax warps' named barrier (barrier 1, 128 threads), ANDing a status
 __device__ __forceinline__ bool epi_sync_and(bool ok) {
   uint32_t res;
@@ -222,6 +228,7 @@ __global__ void __launch_bounds__(NT, 1)
     const uint32_t lane_base = tmem + (uint32_t((warp & 3) * 32) << 16);
     const int64_t qp = qp0 + r / p.R;
     const int64_t qabs = p.query_start + qp;
+    const bool has_valid = p.key_valid != nullptr;
     bool ok = true;
     float m_run = -INFINITY, l = 0.f;
     for (int t = 0; t < ntiles; ++t) {
@@ -239,20 +246,36 @@ __global__ void __launch_bounds__(NT, 1)
       tc_fence_before();
       mbar_arrive(&s_free[s]);
       const float *kf = reinterpret_cast<const float *>(smem + OFF_KF + s * 256);
-      float mt = -INFINITY;
+      // key c of the tile sits d0 - c positions before this query: admitted when
+      // 0 <= d0 - c < window and its flag is set; most tiles lie wholly inside
+      // the window and skip the mask
+      const int d0 = int(qabs - kt0);
+      const bool whole = !has_valid && kt0 + KT <= p.Tk && d0 >= KT - 1 && d0 < p.window;
+      float mx[8];
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const int64_t j = kt0 + c;
-        const bool allowed = kf[c] != 0.f && j <= qabs && j > qabs - p.window;
-        x[c] = allowed ? x[c] * p.scale_log2 : -INFINITY;
-        mt = fmaxf(mt, x[c]);
+      for (int u = 0; u < 8; ++u) mx[u] = -INFINITY;
+      if (whole) {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          x[c] *= p.scale_log2;
+          mx[c & 7] = fmaxf(mx[c & 7], x[c]);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          const bool allowed = unsigned(d0 - c) < unsigned(p.window) && kf[c] != 0.f;
+          x[c] = allowed ? x[c] * p.scale_log2 : -INFINITY;
+          mx[c & 7] = fmaxf(mx[c & 7], x[c]);
+        }
       }
+      const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                             fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
       const float m_new = fmaxf(m_run, mt);
       if (m_new > m_run + kRescale) {
         // the running max grows by more than 2^8: rescale O (once the previous
         // tile's PV has landed) and l to the new max
         if (m_run != -INFINITY) {
-          const float f = exp2f(m_run - m_new);
+          const float f = ex2(m_run - m_new);
           ok = mbar_wait(&o_done[(t - 1) & 1], ((t - 1) >> 1) & 1, abort_flag, ERR_SP_O);
           tc_fence_after();
           if (!ok) break;
@@ -270,11 +293,17 @@ __global__ void __launch_bounds__(NT, 1)
         }
         m_run = m_new;
       }
+      // (m_run is -inf only while every key so far was masked: then all p are 0)
+      float ls[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) ls[u] = 0.f;
+      const bool live = m_run != -INFINITY;
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
-        x[c] = x[c] == -INFINITY ? 0.f : exp2f(x[c] - m_run);
-        l += x[c];
+        x[c] = live ? ex2(x[c] - m_run) : 0.f;
+        ls[c & 7] += x[c];
       }
+      l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
       // P buffer t & 1 was last read by the PV MMA of tile t - 2
       if (t >= 2) ok = mbar_wait(&o_done[s], ((t - 2) >> 1) & 1, abort_flag, ERR_SP_O);
       if (!ok) break;
