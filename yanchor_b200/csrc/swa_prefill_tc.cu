@@ -10,8 +10,10 @@
 // rows are the (position, head) pairs of the group's R heads, brought in by
 // TMA in that order.  The keys the tile can see (at most window + P - 1)
 // stream through in 64-key tiles:
-//   warp 0   TMA producer: Q once; K / V tiles double-buffered, with each
-//            tile's key-validity flags
+//   warp 0   TMA producer of Q (once) and the K tiles, warp 6 of the V tiles;
+//            each double-buffered, K released when its S MMA is done and V
+//            when its PV MMA is done, so the next K tile streams in while the
+//            softmax and PV of the current one run
 //   warp 1   TMEM allocator and MMA issuer: S(t) = Q K(t)^T (M=128, N=64,
 //            K=256) into one of two TMEM buffers, then O += P(t-1) V(t-1)
 //            (N=256), so a tile's softmax overlaps the previous tile's PV
@@ -32,14 +34,13 @@ namespace {
 
 using namespace tc;
 
-constexpr int D = 256, NT = 192, KT = 64;
+constexpr int D = 256, NT = 224, KT = 64;
 constexpr uint32_t OFF_Q = 0;              // Q: 4 column blocks x 128 rows x 128 B (later the O staging)
 constexpr uint32_t OFF_K = 65536;          // K: 2 stages x 4 column blocks x 64 rows x 128 B
 constexpr uint32_t OFF_V = 131072;         // V: same
 constexpr uint32_t OFF_P = 196608;         // P: 2 buffers x 128 rows x 64 keys bf16 (SW128)
-constexpr uint32_t OFF_KF = 229376;        // key flags: 2 stages x 64 floats
-constexpr uint32_t OFF_BAR = OFF_KF + 512;
-constexpr uint32_t OFF_MISC = OFF_BAR + 16 * 8;
+constexpr uint32_t OFF_BAR = 229376;
+constexpr uint32_t OFF_MISC = OFF_BAR + 20 * 8;
 constexpr uint32_t SMEM_BYTES = OFF_MISC + 16;
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 constexpr uint32_t T_S = 0;                // 2 x 64 columns
@@ -97,13 +98,15 @@ __global__ void __launch_bounds__(NT, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
   uint64_t *qbar = bars + 0;
-  uint64_t *full = bars + 1;       // [2] K / V tile and its flags landed (32 + tx)
-  uint64_t *empty = bars + 3;      // [2] the tile's O MMA finished (1)
+  uint64_t *full_k = bars + 1;     // [2] K tile landed (1 + tx)
+  uint64_t *empty_k = bars + 3;    // [2] the tile's S MMA finished (1)
   uint64_t *s_full = bars + 5;     // [2] S of the tile in TMEM (1)
   uint64_t *s_free = bars + 7;     // [2] the softmax warps have read that S buffer (128)
   uint64_t *p_ready = bars + 9;    // [2] P of the tile written, O rescaled if needed (128)
   uint64_t *o_done = bars + 11;    // [2] O += P V of the tile finished (1)
   uint64_t *done_bar = bars + 13;
+  uint64_t *full_v = bars + 14;    // [2] V tile landed (1 + tx)
+  uint64_t *empty_v = bars + 16;   // [2] the tile's PV MMA finished (1)
   uint32_t *tmem_base_smem = reinterpret_cast<uint32_t *>(smem + OFF_MISC);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OFF_MISC + 4);
 
@@ -123,8 +126,10 @@ __global__ void __launch_bounds__(NT, 1)
     if (*abort_flag) atomicCAS(&g_device_error, 0, ERR_SP_Q);
     mbar_init(qbar, 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&full[s], 32);
-      mbar_init(&empty[s], 1);
+      mbar_init(&full_k[s], 1);
+      mbar_init(&empty_k[s], 1);
+      mbar_init(&full_v[s], 1);
+      mbar_init(&empty_v[s], 1);
       mbar_init(&s_full[s], 1);
       mbar_init(&s_free[s], 128);
       mbar_init(&p_ready[s], 128);
@@ -139,48 +144,39 @@ __global__ void __launch_bounds__(NT, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_base_smem;
 
-  if (warp == 0) {
-    // ===================== producer =====================
-    if (lane == 0 && ntiles > 0 && !*abort_flag) {
-      prefetch_tensormap(&map_q);
-      prefetch_tensormap(&map_k);
-      prefetch_tensormap(&map_v);
-      mbar_arrive_expect_tx(qbar, 4 * 16384);
+  if (warp == 0 || warp == 6) {
+    // ===================== producers: Q and K (warp 0), V (warp 6) =====================
+    if (lane == 0) {
+      const bool is_k = warp == 0;
+      if (is_k && ntiles > 0 && !*abort_flag) {
+        prefetch_tensormap(&map_q);
+        prefetch_tensormap(&map_k);
+        mbar_arrive_expect_tx(qbar, 4 * 16384);
 #pragma unroll
-      for (int cb = 0; cb < 4; ++cb)
-        tma_load_4d(smem + OFF_Q + cb * 16384, &map_q, qbar, cb * 64, kvh * p.R, int(qp0), b);
-    }
-    int issued = 0;
-    for (int t = 0; t < ntiles && !*abort_flag; ++t) {
-      const int s = t & 1;
-      const int64_t kt0 = lo + int64_t(t) * KT;
-      if (t >= 2 && !mbar_wait(&empty[s], ((t >> 1) - 1) & 1, abort_flag, ERR_SP_EMPTY)) break;
-      if (lane == 0) {
-        mbar_expect_tx(&full[s], 8 * 8192);
-#pragma unroll
-        for (int cb = 0; cb < 4; ++cb) {
-          tma_load_4d(smem + OFF_K + s * 32768 + cb * 8192, &map_k, &full[s], cb * 64, kvh, int(kt0), b);
-          tma_load_4d(smem + OFF_V + s * 32768 + cb * 8192, &map_v, &full[s], cb * 64, kvh, int(kt0), b);
-        }
+        for (int cb = 0; cb < 4; ++cb)
+          tma_load_4d(smem + OFF_Q + cb * 16384, &map_q, qbar, cb * 64, kvh * p.R, int(qp0), b);
       }
-      issued = t + 1;
-      float *kf = reinterpret_cast<float *>(smem + OFF_KF + s * 256);
+      if (!is_k) prefetch_tensormap(&map_v);
+      uint64_t *fullb = is_k ? full_k : full_v, *emptyb = is_k ? empty_k : empty_v;
+      const CUtensorMap *map = is_k ? &map_k : &map_v;
+      uint8_t *base = smem + (is_k ? OFF_K : OFF_V);
+      int issued = 0;
+      for (int t = 0; t < ntiles && !*abort_flag; ++t) {
+        const int s = t & 1;
+        if (t >= 2 && !mbar_wait(&emptyb[s], ((t >> 1) - 1) & 1, abort_flag, ERR_SP_EMPTY)) break;
+        mbar_arrive_expect_tx(&fullb[s], 4 * 8192);
+        const int kt0 = int(lo + int64_t(t) * KT);
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int c = lane + 32 * h;
-        const int64_t j = kt0 + c;
-        bool ok = j < p.Tk;
-        if (ok && p.key_valid) ok = p.key_valid[int64_t(b) * p.valid_bs + j] != 0;
-        kf[c] = ok ? 1.f : 0.f;
+        for (int cb = 0; cb < 4; ++cb) tma_load_4d(base + s * 32768 + cb * 8192, map, &fullb[s], cb * 64, kvh, kt0, b);
+        issued = t + 1;
       }
-      __syncwarp();
-      mbar_arrive(&full[s]);
+      // drain: every issued copy must have landed before the CTA may exit
+      volatile int drain_flag = 0;
+      if (is_k && ntiles > 0) mbar_wait(qbar, 0, &drain_flag, ERR_SP_Q);
+      for (int t = (issued > 2 ? issued - 2 : 0); t < issued; ++t)
+        mbar_wait(&fullb[t & 1], (t >> 1) & 1, &drain_flag, ERR_SP_FULL);
     }
-    // drain: every issued copy must have landed before the CTA may exit
-    volatile int drain_flag = 0;
-    if (ntiles > 0 && lane == 0) mbar_wait(qbar, 0, &drain_flag, ERR_SP_Q);
-    for (int t = (issued > 2 ? issued - 2 : 0); t < issued; ++t)
-      mbar_wait(&full[t & 1], (t >> 1) & 1, &drain_flag, ERR_SP_FULL);
+    __syncwarp();
   } else if (warp == 1) {
     // ===================== MMA issuer (one thread) =====================
     if (lane == 0 && ntiles > 0) {
@@ -195,7 +191,7 @@ __global__ void __launch_bounds__(NT, 1)
       for (int t = 0; t <= ntiles && ok; ++t) {
         if (t < ntiles) {
           const int s = t & 1;
-          if (!wait(&full[s], (t >> 1) & 1, ERR_SP_FULL)) break;
+          if (!wait(&full_k[s], (t >> 1) & 1, ERR_SP_FULL)) break;
           if (t >= 2 && !wait(&s_free[s], ((t >> 1) - 1) & 1, ERR_SP_FREE)) break;
           const uint32_t k = smem_u32(smem + OFF_K + s * 32768);
 #pragma unroll
@@ -203,10 +199,11 @@ __global__ void __launch_bounds__(NT, 1)
             mma_bf16(tmem + T_S + s * 64, sdesc(q + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
                      sdesc(k + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024), ID_S, kk > 0);
           mma_commit(&s_full[s]);
+          mma_commit(&empty_k[s]);
         }
         if (t >= 1) {
           const int u = t - 1, pb = u & 1;
-          if (!wait(&p_ready[pb], (u >> 1) & 1, ERR_SP_P)) break;
+          if (!wait(&p_ready[pb], (u >> 1) & 1, ERR_SP_P) || !wait(&full_v[pb], (u >> 1) & 1, ERR_SP_FULL)) break;
           const uint32_t pp = smem_u32(smem + OFF_P + pb * 16384);
           const uint32_t v = smem_u32(smem + OFF_V + pb * 32768);
 #pragma unroll
@@ -214,7 +211,7 @@ __global__ void __launch_bounds__(NT, 1)
             mma_bf16(tmem + T_O, sdesc(pp + kk * 32, 16, 1024), sdesc(v + kk * 2048, 8192, 1024), ID_O,
                      u > 0 || kk > 0);
           mma_commit(&o_done[pb]);
-          mma_commit(&empty[pb]);
+          mma_commit(&empty_v[pb]);
         }
       }
       // all issued MMAs finished before TMEM is released
@@ -234,8 +231,6 @@ __global__ void __launch_bounds__(NT, 1)
     for (int t = 0; t < ntiles; ++t) {
       const int s = t & 1;
       const int64_t kt0 = lo + int64_t(t) * KT;
-      // the tile's flags (acquired from the producer) and its S
-      ok = ok && mbar_wait(&full[s], (t >> 1) & 1, abort_flag, ERR_SP_FULL);
       ok = ok && mbar_wait(&s_full[s], (t >> 1) & 1, abort_flag, ERR_SP_S);
       tc_fence_after();
       if (!ok) break;
@@ -245,10 +240,9 @@ __global__ void __launch_bounds__(NT, 1)
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&s_free[s]);
-      const float *kf = reinterpret_cast<const float *>(smem + OFF_KF + s * 256);
       // key c of the tile sits d0 - c positions before this query: admitted when
-      // 0 <= d0 - c < window and its flag is set; most tiles lie wholly inside
-      // the window and skip the mask
+      // 0 <= d0 - c < window, it exists (kt0 + c < Tk) and its key_valid flag
+      // is set; most tiles lie wholly inside the window and skip the mask
       const int d0 = int(qabs - kt0);
       const bool whole = !has_valid && kt0 + KT <= p.Tk && d0 >= KT - 1 && d0 < p.window;
       float mx[8];
@@ -261,9 +255,11 @@ __global__ void __launch_bounds__(NT, 1)
           mx[c & 7] = fmaxf(mx[c & 7], x[c]);
         }
       } else {
+        const int nk = int(p.Tk - kt0 < KT ? p.Tk - kt0 : KT);
+        const uint8_t *kv = has_valid ? p.key_valid + int64_t(b) * p.valid_bs + kt0 : nullptr;
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
-          const bool allowed = unsigned(d0 - c) < unsigned(p.window) && kf[c] != 0.f;
+          const bool allowed = unsigned(d0 - c) < unsigned(p.window) && c < nk && (!has_valid || kv[c] != 0);
           x[c] = allowed ? x[c] * p.scale_log2 : -INFINITY;
           mx[c & 7] = fmaxf(mx[c & 7], x[c]);
         }
