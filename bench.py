@@ -47,6 +47,7 @@ L_GDN, L_MEM = 24, 8
 H_K, H_V, DK, DV = 16, 32, 128, 128
 CONV_C, CONV_KS = 2 * H_K * DK + H_V * DV, 4     # the short convolution over the fused q/k/v projection
 MEM_G, MEM_H, MEM_D, MEM_CAP, MEM_CHUNK = 4, 16, 256, 64, 64
+SW_QH, SW_KVH, SW_W, SW_D = 16, 4, 1024, 256       # the SWA layers: window 1024 (modeling_yanchor.py:451)
 VOCAB = 248320
 GEN_TOKENS = 32768                                # config 3: 32K generated tokens per sequence
 PAD_ID, EOS_IDS = 248044, ()                      # fixed-length generation: no end ids (runtime/inference.py:94)
@@ -427,7 +428,6 @@ def run_gpu(args, rank, world, local_rank, dist):
         ms16 = shard.max_over_ranks(ms16, device=device)
 
     # ---- sliding-window attention decode over the physical ring (the 8 SWA layers, an (f) row) ----
-    SW_QH, SW_KVH, SW_W, SW_D = 16, 4, 1024, 256
     bf = torch.bfloat16
     rings = [(torch.randn(B, SW_KVH, SW_W, SW_D, device=device).to(bf),
               torch.randn(B, SW_KVH, SW_W, SW_D, device=device).to(bf),
@@ -550,6 +550,16 @@ def run_prefill(torch, yb, device, hbm, tf_burst, peak_kind):
     for _ in range(2):
         seq()
     seq_ms = time_events(torch, seq, 3, stream)
+    # sliding-window attention over the same prompts (an SWA layer: 16 query heads
+    # over 4 KV heads, D=256, window 1024); free the GDN inputs first
+    del q, k, v, mq, mq2, wk, wv
+    sq = torch.randn(B, T, SW_QH, SW_D, generator=gen, device=device).to(bf)
+    skv = torch.randn(2, B, T, SW_KVH, SW_D, generator=gen, device=device).to(bf)
+    for _ in range(2):
+        yb.reference_swa(sq, skv[0], skv[1], window=SW_W)
+    swa_ms = time_events(torch, lambda: yb.reference_swa(sq, skv[0], skv[1], window=SW_W), 3, stream)
+    swa_flops = B * SW_QH * sum(min(t + 1, SW_W) for t in range(T)) * 4 * SW_D
+    del sq, skv
     achieved = flops / (ms / 1e3) / 1e12
     return {'workload': 'config 1: chunked prefill B=8 T=8192 H=HV=32 K=V=128 bf16, fp32 state; '
                         'plus the anchor prefill of one memory layer (64 slots, G=4 H=16 D=256, chunk 64)',
@@ -557,6 +567,11 @@ def run_prefill(torch, yb, device, hbm, tf_burst, peak_kind):
             'anchor_prefix_topk_ms': round(topk_ms, 3), 'anchor_sequence_ms': round(seq_ms, 3),
             'tok_s_with_anchor_read': round(B * T / ((ms + mem_ms) / 1e3), 1),
             'tok_s_with_anchor_prefill': round(B * T / ((ms + seq_ms) / 1e3), 1),
+            'swa_prefill': {'ms': round(swa_ms, 3), 'how': f'reference_swa over the same prompts: {SW_QH} query heads '
+                            f'over {SW_KVH} KV heads, D={SW_D}, window {SW_W}, tcgen05',
+                            'tflops': round(swa_flops / (swa_ms / 1e3) / 1e12, 1),
+                            'frac': round(swa_flops / (swa_ms / 1e3) / 1e12 / tf_burst, 4),
+                            'flops_per_launch': swa_flops},
             'roofline': {'bound': 'tensor', 'kernel': 'gdn chunk', 'achieved': round(achieved, 2), 'peak': tf_burst,
                          'unit': 'TFLOP/s', 'frac': round(achieved / tf_burst, 4), 'peak_kind': peak_kind,
                          'flops_per_launch': flops}}
@@ -580,6 +595,11 @@ def run_only(args):
         beta = torch.randn(Bp, T, H, generator=gen, device=dev).sigmoid().to(bf)
         fn = lambda: yb.chunk_gated_delta_rule(q, k, v, g, beta, output_final_state=True,  # noqa: E731
                                                use_qk_l2norm_in_kernel=True)
+    elif args.only == 'swa_prefill':
+        Bp, T = args.prefill_batch, 8192
+        sq = torch.randn(Bp, T, SW_QH, SW_D, generator=gen, device=dev).to(bf)
+        skv = torch.randn(2, Bp, T, SW_KVH, SW_D, generator=gen, device=dev).to(bf)
+        fn = lambda: yb.reference_swa(sq, skv[0], skv[1], window=SW_W)  # noqa: E731
     elif args.only == 'mem_indexed':
         blocks = 128
         mq = torch.randn(8, blocks, 64, MEM_H, MEM_D, generator=gen, device=dev).to(bf)
@@ -721,7 +741,7 @@ def main():
     ap.add_argument('--no-prefill', action='store_true')
     ap.add_argument('--no-cpu', action='store_true')
     ap.add_argument('--only', choices=['conv_update', 'gdn_decode', 'gdn_fused', 'gdn_chunk', 'mem_read', 'mem_commit', 'mem_indexed', 'mem_topk',
-                                       'mem_sequence', 'swa', 'greedy',
+                                       'mem_sequence', 'swa', 'swa_prefill', 'greedy',
                                        'topk'], help='run one kernel family (small ncu captures)')
     ap.add_argument('--prefill-batch', type=int, default=8)
     args = ap.parse_args()
