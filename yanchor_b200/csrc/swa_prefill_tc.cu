@@ -10,21 +10,26 @@
 // rows are the (position, head) pairs of the group's R heads, brought in by
 // TMA in that order.  The keys the tile can see (at most window + P - 1)
 // stream through in 64-key tiles:
-//   warp 0   TMA producer of Q (once) and the K tiles, warp 6 of the V tiles;
-//            each double-buffered, K released when its S MMA is done and V
-//            when its PV MMA is done, so the next K tile streams in while the
-//            softmax and PV of the current one run
-//   warp 1   TMEM allocator and MMA issuer: S(t) = Q K(t)^T (M=128, N=64,
-//            K=256) into one of two TMEM buffers, then O += P(t-1) V(t-1)
-//            (N=256), so a tile's softmax overlaps the previous tile's PV
-//   warps 2-5  one query row per thread: mask, online softmax in base 2
-//            (O in TMEM is rescaled only when the row max grows by more than
-//            2^8), P as bf16 (as FlashAttention rounds it) into one of two
-//            shared buffers; at the end O / l staged over Q and TMA-stored.
-// Every barrier a role can lag on is indexed by tile parity, so no parity
-// wait can see a barrier two phases ahead.  Every wait is bounded in time; a
-// CTA that gives up records an error code, drains its copies and MMAs, frees
-// TMEM and exits.
+//   warp 0   TMA producer of Q (once) and the K tiles (4 stages, each
+//            released when its S MMA is done)
+//   warp 6   TMA producer of the V tiles (3 stages, each released when its
+//            PV MMA is done)
+//   warp 1   TMEM allocator and S issuer: S(t) = Q K(t)^T (M=128, N=64,
+//            K=256) with Q resident in TMEM, issued as soon as the softmax
+//            warps have read S(t-1), so it runs under their softmax
+//   warp 7   PV issuer: O += P(t) V(t) (N=256) with P in TMEM, issued as soon
+//            as P(t) is there (two issuing threads, so neither waits behind
+//            the other's MMAs; they write disjoint TMEM and commit their own)
+//   warps 2-5  one query row per thread: copy the Q row into TMEM once; per
+//            tile mask, online softmax in base 2 (O is rescaled only when the
+//            row max grows by more than 2^8), P as bf16 (as FlashAttention
+//            rounds it) into one of two TMEM buffers; at the end O / l staged
+//            in shared memory and TMA-stored.
+// Shared memory holds only the K / V stages (224 KB), deep enough to hide
+// the ~2 us a tile's copy takes.  Every barrier a role can lag on is indexed
+// by stage or tile parity, so no parity wait can see a barrier two phases
+// ahead.  Every wait is bounded in time; a CTA that gives up records an
+// error code, drains its copies and MMAs, frees TMEM and exits.
 #include "common.cuh"
 #include "kernels.h"
 #include "tc.cuh"
@@ -34,17 +39,17 @@ namespace {
 
 using namespace tc;
 
-constexpr int D = 256, NT = 224, KT = 64;
-constexpr uint32_t OFF_Q = 0;              // Q: 4 column blocks x 128 rows x 128 B (later the O staging)
-constexpr uint32_t OFF_K = 65536;          // K: 2 stages x 4 column blocks x 64 rows x 128 B
-constexpr uint32_t OFF_V = 131072;         // V: same
-constexpr uint32_t OFF_P = 196608;         // P: 2 buffers x 128 rows x 64 keys bf16 (SW128)
+constexpr int D = 256, NT = 256, KT = 64, KST = 4, VST = 3;
+constexpr uint32_t OFF_K = 0;              // K: 4 stages x 4 column blocks x 64 rows x 128 B (later the O staging)
+constexpr uint32_t OFF_V = 131072;         // V: 3 stages (the first two hold Q until it is in TMEM)
 constexpr uint32_t OFF_BAR = 229376;
-constexpr uint32_t OFF_MISC = OFF_BAR + 20 * 8;
+constexpr uint32_t OFF_MISC = OFF_BAR + 24 * 8;   // 24 mbarriers
 constexpr uint32_t SMEM_BYTES = OFF_MISC + 16;
-static_assert(SMEM_BYTES <= 232448, "shared memory budget");
-constexpr uint32_t T_S = 0;                // 2 x 64 columns
-constexpr uint32_t T_O = 256;              // 256 columns
+static_assert(OFF_V + VST * 32768 <= OFF_BAR && SMEM_BYTES <= 232448, "shared memory budget");
+constexpr uint32_t T_Q = 0;                // Q: 128 columns of packed bf16 pairs
+constexpr uint32_t T_S = 128;              // S: 64 columns
+constexpr uint32_t T_P = 192;              // P: 2 x 32 columns of packed bf16 pairs
+constexpr uint32_t T_O = 256;              // O: 256 columns
 constexpr uint32_t ID_S = idesc_bf16(128, 64, false, false);
 constexpr uint32_t ID_O = idesc_bf16(128, 256, false, true);
 constexpr float kRescale = 8.f;            // log2 of the largest exp2 factor P may carry before O is rescaled
@@ -97,16 +102,17 @@ __global__ void __launch_bounds__(NT, 1)
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
-  uint64_t *qbar = bars + 0;
-  uint64_t *full_k = bars + 1;     // [2] K tile landed (1 + tx)
-  uint64_t *empty_k = bars + 3;    // [2] the tile's S MMA finished (1)
-  uint64_t *s_full = bars + 5;     // [2] S of the tile in TMEM (1)
-  uint64_t *s_free = bars + 7;     // [2] the softmax warps have read that S buffer (128)
-  uint64_t *p_ready = bars + 9;    // [2] P of the tile written, O rescaled if needed (128)
-  uint64_t *o_done = bars + 11;    // [2] O += P V of the tile finished (1)
-  uint64_t *done_bar = bars + 13;
-  uint64_t *full_v = bars + 14;    // [2] V tile landed (1 + tx)
-  uint64_t *empty_v = bars + 16;   // [2] the tile's PV MMA finished (1)
+  uint64_t *qbar = bars + 0;       // Q landed in shared memory (1 + tx)
+  uint64_t *q_ready = bars + 1;    // the softmax warps copied Q into TMEM (128)
+  uint64_t *full_k = bars + 2;     // [4] K tile landed (1 + tx)
+  uint64_t *empty_k = bars + 6;    // [4] the tile's S MMA finished (1)
+  uint64_t *full_v = bars + 10;    // [3] V tile landed (1 + tx)
+  uint64_t *empty_v = bars + 13;   // [3] the tile's PV MMA finished (1)
+  uint64_t *s_full = bars + 16;    // S of the tile in TMEM (1)
+  uint64_t *s_free = bars + 17;    // the softmax warps have read S (128)
+  uint64_t *p_ready = bars + 18;   // [2] P of the tile in TMEM, O rescaled if needed (128)
+  uint64_t *o_done = bars + 20;    // [2] O += P V of the tile finished (1)
+  uint64_t *done_bar = bars + 22;   // [2] all MMAs of the S / PV issuer finished
   uint32_t *tmem_base_smem = reinterpret_cast<uint32_t *>(smem + OFF_MISC);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OFF_MISC + 4);
 
@@ -125,17 +131,23 @@ __global__ void __launch_bounds__(NT, 1)
     *abort_flag = (smem_u32(smem) & 1023u) ? 1 : 0;  // SW128 tiles need a 1024-byte aligned base
     if (*abort_flag) atomicCAS(&g_device_error, 0, ERR_SP_Q);
     mbar_init(qbar, 1);
-    for (int s = 0; s < 2; ++s) {
+    mbar_init(q_ready, 128);
+    for (int s = 0; s < KST; ++s) {
       mbar_init(&full_k[s], 1);
       mbar_init(&empty_k[s], 1);
+    }
+    for (int s = 0; s < VST; ++s) {
       mbar_init(&full_v[s], 1);
       mbar_init(&empty_v[s], 1);
-      mbar_init(&s_full[s], 1);
-      mbar_init(&s_free[s], 128);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 128);
+    for (int s = 0; s < 2; ++s) {
       mbar_init(&p_ready[s], 128);
       mbar_init(&o_done[s], 1);
     }
-    mbar_init(done_bar, 1);
+    mbar_init(&done_bar[0], 1);
+    mbar_init(&done_bar[1], 1);
     mbar_fence_init();
   }
   if (warp == 1) tmem_alloc(tmem_base_smem, 512);
@@ -154,16 +166,22 @@ __global__ void __launch_bounds__(NT, 1)
         mbar_arrive_expect_tx(qbar, 4 * 16384);
 #pragma unroll
         for (int cb = 0; cb < 4; ++cb)
-          tma_load_4d(smem + OFF_Q + cb * 16384, &map_q, qbar, cb * 64, kvh * p.R, int(qp0), b);
+          tma_load_4d(smem + OFF_V + cb * 16384, &map_q, qbar, cb * 64, kvh * p.R, int(qp0), b);
       }
-      if (!is_k) prefetch_tensormap(&map_v);
+      const int nst = is_k ? KST : VST;
       uint64_t *fullb = is_k ? full_k : full_v, *emptyb = is_k ? empty_k : empty_v;
       const CUtensorMap *map = is_k ? &map_k : &map_v;
       uint8_t *base = smem + (is_k ? OFF_K : OFF_V);
       int issued = 0;
-      for (int t = 0; t < ntiles && !*abort_flag; ++t) {
-        const int s = t & 1;
-        if (t >= 2 && !mbar_wait(&emptyb[s], ((t >> 1) - 1) & 1, abort_flag, ERR_SP_EMPTY)) break;
+      bool ok = true;
+      // V's first stages hold Q until the softmax warps have copied it into TMEM
+      if (!is_k && ntiles > 0) {
+        prefetch_tensormap(&map_v);
+        ok = mbar_wait(q_ready, 0, abort_flag, ERR_SP_Q);
+      }
+      for (int t = 0; t < ntiles && ok && !*abort_flag; ++t) {
+        const int s = t % nst;
+        if (t >= nst && !mbar_wait(&emptyb[s], (t / nst - 1) & 1, abort_flag, ERR_SP_EMPTY)) break;
         mbar_arrive_expect_tx(&fullb[s], 4 * 8192);
         const int kt0 = int(lo + int64_t(t) * KT);
 #pragma unroll
@@ -173,50 +191,50 @@ __global__ void __launch_bounds__(NT, 1)
       // drain: every issued copy must have landed before the CTA may exit
       volatile int drain_flag = 0;
       if (is_k && ntiles > 0) mbar_wait(qbar, 0, &drain_flag, ERR_SP_Q);
-      for (int t = (issued > 2 ? issued - 2 : 0); t < issued; ++t)
-        mbar_wait(&fullb[t & 1], (t >> 1) & 1, &drain_flag, ERR_SP_FULL);
+      for (int t = (issued > nst ? issued - nst : 0); t < issued; ++t)
+        mbar_wait(&fullb[t % nst], (t / nst) & 1, &drain_flag, ERR_SP_FULL);
     }
     __syncwarp();
-  } else if (warp == 1) {
-    // ===================== MMA issuer (one thread) =====================
+  } else if (warp == 1 || warp == 7) {
+    // ===================== MMA issuers: S (warp 1), PV (warp 7), one thread each =====================
     if (lane == 0 && ntiles > 0) {
+      const bool is_s = warp == 1;
       bool ok = true;
       auto wait = [&](uint64_t *bar, uint32_t parity, int code) {
         ok = ok && mbar_wait(bar, parity, abort_flag, code);
         tc_fence_after();
         return ok;
       };
-      wait(qbar, 0, ERR_SP_Q);
-      const uint32_t q = smem_u32(smem + OFF_Q);
-      for (int t = 0; t <= ntiles && ok; ++t) {
-        if (t < ntiles) {
-          const int s = t & 1;
-          if (!wait(&full_k[s], (t >> 1) & 1, ERR_SP_FULL)) break;
-          if (t >= 2 && !wait(&s_free[s], ((t >> 1) - 1) & 1, ERR_SP_FREE)) break;
+      if (is_s) {
+        wait(q_ready, 0, ERR_SP_Q);
+        for (int t = 0; t < ntiles && ok; ++t) {
+          const int s = t % KST;
+          if (!wait(&full_k[s], (t / KST) & 1, ERR_SP_FULL)) break;
+          if (t >= 1 && !wait(s_free, (t - 1) & 1, ERR_SP_FREE)) break;
           const uint32_t k = smem_u32(smem + OFF_K + s * 32768);
 #pragma unroll
           for (int kk = 0; kk < 16; ++kk)
-            mma_bf16(tmem + T_S + s * 64, sdesc(q + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
-                     sdesc(k + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024), ID_S, kk > 0);
-          mma_commit(&s_full[s]);
+            mma_bf16_ts(tmem + T_S, tmem + T_Q + kk * 8, sdesc(k + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024),
+                        ID_S, kk > 0);
+          mma_commit(s_full);
           mma_commit(&empty_k[s]);
         }
-        if (t >= 1) {
-          const int u = t - 1, pb = u & 1;
-          if (!wait(&p_ready[pb], (u >> 1) & 1, ERR_SP_P) || !wait(&full_v[pb], (u >> 1) & 1, ERR_SP_FULL)) break;
-          const uint32_t pp = smem_u32(smem + OFF_P + pb * 16384);
-          const uint32_t v = smem_u32(smem + OFF_V + pb * 32768);
+      } else {
+        for (int u = 0; u < ntiles && ok; ++u) {
+          const int pb = u & 1, sv = u % VST;
+          if (!wait(&p_ready[pb], (u >> 1) & 1, ERR_SP_P) || !wait(&full_v[sv], (u / VST) & 1, ERR_SP_FULL)) break;
+          const uint32_t v = smem_u32(smem + OFF_V + sv * 32768);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_bf16(tmem + T_O, sdesc(pp + kk * 32, 16, 1024), sdesc(v + kk * 2048, 8192, 1024), ID_O,
-                     u > 0 || kk > 0);
+            mma_bf16_ts(tmem + T_O, tmem + T_P + pb * 32 + kk * 8, sdesc(v + kk * 2048, 8192, 1024), ID_O,
+                        u > 0 || kk > 0);
           mma_commit(&o_done[pb]);
-          mma_commit(&empty_v[pb]);
+          mma_commit(&empty_v[sv]);
         }
       }
-      // all issued MMAs finished before TMEM is released
-      mma_commit(done_bar);
-      mbar_wait(done_bar, 0, abort_flag, ERR_SP_DONE);
+      // all MMAs this thread issued finished before TMEM is released
+      mma_commit(&done_bar[is_s ? 0 : 1]);
+      mbar_wait(&done_bar[is_s ? 0 : 1], 0, abort_flag, ERR_SP_DONE);
     }
     __syncwarp();
   } else {
@@ -227,19 +245,41 @@ __global__ void __launch_bounds__(NT, 1)
     const int64_t qabs = p.query_start + qp;
     const bool has_valid = p.key_valid != nullptr;
     bool ok = true;
+    // ---- this row of Q into TMEM (packed bf16 pairs, as they sit in memory) ----
+    if (ntiles > 0) {
+      ok = mbar_wait(qbar, 0, abort_flag, ERR_SP_Q);
+      if (ok) {
+#pragma unroll 1
+        for (int cb = 0; cb < 4; ++cb) {
+          float w[32];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint4 c4 = *reinterpret_cast<const uint4 *>(smem + OFF_V + sw128_off(128, cb, r, j));
+            w[4 * j] = __uint_as_float(c4.x);
+            w[4 * j + 1] = __uint_as_float(c4.y);
+            w[4 * j + 2] = __uint_as_float(c4.z);
+            w[4 * j + 3] = __uint_as_float(c4.w);
+          }
+          tmem_st32(lane_base + T_Q + cb * 32, w);
+        }
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      mbar_arrive(q_ready);
+    }
     float m_run = -INFINITY, l = 0.f;
     for (int t = 0; t < ntiles; ++t) {
       const int s = t & 1;
       const int64_t kt0 = lo + int64_t(t) * KT;
-      ok = ok && mbar_wait(&s_full[s], (t >> 1) & 1, abort_flag, ERR_SP_S);
+      ok = ok && mbar_wait(s_full, t & 1, abort_flag, ERR_SP_S);
       tc_fence_after();
       if (!ok) break;
       float x[64];
-      tmem_ld32(lane_base + T_S + s * 64, x);
-      tmem_ld32(lane_base + T_S + s * 64 + 32, x + 32);
+      tmem_ld32(lane_base + T_S, x);
+      tmem_ld32(lane_base + T_S + 32, x + 32);
       tmem_wait_ld();
       tc_fence_before();
-      mbar_arrive(&s_free[s]);
+      mbar_arrive(s_free);
       // key c of the tile sits d0 - c positions before this query: admitted when
       // 0 <= d0 - c < window, it exists (kt0 + c < Tk) and its key_valid flag
       // is set; most tiles lie wholly inside the window and skip the mask
@@ -303,8 +343,11 @@ __global__ void __launch_bounds__(NT, 1)
       // P buffer t & 1 was last read by the PV MMA of tile t - 2
       if (t >= 2) ok = mbar_wait(&o_done[s], ((t - 2) >> 1) & 1, abort_flag, ERR_SP_O);
       if (!ok) break;
-      st_row64_bf16(smem + OFF_P + s * 16384, 128, 0, r, x);
-      fence_async_smem();
+      float pw[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) pw[c] = __uint_as_float(pack_bf16x2(x[2 * c], x[2 * c + 1]));
+      tmem_st32(lane_base + T_P + s * 32, pw);
+      tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_ready[s]);
     }
@@ -312,7 +355,8 @@ __global__ void __launch_bounds__(NT, 1)
       ok = mbar_wait(&o_done[(ntiles - 1) & 1], ((ntiles - 1) >> 1) & 1, abort_flag, ERR_SP_O);
       tc_fence_after();
     }
-    // ---- O / l (zero for a query without admitted keys or marked invalid) staged over Q ----
+    // ---- O / l (zero for a query without admitted keys or marked invalid) staged over the K stages
+    //      (every S MMA, the last reader of K, is done) ----
     bool row_valid = qp < p.Tq && l > 0.f;
     if (row_valid && p.key_valid) row_valid = qabs < p.Tk && p.key_valid[int64_t(b) * p.valid_bs + qabs] != 0;
     const float inv = row_valid ? 1.f / l : 0.f;
@@ -327,13 +371,13 @@ __global__ void __launch_bounds__(NT, 1)
       }
 #pragma unroll
       for (int d = 0; d < 64; ++d) o[d] = use_o ? o[d] * inv : 0.f;
-      st_row64_bf16(smem + OFF_Q + cb * 16384, 128, 0, r, o);
+      st_row64_bf16(smem + OFF_K + cb * 16384, 128, 0, r, o);
     }
     fence_async_smem();
     ok = epi_sync_and(ok);
     if (r == 0 && ok) {
 #pragma unroll
-      for (int cb = 0; cb < 4; ++cb) tma_store_4d(&map_o, smem + OFF_Q + cb * 16384, cb * 64, kvh * p.R, int(qp0), b);
+      for (int cb = 0; cb < 4; ++cb) tma_store_4d(&map_o, smem + OFF_K + cb * 16384, cb * 64, kvh * p.R, int(qp0), b);
       asm volatile("cp.async.bulk.commit_group;" ::: "memory");
       asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     }
