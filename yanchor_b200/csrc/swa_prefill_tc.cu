@@ -281,28 +281,30 @@ __global__ void __launch_bounds__(NT, 1)
       tc_fence_before();
       mbar_arrive(s_free);
       // key c of the tile sits d0 - c positions before this query: admitted when
-      // 0 <= d0 - c < window, it exists (kt0 + c < Tk) and its key_valid flag
-      // is set; most tiles lie wholly inside the window and skip the mask
+      // 0 <= d0 - c < window, it exists (kt0 + c < Tk) and its key_valid flag is
+      // set.  The window leaves a contiguous range of c, so the admitted keys
+      // are one 64-bit mask and every tile runs the same loop.
       const int d0 = int(qabs - kt0);
-      const bool whole = !has_valid && kt0 + KT <= p.Tk && d0 >= KT - 1 && d0 < p.window;
+      int c_lo = d0 - p.window + 1, c_hi = d0;                       // window: c in [c_lo, c_hi]
+      const int nk = int(p.Tk - kt0 < KT ? p.Tk - kt0 : KT);
+      c_hi = c_hi < nk - 1 ? c_hi : nk - 1;
+      c_lo = c_lo > 0 ? c_lo : 0;
+      uint64_t adm = 0;
+      if (c_lo <= c_hi) adm = (~uint64_t(0) >> (63 - c_hi)) & (~uint64_t(0) << c_lo);
+      if (has_valid && adm) {
+        const uint8_t *kv = p.key_valid + int64_t(b) * p.valid_bs + kt0;
+        uint64_t vm = 0;
+#pragma unroll 1
+        for (int c = 0; c < nk; ++c) vm |= uint64_t(kv[c] != 0) << c;
+        adm &= vm;
+      }
       float mx[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) mx[u] = -INFINITY;
-      if (whole) {
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          x[c] *= p.scale_log2;
-          mx[c & 7] = fmaxf(mx[c & 7], x[c]);
-        }
-      } else {
-        const int nk = int(p.Tk - kt0 < KT ? p.Tk - kt0 : KT);
-        const uint8_t *kv = has_valid ? p.key_valid + int64_t(b) * p.valid_bs + kt0 : nullptr;
-#pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          const bool allowed = unsigned(d0 - c) < unsigned(p.window) && c < nk && (!has_valid || kv[c] != 0);
-          x[c] = allowed ? x[c] * p.scale_log2 : -INFINITY;
-          mx[c & 7] = fmaxf(mx[c & 7], x[c]);
-        }
+      for (int c = 0; c < 64; ++c) {
+        x[c] = (adm >> c) & 1 ? x[c] * p.scale_log2 : -INFINITY;
+        mx[c & 7] = fmaxf(mx[c & 7], x[c]);
       }
       const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
                              fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
