@@ -289,25 +289,39 @@ __global__ void __launch_bounds__(NT, 1)
       const int nk = int(p.Tk - kt0 < KT ? p.Tk - kt0 : KT);
       c_hi = c_hi < nk - 1 ? c_hi : nk - 1;
       c_lo = c_lo > 0 ? c_lo : 0;
-      uint64_t adm = 0;
-      if (c_lo <= c_hi) adm = (~uint64_t(0) >> (63 - c_hi)) & (~uint64_t(0) << c_lo);
-      if (has_valid && adm) {
-        const uint8_t *kv = p.key_valid + int64_t(b) * p.valid_bs + kt0;
-        uint64_t vm = 0;
-#pragma unroll 1
-        for (int c = 0; c < nk; ++c) vm |= uint64_t(kv[c] != 0) << c;
-        adm &= vm;
-      }
+      // pass 1: the admitted keys' largest raw logit (masked keys become -inf);
+      // a tile wholly inside the window needs no mask
       float mx[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) mx[u] = -INFINITY;
+      if (has_valid) {
+        uint64_t adm = 0;
+        if (c_lo <= c_hi) adm = (~uint64_t(0) >> (63 - c_hi)) & (~uint64_t(0) << c_lo);
+        if (adm) {
+          const uint8_t *kv = p.key_valid + int64_t(b) * p.valid_bs + kt0;
+          uint64_t vm = 0;
+#pragma unroll 1
+          for (int c = 0; c < nk; ++c) vm |= uint64_t(kv[c] != 0) << c;
+          adm &= vm;
+        }
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        x[c] = (adm >> c) & 1 ? x[c] * p.scale_log2 : -INFINITY;
-        mx[c & 7] = fmaxf(mx[c & 7], x[c]);
+        for (int c = 0; c < 64; ++c) {
+          x[c] = (adm >> c) & 1 ? x[c] : -INFINITY;
+          mx[c & 7] = fmaxf(mx[c & 7], x[c]);
+        }
+      } else if (c_lo == 0 && c_hi == KT - 1) {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) mx[c & 7] = fmaxf(mx[c & 7], x[c]);
+      } else {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          x[c] = c >= c_lo && c <= c_hi ? x[c] : -INFINITY;
+          mx[c & 7] = fmaxf(mx[c & 7], x[c]);
+        }
       }
+      // the running max in the scaled base-2 domain (scale_log2 > 0 keeps the order)
       const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                             fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+                             fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * p.scale_log2;
       const float m_new = fmaxf(m_run, mt);
       if (m_new > m_run + kRescale) {
         // the running max grows by more than 2^8: rescale O (once the previous
@@ -331,15 +345,21 @@ __global__ void __launch_bounds__(NT, 1)
         }
         m_run = m_new;
       }
+      // pass 2: p = 2^(x scale_log2 - m_run), one FFMA and one ex2 per key
       // (m_run is -inf only while every key so far was masked: then all p are 0)
       float ls[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) ls[u] = 0.f;
-      const bool live = m_run != -INFINITY;
+      if (m_run != -INFINITY) {
+        const float nm = -m_run;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        x[c] = live ? ex2(x[c] - m_run) : 0.f;
-        ls[c & 7] += x[c];
+        for (int c = 0; c < 64; ++c) {
+          x[c] = ex2(fmaf(x[c], p.scale_log2, nm));
+          ls[c & 7] += x[c];
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) x[c] = 0.f;
       }
       l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
       // P buffer t & 1 was last read by the PV MMA of tile t - 2
@@ -381,7 +401,9 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
       for (int cb = 0; cb < 4; ++cb) tma_store_4d(&map_o, smem + OFF_K + cb * 16384, cb * 64, kvh * p.R, int(qp0), b);
       asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-      asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+      // the CTA may exit once the store has read its staging tile; the
+      // writes to global memory complete on their own
+      asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
     }
   }
 
