@@ -58,7 +58,7 @@ constexpr uint32_t OFF_V = 65536;          // V 64 x 128 (one buffer: only MMA2 
 constexpr uint32_t OFF_LF = 81920;         // L fp32 64 x LP; once solved: Tw_lo / Tu_lo
 constexpr uint32_t OFF_TWLO = OFF_LF;      // Tw_lo bf16 64x64 (SW128)
 constexpr uint32_t OFF_TULO = OFF_LF + 8192;
-constexpr uint32_t OFF_TF = 99328;         // T fp32 64 x LP
+constexpr uint32_t OFF_TF = 99328;         // raw q.k rows fp32 64 x LP, then T fp32
 constexpr uint32_t OFF_P = 116736;         // P bf16 64x64 (SW128)
 constexpr uint32_t OFF_TW = 124928;        // Tw bf16 64x64 (SW128); solve scratch before that
 constexpr uint32_t OFF_TU = 133120;        // Tu bf16 64x64 (SW128)
@@ -77,7 +77,7 @@ constexpr uint32_t SMEM_BYTES = OFF_MISC + 16;
 static_assert(OFF_LF + 64 * LP * 4 <= OFF_TF && OFF_TF + 64 * LP * 4 <= OFF_P, "L / T regions");
 static_assert(OFF_TULO + 8192 <= OFF_TF && OFF_TF % 1024 == 0, "tiles inside L");
 static_assert(OFF_P % 1024 == 0 && OFF_VN % 1024 == 0 && OFF_ST % 1024 == 0 && OFF_ST + 32768 <= OFF_GST, "tiles");
-static_assert(6 * 320 * 4 <= 8192, "solve scratch fits the Tw tile");
+static_assert(3 * 320 * 4 <= 8192, "solve scratch fits the Tw tile");
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
 // TMEM columns (fp32, 128 lanes).  Chunk c uses region R(c) = c even ? T_R0 : T_R1
@@ -212,9 +212,8 @@ __device__ __forceinline__ void st_half_packed(uint8_t *tile, int rows, int cb, 
         make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
 }
 
-// Named barriers of group A (warps 2..5, barrier 1) and of its threads 0..63
-// (warps 4 and 5, barrier 2: L rows and the triangular solve).  The *_and forms
-// also AND a status across the group, so that a wait that gave up ends the
+// Named barrier of group A (warps 2..5, barrier 1).  The *_and forms also AND
+// a status across the group, so that a wait that gave up ends the
 // loop in every thread of the group together (none is left at a barrier).
 __device__ __forceinline__ bool a_sync_and(bool ok) {
   uint32_t res;
@@ -226,17 +225,6 @@ __device__ __forceinline__ bool a_sync_and(bool ok) {
       : "memory");
   return res != 0;
 }
-__device__ __forceinline__ bool solve_sync_and(bool ok) {
-  uint32_t res;
-  asm volatile(
-      "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\tbar.red.and.pred po, 2, 64, pi;\n\t"
-      "selp.u32 %0, 1, 0, po;\n\t}"
-      : "=r"(res)
-      : "r"(uint32_t(ok))
-      : "memory");
-  return res != 0;
-}
-__device__ __forceinline__ void solve_sync() { asm volatile("bar.sync 2, 64;" ::: "memory"); }
 // group B (warps 6..9, barrier 3)
 __device__ __forceinline__ bool b_sync_and(bool ok) {
   uint32_t res;
@@ -260,7 +248,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint64_t *full_v = bars + 4;     // V landed (1 + tx)
   uint64_t *empty_v = bars + 5;    // MMA2 read V (1)
   uint64_t *mma1_bar = bars + 6;   // [2] [K;Q][K;Q]^T of chunk c in TMEM (c & 1 selects)
-  uint64_t *mma2_bar = bars + 8;   // W, U in TMEM
+  uint64_t *mma2_bar = bars + 8;   // W in TMEM
   uint64_t *mma3_bar = bars + 9;   // X, Y in TMEM
   uint64_t *mma45_bar = bars + 10; // O in TMEM, state updated
   uint64_t *a_wt = bars + 11;      // group A: P and W^T tiles written (128)
@@ -419,22 +407,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int s = c & 1;
         const uint32_t kq = smem_u32(smem + (s ? OFF_KQ1 : OFF_KQ0));
         const uint32_t R = tmem + (s ? T_R1 : T_R0);
-        // MMA2: U^T = v^T (Tu_hi + Tu_lo)^T -> R ;  W^T = k^T (Tw_hi + Tw_lo)^T -> R + 64   (M=128, N=64, K=64)
-        if (!wait(&a_tw[s], (c >> 1) & 1, ERR_WAIT_EPI) || !wait(full_v, c & 1, ERR_WAIT_FULL)) break;
+        // MMA2: W^T = k^T (Tw_hi + Tw_lo)^T -> R + 64, committed on its own so group A can copy W^T
+        // while U^T = v^T (Tu_hi + Tu_lo)^T -> R runs   (M=128, N=64, K=64)
+        if (!wait(&a_tw[s], (c >> 1) & 1, ERR_WAIT_EPI)) break;
         const uint32_t vt = smem_u32(smem + OFF_V);
         const uint32_t tw = smem_u32(smem + OFF_TW), tu = smem_u32(smem + OFF_TU);
         const uint32_t twl = smem_u32(smem + OFF_TWLO), tul = smem_u32(smem + OFF_TULO);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
+        for (int kk = 0; kk < 4; ++kk)
           mma_bf16(R + 64, sdesc(kq + kk * 2048, 16384, 1024), sdesc(tw + kk * 32, 16, 1024), ID_N64_MK, kk > 0);
-          mma_bf16(R, sdesc(vt + kk * 2048, 8192, 1024), sdesc(tu + kk * 32, 16, 1024), ID_N64_MK, kk > 0);
-        }
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
+        for (int kk = 0; kk < 4; ++kk)
           mma_bf16(R + 64, sdesc(kq + kk * 2048, 16384, 1024), sdesc(twl + kk * 32, 16, 1024), ID_N64_MK, true);
-          mma_bf16(R, sdesc(vt + kk * 2048, 8192, 1024), sdesc(tul + kk * 32, 16, 1024), ID_N64_MK, true);
-        }
         mma_commit(mma2_bar);
+        if (!wait(full_v, c & 1, ERR_WAIT_FULL)) break;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_bf16(R, sdesc(vt + kk * 2048, 8192, 1024), sdesc(tu + kk * 32, 16, 1024), ID_N64_MK, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_bf16(R, sdesc(vt + kk * 2048, 8192, 1024), sdesc(tul + kk * 32, 16, 1024), ID_N64_MK, true);
         mma_commit(empty_v);
         // MMA1 of chunk c + 1 into R(c + 1): group B read U, X of chunk c - 1 there before its b_vn;
         // the stage's copy was issued a whole group-A phase ago (after MMA5 of chunk c - 1)
@@ -505,7 +497,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       ok = ok && mbar_wait(&mma1_bar[s], (c >> 1) & 1, abort_flag, ERR_WAIT_MMA);
       tc_fence_after();
       YB_DBG_TS(1);
-      // ---------- norms from the diagonal of [K;Q][K;Q]^T ----------
+      // ---------- norms from the diagonal of [K;Q][K;Q]^T; the raw k_i.k_j rows (threads r < 64)
+      //            into the L buffer, the raw q_i.k_j rows (r >= 64) into the T buffer ----------
       if (ok) {
         float dg[32];
         tmem_ld32(lane_base + R + uint32_t(r & ~31), dg);
@@ -527,159 +520,146 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (r < 64) {
           kn[r] = nrm;
           fw[r] = BT[r] * EG[r] * nrm;
-          // the raw k_i.k_j row into the L buffer, for all four warps to scale
-#pragma unroll 1
-          for (int hf = 0; hf < 2; ++hf) {
-            float d1[32];
-            tmem_ld32(lane_base + R + uint32_t(32 * hf), d1);
-            tmem_wait_ld();
-#pragma unroll
-            for (int j4 = 0; j4 < 8; ++j4)
-              *reinterpret_cast<float4 *>(LF + r * LP + 32 * hf + 4 * j4) =
-                  make_float4(d1[4 * j4], d1[4 * j4 + 1], d1[4 * j4 + 2], d1[4 * j4 + 3]);
-          }
         } else {
           qn[r - 64] = nrm * p.scale;
         }
-      }
-      if (!(ok = a_sync_and(ok))) break;
-      YB_DBG_TS(2);
-      // ---------- L row r & 63, columns 32 (r >> 6) .. +31, in place (branch-free mask; the
-      //            exponent is clamped so masked entries stay finite) ----------
-      {
-        const int i = r & 63, jb = 32 * (r >> 6);
-        const float ci = BT[i] * kn[i], gi = G[i];
-        float4 *row4 = reinterpret_cast<float4 *>(LF + i * LP + jb);
-        const float4 *kn4 = reinterpret_cast<const float4 *>(kn + jb);
-        const float4 *g4 = reinterpret_cast<const float4 *>(G + jb);
-#pragma unroll
-        for (int j4 = 0; j4 < 8; ++j4) {
-          float4 d = row4[j4];
-          const float4 kk = kn4[j4], gg = g4[j4];
-          const int j = jb + 4 * j4;
-          d.x *= ci * kk.x * __expf(fminf(gi - gg.x, 0.f)) * float(j < i);
-          d.y *= ci * kk.y * __expf(fminf(gi - gg.y, 0.f)) * float(j + 1 < i);
-          d.z *= ci * kk.z * __expf(fminf(gi - gg.z, 0.f)) * float(j + 2 < i);
-          d.w *= ci * kk.w * __expf(fminf(gi - gg.w, 0.f)) * float(j + 3 < i);
-          row4[j4] = d;
-        }
-      }
-      if (!(ok = a_sync_and(ok))) break;
-      uint32_t pk[32];   // threads r >= 64: P row r - 64 as packed bf16 pairs, stored after MMA2
-      if (r < 64) {
-        YB_DBG_TS(3);
-        {
-        // ---- T = (I + L)^-1 by 16x16 blocks: T_ii = D_i (diagonal inverses),
-        //      T_ij = -sum_{m=j}^{i-1} M_im T_mj with M_im = D_i L_im ----
-        float *TF = reinterpret_cast<float *>(smem + OFF_TF);   // T fp32, pitch LP
-        float *MB = reinterpret_cast<float *>(smem + OFF_TW);   // six M blocks, pitch 20
-        {
-          // diagonal blocks: thread j solves column j of its block in registers
-          const int j = r, b = j >> 4, jj = j & 15;
-          float x[16];
-#pragma unroll
-          for (int ii = 0; ii < 16; ++ii) {
-            const float *Lrow = LF + (b * 16 + ii) * LP + b * 16;
-            float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-            for (int mm = 0; mm + 1 < ii; mm += 2) {
-              a0 = fmaf(Lrow[mm], x[mm], a0);
-              a1 = fmaf(Lrow[mm + 1], x[mm + 1], a1);
-            }
-            if (ii & 1) a0 = fmaf(Lrow[ii - 1], x[ii - 1], a0);
-            x[ii] = ii < jj ? 0.f : (ii == jj ? 1.f : -(a0 + a1));
-          }
-#pragma unroll
-          for (int ii = 0; ii < 16; ++ii) TF[(b * 16 + ii) * LP + j] = x[ii];
-          for (int row = 0; row < b * 16; ++row) TF[row * LP + j] = 0.f;   // upper blocks
-        }
-        solve_sync();
-        // M blocks, list order (1,0) (2,1) (3,2) (2,0) (3,1) (3,0); warp w of the two takes k = w, w+2, w+4
-        const int sw = r >> 5;
-        for (int k = sw; k < 6; k += 2) {
-          const int bi = k < 3 ? k + 1 : (k == 5 ? 3 : k - 1), bm = k < 3 ? k : (k == 3 ? 0 : (k == 4 ? 1 : 0));
-          float acc[2][4] = {};
-          block_mma16_tf32(acc, TF + bi * 16 * LP + bi * 16, LP, LF + bi * 16 * LP + bm * 16, LP);
-          store_block16(MB + k * 320, 20, acc, 1.f);
-        }
-        solve_sync();
-        // distance 1: T_(i,i-1) = -M_(i,i-1) D_(i-1),  i = 1..3
-        for (int i1 = 1 + sw; i1 < 4; i1 += 2) {
-          float acc[2][4] = {};
-          block_mma16_tf32(acc, MB + (i1 - 1) * 320, 20, TF + (i1 - 1) * 16 * LP + (i1 - 1) * 16, LP);
-          store_block16(TF + i1 * 16 * LP + (i1 - 1) * 16, LP, acc, -1.f);
-        }
-        solve_sync();
-        // distance 2: T_(i,i-2) = -(M_(i,i-2) D_(i-2) + M_(i,i-1) T_(i-1,i-2)),  i = 2 (warp 0), 3 (warp 1)
-        {
-          const int i2 = 2 + sw;
-          float acc[2][4] = {};
-          block_mma16_tf32(acc, MB + (i2 + 1) * 320, 20, TF + (i2 - 2) * 16 * LP + (i2 - 2) * 16, LP);
-          block_mma16_tf32(acc, MB + (i2 - 1) * 320, 20, TF + (i2 - 1) * 16 * LP + (i2 - 2) * 16, LP);
-          store_block16(TF + i2 * 16 * LP + (i2 - 2) * 16, LP, acc, -1.f);
-        }
-        solve_sync();
-        // distance 3: T_(3,0) = -(M_30 D_0 + M_31 T_10 + M_32 T_20)
-        if (sw == 0) {
-          float acc[2][4] = {};
-          block_mma16_tf32(acc, MB + 5 * 320, 20, TF, LP);
-          block_mma16_tf32(acc, MB + 4 * 320, 20, TF + 16 * LP, LP);
-          block_mma16_tf32(acc, MB + 2 * 320, 20, TF + 32 * LP, LP);
-          store_block16(TF + 48 * LP, LP, acc, -1.f);
-        }
-        }
-      } else {
-        // ---------- P row r - 64, held packed until MMA4 of chunk c - 1 has read the tile ----------
-        const int i = r - 64;
-        const float ci = qn[i], gi = G[i];
-#pragma unroll
+        float *raw = (r < 64 ? LF : reinterpret_cast<float *>(smem + OFF_TF)) + (r & 63) * LP;
+#pragma unroll 1
         for (int hf = 0; hf < 2; ++hf) {
           float d1[32];
           tmem_ld32(lane_base + R + uint32_t(32 * hf), d1);
           tmem_wait_ld();
 #pragma unroll
-          for (int t = 0; t < 16; ++t) {
-            const int j = 32 * hf + 2 * t;
-            const float p0 = ci * kn[j] * __expf(fminf(gi - G[j], 0.f)) * d1[2 * t] * float(j <= i);
-            const float p1 = ci * kn[j + 1] * __expf(fminf(gi - G[j + 1], 0.f)) * d1[2 * t + 1] * float(j + 1 <= i);
-            pk[16 * hf + t] = pack_bf16x2(p0, p1);
+          for (int j4 = 0; j4 < 8; ++j4)
+            *reinterpret_cast<float4 *>(raw + 32 * hf + 4 * j4) =
+                make_float4(d1[4 * j4], d1[4 * j4 + 1], d1[4 * j4 + 2], d1[4 * j4 + 3]);
+        }
+      }
+      if (!(ok = a_sync_and(ok))) break;
+      YB_DBG_TS(2);
+      // ---------- L and P of row i = r & 63, columns 32 (r >> 6) .. +31, sharing one
+      //            e^{g_i - g_j} per entry: L in place (k_i.k_j, j < i), P packed into registers
+      //            (q_i.k_j, j <= i) and stored once MMA2 shows that MMA4 of chunk c - 1 has
+      //            read the P tile.  Branch-free masks; the exponent is clamped so masked entries
+      //            stay finite.  Rows i < 32 have nothing in columns 32..63 (L is never read there). ----------
+      float *TF = reinterpret_cast<float *>(smem + OFF_TF);   // raw q.k, then T fp32, pitch LP
+      uint32_t pk[16];
+      {
+        const int i = r & 63, jb = 32 * (r >> 6);
+        if (jb > i) {   // uniform across a warp: its lanes share r >> 5
+#pragma unroll
+          for (int t = 0; t < 16; ++t) pk[t] = 0u;
+        } else {
+          const float ci = BT[i] * kn[i], qi = qn[i], gi = G[i];
+          float4 *row4 = reinterpret_cast<float4 *>(LF + i * LP + jb);
+          const float4 *qk4 = reinterpret_cast<const float4 *>(TF + i * LP + jb);
+          const float4 *kn4 = reinterpret_cast<const float4 *>(kn + jb);
+          const float4 *g4 = reinterpret_cast<const float4 *>(G + jb);
+#pragma unroll
+          for (int j4 = 0; j4 < 8; ++j4) {
+            float4 d = row4[j4];
+            const float4 qq = qk4[j4], kk = kn4[j4], gg = g4[j4];
+            const int j = jb + 4 * j4;
+            const float e0 = __expf(fminf(gi - gg.x, 0.f)), e1 = __expf(fminf(gi - gg.y, 0.f));
+            const float e2 = __expf(fminf(gi - gg.z, 0.f)), e3 = __expf(fminf(gi - gg.w, 0.f));
+            d.x *= ci * kk.x * e0 * float(j < i);
+            d.y *= ci * kk.y * e1 * float(j + 1 < i);
+            d.z *= ci * kk.z * e2 * float(j + 2 < i);
+            d.w *= ci * kk.w * e3 * float(j + 3 < i);
+            row4[j4] = d;
+            pk[2 * j4] = pack_bf16x2(qi * kk.x * e0 * qq.x * float(j <= i), qi * kk.y * e1 * qq.y * float(j + 1 <= i));
+            pk[2 * j4 + 1] =
+                pack_bf16x2(qi * kk.z * e2 * qq.z * float(j + 2 <= i), qi * kk.w * e3 * qq.w * float(j + 3 <= i));
+          }
+        }
+      }
+      if (!(ok = a_sync_and(ok))) break;
+      YB_DBG_TS(3);
+      // ---------- T = (I + L)^-1 by 16x16 blocks: the diagonal blocks D_j = (I + L_jj)^-1 by
+      //            forward substitution (thread r < 64 solves column r of its block in registers),
+      //            then T_ij = -D_i sum_{m=j}^{i-1} L_im T_mj for i > j, one warp per column
+      //            block j walking down its blocks, so a warp only reads the T blocks it wrote ----------
+      if (r < 64) {
+        const int j = r, b = j >> 4, jj = j & 15;
+        float x[16];
+#pragma unroll
+        for (int ii = 0; ii < 16; ++ii) {
+          const float4 *L4 = reinterpret_cast<const float4 *>(LF + (b * 16 + ii) * LP + b * 16);
+          float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+          for (int q = 0; 4 * q < ii; ++q) {
+            const float4 l = L4[q];
+            if (4 * q < ii) a0 = fmaf(l.x, x[4 * q], a0);
+            if (4 * q + 1 < ii) a1 = fmaf(l.y, x[4 * q + 1], a1);
+            if (4 * q + 2 < ii) a0 = fmaf(l.z, x[4 * q + 2], a0);
+            if (4 * q + 3 < ii) a1 = fmaf(l.w, x[4 * q + 3], a1);
+          }
+          x[ii] = ii < jj ? 0.f : (ii == jj ? 1.f : -(a0 + a1));
+        }
+#pragma unroll
+        for (int ii = 0; ii < 16; ++ii) TF[(b * 16 + ii) * LP + j] = x[ii];
+      }
+      if (!(ok = a_sync_and(ok))) break;
+      {
+        const int jc = r >> 5;   // this warp's column block
+        if (jc < 3) {
+          float *scr = reinterpret_cast<float *>(smem + OFF_TW) + jc * 320;   // 16x16, pitch 20
+          auto lblk = [&](int i, int m) { return LF + (i * 16) * LP + m * 16; };
+          auto tblk = [&](int i, int m) { return TF + (i * 16) * LP + m * 16; };
+          // acc[n]: sum_m L_im T_mj for block row i = jc + 1 + n, over the T_mj known so far
+          float acc[3][2][4] = {};
+#pragma unroll
+          for (int n = 0; n < 3; ++n)
+            if (jc + 1 + n < 4) block_mma16_tf32(acc[n], lblk(jc + 1 + n, jc), LP, tblk(jc, jc), LP);
+#pragma unroll
+          for (int n = 0; n < 3; ++n) {
+            const int i = jc + 1 + n;
+            if (i < 4) {
+              store_block16(scr, 20, acc[n], 1.f);
+              __syncwarp();
+              float t[2][4] = {};
+              block_mma16_tf32(t, tblk(i, i), LP, scr, 20);
+              store_block16(tblk(i, jc), LP, t, -1.f);
+              __syncwarp();
+#pragma unroll
+              for (int n2 = n + 1; n2 < 3; ++n2)
+                if (jc + 1 + n2 < 4) block_mma16_tf32(acc[n2], lblk(jc + 1 + n2, i), LP, tblk(i, jc), LP);
+            }
           }
         }
       }
       if (!(ok = a_sync_and(ok))) break;
       YB_DBG_TS(4);
-      // ---------- Tw (rows of threads r < 64) and Tu (r >= 64) from T, as bf16 hi + lo tiles ----------
+      // ---------- Tw (rows of threads r < 64) and Tu (r >= 64) from T, as bf16 hi + lo tiles:
+      //            both factors enter MMA2 as hi + lo, since a single bf16 rounding of T alone
+      //            costs ~2e-3 relative on the state ----------
       {
-        const float *TF = reinterpret_cast<const float *>(smem + OFF_TF);
         const int i = r & 63;
+        const float *fac = r < 64 ? fw : BT;   // Tw = T diag(beta e^G kn), Tu = T diag(beta)
 #pragma unroll 1
         for (int hf = 0; hf < 2; ++hf) {
-          float rowv[32];
+          uint32_t hi[16], lo[16];
 #pragma unroll
           for (int j4 = 0; j4 < 8; ++j4) {
-            const float4 t4 = *reinterpret_cast<const float4 *>(TF + i * LP + 32 * hf + 4 * j4);
-            rowv[4 * j4] = t4.x;
-            rowv[4 * j4 + 1] = t4.y;
-            rowv[4 * j4 + 2] = t4.z;
-            rowv[4 * j4 + 3] = t4.w;
-          }
+            // blocks above the diagonal are zero (the buffer holds stale data there)
+            float4 t4 = *reinterpret_cast<const float4 *>(TF + i * LP + 32 * hf + 4 * j4);
+            if (((32 * hf + 4 * j4) >> 4) > (i >> 4)) t4 = make_float4(0.f, 0.f, 0.f, 0.f);
 #ifdef YB_TC_DEBUG
-          if (p.dbg && blockIdx.x == 0 && c == 0 && r < 64)
-            for (int jj = 0; jj < 32; ++jj) p.dbg[DBG_T + r * 64 + 32 * hf + jj] = rowv[jj];
+            if (p.dbg && blockIdx.x == 0 && c == 0 && r < 64) {
+              float *d = p.dbg + DBG_T + r * 64 + 32 * hf + 4 * j4;
+              d[0] = t4.x, d[1] = t4.y, d[2] = t4.z, d[3] = t4.w;
+            }
 #endif
-          // both factors enter MMA2 as bf16 hi + lo: a single bf16 rounding of T
-          // alone costs ~2e-3 relative on the state
-          if (r < 64) {
-#pragma unroll
-            for (int jj = 0; jj < 32; ++jj) rowv[jj] *= fw[32 * hf + jj];
-          } else {
-#pragma unroll
-            for (int jj = 0; jj < 32; ++jj) rowv[jj] *= BT[32 * hf + jj];
+            const float4 f4 = *reinterpret_cast<const float4 *>(fac + 32 * hf + 4 * j4);
+            t4.x *= f4.x, t4.y *= f4.y, t4.z *= f4.z, t4.w *= f4.w;
+            const uint32_t h0 = pack_bf16x2(t4.x, t4.y), h1 = pack_bf16x2(t4.z, t4.w);
+            hi[2 * j4] = h0;
+            hi[2 * j4 + 1] = h1;
+            lo[2 * j4] = pack_bf16x2(t4.x - __uint_as_float(h0 << 16), t4.y - __uint_as_float(h0 & 0xffff0000u));
+            lo[2 * j4 + 1] = pack_bf16x2(t4.z - __uint_as_float(h1 << 16), t4.w - __uint_as_float(h1 & 0xffff0000u));
           }
-          st_half_bf16(smem + (r < 64 ? OFF_TW : OFF_TU), 64, 0, i, 4 * hf, rowv);
-#pragma unroll
-          for (int jj = 0; jj < 32; ++jj) rowv[jj] -= __bfloat162float(__float2bfloat16_rn(rowv[jj]));
-          st_half_bf16(smem + (r < 64 ? OFF_TWLO : OFF_TULO), 64, 0, i, 4 * hf, rowv);
+          st_half_packed(smem + (r < 64 ? OFF_TW : OFF_TU), 64, 0, i, 4 * hf, hi);
+          st_half_packed(smem + (r < 64 ? OFF_TWLO : OFF_TULO), 64, 0, i, 4 * hf, lo);
         }
 #ifdef YB_TC_DEBUG
         if (p.dbg && blockIdx.x == 0 && c == 0) p.dbg[DBG_NORM + r] = r < 64 ? kn[r] : qn[r - 64];
@@ -694,10 +674,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tc_fence_after();
       if (!(ok = a_sync_and(ok))) break;
       YB_DBG_TS(6);
-      if (r >= 64) {
-        st_half_packed(smem + OFF_P, 64, 0, r - 64, 0, pk);
-        st_half_packed(smem + OFF_P, 64, 0, r - 64, 4, pk + 16);
-      }
+      st_half_packed(smem + OFF_P, 64, 0, r & 63, 4 * (r >> 6), pk);
 #pragma unroll 1
       for (int hf = 0; hf < 2; ++hf) {
         float w[32];
