@@ -124,9 +124,9 @@ __device__ __forceinline__ float load_scalar(const void *p, int64_t idx, int dty
 
 
 __device__ __forceinline__ uint32_t to_tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return r;
+  // the raw fp32 bits: the tf32 MMA reads the top 19 bits (truncation), which
+  // saves a conversion per operand on the inverse's latency-bound chains
+  return __float_as_uint(x);
 }
 
 // acc (16x16 as two 16x8 tiles, m16n8 accumulator fragments) += A (16x16) B (16x16),
