@@ -21,6 +21,10 @@
 // registers only one fits).  The prefetch wait is bounded; on timeout the
 // CTA records an error code, waits (bounded) for the copy in flight, exits.
 //
+// That persistent form serves HV = H; for HV = 2H the paired form further
+// down (two CTAs per k-head in a cluster, state in registers, two CTAs per
+// SM) is faster and is used instead.
+//
 // Roundings follow the reference chain: conv outputs are rounded to the
 // activation dtype (the conv update writes a bf16 tensor), beta = sigmoid(b)
 // likewise (the fused gates kernel stores it in b's dtype), the decay stays
@@ -28,6 +32,8 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "tc.cuh"
+
+#include <cooperative_groups.h>
 
 namespace yb {
 namespace {
@@ -90,9 +96,9 @@ __device__ __forceinline__ void st4s(T16 *dst, const float *x) {
 // token `tok`: y[4 g + j] gets the (dtype-rounded) SiLU outputs and the conv
 // state is shifted in place.  Every load is issued before any store (the
 // stores would otherwise order the next group's loads behind them).
-template <typename TIO, int NG>
+template <typename TIO, int NG, bool STORE = true>
 __device__ __forceinline__ void conv_groups(const FusedParams &p, int64_t n, int64_t tok, const int64_t *cs,
-                                            float *y) {
+                                            float *y, uint2 (*kept)[4] = nullptr) {
   const TIO *xrow = static_cast<const TIO *>(p.mixed) + tok * p.mixed_ts;
   TIO *srow = static_cast<TIO *>(p.conv_state) + n * p.conv_bs;
   uint2 xv[NG], sv[NG][4];
@@ -124,10 +130,24 @@ __device__ __forceinline__ void conv_groups(const FusedParams &p, int64_t n, int
       y[4 * g + j] = round_to<TIO>(acc * sigmoidf_(acc));
     }
   }
+  if constexpr (STORE) {
 #pragma unroll
-  for (int g = 0; g < NG; ++g)
+    for (int g = 0; g < NG; ++g)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) *reinterpret_cast<uint2 *>(srow + (cs[g] + j) * CONV_KS) = sv[g][j];
+      for (int j = 0; j < 4; ++j) *reinterpret_cast<uint2 *>(srow + (cs[g] + j) * CONV_KS) = sv[g][j];
+  } else {
+#pragma unroll
+    for (int g = 0; g < NG; ++g)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) kept[g][j] = sv[g][j];
+  }
+}
+// the shifted conv state kept by conv_groups<.., false>, stored for one group of 4 channels
+template <typename TIO>
+__device__ __forceinline__ void conv_state_store(const FusedParams &p, int64_t n, int64_t c, const uint2 *sv) {
+  TIO *srow = static_cast<TIO *>(p.conv_state) + n * p.conv_bs;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) *reinterpret_cast<uint2 *>(srow + (c + j) * CONV_KS) = sv[j];
 }
 
 template <typename TIO, typename TS, int R, bool TRANS>
@@ -338,6 +358,209 @@ __global__ void __launch_bounds__(256 * R, 1) gdn_decode_fused_kernel(const Fuse
   }
 }
 
+// ---- the paired form (HV = 2 H): one CTA per (sequence, value head), launched as clusters of
+// the two value heads of a k-head.  Rank 0 convolves the k-head's q channels and rank 1 its k
+// channels (each shifting those channels' conv state once); after a cluster barrier each reads
+// the other's half through distributed shared memory.  Each CTA convolves its own v channels.
+// The state goes straight into registers as in the recurrence kernel, so two CTAs fit on an SM
+// and every load of a CTA is issued at its start.  The exchange buffer is double-buffered by
+// token parity: the barrier of token t + 1 orders the peer's reads of token t before its
+// overwrite at token t + 2, and a last relaxed arrive (after the last read) with its wait at
+// exit keeps this CTA's shared memory alive until the peer has read it. ----
+template <typename TIO, typename TS, bool TRANS>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) gdn_decode_pair_kernel(const FusedParams p) {
+  constexpr int ROWS = TRANS ? VD : KD;
+  constexpr int COLS = TRANS ? KD : VD;
+  constexpr int NCG = COLS / 4, RG = 256 / NCG, RPT = ROWS / RG;
+  namespace cgr = cooperative_groups;
+  cgr::cluster_group cluster = cgr::this_cluster();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int cg = tid % NCG, rg = tid / NCG, c0 = cg * 4;
+  const int64_t n = blockIdx.x / p.HV;
+  const int hv = int(blockIdx.x % p.HV), h = hv >> 1;
+  const unsigned rank = cluster.block_rank();   // hv & 1
+
+  __shared__ __align__(16) float sx[2][KD];     // this CTA's conv output: q (rank 0) or k (rank 1)
+  __shared__ __align__(16) float sq[KD];
+  __shared__ __align__(16) float sk[KD];
+  __shared__ __align__(16) float sv[VD];
+  __shared__ __align__(16) float so[VD];
+  __shared__ __align__(16) float red_k[TRANS ? 1 : RG][TRANS ? 4 : VD];
+  __shared__ __align__(16) float red_q[TRANS ? 1 : RG][TRANS ? 4 : VD];
+  __shared__ float s_decay, s_beta, s_kq;
+
+  TS *stp = static_cast<TS *>(p.state) + (n * p.HV + hv) * int64_t(KD) * VD;
+  // the state into L2 before the wait (the previous kernel may be the one that wrote it), then
+  // into registers
+#pragma unroll
+  for (int i = 0; i < RPT; i += (sizeof(TS) == 4 ? 1 : 2)) prefetch_l2(stp + (rg * RPT + i) * COLS + c0);
+  pdl_wait();
+  pdl_release();
+  float s[RPT][4];
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) {
+    const TS *e = stp + (rg * RPT + i) * COLS + c0;
+    if constexpr (sizeof(TS) == 4) {
+      const float4 v = __ldcs(reinterpret_cast<const float4 *>(e));
+      s[i][0] = v.x; s[i][1] = v.y; s[i][2] = v.z; s[i][3] = v.w;
+    } else {
+      const uint2 v = __ldcs(reinterpret_cast<const uint2 *>(e));
+      const TS *hh = reinterpret_cast<const TS *>(&v);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s[i][j] = to_f(hh[j]);
+    }
+  }
+  const int64_t xch = rank == 0 ? int64_t(h) * KD : int64_t(p.H) * KD + int64_t(h) * KD;
+  const int64_t vch = 2 * int64_t(p.H) * KD + int64_t(hv) * VD;
+
+  for (int64_t t = 0; t < p.T; ++t) {
+    const int64_t tok = n * p.T + t;
+    const int buf = int(t & 1);
+    // the shifted conv state of warp 0's or warp 1's channels, stored after the exchange barrier
+    // (a release barrier would otherwise wait for those global stores)
+    uint2 cst[1][4];
+    if (warp == 0) {
+      float y[4];
+      const int64_t cs[1] = {xch + lane * 4};
+      conv_groups<TIO, 1, false>(p, n, tok, cs, y, cst);
+      *reinterpret_cast<float4 *>(&sx[buf][lane * 4]) = make_float4(y[0], y[1], y[2], y[3]);
+    } else if (warp == 1) {
+      // v of value head hv, and its gates
+      float vv[4];
+      const int64_t cs[1] = {vch + lane * 4};
+      conv_groups<TIO, 1, false>(p, n, tok, cs, vv, cst);
+      *reinterpret_cast<float4 *>(sv + lane * 4) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+      if (lane == 0) {
+        const float av = to_f(static_cast<const TIO *>(p.a)[tok * p.ab_ts + hv]);
+        const float bv = to_f(static_cast<const TIO *>(p.b)[tok * p.ab_ts + hv]);
+        const float gl = -expf(p.A_log[hv]) * softplus20(av + (p.dt_bias ? p.dt_bias[hv] : 0.f));
+        s_decay = expf(gl);
+        s_beta = round_to<TIO>(sigmoidf_(bv));
+      }
+    }
+    cluster.sync();   // q and k of the k-head written by the two CTAs
+    if (warp < 2) conv_state_store<TIO>(p, n, (warp == 0 ? xch : vch) + lane * 4, cst[0]);
+    if (warp == 0) {
+      // q and k: L2 norm, q scale, and q.k
+      const float *xq = rank == 0 ? &sx[buf][0] : cluster.map_shared_rank(&sx[buf][0], 0);
+      const float *xk = rank == 1 ? &sx[buf][0] : cluster.map_shared_rank(&sx[buf][0], 1);
+      const float4 q4 = *reinterpret_cast<const float4 *>(xq + lane * 4);
+      const float4 k4 = *reinterpret_cast<const float4 *>(xk + lane * 4);
+      float qv[4] = {q4.x, q4.y, q4.z, q4.w}, kv[4] = {k4.x, k4.y, k4.z, k4.w};
+      float qs2 = qv[0] * qv[0] + qv[1] * qv[1] + qv[2] * qv[2] + qv[3] * qv[3];
+      float ks2 = kv[0] * kv[0] + kv[1] * kv[1] + kv[2] * kv[2] + kv[3] * kv[3];
+      const float qn = rsqrtf(warp_sum(qs2) + 1e-6f), kn = rsqrtf(warp_sum(ks2) + 1e-6f);
+      float dot = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        qv[j] *= qn * p.scale;
+        kv[j] *= kn;
+        dot += qv[j] * kv[j];
+      }
+      dot = warp_sum(dot);
+      *reinterpret_cast<float4 *>(sq + lane * 4) = make_float4(qv[0], qv[1], qv[2], qv[3]);
+      *reinterpret_cast<float4 *>(sk + lane * 4) = make_float4(kv[0], kv[1], kv[2], kv[3]);
+      if (lane == 0) s_kq = dot;
+    }
+    __syncthreads();
+    // after the last token's exchange: this CTA is done reading the peer's buffer (the matching
+    // wait comes at exit, so neither CTA's shared memory goes away while the other reads it)
+    if (t == p.T - 1) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+    const float dec = s_decay, bet = s_beta, kq = s_kq;
+
+    if constexpr (!TRANS) {
+      float ak[4] = {0.f, 0.f, 0.f, 0.f}, aq[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int i = 0; i < RPT; ++i) {
+        const float kr = sk[rg * RPT + i], qr = sq[rg * RPT + i];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          s[i][j] *= dec;
+          ak[j] = fmaf(s[i][j], kr, ak[j]);
+          aq[j] = fmaf(s[i][j], qr, aq[j]);
+        }
+      }
+      *reinterpret_cast<float4 *>(&red_k[rg][c0]) = make_float4(ak[0], ak[1], ak[2], ak[3]);
+      *reinterpret_cast<float4 *>(&red_q[rg][c0]) = make_float4(aq[0], aq[1], aq[2], aq[3]);
+      __syncthreads();
+      float kvs[4] = {0.f, 0.f, 0.f, 0.f}, qss[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int r = 0; r < RG; ++r) {
+        const float4 x = *reinterpret_cast<const float4 *>(&red_k[r][c0]);
+        const float4 y = *reinterpret_cast<const float4 *>(&red_q[r][c0]);
+        kvs[0] += x.x; kvs[1] += x.y; kvs[2] += x.z; kvs[3] += x.w;
+        qss[0] += y.x; qss[1] += y.y; qss[2] += y.z; qss[3] += y.w;
+      }
+      float delta[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) delta[j] = bet * (sv[c0 + j] - kvs[j]);
+#pragma unroll
+      for (int i = 0; i < RPT; ++i) {
+        const float kr = sk[rg * RPT + i];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) s[i][j] = fmaf(kr, delta[j], s[i][j]);
+      }
+      if (rg == 0) {
+        float ov[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) ov[j] = fmaf(delta[j], kq, qss[j]);
+        *reinterpret_cast<float4 *>(&so[c0]) = make_float4(ov[0], ov[1], ov[2], ov[3]);
+      }
+    } else {
+      float kc[4], qc[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        kc[j] = sk[c0 + j];
+        qc[j] = sq[c0 + j];
+      }
+#pragma unroll
+      for (int i = 0; i < RPT; ++i) {
+        float pk = 0.f, pq = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          s[i][j] *= dec;
+          pk = fmaf(s[i][j], kc[j], pk);
+          pq = fmaf(s[i][j], qc[j], pq);
+        }
+        pk = group_sum<NCG>(pk);
+        pq = group_sum<NCG>(pq);
+        const int r = rg * RPT + i;
+        const float delta = bet * (sv[r] - pk);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) s[i][j] = fmaf(kc[j], delta, s[i][j]);
+        if (cg == 0) so[r] = fmaf(delta, kq, pq);
+      }
+    }
+    __syncthreads();
+
+    // ---- gated RMSNorm of the output (Qwen3_5RMSNormGated, io-dtype roundings) ----
+    if (warp == 0) {
+      float ov[4];
+      const float4 x = *reinterpret_cast<const float4 *>(&so[lane * 4]);
+      ov[0] = x.x; ov[1] = x.y; ov[2] = x.z; ov[3] = x.w;
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        ov[j] = round_to<TIO>(ov[j]);
+        ss += ov[j] * ov[j];
+      }
+      const float inv = rsqrtf(warp_sum(ss) / float(VD) + p.norm_eps);
+      float zz[4], w[4];
+      load4(static_cast<const TIO *>(p.z) + tok * p.z_ts + int64_t(hv) * VD + lane * 4, zz);
+      load4(static_cast<const TIO *>(p.norm_w) + lane * 4, w);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float yv = round_to<TIO>(w[j] * round_to<TIO>(ov[j] * inv));
+        ov[j] = yv * (zz[j] * sigmoidf_(zz[j]));
+      }
+      store4(static_cast<TIO *>(p.o) + (tok * p.HV + hv) * int64_t(VD) + lane * 4, ov);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) st4s(stp + (rg * RPT + i) * COLS + c0, s[i]);
+  if (p.T > 0) asm volatile("barrier.cluster.wait.aligned;" ::: "memory");   // the peer has read this CTA's buffer
+}
+
 int sm_count() {
   static int count[64] = {0};
   int dev = 0;
@@ -360,7 +583,16 @@ int launch_r(const FusedArgs &a, const FusedParams &p) {
 }
 
 template <typename TIO, typename TS>
+int launch_pair(const FusedArgs &a, const FusedParams &p) {
+  auto kern = a.trans ? gdn_decode_pair_kernel<TIO, TS, true> : gdn_decode_pair_kernel<TIO, TS, false>;
+  const cudaError_t e = launch_pdl(kern, dim3(unsigned(a.N * a.HV)), dim3(256), 0, a.stream, p);
+  if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "gdn_decode_pair_kernel: %s", cudaGetErrorString(e));
+  return check_launch("gdn_decode_pair_kernel");
+}
+
+template <typename TIO, typename TS>
 int launch_ts(const FusedArgs &a, const FusedParams &p) {
+  if (a.HV == 2 * a.H) return launch_pair<TIO, TS>(a, p);   // two value heads per k-head: paired CTAs
   switch (a.HV / a.H) {   // 256 threads per value head: at most 512 per CTA keeps the state in registers
     case 1: return launch_r<TIO, TS, 1>(a, p);
     case 2: return launch_r<TIO, TS, 2>(a, p);
