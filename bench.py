@@ -655,8 +655,9 @@ def run_only(args):
 
 
 # ------------------------------------------------------------- CPU arm ------
-def cpu_decode_sample(steps=2, B=64, seed=0):
-    """Time the numpy restatement of the same decode step on the host."""
+def cpu_decode_sample(steps=2, B=64, seed=0, warmup=0):
+    """Time the numpy restatement of the same decode step on the host
+    (`warmup` untimed steps first)."""
     from oracle import conv as oconv, decode_state as ods, gdn as ogdn, memory as omem, sampling as osamp
     rng = np.random.default_rng(seed)
     i64 = np.int64
@@ -672,7 +673,9 @@ def cpu_decode_sample(steps=2, B=64, seed=0):
     A_log = np.log(rng.uniform(1, 16, H_V)).astype(f32)
     mem = [omem.empty_state(B, MEM_G, MEM_CAP, MEM_CHUNK, MEM_D) for _ in range(L_MEM)]
     t0 = time.perf_counter()
-    for _ in range(steps):
+    for it in range(warmup + steps):
+        if it == warmup:
+            t0 = time.perf_counter()
         for i in range(L_GDN):
             mixed = rng.standard_normal((B, CONV_C, 1)).astype(f32)
             y, conv_states[i] = oconv.conv_update(mixed, conv_states[i], conv_w)
@@ -701,13 +704,13 @@ def cpu_decode_sample(steps=2, B=64, seed=0):
 
 
 def _cpu_worker(job):
-    steps, B, seed = job
+    steps, B, seed, warmup = job
     if ROOT not in sys.path:
         sys.path.insert(0, ROOT)
-    return cpu_decode_sample(steps=steps, B=B, seed=seed)[1]
+    return cpu_decode_sample(steps=steps, B=B, seed=seed, warmup=warmup)[1]
 
 
-def cpu_decode_parallel(steps=2, B=64):
+def cpu_decode_parallel(steps=2, B=64, warmup=0):
     """The numpy decode step over all host cores: the B sequences are
     independent, so each worker process (spawned, one BLAS thread each) runs
     its share of rows; the step time is the slowest worker's.  Returns
@@ -720,7 +723,7 @@ def cpu_decode_parallel(steps=2, B=64):
     os.environ.update({k: '1' for k in saved})
     try:
         with concurrent.futures.ProcessPoolExecutor(workers, mp_context=multiprocessing.get_context('spawn')) as ex:
-            dts = list(ex.map(_cpu_worker, [(steps, b, 17 + i) for i, b in enumerate(shares)]))
+            dts = list(ex.map(_cpu_worker, [(steps, b, 17 + i, warmup) for i, b in enumerate(shares)]))
     finally:
         for k, v in saved.items():
             if v is None:
@@ -758,15 +761,16 @@ def main():
         if rank != 0:
             return
         steps = max(1, min(args.steps, 3))
+        warm = min(args.warmup, 3)              # untimed steps first, bounded like the timed ones
         rows = args.batch * args.gpus            # the arm's global batch, on the host cores
-        value, dt, cores = cpu_decode_parallel(steps=steps, B=rows)
+        value, dt, cores = cpu_decode_parallel(steps=steps, B=rows, warmup=warm)
         line = {'metric': METRIC, 'value': round(value, 3), 'unit': 'tok/s', 'n_gpus': args.gpus, 'steps': steps,
-                'warmup': 0, 'ms_per_step': round(dt / steps * 1e3, 1), 'higher_is_better': True,
+                'warmup': warm, 'ms_per_step': round(dt / steps * 1e3, 1), 'higher_is_better': True,
                 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'fp32', 'data': 'synthetic (random init, seeded)',
                 'impl': 'reference',
                 'config': decode_config(args.batch, args.gpus),
                 'cpu_baseline': {'value': round(value, 3), 'unit': 'tok/s', 'cores': cores, 'kind': 'port',
-                                 'sample': f'{steps} full decode steps at B={rows} through the numpy '
+                                 'sample': f'{steps} full decode steps (after {warm} untimed) at B={rows} through the numpy '
                                            f'restatement of the reference algorithm (oracle/), rows split over '
                                            f'{cores} worker processes (one thread each), slowest worker '
                                            f'{dt:.1f} s'},
@@ -790,9 +794,9 @@ def main():
         if not args.no_prefill:
             result['prefill'] = run_prefill(torch, yb, torch.device('cuda', local_rank), hbm, tf_burst, peak_kind)
         if world == 1 and not args.no_cpu:
-            value, dt, cores = cpu_decode_parallel(steps=2, B=args.batch)
+            value, dt, cores = cpu_decode_parallel(steps=2, B=args.batch, warmup=1)
             result['cpu_baseline'] = {'value': round(value, 3), 'unit': 'tok/s', 'cores': cores, 'kind': 'port',
-                                      'sample': f'2 full decode steps at B={args.batch} through the numpy '
+                                      'sample': f'2 full decode steps (after 1 untimed) at B={args.batch} through the numpy '
                                                 f'restatement (oracle/), rows split over {cores} worker '
                                                 f'processes (one thread each), slowest worker {dt:.1f} s'}
         print(json.dumps(result), flush=True)

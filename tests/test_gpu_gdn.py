@@ -202,7 +202,8 @@ def test_decode_gates_and_norm_in_kernel(yb):
 
 
 @pytest.mark.parametrize('sdtype,trans,T', [(torch.float32, False, 1), (torch.float16, False, 1),
-                                            (torch.float32, True, 1), (torch.float32, False, 3)])
+                                            (torch.float32, True, 1), (torch.float32, False, 3),
+                                            (torch.bfloat16, True, 2)])
 def test_fused_decode_layer_vs_oracle(yb, sdtype, trans, T):
     """The one-launch GDN decode core (conv -> gates -> L2 norm -> recurrence
     -> gated RMSNorm), 4 calls, against the reference chain in the oracle:
