@@ -155,6 +155,32 @@ def test_decode_16bit_state_storage(yb, sdtype, trans):
     assert rel(host(state), es) <= STATE_RTOL
 
 
+@pytest.mark.parametrize('sdtype', [torch.float16, torch.bfloat16])
+def test_decode_16bit_packed_path_matches_generic(yb, sdtype):
+    """One token per sequence with a 16-bit state in place runs the packed
+    kernel (the state kept as 16-bit pairs, the decayed value rebuilt); the
+    same inputs laid out as varlen sequences of length 1 run the generic
+    kernel.  Both do the same fp32 operations, so outputs and states agree
+    bit for bit."""
+    rng = np.random.default_rng(91)
+    B, H, HV, K, V = 6, 16, 32, 128, 128
+    q, k, v, g, beta, h0 = make_inputs(rng, B, 1, H, HV, K, V, h0_std=0.05)
+    bf = torch.bfloat16
+    sa = cuda(h0).to(sdtype)
+    sb = sa.clone()
+    oa, _ = yb.fused_recurrent_gated_delta_rule(cuda(q, bf), cuda(k, bf), cuda(v, bf), g=cuda(g), beta=cuda(beta),
+                                                initial_state=sa, output_final_state=True,
+                                                use_qk_l2norm_in_kernel=True, inplace=True)
+    cu = torch.arange(B + 1, device='cuda', dtype=torch.int64)
+    flat = lambda x, dt=None: cuda(x, dt).reshape(1, B, *x.shape[2:]) if dt else cuda(x).reshape(1, B, *x.shape[2:])  # noqa: E731
+    ob, _ = yb.fused_recurrent_gated_delta_rule(flat(q, bf), flat(k, bf), flat(v, bf), g=flat(g), beta=flat(beta),
+                                                initial_state=sb, output_final_state=True,
+                                                use_qk_l2norm_in_kernel=True, inplace=True, cu_seqlens=cu)
+    torch.cuda.synchronize()
+    assert torch.equal(sa, sb)
+    assert torch.equal(oa.reshape(-1), ob.reshape(-1))
+
+
 def test_decode_16bit_state_not_inplace_returns_fp32(yb):
     """Without ``inplace`` a 16-bit initial state is read and a new float32
     final state returned, as fla does."""
