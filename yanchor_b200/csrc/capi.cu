@@ -72,8 +72,8 @@ const char *yb_last_error(void) { return g_err; }
 int yb_abi_version(void) { return 1; }
 int yb_device_error(int clear) {
   const int a = read_device_error(clear), b = read_device_error_idx(clear), c = read_device_error_fused(clear),
-            d = read_device_error_loop(clear), e = read_device_error_swa(clear);
-  return a ? a : (b ? b : (c ? c : (d ? d : e)));
+            d = read_device_error_loop(clear), e = read_device_error_swa(clear), f = read_device_error_rec(clear);
+  return a ? a : (b ? b : (c ? c : (d ? d : (e ? e : f))));
 }
 
 int yb_gdn_recurrent_fwd(const void *q, const void *k, const void *v, int64_t q_tok_stride, int64_t k_tok_stride,

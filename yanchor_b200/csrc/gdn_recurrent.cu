@@ -23,6 +23,7 @@
 // final store — as fla's fused recurrent kernel does with a 16-bit h0 / ht.
 #include "common.cuh"
 #include "kernels.h"
+#include "tc.cuh"
 
 namespace yb {
 namespace {
@@ -465,11 +466,225 @@ __global__ void __launch_bounds__(kThreads, 3) gdn_recurrent_p16_kernel(const Re
   }
 }
 
+// fp32 state, one token per sequence, row-major: the state is staged in
+// shared memory by one 64 KB bulk copy rather than held in registers, so
+// three CTAs share an SM (192 KB of state in flight per SM against 128 KB
+// for two register-resident CTAs), and one instruction replaces sixteen
+// vector loads per thread.  The copy's wait is bounded: on timeout the CTA
+// records ERR_REC_STATE, skips the update, and waits (bounded) for the copy
+// before it exits.  The arithmetic is the generic kernel's.
+constexpr int ERR_REC_STATE = 0x601;
+constexpr uint32_t kS32Bytes = 128u * 128u * 4u;
+
+__device__ __forceinline__ void bulk_load_state(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(tc::smem_u32(dst)), "l"(src), "r"(bytes), "r"(tc::smem_u32(bar))
+               : "memory");
+}
+
+template <typename TIO, bool NORM>
+__global__ void __launch_bounds__(kThreads, 3) gdn_recurrent_s32_kernel(const RecParams p) {
+  constexpr int K = 128, V = 128, COLS = V, NCG = COLS / 4, RG = kThreads / NCG, RPT = K / RG;
+  extern __shared__ __align__(128) unsigned char s32_dyn[];
+  float *st = reinterpret_cast<float *>(s32_dyn);                    // [K][V]
+  uint64_t *bar = reinterpret_cast<uint64_t *>(s32_dyn + kS32Bytes);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(bar + 1);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int cg = tid % NCG, rg = tid / NCG, c0 = cg * 4;
+  const int n = blockIdx.x / p.HV, hv = blockIdx.x % p.HV;
+  const int h = hv / (p.HV / p.H);
+  const int64_t tok = int64_t(n) * p.T;   // the sequence's only token
+
+  __shared__ __align__(16) float sq[K];
+  __shared__ __align__(16) float sk[K];
+  __shared__ __align__(16) float sv[V];
+  __shared__ __align__(16) float so[V];
+  __shared__ __align__(16) float red_k[RG][V];
+  __shared__ __align__(16) float red_q[RG][V];
+  __shared__ float s_decay, s_beta, s_kq;
+
+  const int64_t head = (int64_t(n) * p.HV + hv) * K * V;
+  const float *src = static_cast<const float *>(p.h0) + head;
+  if (tid == 0) {
+    *abort_flag = 0;
+    tc::mbar_init(bar, 1);
+    tc::mbar_fence_init();
+    // warm L2 with the state before the wait (an L2 prefetch is safe even if the previous kernel writes it)
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(kS32Bytes) : "memory");
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_release();
+  if (warp == 0) {
+    // four 16 KB copies (32 rows each) on one barrier, so the copy engine works on them in parallel
+    if (lane == 0) tc::mbar_arrive_expect_tx(bar, kS32Bytes);
+    __syncwarp();
+    if (lane < 4) bulk_load_state(st + lane * (K / 4) * COLS, src + lane * (K / 4) * COLS, kS32Bytes / 4, bar);
+  }
+
+  const bool l2 = p.flags & YB_GDN_QK_L2NORM;
+  const bool gate_in = p.flags & YB_GDN_GATE_IN_KERNEL;
+  const bool beta_sig = p.flags & YB_GDN_BETA_SIGMOID;
+  const TIO *qp = static_cast<const TIO *>(p.q);
+  const TIO *kp = static_cast<const TIO *>(p.k);
+  const TIO *vp = static_cast<const TIO *>(p.v);
+  TIO *op = static_cast<TIO *>(p.o);
+  bool ok = true;
+  {
+    // ---- stage q, k (normalised, q scaled), v, decay, beta ----
+    if (warp == 0) {
+      float qv[4] = {0.f, 0.f, 0.f, 0.f}, kv[4] = {0.f, 0.f, 0.f, 0.f};
+      if (lane < K / 4) {
+        load4(qp + tok * p.q_ts + int64_t(h) * K + lane * 4, qv);
+        load4(kp + tok * p.k_ts + int64_t(h) * K + lane * 4, kv);
+      }
+      float qn = 1.f, kn = 1.f;
+      if (l2) {
+        float qs2 = qv[0] * qv[0] + qv[1] * qv[1] + qv[2] * qv[2] + qv[3] * qv[3];
+        float ks2 = kv[0] * kv[0] + kv[1] * kv[1] + kv[2] * kv[2] + kv[3] * kv[3];
+        qn = rsqrtf(warp_sum(qs2) + 1e-6f);
+        kn = rsqrtf(warp_sum(ks2) + 1e-6f);
+      }
+      float dot = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        qv[j] *= qn * p.scale;
+        kv[j] *= kn;
+        dot += qv[j] * kv[j];
+      }
+      dot = warp_sum(dot);
+      if (lane < K / 4) {
+        *reinterpret_cast<float4 *>(sq + lane * 4) = make_float4(qv[0], qv[1], qv[2], qv[3]);
+        *reinterpret_cast<float4 *>(sk + lane * 4) = make_float4(kv[0], kv[1], kv[2], kv[3]);
+      }
+      if (lane == 0) s_kq = dot;
+    } else if (warp == 1) {
+      if (lane < V / 4) {
+        float vv[4];
+        load4(vp + tok * p.v_ts + int64_t(hv) * V + lane * 4, vv);
+        *reinterpret_cast<float4 *>(sv + lane * 4) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+      }
+      if (lane == 0) {
+        float gl = load_scalar(p.g, tok * p.g_ts + hv, p.g_dtype);
+        if (gate_in) gl = -expf(p.A_log[hv]) * softplus20(gl + (p.dt_bias ? p.dt_bias[hv] : 0.f));
+        float b = load_scalar(p.beta, tok * p.beta_ts + hv, p.beta_dtype);
+        s_decay = expf(gl);
+        s_beta = beta_sig ? sigmoidf_(b) : b;
+      }
+    }
+    __syncthreads();
+    ok = tc::mbar_wait(bar, 0, abort_flag, ERR_REC_STATE);
+    ok = !__syncthreads_or(!ok);
+    const float dec = s_decay, bet = s_beta, kq = s_kq;
+    if (ok) {
+      float ak[4] = {0.f, 0.f, 0.f, 0.f}, aq[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int i = 0; i < RPT; ++i) {
+        const float4 x4 = *reinterpret_cast<const float4 *>(st + (rg * RPT + i) * COLS + c0);
+        float x[4] = {x4.x, x4.y, x4.z, x4.w};
+        const float kr = sk[rg * RPT + i], qr = sq[rg * RPT + i];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          x[j] *= dec;
+          ak[j] = fmaf(x[j], kr, ak[j]);
+          aq[j] = fmaf(x[j], qr, aq[j]);
+        }
+      }
+      *reinterpret_cast<float4 *>(&red_k[rg][c0]) = make_float4(ak[0], ak[1], ak[2], ak[3]);
+      *reinterpret_cast<float4 *>(&red_q[rg][c0]) = make_float4(aq[0], aq[1], aq[2], aq[3]);
+    }
+    __syncthreads();
+    if (ok) {
+      float kvs[4] = {0.f, 0.f, 0.f, 0.f}, qss[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int r = 0; r < RG; ++r) {
+        float4 a = *reinterpret_cast<const float4 *>(&red_k[r][c0]);
+        float4 b = *reinterpret_cast<const float4 *>(&red_q[r][c0]);
+        kvs[0] += a.x; kvs[1] += a.y; kvs[2] += a.z; kvs[3] += a.w;
+        qss[0] += b.x; qss[1] += b.y; qss[2] += b.z; qss[3] += b.w;
+      }
+      float delta[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) delta[j] = bet * (sv[c0 + j] - kvs[j]);
+      float *dst = static_cast<float *>(p.ht) + head;
+#pragma unroll
+      for (int i = 0; i < RPT; ++i) {
+        const float4 x4 = *reinterpret_cast<const float4 *>(st + (rg * RPT + i) * COLS + c0);
+        float x[4] = {x4.x, x4.y, x4.z, x4.w};
+        const float kr = sk[rg * RPT + i];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          x[j] *= dec;
+          x[j] = fmaf(kr, delta[j], x[j]);
+        }
+        st_state4(dst + (rg * RPT + i) * COLS + c0, x);
+      }
+      if (rg == 0) {
+        float ov[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) ov[j] = fmaf(delta[j], kq, qss[j]);
+        *reinterpret_cast<float4 *>(so + c0) = make_float4(ov[0], ov[1], ov[2], ov[3]);
+      }
+    }
+    __syncthreads();
+    if (ok) {
+    // ---- output (and the fused gated RMSNorm) by warp 0 ----
+    if (warp == 0) {
+      float ov[4] = {0.f, 0.f, 0.f, 0.f};
+      if (lane < V / 4) {
+        float4 x = *reinterpret_cast<const float4 *>(so + lane * 4);
+        ov[0] = x.x; ov[1] = x.y; ov[2] = x.z; ov[3] = x.w;
+      }
+      TIO *dst = op + tok * int64_t(p.HV) * V + int64_t(hv) * V + lane * 4;
+      if constexpr (NORM) {
+        // Qwen3_5RMSNormGated on the io-dtype output, with its roundings.
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          ov[j] = round_to<TIO>(ov[j]);
+          ss += ov[j] * ov[j];
+        }
+        const float inv = rsqrtf(warp_sum(ss) / float(V) + p.norm_eps);
+        if (lane < V / 4) {
+          float zz[4], w[4];
+          load4(static_cast<const TIO *>(p.z) + tok * int64_t(p.HV) * V + int64_t(hv) * V + lane * 4, zz);
+          load4(static_cast<const TIO *>(p.norm_w) + lane * 4, w);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float y = round_to<TIO>(w[j] * round_to<TIO>(ov[j] * inv));
+            ov[j] = y * (zz[j] * sigmoidf_(zz[j]));
+          }
+          store4(dst, ov);
+        }
+      } else {
+        if (lane < V / 4) store4(dst, ov);
+      }
+    }
+    }
+  }
+  if (!ok && tid == 0) {
+    // the copy may still land: wait for it (bounded, not cut short) before the CTA exits
+    volatile int keep_waiting = 0;
+    tc::mbar_wait(bar, 0, &keep_waiting, ERR_REC_STATE);
+  }
+}
+
 template <typename TIO, int K, int V, typename TS = float>
 int launch_kv(const GdnArgs &a, const RecParams &p) {
   const bool trans = a.flags & YB_GDN_TRANSPOSE_STATE;
   const bool norm = a.z != nullptr;
   dim3 grid(unsigned(a.N * a.HV));
+  if constexpr (sizeof(TS) == 4 && K == 128 && V == 128) {
+    // one token per sequence, fp32 state: staged in shared memory, three CTAs per SM
+    if (!trans && a.T == 1 && !a.cu_seqlens && a.h0 && a.ht && (reinterpret_cast<uintptr_t>(a.h0) & 15u) == 0) {
+      auto ks = norm ? gdn_recurrent_s32_kernel<TIO, true> : gdn_recurrent_s32_kernel<TIO, false>;
+      const int smem = int(kS32Bytes) + 16;
+      cudaError_t e = cudaFuncSetAttribute(ks, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e == cudaSuccess) e = launch_pdl(ks, grid, dim3(kThreads), size_t(smem), a.stream, p);
+      if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "gdn_recurrent_s32_kernel: %s", cudaGetErrorString(e));
+      return check_launch("gdn_recurrent_s32_kernel");
+    }
+  }
   if constexpr (sizeof(TS) == 2 && K == 128 && V == 128) {
     // one token per sequence, state read and written in place-or-not: the packed 16-bit form
     if (!trans && a.T == 1 && !a.cu_seqlens && a.h0 && a.ht) {
@@ -504,6 +719,16 @@ int launch_io(const GdnArgs &a, const RecParams &p) {
 }
 
 }  // namespace
+
+int read_device_error_rec(int clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, tc::g_device_error, sizeof(int)) != cudaSuccess) return -1;
+  if (clear && v) {
+    const int z = 0;
+    cudaMemcpyToSymbol(tc::g_device_error, &z, sizeof(int));
+  }
+  return v;
+}
 
 int launch_gdn_recurrent(const GdnArgs &a) {
   RecParams p;

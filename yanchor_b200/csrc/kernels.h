@@ -137,6 +137,7 @@ struct FusedArgs {
 };
 int launch_gdn_decode_fused(const FusedArgs &a);
 int read_device_error_fused(int clear);
+int read_device_error_rec(int clear);
 
 struct SwaArgs {
   const void *new_k, *new_v;      // ring write: the new token [B, KVH, 1, D]
