@@ -54,8 +54,10 @@ const char *yb_last_error(void);
 int yb_abi_version(void);
 /*
  * Error word of the kernels that synchronise through time-bounded waits (the
- * tensor-core kernels) or skip a store whose index leaves its table (the
- * decode bookkeeping, 0x401): 0 when every wait completed and every index
+ * tensor-core kernels, the one-launch decode layer's state prefetch, the
+ * single-token fp32 decode's state copy, 0x601) or skip a store whose index
+ * leaves its table (the decode bookkeeping, 0x401): 0 when every wait
+ * completed and every index
  * was in range, else the first code recorded (that launch's outputs are then
  * invalid).
  * Synchronises the current device; `clear` resets the word.  No reference
