@@ -293,188 +293,28 @@ __global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(const RecParams
   }
 }
 
-// Single-token decode with a 16-bit state kept packed: each thread holds its
-// RPT rows x 4 columns as the 16-bit pairs it loaded (32 registers instead of
-// 64) and rebuilds the decayed fp32 value -- the same operations as the
-// generic kernel, so the results are identical -- once for the reductions
-// and once for the update, whose result it stores at once.  With fewer
-// registers three CTAs share an SM, so the halved bytes per CTA still leave
-// as many bytes in flight per SM as the fp32 state does.
-template <typename TIO, typename TS, bool NORM>
-__global__ void __launch_bounds__(kThreads, 3) gdn_recurrent_p16_kernel(const RecParams p) {
-  constexpr int K = 128, V = 128, COLS = V, NCG = COLS / 4, RG = kThreads / NCG, RPT = K / RG;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int cg = tid % NCG, rg = tid / NCG, c0 = cg * 4;
-  const int n = blockIdx.x / p.HV, hv = blockIdx.x % p.HV;
-  const int h = hv / (p.HV / p.H);
-  const int64_t tok = int64_t(n) * p.T;   // the sequence's only token
-
-  __shared__ __align__(16) float sq[K];
-  __shared__ __align__(16) float sk[K];
-  __shared__ __align__(16) float sv[V];
-  __shared__ __align__(16) float so[V];
-  __shared__ __align__(16) float red_k[RG][V];
-  __shared__ __align__(16) float red_q[RG][V];
-  __shared__ float s_decay, s_beta, s_kq;
-
-  const int64_t head = (int64_t(n) * p.HV + hv) * K * V;
-  const TS *src = static_cast<const TS *>(p.h0) + head;
-#pragma unroll
-  for (int i = 0; i < RPT; i += 2) prefetch_l2(src + (rg * RPT + i) * COLS + c0);
-  pdl_wait();
-  pdl_release();
-  uint2 hs[RPT];
-#pragma unroll
-  for (int i = 0; i < RPT; ++i) hs[i] = __ldcs(reinterpret_cast<const uint2 *>(src + (rg * RPT + i) * COLS + c0));
-  auto unpack = [](uint2 v, float x[4]) {
-    const TS *e = reinterpret_cast<const TS *>(&v);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) x[j] = to_f(e[j]);
-  };
-
-  const bool l2 = p.flags & YB_GDN_QK_L2NORM;
-  const bool gate_in = p.flags & YB_GDN_GATE_IN_KERNEL;
-  const bool beta_sig = p.flags & YB_GDN_BETA_SIGMOID;
-  const TIO *qp = static_cast<const TIO *>(p.q);
-  const TIO *kp = static_cast<const TIO *>(p.k);
-  const TIO *vp = static_cast<const TIO *>(p.v);
-  TIO *op = static_cast<TIO *>(p.o);
-  {
-    // ---- stage q, k (normalised, q scaled), v, decay, beta ----
-    if (warp == 0) {
-      float qv[4] = {0.f, 0.f, 0.f, 0.f}, kv[4] = {0.f, 0.f, 0.f, 0.f};
-      if (lane < K / 4) {
-        load4(qp + tok * p.q_ts + int64_t(h) * K + lane * 4, qv);
-        load4(kp + tok * p.k_ts + int64_t(h) * K + lane * 4, kv);
-      }
-      float qn = 1.f, kn = 1.f;
-      if (l2) {
-        float qs2 = qv[0] * qv[0] + qv[1] * qv[1] + qv[2] * qv[2] + qv[3] * qv[3];
-        float ks2 = kv[0] * kv[0] + kv[1] * kv[1] + kv[2] * kv[2] + kv[3] * kv[3];
-        qn = rsqrtf(warp_sum(qs2) + 1e-6f);
-        kn = rsqrtf(warp_sum(ks2) + 1e-6f);
-      }
-      float dot = 0.f;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        qv[j] *= qn * p.scale;
-        kv[j] *= kn;
-        dot += qv[j] * kv[j];
-      }
-      dot = warp_sum(dot);
-      if (lane < K / 4) {
-        *reinterpret_cast<float4 *>(sq + lane * 4) = make_float4(qv[0], qv[1], qv[2], qv[3]);
-        *reinterpret_cast<float4 *>(sk + lane * 4) = make_float4(kv[0], kv[1], kv[2], kv[3]);
-      }
-      if (lane == 0) s_kq = dot;
-    } else if (warp == 1) {
-      if (lane < V / 4) {
-        float vv[4];
-        load4(vp + tok * p.v_ts + int64_t(hv) * V + lane * 4, vv);
-        *reinterpret_cast<float4 *>(sv + lane * 4) = make_float4(vv[0], vv[1], vv[2], vv[3]);
-      }
-      if (lane == 0) {
-        float gl = load_scalar(p.g, tok * p.g_ts + hv, p.g_dtype);
-        if (gate_in) gl = -expf(p.A_log[hv]) * softplus20(gl + (p.dt_bias ? p.dt_bias[hv] : 0.f));
-        float b = load_scalar(p.beta, tok * p.beta_ts + hv, p.beta_dtype);
-        s_decay = expf(gl);
-        s_beta = beta_sig ? sigmoidf_(b) : b;
-      }
-    }
-    __syncthreads();
-    const float dec = s_decay, bet = s_beta, kq = s_kq;
-    float ak[4] = {0.f, 0.f, 0.f, 0.f}, aq[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int i = 0; i < RPT; ++i) {
-      float x[4];
-      unpack(hs[i], x);
-      const float kr = sk[rg * RPT + i], qr = sq[rg * RPT + i];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        x[j] *= dec;
-        ak[j] = fmaf(x[j], kr, ak[j]);
-        aq[j] = fmaf(x[j], qr, aq[j]);
-      }
-    }
-    *reinterpret_cast<float4 *>(&red_k[rg][c0]) = make_float4(ak[0], ak[1], ak[2], ak[3]);
-    *reinterpret_cast<float4 *>(&red_q[rg][c0]) = make_float4(aq[0], aq[1], aq[2], aq[3]);
-    __syncthreads();
-    float kvs[4] = {0.f, 0.f, 0.f, 0.f}, qss[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int r = 0; r < RG; ++r) {
-      float4 a = *reinterpret_cast<const float4 *>(&red_k[r][c0]);
-      float4 b = *reinterpret_cast<const float4 *>(&red_q[r][c0]);
-      kvs[0] += a.x; kvs[1] += a.y; kvs[2] += a.z; kvs[3] += a.w;
-      qss[0] += b.x; qss[1] += b.y; qss[2] += b.z; qss[3] += b.w;
-    }
-    float delta[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) delta[j] = bet * (sv[c0 + j] - kvs[j]);
-    TS *dst = static_cast<TS *>(p.ht) + head;
-#pragma unroll
-    for (int i = 0; i < RPT; ++i) {
-      float x[4];
-      unpack(hs[i], x);
-      const float kr = sk[rg * RPT + i];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        x[j] *= dec;
-        x[j] = fmaf(kr, delta[j], x[j]);
-      }
-      st_state4(dst + (rg * RPT + i) * COLS + c0, x);
-    }
-    if (rg == 0) {
-      float ov[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) ov[j] = fmaf(delta[j], kq, qss[j]);
-      *reinterpret_cast<float4 *>(so + c0) = make_float4(ov[0], ov[1], ov[2], ov[3]);
-    }
-    __syncthreads();
-
-    // ---- output (and the fused gated RMSNorm) by warp 0 ----
-    if (warp == 0) {
-      float ov[4] = {0.f, 0.f, 0.f, 0.f};
-      if (lane < V / 4) {
-        float4 x = *reinterpret_cast<const float4 *>(so + lane * 4);
-        ov[0] = x.x; ov[1] = x.y; ov[2] = x.z; ov[3] = x.w;
-      }
-      TIO *dst = op + tok * int64_t(p.HV) * V + int64_t(hv) * V + lane * 4;
-      if constexpr (NORM) {
-        // Qwen3_5RMSNormGated on the io-dtype output, with its roundings.
-        float ss = 0.f;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          ov[j] = round_to<TIO>(ov[j]);
-          ss += ov[j] * ov[j];
-        }
-        const float inv = rsqrtf(warp_sum(ss) / float(V) + p.norm_eps);
-        if (lane < V / 4) {
-          float zz[4], w[4];
-          load4(static_cast<const TIO *>(p.z) + tok * int64_t(p.HV) * V + int64_t(hv) * V + lane * 4, zz);
-          load4(static_cast<const TIO *>(p.norm_w) + lane * 4, w);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float y = round_to<TIO>(w[j] * round_to<TIO>(ov[j] * inv));
-            ov[j] = y * (zz[j] * sigmoidf_(zz[j]));
-          }
-          store4(dst, ov);
-        }
-      } else {
-        if (lane < V / 4) store4(dst, ov);
-      }
-    }
-  }
-}
-
-// fp32 state, one token per sequence, row-major: the state is staged in
-// shared memory by one 64 KB bulk copy rather than held in registers, so
-// three CTAs share an SM (192 KB of state in flight per SM against 128 KB
-// for two register-resident CTAs), and one instruction replaces sixteen
-// vector loads per thread.  The copy's wait is bounded: on timeout the CTA
-// records ERR_REC_STATE, skips the update, and waits (bounded) for the copy
-// before it exits.  The arithmetic is the generic kernel's.
+// One token per sequence, row-major state: the state is staged in shared
+// memory by four bulk copies (16 KB each for fp32, 8 KB for a 16-bit state)
+// rather than held in registers, so three (fp32) or four (16-bit) CTAs share
+// an SM and more bytes are in flight per SM than with register-resident
+// CTAs; four copies instead of sixteen vector loads per thread.  The copies'
+// wait is bounded: on timeout the CTA records ERR_REC_STATE, skips the
+// update, and waits (bounded) for the copies before it exits.  The arithmetic
+// is the generic kernel's, so the results are identical.
 constexpr int ERR_REC_STATE = 0x601;
-constexpr uint32_t kS32Bytes = 128u * 128u * 4u;
+template <typename TS> __host__ __device__ constexpr uint32_t staged_bytes() { return 128u * 128u * uint32_t(sizeof(TS)); }
+// 4 consecutive state values of the staged tile, widened to fp32
+__device__ __forceinline__ void lds4(const float *p, float *x) {
+  const float4 v = *reinterpret_cast<const float4 *>(p);
+  x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+}
+template <typename T16>
+__device__ __forceinline__ void lds4(const T16 *p, float *x) {
+  const uint2 v = *reinterpret_cast<const uint2 *>(p);
+  const T16 *e = reinterpret_cast<const T16 *>(&v);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) x[j] = to_f(e[j]);
+}
 
 __device__ __forceinline__ void bulk_load_state(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
@@ -482,11 +322,12 @@ __device__ __forceinline__ void bulk_load_state(void *dst, const void *src, uint
                : "memory");
 }
 
-template <typename TIO, bool NORM>
-__global__ void __launch_bounds__(kThreads, 3) gdn_recurrent_s32_kernel(const RecParams p) {
+template <typename TIO, typename TS, bool NORM>
+__global__ void __launch_bounds__(kThreads, sizeof(TS) == 4 ? 3 : 4) gdn_recurrent_sst_kernel(const RecParams p) {
   constexpr int K = 128, V = 128, COLS = V, NCG = COLS / 4, RG = kThreads / NCG, RPT = K / RG;
+  constexpr uint32_t kS32Bytes = staged_bytes<TS>();
   extern __shared__ __align__(128) unsigned char s32_dyn[];
-  float *st = reinterpret_cast<float *>(s32_dyn);                    // [K][V]
+  TS *st = reinterpret_cast<TS *>(s32_dyn);                          // [K][V]
   uint64_t *bar = reinterpret_cast<uint64_t *>(s32_dyn + kS32Bytes);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(bar + 1);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -504,7 +345,7 @@ __global__ void __launch_bounds__(kThreads, 3) gdn_recurrent_s32_kernel(const Re
   __shared__ float s_decay, s_beta, s_kq;
 
   const int64_t head = (int64_t(n) * p.HV + hv) * K * V;
-  const float *src = static_cast<const float *>(p.h0) + head;
+  const TS *src = static_cast<const TS *>(p.h0) + head;
   if (tid == 0) {
     *abort_flag = 0;
     tc::mbar_init(bar, 1);
@@ -580,8 +421,8 @@ __global__ void __launch_bounds__(kThreads, 3) gdn_recurrent_s32_kernel(const Re
       float ak[4] = {0.f, 0.f, 0.f, 0.f}, aq[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < RPT; ++i) {
-        const float4 x4 = *reinterpret_cast<const float4 *>(st + (rg * RPT + i) * COLS + c0);
-        float x[4] = {x4.x, x4.y, x4.z, x4.w};
+        float x[4];
+        lds4(st + (rg * RPT + i) * COLS + c0, x);
         const float kr = sk[rg * RPT + i], qr = sq[rg * RPT + i];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -606,11 +447,11 @@ __global__ void __launch_bounds__(kThreads, 3) gdn_recurrent_s32_kernel(const Re
       float delta[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) delta[j] = bet * (sv[c0 + j] - kvs[j]);
-      float *dst = static_cast<float *>(p.ht) + head;
+      TS *dst = static_cast<TS *>(p.ht) + head;
 #pragma unroll
       for (int i = 0; i < RPT; ++i) {
-        const float4 x4 = *reinterpret_cast<const float4 *>(st + (rg * RPT + i) * COLS + c0);
-        float x[4] = {x4.x, x4.y, x4.z, x4.w};
+        float x[4];
+        lds4(st + (rg * RPT + i) * COLS + c0, x);
         const float kr = sk[rg * RPT + i];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -674,24 +515,16 @@ int launch_kv(const GdnArgs &a, const RecParams &p) {
   const bool trans = a.flags & YB_GDN_TRANSPOSE_STATE;
   const bool norm = a.z != nullptr;
   dim3 grid(unsigned(a.N * a.HV));
-  if constexpr (sizeof(TS) == 4 && K == 128 && V == 128) {
-    // one token per sequence, fp32 state: staged in shared memory, three CTAs per SM
+  if constexpr (K == 128 && V == 128) {
+    // one token per sequence: the state staged in shared memory, three (fp32) or four (16-bit)
+    // CTAs per SM
     if (!trans && a.T == 1 && !a.cu_seqlens && a.h0 && a.ht && (reinterpret_cast<uintptr_t>(a.h0) & 15u) == 0) {
-      auto ks = norm ? gdn_recurrent_s32_kernel<TIO, true> : gdn_recurrent_s32_kernel<TIO, false>;
-      const int smem = int(kS32Bytes) + 16;
+      auto ks = norm ? gdn_recurrent_sst_kernel<TIO, TS, true> : gdn_recurrent_sst_kernel<TIO, TS, false>;
+      const int smem = int(staged_bytes<TS>()) + 16;
       cudaError_t e = cudaFuncSetAttribute(ks, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       if (e == cudaSuccess) e = launch_pdl(ks, grid, dim3(kThreads), size_t(smem), a.stream, p);
-      if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "gdn_recurrent_s32_kernel: %s", cudaGetErrorString(e));
-      return check_launch("gdn_recurrent_s32_kernel");
-    }
-  }
-  if constexpr (sizeof(TS) == 2 && K == 128 && V == 128) {
-    // one token per sequence, state read and written in place-or-not: the packed 16-bit form
-    if (!trans && a.T == 1 && !a.cu_seqlens && a.h0 && a.ht) {
-      auto k16 = norm ? gdn_recurrent_p16_kernel<TIO, TS, true> : gdn_recurrent_p16_kernel<TIO, TS, false>;
-      const cudaError_t e = launch_pdl(k16, grid, dim3(kThreads), 0, a.stream, p);
-      if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "gdn_recurrent_p16_kernel: %s", cudaGetErrorString(e));
-      return check_launch("gdn_recurrent_p16_kernel");
+      if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "gdn_recurrent_sst_kernel: %s", cudaGetErrorString(e));
+      return check_launch("gdn_recurrent_sst_kernel");
     }
   }
   auto kern = trans ? (norm ? gdn_recurrent_kernel<TIO, TS, K, V, true, true> : gdn_recurrent_kernel<TIO, TS, K, V, true, false>)
