@@ -456,7 +456,7 @@ def run_gpu(args, rank, world, local_rank, dist):
         'warmup': args.warmup, 'ms_per_step': round(ms, 4), 'higher_is_better': True, 'scaling': 'weak',
         'vs_baseline': None, 'dtype': 'fp32 state, bf16 activations', 'data': 'synthetic (random init, seeded)',
         'config': decode_config(B, world),
-        'roofline': {'bound': 'hbm', 'kernel': 'gdn_recurrent_kernel', 'achieved': round(achieved, 1),
+        'roofline': {'bound': 'hbm', 'kernel': 'gdn_recurrent_sst_kernel', 'achieved': round(achieved, 1),
                      'peak': hbm, 'unit': 'GB/s', 'frac': round(achieved / hbm, 4), 'peak_kind': peak_kind,
                      'bytes_per_launch': gbytes, 'launch_ms': round(gdn_ms, 5), 'traffic': traffic_per_launch()},
         'e2e': {'value': round(world * B / (e2e_ms / 1e3), 1), 'unit': 'tok/s', 'h2d_bytes_per_step': h2d,
@@ -485,9 +485,9 @@ def run_gpu(args, rank, world, local_rank, dist):
 
 
 def traffic_per_launch():
-    """DRAM bytes (read + write) of one gdn_recurrent_kernel launch from the
+    """DRAM bytes (read + write) of one gdn_recurrent_sst_kernel launch from the
     committed ncu summary, or None when no capture has been summarised."""
-    path = os.path.join(ROOT, 'profiles', 'gdn_recurrent_decode_b64.json')
+    path = os.path.join(ROOT, 'profiles', 'gdn_recurrent_sst_decode_b64.json')
     try:
         with open(path) as f:
             return json.load(f).get('dram_bytes_per_launch')
