@@ -48,7 +48,7 @@ __device__ __forceinline__ bool better(float v, int64_t i, float bv, int64_t bi)
 }
 
 int greedy_splits(int64_t B, int64_t vocab) {
-  int64_t s = (296 + B - 1) / B;
+  int64_t s = (1184 + B - 1) / B;   // ~8 CTAs per SM: enough loads in flight to stream the scores
   const int64_t cap = (vocab + 2047) / 2048;
   if (s > cap) s = cap;
   return int(s < 1 ? 1 : s);
@@ -87,7 +87,25 @@ __global__ void __launch_bounds__(kNT) greedy_partial_kernel(const T *scores, in
     if (better(x, j, best, bi)) { best = x; bi = j; }
   }
   const int64_t nvec = (hi - head) / VEC;
-  for (int64_t u = threadIdx.x; u < nvec; u += kNT) {
+  // four vectors per pass, all loads issued before the compares
+  int64_t u = threadIdx.x;
+  for (; u + 3 * kNT < nvec; u += 4 * kNT) {
+    float x[4][VEC];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const int64_t i = head + (u + w * kNT) * VEC;
+      if constexpr (VEC == 4) load4(reinterpret_cast<const float *>(row + i), x[w]);
+      else load8(row + i, x[w]);
+    }
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const int64_t i = head + (u + w * kNT) * VEC;
+#pragma unroll
+      for (int t = 0; t < VEC; ++t)
+        if (better(x[w][t], i + t, best, bi)) { best = x[w][t]; bi = i + t; }
+    }
+  }
+  for (; u < nvec; u += kNT) {
     const int64_t i = head + u * VEC;
     float x[VEC];
     if constexpr (VEC == 4) load4(reinterpret_cast<const float *>(row + i), x);
