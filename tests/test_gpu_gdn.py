@@ -281,6 +281,41 @@ def test_fused_decode_layer_vs_oracle(yb, sdtype, trans, T):
     assert rel(host(state), es) <= STATE_RTOL
 
 
+def test_fused_decode_staged_pair_matches_pair(yb):
+    """Two one-token calls (the staged paired kernel: state in shared memory,
+    conv under the state copy) against one two-token call (the register
+    paired kernel) from the same fp32 state: the same arithmetic in the same
+    order, so outputs, state and conv state agree bit for bit."""
+    rng = np.random.default_rng(77)
+    B, T, H, HV, K, V = 3, 2, 16, 32, 128, 128
+    C = 2 * H * K + HV * V
+    bf = torch.bfloat16
+    mixed = cuda(rng.standard_normal((B, T, C)), bf)
+    z = cuda(rng.standard_normal((B, T, HV, V)), bf)
+    a = cuda(2 * rng.standard_normal((B, T, HV)), bf)
+    blog = cuda(rng.standard_normal((B, T, HV)), bf)
+    f32 = lambda x: cuda(np.float32(x))  # noqa: E731
+    w_conv = f32(0.5 * rng.standard_normal((C, 4)))
+    A_log = f32(np.log(rng.uniform(1, 16, HV)))
+    dt_bias = f32(rng.standard_normal(HV))
+    wn = cuda(1 + 0.1 * rng.standard_normal(V), bf)
+    cs0 = cuda(rng.standard_normal((B, C, 4)), bf)
+    h0 = f32(0.05 * rng.standard_normal((B, HV, K, V)))
+
+    cs_pair, st_pair = cs0.clone(), h0.clone()
+    o_pair = yb.fused_gdn_decode(mixed, z, a, blog, cs_pair, w_conv, None, st_pair, A_log, dt_bias, wn,
+                                 num_k_heads=H)
+    cs_st, st_st = cs0.clone(), h0.clone()
+    o_st = [yb.fused_gdn_decode(mixed[:, t:t + 1].contiguous(), z[:, t:t + 1].contiguous(),
+                                a[:, t:t + 1].contiguous(), blog[:, t:t + 1].contiguous(), cs_st, w_conv, None,
+                                st_st, A_log, dt_bias, wn, num_k_heads=H) for t in range(T)]
+    torch.cuda.synchronize()
+    assert yb.lib().yb_device_error(1) == 0
+    assert torch.equal(torch.cat(o_st, 1), o_pair)
+    assert torch.equal(st_st, st_pair)
+    assert torch.equal(cs_st, cs_pair)
+
+
 def test_gdn_gates_kernel(yb, golden):
     d = golden('gdn')
     beta, g = yb.gdn_gates(cuda(d['gate_b']), cuda(d['gate_a']), cuda(d['gate_A_log']), cuda(d['gate_dt_bias']))

@@ -21,9 +21,11 @@
 // registers only one fits).  The prefetch wait is bounded; on timeout the
 // CTA records an error code, waits (bounded) for the copy in flight, exits.
 //
-// That persistent form serves HV = H; for HV = 2H the paired form further
-// down (two CTAs per k-head in a cluster, state in registers, two CTAs per
-// SM) is faster and is used instead.
+// That persistent form serves HV = H; for HV = 2H the paired forms further
+// down (two CTAs per k-head in a cluster) are faster and are used instead:
+// one token with the row-major state stages the state in shared memory
+// (three CTAs per SM for fp32, four for 16-bit); more tokens or the
+// transposed layout keep it in registers (two CTAs per SM).
 //
 // Roundings follow the reference chain: conv outputs are rounded to the
 // activation dtype (the conv update writes a bf16 tensor), beta = sigmoid(b)
@@ -561,6 +563,209 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) gdn_decode_p
   if (p.T > 0) asm volatile("barrier.cluster.wait.aligned;" ::: "memory");   // the peer has read this CTA's buffer
 }
 
+// ---- the staged paired form (HV = 2 H, one token, row-major state): the pair kernel's conv and
+// q/k exchange, with the state staged in shared memory by four bulk copies (warmed into L2 before
+// the dependent-launch wait, issued once the conv is done, in flight during the q/k norms), so
+// three (fp32) or four (16-bit) CTAs share an SM.  The recurrence is the staged
+// recurrence kernel's: same arithmetic, same order, identical results.  The copies' wait is
+// bounded: on timeout the CTA records ERR_WAIT_STATE, skips the update, and waits (bounded) for
+// the copies before it exits. ----
+template <typename T16>
+__device__ __forceinline__ void lds_state4(const T16 *p, float *x) {
+  const uint2 v = *reinterpret_cast<const uint2 *>(p);
+  const T16 *e = reinterpret_cast<const T16 *>(&v);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) x[j] = to_f(e[j]);
+}
+__device__ __forceinline__ void lds_state4(const float *p, float *x) {
+  const float4 v = *reinterpret_cast<const float4 *>(p);
+  x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+}
+template <typename TS> __host__ __device__ constexpr uint32_t pair_staged_bytes() {
+  return uint32_t(KD) * VD * uint32_t(sizeof(TS));
+}
+
+template <typename TIO, typename TS>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, sizeof(TS) == 4 ? 3 : 4)
+    gdn_decode_pair_sst_kernel(const FusedParams p) {
+  constexpr int COLS = VD, NCG = COLS / 4, RG = 256 / NCG, RPT = KD / RG;
+  constexpr uint32_t SB = pair_staged_bytes<TS>();
+  namespace cgr = cooperative_groups;
+  cgr::cluster_group cluster = cgr::this_cluster();
+  extern __shared__ __align__(128) unsigned char pair_dyn[];
+  TS *st = reinterpret_cast<TS *>(pair_dyn);                           // [K][V]
+  uint64_t *bar = reinterpret_cast<uint64_t *>(pair_dyn + SB);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(bar + 1);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int cg = tid % NCG, rg = tid / NCG, c0 = cg * 4;
+  const int64_t n = blockIdx.x / p.HV;
+  const int hv = int(blockIdx.x % p.HV), h = hv >> 1;
+  const unsigned rank = cluster.block_rank();   // hv & 1
+  const int64_t tok = n;                        // the sequence's only token
+
+  __shared__ __align__(16) float sx[KD];        // this CTA's conv output: q (rank 0) or k (rank 1)
+  __shared__ __align__(16) float sq[KD];
+  __shared__ __align__(16) float sk[KD];
+  __shared__ __align__(16) float sv[VD];
+  __shared__ __align__(16) float so[VD];
+  __shared__ __align__(16) float red_k[RG][VD];
+  __shared__ __align__(16) float red_q[RG][VD];
+  __shared__ float s_decay, s_beta, s_kq;
+
+  TS *stp = static_cast<TS *>(p.state) + (n * p.HV + hv) * int64_t(KD) * VD;
+  if (tid == 0) {
+    *abort_flag = 0;
+    mbar_init(bar, 1);
+    mbar_fence_init();
+    // warm L2 with the state before the wait (an L2 prefetch is safe even if the previous kernel writes it)
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(stp), "r"(SB) : "memory");
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_release();
+  const int64_t xch = rank == 0 ? int64_t(h) * KD : int64_t(p.H) * KD + int64_t(h) * KD;
+  const int64_t vch = 2 * int64_t(p.H) * KD + int64_t(hv) * VD;
+  // the shifted conv state of warp 0's or warp 1's channels, stored after the exchange barrier
+  uint2 cst[1][4];
+  if (warp == 0) {
+    float y[4];
+    const int64_t cs[1] = {xch + lane * 4};
+    conv_groups<TIO, 1, false>(p, n, tok, cs, y, cst);
+    *reinterpret_cast<float4 *>(&sx[lane * 4]) = make_float4(y[0], y[1], y[2], y[3]);
+  } else if (warp == 1) {
+    // v of value head hv, and its gates
+    float vv[4];
+    const int64_t cs[1] = {vch + lane * 4};
+    conv_groups<TIO, 1, false>(p, n, tok, cs, vv, cst);
+    *reinterpret_cast<float4 *>(sv + lane * 4) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+    if (lane == 0) {
+      const float av = to_f(static_cast<const TIO *>(p.a)[tok * p.ab_ts + hv]);
+      const float bv = to_f(static_cast<const TIO *>(p.b)[tok * p.ab_ts + hv]);
+      const float gl = -expf(p.A_log[hv]) * softplus20(av + (p.dt_bias ? p.dt_bias[hv] : 0.f));
+      s_decay = expf(gl);
+      s_beta = round_to<TIO>(sigmoidf_(bv));
+    }
+  }
+  cluster.sync();   // q and k of the k-head written by the two CTAs
+  if (warp == 2) {
+    // four copies (32 rows each) on one barrier, so the copy engine works on them in parallel.
+    // They go out once the conv is done: issued first, they queue the conv's small loads behind
+    // 64 KB of state per CTA (24 layers at B=64: 1,415 us against 1,291 us this way).
+    if (lane == 0) mbar_arrive_expect_tx(bar, SB);
+    __syncwarp();
+    if (lane < 4) bulk_load(st + lane * (KD / 4) * COLS, stp + lane * (KD / 4) * COLS, SB / 4, bar);
+  }
+  if (warp < 2) conv_state_store<TIO>(p, n, (warp == 0 ? xch : vch) + lane * 4, cst[0]);
+  if (warp == 0) {
+    // q and k: L2 norm, q scale, and q.k
+    const float *xq = rank == 0 ? sx : cluster.map_shared_rank(sx, 0);
+    const float *xk = rank == 1 ? sx : cluster.map_shared_rank(sx, 1);
+    const float4 q4 = *reinterpret_cast<const float4 *>(xq + lane * 4);
+    const float4 k4 = *reinterpret_cast<const float4 *>(xk + lane * 4);
+    float qv[4] = {q4.x, q4.y, q4.z, q4.w}, kv[4] = {k4.x, k4.y, k4.z, k4.w};
+    float qs2 = qv[0] * qv[0] + qv[1] * qv[1] + qv[2] * qv[2] + qv[3] * qv[3];
+    float ks2 = kv[0] * kv[0] + kv[1] * kv[1] + kv[2] * kv[2] + kv[3] * kv[3];
+    const float qn = rsqrtf(warp_sum(qs2) + 1e-6f), kn = rsqrtf(warp_sum(ks2) + 1e-6f);
+    float dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      qv[j] *= qn * p.scale;
+      kv[j] *= kn;
+      dot += qv[j] * kv[j];
+    }
+    dot = warp_sum(dot);
+    *reinterpret_cast<float4 *>(sq + lane * 4) = make_float4(qv[0], qv[1], qv[2], qv[3]);
+    *reinterpret_cast<float4 *>(sk + lane * 4) = make_float4(kv[0], kv[1], kv[2], kv[3]);
+    if (lane == 0) s_kq = dot;
+  }
+  __syncthreads();
+  // this CTA is done reading the peer's buffer (the matching wait comes at exit, so neither CTA's
+  // shared memory goes away while the other reads it)
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+  bool ok = mbar_wait(bar, 0, abort_flag, ERR_WAIT_STATE);
+  ok = !__syncthreads_or(!ok);
+  const float dec = s_decay, bet = s_beta, kq = s_kq;
+  if (ok) {
+    float ak[4] = {0.f, 0.f, 0.f, 0.f}, aq[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) {
+      float x[4];
+      lds_state4(st + (rg * RPT + i) * COLS + c0, x);
+      const float kr = sk[rg * RPT + i], qr = sq[rg * RPT + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        x[j] *= dec;
+        ak[j] = fmaf(x[j], kr, ak[j]);
+        aq[j] = fmaf(x[j], qr, aq[j]);
+      }
+    }
+    *reinterpret_cast<float4 *>(&red_k[rg][c0]) = make_float4(ak[0], ak[1], ak[2], ak[3]);
+    *reinterpret_cast<float4 *>(&red_q[rg][c0]) = make_float4(aq[0], aq[1], aq[2], aq[3]);
+  }
+  __syncthreads();
+  if (ok) {
+    float kvs[4] = {0.f, 0.f, 0.f, 0.f}, qss[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int r = 0; r < RG; ++r) {
+      const float4 x = *reinterpret_cast<const float4 *>(&red_k[r][c0]);
+      const float4 y = *reinterpret_cast<const float4 *>(&red_q[r][c0]);
+      kvs[0] += x.x; kvs[1] += x.y; kvs[2] += x.z; kvs[3] += x.w;
+      qss[0] += y.x; qss[1] += y.y; qss[2] += y.z; qss[3] += y.w;
+    }
+    float delta[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) delta[j] = bet * (sv[c0 + j] - kvs[j]);
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) {
+      float x[4];
+      lds_state4(st + (rg * RPT + i) * COLS + c0, x);
+      const float kr = sk[rg * RPT + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        x[j] *= dec;
+        x[j] = fmaf(kr, delta[j], x[j]);
+      }
+      st4s(stp + (rg * RPT + i) * COLS + c0, x);
+    }
+    if (rg == 0) {
+      float ov[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) ov[j] = fmaf(delta[j], kq, qss[j]);
+      *reinterpret_cast<float4 *>(&so[c0]) = make_float4(ov[0], ov[1], ov[2], ov[3]);
+    }
+  }
+  __syncthreads();
+  // ---- gated RMSNorm of the output (Qwen3_5RMSNormGated, io-dtype roundings) ----
+  if (ok && warp == 0) {
+    float ov[4];
+    const float4 x = *reinterpret_cast<const float4 *>(&so[lane * 4]);
+    ov[0] = x.x; ov[1] = x.y; ov[2] = x.z; ov[3] = x.w;
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      ov[j] = round_to<TIO>(ov[j]);
+      ss += ov[j] * ov[j];
+    }
+    const float inv = rsqrtf(warp_sum(ss) / float(VD) + p.norm_eps);
+    float zz[4], w[4];
+    load4(static_cast<const TIO *>(p.z) + tok * p.z_ts + int64_t(hv) * VD + lane * 4, zz);
+    load4(static_cast<const TIO *>(p.norm_w) + lane * 4, w);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float yv = round_to<TIO>(w[j] * round_to<TIO>(ov[j] * inv));
+      ov[j] = yv * (zz[j] * sigmoidf_(zz[j]));
+    }
+    store4(static_cast<TIO *>(p.o) + (tok * p.HV + hv) * int64_t(VD) + lane * 4, ov);
+  }
+  if (!ok && tid == 0) {
+    // the copies this CTA waited for may still land: wait for them (bounded) before exiting
+    volatile int keep_waiting = 0;
+    mbar_wait(bar, 0, &keep_waiting, ERR_WAIT_STATE);
+  }
+  __syncwarp();   // the aligned barrier below wants every lane of the warp together
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");   // the peer has read this CTA's buffer
+}
+
 int sm_count() {
   static int count[64] = {0};
   int dev = 0;
@@ -591,8 +796,22 @@ int launch_pair(const FusedArgs &a, const FusedParams &p) {
 }
 
 template <typename TIO, typename TS>
+int launch_pair_sst(const FusedArgs &a, const FusedParams &p) {
+  auto kern = gdn_decode_pair_sst_kernel<TIO, TS>;
+  const int smem = int(pair_staged_bytes<TS>()) + 16;   // the staged state, its mbarrier and the abort flag
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess) e = launch_pdl(kern, dim3(unsigned(a.N * a.HV)), dim3(256), size_t(smem), a.stream, p);
+  if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "gdn_decode_pair_sst_kernel: %s", cudaGetErrorString(e));
+  return check_launch("gdn_decode_pair_sst_kernel");
+}
+
+template <typename TIO, typename TS>
 int launch_ts(const FusedArgs &a, const FusedParams &p) {
-  if (a.HV == 2 * a.H) return launch_pair<TIO, TS>(a, p);   // two value heads per k-head: paired CTAs
+  if (a.HV == 2 * a.H) {   // two value heads per k-head: paired CTAs
+    // one token with the row-major state: staged in shared memory while the conv runs
+    if (!a.trans && a.T == 1 && (reinterpret_cast<uintptr_t>(a.state) & 15u) == 0) return launch_pair_sst<TIO, TS>(a, p);
+    return launch_pair<TIO, TS>(a, p);
+  }
   switch (a.HV / a.H) {   // 256 threads per value head: at most 512 per CTA keeps the state in registers
     case 1: return launch_r<TIO, TS, 1>(a, p);
     case 2: return launch_r<TIO, TS, 2>(a, p);
