@@ -9,7 +9,8 @@ batch on this GPU (weak scaling: every rank owns its own sequences):
     fp32 state 32 x 128 x 128 per sequence updated in place, gated RMSNorm
     epilogue) — ``fused_recurrent_gated_delta_rule``
   * 8 anchor-memory layers: decode read + commit (G=4, H=16, D=256,
-    CAP=64, chunk=64) — ``committed_gqa`` / ``commit_decode``
+    CAP=64, chunk=64) — ``committed_gqa`` then ``commit_decode``, in one
+    launch (``memory_decode_step``)
   * greedy sampling over the 248,320-token vocabulary — ``greedy``
 
 ``value`` is whole-job decode tokens/s (N x batch / step time) with inputs
@@ -216,17 +217,16 @@ def decode_step(yb, layers, mems, x, active, ws, table, fused=False):
             output_final_state=True, use_qk_l2norm_in_kernel=True, use_gate_in_kernel=True, A_log=L['A_log'],
             dt_bias=L['dt_bias'], use_beta_sigmoid_in_kernel=True, z=x['z'][i], norm_weight=L['norm_w'],
             inplace=True)
-    for i, st in enumerate(mems):
-        yb.committed_gqa(x['mq'][i], st)
-        yb.commit_decode(x['mk'][i], x['mv'][i], x['ms'][i], active, MEM_CHUNK, st)
+    for i, st in enumerate(mems):   # committed_gqa then commit_decode, in one launch
+        yb.memory_decode_step(x['mq'][i], x['mk'][i], x['mv'][i], x['ms'][i], active, MEM_CHUNK, st)
     tok = yb.greedy(x['logits'], workspace=ws)
     yb.update_fixed_decode_state_(tok, *(table[k] for k in TABLE_FIELDS), maximum_new_tokens=GEN_TOKENS,
                                   pad_token_id=PAD_ID, eos_token_ids=EOS_IDS)
     return tok
 
 
-# conv + recurrence per GDN layer, read + commit per memory layer, greedy (2), bookkeeping (1)
-LAUNCHES_PER_STEP = 2 * L_GDN + 2 * L_MEM + 3
+# conv + recurrence per GDN layer, read + commit (one launch) per memory layer, greedy (2), bookkeeping (1)
+LAUNCHES_PER_STEP = 2 * L_GDN + L_MEM + 3
 
 
 def gdn_bytes_per_launch(B, state_bytes=4):

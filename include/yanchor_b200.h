@@ -250,6 +250,28 @@ int yb_mem_decode_commit(const void *key, const void *value, const float *scores
                          void *stream);
 
 /*
+ * Anchor memory, one decode step of a memory layer: yb_mem_decode_read, then
+ * yb_mem_decode_commit on the same state, in one launch where the read takes
+ * its tensor-core path (16-bit, CAP <= 64): the last of each row's G CTAs to
+ * finish reading commits the row, so every read sees the bank from before
+ * this step's commit, as with the two calls in that order.  Otherwise it
+ * makes those two calls.  Results are identical to the two calls.
+ * The sequence of runtime/model/independent_memory.py:177 `committed_gqa`
+ * then :190 `commit_decode` in the reference's decode layer
+ * (modeling_yanchor.py:283-312).
+ *   Arguments as in the two calls (one indices array serves both), plus
+ *   arrive: B int32 counters, zero before the first call, left zero by every
+ *   call.  Calls that overlap on the GPU must not share them.
+ */
+int yb_mem_decode_step(const void *query, void *out, const void *key, const void *value, const float *scores,
+                       const uint8_t *active, int64_t chunk, void *keys, void *values, float *bank_scores,
+                       int32_t *positions, void *pending_keys, void *pending_values, float *pending_scores,
+                       int64_t *count, int64_t *total, const int64_t *indices, int32_t *arrive, int64_t B,
+                       int64_t H, int64_t G, int64_t CAP, int64_t PC, int64_t D, int64_t kv_stride0,
+                       int64_t meta_stride0, int64_t pkv_stride0, int64_t pmeta_stride0, int64_t count_stride0,
+                       int dtype, void *stream);
+
+/*
  * Anchor memory, prefill read: each block's queries attend to their group's
  * referenced rows plus the null slot.
  * Replaces runtime/model/independent_memory.py:38 `indexed_gqa`

@@ -107,6 +107,38 @@ def test_decode_strided_pool_view(yb):
         np.testing.assert_array_equal(host(getattr(st, f)), st_np[f].astype(host(getattr(st, f)).dtype))
 
 
+@pytest.mark.parametrize('R,D,pool', [(4, 256, False), (2, 128, True)])
+def test_memory_decode_step_matches_read_then_commit(yb, R, D, pool):
+    """The one-launch decode step of a memory layer against committed_gqa
+    then commit_decode on a copy of the same state, bit for bit, over 170
+    steps (two commits at chunk 64 for rows active in 128 of them, the second
+    merging a full bank with a full chunk): tied scores, inactive rows, and (pool)
+    requests mapped into a larger slot pool with one skipped request."""
+    rng = np.random.default_rng(90 + D)
+    B, G, CAP, chunk = 6, 4, 64, 64
+    H = G * R
+    bf = torch.bfloat16
+    rows = 9 if pool else B
+    idx = cuda(np.array([3, 0, -1, 8, 5, 1], np.int64)) if pool else None
+    st_a = yb.MemoryState.empty(rows, G, CAP, chunk, D, 'cuda', bf)
+    st_b = yb.MemoryState.empty(rows, G, CAP, chunk, D, 'cuda', bf)
+    for t in range(170):
+        q = cuda(rng.standard_normal((B, 1, H, D)), bf)
+        k = cuda(rng.standard_normal((B, 1, G, D)), bf)
+        v = cuda(rng.standard_normal((B, 1, G, D)), bf)
+        sc = cuda(np.round(rng.standard_normal((B, 1, G)) * 2).astype(np.float32) / 2)   # ties
+        act = cuda(rng.random(B) > 0.15)
+        out_a = yb.memory_decode_step(q, k, v, sc, act, chunk, st_a, indices=idx)
+        out_b = yb.committed_gqa(q, st_b, indices=idx)
+        yb.commit_decode(k, v, sc, act, chunk, st_b, indices=idx)
+        assert torch.equal(out_a, out_b), f'read @ {t}'
+        if t in (62, 63, 64, 127, 150, 169):
+            for f in FIELDS:
+                assert torch.equal(getattr(st_a, f), getattr(st_b, f)), f'{f} @ {t}'
+    assert int(st_a.positions.max()) >= 64   # the bank holds rows from the second chunk
+    assert yb.lib().yb_device_error(1) == 0
+
+
 def test_indexed_read_golden(yb, golden):
     d = golden('memory')
     out = yb.indexed_gqa(cuda(d['idx_q']), cuda(d['idx_k']), cuda(d['idx_v']), cuda(d['idx_refs']))

@@ -7,7 +7,8 @@ Operators (all CUDA, via the C ABI library libyanchor_b200.so):
   short convolution before it: ``causal_conv1d_update`` /
   ``causal_conv1d_fn``
 * anchor memory: ``indexed_gqa`` (prefill read), ``committed_gqa`` (decode
-  read), ``commit_decode`` (decode write), ``select_topk`` / ``merge_topk`` /
+  read), ``commit_decode`` (decode write), ``memory_decode_step`` (the read
+  and the write of one decode step in one launch), ``select_topk`` / ``merge_topk`` /
   ``exclusive_prefix_topk`` (top-CAP selection) and ``sequence`` (the
   prefill read / write orchestration)
 * sliding-window attention decode over the physical ring:
@@ -25,6 +26,7 @@ from .conv import causal_conv1d_fn, causal_conv1d_update  # noqa: F401
 from .swa import (flash_swa, initialize_physical_ring, layer_ring_update, physical_ring_decode_attention,  # noqa: F401
                   physical_ring_update_, reference_swa)
 from .independent_memory import MemoryState, commit_decode, committed_gqa, indexed_gqa  # noqa: F401
+from .independent_memory import decode_step as memory_decode_step  # noqa: F401
 from .memory_prefill import exclusive_prefix_topk, merge_topk, select_topk, sequence  # noqa: F401
 from .sampling import apply_dense_presence_penalty_, greedy, sample_top_k_top_p_counter  # noqa: F401
 from .decode_loop import (FixedMemoryDecodeGraph, resolve_recurrent_state_storage,  # noqa: F401

@@ -42,6 +42,8 @@ SIGNATURES = {
     'yb_mem_decode_read': (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I, _P]),
     'yb_mem_decode_commit': (_I, [_P, _P, _P, _P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64,
                                   _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I, _P]),
+    'yb_mem_decode_step': (_I, [_P, _P, _P, _P, _P, _P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64,
+                                _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I, _P]),
     'yb_mem_indexed_read': (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I, _P]),
     'yb_mem_indexed_read_timeline': (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
                                           _I64, _P, _P, _P, _I, _P]),

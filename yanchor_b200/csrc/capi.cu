@@ -180,6 +180,34 @@ int yb_mem_decode_commit(const void *key, const void *value, const float *scores
   return launch_mem_decode_commit(a);
 }
 
+int yb_mem_decode_step(const void *query, void *out, const void *key, const void *value, const float *scores,
+                       const uint8_t *active, int64_t chunk, void *keys, void *values, float *bank_scores,
+                       int32_t *positions, void *pending_keys, void *pending_values, float *pending_scores,
+                       int64_t *count, int64_t *total, const int64_t *indices, int32_t *arrive, int64_t B,
+                       int64_t H, int64_t G, int64_t CAP, int64_t PC, int64_t D, int64_t kv_stride0,
+                       int64_t meta_stride0, int64_t pkv_stride0, int64_t pmeta_stride0, int64_t count_stride0,
+                       int dtype, void *stream) {
+  YB_REQUIRE(dtype_ok(dtype), "mem_decode_step: bad dtype");
+  YB_REQUIRE(B >= 0 && H > 0 && G > 0 && CAP > 0 && PC > 0 && D > 0 && H % G == 0, "mem_decode_step: bad sizes");
+  YB_REQUIRE(chunk >= 1 && chunk <= PC, "mem_decode_step: chunk=%lld must be in [1, PC=%lld]", (long long)chunk,
+             (long long)PC);
+  YB_REQUIRE(query && out && key && value && scores && active && keys && values && bank_scores && positions &&
+                 pending_keys && pending_values && pending_scores && count && total && arrive,
+             "mem_decode_step: null tensor");
+  YB_REQUIRE(kv_stride0 >= G * CAP * D && meta_stride0 >= G * CAP && pkv_stride0 >= G * PC * D &&
+                 pmeta_stride0 >= G * PC && count_stride0 >= 1,
+             "mem_decode_step: batch stride too small");
+  YB_REQUIRE((kv_stride0 * dtype_size(dtype)) % 16 == 0, "mem_decode_step: key batch stride must be 16-byte multiple");
+  YB_REQUIRE(aligned(query, 16) && aligned(keys, 16) && aligned(values, 16) && aligned(out, 16),
+             "mem_decode_step: tensors must be 16-byte aligned");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  MemReadArgs r{query, keys, values, positions, indices, out, B, H, G, CAP, D, kv_stride0, meta_stride0, dtype, st};
+  MemCommitArgs c{key, value, scores, active, chunk, keys, values, bank_scores, positions, pending_keys,
+                  pending_values, pending_scores, count, total, indices, B, G, CAP, PC, D, kv_stride0,
+                  meta_stride0, pkv_stride0, pmeta_stride0, count_stride0, dtype, st};
+  return launch_mem_decode_step(r, c, arrive);
+}
+
 int yb_mem_indexed_read(const void *query, const void *key, const void *value, const int64_t *references, void *out,
                         int64_t B, int64_t blocks, int64_t chunk, int64_t H, int64_t G, int64_t D, int64_t S,
                         int64_t KB, int64_t CAP, int dtype, void *stream) {

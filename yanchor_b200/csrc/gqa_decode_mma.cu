@@ -15,6 +15,7 @@
 // ldmatrix.trans, B = P) gives each warp a quarter of the D columns.
 #include "common.cuh"
 #include "kernels.h"
+#include "mem_commit.cuh"
 
 namespace yb {
 
@@ -62,8 +63,8 @@ __device__ __forceinline__ void cp16(void *dst, const void *src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
 }
 
-template <typename T, int R, int D>
-__global__ void __launch_bounds__(kGqaThreads) gqa_decode_mma_kernel(const GqaDecodeArgs a) {
+template <typename T, int R, int D, bool COMMIT>
+__global__ void __launch_bounds__(kGqaThreads) gqa_decode_mma_kernel(const GqaDecodeArgs a, const MemCommitTail ct) {
   static_assert(R <= 8 && D % 64 == 0, "R <= 8 heads, D a multiple of 64");
   constexpr int ROW = D + 8;          // padded K / V / Q row (elements)
   constexpr int PROW = kGqaSlice + 8; // padded P row
@@ -242,38 +243,67 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_decode_mma_kernel(const GqaDe
           o[h * D + d] = from_f<T>(l > 0.f ? acc[t][j] / l : 0.f);
         }
       }
+    if constexpr (COMMIT) {
+      // This group's commit (push, and the merge when the chunk fills), right after its read: the
+      // group's bank is read by this CTA alone, so every read of the step still sees the bank
+      // from before the commit, as with a read launch followed by a commit launch.  The last of
+      // the row's G CTAs to finish updates count / total, which all of them read first; its
+      // arrival counter goes back to 0 for the next call.  The commit's buffers reuse the K / V
+      // rows, which every warp is done with after the first barrier.
+      const MemCommitArgs &c = ct.c;
+      if (c.active[b]) {   // the same for the row's G CTAs
+        const int64_t count = c.count[s * c.count_s0];
+        const int64_t total = c.total[s * c.count_s0];
+        float *c_score = reinterpret_cast<float *>(sv);
+        int64_t *c_pkey = reinterpret_cast<int64_t *>(c_score + memcommit::kMaxCand);
+        int *sel = reinterpret_cast<int *>(c_pkey + memcommit::kMaxCand);
+        __syncthreads();
+        memcommit::commit_group<T>(c, b, s, int(g), count, total, c_score, c_pkey, sel, sk);
+        __syncthreads();
+        if (tid == 0) {
+          __threadfence();
+          if (atomicAdd(ct.arrive + b, 1) == int(a.G) - 1) {
+            ct.arrive[b] = 0;
+            c.count[s * c.count_s0] = count + 1 == c.chunk ? 0 : count + 1;
+            c.total[s * c.count_s0] = total + 1;
+          }
+        }
+      }
+    }
   }
 }
 
-template <typename T, int R, int D>
-int launch_gqa(const GqaDecodeArgs &a, unsigned slices) {
+template <typename T, int R, int D, bool COMMIT>
+int launch_gqa(const GqaDecodeArgs &a, const MemCommitTail &ct, unsigned slices) {
   constexpr int ROW = D + 8, PROW = kGqaSlice + 8;
+  static_assert(kGqaSlice * ROW * sizeof(T) >= (sizeof(float) + sizeof(int64_t) + sizeof(int)) * memcommit::kMaxCand,
+                "the commit's candidate arrays fit in the V rows");
   const size_t smem = sizeof(T) * (2 * kGqaSlice * ROW + 8 * ROW + 2 * 8 * PROW) + sizeof(float) * (64 + 16);
-  auto k = gqa_decode_mma_kernel<T, R, D>;
+  auto k = gqa_decode_mma_kernel<T, R, D, COMMIT>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "gqa decode: smem attribute: %s", cudaGetErrorString(e));
-  e = launch_pdl(k, dim3(unsigned(a.B * a.G), slices), dim3(kGqaThreads), smem, a.stream, a);
+  e = launch_pdl(k, dim3(unsigned(a.B * a.G), slices), dim3(kGqaThreads), smem, a.stream, a, ct);
   if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "gqa decode: %s", cudaGetErrorString(e));
   return check_launch("gqa_decode_mma_kernel");
 }
 
-template <typename T, int R>
-int gqa_d(const GqaDecodeArgs &a, unsigned slices) {
+template <typename T, int R, bool COMMIT>
+int gqa_d(const GqaDecodeArgs &a, const MemCommitTail &ct, unsigned slices) {
   switch (a.D) {
-    case 64: return launch_gqa<T, R, 64>(a, slices);
-    case 128: return launch_gqa<T, R, 128>(a, slices);
-    case 256: return launch_gqa<T, R, 256>(a, slices);
+    case 64: return launch_gqa<T, R, 64, COMMIT>(a, ct, slices);
+    case 128: return launch_gqa<T, R, 128, COMMIT>(a, ct, slices);
+    case 256: return launch_gqa<T, R, 256, COMMIT>(a, ct, slices);
   }
   return -1;
 }
 
-template <typename T>
-int gqa_r(const GqaDecodeArgs &a, unsigned slices) {
+template <typename T, bool COMMIT>
+int gqa_r(const GqaDecodeArgs &a, const MemCommitTail &ct, unsigned slices) {
   switch (a.QH / a.G) {
-    case 1: return gqa_d<T, 1>(a, slices);
-    case 2: return gqa_d<T, 2>(a, slices);
-    case 4: return gqa_d<T, 4>(a, slices);
-    case 8: return gqa_d<T, 8>(a, slices);
+    case 1: return gqa_d<T, 1, COMMIT>(a, ct, slices);
+    case 2: return gqa_d<T, 2, COMMIT>(a, ct, slices);
+    case 4: return gqa_d<T, 4, COMMIT>(a, ct, slices);
+    case 8: return gqa_d<T, 8, COMMIT>(a, ct, slices);
   }
   return -1;
 }
@@ -290,8 +320,20 @@ int launch_gqa_decode_mma(const GqaDecodeArgs &a) {
   if (a.B * a.G == 0) return YB_OK;
   const unsigned slices = unsigned((a.P + kGqaSlice - 1) / kGqaSlice);
   if (!a.partial && slices != 1) return set_error(YB_ERR_UNSUPPORTED, "gqa decode: a direct read covers <= 64 slots");
-  const int rc = a.dtype == YB_BF16 ? gqa_r<__nv_bfloat16>(a, slices) : gqa_r<__half>(a, slices);
+  const MemCommitTail none{};
+  const int rc = a.dtype == YB_BF16 ? gqa_r<__nv_bfloat16, false>(a, none, slices) : gqa_r<__half, false>(a, none, slices);
   if (rc < 0) return set_error(YB_ERR_UNSUPPORTED, "gqa decode: shape not built");
+  return rc;
+}
+
+int launch_gqa_decode_commit(const GqaDecodeArgs &a, const MemCommitArgs &c, int32_t *arrive) {
+  if (a.B * a.G == 0) return YB_OK;
+  if (a.partial || a.P > kGqaSlice || a.B != c.B || a.G != c.G || a.indices != c.indices || !arrive ||
+      c.CAP + c.chunk > memcommit::kMaxCand || c.CAP != a.P || c.D != a.D || c.dtype != a.dtype)
+    return set_error(YB_ERR_UNSUPPORTED, "gqa decode + commit: arguments do not describe one memory layer");
+  const MemCommitTail ct{c, arrive};
+  const int rc = a.dtype == YB_BF16 ? gqa_r<__nv_bfloat16, true>(a, ct, 1) : gqa_r<__half, true>(a, ct, 1);
+  if (rc < 0) return set_error(YB_ERR_UNSUPPORTED, "gqa decode + commit: shape not built");
   return rc;
 }
 

@@ -68,6 +68,8 @@ struct MemCommitArgs {
   cudaStream_t stream;
 };
 int launch_mem_decode_commit(const MemCommitArgs &a);
+// read then commit of one memory layer: one launch on the tensor-core read path, else two
+int launch_mem_decode_step(const MemReadArgs &r, const MemCommitArgs &c, int32_t *arrive);
 
 struct MemIndexedArgs {
   const void *query, *key, *value;
@@ -178,6 +180,13 @@ struct GqaDecodeArgs {
 };
 bool gqa_decode_mma_supported(int dtype, int64_t QH, int64_t G, int64_t D);
 int launch_gqa_decode_mma(const GqaDecodeArgs &a);
+// A direct memory read followed, in the same launch, by the commit of each row (done by the last
+// of the row's G CTAs; `arrive` holds B zeroed counters, left zeroed).
+struct MemCommitTail {
+  MemCommitArgs c;
+  int32_t *arrive;
+};
+int launch_gqa_decode_commit(const GqaDecodeArgs &a, const MemCommitArgs &c, int32_t *arrive);
 
 // Decode-loop bookkeeping after a sampled token (one launch per step).
 constexpr int kMaxEos = 8;

@@ -1,0 +1,176 @@
+// Anchor-memory decode commit of one request row, shared by the commit kernel
+// (memory.cu) and the read kernel's commit tail (gqa_decode_mma.cu)
+// (runtime/model/independent_memory.py:190 `commit_decode`,
+// modeling_yanchor.py:186-216 `_commit`, :229-251 `select_topk`).
+//
+// Push (key, value, score) of every group into pending slot `count`; when the
+// chunk fills, merge the CAP bank slots and the `chunk` pending slots of each
+// group into the new top-CAP bank.  Groups are independent: commit_group does
+// one, so the read kernel's tail commits each group in its own CTA.  Order:
+// score descending, then position ascending (invalid last), then candidate
+// index — the stable double argsort of select_topk.  Invalid winners get position -1 and copy bank slot 0, as
+// the reference's gather with references clamped at 0 does.  Every thread of
+// the CTA calls it; loops stride by the CTA's thread count.
+#pragma once
+#include "common.cuh"
+#include "kernels.h"
+
+namespace yb {
+namespace memcommit {
+
+constexpr int kMaxCand = 512;
+
+__device__ __forceinline__ bool cand_before(float sa, int64_t pa, int ia, float sb, int64_t pb, int ib) {
+  if (sa != sb) return sa > sb;  // -0.0 == 0.0, as in a float sort
+  if (pa != pb) return pa < pb;
+  return ia < ib;
+}
+
+template <typename T>
+__device__ void commit_gather(T *bank, const T *pend, T *stage, const int *sel, const int64_t *pkey, int g,
+                              int CAP, int PC, int D) {
+  const int tid = threadIdx.x, nt = blockDim.x;
+  constexpr int VEC = 16 / int(sizeof(T));
+  const bool vec = (D % VEC) == 0 && (reinterpret_cast<uintptr_t>(bank) % 16) == 0 &&
+                   (reinterpret_cast<uintptr_t>(pend) % 16) == 0;
+  if (vec) {   // 16-byte pieces of the winning rows
+    const int DV = D / VEC;
+    for (int e = tid; e < CAP * DV; e += nt) {
+      const int r = e / DV, d = (e % DV) * VEC;
+      const int c = sel[r];
+      const int src = pkey[c] == INT64_MAX ? 0 : c;
+      const T *from = src < CAP ? bank + (int64_t(g) * CAP + src) * D : pend + (int64_t(g) * PC + src - CAP) * D;
+      *reinterpret_cast<uint4 *>(stage + r * D + d) = *reinterpret_cast<const uint4 *>(from + d);
+    }
+    __syncthreads();
+    for (int e = tid; e < CAP * DV; e += nt)
+      *reinterpret_cast<uint4 *>(bank + int64_t(g) * CAP * D + e * VEC) = *reinterpret_cast<const uint4 *>(stage + e * VEC);
+    __syncthreads();
+    return;
+  }
+  for (int e = tid; e < CAP * D; e += nt) {
+    const int r = e / D, d = e % D;
+    const int c = sel[r];
+    const int src = pkey[c] == INT64_MAX ? 0 : c;
+    stage[e] = src < CAP ? bank[(int64_t(g) * CAP + src) * D + d] : pend[(int64_t(g) * PC + src - CAP) * D + d];
+  }
+  __syncthreads();
+  for (int e = tid; e < CAP * D; e += nt) bank[int64_t(g) * CAP * D + e] = stage[e];
+  __syncthreads();
+}
+
+// Group g of request row `row` (state row s, active): push into pending slot `count` (unless
+// PUSH is false: the caller pushed every group already), and merge when the chunk fills.
+// count / total are read by the caller and not updated here.
+// c_score, c_pkey, sel: kMaxCand entries each; stage: CAP * D elements (all shared memory).
+template <typename T, bool PUSH = true>
+__device__ void commit_group(const MemCommitArgs &a, int64_t row, int64_t s, int g, int64_t count, int64_t total,
+                             float *c_score, int64_t *c_pkey, int *sel, T *stage) {
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const int CAP = int(a.CAP), D = int(a.D), chunk = int(a.chunk), G = int(a.G), PC = int(a.PC);
+  const bool commit = count + 1 == chunk;
+  const T *key = static_cast<const T *>(a.key) + (row * G + g) * D;
+  const T *val = static_cast<const T *>(a.value) + (row * G + g) * D;
+  T *bank_k = static_cast<T *>(a.keys) + s * a.kv_s0;
+  T *bank_v = static_cast<T *>(a.values) + s * a.kv_s0;
+  T *pend_k = static_cast<T *>(a.pkeys) + s * a.pkv_s0;
+  T *pend_v = static_cast<T *>(a.pvalues) + s * a.pkv_s0;
+  float *bscore = a.bank_scores + s * a.meta_s0;
+  int32_t *bpos = a.positions + s * a.meta_s0;
+  float *pscore = a.pscores + s * a.pmeta_s0;
+
+  if constexpr (PUSH) {
+    // push into pending slot `count` (16-byte pieces when every row start is aligned)
+    T *pk = pend_k + (int64_t(g) * PC + count) * D, *pv = pend_v + (int64_t(g) * PC + count) * D;
+    constexpr int VEC = 16 / int(sizeof(T));
+    const bool vec = (D % VEC) == 0 && (reinterpret_cast<uintptr_t>(key) % 16) == 0 &&
+                     (reinterpret_cast<uintptr_t>(val) % 16) == 0 && (reinterpret_cast<uintptr_t>(pk) % 16) == 0 &&
+                     (reinterpret_cast<uintptr_t>(pv) % 16) == 0;
+    if (vec) {
+      for (int e = tid * VEC; e < D; e += nt * VEC) {
+        *reinterpret_cast<uint4 *>(pk + e) = *reinterpret_cast<const uint4 *>(key + e);
+        *reinterpret_cast<uint4 *>(pv + e) = *reinterpret_cast<const uint4 *>(val + e);
+      }
+    } else {
+      for (int e = tid; e < D; e += nt) {
+        pk[e] = key[e];
+        pv[e] = val[e];
+      }
+    }
+    if (tid == 0) pscore[int64_t(g) * PC + count] = a.scores[row * G + g];
+  }
+  if (!commit) return;
+  const int n = CAP + chunk;
+  __syncthreads();  // the push is visible; the previous group's use of the candidate arrays is over
+  for (int c = tid; c < n; c += nt) {
+    if (c < CAP) {
+      const int32_t pos = bpos[int64_t(g) * CAP + c];
+      c_score[c] = bscore[int64_t(g) * CAP + c];
+      c_pkey[c] = pos < 0 ? INT64_MAX : int64_t(pos);
+    } else {
+      const int i = c - CAP;  // every pending slot is filled when committing
+      c_score[c] = pscore[int64_t(g) * PC + i];
+      c_pkey[c] = total - count + i;
+    }
+  }
+  __syncthreads();
+  for (int c = tid; c < n; c += nt) {
+    const float sc = c_score[c];
+    const int64_t pkc = c_pkey[c];
+    int rank = 0;
+    for (int o = 0; o < n; ++o) rank += cand_before(c_score[o], c_pkey[o], o, sc, pkc, c);
+    if (rank < CAP) sel[rank] = c;
+  }
+  __syncthreads();
+  commit_gather(bank_k, pend_k, stage, sel, c_pkey, g, CAP, PC, D);
+  commit_gather(bank_v, pend_v, stage, sel, c_pkey, g, CAP, PC, D);
+  for (int r = tid; r < CAP; r += nt) {
+    const int c = sel[r];
+    bscore[int64_t(g) * CAP + r] = c_score[c];
+    bpos[int64_t(g) * CAP + r] = c_pkey[c] == INT64_MAX ? -1 : int32_t(c_pkey[c]);
+  }
+}
+
+// the whole row, every group in turn, then its count / total
+template <typename T>
+__device__ void commit_row(const MemCommitArgs &a, int64_t row, float *c_score, int64_t *c_pkey, int *sel,
+                           T *stage) {
+  const int64_t s = a.indices ? a.indices[row] : row;
+  if (s < 0 || !a.active[row]) return;
+  const int64_t count = a.count[s * a.count_s0];
+  const int64_t total = a.total[s * a.count_s0];
+  // push every group into pending slot `count` at once (16-byte pieces when every row start is aligned)
+  const int tid = threadIdx.x, nt = blockDim.x, G = int(a.G), D = int(a.D), PC = int(a.PC);
+  const T *key = static_cast<const T *>(a.key) + row * G * D;
+  const T *val = static_cast<const T *>(a.value) + row * G * D;
+  T *pend_k = static_cast<T *>(a.pkeys) + s * a.pkv_s0;
+  T *pend_v = static_cast<T *>(a.pvalues) + s * a.pkv_s0;
+  constexpr int VEC = 16 / int(sizeof(T));
+  const bool vec = (D % VEC) == 0 && (reinterpret_cast<uintptr_t>(key) % 16) == 0 &&
+                   (reinterpret_cast<uintptr_t>(val) % 16) == 0 && (reinterpret_cast<uintptr_t>(pend_k) % 16) == 0 &&
+                   (reinterpret_cast<uintptr_t>(pend_v) % 16) == 0;
+  if (vec) {
+    for (int e = tid * VEC; e < G * D; e += nt * VEC) {
+      const int g = e / D, d = e % D;
+      const int64_t dst = (int64_t(g) * PC + count) * D + d;
+      *reinterpret_cast<uint4 *>(pend_k + dst) = *reinterpret_cast<const uint4 *>(key + e);
+      *reinterpret_cast<uint4 *>(pend_v + dst) = *reinterpret_cast<const uint4 *>(val + e);
+    }
+  } else {
+    for (int e = tid; e < G * D; e += nt) {
+      const int g = e / D, d = e % D;
+      pend_k[(int64_t(g) * PC + count) * D + d] = key[e];
+      pend_v[(int64_t(g) * PC + count) * D + d] = val[e];
+    }
+  }
+  if (tid < G) a.pscores[s * a.pmeta_s0 + int64_t(tid) * PC + count] = a.scores[row * G + tid];
+  for (int g = 0; g < G; ++g) commit_group<T, false>(a, row, s, g, count, total, c_score, c_pkey, sel, stage);
+  __syncthreads();  // every thread has read count / total
+  if (threadIdx.x == 0) {
+    a.count[s * a.count_s0] = count + 1 == a.chunk ? 0 : count + 1;
+    a.total[s * a.count_s0] = total + 1;
+  }
+}
+
+}  // namespace memcommit
+}  // namespace yb

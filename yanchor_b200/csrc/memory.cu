@@ -7,6 +7,7 @@
 // the null slot: one extra logit 0 whose value row is zero.
 #include "common.cuh"
 #include "kernels.h"
+#include "mem_commit.cuh"
 
 namespace yb {
 namespace {
@@ -265,36 +266,11 @@ int launch_read_t(const MemReadArgs &a) {
 }
 
 // ---------------------------------------------------------------------------
-// Decode commit: one CTA per request row, looping over groups.
-// Candidates are the CAP bank slots followed by the `chunk` pending slots.
-// Order: score descending, then position ascending (invalid last), then
-// candidate index — the stable double argsort of select_topk.  Invalid
-// winners get position -1 and copy bank slot 0, as the reference's
-// gather with references clamped at 0 does.
+// Decode commit: one CTA per request row (the row's work is
+// memcommit::commit_row, shared with the read kernel's commit tail).
 // ---------------------------------------------------------------------------
 constexpr int kCommitThreads = 256;
-constexpr int kMaxCand = 512;
-
-__device__ __forceinline__ bool cand_before(float sa, int64_t pa, int ia, float sb, int64_t pb, int ib) {
-  if (sa != sb) return sa > sb;  // -0.0 == 0.0, as in a float sort
-  if (pa != pb) return pa < pb;
-  return ia < ib;
-}
-
-template <typename T>
-__device__ void commit_gather(T *bank, const T *pend, T *stage, const int *sel, const int64_t *pkey, int g,
-                              int CAP, int PC, int D) {
-  const int tid = threadIdx.x;
-  for (int e = tid; e < CAP * D; e += kCommitThreads) {
-    const int r = e / D, d = e % D;
-    const int c = sel[r];
-    const int src = pkey[c] == INT64_MAX ? 0 : c;
-    stage[e] = src < CAP ? bank[(int64_t(g) * CAP + src) * D + d] : pend[(int64_t(g) * PC + src - CAP) * D + d];
-  }
-  __syncthreads();
-  for (int e = tid; e < CAP * D; e += kCommitThreads) bank[int64_t(g) * CAP * D + e] = stage[e];
-  __syncthreads();
-}
+constexpr int kMaxCand = memcommit::kMaxCand;
 
 template <typename T>
 __global__ void __launch_bounds__(kCommitThreads) mem_decode_commit_kernel(const MemCommitArgs a) {
@@ -304,84 +280,7 @@ __global__ void __launch_bounds__(kCommitThreads) mem_decode_commit_kernel(const
   __shared__ int64_t c_pkey[kMaxCand];  // position, INT64_MAX for an invalid slot
   __shared__ int sel[kMaxCand];         // new slot -> winning candidate
   extern __shared__ __align__(16) unsigned char cm_raw[];
-  T *stage = reinterpret_cast<T *>(cm_raw);  // [CAP][D]
-  const int tid = threadIdx.x;
-  const int64_t row = blockIdx.x;
-  const int64_t s = a.indices ? a.indices[row] : row;
-  if (s < 0 || !a.active[row]) return;
-  const int CAP = int(a.CAP), D = int(a.D), chunk = int(a.chunk), G = int(a.G), PC = int(a.PC);
-  const int64_t count = a.count[s * a.count_s0];
-  const int64_t total = a.total[s * a.count_s0];
-  const bool commit = count + 1 == chunk;
-  const T *key = static_cast<const T *>(a.key) + row * G * D;
-  const T *val = static_cast<const T *>(a.value) + row * G * D;
-  T *bank_k = static_cast<T *>(a.keys) + s * a.kv_s0;
-  T *bank_v = static_cast<T *>(a.values) + s * a.kv_s0;
-  T *pend_k = static_cast<T *>(a.pkeys) + s * a.pkv_s0;
-  T *pend_v = static_cast<T *>(a.pvalues) + s * a.pkv_s0;
-  float *bscore = a.bank_scores + s * a.meta_s0;
-  int32_t *bpos = a.positions + s * a.meta_s0;
-  float *pscore = a.pscores + s * a.pmeta_s0;
-
-  // push into pending slot `count` (16-byte pieces when every row start is aligned)
-  constexpr int VEC = 16 / int(sizeof(T));
-  const bool vec = (D % VEC) == 0 && (reinterpret_cast<uintptr_t>(key) % 16) == 0 &&
-                   (reinterpret_cast<uintptr_t>(val) % 16) == 0 && (reinterpret_cast<uintptr_t>(pend_k) % 16) == 0 &&
-                   (reinterpret_cast<uintptr_t>(pend_v) % 16) == 0;
-  if (vec) {
-    for (int e = tid * VEC; e < G * D; e += kCommitThreads * VEC) {
-      const int g = e / D, d = e % D;
-      const int64_t dst = (int64_t(g) * PC + count) * D + d;
-      const uint4 kv = *reinterpret_cast<const uint4 *>(key + e), vv = *reinterpret_cast<const uint4 *>(val + e);
-      *reinterpret_cast<uint4 *>(pend_k + dst) = kv;
-      *reinterpret_cast<uint4 *>(pend_v + dst) = vv;
-    }
-  } else {
-    for (int e = tid; e < G * D; e += kCommitThreads) {
-      const int g = e / D, d = e % D;
-      pend_k[(int64_t(g) * PC + count) * D + d] = key[e];
-      pend_v[(int64_t(g) * PC + count) * D + d] = val[e];
-    }
-  }
-  if (tid < G) pscore[int64_t(tid) * PC + count] = a.scores[row * G + tid];
-  if (commit) {
-    const int n = CAP + chunk;
-    for (int g = 0; g < G; ++g) {
-      __syncthreads();  // pushes visible; previous group finished
-      for (int c = tid; c < n; c += kCommitThreads) {
-        if (c < CAP) {
-          const int32_t pos = bpos[int64_t(g) * CAP + c];
-          c_score[c] = bscore[int64_t(g) * CAP + c];
-          c_pkey[c] = pos < 0 ? INT64_MAX : int64_t(pos);
-        } else {
-          const int i = c - CAP;  // every pending slot is filled when committing
-          c_score[c] = pscore[int64_t(g) * PC + i];
-          c_pkey[c] = total - count + i;
-        }
-      }
-      __syncthreads();
-      for (int c = tid; c < n; c += kCommitThreads) {
-        const float sc = c_score[c];
-        const int64_t pk = c_pkey[c];
-        int rank = 0;
-        for (int o = 0; o < n; ++o) rank += cand_before(c_score[o], c_pkey[o], o, sc, pk, c);
-        if (rank < CAP) sel[rank] = c;
-      }
-      __syncthreads();
-      commit_gather(bank_k, pend_k, stage, sel, c_pkey, g, CAP, PC, D);
-      commit_gather(bank_v, pend_v, stage, sel, c_pkey, g, CAP, PC, D);
-      for (int r = tid; r < CAP; r += kCommitThreads) {
-        const int c = sel[r];
-        bscore[int64_t(g) * CAP + r] = c_score[c];
-        bpos[int64_t(g) * CAP + r] = c_pkey[c] == INT64_MAX ? -1 : int32_t(c_pkey[c]);
-      }
-    }
-  }
-  __syncthreads();  // every thread has read count / total
-  if (tid == 0) {
-    a.count[s * a.count_s0] = commit ? 0 : count + 1;
-    a.total[s * a.count_s0] = total + 1;
-  }
+  memcommit::commit_row<T>(a, blockIdx.x, c_score, c_pkey, sel, reinterpret_cast<T *>(cm_raw));
 }
 
 template <typename T>
@@ -565,33 +464,38 @@ int launch_indexed_t(const MemIndexedArgs &a) {
 
 }  // namespace
 
+// a bank of at most 64 slots, 16-bit, aligned: the tensor-core read (one CTA per (row, group))
+static bool mma_read_args(const MemReadArgs &a, GqaDecodeArgs &g) {
+  const auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (!(a.CAP <= 64 && gqa_decode_mma_supported(a.dtype, a.H, a.G, a.D) && a.kv_s0 % 8 == 0 && al16(a.query) &&
+        al16(a.keys) && al16(a.values) && al16(a.out)))
+    return false;
+  g = GqaDecodeArgs{};
+  g.query = a.query;
+  g.keys = a.keys;
+  g.values = a.values;
+  g.kv_bs = a.kv_s0;
+  g.kv_gs = a.CAP * a.D;
+  g.positions = a.positions;
+  g.pos_bs = a.pos_s0;
+  g.pos_gs = a.CAP;
+  g.indices = a.indices;
+  g.out = a.out;
+  g.null_slot = 1;
+  g.B = a.B;
+  g.G = a.G;
+  g.QH = a.H;
+  g.D = a.D;
+  g.P = a.CAP;
+  g.dtype = a.dtype;
+  g.stream = a.stream;
+  return true;
+}
+
 int launch_mem_decode_read(const MemReadArgs &a) {
   if (a.B * a.G == 0) return YB_OK;
-  const auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-  if (a.CAP <= 64 && gqa_decode_mma_supported(a.dtype, a.H, a.G, a.D) && a.kv_s0 % 8 == 0 && al16(a.query) &&
-      al16(a.keys) && al16(a.values) && al16(a.out)) {
-    // a bank of at most 64 slots: one tensor-core CTA per (row, group)
-    GqaDecodeArgs g{};
-    g.query = a.query;
-    g.keys = a.keys;
-    g.values = a.values;
-    g.kv_bs = a.kv_s0;
-    g.kv_gs = a.CAP * a.D;
-    g.positions = a.positions;
-    g.pos_bs = a.pos_s0;
-    g.pos_gs = a.CAP;
-    g.indices = a.indices;
-    g.out = a.out;
-    g.null_slot = 1;
-    g.B = a.B;
-    g.G = a.G;
-    g.QH = a.H;
-    g.D = a.D;
-    g.P = a.CAP;
-    g.dtype = a.dtype;
-    g.stream = a.stream;
-    return launch_gqa_decode_mma(g);
-  }
+  GqaDecodeArgs g;
+  if (mma_read_args(a, g)) return launch_gqa_decode_mma(g);
   switch (a.dtype) {
     case YB_F32: return launch_read_t<float>(a);
     case YB_BF16: return launch_read_t<__nv_bfloat16>(a);
@@ -611,6 +515,14 @@ int launch_mem_decode_commit(const MemCommitArgs &a) {
     case YB_F16: return launch_commit_t<__half>(a);
   }
   return set_error(YB_ERR_ARGUMENT, "memory commit: bad dtype %d", a.dtype);
+}
+
+int launch_mem_decode_step(const MemReadArgs &r, const MemCommitArgs &c, int32_t *arrive) {
+  GqaDecodeArgs g;
+  if (r.B * r.G > 0 && arrive && c.CAP + c.chunk <= kMaxCand && mma_read_args(r, g))
+    return launch_gqa_decode_commit(g, c, arrive);
+  const int rc = launch_mem_decode_read(r);
+  return rc != YB_OK ? rc : launch_mem_decode_commit(c);
 }
 
 int launch_mem_indexed_read(const MemIndexedArgs &a) {

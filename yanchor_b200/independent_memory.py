@@ -8,6 +8,8 @@ Drop-in for ``runtime/model/independent_memory.py`` (the module that
     committed_gqa(query, state, indices=None)             -> read   (decode)
     commit_decode(key, value, scores, active, chunk, state, indices=None)
                                                           -> None   (decode write)
+    decode_step(query, key, value, scores, active, chunk, state, indices=None)
+                                                          -> read   (read + write, one launch)
 
 ``state`` is any object with the fields of ``IndependentMemoryState``
 (``modeling_yanchor.py:80-120``): keys / values ``[B, G, CAP, D]``, scores
@@ -181,6 +183,54 @@ def committed_gqa(query, state, indices=None):
                                        state.keys.stride(0), state.positions.stride(0), dtype_code(query),
                                        stream_ptr(query.device))
     _lib.check(rc, 'committed_gqa')
+    return out
+
+
+_ARRIVE = {}
+
+
+def _arrive(batch, device):
+    """B zeroed int32 counters per device for ``decode_step`` (every call
+    leaves them zero); grown, never shrunk."""
+    t = _ARRIVE.get(device)
+    if t is None or t.numel() < batch:
+        t = _ARRIVE[device] = torch.zeros(max(batch, 64), device=device, dtype=torch.int32)
+    return t
+
+
+def decode_step(query, key, value, scores, active, chunk, state, indices=None):
+    """One decode step of a memory layer: ``committed_gqa(query, state)`` then
+    ``commit_decode(key, value, scores, active, chunk, state)`` — the reference
+    decode layer's order (``modeling_yanchor.py:283-312``) — with identical
+    results, in one launch on the tensor-core read path.  Returns the read.
+    Steps of one device run in stream order: calls that overlap on the GPU
+    share the arrival counters and must not."""
+    require_cuda(query, key, value, scores, active, state.keys)
+    _check_state(state)
+    if state.positions.stride(0) != state.scores.stride(0):
+        out = committed_gqa(query, state, indices)
+        commit_decode(key, value, scores, active, chunk, state, indices)
+        return out
+    query = query.contiguous()
+    key, value = key.contiguous(), value.contiguous()
+    scores = scores.to(torch.float32).contiguous()
+    active = active.to(torch.bool).contiguous()
+    b, _, h, d = query.shape
+    g, cap = state.keys.shape[1:3]
+    pc = state.pending_keys.shape[2]
+    if state.keys.dtype != query.dtype or key.dtype != state.keys.dtype or value.dtype != state.values.dtype:
+        raise TypeError('query, key, value and the memory must share a dtype')
+    idx = _indices(indices, query.device)
+    out = torch.empty_like(query)
+    rc = _lib.lib().yb_mem_decode_step(
+        query.data_ptr(), out.data_ptr(), key.data_ptr(), value.data_ptr(), scores.data_ptr(), active.data_ptr(),
+        int(chunk), state.keys.data_ptr(), state.values.data_ptr(), state.scores.data_ptr(),
+        state.positions.data_ptr(), state.pending_keys.data_ptr(), state.pending_values.data_ptr(),
+        state.pending_scores.data_ptr(), state.count.data_ptr(), state.total.data_ptr(), ptr(idx),
+        _arrive(b, query.device).data_ptr(), b, h, g, cap, pc, d, state.keys.stride(0), state.scores.stride(0),
+        state.pending_keys.stride(0), state.pending_scores.stride(0), state.count.stride(0), dtype_code(query),
+        stream_ptr(query.device))
+    _lib.check(rc, 'decode_step')
     return out
 
 
