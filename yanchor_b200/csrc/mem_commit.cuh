@@ -8,9 +8,10 @@
 // group into the new top-CAP bank.  Groups are independent: commit_group does
 // one, so the read kernel's tail commits each group in its own CTA.  Order:
 // score descending, then position ascending (invalid last), then candidate
-// index — the stable double argsort of select_topk.  Invalid winners get position -1 and copy bank slot 0, as
-// the reference's gather with references clamped at 0 does.  Every thread of
-// the CTA calls it; loops stride by the CTA's thread count.
+// index — the stable double argsort of select_topk.  Invalid winners get
+// position -1 and copy bank slot 0, as the reference's gather with references
+// clamped at 0 does.  Every thread of the CTA calls these; loops stride by the
+// CTA's thread count.
 #pragma once
 #include "common.cuh"
 #include "kernels.h"
