@@ -252,10 +252,13 @@ int yb_mem_decode_commit(const void *key, const void *value, const float *scores
 /*
  * Anchor memory, one decode step of a memory layer: yb_mem_decode_read, then
  * yb_mem_decode_commit on the same state, in one launch where the read takes
- * its tensor-core path (16-bit, CAP <= 64): the last of each row's G CTAs to
- * finish reading commits the row, so every read sees the bank from before
- * this step's commit, as with the two calls in that order.  Otherwise it
- * makes those two calls.  Results are identical to the two calls.
+ * its tensor-core path (16-bit, CAP <= 64): each (row, group) CTA reads its
+ * group and then commits that same group (push, and the merge when the chunk
+ * fills).  Only that CTA reads the group's bank, so every read still sees the
+ * bank from before this step's commit, as with the two calls in that order.
+ * The last of the row's G CTAs to arrive updates count / total and sets the
+ * row's arrival counter back to 0.  Otherwise it makes those two calls.
+ * Results are identical to the two calls.
  * The sequence of runtime/model/independent_memory.py:177 `committed_gqa`
  * then :190 `commit_decode` in the reference's decode layer
  * (modeling_yanchor.py:283-312).
@@ -357,8 +360,9 @@ int yb_sample_greedy(const void *scores, int64_t row_stride, int64_t B, int64_t 
  * workspace: its partial results go to a fixed 64 KiB device array inside
  * this library, which covers at most 4096 rows (larger batches get
  * YB_ERR_UNSUPPORTED).  It allocates nothing and frees nothing.  The first
- * call on a device looks the array's device address up once for that device,
- * so make that first call before any stream capture.  All calls on a device
+ * call in a CUDA context looks the array's device address up once for that
+ * context (a context made after cudaDeviceReset looks it up again), so make
+ * that first call before any stream capture.  All calls on a device
  * share the array: calls that may run at the same time on the GPU (different
  * streams with no ordering between them) race on it.  No counterpart in the
  * reference, which always lets torch allocate.

@@ -51,15 +51,3 @@ def update_decode_state(sampled_token, storage, dense_seen, generated_lengths, f
     row_positions += active.astype(row_positions.dtype)
     decode_ids.reshape(-1)[:] = np.where(finished, np.int64(pad_token_id), tok)
     decode_useful_events.reshape(-1)[0] += int(active.sum())
-
-
-def resolve_recurrent_state_storage(storage, batch_size):
-    """runtime/model/inference_kernels.py:428-435: the recurrent-state storage
-    a decode graph of ``batch_size`` rows uses."""
-    if batch_size <= 0:
-        raise ValueError('recurrent-state storage requires a positive batch')
-    if storage == 'fp16_non_anchor_auto_b64':
-        return 'fp16_non_anchor' if batch_size >= 64 else 'fp32'
-    if storage not in {'fp32', 'bf16_non_anchor', 'fp16_non_anchor'}:
-        raise ValueError(f'unsupported GDN recurrent state storage: {storage}')
-    return storage

@@ -99,6 +99,24 @@ def test_python_ops_refuse_cpu_tensors():
         yb.greedy(torch.randn(2, 10))
 
 
+def test_greedy_noalloc_checks_out_and_stride_on_host():
+    """The no-allocation greedy refuses an ``out`` the kernel would write past
+    (wrong dtype, too short, non-contiguous) and scores it would have to copy,
+    before anything touches a device."""
+    import yanchor_b200 as yb
+    scores = torch.randn(4, 10)
+    with pytest.raises(ValueError, match='int64'):
+        yb.greedy_noalloc(scores, out=torch.empty(4, dtype=torch.int32))
+    with pytest.raises(ValueError, match='rows need one each'):
+        yb.greedy_noalloc(scores, out=torch.empty(3, dtype=torch.int64))
+    with pytest.raises(ValueError, match='contiguous'):
+        yb.greedy_noalloc(scores, out=torch.empty(4, 2, dtype=torch.int64)[:, 0])
+    with pytest.raises(ValueError, match='unit stride'):
+        yb.greedy_noalloc(torch.randn(10, 4).t())
+    with pytest.raises(ValueError, match='CUDA tensors only'):
+        yb.greedy_noalloc(scores, out=torch.empty(4, dtype=torch.int64))
+
+
 def test_python_ops_validate_shapes_first():
     """fla's head-count checks fire before anything touches a device."""
     import yanchor_b200.gated_delta_rule as gdr

@@ -3,7 +3,6 @@ reference fixtures and the oracle (bit-exact: integer work), and the CUDA
 graph driver against eager decode steps of a small recurrent model built on
 this package's kernels."""
 import os
-from types import SimpleNamespace
 
 import numpy as np
 import pytest
@@ -101,85 +100,63 @@ def test_state_update_out_of_vocabulary_token_is_reported(yb):
 
 class TinyRecurrentLM:
     """A one-layer recurrent decoder on this package's kernels: embedding ->
-    q, k, v, gates -> in-place GDN decode step -> logits.  The cache holds the
-    recurrent state (one layer), so the graph driver's snapshot covers it."""
+    q, k, v, gates -> in-place GDN decode step -> logits -> greedy, with the
+    state, token ids and positions in tensors at fixed addresses."""
 
-    def __init__(self, vocab=97, H=2, HV=4, K=128, V=128, seed=0):
+    def __init__(self, rows, vocab=97, H=2, HV=4, K=128, V=128, seed=0):
         g = torch.Generator(device='cuda').manual_seed(seed)
         self.H, self.HV, self.K, self.V = H, HV, K, V
         self.emb = torch.randn(vocab, (2 * H * K + HV * V + 2 * HV), generator=g, device='cuda') * 0.3
         self.out = torch.randn(HV * V, vocab, generator=g, device='cuda') * 0.05
-        self.config = SimpleNamespace(gdn_recurrent_state_storage='fp32')
+        self.state = torch.randn(rows, HV, K, V, generator=g, device='cuda') * 0.02
+        self.ids = torch.randint(0, vocab, (rows, 1), device='cuda', generator=g)
+        self.pos = torch.arange(100, 100 + rows, device='cuda')
         import yanchor_b200
         self.yb = yanchor_b200
 
-    def __call__(self, input_ids, position_ids, past_key_values, use_cache, logits_to_keep):
+    def step(self, b):
+        """One decode step of the first b rows, in place: returns the ids."""
         H, HV, K, V = self.H, self.HV, self.K, self.V
-        B = input_ids.shape[0]
-        x = self.emb[input_ids[:, 0]] + 1e-3 * position_ids.to(torch.float32)
-        q, k, v, a, b = torch.split(x, [H * K, H * K, HV * V, HV, HV], dim=-1)
-        q = q.reshape(B, 1, H, K).to(torch.bfloat16)
-        k = k.reshape(B, 1, H, K).to(torch.bfloat16)
-        v = v.reshape(B, 1, HV, V).to(torch.bfloat16)
-        g = torch.nn.functional.logsigmoid(a).reshape(B, 1, HV)
-        beta = torch.sigmoid(b).reshape(B, 1, HV).to(torch.bfloat16)
-        state = past_key_values.layers[0].recurrent_states
-        o, _ = self.yb.fused_recurrent_gated_delta_rule(q, k, v, g=g, beta=beta, initial_state=state,
+        x = self.emb[self.ids[:b, 0]] + 1e-3 * self.pos[:b, None].to(torch.float32)
+        q, k, v, a, beta = torch.split(x, [H * K, H * K, HV * V, HV, HV], dim=-1)
+        q = q.reshape(b, 1, H, K).to(torch.bfloat16)
+        k = k.reshape(b, 1, H, K).to(torch.bfloat16)
+        v = v.reshape(b, 1, HV, V).to(torch.bfloat16)
+        g = torch.nn.functional.logsigmoid(a).reshape(b, 1, HV)
+        beta = torch.sigmoid(beta).reshape(b, 1, HV).to(torch.bfloat16)
+        o, _ = self.yb.fused_recurrent_gated_delta_rule(q, k, v, g=g, beta=beta, initial_state=self.state[:b],
                                                         output_final_state=True, use_qk_l2norm_in_kernel=True,
                                                         inplace=True)
-        return SimpleNamespace(logits=(o.reshape(B, HV * V).float() @ self.out)[:, None])
+        scores = o.reshape(b, HV * V).float() @ self.out
+        self.ids[:b].copy_(self.yb.greedy(scores))
+        self.pos[:b].add_(1)
+        return self.ids[:b]
+
+    def warm(self):
+        torch.randn(8, 8, device='cuda') @ torch.randn(8, 8, device='cuda')   # cuBLAS set-up
 
 
-def fresh_cache(B, HV=4, K=128, V=128, seed=1):
-    g = torch.Generator(device='cuda').manual_seed(seed)
-    return SimpleNamespace(layers=[SimpleNamespace(recurrent_states=torch.randn(B, HV, K, V, generator=g,
-                                                                                  device='cuda') * 0.02)])
-
-
-@pytest.mark.parametrize('consume', [False, True])
-def test_decode_graph_matches_eager_steps(yb, consume):
-    """Greedy decoding through FixedMemoryDecodeGraph (with the bookkeeping
-    kernel after each step) equals the same loop run eagerly, token for token
-    and state for state."""
-    B, steps = 6, 12
-    model = TinyRecurrentLM()
-    first = torch.randint(0, 97, (B, 1), device='cuda', generator=torch.Generator(device='cuda').manual_seed(3))
-    pos0 = torch.arange(100, 100 + B, device='cuda')
-
-    def run(use_graph):
-        cache = fresh_cache(B)
-        ids, pos = first.clone(), pos0.clone()
-        toks = []
-        graph = yb.FixedMemoryDecodeGraph(model, cache, ids, pos, consume_capture_steps=consume) if use_graph \
-            else None
-        for _ in range(steps):
-            if use_graph:
-                scores = graph.replay(ids, position_ids=pos)
-            else:
-                scores = model(input_ids=ids, position_ids=pos[:, None], past_key_values=cache, use_cache=True,
-                               logits_to_keep=1).logits[:, -1]
-            ids = yb.greedy(scores)
-            pos = pos + 1
-            toks.append(ids.clone())
-        if graph is not None:
-            graph.close()
-        return torch.cat(toks, 1), cache.layers[0].recurrent_states
-
-    t_eager, s_eager = run(False)
-    t_graph, s_graph = run(True)
-    assert torch.equal(t_eager, t_graph)
-    assert torch.equal(s_eager, s_graph)
-
-
-def test_decode_graph_capture_leaves_cache_unchanged(yb):
-    """Without capture-consuming steps the warm-up and capture forwards are
-    undone: the cache equals its value before the driver was built."""
-    cache = fresh_cache(3)
-    before = cache.layers[0].recurrent_states.clone()
-    model = TinyRecurrentLM()
-    graph = yb.FixedMemoryDecodeGraph(model, cache, torch.zeros((3, 1), dtype=torch.long, device='cuda'), 5)
-    assert torch.equal(cache.layers[0].recurrent_states, before)
-    assert int(graph.static_position_ids[0]) == 5
-    graph.replay(torch.ones((3, 1), dtype=torch.long, device='cuda'))
-    assert not torch.equal(cache.layers[0].recurrent_states, before)
-    graph.close()
+def test_step_graphs_match_eager_steps(yb):
+    """Greedy decoding through StepGraphs equals the same loop run eagerly,
+    token for token and state for state; capturing leaves the state, ids and
+    positions untouched (nothing runs during capture), and a batch between
+    two captured sizes replays the larger graph."""
+    rows, steps = 8, 12
+    eager, graphed = TinyRecurrentLM(rows), TinyRecurrentLM(rows)
+    before = (graphed.state.clone(), graphed.ids.clone(), graphed.pos.clone())
+    graphs = yb.StepGraphs(graphed.step, [2, 6, 8], warm=graphed.warm)
+    assert torch.equal(graphed.state, before[0]) and torch.equal(graphed.ids, before[1])
+    assert torch.equal(graphed.pos, before[2])
+    assert graphs.bucket(5) == 6 and graphs.bucket(6) == 6 and graphs.bucket(7) == 8
+    with pytest.raises(ValueError):
+        graphs.bucket(9)
+    toks_e, toks_g = [], []
+    for t in range(steps):
+        b = 6 if t < 5 else 8
+        toks_e.append(eager.step(b).clone())
+        toks_g.append(graphs.replay(b).clone())
+    graphs.close()
+    for t, (a, b) in enumerate(zip(toks_e, toks_g)):
+        assert torch.equal(a, b), t
+    assert torch.equal(eager.state, graphed.state)
+    assert torch.equal(eager.pos, graphed.pos)

@@ -217,3 +217,57 @@ def test_decode_read_16bit_shapes(yb, R, D, CAP, dt):
     ref = omem.decode_read(host(qd), host(dev.keys), host(dev.values), st['positions'], idx)
     assert np.abs(host(out) - ref).max() <= 2e-2
     assert not host(out)[2].any()
+
+
+def test_memory_decode_step_graph_survives_counter_growth(yb):
+    """A CUDA graph captured around memory_decode_step at B=8 keeps the
+    arrival counters it was captured with.  An eager call at B=128 makes the
+    module grow its counter buffer; the captured graph must still replay
+    correctly afterwards (its counters are never freed or reused), over 70
+    steps that cross one commit at chunk 64, bit-exact against the oracle
+    (modeling_yanchor.py:277-313 restated in oracle/memory.py)."""
+    rng = np.random.default_rng(77)
+    B, G, H, D, CAP, CH = 8, 4, 16, 256, 64, 64
+    bf = torch.bfloat16
+    st_np = omem.empty_state(B, G, CAP, CH, D)
+    st = to_device_state(yb, st_np, bf)
+    q = torch.zeros(B, 1, H, D, device='cuda', dtype=bf)
+    k = torch.zeros(B, 1, G, D, device='cuda', dtype=bf)
+    v = torch.zeros(B, 1, G, D, device='cuda', dtype=bf)
+    sc = torch.zeros(B, 1, G, device='cuda')
+    act = torch.ones(B, device='cuda', dtype=torch.bool)
+    # warm up on a scratch state (the first call may set up the module), then capture
+    scratch = yb.MemoryState.empty(B, G, CAP, CH, D, 'cuda', bf)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        yb.memory_decode_step(q, k, v, sc, act, CH, scratch)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = yb.memory_decode_step(q, k, v, sc, act, CH, st)
+    # an eager call at a larger batch grows the module's counter buffer
+    big = yb.MemoryState.empty(128, G, CAP, CH, D, 'cuda', bf)
+    yb.memory_decode_step(torch.randn(128, 1, H, D, device='cuda').to(bf), torch.randn(128, 1, G, D, device='cuda').to(bf),
+                          torch.randn(128, 1, G, D, device='cuda').to(bf), torch.randn(128, 1, G, device='cuda'),
+                          torch.ones(128, device='cuda', dtype=torch.bool), CH, big)
+    filler = [torch.full((1 << 16,), 7, device='cuda', dtype=torch.int32) for _ in range(8)]   # reuse freed memory
+    torch.cuda.synchronize()
+    for t in range(70):
+        qn = rng.standard_normal((B, 1, H, D)).astype(np.float32)
+        kn = rng.standard_normal((B, 1, G, D)).astype(np.float32)
+        vn = rng.standard_normal((B, 1, G, D)).astype(np.float32)
+        sn = np.round(rng.standard_normal((B, 1, G)) * 2).astype(np.float32) / 2
+        q.copy_(cuda(qn, bf))
+        k.copy_(cuda(kn, bf))
+        v.copy_(cuda(vn, bf))
+        sc.copy_(cuda(sn))
+        graph.replay()
+        ref = omem.decode_read(host(q), st_np['keys'], st_np['values'], st_np['positions'])
+        assert np.abs(host(out) - ref).max() <= 2e-2, t
+        omem.commit_decode(host(k), host(v), sn, np.ones(B, bool), CH, st_np)
+    for f in FIELDS:
+        np.testing.assert_array_equal(host(getattr(st, f)), st_np[f].astype(host(getattr(st, f)).dtype), err_msg=f)
+    assert all(int(x.min()) == 7 for x in filler)
+    del graph

@@ -16,21 +16,21 @@ Operators (all CUDA, via the C ABI library libyanchor_b200.so):
 * sampling: ``greedy``, ``sample_top_k_top_p_counter``,
   ``apply_dense_presence_penalty_``
 * decode loop: ``update_fixed_decode_state_`` (per-step bookkeeping in one
-  launch) and ``FixedMemoryDecodeGraph`` (the CUDA-graph decode driver)
+  launch), ``prepare_capture`` and ``StepGraphs`` (CUDA graphs of a decode
+  step per batch size, captured without warm-up forwards)
 * ``bind_gdn_kernels`` / ``install_memory_module`` / ``bind_memory_prefill``
   put them where the reference model code looks them up.
 """
 from .gated_delta_rule import (chunk_gated_delta_rule, fused_gdn_decode, fused_recurrent_gated_delta_rule,  # noqa: F401
                                gdn_gates)
 from .conv import causal_conv1d_fn, causal_conv1d_update  # noqa: F401
-from .swa import (flash_swa, initialize_physical_ring, layer_ring_update, physical_ring_decode_attention,  # noqa: F401
+from .swa import (flash_swa, layer_ring_update, physical_ring_decode_attention,  # noqa: F401
                   physical_ring_update_, reference_swa)
 from .independent_memory import MemoryState, commit_decode, committed_gqa, indexed_gqa  # noqa: F401
 from .independent_memory import decode_step as memory_decode_step  # noqa: F401
 from .memory_prefill import exclusive_prefix_topk, merge_topk, select_topk, sequence  # noqa: F401
-from .sampling import apply_dense_presence_penalty_, greedy, sample_top_k_top_p_counter  # noqa: F401
-from .decode_loop import (FixedMemoryDecodeGraph, resolve_recurrent_state_storage,  # noqa: F401
-                          restore_cuda_graph_cache, snapshot_cuda_graph_cache, update_fixed_decode_state_)
+from .sampling import apply_dense_presence_penalty_, greedy, greedy_noalloc, sample_top_k_top_p_counter  # noqa: F401
+from .decode_loop import StepGraphs, prepare_capture, update_fixed_decode_state_  # noqa: F401
 from .bind import bind_gdn_kernels, bind_memory_prefill, install_memory_module  # noqa: F401
 from ._lib import LIB_PATH, YanchorError, lib  # noqa: F401
 

@@ -659,9 +659,40 @@ int64_t greedy_builtin_scratch_bytes() { return kGreedyScratchBytes; }
 namespace {
 // Host code may not use g_greedy_scratch's address directly (the host-side
 // name is only a stand-in); the device address comes from
-// cudaGetSymbolAddress, looked up once per device with that device current.
+// cudaGetSymbolAddress, looked up with the device current.  The lookup is
+// cached per device together with the unique id of the CUDA context it was
+// made in (cuCtxGetId: never reused within a process).  A context created
+// later on that device, e.g. after cudaDeviceReset or by a caller's own
+// driver-API context, has another id, so its first call looks the address up
+// again instead of using one from a context that no longer exists.
+typedef int (*CtxGetCurrentFn)(void **);
+typedef int (*CtxGetIdFn)(void *, unsigned long long *);
 std::mutex g_scratch_mu;
 void *g_scratch_addr[kMaxDevices] = {};
+unsigned long long g_scratch_ctx[kMaxDevices] = {};
+
+// unique id of the calling thread's current context, 0 if the driver cannot tell
+unsigned long long current_context_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static bool looked_up = false;
+  if (!looked_up) {
+    void *f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(f);
+    f = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(f);
+    looked_up = true;
+  }
+  void *ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current && get_id && get_current(&ctx) == 0 && ctx && get_id(ctx, &id) == 0) return id;
+  return 0;
+}
 }  // namespace
 
 int launch_sample_greedy_noalloc(const SampleArgs &a) {
@@ -679,12 +710,14 @@ int launch_sample_greedy_noalloc(const SampleArgs &a) {
   void *scratch = nullptr;
   {
     std::lock_guard<std::mutex> lock(g_scratch_mu);
-    if (!g_scratch_addr[dev]) {
+    const unsigned long long ctx = current_context_id();
+    if (!g_scratch_addr[dev] || ctx == 0 || ctx != g_scratch_ctx[dev]) {
       void *p = nullptr;
       e = cudaGetSymbolAddress(&p, g_greedy_scratch);
       if (e != cudaSuccess)
         return set_error(YB_ERR_CUDA, "sample_greedy_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
       g_scratch_addr[dev] = p;
+      g_scratch_ctx[dev] = ctx;
     }
     scratch = g_scratch_addr[dev];
   }

@@ -1,27 +1,27 @@
 """Decode-loop plumbing around the hot path: the per-step bookkeeping kernel
-and the CUDA-graph driver of the fixed-memory decode, with the reference's
-call shapes.
+and a CUDA-graph driver for decode steps built from this package's ops.
 
     update_fixed_decode_state_(...)
         runtime/model/inference_kernels.py:1206-1208 (`_update_fixed_decode_state_`,
         Triton kernel :1169-1204; torch statements :1701-1717): one launch
         of ``yb_decode_state_update``
-    resolve_recurrent_state_storage(storage, batch_size)
-        same file :428-435
-    snapshot_cuda_graph_cache(cache) / restore_cuda_graph_cache(cache, snap)
-        same file :388-426: device copies of every cache tensor, so that the
-        warm-up and capture forwards leave the cache as they found it
-    FixedMemoryDecodeGraph(model, cache, token, position, ...)
-        same file :437-553: warm up, capture one decode forward (and the
-        position increment) into a CUDA graph, then ``replay(token,
-        position_ids)`` copies the new ids in and replays
+    prepare_capture(device, max_batch)
+        the one-time set-up of every lazily initialised piece of this package
+        on a device, so that a step made of its ops can be captured without
+        first running it
+    StepGraphs(step, batch_sizes)
+        one CUDA graph of ``step(batch)`` per batch size, captured largest
+        first into one shared memory pool; ``replay(batch)`` runs the graph
+        of the smallest captured size that holds ``batch`` rows
 
-The graph driver is model-agnostic: ``model`` is called as the reference
-calls it (``input_ids``, ``position_ids``, ``past_key_values``,
-``use_cache=True``, ``logits_to_keep=1``) and must return an object with
-``.logits [B, 1, vocab]``.  The reference's two model hooks (switching its
-layers to graph mode, converting the recurrent-state storage) are optional
-callables here.
+The reference's own driver (`FixedMemoryDecodeGraph`,
+runtime/model/inference_kernels.py:437-553) runs warm-up forwards before
+capture and therefore snapshots and restores the whole cache around them.
+The ops here need no warm-up forward: ``prepare_capture`` does their set-up
+without touching any caller state, and capturing records the step without
+executing it, so the caller's recurrent, memory and ring state is exactly as
+it was when the graphs are ready.  The reference's driver can also drive
+these ops unchanged (it calls the rebound kernels).
 """
 from __future__ import annotations
 
@@ -78,190 +78,73 @@ def update_fixed_decode_state_(sampled_token, storage, dense_seen, generated_len
     _lib.check(rc, 'update_fixed_decode_state_')
 
 
-def resolve_recurrent_state_storage(storage: str, batch_size: int) -> str:
-    if batch_size <= 0:
-        raise ValueError('recurrent-state storage requires a positive batch')
-    if storage == 'fp16_non_anchor_auto_b64':
-        return 'fp16_non_anchor' if batch_size >= 64 else 'fp32'
-    if storage not in {'fp32', 'bf16_non_anchor', 'fp16_non_anchor'}:
-        raise ValueError(f'unsupported GDN recurrent state storage: {storage}')
-    return storage
+
+def prepare_capture(device=None, max_batch: int = 4096) -> None:
+    """Set up, once, everything in this package that is initialised on first
+    use, so that a decode step built from its ops can be captured in a CUDA
+    graph without running it first: the library is loaded, the anchor-memory
+    step's arrival counters are sized for ``max_batch`` rows, and the
+    no-allocation sampler has looked up its scratch address.  Touches no
+    caller state; must not run during a capture."""
+    from . import independent_memory, sampling
+    device = torch.device('cuda', torch.cuda.current_device()) if device is None else torch.device(device)
+    _lib.lib()
+    independent_memory._arrive(int(max_batch), device)
+    with torch.cuda.device(device):
+        sampling.greedy_noalloc(torch.zeros((1, 1), device=device), out=torch.empty(1, device=device,
+                                                                                    dtype=torch.int64))
+    torch.cuda.synchronize(device)
 
 
-STATE_DTYPES = {'fp32': torch.float32, 'bf16_non_anchor': torch.bfloat16, 'fp16_non_anchor': torch.float16}
+class StepGraphs:
+    """CUDA graphs of one decode step, one per batch size.
 
-_RING_PREFIXES = ('_qwen35_swa_scratch_', '_qwen35_swa_physical_ring_')
+    ``step(batch)`` is the caller's function for ``batch`` rows: it reads its
+    inputs from tensors the caller owns and keeps at fixed addresses (token
+    ids, positions, the recurrent / memory / ring state of the first
+    ``batch`` rows) and returns the step's outputs (tensors, or a tuple of
+    them).  Each size is captured once, largest first, into one shared pool,
+    so smaller sizes reuse the largest graph's activation memory; nothing is
+    executed while capturing.  ``replay(batch)`` runs the graph of the
+    smallest captured size >= ``batch`` and returns that graph's outputs
+    (rows beyond ``batch`` belong to padding rows the caller keeps inactive).
+    Call ``close()`` (or drop the object) before tearing the process group or
+    the device down.
 
+    ``warm``, if given, runs once before the first capture: the place for
+    set-up of code outside this package (e.g. cuBLAS handles of the caller's
+    projections) that must not run inside a capture."""
 
-def _cache_tensors(cache, include_ring_backing):
-    found = []
-    for li, layer in enumerate(cache.layers):
-        for name, value in vars(layer).items():
-            if not include_ring_backing and name.startswith(_RING_PREFIXES):
-                continue
-            if isinstance(value, torch.Tensor):
-                found.append((f'{li}.{name}', value))
-            elif isinstance(value, dict):
-                found.extend((f'{li}.{name}.{k}', v) for k, v in value.items() if isinstance(v, torch.Tensor))
-            elif name == 'memory_state' and value is not None:
-                found.extend((f'{li}.memory_state.{k}', v) for k, v in vars(value).items()
-                             if isinstance(v, torch.Tensor))
-    return found
+    def __init__(self, step, batch_sizes, *, device=None, warm=None):
+        sizes = sorted({int(b) for b in batch_sizes})
+        if not sizes or sizes[0] <= 0:
+            raise ValueError('StepGraphs needs positive batch sizes')
+        self.device = torch.device('cuda', torch.cuda.current_device()) if device is None else torch.device(device)
+        prepare_capture(self.device, sizes[-1])
+        if warm is not None:
+            warm()
+            torch.cuda.synchronize(self.device)
+        self.sizes = sizes
+        self.pool = torch.cuda.graph_pool_handle()
+        self.graphs = {}
+        self.outputs = {}
+        for b in reversed(sizes):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=self.pool):
+                out = step(b)
+            self.graphs[b], self.outputs[b] = g, out
 
+    def bucket(self, batch: int) -> int:
+        for b in self.sizes:
+            if b >= batch:
+                return b
+        raise ValueError(f'no captured decode step holds {batch} rows (largest: {self.sizes[-1]})')
 
-def snapshot_cuda_graph_cache(cache, *, include_ring_backing=False):
-    return {'entries': [(n, t, t.clone()) for n, t in _cache_tensors(cache, include_ring_backing)],
-            'include_ring_backing': bool(include_ring_backing),
-            'seen_tokens': getattr(cache, '_seen_tokens', None),
-            'layer_metadata': [{'cumulative_length': getattr(layer, 'cumulative_length', None),
-                                'all_valid_host': getattr(layer, 'all_valid_host', None)} for layer in cache.layers]}
-
-
-def restore_cuda_graph_cache(cache, snapshot, *, reset_ring=None):
-    """Copy the saved values back into the same tensors (a tensor that the
-    forward replaced by a new object is an error: a graph would keep the old
-    one).  ``reset_ring(layer)`` runs for layers holding a physical ring when
-    the ring backing was not saved."""
-    current = dict(_cache_tensors(cache, snapshot.get('include_ring_backing', False)))
-    for name, tensor, saved in snapshot['entries']:
-        if current.get(name) is not tensor:
-            raise RuntimeError(f'CUDA Graph capture replaced cache tensor {name}')
-        tensor.copy_(saved)
-    if snapshot['seen_tokens'] is not None:
-        cache._seen_tokens = int(snapshot['seen_tokens'])
-    for layer, meta in zip(cache.layers, snapshot['layer_metadata']):
-        for name, value in meta.items():
-            if hasattr(layer, name):
-                setattr(layer, name, value)
-        if not snapshot.get('include_ring_backing', False) and reset_ring is not None and \
-                hasattr(layer, '_qwen35_swa_physical_ring_index'):
-            reset_ring(layer)
-
-
-class FixedMemoryDecodeGraph:
-    """One captured decode forward, replayed once per generated token."""
-
-    @torch.no_grad()
-    def __init__(self, model, cache, token, position, scores_dtype=torch.float32, consume_capture_steps=False, *,
-                 set_graph_decode=None, convert_state_storage=None, state_storage=None, reset_ring=None):
-        if token.ndim != 2 or token.shape[1] != 1 or not token.is_cuda:
-            raise ValueError('fixed-memory CUDA Graph requires CUDA [batch, 1] tokens')
-        if scores_dtype not in (torch.float32, torch.bfloat16):
-            raise ValueError('decode scores must use FP32 or BF16')
-        self.model, self.cache, self._reset_ring = model, cache, reset_ring
-        storage = resolve_recurrent_state_storage(
-            state_storage or str(getattr(getattr(model, 'config', None), 'gdn_recurrent_state_storage', 'fp32')),
-            int(token.shape[0]))
-        self.recurrent_state_storage_receipt = (convert_state_storage(cache, STATE_DTYPES[storage])
-                                                if convert_state_storage is not None else None)
-        self.static_ids = token.clone()
-        if isinstance(position, torch.Tensor):
-            pv = position.to(device=token.device, dtype=torch.long)
-            if pv.ndim == 1:
-                pv = pv[:, None]
-            if pv.shape not in (token.shape, (4, *token.shape)):
-                raise ValueError('decode positions require one value per token row')
-            self.static_position_ids = pv.clone()
-        else:
-            self.static_position_ids = torch.full((token.shape[0], 1), int(position), dtype=torch.long,
-                                                  device=token.device)
-        initial = self.static_position_ids.clone()
-        self.replays = 0
-        self.graph = None
-        self.scores = None
-        self._pending_scores = None
-        self.consume_capture_steps = bool(consume_capture_steps)
-        self._set_graph_decode = set_graph_decode
-        if set_graph_decode is not None:
-            set_graph_decode(model, cache, True)
-        if self.consume_capture_steps:
-            # the warm-up forward is a real decode step: its scores are handed
-            # out by the first replay, and the graph is captured on that replay
-            host = self._snapshot_host_metadata()
-            out = self._forward()
-            self.scores = out.logits[:, -1].to(dtype=scores_dtype)
-            self._pending_scores = self.scores
-            self.static_position_ids.add_(1)
-            self._restore_host_metadata(host)
-            self.replays += 1
-            torch.cuda.synchronize(token.device)
-            return
-        warm = snapshot_cuda_graph_cache(cache)
-        self._forward()
-        torch.cuda.synchronize(token.device)
-        restore_cuda_graph_cache(cache, warm, reset_ring=reset_ring)
-        del warm
-        snap = snapshot_cuda_graph_cache(cache)
-        self.static_position_ids.copy_(initial)
-        self.graph = torch.cuda.CUDAGraph()
-        torch.cuda.synchronize(token.device)
-        with torch.cuda.graph(self.graph):
-            out = self._forward()
-            self.scores = out.logits[:, -1].to(dtype=scores_dtype)
-            self.static_position_ids.add_(1)
-        torch.cuda.synchronize(token.device)
-        restore_cuda_graph_cache(cache, snap, reset_ring=reset_ring)
-        self.static_position_ids.copy_(initial)
-
-    def _forward(self):
-        return self.model(input_ids=self.static_ids, position_ids=self.static_position_ids,
-                          past_key_values=self.cache, use_cache=True, logits_to_keep=1)
-
-    def _snapshot_host_metadata(self):
-        return (getattr(self.cache, '_seen_tokens', None),
-                [(getattr(layer, 'cumulative_length', None), getattr(layer, 'all_valid_host', None))
-                 for layer in self.cache.layers])
-
-    def _restore_host_metadata(self, snapshot):
-        seen, layers = snapshot
-        if seen is not None:
-            self.cache._seen_tokens = int(seen)
-        for layer, (cum, valid) in zip(self.cache.layers, layers):
-            if cum is not None and hasattr(layer, 'cumulative_length'):
-                layer.cumulative_length = cum
-            if valid is not None and hasattr(layer, 'all_valid_host'):
-                layer.all_valid_host = valid
-
-    def _copy_position_ids(self, position_ids):
-        if position_ids is None:
-            return
-        pv = position_ids.to(device=self.static_position_ids.device, dtype=torch.long)
-        if pv.ndim == 1:
-            pv = pv[:, None]
-        if pv.shape != self.static_position_ids.shape:
-            raise ValueError('decode positions require one value per captured row')
-        self.static_position_ids.copy_(pv)
-
-    @torch.no_grad()
-    def replay(self, token, position_ids=None):
-        if self._pending_scores is not None:
-            if not torch.equal(token, self.static_ids):
-                raise RuntimeError('capture-consuming warm token changed before use')
-            scores, self._pending_scores = self._pending_scores, None
-            return scores
-        self.static_ids.copy_(token)
-        self._copy_position_ids(position_ids)
-        if self.graph is None:
-            # first replay after a capture-consuming warm-up: capture now, then
-            # replay, so this step's forward runs exactly once
-            self.graph = torch.cuda.CUDAGraph()
-            host = self._snapshot_host_metadata()
-            torch.cuda.synchronize(token.device)
-            with torch.cuda.graph(self.graph):
-                out = self._forward()
-                self.scores = out.logits[:, -1].to(dtype=self.scores.dtype)
-                self.static_position_ids.add_(1)
-            self._restore_host_metadata(host)
-            self.graph.replay()
-            torch.cuda.synchronize(token.device)
-            self.replays += 1
-            return self.scores
-        self.graph.replay()
-        self.replays += 1
-        return self.scores
+    def replay(self, batch: int):
+        b = self.bucket(int(batch))
+        self.graphs[b].replay()
+        return self.outputs[b]
 
     def close(self):
-        """Release the graph (and the hook's graph mode)."""
-        self.graph = None
-        if self._set_graph_decode is not None:
-            self._set_graph_decode(self.model, self.cache, False)
+        self.graphs.clear()
+        self.outputs.clear()

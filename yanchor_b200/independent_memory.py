@@ -187,24 +187,32 @@ def committed_gqa(query, state, indices=None):
 
 
 _ARRIVE = {}
+_ARRIVE_RETIRED = []
 
 
 def _arrive(batch, device):
     """B zeroed int32 counters per device for ``decode_step`` (every call
-    leaves them zero); grown, never shrunk."""
+    leaves them zero).  When a larger batch comes, a larger buffer replaces
+    the current one, but the old one is kept alive for the life of the
+    process: a CUDA graph captured at a smaller batch still holds its address
+    and must never see that memory handed to another tensor."""
     t = _ARRIVE.get(device)
     if t is None or t.numel() < batch:
+        if t is not None:
+            _ARRIVE_RETIRED.append(t)
         t = _ARRIVE[device] = torch.zeros(max(batch, 64), device=device, dtype=torch.int32)
     return t
 
 
-def decode_step(query, key, value, scores, active, chunk, state, indices=None):
+def decode_step(query, key, value, scores, active, chunk, state, indices=None, arrive=None):
     """One decode step of a memory layer: ``committed_gqa(query, state)`` then
     ``commit_decode(key, value, scores, active, chunk, state)`` — the reference
     decode layer's order (``modeling_yanchor.py:283-312``) — with identical
     results, in one launch on the tensor-core read path.  Returns the read.
-    Steps of one device run in stream order: calls that overlap on the GPU
-    share the arrival counters and must not."""
+    ``arrive`` is an optional int32 tensor of at least B zeroed counters that
+    the caller owns (every call leaves them zero); by default the module keeps
+    one buffer per device.  Calls that overlap on the GPU must not share
+    counters."""
     require_cuda(query, key, value, scores, active, state.keys)
     _check_state(state)
     if state.positions.stride(0) != state.scores.stride(0):
@@ -221,13 +229,20 @@ def decode_step(query, key, value, scores, active, chunk, state, indices=None):
     if state.keys.dtype != query.dtype or key.dtype != state.keys.dtype or value.dtype != state.values.dtype:
         raise TypeError('query, key, value and the memory must share a dtype')
     idx = _indices(indices, query.device)
+    if arrive is None:
+        arr = _arrive(b, query.device)
+    else:
+        if arrive.dtype != torch.int32 or not arrive.is_contiguous() or arrive.numel() < b \
+                or arrive.device != query.device:
+            raise ValueError('arrive must be a contiguous int32 tensor of at least B counters on the query device')
+        arr = arrive
     out = torch.empty_like(query)
     rc = _lib.lib().yb_mem_decode_step(
         query.data_ptr(), out.data_ptr(), key.data_ptr(), value.data_ptr(), scores.data_ptr(), active.data_ptr(),
         int(chunk), state.keys.data_ptr(), state.values.data_ptr(), state.scores.data_ptr(),
         state.positions.data_ptr(), state.pending_keys.data_ptr(), state.pending_values.data_ptr(),
         state.pending_scores.data_ptr(), state.count.data_ptr(), state.total.data_ptr(), ptr(idx),
-        _arrive(b, query.device).data_ptr(), b, h, g, cap, pc, d, state.keys.stride(0), state.scores.stride(0),
+        arr.data_ptr(), b, h, g, cap, pc, d, state.keys.stride(0), state.scores.stride(0),
         state.pending_keys.stride(0), state.pending_scores.stride(0), state.count.stride(0), dtype_code(query),
         stream_ptr(query.device))
     _lib.check(rc, 'decode_step')

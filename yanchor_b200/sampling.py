@@ -49,13 +49,28 @@ def greedy(scores, workspace=None):
 def greedy_noalloc(scores, out=None):
     """argmax like ``greedy``, for callers that cannot allocate device memory
     when they sample: it needs no workspace (the library keeps a fixed 64 KiB
-    device array for the partial results, enough for 4096 rows).  Pass a
-    preallocated ``out`` ([B, 1] int64) to allocate nothing at all.  Calls that
-    may run concurrently on the GPU share that array and race; make the first
-    call on each device before capturing a CUDA graph."""
-    require_cuda(scores)
-    scores = _rows(scores)
+    device array for the partial results, enough for 4096 rows).  With a
+    preallocated ``out`` ([B, 1] or [B] int64, contiguous, on the scores'
+    device) and scores whose last stride is 1, the call allocates nothing at
+    all; scores with another last stride are refused rather than copied.
+    Calls that may run concurrently on the GPU share that array and race; make
+    the first call on each device before capturing a CUDA graph."""
+    if scores.dim() != 2:
+        raise ValueError('sampling scores must have shape [batch, vocabulary]')
+    if scores.stride(-1) != 1:
+        raise ValueError('greedy_noalloc needs scores with unit stride along the vocabulary '
+                         '(a copy would allocate)')
     B, V = scores.shape
+    if out is not None:
+        if out.dtype != torch.int64:
+            raise ValueError('greedy_noalloc: out must be int64')
+        if not out.is_contiguous():
+            raise ValueError('greedy_noalloc: out must be contiguous')
+        if out.numel() < B:
+            raise ValueError(f'greedy_noalloc: out holds {out.numel()} ids, {B} rows need one each')
+        if out.device != scores.device:
+            raise ValueError('greedy_noalloc: out must be on the scores\' device')
+    require_cuda(scores)
     if out is None:
         out = torch.empty((B, 1), device=scores.device, dtype=torch.int64)
     rc = _lib.lib().yb_sample_greedy_noalloc(scores.data_ptr(), scores.stride(0), B, V, dtype_code(scores),

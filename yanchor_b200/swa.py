@@ -12,9 +12,8 @@ reference's call shapes.
         the same update on a layer cache object, with the reference's
         signature (runtime/model/inference_kernels.py:1861-1879,
         `triton_fixed_memory_swa_physical_ring_update`): the ring lives in the
-        cache's ``_qwen35_swa_physical_ring_*`` attributes and is built on
-        first use as the reference builds it (`initialize_physical_ring`,
-        same file :555-598)
+        cache's ``_qwen35_swa_physical_ring_*`` attributes; a cache without
+        one gets it from the reference's own initialiser (same file :555-598)
 
     reference_swa(q, k, v, *, window, key_valid=None, query_start=0)
         modeling_yanchor.py:412-427: sliding-window attention over a prompt
@@ -101,61 +100,33 @@ def physical_ring_decode_attention(query, ring_key, ring_value, valid, *, reprod
 _RING = '_qwen35_swa_physical_ring_'
 
 
-def initialize_physical_ring(layer_cache):
-    """Build the ring from a chronological window cache (``keys`` / ``values``
-    ``[B, KVH, keep, D]``, ``valid [B, keep]``): ring width keep + 1, the
-    cached positions at 0 .. keep - 1, the write index at keep (int32).  With
-    ``_qwen35_swa_shared_ring_storage`` the cache's fields become views into
-    the ring.  Host-issued copies only (cache set-up, as the reference's)."""
-    tensors = (layer_cache.keys, layer_cache.values, layer_cache.valid)
-    if any(t is None or not t.is_cuda for t in tensors):
-        raise ValueError('physical SWA ring requires CUDA cache tensors')
-    keep = int(layer_cache.keys.shape[-2])
-    window = keep + 1
-    if getattr(layer_cache, '_qwen35_swa_shared_ring_storage', False):
-        for field, dim in (('keys', 2), ('values', 2), ('valid', 1)):
-            source = getattr(layer_cache, field)
-            shape = list(source.shape)
-            shape[dim] = window
-            target = getattr(layer_cache, _RING + field, None)
-            if target is not None and target.shape == tuple(shape) and source.data_ptr() == target.data_ptr():
-                target.narrow(dim, keep, 1).zero_()
-            else:
-                target = source.new_zeros(shape)
-                target.narrow(dim, 0, keep).copy_(source)
-            setattr(layer_cache, _RING + field, target)
-            setattr(layer_cache, field, target.narrow(dim, 0, keep))
-    else:
-        for field, source in (('keys', layer_cache.keys), ('values', layer_cache.values),
-                              ('valid', layer_cache.valid)):
-            shape = (*source.shape[:-2], window, source.shape[-1]) if field != 'valid' else (source.shape[0], window)
-            target = getattr(layer_cache, _RING + field, None)
-            if target is None or target.shape != shape or target.device != source.device:
-                target = source.new_zeros(shape)
-                setattr(layer_cache, _RING + field, target)
-            else:
-                target.zero_()
-            if field == 'valid':
-                target[:, :keep].copy_(source)
-            else:
-                target[:, :, :keep].copy_(source)
-    index = getattr(layer_cache, _RING + 'index', None)
-    if index is None or index.device != layer_cache.keys.device:
-        setattr(layer_cache, _RING + 'index', torch.tensor(keep, dtype=torch.int32, device=layer_cache.keys.device))
-    else:
-        index.fill_(keep)
+def _reference_ring_initializer():
+    """The reference's own ring set-up, ``initialize_fixed_memory_swa_physical_ring``
+    (runtime/model/inference_kernels.py:555-598), from the module the
+    reference model imports (``model.inference_kernels``).  A layer cache
+    with the ``_qwen35_swa_physical_ring_*`` fields only exists inside the
+    reference's decode path, where that module is importable; the ring it
+    builds is exactly the layout the kernels here read and write."""
+    import importlib
+    try:
+        return importlib.import_module('model.inference_kernels').initialize_fixed_memory_swa_physical_ring
+    except (ImportError, AttributeError) as e:
+        raise RuntimeError('this layer cache has no physical ring yet, and the reference\'s '
+                           'initialize_fixed_memory_swa_physical_ring (model.inference_kernels) that builds it '
+                           'is not importable') from e
 
 
 def layer_ring_update(layer_cache, key, value, valid):
-    """One decode token into the layer cache's ring (built on first use);
-    returns ``(ring_key, ring_value, ring_valid)`` as the reference does."""
+    """One decode token into the layer cache's ring; returns ``(ring_key,
+    ring_value, ring_valid)`` as the reference does.  A cache without a ring
+    yet gets one from the reference's own initialiser first."""
     require_cuda(key, value, valid)
     if key.shape[-2] != 1 or value.shape[-2] != 1 or valid.shape[-1] != 1:
         raise ValueError('physical SWA ring accepts one token')
     if key.shape != value.shape or key.stride(-1) != 1 or value.stride(-1) != 1:
         raise ValueError('physical SWA ring requires matching contiguous KV heads')
     if not hasattr(layer_cache, _RING + 'index'):
-        initialize_physical_ring(layer_cache)
+        _reference_ring_initializer()(layer_cache)
     return physical_ring_update_(getattr(layer_cache, _RING + 'keys'), getattr(layer_cache, _RING + 'values'),
                                  getattr(layer_cache, _RING + 'valid'), getattr(layer_cache, _RING + 'index'),
                                  key, value, valid)
