@@ -279,9 +279,75 @@ def decode_config(B, world):
         'conv': {'channels': CONV_C, 'kernel': CONV_KS, 'state': 'bf16, in place'},
         'batch_per_gpu': B, 'global_batch': B * world,
         'gdn': {'layers': L_GDN, 'H': H_K, 'HV': H_V, 'K': DK, 'V': DV, 'state': 'fp32, in place'},
-        'memory': {'layers': L_MEM, 'G': MEM_G, 'H': MEM_H, 'D': MEM_D, 'CAP': MEM_CAP, 'chunk': MEM_CHUNK},
+        'memory': {'layers': L_MEM, 'G': MEM_G, 'H': MEM_H, 'D': MEM_D, 'CAP': MEM_CAP, 'chunk': MEM_CHUNK,
+                   'steady_state': f'{MEM_CHUNK + 2} untimed steps fill every bank and pending chunk, then row b '
+                                   f'starts at pending count b % {MEM_CHUNK}: each timed step merges 1 in '
+                                   f'{MEM_CHUNK} rows of every memory layer'},
         'vocab': VOCAB, 'parallelism': f'sequence-sharded x{world}, no collective',
         'l2': 'no flush: 3.2 GB of GDN state per GPU streams through each step (> 126 MB L2)'}
+
+
+def fill_and_stagger(torch, yb, layers, mems, inputs, active, ws, table):
+    """Bring the anchor memory to a steady state before anything is timed:
+    MEM_CHUNK + 2 eager steps fill every pending chunk and commit a bank,
+    then row b's pending count is set to b % MEM_CHUNK (its pending slots
+    hold the entries pushed by those steps).  From then on every step
+    merges the rows whose chunk fills: 1 in MEM_CHUNK of the rows per step,
+    as rows at different prompt lengths do."""
+    for w in range(MEM_CHUNK + 2):
+        decode_step(yb, layers, mems, inputs[w % len(inputs)], active, ws, table)
+    B = active.shape[0]
+    counts = torch.arange(B, device=active.device, dtype=torch.int64) % MEM_CHUNK
+    for st in mems:
+        st.count.copy_(counts)
+    torch.cuda.synchronize()
+
+
+def capture_steps(torch, yb, layers, mems, inputs, active, ws, table, device, extra=None):
+    """One CUDA graph of the decode step per input set (plus `extra()` after
+    the step, if given)."""
+    stream = torch.cuda.current_stream(device)
+    graphs, outs = [], []
+    for x in inputs:
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(device)
+        s.wait_stream(stream)
+        with torch.cuda.stream(s):
+            decode_step(yb, layers, mems, x, active, ws, table)   # pre-capture run on the side stream
+            if extra is not None:
+                extra()
+        stream.wait_stream(s)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g):
+            outs.append(decode_step(yb, layers, mems, x, active, ws, table))
+            if extra is not None:
+                extra()
+        graphs.append(g)
+    return graphs, outs
+
+
+def lockstep_merge_ms(torch, mems, graphs, stream, reps=3):
+    """Time of one step in which every row of every memory layer merges its
+    full pending chunk into its bank (counts set to MEM_CHUNK - 1 before
+    each timed replay)."""
+    total = 0.0
+    for r in range(reps):
+        for st in mems:
+            st.count.fill_(MEM_CHUNK - 1)
+        torch.cuda.synchronize()
+        total += time_events(torch, graphs[r % len(graphs)].replay, 1, stream)
+    return total / reps
+
+
+def step_bytes(B, state_bytes=4):
+    """Algorithmic HBM bytes of one decode step: per GDN layer the conv state
+    read + write and the recurrence's bytes; per memory layer the bank read
+    (2 CAP D 2 B per group), the push and, averaged over the chunk, the
+    merge's bank rewrite; the logits once."""
+    conv = B * CONV_C * CONV_KS * 2 * 2 + B * CONV_C * 2 * 2
+    mem = B * MEM_G * (2 * MEM_CAP * MEM_D * 2 + 2 * MEM_D * 2 + 2 * MEM_CAP * MEM_D * 2 // MEM_CHUNK) \
+        + B * MEM_H * MEM_D * 2 * 2
+    return L_GDN * (conv + gdn_bytes_per_launch(B, state_bytes)) + L_MEM * mem + B * VOCAB * 2
 
 
 def run_gpu(args, rank, world, local_rank, dist):
@@ -294,22 +360,13 @@ def run_gpu(args, rank, world, local_rank, dist):
     layers, mems, inputs, active, ws, table = build_decode(torch, yb, B, device, seed=1234 + rank)
     stream = torch.cuda.current_stream(device)
 
+    # memory in steady state (filled banks, staggered pending counts), then
     # eager warm-up (also loads the library and sets kernel attributes)
+    fill_and_stagger(torch, yb, layers, mems, inputs, active, ws, table)
     for w in range(max(args.warmup, 3)):
         decode_step(yb, layers, mems, inputs[w % len(inputs)], active, ws, table)
     torch.cuda.synchronize()
-    graphs, outs = [], []
-    for x in inputs:
-        g = torch.cuda.CUDAGraph()
-        s = torch.cuda.Stream(device)
-        s.wait_stream(stream)
-        with torch.cuda.stream(s):
-            decode_step(yb, layers, mems, x, active, ws, table)   # pre-capture run on the side stream
-        stream.wait_stream(s)
-        torch.cuda.synchronize()
-        with torch.cuda.graph(g):
-            outs.append(decode_step(yb, layers, mems, x, active, ws, table))
-        graphs.append(g)
+    graphs, outs = capture_steps(torch, yb, layers, mems, inputs, active, ws, table, device)
     for w in range(args.warmup):
         graphs[w % len(graphs)].replay()
     torch.cuda.synchronize()
@@ -333,6 +390,10 @@ def run_gpu(args, rank, world, local_rank, dist):
     if dist is not None:
         ms = shard.max_over_ranks(ms, device=device)
     value = world * B / (ms / 1e3)
+    merge_ms = lockstep_merge_ms(torch, mems, graphs, stream)
+    for st in mems:                                  # back to the staggered counts
+        st.count.copy_(torch.arange(B, device=device, dtype=torch.int64) % MEM_CHUNK)
+    torch.cuda.synchronize()
 
     # ---- dominant kernel alone: the recurrence, CUDA events on its stream ----
     gdn_ms = time_recurrences(torch, yb, layers, inputs[0], stream)
@@ -362,9 +423,7 @@ def run_gpu(args, rank, world, local_rank, dist):
     # still copies its full inputs in and its token ids out inside the timed
     # region; no step's inputs depend on the other group.
     layers_b, mems_b, inputs_b, _, ws_b, table_b = build_decode(torch, yb, B, device, n_inputs=1, seed=4321 + rank)
-    for _ in range(2):
-        decode_step(yb, layers_b, mems_b, inputs_b[0], active, ws_b, table_b)
-    torch.cuda.synchronize()
+    fill_and_stagger(torch, yb, layers_b, mems_b, inputs_b, active, ws_b, table_b)
     g_b = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_b):
         out_b = decode_step(yb, layers_b, mems_b, inputs_b[0], active, ws_b, table_b)
@@ -399,16 +458,23 @@ def run_gpu(args, rank, world, local_rank, dist):
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / n_e2e
     del g_b
+
+    # ---- the host link alone: the same pinned copies with no step ----
+    def h2d_only():
+        for k_, t in host_in.items():
+            inputs[0][k_].copy_(t, non_blocking=True)
+    h2d_only()
+    barrier()
+    h2d_ms = time_events(torch, h2d_only, 5, stream)
     if dist is not None:
         e2e_ms = shard.max_over_ranks(e2e_ms, device=device)
         e2e_serial_ms = shard.max_over_ranks(e2e_serial_ms, device=device)
+        h2d_ms = shard.max_over_ranks(h2d_ms, device=device)
 
     # ---- the reference's opt-in fp16 recurrent-state storage (install_inference(fp16_state=True)) ----
     layers16, mems16, inputs16, _, ws16, table16 = build_decode(torch, yb, B, device, n_inputs=1, seed=99 + rank,
                                                        state_dtype=torch.float16)
-    for _ in range(3):
-        decode_step(yb, layers16, mems16, inputs16[0], active, ws16, table16)
-    torch.cuda.synchronize()
+    fill_and_stagger(torch, yb, layers16, mems16, inputs16, active, ws16, table16)
     g16 = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g16):
         decode_step(yb, layers16, mems16, inputs16[0], active, ws16, table16)
@@ -443,7 +509,15 @@ def run_gpu(args, rank, world, local_rank, dist):
     gsw.replay()
     swa_ms = time_events(torch, gsw.replay, 20, stream) / L_MEM
     swa_bytes = B * SW_KVH * SW_W * SW_D * 2 * 2 + B * SW_QH * SW_D * 2 * 2
-    del gsw, rings
+    del gsw
+    # the whole decode step with the 8 SWA layers in it (ring write + attention after the hot path)
+    gfull, _ = capture_steps(torch, yb, layers, mems, inputs[:1], active, ws, table, device, extra=swa_layers)
+    for _ in range(3):
+        gfull[0].replay()
+    full_ms = time_events(torch, gfull[0].replay, max(5, args.steps // 2), stream)
+    del gfull, rings
+    if dist is not None:
+        full_ms = shard.max_over_ranks(full_ms, device=device)
 
     result = {
         'metric': METRIC, 'value': round(value, 1), 'unit': 'tok/s', 'n_gpus': world, 'steps': args.steps,
@@ -453,8 +527,18 @@ def run_gpu(args, rank, world, local_rank, dist):
         'roofline': {'bound': 'hbm', 'kernel': 'gdn_recurrent_sst_kernel', 'achieved': round(achieved, 1),
                      'peak': hbm, 'unit': 'GB/s', 'frac': round(achieved / hbm, 4), 'peak_kind': peak_kind,
                      'bytes_per_launch': gbytes, 'launch_ms': round(gdn_ms, 5), 'traffic': traffic_per_launch()},
+        'step': {'bytes': step_bytes(B), 'achieved_gbs': round(step_bytes(B) / (ms / 1e3) / 1e9, 1),
+                 'frac_of_hbm': round(step_bytes(B) / (ms / 1e3) / 1e9 / hbm, 4),
+                 'lockstep_merge_ms': round(merge_ms, 4),
+                 'how': 'algorithmic bytes of the whole step (conv, GDN state and activations, memory banks, '
+                        'logits) over its CUDA-event time; lockstep_merge_ms: one step in which every row of '
+                        'every memory layer merges its pending chunk'},
         'e2e': {'value': round(world * B / (e2e_ms / 1e3), 1), 'unit': 'tok/s', 'h2d_bytes_per_step': h2d,
                 'd2h_bytes_per_step': d2h, 'ms_per_step': round(e2e_ms, 4),
+                'h2d_gbs_per_rank': round(h2d / (e2e_ms / 1e3) / 1e9, 2),
+                'h2d_gbs_aggregate': round(world * h2d / (e2e_ms / 1e3) / 1e9, 2),
+                'h2d_only_ms': round(h2d_ms, 4), 'h2d_only_gbs_per_rank': round(h2d / (h2d_ms / 1e3) / 1e9, 2),
+                'h2d_only_gbs_aggregate': round(world * h2d / (h2d_ms / 1e3) / 1e9, 2),
                 'serial_ms_per_step': round(e2e_serial_ms, 4),
                 'serial_value': round(world * B / (e2e_serial_ms / 1e3), 1),
                 'how': 'two independent request groups of B sequences alternate; each step copies its pinned host '
@@ -472,10 +556,159 @@ def run_gpu(args, rank, world, local_rank, dist):
                        '16 query heads over 4 KV heads, D=256, B per GPU, CUDA graph over 8 layers',
                        'achieved_gbs': round(swa_bytes / (swa_ms / 1e3) / 1e9, 1), 'peak': hbm,
                        'frac': round(swa_bytes / (swa_ms / 1e3) / 1e9 / hbm, 4), 'bytes_per_layer': swa_bytes},
+        'decode_with_swa': {'value': round(world * B / (full_ms / 1e3), 1), 'unit': 'tok/s',
+                            'ms_per_step': round(full_ms, 4),
+                            'how': 'the same step with the 8 SWA layers (ring write + attention over W=1024) in '
+                                   'its graph'},
         'gpu_launches': LAUNCHES_PER_STEP * args.steps,
         'clocks': clocks.summary(),
     }
     return result, (layers, mems, inputs)
+
+
+def run_batch_decode(torch, yb, B, device, steps, warmup, hbm, seed):
+    """The decode step at another batch (config 2: B=256), memory in steady
+    state; returns its rate, the recurrence's HBM rate and the whole step's."""
+    layers, mems, inputs, active, ws, table = build_decode(torch, yb, B, device, n_inputs=2, seed=seed)
+    fill_and_stagger(torch, yb, layers, mems, inputs, active, ws, table)
+    graphs, _ = capture_steps(torch, yb, layers, mems, inputs, active, ws, table, device)
+    stream = torch.cuda.current_stream(device)
+    for w in range(warmup):
+        graphs[w % 2].replay()
+    torch.cuda.synchronize()
+    turn = [0]
+
+    def replay():
+        graphs[turn[0] % 2].replay()
+        turn[0] += 1
+    ms = time_events(torch, replay, steps, stream)
+    gdn_ms = time_recurrences(torch, yb, layers, inputs[0], stream)
+    gbytes = gdn_bytes_per_launch(B)
+    del graphs, layers, mems, inputs, table
+    torch.cuda.empty_cache()
+    return {'batch': B, 'value': round(B / (ms / 1e3), 1), 'unit': 'tok/s', 'ms_per_step': round(ms, 4),
+            'steps': steps,
+            'step_gbs': round(step_bytes(B) / (ms / 1e3) / 1e9, 1), 'step_bytes': step_bytes(B),
+            'gdn_kernel': {'achieved': round(gbytes / (gdn_ms / 1e3) / 1e9, 1), 'peak': hbm, 'unit': 'GB/s',
+                           'frac': round(gbytes / (gdn_ms / 1e3) / 1e9 / hbm, 4), 'bytes_per_launch': gbytes,
+                           'launch_ms': round(gdn_ms, 5)},
+            'how': 'config 2: the decode step (24 GDN + 8 memory layers + greedy + bookkeeping) at B=256, '
+                   'fp32 state 12.9 GB, memory in steady state, CUDA-graph replay, CUDA events; the GDN kernel '
+                   'timed over the 24 layers\' own states'}
+
+
+SERVE_REQUESTS, SERVE_MIN_LEN, SERVE_MAX_LEN = 512, 512, 16384
+SERVE_GROUP_TOKENS = 1 << 19        # packed prompt tokens per prefill launch
+
+
+def serve_lengths():
+    """Config 4's prompt lengths: uniform over [512, 16384], seeded (the same on every rank)."""
+    return np.random.default_rng(2024).integers(SERVE_MIN_LEN, SERVE_MAX_LEN + 1, SERVE_REQUESTS)
+
+
+def run_serve(torch, yb, args, rank, world, device, dist):
+    """Config 4 on this rank's share of the 512 requests (split by prompt
+    length with shard.shard_requests, no collective on the data path):
+
+    * prefill: the prompts packed by cu_seqlens in groups of at most
+      SERVE_GROUP_TOKENS tokens, longest first; per group the chunked GDN
+      prefill of all 24 layers (varlen, final states into the decode pool)
+      and the anchor prefill of all 8 memory layers (the group left-padded to
+      its longest prompt, states into the pool); the short convolution's
+      prefill is not packed-varlen here and is left out;
+    * decode: all of the rank's requests as one batch, starting from the
+      states the prefill left (GDN states, banks, pending chunks and counts),
+      `steps` timed steps of the CUDA-graph step.
+
+    Times are CUDA events, max over ranks.  The 32K-token generation is
+    reported as a projection: prefill time + 32768 x the measured step."""
+    from yanchor_b200 import shard
+    bf = torch.bfloat16
+    lengths = serve_lengths()
+    owned = shard.shard_requests(lengths, world)[rank]
+    own = np.array(sorted(owned, key=lambda i: (-int(lengths[i]), i)), dtype=np.int64)   # pool row order
+    own_len = lengths[own].astype(np.int64)
+    groups, cur, tok = [], [], 0
+    for r, n in enumerate(own_len):
+        if cur and tok + n > SERVE_GROUP_TOKENS:
+            groups.append(cur)
+            cur, tok = [], 0
+        cur.append(r)
+        tok += int(n)
+    groups.append(cur)
+    Bd = len(own)
+    layers, mems, inputs, active, ws, table = build_decode(torch, yb, Bd, device, n_inputs=1, seed=555 + rank)
+    gen = torch.Generator(device=device).manual_seed(777 + rank)
+    stream = torch.cuda.current_stream(device)
+
+    def rnd(*shape, dtype=bf):
+        return torch.randn(*shape, generator=gen, device=device).to(dtype)
+    A_log = torch.empty(H_V, device=device).uniform_(1, 16, generator=gen).log()
+    dt_bias = torch.ones(H_V, device=device)
+    prefill_ms = 0.0
+    for grp in groups:
+        r0, r1 = grp[0], grp[-1] + 1
+        lens = own_len[r0:r1]
+        T = int(lens.sum())
+        cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), device=device, dtype=torch.int64)
+        q, k = rnd(1, T, H_K, DK), rnd(1, T, H_K, DK)
+        v = rnd(1, T, H_V, DV)
+        a, b_ = rnd(1, T, H_V, dtype=torch.float32), rnd(1, T, H_V)
+        Tm = int(lens.max())
+        valid = torch.arange(Tm, device=device)[None, :] >= torch.tensor(Tm - lens, device=device)[:, None]
+        mq = rnd(r1 - r0, Tm, MEM_H, MEM_D)
+        msc = (torch.randn(r1 - r0, Tm, MEM_G, generator=gen, device=device) * 2).round() / 2
+        wk, wv = rnd((r1 - r0) * Tm, MEM_G, MEM_D), rnd((r1 - r0) * Tm, MEM_G, MEM_D)
+
+        def writer(bi, ti):
+            rows = bi * Tm + ti
+            return wk.index_select(0, rows), wv.index_select(0, rows)
+
+        def prefill_group():
+            for L in layers:
+                _, s = yb.chunk_gated_delta_rule(q, k, v, a, b_, output_final_state=True,
+                                                 use_qk_l2norm_in_kernel=True, cu_seqlens=cu,
+                                                 use_gate_in_kernel=True, A_log=A_log, dt_bias=dt_bias,
+                                                 use_beta_sigmoid_in_kernel=True)
+                L['state'][r0:r1].copy_(s)
+            for st in mems:
+                view = yb.MemoryState(*(getattr(st, f)[r0:r1] for f in MEMORY_FIELDS))
+                yb.sequence(mq, msc, writer, valid, MEM_CHUNK, view)
+        prefill_ms += time_events(torch, prefill_group, 1, stream)
+        del q, k, v, a, b_, mq, msc, wk, wv
+    torch.cuda.empty_cache()
+    graphs, _ = capture_steps(torch, yb, layers, mems, inputs, active, ws, table, device)
+    for _ in range(3):
+        graphs[0].replay()
+    steps = max(5, args.steps // 4)
+    step_ms = time_events(torch, graphs[0].replay, steps, stream)
+    del graphs, layers, mems, inputs, table
+    torch.cuda.empty_cache()
+    tokens = int(own_len.sum())
+    if dist is not None:
+        prefill_ms = shard.max_over_ranks(prefill_ms, device=device)
+        step_ms = shard.max_over_ranks(step_ms, device=device)
+    total_prompt = int(lengths.sum())
+    job_s = prefill_ms / 1e3 + GEN_TOKENS * step_ms / 1e3
+    return {'requests': SERVE_REQUESTS, 'requests_per_rank': Bd, 'prompt_tokens': total_prompt,
+            'prompt_tokens_rank0': tokens, 'prefill_groups_rank0': len(groups),
+            'prefill_ms': round(prefill_ms, 3),
+            'prefill_tok_s': round(total_prompt / (prefill_ms / 1e3), 1),
+            'prefill_tok_s_per_gpu': round(total_prompt / (prefill_ms / 1e3) / world, 1),
+            'decode_ms_per_step': round(step_ms, 4), 'decode_steps_timed': steps,
+            'decode_tok_s': round(SERVE_REQUESTS / (step_ms / 1e3), 1),
+            'decode_tok_s_per_gpu': round(SERVE_REQUESTS / (step_ms / 1e3) / world, 1),
+            'projected_job_s': round(job_s, 2),
+            'projected_tok_s': round((total_prompt + SERVE_REQUESTS * GEN_TOKENS) / job_s, 1),
+            'how': 'config 4: 512 requests, prompts U[512, 16384] (seeded), split over ranks by prompt tokens '
+                   '(shard.shard_requests); prefill = 24 GDN layers (varlen chunked, cu_seqlens) + 8 anchor '
+                   'prefills per packed group, the short conv left out; decode = all of the rank\'s requests in one '
+                   'CUDA-graph step from the prefill\'s states; times max over ranks; the 32K-token generation '
+                   'projected as prefill + 32768 x step'}
+
+
+MEMORY_FIELDS = ('keys', 'values', 'scores', 'positions', 'pending_keys', 'pending_values', 'pending_scores', 'count',
+                 'total')
 
 
 def traffic_per_launch():
@@ -697,6 +930,134 @@ def cpu_decode_sample(steps=2, B=64, seed=0, warmup=0):
     return B * steps / dt, dt
 
 
+def cpu_model():
+    """The host CPU's model name (Linux /proc/cpuinfo), for the baseline lines."""
+    try:
+        with open('/proc/cpuinfo') as f:
+            for line in f:
+                if line.startswith('model name'):
+                    return line.split(':', 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or 'unknown'
+
+
+REF_ROOT = os.path.join(ROOT, 'baseline', '_ref')
+
+
+def reference_installed():
+    return os.path.exists(os.path.join(REF_ROOT, 'modeling_yanchor.py'))
+
+
+def reference_torch_decode(B, steps, warmup):
+    """The reference's own CPU path for the same decode step, imported from the
+    reference install (baseline/_ref), fp32, all host threads:
+
+    * per GDN layer: ``torch_causal_conv1d_update`` (modeling_yanchor.py:349),
+      the gate expressions of ``Qwen3_5GatedDeltaNet.forward`` (transformers
+      qwen3_5 modeling_qwen3_5.py:500-502), q/k repeated for the 32 value
+      heads, ``torch_recurrent_gated_delta_rule`` (same file :314-353) with
+      the q/k L2 norm, and ``Qwen3_5RMSNormGated`` (:175-190);
+    * per memory layer: ``IndependentGQAMemory._decode`` with the torch
+      backend (modeling_yanchor.py:277-313), pending counts staggered as in
+      the GPU arm;
+    * ``sample_top_k_top_p_counter`` with top_k = 1 (greedy,
+      runtime/model/inference_kernels.py:73-84).
+
+    The per-step slot-table bookkeeping (a few small writes) is left out.
+    Returns (tok/s, seconds for `steps` steps, threads)."""
+    sys.path[:0] = [REF_ROOT, os.path.join(REF_ROOT, 'runtime')]
+    import torch
+    from types import SimpleNamespace
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    from transformers.models.qwen3_5 import modeling_qwen3_5 as qwen
+    import modeling_yanchor as my
+    import model.inference_kernels as ik
+    F = torch.nn.functional
+    gen = torch.Generator().manual_seed(5)
+    rnd = lambda *shape: torch.randn(*shape, generator=gen)  # noqa: E731
+    with torch.no_grad():
+        states = [0.02 * rnd(B, H_V, DK, DV) for _ in range(L_GDN)]
+        conv_states = [rnd(B, CONV_C, CONV_KS) for _ in range(L_GDN)]
+        conv_w = 0.5 * rnd(CONV_C, CONV_KS)
+        A_log = torch.empty(H_V).uniform_(1, 16, generator=gen).log()
+        dt_bias = torch.ones(H_V)
+        norm = qwen.Qwen3_5RMSNormGated(DV, eps=1e-6)
+        mems = []
+        for _ in range(L_MEM):
+            st = my.IndependentMemoryState.empty(B, MEM_G, MEM_CAP, MEM_CHUNK, MEM_D, 'cpu', torch.float32)
+            st.pending_keys.copy_(rnd(*st.pending_keys.shape))
+            st.pending_values.copy_(rnd(*st.pending_values.shape))
+            st.pending_scores.copy_(rnd(*st.pending_scores.shape))
+            st.count.copy_(torch.arange(B) % MEM_CHUNK)
+            st.total.copy_(torch.arange(B) % MEM_CHUNK)
+            mems.append(st)
+        ns = SimpleNamespace(backend='torch', capacity=MEM_CAP, groups=MEM_G, heads=MEM_H, dim=MEM_D)
+        valid = torch.ones(B, 1, dtype=torch.bool)
+        attempt = torch.arange(B)
+        rep = H_V // H_K
+
+        def inputs():
+            return dict(mixed=rnd(L_GDN, B, CONV_C, 1), a=rnd(L_GDN, B, 1, H_V), b=rnd(L_GDN, B, 1, H_V),
+                        z=rnd(L_GDN, B, 1, H_V, DV), mq=rnd(L_MEM, B, 1, MEM_H, MEM_D),
+                        mk=rnd(L_MEM, B, 1, MEM_G, MEM_D), mv=rnd(L_MEM, B, 1, MEM_G, MEM_D),
+                        ms=rnd(L_MEM, B, 1, MEM_G), logits=3 * rnd(B, VOCAB))
+        xs = [inputs() for _ in range(warmup + steps)]
+        t0 = time.perf_counter()
+        for it, x in enumerate(xs):
+            if it == warmup:
+                t0 = time.perf_counter()
+            for i in range(L_GDN):
+                y = my.torch_causal_conv1d_update(x['mixed'][i], conv_states[i], conv_w, None, 'silu')[:, :, 0]
+                q = y[:, None, :H_K * DK].reshape(B, 1, H_K, DK).repeat_interleave(rep, dim=2)
+                k = y[:, None, H_K * DK:2 * H_K * DK].reshape(B, 1, H_K, DK).repeat_interleave(rep, dim=2)
+                v = y[:, None, 2 * H_K * DK:].reshape(B, 1, H_V, DV)
+                beta = x['b'][i].sigmoid()
+                g = -A_log.float().exp() * F.softplus(x['a'][i].float() + dt_bias)
+                o, states[i] = qwen.torch_recurrent_gated_delta_rule(q, k, v, g, beta, initial_state=states[i],
+                                                                     output_final_state=True,
+                                                                     use_qk_l2norm_in_kernel=True)
+                norm(o.reshape(-1, DV), x['z'][i].reshape(-1, DV))
+            for j, st in enumerate(mems):
+                my.IndependentGQAMemory._decode(ns, x['mq'][j], x['mk'][j], x['mv'][j], x['ms'][j], valid,
+                                                MEM_CHUNK, st)
+            ik.sample_top_k_top_p_counter(x['logits'], attempt, it, seed=0, temperature=1.0, top_k=1, top_p=1.0)
+        dt = time.perf_counter() - t0
+    return B * steps / dt, dt, threads
+
+
+def cpu_sample_line(B, steps, warmup):
+    """The CPU baseline sample as a dict: the reference's own torch path when
+    the reference is installed here, else the numpy restatement (oracle/)."""
+    if reference_installed():
+        value, dt, threads = reference_torch_decode(B, steps, warmup)
+        return {'value': round(value, 3), 'unit': 'tok/s', 'cores': threads, 'kind': 'reference',
+                'cpu': cpu_model(),
+                'sample': f'{steps} full decode steps (after {warmup} untimed) at B={B} through the reference\'s '
+                          f'own torch path from baseline/_ref (conv update, gates, torch_recurrent_gated_delta_rule, '
+                          f'Qwen3_5RMSNormGated, IndependentGQAMemory._decode torch backend, greedy sampler), fp32, '
+                          f'{threads} torch threads, {dt:.1f} s'}, dt
+    value, dt, cores = cpu_decode_parallel(steps=steps, B=B, warmup=warmup)
+    return {'value': round(value, 3), 'unit': 'tok/s', 'cores': cores, 'kind': 'port', 'cpu': cpu_model(),
+            'sample': f'{steps} full decode steps (after {warmup} untimed) at B={B} through the numpy restatement of '
+                      f'the reference algorithm (oracle/), rows split over {cores} worker processes (one thread '
+                      f'each), slowest worker {dt:.1f} s'}, dt
+
+
+def cpu_sample_subprocess(B, steps, warmup):
+    """cpu_sample_line in a fresh interpreter (no CUDA context, its own
+    sys.path and thread settings)."""
+    import subprocess
+    res = subprocess.run([sys.executable, os.path.join(ROOT, 'bench.py'), '--cpu-sample', str(B), str(steps),
+                          str(warmup)], capture_output=True, text=True, timeout=900)
+    for line in res.stdout.splitlines()[::-1]:
+        if line.startswith('{'):
+            return json.loads(line)
+    raise RuntimeError(f'CPU sample failed: {res.stderr[-2000:]}')
+
+
 def _cpu_worker(job):
     steps, B, seed, warmup = job
     if ROOT not in sys.path:
@@ -737,10 +1098,13 @@ def main():
     ap.add_argument('--impl', default='yanchor_b200', choices=['yanchor_b200', 'reference'])
     ap.add_argument('--no-prefill', action='store_true')
     ap.add_argument('--no-cpu', action='store_true')
+    ap.add_argument('--no-serve', action='store_true', help='skip the config-4 serving sweep')
+    ap.add_argument('--no-b256', action='store_true', help='skip the config-2 batch (B=256)')
     ap.add_argument('--only', choices=['conv_update', 'gdn_decode', 'gdn_fused', 'gdn_chunk', 'mem_read', 'mem_commit', 'mem_indexed', 'mem_topk',
                                        'mem_sequence', 'swa', 'swa_prefill', 'greedy',
                                        'topk'], help='run one kernel family (small ncu captures)')
     ap.add_argument('--prefill-batch', type=int, default=8)
+    ap.add_argument('--cpu-sample', nargs=3, type=int, metavar=('B', 'STEPS', 'WARMUP'), help=argparse.SUPPRESS)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get('WORLD_SIZE', '1'))
@@ -748,6 +1112,10 @@ def main():
     local_rank = int(os.environ.get('LOCAL_RANK', '0'))
     sys.path.insert(0, ROOT)
 
+    if args.cpu_sample:
+        line, _ = cpu_sample_line(*args.cpu_sample)
+        print(json.dumps(line), flush=True)
+        return
     if args.only:
         run_only(args)
         return
@@ -755,20 +1123,16 @@ def main():
         if rank != 0:
             return
         steps = max(1, min(args.steps, 3))
-        warm = min(args.warmup, 3)              # untimed steps first, bounded like the timed ones
-        rows = args.batch * args.gpus            # the arm's global batch, on the host cores
-        value, dt, cores = cpu_decode_parallel(steps=steps, B=rows, warmup=warm)
-        line = {'metric': METRIC, 'value': round(value, 3), 'unit': 'tok/s', 'n_gpus': args.gpus, 'steps': steps,
+        warm = min(args.warmup, 1)              # untimed steps first, bounded like the timed ones
+        rows = args.batch                        # one GPU's batch: the host's rate on this step
+        base, dt = cpu_sample_line(rows, steps, warm)
+        line = {'metric': METRIC, 'value': base['value'], 'unit': 'tok/s', 'n_gpus': args.gpus, 'steps': steps,
                 'warmup': warm, 'ms_per_step': round(dt / steps * 1e3, 1), 'higher_is_better': True,
                 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'fp32', 'data': 'synthetic (random init, seeded)',
                 'impl': 'reference',
                 'config': decode_config(args.batch, args.gpus),
-                'cpu_baseline': {'value': round(value, 3), 'unit': 'tok/s', 'cores': cores, 'kind': 'port',
-                                 'sample': f'{steps} full decode steps (after {warm} untimed) at B={rows} through the numpy '
-                                           f'restatement of the reference algorithm (oracle/), rows split over '
-                                           f'{cores} worker processes (one thread each), slowest worker '
-                                           f'{dt:.1f} s'},
-                'e2e': {'value': round(value, 3), 'unit': 'tok/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
+                'cpu_baseline': base,
+                'e2e': {'value': base['value'], 'unit': 'tok/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
         print(json.dumps(line), flush=True)
         return
 
@@ -781,18 +1145,23 @@ def main():
         tdist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120))
         dist = tdist
     result, _ = run_gpu(args, rank, world, local_rank, dist)
+    import torch
+    import yanchor_b200 as yb
+    hbm, tf_burst, tf_sust, peak_kind = peaks()
+    device = torch.device('cuda', local_rank)
+    if not args.no_serve:
+        serve = run_serve(torch, yb, args, rank, world, device, dist)
+        if rank == 0:
+            result['serve'] = serve
     if rank == 0:
-        import torch
-        import yanchor_b200 as yb
-        hbm, tf_burst, tf_sust, peak_kind = peaks()
+        if world == 1 and not args.no_b256:
+            result['decode_b256'] = run_batch_decode(torch, yb, 256, device, max(10, args.steps // 4), args.warmup,
+                                                     hbm, seed=256)
         if not args.no_prefill:
-            result['prefill'] = run_prefill(torch, yb, torch.device('cuda', local_rank), hbm, tf_burst, peak_kind)
+            result['prefill'] = run_prefill(torch, yb, device, hbm, tf_burst, peak_kind)
         if world == 1 and not args.no_cpu:
-            value, dt, cores = cpu_decode_parallel(steps=2, B=args.batch, warmup=1)
-            result['cpu_baseline'] = {'value': round(value, 3), 'unit': 'tok/s', 'cores': cores, 'kind': 'port',
-                                      'sample': f'2 full decode steps (after 1 untimed) at B={args.batch} through the numpy '
-                                                f'restatement (oracle/), rows split over {cores} worker '
-                                                f'processes (one thread each), slowest worker {dt:.1f} s'}
+            result['cpu_baseline'], _ = cpu_sample_line(args.batch, 2, 1) if not reference_installed() else \
+                (cpu_sample_subprocess(args.batch, 2, 1), None)
         print(json.dumps(result), flush=True)
     if dist is not None:
         dist.barrier()

@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(NT) gdn_chunk_simt_kernel(const ChunkParams p)
         gl = load_scalar(p.g, tok * p.g_ts + hv, p.g_dtype);
         if (gate_in) gl = -expf(p.A_log[hv]) * softplus20(gl + (p.dt_bias ? p.dt_bias[hv] : 0.f));
         b = load_scalar(p.beta, tok * p.beta_ts + hv, p.beta_dtype);
-        if (beta_sig) b = sigmoidf_(b);
+        if (beta_sig) b = round_to<TIO>(sigmoidf_(b));   // beta in the input dtype, as the reference stores it
       }
       sm.G[tid] = gl;
       sm.bet[tid] = b;

@@ -342,7 +342,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           gl = load_scalar(p.g, tok * p.g_ts + hv, p.g_dtype);
           if (gate_in) gl = a_coef * softplus20(gl + dtb);
           b = load_scalar(p.beta, tok * p.beta_ts + hv, p.beta_dtype);
-          if (beta_sig) b = sigmoidf_(b);
+          if (beta_sig) b = round_to<__nv_bfloat16>(sigmoidf_(b));   // beta in the input dtype, as the reference stores it
         }
         gv[half] = gl;
         bv[half] = b;

@@ -179,7 +179,7 @@ __global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(const RecParams
         if (gate_in) gl = -expf(p.A_log[hv]) * softplus20(gl + (p.dt_bias ? p.dt_bias[hv] : 0.f));
         float b = load_scalar(p.beta, tok * p.beta_ts + hv, p.beta_dtype);
         s_decay = expf(gl);
-        s_beta = beta_sig ? sigmoidf_(b) : b;
+        s_beta = beta_sig ? round_to<TIO>(sigmoidf_(b)) : b;   // sigmoid(b) in the input dtype, as the reference stores beta
       }
     }
     __syncthreads();
@@ -410,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, sizeof(TS) == 4 ? 3 : 4) gdn_recurre
         if (gate_in) gl = -expf(p.A_log[hv]) * softplus20(gl + (p.dt_bias ? p.dt_bias[hv] : 0.f));
         float b = load_scalar(p.beta, tok * p.beta_ts + hv, p.beta_dtype);
         s_decay = expf(gl);
-        s_beta = beta_sig ? sigmoidf_(b) : b;
+        s_beta = beta_sig ? round_to<TIO>(sigmoidf_(b)) : b;   // sigmoid(b) in the input dtype, as the reference stores beta
       }
     }
     __syncthreads();
