@@ -216,6 +216,7 @@ def test_decode_gates_and_norm_in_kernel(yb):
         dt_bias=cuda(dt_bias), use_beta_sigmoid_in_kernel=True, z=cuda(z, bf), norm_weight=cuda(w, bf))
     g, beta = ogdn.gdn_gates(a, host(cuda(blog, bf)), A_log, dt_bias, dtype=np.float64)
     rb = lambda x: host(cuda(x, bf))  # noqa: E731
+    beta = rb(beta.astype(np.float32))   # beta = sigmoid(b) is stored in the input dtype (modeling_qwen3_5.py:500)
     eo, es = ogdn.recurrent_gated_delta_rule(rb(q), rb(k), rb(v), g, beta, initial_state=h0, use_qk_l2norm=True,
                                              dtype=np.float64)
     en = ogdn.rmsnorm_gated(eo, rb(z), rb(w), dtype=np.float64)

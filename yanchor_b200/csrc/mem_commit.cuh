@@ -27,6 +27,15 @@ __device__ __forceinline__ bool cand_before(float sa, int64_t pa, int ia, float 
   return ia < ib;
 }
 
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+               "l"(gsrc)
+               : "memory");
+}
+
+// The winning rows (bank slot or pending slot per new bank slot) into `stage`, then back over the
+// bank.  With 16-byte aligned rows every piece is fetched by cp.async, all of them in flight at
+// once, so the gather costs about one memory latency instead of one per piece a thread handles.
 template <typename T>
 __device__ void commit_gather(T *bank, const T *pend, T *stage, const int *sel, const int64_t *pkey, int g,
                               int CAP, int PC, int D) {
@@ -34,15 +43,16 @@ __device__ void commit_gather(T *bank, const T *pend, T *stage, const int *sel, 
   constexpr int VEC = 16 / int(sizeof(T));
   const bool vec = (D % VEC) == 0 && (reinterpret_cast<uintptr_t>(bank) % 16) == 0 &&
                    (reinterpret_cast<uintptr_t>(pend) % 16) == 0;
-  if (vec) {   // 16-byte pieces of the winning rows
+  if (vec) {
     const int DV = D / VEC;
     for (int e = tid; e < CAP * DV; e += nt) {
       const int r = e / DV, d = (e % DV) * VEC;
       const int c = sel[r];
       const int src = pkey[c] == INT64_MAX ? 0 : c;
       const T *from = src < CAP ? bank + (int64_t(g) * CAP + src) * D : pend + (int64_t(g) * PC + src - CAP) * D;
-      *reinterpret_cast<uint4 *>(stage + r * D + d) = *reinterpret_cast<const uint4 *>(from + d);
+      cp_async16(stage + r * D + d, from + d);
     }
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
     __syncthreads();
     for (int e = tid; e < CAP * DV; e += nt)
       *reinterpret_cast<uint4 *>(bank + int64_t(g) * CAP * D + e * VEC) = *reinterpret_cast<const uint4 *>(stage + e * VEC);

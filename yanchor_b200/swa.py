@@ -164,7 +164,9 @@ def reference_swa(q, k, v, *, window, key_valid=None, query_start=0):
 
 def flash_swa(q, k, v, *, window, attention_mask):
     """The prefill SWA of the CUDA path, modeling_yanchor.py:429-449: causal
-    window of ``window`` tokens; with ``attention_mask`` ([B, >= T], the last T
+    window of ``window`` tokens, the queries aligned to the last keys as
+    FlashAttention aligns them (a decode query over a cached window attends
+    to the window's last ``window`` keys); with ``attention_mask`` ([B, >= T], the last T
     columns belong to this prompt) over each row's valid tokens in order, as
     the reference's unpad / variable-length FlashAttention call does, padded
     positions giving zeros.  Rows whose valid tokens form one run (left or
@@ -172,7 +174,11 @@ def flash_swa(q, k, v, *, window, attention_mask):
     scattered back."""
     require_cuda(q, k, v)
     if attention_mask is None:
-        return reference_swa(q, k, v, window=window)
+        # FlashAttention's causal mask is aligned to the end of the keys: the
+        # last query sits at the last key (a decode query over a cached window)
+        return reference_swa(q, k, v, window=window, query_start=k.shape[1] - q.shape[1])
+    if k.shape[1] != q.shape[1]:
+        raise ValueError('flash_swa with an attention mask needs as many keys as queries')
     B, T = q.shape[:2]
     mask = attention_mask[:, -T:].to(device=q.device, dtype=torch.bool)
     m8 = mask.to(torch.int8)
