@@ -856,6 +856,18 @@ def run_only(args):
             st = yb.MemoryState.empty(8, MEM_G, MEM_CAP, MEM_CHUNK, MEM_D, dev, bf)
             yb.sequence(mq, msc, writer, None, MEM_CHUNK, st)
         fn = (lambda: yb.exclusive_prefix_topk(psc, ppos, ppos, 64)) if args.only == 'mem_topk' else seq
+    elif args.only in ('mem_step', 'mem_step_merge'):
+        # one memory layer's decode step (read + commit, one launch) on a full bank: pending counts
+        # staggered over the chunk (1 in MEM_CHUNK rows merges per call), or every row merging
+        for _ in range(MEM_CHUNK + 2):
+            yb.memory_decode_step(x['mq'][0], x['mk'][0], x['mv'][0], x['ms'][0], active, MEM_CHUNK, st)
+        st.count.copy_(torch.arange(B, device=dev) % MEM_CHUNK)
+        torch.cuda.synchronize()
+
+        def fn():
+            if args.only == 'mem_step_merge':
+                st.count.fill_(MEM_CHUNK - 1)
+            yb.memory_decode_step(x['mq'][0], x['mk'][0], x['mv'][0], x['ms'][0], active, MEM_CHUNK, st)
     else:
         q0, k0, v0 = conv_qkv(yb, L0, x['mixed'][0])
         fns = {
@@ -1100,7 +1112,8 @@ def main():
     ap.add_argument('--no-cpu', action='store_true')
     ap.add_argument('--no-serve', action='store_true', help='skip the config-4 serving sweep')
     ap.add_argument('--no-b256', action='store_true', help='skip the config-2 batch (B=256)')
-    ap.add_argument('--only', choices=['conv_update', 'gdn_decode', 'gdn_fused', 'gdn_chunk', 'mem_read', 'mem_commit', 'mem_indexed', 'mem_topk',
+    ap.add_argument('--only', choices=['conv_update', 'gdn_decode', 'gdn_fused', 'gdn_chunk', 'mem_read', 'mem_commit',
+                                       'mem_step', 'mem_step_merge', 'mem_indexed', 'mem_topk',
                                        'mem_sequence', 'swa', 'swa_prefill', 'greedy',
                                        'topk'], help='run one kernel family (small ncu captures)')
     ap.add_argument('--prefill-batch', type=int, default=8)

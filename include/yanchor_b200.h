@@ -164,7 +164,12 @@ int yb_swa_decode_attention(const void *query, const void *ring_key, const void 
  * Activations are token-major with channels contiguous: x, out [B, T, C]
  * (the memory of the reference's [B, C, T] transposed view), given by batch
  * and token strides in elements.  State [B, C, W], W = KS (the cache's
- * convention) or KS - 1 (`initial_states` of the causal-conv1d package);
+ * convention) or KS - 1 (`initial_states` of the causal-conv1d package),
+ * given by batch, channel and tap strides in elements: packed rows (W, 1),
+ * or channels contiguous with taps C apart (1, C), which is how the
+ * reference's cache holds it after padding the transposed projection
+ * (transformers qwen3_5 modeling_qwen3_5.py:466-467); any layout whose
+ * (channel, tap) elements do not overlap is accepted;
  * its last KS - 1 entries are the inputs before t = 0.  weight [C, KS] and
  * bias [C] (or NULL) are fp32.  KS in {2, 3, 4}.
  *
@@ -180,13 +185,14 @@ int yb_swa_decode_attention(const void *query, const void *ring_key, const void 
  * qwen3_5 modeling_qwen3_5.py:462-480 (`causal_conv1d_fn` / `conv1d`).
  */
 int yb_conv1d_update(const void *x, int64_t x_batch_stride, void *conv_state, int64_t state_batch_stride,
-                     int64_t state_width, const float *weight, const float *bias, void *out,
-                     int64_t out_batch_stride, int64_t B, int64_t C, int64_t KS, int silu, int dtype,
-                     void *stream);
+                     int64_t state_channel_stride, int64_t state_tap_stride, int64_t state_width,
+                     const float *weight, const float *bias, void *out, int64_t out_batch_stride, int64_t B,
+                     int64_t C, int64_t KS, int silu, int dtype, void *stream);
 int yb_conv1d_fwd(const void *x, int64_t x_batch_stride, int64_t x_token_stride, const void *initial_state,
-                  void *final_state, int64_t state_batch_stride, int64_t state_width, const float *weight,
-                  const float *bias, void *out, int64_t out_batch_stride, int64_t out_token_stride, int64_t B,
-                  int64_t T, int64_t C, int64_t KS, int silu, int dtype, void *stream);
+                  void *final_state, int64_t state_batch_stride, int64_t state_channel_stride,
+                  int64_t state_tap_stride, int64_t state_width, const float *weight, const float *bias, void *out,
+                  int64_t out_batch_stride, int64_t out_token_stride, int64_t B, int64_t T, int64_t C, int64_t KS,
+                  int silu, int dtype, void *stream);
 
 /*
  * Chunked (64-token WY/UT transform) gated delta rule for prefill.

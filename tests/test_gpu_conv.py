@@ -91,3 +91,41 @@ def test_prefill_yanchor_shape(yb, width, T):
     np.testing.assert_allclose(host(y), ey, atol=2e-2, rtol=2e-2)
     np.testing.assert_array_equal(host(st), est[:, :, KS - width:].astype(np.float32))
     assert y.shape == (B, C, T) and y.transpose(1, 2).is_contiguous()
+
+
+@pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float32])
+def test_state_in_the_reference_cache_layout(yb, dtype):
+    """The reference's cache keeps the conv state as F.pad of the transposed
+    projection (transformers qwen3_5 modeling_qwen3_5.py:466-467): channels
+    contiguous, taps C apart.  Prefill writing that state and decode steps
+    updating it in place give the same outputs and states as the packed
+    layout, and the oracle's."""
+    rng = np.random.default_rng(31)
+    B, C, KS, T = 3, 1024, 4, 37
+    w = (0.5 * rng.standard_normal((C, KS))).astype(np.float32)
+    xp = rng.standard_normal((B, C, T)).astype(np.float32)
+    mixed = token_major(xp, dtype)
+    # the cache's state: the last KS inputs, in the transposed projection's memory layout
+    ref_state = torch.nn.functional.pad(mixed, (KS - T, 0))
+    assert ref_state.stride(1) == 1 and ref_state.stride(2) == C
+    packed = ref_state.contiguous()
+    y_ref = yb.causal_conv1d_fn(mixed, cuda(w), activation='silu')
+    ey, est = oconv.conv_fwd(host(mixed), w)
+    assert np.abs(host(y_ref) - ey).max() <= (1e-5 if dtype == torch.float32 else 2e-2)
+    for t in range(5):
+        x1 = token_major(rng.standard_normal((B, C, 1)).astype(np.float32), dtype)
+        y_a = yb.causal_conv1d_update(x1, ref_state, cuda(w), None, 'silu')
+        y_b = yb.causal_conv1d_update(x1, packed, cuda(w), None, 'silu')
+        assert torch.equal(y_a, y_b), t
+        assert torch.equal(ref_state, packed), t
+        ey1, est = oconv.conv_update(host(x1), est, w)
+        assert np.abs(host(y_a) - ey1).max() <= (1e-5 if dtype == torch.float32 else 2e-2)
+    np.testing.assert_array_equal(host(ref_state), est.astype(np.float32))
+    # a prefill continuing from / writing a state in that layout
+    init = ref_state.clone()
+    fin = torch.nn.functional.pad(torch.zeros_like(mixed), (KS - T, 0))
+    y2, _ = yb.causal_conv1d_fn(mixed, cuda(w), initial_states=init, return_final_states=True,
+                                final_states_out=fin, activation='silu')
+    y3, fin_p = yb.causal_conv1d_fn(mixed, cuda(w), initial_states=init.contiguous(), return_final_states=True,
+                                    activation='silu')
+    assert torch.equal(y2, y3) and torch.equal(fin, fin_p)

@@ -54,8 +54,10 @@ SIGNATURES = {
     'yb_swa_decode_workspace_bytes': (_I64, [_I64, _I64, _I64, _I64, _I64]),
     'yb_swa_decode_attention': (_I, [_P, _P, _P, _I64, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I64, _I, _P, _I64,
                                      _P]),
-    'yb_conv1d_update': (_I, [_P, _I64, _P, _I64, _I64, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _I, _P]),
-    'yb_conv1d_fwd': (_I, [_P, _I64, _I64, _P, _P, _I64, _I64, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I,
+    'yb_conv1d_update': (_I, [_P, _I64, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _I,
+                              _P]),
+    'yb_conv1d_fwd': (_I, [_P, _I64, _I64, _P, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _I64, _I64, _I64, _I64, _I64,
+                           _I64, _I,
                            _I, _P]),
     'yb_mem_select_topk': (_I, [_P, _P, _I, _P, _I64, _I64, _I64, _P, _P, _P, _P]),
     'yb_mem_exclusive_prefix_topk': (_I, [_P, _P, _I, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _I, _P, _P, _P, _P,

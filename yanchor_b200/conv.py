@@ -46,6 +46,16 @@ def _token_major(x):
     return x
 
 
+def _state_strides(st):
+    """A conv state [B, C, W] may have any layout whose (channel, tap)
+    elements do not overlap: packed per row (the kernels' fast path) or, as
+    the reference's cache keeps it after padding a transposed projection,
+    channels contiguous with taps C apart."""
+    cs, ts = st.stride(1), st.stride(2)
+    if cs < 1 or ts < 1 or not (cs >= st.shape[2] * ts or ts >= st.shape[1] * cs):
+        raise ValueError('conv_state channel and tap strides overlap')
+
+
 def causal_conv1d_update(x, conv_state, weight, bias=None, activation=None):
     """One token: x [B, C, 1] (or [B, C]); conv_state [B, C, W] updated in
     place (shifted left, the input appended); returns the output, shaped and
@@ -62,14 +72,14 @@ def causal_conv1d_update(x, conv_state, weight, bias=None, activation=None):
         raise ValueError('conv_state must be [B, C, KS] (or [B, C, KS - 1])')
     if conv_state.dtype != x3.dtype:
         raise TypeError('conv_state and x must share a dtype')
-    if conv_state.stride(2) != 1 or conv_state.stride(1) != conv_state.shape[2]:
-        raise ValueError('conv_state must be contiguous inside each batch row')
+    _state_strides(conv_state)
     xin = x3 if x3.stride(1) == 1 else x3.contiguous()
     out = torch.empty((B, C, 1), device=x3.device, dtype=x3.dtype)
     b = None if bias is None else bias.to(torch.float32).contiguous()
     rc = _lib.lib().yb_conv1d_update(xin.data_ptr(), xin.stride(0), conv_state.data_ptr(), conv_state.stride(0),
-                                     conv_state.shape[2], w.data_ptr(), ptr(b), out.data_ptr(), out.stride(0), B, C,
-                                     KS, _silu(activation), dtype_code(x3), stream_ptr(x3.device))
+                                     conv_state.stride(1), conv_state.stride(2), conv_state.shape[2], w.data_ptr(),
+                                     ptr(b), out.data_ptr(), out.stride(0), B, C, KS, _silu(activation),
+                                     dtype_code(x3), stream_ptr(x3.device))
     _lib.check(rc, 'causal_conv1d_update')
     return out[:, :, 0] if squeeze else out
 
@@ -94,21 +104,23 @@ def causal_conv1d_fn(x, weight, bias=None, seq_idx=None, initial_states=None, re
         if st is not None:
             if st.dim() != 3 or st.shape[:2] != (B, C) or st.shape[2] not in (KS, KS - 1):
                 raise ValueError('conv states must be [B, C, KS - 1] (or [B, C, KS])')
-            if st.dtype != x.dtype or st.stride(2) != 1 or st.stride(1) != st.shape[2]:
-                raise ValueError('conv states must share x dtype and be contiguous inside each batch row')
+            if st.dtype != x.dtype:
+                raise ValueError('conv states must share the dtype of x')
+            _state_strides(st)
             W = st.shape[2]
     if initial_states is not None and final_states_out is not None and \
             (initial_states.shape[2] != final_states_out.shape[2] or
-             initial_states.stride(0) != final_states_out.stride(0)):
-        raise ValueError('initial and final states must share width and batch stride')
+             initial_states.stride() != final_states_out.stride()):
+        raise ValueError('initial and final states must share width and strides')
     if return_final_states and final_states_out is None:
         final_states_out = torch.empty((B, C, W), device=x.device, dtype=x.dtype)
     out = torch.empty((B, T, C), device=x.device, dtype=x.dtype).transpose(1, 2)
     b = None if bias is None else bias.to(torch.float32).contiguous()
-    st_stride = (initial_states if initial_states is not None else final_states_out).stride(0) \
-        if (initial_states is not None or final_states_out is not None) else 0
+    st = initial_states if initial_states is not None else final_states_out
+    st_strides = st.stride() if st is not None else (0, W, 1)
     rc = _lib.lib().yb_conv1d_fwd(x.data_ptr(), x.stride(0), x.stride(2), ptr(initial_states),
-                                  ptr(final_states_out), st_stride, W, w.data_ptr(), ptr(b), out.data_ptr(),
+                                  ptr(final_states_out), st_strides[0], st_strides[1], st_strides[2], W, w.data_ptr(),
+                                  ptr(b), out.data_ptr(),
                                   out.stride(0), out.stride(2), B, T, C, KS, _silu(activation), dtype_code(x),
                                   stream_ptr(x.device))
     _lib.check(rc, 'causal_conv1d_fn')

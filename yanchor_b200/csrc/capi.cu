@@ -335,18 +335,22 @@ int yb_swa_decode_attention(const void *query, const void *ring_key, const void 
 }
 
 int yb_conv1d_update(const void *x, int64_t x_batch_stride, void *conv_state, int64_t state_batch_stride,
-                     int64_t state_width, const float *weight, const float *bias, void *out,
-                     int64_t out_batch_stride, int64_t B, int64_t C, int64_t KS, int silu, int dtype,
-                     void *stream) {
+                     int64_t state_channel_stride, int64_t state_tap_stride, int64_t state_width,
+                     const float *weight, const float *bias, void *out, int64_t out_batch_stride, int64_t B,
+                     int64_t C, int64_t KS, int silu, int dtype, void *stream) {
   YB_REQUIRE(dtype_ok(dtype), "conv1d_update: bad dtype");
   YB_REQUIRE(B >= 0 && C >= 0 && KS >= 2 && KS <= 8 && (state_width == KS || state_width == KS - 1),
              "conv1d_update: bad sizes (state width must be KS or KS - 1)");
+  YB_REQUIRE(state_channel_stride >= 1 && state_tap_stride >= 1 &&
+             (state_channel_stride >= state_width * state_tap_stride || state_tap_stride >= C * state_channel_stride),
+             "conv1d_update: state channel / tap strides overlap");
   YB_REQUIRE(B <= 1 || (x_batch_stride >= C && out_batch_stride >= C && state_batch_stride >= C * state_width),
              "conv1d_update: batch strides too small");   // (a size-1 axis may carry any stride)
   YB_REQUIRE(B * C == 0 || (x && conv_state && weight && out), "conv1d_update: null tensor");
   ConvArgs a{};
   a.x = x; a.x_bs = x_batch_stride; a.x_ts = 0;
   a.state = conv_state; a.state_bs = state_batch_stride; a.W = state_width;
+  a.state_cs = state_channel_stride; a.state_ts = state_tap_stride;
   a.weight = weight; a.bias = bias; a.out = out; a.out_bs = out_batch_stride; a.out_ts = 0;
   a.B = B; a.T = 1; a.C = C; a.KS = KS; a.silu = silu != 0; a.dtype = dtype;
   a.stream = static_cast<cudaStream_t>(stream);
@@ -354,12 +358,16 @@ int yb_conv1d_update(const void *x, int64_t x_batch_stride, void *conv_state, in
 }
 
 int yb_conv1d_fwd(const void *x, int64_t x_batch_stride, int64_t x_token_stride, const void *initial_state,
-                  void *final_state, int64_t state_batch_stride, int64_t state_width, const float *weight,
-                  const float *bias, void *out, int64_t out_batch_stride, int64_t out_token_stride, int64_t B,
-                  int64_t T, int64_t C, int64_t KS, int silu, int dtype, void *stream) {
+                  void *final_state, int64_t state_batch_stride, int64_t state_channel_stride,
+                  int64_t state_tap_stride, int64_t state_width, const float *weight, const float *bias, void *out,
+                  int64_t out_batch_stride, int64_t out_token_stride, int64_t B, int64_t T, int64_t C, int64_t KS,
+                  int silu, int dtype, void *stream) {
   YB_REQUIRE(dtype_ok(dtype), "conv1d_fwd: bad dtype");
   YB_REQUIRE(B >= 0 && T >= 0 && C >= 0 && KS >= 2 && KS <= 8 && (state_width == KS || state_width == KS - 1),
              "conv1d_fwd: bad sizes (state width must be KS or KS - 1)");
+  YB_REQUIRE(state_channel_stride >= 1 && state_tap_stride >= 1 &&
+             (state_channel_stride >= state_width * state_tap_stride || state_tap_stride >= C * state_channel_stride),
+             "conv1d_fwd: state channel / tap strides overlap");
   YB_REQUIRE(T <= 1 || (x_token_stride >= C && out_token_stride >= C), "conv1d_fwd: token strides too small");
   YB_REQUIRE(B <= 1 || (!initial_state && !final_state) || state_batch_stride >= C * state_width,
              "conv1d_fwd: state batch stride too small");
@@ -367,6 +375,7 @@ int yb_conv1d_fwd(const void *x, int64_t x_batch_stride, int64_t x_token_stride,
   ConvArgs a{};
   a.x = x; a.x_bs = x_batch_stride; a.x_ts = x_token_stride;
   a.state_in = initial_state; a.state_out = final_state; a.state_bs = state_batch_stride; a.W = state_width;
+  a.state_cs = state_channel_stride; a.state_ts = state_tap_stride;
   a.weight = weight; a.bias = bias; a.out = out; a.out_bs = out_batch_stride; a.out_ts = out_token_stride;
   a.B = B; a.T = T; a.C = C; a.KS = KS; a.silu = silu != 0; a.dtype = dtype;
   a.stream = static_cast<cudaStream_t>(stream);

@@ -90,12 +90,12 @@ __global__ void __launch_bounds__(kConvThreads) conv_update_kernel(const ConvArg
   pdl_release();
   if (c >= a.C) return;
   const T *x = static_cast<const T *>(a.x) + b * a.x_bs;
-  T *st = static_cast<T *>(a.state) + b * a.state_bs + c * a.W;
+  T *st = static_cast<T *>(a.state) + b * a.state_bs + c * a.state_cs;
   if constexpr (KS == 4) {
     // the common case (width-4 cache state): the channel's state and weights
     // move as single vectors
     using V = typename std::conditional<sizeof(T) == 4, float4, uint2>::type;
-    if (a.W == 4 && (reinterpret_cast<uintptr_t>(st) % sizeof(V)) == 0 &&
+    if (a.W == 4 && a.state_ts == 1 && (reinterpret_cast<uintptr_t>(st) % sizeof(V)) == 0 &&
         (reinterpret_cast<uintptr_t>(a.weight + c * 4) % 16) == 0) {
       V sv = *reinterpret_cast<const V *>(st);
       T *h = reinterpret_cast<T *>(&sv);
@@ -117,15 +117,15 @@ __global__ void __launch_bounds__(kConvThreads) conv_update_kernel(const ConvArg
   }
   float win[KS];
 #pragma unroll
-  for (int j = 0; j < KS - 1; ++j) win[j] = to_f(st[a.W - (KS - 1) + j]);
+  for (int j = 0; j < KS - 1; ++j) win[j] = to_f(st[(a.W - (KS - 1) + j) * a.state_ts]);
   const T xin = x[c];
   win[KS - 1] = to_f(xin);
   float y = a.bias ? a.bias[c] : 0.f;
 #pragma unroll
   for (int j = 0; j < KS; ++j) y = fmaf(a.weight[c * KS + j], win[j], y);
   // shift the state left by one and append the input (stored values are inputs: no rounding)
-  for (int j = 0; j + 1 < a.W; ++j) st[j] = st[j + 1];
-  st[a.W - 1] = xin;
+  for (int j = 0; j + 1 < a.W; ++j) st[j * a.state_ts] = st[(j + 1) * a.state_ts];
+  st[(a.W - 1) * a.state_ts] = xin;
   static_cast<T *>(a.out)[b * a.out_bs + c] = from_f<T>(conv_act(y, a.silu));
 }
 
@@ -136,7 +136,7 @@ __global__ void __launch_bounds__(kConvThreads) conv_fwd_kernel(const ConvArgs a
   const int64_t t0 = int64_t(blockIdx.y) * kConvTile;
   if (c >= a.C) return;
   const T *x = static_cast<const T *>(a.x) + b * a.x_bs + c;
-  const T *st_in = a.state_in ? static_cast<const T *>(a.state_in) + b * a.state_bs + c * a.W : nullptr;
+  const T *st_in = a.state_in ? static_cast<const T *>(a.state_in) + b * a.state_bs + c * a.state_cs : nullptr;
   float w[KS];
 #pragma unroll
   for (int j = 0; j < KS; ++j) w[j] = a.weight[c * KS + j];
@@ -145,7 +145,7 @@ __global__ void __launch_bounds__(kConvThreads) conv_fwd_kernel(const ConvArgs a
   auto input = [&](int64_t t) -> float {
     if (t >= 0) return to_f(x[t * a.x_ts]);
     const int64_t back = -t;   // 1 .. KS - 1 (or more, before the state: zero)
-    if (st_in && back <= a.W) return to_f(st_in[a.W - back]);
+    if (st_in && back <= a.W) return to_f(st_in[(a.W - back) * a.state_ts]);
     return 0.f;
   };
   float win[KS];
@@ -165,15 +165,15 @@ __global__ void __launch_bounds__(kConvThreads) conv_fwd_kernel(const ConvArgs a
   // final state: the last W inputs of [state | x] (zeros before both); tile 0
   // is the only reader of the initial state, so the two may alias
   if (blockIdx.y == 0 && a.state_out) {
-    T *so = static_cast<T *>(a.state_out) + b * a.state_bs + c * a.W;
+    T *so = static_cast<T *>(a.state_out) + b * a.state_bs + c * a.state_cs;
     T vals[8];
     for (int j = 0; j < a.W; ++j) {
       const int64_t t = a.T - a.W + j;
       if (t >= 0) vals[j] = x[t * a.x_ts];
-      else if (st_in && -t <= a.W) vals[j] = st_in[a.W + t];
+      else if (st_in && -t <= a.W) vals[j] = st_in[(a.W + t) * a.state_ts];
       else vals[j] = from_f<T>(0.f);
     }
-    for (int j = 0; j < a.W; ++j) so[j] = vals[j];
+    for (int j = 0; j < a.W; ++j) so[j * a.state_ts] = vals[j];
   }
 }
 
@@ -182,7 +182,8 @@ int conv_dispatch(const ConvArgs &a, bool update) {
   if constexpr (sizeof(T) == 2) {
     const uintptr_t al = reinterpret_cast<uintptr_t>(a.x) | reinterpret_cast<uintptr_t>(a.state) |
                          reinterpret_cast<uintptr_t>(a.out) | reinterpret_cast<uintptr_t>(a.weight);
-    if (update && a.KS == 4 && a.W == 4 && a.C % 4 == 0 && (al % 16) == 0 && (a.x_bs % 4) == 0 &&
+    if (update && a.KS == 4 && a.W == 4 && a.state_cs == 4 && a.state_ts == 1 && a.C % 4 == 0 && (al % 16) == 0 &&
+        (a.x_bs % 4) == 0 &&
         (a.out_bs % 4) == 0 && (a.state_bs % 8) == 0) {
       const dim3 grid(unsigned((a.C / 4 + kConvThreads - 1) / kConvThreads), unsigned((a.B + kConvRows - 1) / kConvRows));
       const cudaError_t e = launch_pdl(conv_update4_kernel<T>, grid, dim3(kConvThreads), 0, a.stream, a);

@@ -240,6 +240,7 @@ struct ConvArgs {
   const void *state_in;           // prefill: optional initial state
   void *state_out;                // prefill: optional final state (may alias state_in)
   int64_t state_bs, W;            // state batch stride (elements), width (KS or KS - 1)
+  int64_t state_cs, state_ts;     // state channel / tap strides (elements): W and 1 when packed
   const float *weight, *bias;     // [C, KS] fp32, [C] fp32 or null
   void *out;
   int64_t out_bs, out_ts;
