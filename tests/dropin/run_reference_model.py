@@ -12,7 +12,9 @@ random-init ``YANchorForCausalLM`` (modeling_yanchor.py) with
      repository's CUDA library.
 
 Same weights (B loads A's state dict), bf16, a 150-token prefill of two
-prompts then 49 decode steps fed with A's greedy tokens.  The model shape
+prompts then 49 decode steps.  A third run, the same weights in fp32 on the
+reference's torch path, is the yardstick: its greedy tokens feed all three
+runs, and each bf16 path's logits are compared with it.  The model shape
 (§8(c) of the task's survey: 4 layers, 3 GDN + 1 SWA layer with an
 IndependentGQAMemory of 16 slots, commit chunk 16, window 32) uses the
 YANchor head shapes (GDN K = V = 128, memory / SWA head_dim 256).
@@ -54,6 +56,9 @@ def main():
     dev = torch.device('cuda', 0)
     torch.manual_seed(0)
     ref_model = my.YANchorForCausalLM(config('torch')).to(dev, torch.bfloat16).eval()
+    # the same weights in fp32 on the reference's torch path: the yardstick for both bf16 paths
+    f32_model = my.YANchorForCausalLM(config('torch')).to(dev, torch.float32).eval()
+    f32_model.load_state_dict({k: v.float() for k, v in ref_model.state_dict().items()}, strict=True)
     # the maintainer's patch, applied to the imported reference modules
     yanchor_b200.install_memory_module()
     yanchor_b200.bind_memory_prefill(my)
@@ -68,36 +73,52 @@ def main():
     prompt = torch.randint(0, 1024, (2, 150), generator=gen).to(dev)
     steps = 49
 
-    def run(model, backend_feed):
+    def run(model, feed):
         cache = my.FixedMemoryHybridDynamicCache(model.config)
         with torch.no_grad():
             out = model(input_ids=prompt, past_key_values=cache, use_cache=True)
             logits = [out.logits.float()]
-            ids = [out.logits[:, -1:].argmax(-1)] if backend_feed is None else [backend_feed[:, :1]]
+            ids = [out.logits[:, -1:].argmax(-1)] if feed is None else [feed[:, :1]]
             for t in range(steps):
                 out = model(input_ids=ids[-1], past_key_values=cache, use_cache=True)
                 logits.append(out.logits.float())
-                nxt = out.logits[:, -1:].argmax(-1)
-                ids.append(nxt if backend_feed is None else backend_feed[:, t + 1:t + 2])
+                ids.append(out.logits[:, -1:].argmax(-1) if feed is None else feed[:, t + 1:t + 2])
         torch.cuda.synchronize()
         return logits, torch.cat(ids, 1)
 
-    ref_logits, ref_ids = run(ref_model, None)
-    b200_logits, _ = run(b200_model, ref_ids)
-    worst_prefill = (ref_logits[0] - b200_logits[0]).abs().max().item()
-    worst_decode = max((a - b).abs().max().item() for a, b in zip(ref_logits[1:], b200_logits[1:]))
-    # greedy ids wherever the reference's top-2 margin exceeds 1e-2 (every prefill position and decode step)
-    compared = agree = 0
-    for a, b in zip(ref_logits, b200_logits):
-        top2 = a.topk(2, -1).values
-        sure = (top2[..., 0] - top2[..., 1]) > 1e-2
-        same = a.argmax(-1) == b.argmax(-1)
-        compared += int(sure.sum())
-        agree += int((same & sure).sum())
-    print(json.dumps({'prefill_max_abs': worst_prefill, 'decode_max_abs': worst_decode,
-                      'ids_compared': compared, 'ids_agree': agree, 'logit_scale': ref_logits[0].abs().max().item(),
-                      'bound_layers': bound.get('native_gdn_layers'), 'state_dict_keys_ok': not missing.missing_keys
-                      and not missing.unexpected_keys}), flush=True)
+    f32_logits, f32_ids = run(f32_model, None)          # the fp32 model's own greedy tokens
+    ref_logits, _ = run(ref_model, f32_ids)             # both bf16 paths fed the same tokens
+    b200_logits, _ = run(b200_model, f32_ids)
+
+    def worst(a, b, part):
+        pairs = list(zip(a, b))
+        pairs = pairs[:1] if part == 'prefill' else pairs[1:]
+        return max((x - y).abs().max().item() for x, y in pairs)
+
+    def ids_agree(test, truth, margin):
+        compared = agree = 0
+        for a, b in zip(truth, test):
+            top2 = a.topk(2, -1).values
+            sure = (top2[..., 0] - top2[..., 1]) > margin
+            compared += int(sure.sum())
+            agree += int(((a.argmax(-1) == b.argmax(-1)) & sure).sum())
+        return compared, agree
+
+    r = {'logit_scale': f32_logits[0].abs().max().item(),
+         'b200_vs_ref_bf16': {'prefill': worst(b200_logits, ref_logits, 'prefill'),
+                              'decode': worst(b200_logits, ref_logits, 'decode')},
+         'b200_vs_fp32': {'prefill': worst(b200_logits, f32_logits, 'prefill'),
+                          'decode': worst(b200_logits, f32_logits, 'decode')},
+         'ref_bf16_vs_fp32': {'prefill': worst(ref_logits, f32_logits, 'prefill'),
+                              'decode': worst(ref_logits, f32_logits, 'decode')},
+         'bound_layers': bound.get('native_gdn_layers'),
+         'state_dict_keys_ok': not missing.missing_keys and not missing.unexpected_keys}
+    noise = max(max(r['b200_vs_fp32'].values()), max(r['ref_bf16_vs_fp32'].values()))
+    r['id_margin'] = 2 * noise
+    r['ids_b200'] = ids_agree(b200_logits, f32_logits, r['id_margin'])
+    r['ids_ref_bf16'] = ids_agree(ref_logits, f32_logits, r['id_margin'])
+    r['ids_b200_vs_ref_bf16_margin_1e-2'] = ids_agree(b200_logits, ref_logits, 1e-2)
+    print(json.dumps(r), flush=True)
 
 
 if __name__ == '__main__':

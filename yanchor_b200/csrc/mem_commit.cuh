@@ -70,6 +70,52 @@ __device__ void commit_gather(T *bank, const T *pend, T *stage, const int *sel, 
   __syncthreads();
 }
 
+// Both banks at once: the key rows by cp.async into `stage`, the value rows into registers, all
+// of them in flight together, then both written back.  Used when every thread holds at most
+// kRegPieces value pieces (the YANchor shape: CAP 64, D 256, 128 threads -> 16); otherwise the
+// two banks go one after the other through `stage`.
+constexpr int kRegPieces = 16;
+
+template <typename T>
+__device__ void commit_gather_kv(T *bank_k, T *bank_v, const T *pend_k, const T *pend_v, T *stage, const int *sel,
+                                 const int64_t *pkey, int g, int CAP, int PC, int D) {
+  const int tid = threadIdx.x, nt = blockDim.x;
+  constexpr int VEC = 16 / int(sizeof(T));
+  const int DV = D / VEC;
+  const bool vec = (D % VEC) == 0 && ((reinterpret_cast<uintptr_t>(bank_k) | reinterpret_cast<uintptr_t>(bank_v) |
+                                       reinterpret_cast<uintptr_t>(pend_k) | reinterpret_cast<uintptr_t>(pend_v)) %
+                                      16) == 0;
+  if (!vec || CAP * DV > nt * kRegPieces) {
+    commit_gather(bank_k, pend_k, stage, sel, pkey, g, CAP, PC, D);
+    commit_gather(bank_v, pend_v, stage, sel, pkey, g, CAP, PC, D);
+    return;
+  }
+  uint4 vreg[kRegPieces];
+#pragma unroll
+  for (int i = 0; i < kRegPieces; ++i) {
+    const int e = tid + i * nt;
+    if (e < CAP * DV) {
+      const int r = e / DV, d = (e % DV) * VEC;
+      const int c = sel[r];
+      const int src = pkey[c] == INT64_MAX ? 0 : c;
+      const int64_t off = src < CAP ? (int64_t(g) * CAP + src) * D : (int64_t(g) * PC + src - CAP) * D;
+      cp_async16(stage + r * D + d, (src < CAP ? bank_k : pend_k) + off + d);
+      vreg[i] = *reinterpret_cast<const uint4 *>((src < CAP ? bank_v : pend_v) + off + d);
+    }
+  }
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < kRegPieces; ++i) {
+    const int e = tid + i * nt;
+    if (e < CAP * DV) {
+      *reinterpret_cast<uint4 *>(bank_k + int64_t(g) * CAP * D + e * VEC) = *reinterpret_cast<const uint4 *>(stage + e * VEC);
+      *reinterpret_cast<uint4 *>(bank_v + int64_t(g) * CAP * D + e * VEC) = vreg[i];
+    }
+  }
+  __syncthreads();
+}
+
 // Group g of request row `row` (state row s, active): push into pending slot `count` (unless
 // PUSH is false: the caller pushed every group already), and merge when the chunk fills.
 // count / total are read by the caller and not updated here.
@@ -133,8 +179,7 @@ __device__ void commit_group(const MemCommitArgs &a, int64_t row, int64_t s, int
     if (rank < CAP) sel[rank] = c;
   }
   __syncthreads();
-  commit_gather(bank_k, pend_k, stage, sel, c_pkey, g, CAP, PC, D);
-  commit_gather(bank_v, pend_v, stage, sel, c_pkey, g, CAP, PC, D);
+  commit_gather_kv(bank_k, bank_v, pend_k, pend_v, stage, sel, c_pkey, g, CAP, PC, D);
   for (int r = tid; r < CAP; r += nt) {
     const int c = sel[r];
     bscore[int64_t(g) * CAP + r] = c_score[c];
