@@ -59,16 +59,6 @@ def main():
     # the same weights in fp32 on the reference's torch path: the yardstick for both bf16 paths
     f32_model = my.YANchorForCausalLM(config('torch')).to(dev, torch.float32).eval()
     f32_model.load_state_dict({k: v.float() for k, v in ref_model.state_dict().items()}, strict=True)
-    # the maintainer's patch (INTEGRATION.md), applied to the imported reference modules
-    yanchor_b200.install_memory_module()
-    yanchor_b200.bind_memory_prefill(my)
-    my.flash_swa = yanchor_b200.flash_swa
-    my.reference_swa = yanchor_b200.reference_swa
-    my.bind_native_qwen_gdn_kernels = lambda model: yanchor_b200.bind_gdn_kernels(model, inplace_decode=True)
-    b200_model = my.YANchorForCausalLM(config('cuda')).to(dev, torch.bfloat16).eval()
-    missing = b200_model.load_state_dict(ref_model.state_dict(), strict=True)
-    bound = b200_model.bind_runtime_kernels()
-
     gen = torch.Generator().manual_seed(1)
     prompt = torch.randint(0, 1024, (2, 150), generator=gen).to(dev)
     steps = 49
@@ -86,8 +76,18 @@ def main():
         torch.cuda.synchronize()
         return logits, torch.cat(ids, 1)
 
+    # the two torch-path runs first: the patch below rebinds module-level functions for every model
     f32_logits, f32_ids = run(f32_model, None)          # the fp32 model's own greedy tokens
     ref_logits, _ = run(ref_model, f32_ids)             # both bf16 paths fed the same tokens
+    # the maintainer's patch (INTEGRATION.md), applied to the imported reference modules
+    yanchor_b200.install_memory_module()
+    yanchor_b200.bind_memory_prefill(my)
+    my.flash_swa = yanchor_b200.flash_swa
+    my.reference_swa = yanchor_b200.reference_swa
+    my.bind_native_qwen_gdn_kernels = lambda model: yanchor_b200.bind_gdn_kernels(model, inplace_decode=True)
+    b200_model = my.YANchorForCausalLM(config('cuda')).to(dev, torch.bfloat16).eval()
+    missing = b200_model.load_state_dict(ref_model.state_dict(), strict=True)
+    bound = b200_model.bind_runtime_kernels()
     b200_logits, _ = run(b200_model, f32_ids)
 
     def worst(a, b, part):

@@ -20,6 +20,9 @@ Operators (all CUDA, via the C ABI library libyanchor_b200.so):
   step per batch size, captured without warm-up forwards)
 * ``bind_gdn_kernels`` / ``install_memory_module`` / ``bind_memory_prefill``
   put them where the reference model code looks them up.
+* ``torch.ops.yanchor_b200.*`` (``yanchor_b200.ops``): the same operators
+  registered as torch custom ops with fake implementations, for tracers
+  such as ``torch.compile``.
 """
 from .gated_delta_rule import (chunk_gated_delta_rule, fused_gdn_decode, fused_recurrent_gated_delta_rule,  # noqa: F401
                                gdn_gates)
@@ -32,6 +35,7 @@ from .memory_prefill import exclusive_prefix_topk, merge_topk, select_topk, sequ
 from .sampling import apply_dense_presence_penalty_, greedy, greedy_noalloc, sample_top_k_top_p_counter  # noqa: F401
 from .decode_loop import StepGraphs, prepare_capture, update_fixed_decode_state_  # noqa: F401
 from .bind import bind_gdn_kernels, bind_memory_prefill, install_memory_module  # noqa: F401
+from . import ops  # noqa: F401  (registers torch.ops.yanchor_b200.*)
 from ._lib import LIB_PATH, YanchorError, lib  # noqa: F401
 
 __version__ = '0.1.0'
