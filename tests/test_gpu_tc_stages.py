@@ -14,7 +14,7 @@ from conftest import ROOT
 pytestmark = pytest.mark.gpu
 
 LIB = os.path.join(ROOT, 'tests', '_build', 'libyb_tc_debug.so')
-DBG = dict(D1=0, W=16384, VN=32768, O=49152, S1=57344, T=73728, NORM=77824)
+DBG = dict(D1=0, W=16384, U=24576, X=32768, Y=40960, O=49152, S1=57344, T=73728, NORM=77824)
 
 
 def bf(x):
@@ -84,21 +84,22 @@ def expected(d):
     Tw = hilo(Tm * (bt * np.exp(G) * kn)[None, :])
     Tu = hilo(Tm * bt[None, :])
     e['W'] = K_.T @ Tw.T
-    U = V_.T @ Tu.T
+    e['U'] = V_.T @ Tu.T
     ST = bf(d['h0'][0, 0].T)
-    vn = U - ST @ bf(e['W'])                 # MMA3 accumulates S^T (-W^T) over U^T
-    e['VN'] = vn
+    e['X'] = ST @ bf(e['W'])
+    e['Y'] = ST @ Q_.T
+    vn = e['U'] - e['X']
     P = bf(np.tril(qn[:, None] * kn[None, :] * dec * (Q_ @ K_.T)))
-    qt = bf(Q_ * (np.exp(G) * qn)[:, None])  # the Q tile scaled in place
-    e['O'] = ST @ qt.T + bf(vn) @ P.T
+    e['O'] = bf(vn) @ P.T
     vt = hilo(vn * (np.exp(G[-1] - G) * kn)[None, :])
     e['S1'] = np.exp(G[-1]) * d['h0'][0, 0].T + vt @ K_      # the state after chunk 0 (S^T)
     return e
 
 
-SHAPES = dict(D1=(128, 128), W=(128, 64), VN=(128, 64), O=(128, 64), S1=(128, 128), T=(64, 64), NORM=(128,))
-ORDER = ['D1', 'NORM', 'T', 'W', 'VN', 'O', 'S1']
-TOL = dict(D1=2e-3, NORM=2e-3, T=2e-3, W=2e-3, VN=2e-2, O=2e-2, S1=2e-3)
+SHAPES = dict(D1=(128, 128), W=(128, 64), U=(128, 64), X=(128, 64), Y=(128, 64), O=(128, 64), S1=(128, 128),
+              T=(64, 64), NORM=(128,))
+ORDER = ['D1', 'NORM', 'T', 'W', 'U', 'X', 'Y', 'O', 'S1']
+TOL = dict(D1=2e-3, NORM=2e-3, T=2e-3, W=2e-3, U=2e-3, X=2e-2, Y=1e-2, O=2e-2, S1=2e-3)
 
 
 @pytest.mark.parametrize('stage', ORDER)

@@ -12,11 +12,11 @@
 //   A     T = (I + L)^-1 in fp32 (16x16 blocked forward substitution)
 //   MMA2  W^T = k^T Tw^T, U^T = v^T Tu^T   with Tw_ij = T_ij beta_j e^{G_j} kn_j,
 //                                                Tu_ij = T_ij beta_j   (bf16 hi + lo)
-//   A     q~ = e^{G} qn q, in place over the Q tile once the Gram has read it
-//   MMA3  v_new^T = U^T + S^T (-W^T)  (accumulated over U^T),  O^T = S^T q~^T   (state bf16)
-//         (S^T in TMEM already holds e^{G_last} S^T)
+//   MMA3  X^T = S^T W^T, Y^T = S^T q^T                          (state bf16)
+//   B     v_new^T = U^T - X^T  (S^T in TMEM already holds e^{G_last} S^T)
+//   MMA4  O^T = v_new^T P^T
 //   MMA5  S^T += (v_new^T * e^{G_last-G} kn) k     (that operand as bf16 hi + lo)
-//   MMA4  O^T += v_new^T P^T                                   -> o
+//   B     o = e^{G} qn Y + O
 //
 // (the chunk form of transformers qwen3_5 modeling_qwen3_5.py:234-311 and
 // of fla's chunk_gated_delta_rule_fwd).  Every state-dependent product is
@@ -33,10 +33,7 @@
 // chunk c + 1 while group B finishes chunk c: MMA1 of chunk c + 1 is issued
 // right after MMA2 of chunk c, into the other of two alternating TMEM
 // regions, and the shared tiles the two groups touch are distinct or ordered
-// by the MMA barriers.  Group B's chain is ordered so that the state comes
-// first: the state update (MMA5) is committed on its own, the next state
-// copy is released before the output of the chunk (in one of two
-// alternating TMEM regions) is read out.
+// by the MMA barriers.
 // Every wait is bounded in time; a CTA that gives up records an error code,
 // drains its in-flight copies and MMAs, frees TMEM and exits.
 #include "common.cuh"
@@ -84,12 +81,11 @@ static_assert(3 * 320 * 4 <= 8192, "solve scratch fits the Tw tile");
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
 // TMEM columns (fp32, 128 lanes).  Chunk c uses region R(c) = c even ? T_R0 : T_R1
-// for [K;Q][K;Q]^T, then U^T -> v_new^T (first 64 columns) and W^T (last 64),
-// and output region O(c) = c even ? T_O0 : T_O1.
+// for [K;Q][K;Q]^T, then U^T (first 64 columns) and W^T / X^T (last 64).
 constexpr uint32_t T_R0 = 0;
 constexpr uint32_t T_R1 = 128;
-constexpr uint32_t T_O0 = 256;   // O^T of even chunks
-constexpr uint32_t T_O1 = 320;   // O^T of odd chunks
+constexpr uint32_t T_Y = 256;    // Y^T
+constexpr uint32_t T_O = 320;    // O^T
 constexpr uint32_t T_S = 384;    // S^T fp32 state (128 columns)
 
 constexpr uint32_t ID_N64_KK = idesc_bf16(128, 64, false, false);
@@ -166,7 +162,7 @@ __device__ __forceinline__ void store_block16(float *dst, int ld, const float ac
   }
 }
 
-constexpr int DBG_D1 = 0, DBG_W = 16384, DBG_VN = 32768, DBG_O = 49152,
+constexpr int DBG_D1 = 0, DBG_W = 16384, DBG_U = 24576, DBG_X = 32768, DBG_Y = 40960, DBG_O = 49152,
               DBG_S1 = 57344, DBG_T = 73728, DBG_NORM = 77824, DBG_TS = 78000;
 #ifdef YB_TC_DEBUG
 // Test-only: copy `n` values of TMEM row r (already in registers) into the
@@ -253,13 +249,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint64_t *empty_v = bars + 5;    // MMA2 read V (1)
   uint64_t *mma1_bar = bars + 6;   // [2] [K;Q][K;Q]^T of chunk c in TMEM (c & 1 selects)
   uint64_t *mma2_bar = bars + 8;   // W in TMEM
-  uint64_t *mma3_bar = bars + 9;   // v_new^T in TMEM (and the S^T q~^T part of O^T)
-  uint64_t *mma5_bar = bars + 10;  // the state updated
-  uint64_t *mma4_bar = bars + 17;  // [2] O^T of chunk c complete (c & 1 selects)
+  uint64_t *mma3_bar = bars + 9;   // X, Y in TMEM
+  uint64_t *mma45_bar = bars + 10; // O in TMEM, state updated
   uint64_t *a_wt = bars + 11;      // group A: P and W^T tiles written (128)
   uint64_t *b_vn = bars + 12;      // group B: v_new, v~ tiles written (128)
-  uint64_t *b_done = bars + 13;    // group B: state copy for the next MMA3 written, the state scaled by
-                                   //          the next chunk's decay, O of chunk c - 1 consumed (128)
+  uint64_t *b_done = bars + 13;    // group B: state copy for the next MMA3 written, Y / O consumed, the
+                                   //          state scaled by the next chunk's decay (128)
   uint64_t *done_bar = bars + 14;
   uint64_t *a_tw = bars + 15;      // [2] group A: Tw / Tu tiles and the norms written, [K;Q][K;Q]^T
                                    //     consumed (128; c & 1 selects)
@@ -293,9 +288,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     mbar_init(&mma1_bar[1], 1);
     mbar_init(mma2_bar, 1);
     mbar_init(mma3_bar, 1);
-    mbar_init(mma5_bar, 1);
-    mbar_init(&mma4_bar[0], 1);
-    mbar_init(&mma4_bar[1], 1);
+    mbar_init(mma45_bar, 1);
     mbar_init(&a_tw[0], 128);
     mbar_init(&a_tw[1], 128);
     mbar_init(a_wt, 128);
@@ -441,37 +434,33 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           if (!wait(&full_kq[s ^ 1], ((c + 1) >> 1) & 1, ERR_WAIT_FULL)) break;
           mma1(c + 1);
         }
-        // MMA3: v_new^T = U^T + S^T (-W^T), accumulated over U^T in R ;  O^T = S^T q~^T -> O(c)
-        //       (M=128, N=64, K=128; group A wrote -W^T and scaled the Q tile into q~)
+        // MMA3: X^T = S^T W^T -> R + 64 ;  Y^T = S^T q^T -> T_Y   (M=128, N=64, K=128)
         if (!wait(a_wt, c & 1, ERR_WAIT_EPI) || !wait(b_done, c & 1, ERR_WAIT_EPI)) break;
         const uint32_t st = smem_u32(smem + OFF_ST), wt = smem_u32(smem + OFF_WT);
-        const uint32_t O = tmem + ((c & 1) ? T_O1 : T_O0);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint64_t a = sdesc(st + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
-          mma_bf16(R, a, sdesc(wt + kk * 2048, 16384, 1024), ID_N64_KM, true);
-          mma_bf16(O, a, sdesc(kq + 8192 + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024), ID_N64_KK, kk > 0);
+          mma_bf16(R + 64, a, sdesc(wt + kk * 2048, 16384, 1024), ID_N64_KM, kk > 0);
+          mma_bf16(tmem + T_Y, a, sdesc(kq + 8192 + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024), ID_N64_KK,
+                   kk > 0);
         }
         mma_commit(mma3_bar);
-        // MMA5: S^T += (v~_hi + v~_lo)^T k (N=128, K=64), the state already scaled by the chunk's decay
-        // (group B did it with the previous state copy), committed on its own: the state chain goes on
-        // as soon as it completes.  MMA4: O^T += v_new^T P^T (N=64, K=64) after it.
+        // MMA4: O^T = v_new^T P^T (N=64, K=64) ;  MMA5: S^T += (v~_hi + v~_lo)^T k (N=128, K=64), the
+        // state already scaled by the chunk's decay (group B did it with the previous state copy)
         if (!wait(b_vn, c & 1, ERR_WAIT_EPI)) break;
         const uint32_t vn = smem_u32(smem + OFF_VN), pp = smem_u32(smem + OFF_P);
         const uint32_t vhi = smem_u32(smem + OFF_VHI), vlo = smem_u32(smem + OFF_VLO);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
+        for (int kk = 0; kk < 4; ++kk) {
+          mma_bf16(tmem + T_O, sdesc(vn + kk * 32, 16, 1024), sdesc(pp + kk * 32, 16, 1024), ID_N64_KK, kk > 0);
           mma_bf16(tmem + T_S, sdesc(vhi + kk * 32, 16, 1024), sdesc(kq + kk * 2048, 16384, 1024), ID_N128_KM,
                    true);
+        }
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
           mma_bf16(tmem + T_S, sdesc(vlo + kk * 32, 16, 1024), sdesc(kq + kk * 2048, 16384, 1024), ID_N128_KM,
                    true);
-        mma_commit(mma5_bar);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_bf16(O, sdesc(vn + kk * 32, 16, 1024), sdesc(pp + kk * 32, 16, 1024), ID_N64_KK, true);
-        mma_commit(&mma4_bar[c & 1]);
+        mma_commit(mma45_bar);
         mma_commit(&empty_kq[s]);
       }
       // all issued MMAs finished before TMEM is released
@@ -678,27 +667,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
       signal(&a_tw[s]);
       YB_DBG_TS(5);
-      // ---------- q~ = e^{G} qn q in place over the Q tile (MMA1 has read it; MMA3 takes it for
-      //            O^T = S^T q~^T): thread r scales half a row, row r & 63, column block r >> 6 ----------
-      {
-        const int i = r & 63, cb = r >> 6;
-        const float f = EG[i] * qn[i];
-        uint8_t *qrow = smem + (s ? OFF_KQ1 : OFF_KQ0) + cb * 16384 + 8192;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          uint4 *pc = reinterpret_cast<uint4 *>(qrow + sw128_off(64, 0, i, j));
-          uint4 w = *pc;
-          uint32_t *h = reinterpret_cast<uint32_t *>(&w);
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&h[t]));
-            h[t] = pack_bf16x2(x.x * f, x.y * f);
-          }
-          *pc = w;
-        }
-      }
-      // ---------- P, and -W^T (MN-major B operand of MMA3) over the v_new tile ----------
-      // MMA2 of this chunk was issued after MMA5 / MMA4 of the previous one, so
+      // ---------- P, and W^T (MN-major B operand of MMA3) over the v_new tile ----------
+      // MMA2 of this chunk was issued after MMA4 / MMA5 of the previous one, so
       // once it is done the P and v_new tiles of chunk c - 1 have been read
       ok = mbar_wait(mma2_bar, c & 1, abort_flag, ERR_WAIT_MMA);
       tc_fence_after();
@@ -711,8 +681,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         tmem_ld32(lane_base + R + 64 + uint32_t(32 * hf), w);
         tmem_wait_ld();
         YB_DBG_ROW(DBG_W, 64, 32 * hf, 32, w);
-#pragma unroll
-        for (int t = 0; t < 32; ++t) w[t] = -w[t];   // MMA3 accumulates S^T (-W^T) over U^T
         st_half_bf16(smem + OFF_WT, 128, 0, r, 4 * hf, w);
       }
       signal(a_wt);
@@ -771,8 +739,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const int s = c & 1;
       const uint32_t R = s ? T_R1 : T_R0;
       const float *gst = reinterpret_cast<const float *>(smem + OFF_GST + (c % 3) * 1024);
-      const float *TAIL = gst + 192;
+      const float *EG = gst + 128, *TAIL = gst + 192;
       const float *kn = reinterpret_cast<const float *>(smem + OFF_NORM + (c % 3) * 512);
+      const float *qn = kn + 64;
       const int m = int(len - int64_t(c) * C < C ? len - int64_t(c) * C : C);
       const bool last = c == nchunks - 1;
       YB_DBG_TS(8);
@@ -782,14 +751,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       ok = ok && mbar_wait(&a_tw[s], (c >> 1) & 1, abort_flag, ERR_WAIT_EPI);
       tc_fence_after();
       YB_DBG_TS(9);
-      // ---------- v_new (MMA3 accumulated it over U^T); v~ = v_new e^{G_last-G} kn as bf16 hi + lo ----------
+      // ---------- v_new = U - X; v~ = v_new e^{G_last-G} kn as bf16 hi + lo ----------
       if (ok) {
 #pragma unroll 1
         for (int hf = 0; hf < 2; ++hf) {
-          float u[32];
+          float u[32], x[32];
           tmem_ld32(lane_base + R + uint32_t(32 * hf), u);
+          tmem_ld32(lane_base + R + 64 + uint32_t(32 * hf), x);
           tmem_wait_ld();
-          YB_DBG_ROW(DBG_VN, 64, 32 * hf, 32, u);
+          YB_DBG_ROW(DBG_U, 64, 32 * hf, 32, u);
+          YB_DBG_ROW(DBG_X, 64, 32 * hf, 32, x);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) u[i] -= x[i];
           st_half_bf16(smem + OFF_VN, 128, 0, r, 4 * hf, u);
 #pragma unroll
           for (int i = 0; i < 32; ++i) u[i] *= TAIL[32 * hf + i] * kn[32 * hf + i];
@@ -801,14 +774,31 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         signal(b_vn);
       }
       YB_DBG_TS(10);
-      ok = ok && mbar_wait(mma5_bar, c & 1, abort_flag, ERR_WAIT_MMA);
+      ok = ok && mbar_wait(mma45_bar, c & 1, abort_flag, ERR_WAIT_MMA);
       // the next chunk's decay scales the state now (its gates were written two chunks ahead)
       if (!last) ok = ok && mbar_wait(&full_kq[s ^ 1], ((c + 1) >> 1) & 1, abort_flag, ERR_WAIT_FULL);
       tc_fence_after();
       YB_DBG_TS(11);
       if (ok) {
-        // ---------- the updated state first: bf16 copy for the next MMA3 (ht after the last
-        //            chunk), then fp32 scaled by the next chunk's decay back into TMEM ----------
+        // ---------- o = e^{G} qn Y + O for this value column, staged as [token][value]
+        //            rows over the v~_hi tile (MMA5 has read it) ----------
+        __nv_bfloat16 *ostage = reinterpret_cast<__nv_bfloat16 *>(smem + OFF_OST);
+#pragma unroll 1
+        for (int hf = 0; hf < 2; ++hf) {
+          float y[32], oo[32];
+          tmem_ld32(lane_base + T_Y + uint32_t(32 * hf), y);
+          tmem_ld32(lane_base + T_O + uint32_t(32 * hf), oo);
+          tmem_wait_ld();
+          YB_DBG_ROW(DBG_Y, 64, 32 * hf, 32, y);
+          YB_DBG_ROW(DBG_O, 64, 32 * hf, 32, oo);
+#pragma unroll
+          for (int t = 0; t < 32; ++t) {
+            const int a = 32 * hf + t;
+            ostage[a * 128 + r] = __float2bfloat16_rn(EG[a] * qn[a] * y[t] + oo[t]);
+          }
+        }
+        // ---------- the updated state: bf16 copy for the next MMA3 (ht after the last chunk),
+        //            then fp32 scaled by the next chunk's decay back into TMEM ----------
         const float dnext =
             last ? 1.f : reinterpret_cast<const float *>(smem + OFF_GST + ((c + 1) % 3) * 1024)[128 + 63];
 #pragma unroll 1
@@ -839,23 +829,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         tmem_wait_st();
         signal(b_done);
         YB_DBG_TS(12);
-      }
-      // ---------- o of this value column, staged as [token][value] rows over the v~_hi tile
-      //            (MMA5 has read it; the next chunk writes it only after this one's o is out) ----------
-      ok = ok && mbar_wait(&mma4_bar[c & 1], (c >> 1) & 1, abort_flag, ERR_WAIT_MMA);
-      tc_fence_after();
-      if (ok) {
-        __nv_bfloat16 *ostage = reinterpret_cast<__nv_bfloat16 *>(smem + OFF_OST);
-        const uint32_t O = (c & 1) ? T_O1 : T_O0;
-#pragma unroll 1
-        for (int hf = 0; hf < 2; ++hf) {
-          float oo[32];
-          tmem_ld32(lane_base + O + uint32_t(32 * hf), oo);
-          tmem_wait_ld();
-          YB_DBG_ROW(DBG_O, 64, 32 * hf, 32, oo);
-#pragma unroll
-          for (int t = 0; t < 32; ++t) ostage[(32 * hf + t) * 128 + r] = __float2bfloat16_rn(oo[t]);
-        }
       }
       if (!(ok = b_sync_and(ok))) break;
       // ---------- o out: 16-byte piece q = r + 128 t covers token q / 16, bytes 16 (q % 16) ----------
