@@ -777,6 +777,21 @@ def run_prefill(torch, yb, device, hbm, tf_burst, peak_kind):
     for _ in range(2):
         seq()
     seq_ms = time_events(torch, seq, 3, stream)
+    # the same layer's prefill with no host synchronisation, captured once in a CUDA graph and replayed
+    # (each replay continues the state the previous one left: same shapes, same work)
+    st_g = yb.MemoryState.empty(B, MEM_G, 64, MEM_CHUNK, MEM_D, device, bf)
+    side = torch.cuda.Stream(device)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        yb.sequence(mq2, msc, writer, None, MEM_CHUNK, st_g, capture_safe=True)
+    stream.wait_stream(side)
+    torch.cuda.synchronize()
+    g_seq = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_seq):
+        yb.sequence(mq2, msc, writer, None, MEM_CHUNK, st_g, capture_safe=True)
+    g_seq.replay()
+    seq_graph_ms = time_events(torch, g_seq.replay, 3, stream)
+    del g_seq, st_g
     # sliding-window attention over the same prompts (an SWA layer: 16 query heads
     # over 4 KV heads, D=256, window 1024); free the GDN inputs first
     del q, k, v, mq, mq2, wk, wv
@@ -792,6 +807,7 @@ def run_prefill(torch, yb, device, hbm, tf_burst, peak_kind):
                         'plus the anchor prefill of one memory layer (64 slots, G=4 H=16 D=256, chunk 64)',
             'tok_s': round(B * T / (ms / 1e3), 1), 'gdn_ms': round(ms, 3), 'anchor_read_ms': round(mem_ms, 3),
             'anchor_prefix_topk_ms': round(topk_ms, 3), 'anchor_sequence_ms': round(seq_ms, 3),
+            'anchor_sequence_graph_ms': round(seq_graph_ms, 3),
             'tok_s_with_anchor_read': round(B * T / ((ms + mem_ms) / 1e3), 1),
             'tok_s_with_anchor_prefill': round(B * T / ((ms + seq_ms) / 1e3), 1),
             'swa_prefill': {'ms': round(swa_ms, 3), 'how': f'reference_swa over the same prompts: {SW_QH} query heads '
@@ -856,6 +872,38 @@ def run_only(args):
             st = yb.MemoryState.empty(8, MEM_G, MEM_CAP, MEM_CHUNK, MEM_D, dev, bf)
             yb.sequence(mq, msc, writer, None, MEM_CHUNK, st)
         fn = (lambda: yb.exclusive_prefix_topk(psc, ppos, ppos, 64)) if args.only == 'mem_topk' else seq
+    elif args.only == 'mem_layers':
+        # the 8 memory layers' decode step in one CUDA graph, three bank states: empty banks, full banks
+        # with no row merging during the timed replays (counts restarted at 0), and full banks with pending
+        # counts staggered over the chunk (1 in MEM_CHUNK rows merges per replay)
+        mems8 = [yb.MemoryState.empty(B, MEM_G, MEM_CAP, MEM_CHUNK, MEM_D, dev, bf) for _ in range(L_MEM)]
+
+        def layers8():
+            for i, m in enumerate(mems8):
+                yb.memory_decode_step(x['mq'][i], x['mk'][i], x['mv'][i], x['ms'][i], active, MEM_CHUNK, m)
+        stream = torch.cuda.current_stream(dev)
+        layers8()
+        torch.cuda.synchronize()
+        g8 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g8):
+            layers8()
+        res = {}
+        for m in mems8:
+            m.count.zero_()
+        res['empty_banks_us'] = time_events(torch, g8.replay, 20, stream) * 1e3 / L_MEM
+        for _ in range(MEM_CHUNK + 2):
+            g8.replay()
+        for m in mems8:
+            m.count.zero_()
+        res['full_banks_no_merge_us'] = time_events(torch, g8.replay, 20, stream) * 1e3 / L_MEM
+        for m in mems8:
+            m.count.copy_(torch.arange(B, device=dev) % MEM_CHUNK)
+        res['full_banks_staggered_us'] = time_events(torch, g8.replay, 20, stream) * 1e3 / L_MEM
+        for m in mems8:
+            m.count.fill_(MEM_CHUNK - 1)
+        res['all_rows_merge_us'] = time_events(torch, g8.replay, 1, stream) * 1e3 / L_MEM
+        print(json.dumps({'only': 'mem_layers', 'batch': B, **{k: round(v, 2) for k, v in res.items()}}), flush=True)
+        return
     elif args.only in ('mem_step', 'mem_step_merge'):
         # one memory layer's decode step (read + commit, one launch) on a full bank: pending counts
         # staggered over the chunk (1 in MEM_CHUNK rows merges per call), or every row merging
@@ -1113,7 +1161,7 @@ def main():
     ap.add_argument('--no-serve', action='store_true', help='skip the config-4 serving sweep')
     ap.add_argument('--no-b256', action='store_true', help='skip the config-2 batch (B=256)')
     ap.add_argument('--only', choices=['conv_update', 'gdn_decode', 'gdn_fused', 'gdn_chunk', 'mem_read', 'mem_commit',
-                                       'mem_step', 'mem_step_merge', 'mem_indexed', 'mem_topk',
+                                       'mem_step', 'mem_step_merge', 'mem_layers', 'mem_indexed', 'mem_topk',
                                        'mem_sequence', 'swa', 'swa_prefill', 'greedy',
                                        'topk'], help='run one kernel family (small ncu captures)')
     ap.add_argument('--prefill-batch', type=int, default=8)

@@ -168,3 +168,66 @@ def test_sequence_bf16_yanchor_shape(yb):
         for f in FIELDS:
             np.testing.assert_array_equal(host(getattr(state, f)), st[f].astype(host(getattr(state, f)).dtype),
                                           err_msg=f'T={T} {mask} {f}')
+
+
+def test_sequence_capture_safe_matches_and_graphs(yb):
+    """capture_safe=True (the writer on every timeline slot, the mask kind
+    given by the caller, no host synchronisation) gives results identical to
+    the default path over the same calls as the YANchor-shape test, and a
+    left-padded call captured in a CUDA graph and replayed gives them too."""
+    rng = np.random.default_rng(78)
+    B, H, G, D, CAP, CH = 3, 16, 4, 256, 64, 64
+    bf = torch.bfloat16
+    st_a, st_b = _state(yb, B, G, CAP, CH, D, bf), _state(yb, B, G, CAP, CH, D, bf)
+    calls = [(300, 'left'), (150, 'left'), (64, None), (77, 'holes'), (129, None)]
+    for T, mask in calls:
+        q = cuda(rng.standard_normal((B, T, H, D)).astype(np.float32), bf)
+        sc = cuda((rng.standard_normal((B, T, G)) * 2).round().astype(np.float32) / 2)
+        K = cuda(rng.standard_normal((B, T, G, D)).astype(np.float32), bf)
+        V = cuda(rng.standard_normal((B, T, G, D)).astype(np.float32), bf)
+        valid, run = None, None
+        if mask == 'left':
+            vm = np.ones((B, T), bool)
+            vm[1, :37] = False
+            vm[2, :T - 70] = False
+            valid, run = cuda(vm), True
+        elif mask == 'holes':
+            vm = rng.random((B, T)) > 0.3
+            vm[0] = False
+            valid, run = cuda(vm), False
+        writer = lambda b, t: (K[b, t], V[b, t])  # noqa: E731
+        o_a = yb.sequence(q, sc, writer, valid, CH, st_a)
+        o_b = yb.sequence(q, sc, writer, valid, CH, st_b, capture_safe=True, mask_is_run=run)
+        assert torch.equal(o_a, o_b), f'T={T} {mask}'
+        for f in FIELDS:
+            assert torch.equal(getattr(st_a, f), getattr(st_b, f)), f'T={T} {mask} {f}'
+    # a graph of one left-padded call on a copy of the state, replayed: the same as the eager call
+    T = 200
+    q = cuda(rng.standard_normal((B, T, H, D)).astype(np.float32), bf)
+    sc = cuda((rng.standard_normal((B, T, G)) * 2).round().astype(np.float32) / 2)
+    K = cuda(rng.standard_normal((B, T, G, D)).astype(np.float32), bf)
+    V = cuda(rng.standard_normal((B, T, G, D)).astype(np.float32), bf)
+    vm = np.ones((B, T), bool)
+    vm[0, :20] = False
+    valid = cuda(vm)
+    writer = lambda b, t: (K[b, t], V[b, t])  # noqa: E731
+    st_g = yb.MemoryState(*(getattr(st_b, f).clone() for f in FIELDS))
+    saved = [getattr(st_g, f).clone() for f in FIELDS]
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):      # warm-up (library set-up, allocator pools) on the copy
+        yb.sequence(q, sc, writer, valid, CH, st_g, capture_safe=True, mask_is_run=True)
+    torch.cuda.current_stream().wait_stream(side)
+    for f, t in zip(FIELDS, saved):
+        getattr(st_g, f).copy_(t)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        o_g = yb.sequence(q, sc, writer, valid, CH, st_g, capture_safe=True, mask_is_run=True)
+    graph.replay()
+    o_a = yb.sequence(q, sc, writer, valid, CH, st_a)
+    torch.cuda.synchronize()
+    assert torch.equal(o_g, o_a)
+    for f in FIELDS:
+        assert torch.equal(getattr(st_g, f), getattr(st_a, f)), f
+    del graph

@@ -124,7 +124,8 @@ def _read_timeline(query, src_k, src_v, refs, shift, lo, hi, blocks, chunk, zero
     return out
 
 
-def sequence(query, scores, write_kv, valid, chunk, state=None, capacity=None):
+def sequence(query, scores, write_kv, valid, chunk, state=None, capacity=None, *, capture_safe=False,
+             mask_is_run=None):
     """Prefill anchor read and write (``IndependentGQAMemory._sequence``,
     modeling_yanchor.py:178-275).
 
@@ -141,8 +142,21 @@ def sequence(query, scores, write_kv, valid, chunk, state=None, capacity=None):
     ``chunk``.  Block ``i`` reads the top-CAP over the state's bank and
     blocks ``0 .. i-1``; afterwards the bank becomes the top-CAP over all
     complete blocks and the incomplete tail becomes the pending chunk.
+
+    By default this follows the reference's data flow, which has two host
+    synchronisations: the writer runs only on the tokens some block reads or
+    that stay pending (a ``nonzero`` over the timeline sizes that list), and
+    the read's fast path is chosen by checking on the host that each row's
+    valid tokens form one run.  With ``capture_safe=True`` neither happens,
+    so the call can be captured in a CUDA graph: the writer runs on every
+    slot of the timeline (``B * extent`` rows, entries that no block reads
+    are computed and left unused; results are identical), and the caller
+    states whether each row's valid tokens are one run (``mask_is_run``;
+    not needed without a mask).
     """
     require_cuda(query, scores)
+    if capture_safe and valid is not None and mask_is_run is None:
+        raise ValueError('capture_safe=True with a mask needs mask_is_run (is every row\'s valid run contiguous?)')
     B, T, H, D = query.shape
     G = scores.shape[-1]
     dev = query.device
@@ -202,8 +216,13 @@ def sequence(query, scores, write_kv, valid, chunk, state=None, capacity=None):
         full = fill // chunk
         needed |= live & (slot >= (full * chunk)[:, None])    # the tail that stays pending
     needed &= live & is_new
-    sel_b, sel_slot = needed.nonzero(as_tuple=True)
-    k_new, v_new = write_kv(sel_b, tok[sel_b, sel_slot])
+    if capture_safe:
+        # every slot of the timeline gets a writer row (row b * extent + slot); no list to size
+        sel_b = rows.expand(B, extent).reshape(-1)
+        k_new, v_new = write_kv(sel_b, tok.reshape(-1))
+    else:
+        sel_b, sel_slot = needed.nonzero(as_tuple=True)
+        k_new, v_new = write_kv(sel_b, tok[sel_b, sel_slot])
     k_new = k_new.to(query.dtype).reshape(-1, G, D)
     v_new = v_new.to(query.dtype).reshape(-1, G, D)
 
@@ -224,15 +243,21 @@ def sequence(query, scores, write_kv, valid, chunk, state=None, capacity=None):
         src_k = torch.cat((k_new, zero), 0)
         src_v = torch.cat((v_new, zero), 0)
         offset = 0
-    table[sel_b, shift + sel_slot] = offset + torch.arange(sel_b.numel(), **i64)
+    if capture_safe:
+        table[:, shift:] = torch.where(needed, offset + rows * extent + slot, table[:, shift:])
+    else:
+        table[sel_b, shift + sel_slot] = offset + torch.arange(sel_b.numel(), **i64)
 
     # ---- read: block i attends to prefix entry i ----
     reads = pre_r[:, :-1]
     read_refs = torch.where(reads < 0, -1, table[rows[:, :, None, None], reads.clamp(min=0)])
     run = True                                                # each row's valid tokens are one run
     if order is not None:
-        v8 = valid.to(torch.int8)
-        run = bool((((v8[:, 1:] > v8[:, :-1]).sum(1) + v8[:, 0]) <= 1).all())
+        if mask_is_run is not None:
+            run = bool(mask_is_run)
+        else:
+            v8 = valid.to(torch.int8)
+            run = bool((((v8[:, 1:] > v8[:, :-1]).sum(1) + v8[:, 0]) <= 1).all())
     if run:
         # the read kernel addresses the prompt's own rows: slot s of row b is
         # token s - count + first valid token; only new, live slots are written
