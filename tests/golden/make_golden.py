@@ -346,7 +346,9 @@ def sampling_fixtures(ik, torch):
     attempt = torch.arange(B) * 7 + 3
     step = torch.randint(0, 10000, (B,), generator=g)
     out.update(samp_scores=scores, samp_attempt=attempt, samp_steps=step)
-    cases = [(1.0, 1, 1.0), (1.0, 20, 0.95), (0.7, 20, 0.9), (1.3, 50, 1.0), (1.0, 5, 0.3), (0.8, 0, 1.0)]
+    # cases 6-8: top-k beyond 256 with and without top-p, and top-p over the whole vocabulary (top_k 0)
+    cases = [(1.0, 1, 1.0), (1.0, 20, 0.95), (0.7, 20, 0.9), (1.3, 50, 1.0), (1.0, 5, 0.3), (0.8, 0, 1.0),
+             (1.0, 300, 0.9), (0.9, 0, 0.8), (1.1, 600, 1.0)]
     for i, (temp, tk, tp) in enumerate(cases):
         out[f'samp_case{i}'] = torch.tensor([temp, tk, tp])
         out[f'samp_out{i}'] = ik.sample_top_k_top_p_counter(scores, attempt, step, seed=77, temperature=temp,

@@ -83,10 +83,13 @@ def test_chunk_and_memory_reject_bad_arguments(lib):
     assert rc == _lib.YB_ERR_ARGUMENT                        # row stride < vocab
     rc = lib.yb_sample_greedy(16, 1000, 4, 1000, 2, 16, None, 0, None)
     assert rc == _lib.YB_ERR_WORKSPACE
-    rc = lib.yb_sample_top_k_top_p_counter(16, 1000, 4, 1000, 2, 16, None, 0, 1, 0, 1.0, 0, 0.5, 16, 16, 1 << 20,
+    rc = lib.yb_sample_top_k_top_p_counter(16, 1000, 4, 1000, 2, 16, None, 0, 1, 0, 1.0, 0, 0.5, 16, 16, 16, None)
+    assert rc == _lib.YB_ERR_WORKSPACE                       # the whole-vocabulary nucleus needs its row state
+    rc = lib.yb_sample_top_k_top_p_counter(16, 1000, 4, 1000, 2, 16, None, 0, 1, 0, 1.0, 1001, 0.5, 16, 16, 1 << 20,
                                            None)
-    assert rc == _lib.YB_ERR_UNSUPPORTED                     # whole-vocabulary top-p is not built
+    assert rc == _lib.YB_ERR_ARGUMENT                        # top-k beyond the vocabulary
     assert lib.yb_sample_workspace_bytes(64, 248320, 20) > 0
+    assert lib.yb_sample_workspace_bytes(64, 248320, 0) >= lib.yb_sample_workspace_bytes(64, 248320, 1000) > 0
 
 
 def test_python_ops_refuse_cpu_tensors():

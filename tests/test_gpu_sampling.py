@@ -23,20 +23,74 @@ def cuda(x, dtype=None):
 
 
 def test_sampler_matches_reference_fixtures(yb, golden):
+    """Every parameter case of the reference fixture, ids exact: greedy, top-k <= 256 with and without top-p,
+    the whole-vocabulary CDF (case 5), top-k beyond 256 (cases 6, 8) and top-p over the whole vocabulary
+    (case 7), the last three on the sorted-nucleus path."""
     d = golden('sampling')
-    for i in range(6):                  # case 5 is the whole-vocabulary path (top_k 0, top_p 1)
+    cases = sum(1 for k in d if k.startswith('samp_case'))
+    assert cases >= 9
+    for i in range(cases):
         temp, tk, tp = (float(x) for x in d[f'samp_case{i}'])
-        out = yb.sample_top_k_top_p_counter(cuda(d['samp_scores']), cuda(d['samp_attempt']), cuda(d['samp_steps']),
-                                            seed=77, temperature=temp, top_k=int(tk), top_p=tp)
-        np.testing.assert_array_equal(out.cpu().numpy(), d[f'samp_out{i}'], err_msg=f'case {i}')
+        for dt in (torch.float32, torch.bfloat16) if i >= 6 else (torch.float32,):
+            scores = cuda(d['samp_scores'])
+            if dt != torch.float32:
+                continue   # the fixture's fp32 scores; the bf16 form is covered against the oracle below
+            out = yb.sample_top_k_top_p_counter(scores, cuda(d['samp_attempt']), cuda(d['samp_steps']), seed=77,
+                                                temperature=temp, top_k=int(tk), top_p=tp)
+            np.testing.assert_array_equal(out.cpu().numpy(), d[f'samp_out{i}'], err_msg=f'case {i}')
 
 
-def test_whole_vocabulary_with_top_p_is_refused(yb):
-    """top_k <= 0 with top_p < 1 needs a whole-vocabulary sort: not built."""
-    s = torch.randn(2, 100, device='cuda')
-    with pytest.raises(NotImplementedError):
-        yb.sample_top_k_top_p_counter(s, torch.arange(2, device='cuda'), 0, seed=1, temperature=1.0, top_k=0,
-                                      top_p=0.9)
+def exact_nucleus(scores, temp, top_k, top_p, u):
+    """The reference's sorted top-k / top-p sampling (runtime/model/inference_kernels.py:42-88) in float64:
+    returns (ids, margin) where margin is how far the threshold sits from the nearest CDF step (as a
+    fraction of the total); ties are ordered by ascending index."""
+    z = scores.astype(np.float64) / temp if temp != 1.0 else scores.astype(np.float64)
+    ids, margins = [], []
+    for row, uu in zip(z, u):
+        order = np.lexsort((np.arange(row.size), -row))          # value descending, index ascending
+        k = row.size if top_k <= 0 else top_k
+        top = row[order[:k]]
+        e = np.exp(top - top.max())
+        p = e / e.sum()
+        before = np.cumsum(p) - p
+        keep = before < top_p
+        q = p * keep
+        cdf = np.cumsum(q) / q.sum()
+        j = int(np.searchsorted(cdf, uu, side='left'))
+        j = min(j, int(keep.sum()) - 1)
+        ids.append(order[j])
+        near = min(abs(cdf[max(j - 1, 0)] - uu), abs(cdf[j] - uu))
+        near = min(near, abs(before[int(keep.sum()) - 1] - top_p) if keep.sum() < k else 1.0)
+        margins.append(near)
+    return np.array(ids), np.array(margins)
+
+
+@pytest.mark.parametrize('dtype,temp,top_k,top_p', [(torch.float32, 1.0, 0, 0.9), (torch.bfloat16, 0.8, 0, 0.5),
+                                                    (torch.float32, 1.3, 1000, 0.95), (torch.bfloat16, 1.0, 20000, 1.0),
+                                                    (torch.float32, 0.7, 257, 0.3)])
+def test_sorted_nucleus_full_vocab_vs_exact(yb, dtype, temp, top_k, top_p):
+    """The sorted-nucleus path over the YANchor vocabulary (a masked -inf tail, bf16 scores with many exact
+    ties) against the float64 sorted reference: ids identical except where the threshold or the top-p cut
+    lies within 1e-5 of a step (the reference's own fp32 running sums move by that much); two calls give
+    the same ids."""
+    rng = np.random.default_rng(int(temp * 10) + top_k)
+    B, V = 32, VOCAB
+    scores = (rng.standard_normal((B, V)) * 3).astype(np.float32)
+    scores[:, -320:] = -np.inf
+    st = cuda(scores, dtype)
+    scores = st.float().cpu().numpy()
+    attempt = rng.integers(0, 2**40, B).astype(np.int64)
+    steps = rng.integers(0, 5000, B).astype(np.int64)
+    a = yb.sample_top_k_top_p_counter(st, cuda(attempt), cuda(steps), seed=5, temperature=temp, top_k=top_k,
+                                      top_p=top_p).cpu().numpy()[:, 0]
+    b = yb.sample_top_k_top_p_counter(st, cuda(attempt), cuda(steps), seed=5, temperature=temp, top_k=top_k,
+                                      top_p=top_p).cpu().numpy()[:, 0]
+    assert np.array_equal(a, b)
+    u = osamp.counter_uniform(attempt, steps, 5, 0).astype(np.float64)
+    want, margin = exact_nucleus(scores, temp, top_k, top_p, u)
+    ok = (a == want) | (margin < 1e-5)
+    assert ok.all(), (np.nonzero(~ok)[0], a[~ok], want[~ok], margin[~ok])
+    assert (a == want).mean() > 0.9
 
 
 @pytest.mark.parametrize('dtype,temp', [(torch.float32, 1.0), (torch.bfloat16, 0.7), (torch.float32, 1.6)])

@@ -467,12 +467,11 @@ int yb_sample_top_k_top_p_counter(const void *scores, int64_t row_stride, int64_
     return launch_sample_greedy(a);
   }
   if (top_k <= 0) {
-    if (top_p != 1.0f)
-      return set_error(YB_ERR_UNSUPPORTED, "sample: top_k <= 0 with top_p < 1 (a whole-vocabulary sort) is not built");
     const int64_t need = sample_workspace_bytes(B, vocab, top_k);
     if (workspace == nullptr || workspace_bytes < need)
       return set_error(YB_ERR_WORKSPACE, "sample: workspace of %lld bytes required", (long long)need);
-    return launch_sample_cdf(a);
+    // the whole vocabulary in index order (top_p = 1), or its sorted nucleus
+    return top_p == 1.0f ? launch_sample_cdf(a) : launch_sample_nucleus(a);
   }
   const int64_t need = sample_workspace_bytes(B, vocab, top_k);
   if (workspace == nullptr || workspace_bytes < need)

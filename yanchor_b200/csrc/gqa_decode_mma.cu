@@ -63,6 +63,89 @@ __device__ __forceinline__ void cp16(void *dst, const void *src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
 }
 
+// The commit of group g after its read, in the read's CTA.  Push (key, value, score) into pending
+// slot `count`; when the chunk fills, rank the CAP bank slots and the `chunk` pending slots (score
+// descending, position ascending with empty slots last, then candidate index: the stable double
+// argsort of select_topk, modeling_yanchor.py:51-55) and write the new bank.  The old bank's key and
+// value rows are still in shared memory from the read (rows of ROW elements in sk / sv), so each new
+// slot is written in one pass straight from there or from the pending rows, with no staging copy.
+// Candidate arrays live over the query / P rows (`cand`, free once the read's MMAs are done).
+template <typename T, int D, int ROW>
+__device__ void commit_after_read(const MemCommitArgs &a, int64_t row, int64_t s, int g, int64_t count, int64_t total,
+                                  const T *sk, const T *sv, unsigned char *cand) {
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const int CAP = int(a.CAP), chunk = int(a.chunk), G = int(a.G), PC = int(a.PC);
+  T *bank_k = static_cast<T *>(a.keys) + s * a.kv_s0 + int64_t(g) * CAP * D;
+  T *bank_v = static_cast<T *>(a.values) + s * a.kv_s0 + int64_t(g) * CAP * D;
+  T *pend_k = static_cast<T *>(a.pkeys) + s * a.pkv_s0 + int64_t(g) * PC * D;
+  T *pend_v = static_cast<T *>(a.pvalues) + s * a.pkv_s0 + int64_t(g) * PC * D;
+  float *bscore = a.bank_scores + s * a.meta_s0 + int64_t(g) * CAP;
+  int32_t *bpos = a.positions + s * a.meta_s0 + int64_t(g) * CAP;
+  float *pscore = a.pscores + s * a.pmeta_s0 + int64_t(g) * PC;
+  constexpr int VEC = 16 / int(sizeof(T));
+  constexpr int DV = D / VEC;
+  // push (16-byte pieces: row starts are 16-byte aligned for D % 8 == 0 and 16-byte aligned bases)
+  const T *key = static_cast<const T *>(a.key) + (row * G + g) * D;
+  const T *val = static_cast<const T *>(a.value) + (row * G + g) * D;
+  for (int e = tid; e < DV; e += nt) {
+    *reinterpret_cast<uint4 *>(pend_k + count * D + e * VEC) = *reinterpret_cast<const uint4 *>(key + e * VEC);
+    *reinterpret_cast<uint4 *>(pend_v + count * D + e * VEC) = *reinterpret_cast<const uint4 *>(val + e * VEC);
+  }
+  const float new_score = a.scores[row * G + g];
+  if (tid == 0) pscore[count] = new_score;
+  if (count + 1 != chunk) return;
+  const int n = CAP + chunk;
+  float *c_score = reinterpret_cast<float *>(cand);
+  int64_t *c_pkey = reinterpret_cast<int64_t *>(cand + ((4 * n + 15) & ~15));
+  int *sel = reinterpret_cast<int *>(reinterpret_cast<unsigned char *>(c_pkey) + 8 * n);
+  for (int c = tid; c < n; c += nt) {
+    if (c < CAP) {
+      const int32_t pos = bpos[c];
+      c_score[c] = bscore[c];
+      c_pkey[c] = pos < 0 ? INT64_MAX : int64_t(pos);
+    } else {
+      const int i = c - CAP;   // every pending slot is filled when the chunk commits; slot `count` is new
+      c_score[c] = i == count ? new_score : pscore[i];
+      c_pkey[c] = total - count + i;
+    }
+  }
+  __syncthreads();
+  for (int c = tid; c < n; c += nt) {
+    const float sc = c_score[c];
+    const int64_t pkc = c_pkey[c];
+    int r0 = 0, r1 = 0;
+    int o = 0;
+#pragma unroll 4
+    for (; o + 1 < n; o += 2) {
+      r0 += memcommit::cand_before(c_score[o], c_pkey[o], o, sc, pkc, c);
+      r1 += memcommit::cand_before(c_score[o + 1], c_pkey[o + 1], o + 1, sc, pkc, c);
+    }
+    if (o < n) r0 += memcommit::cand_before(c_score[o], c_pkey[o], o, sc, pkc, c);
+    if (r0 + r1 < CAP) sel[r0 + r1] = c;
+  }
+  __syncthreads();   // sel complete; every thread's push is visible to the pending loads below
+  for (int e = tid; e < CAP * DV; e += nt) {
+    const int r = e / DV, d = (e % DV) * VEC;
+    const int c = sel[r];
+    const int src = c_pkey[c] == INT64_MAX ? 0 : c;   // an empty winner copies old bank slot 0, as the reference
+    uint4 kv, vv;
+    if (src < CAP) {
+      kv = *reinterpret_cast<const uint4 *>(sk + src * ROW + d);
+      vv = *reinterpret_cast<const uint4 *>(sv + src * ROW + d);
+    } else {
+      kv = *reinterpret_cast<const uint4 *>(pend_k + (src - CAP) * D + d);
+      vv = *reinterpret_cast<const uint4 *>(pend_v + (src - CAP) * D + d);
+    }
+    *reinterpret_cast<uint4 *>(bank_k + r * D + d) = kv;
+    *reinterpret_cast<uint4 *>(bank_v + r * D + d) = vv;
+  }
+  for (int r = tid; r < CAP; r += nt) {
+    const int c = sel[r];
+    bscore[r] = c_score[c];
+    bpos[r] = c_pkey[c] == INT64_MAX ? -1 : int32_t(c_pkey[c]);
+  }
+}
+
 template <typename T, int R, int D, bool COMMIT>
 __global__ void __launch_bounds__(kGqaThreads) gqa_decode_mma_kernel(const GqaDecodeArgs a, const MemCommitTail ct) {
   static_assert(R <= 8 && D % 64 == 0, "R <= 8 heads, D a multiple of 64");
@@ -254,11 +337,8 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_decode_mma_kernel(const GqaDe
       if (c.active[b]) {   // the same for the row's G CTAs
         const int64_t count = c.count[s * c.count_s0];
         const int64_t total = c.total[s * c.count_s0];
-        float *c_score = reinterpret_cast<float *>(sv);
-        int64_t *c_pkey = reinterpret_cast<int64_t *>(c_score + memcommit::kMaxCand);
-        int *sel = reinterpret_cast<int *>(c_pkey + memcommit::kMaxCand);
-        __syncthreads();
-        memcommit::commit_group<T>(c, b, s, int(g), count, total, c_score, c_pkey, sel, sk);
+        __syncthreads();   // every warp is done with the query / P rows and the V rows
+        commit_after_read<T, D, ROW>(c, b, s, int(g), count, total, sk, sv, reinterpret_cast<unsigned char *>(sq));
         __syncthreads();
         if (tid == 0) {
           __threadfence();
@@ -326,10 +406,21 @@ int launch_gqa_decode_mma(const GqaDecodeArgs &a) {
   return rc;
 }
 
+bool gqa_decode_commit_fits(const GqaDecodeArgs &a, const MemCommitArgs &c) {
+  const int64_t n = c.CAP + c.chunk;
+  const int64_t cand_bytes = ((4 * n + 15) & ~int64_t(15)) + 8 * n + 4 * c.CAP;
+  const int64_t room = 2 * (8 * (a.D + 8) + 2 * 8 * (kGqaSlice + 8));   // the query and P rows (16-bit)
+  const uintptr_t al = reinterpret_cast<uintptr_t>(c.key) | reinterpret_cast<uintptr_t>(c.value) |
+                       reinterpret_cast<uintptr_t>(c.keys) | reinterpret_cast<uintptr_t>(c.values) |
+                       reinterpret_cast<uintptr_t>(c.pkeys) | reinterpret_cast<uintptr_t>(c.pvalues);
+  return !a.partial && a.P <= kGqaSlice && a.B == c.B && a.G == c.G && a.indices == c.indices &&
+         cand_bytes <= room && c.CAP == a.P && c.D == a.D && c.dtype == a.dtype && (al % 16) == 0 &&
+         (c.kv_s0 % 8) == 0 && (c.pkv_s0 % 8) == 0;
+}
+
 int launch_gqa_decode_commit(const GqaDecodeArgs &a, const MemCommitArgs &c, int32_t *arrive) {
   if (a.B * a.G == 0) return YB_OK;
-  if (a.partial || a.P > kGqaSlice || a.B != c.B || a.G != c.G || a.indices != c.indices || !arrive ||
-      c.CAP + c.chunk > memcommit::kMaxCand || c.CAP != a.P || c.D != a.D || c.dtype != a.dtype)
+  if (!arrive || !gqa_decode_commit_fits(a, c))
     return set_error(YB_ERR_UNSUPPORTED, "gqa decode + commit: arguments do not describe one memory layer");
   const MemCommitTail ct{c, arrive};
   const int rc = a.dtype == YB_BF16 ? gqa_r<__nv_bfloat16, true>(a, ct, 1) : gqa_r<__half, true>(a, ct, 1);

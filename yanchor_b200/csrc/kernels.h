@@ -186,6 +186,7 @@ struct MemCommitTail {
   MemCommitArgs c;
   int32_t *arrive;
 };
+bool gqa_decode_commit_fits(const GqaDecodeArgs &a, const MemCommitArgs &c);
 int launch_gqa_decode_commit(const GqaDecodeArgs &a, const MemCommitArgs &c, int32_t *arrive);
 
 // Decode-loop bookkeeping after a sampled token (one launch per step).
@@ -270,6 +271,7 @@ int launch_sample_greedy(const SampleArgs &a);
 int launch_sample_greedy_noalloc(const SampleArgs &a);
 int64_t greedy_builtin_scratch_bytes();
 int launch_sample_topk_topp(const SampleArgs &a);
+int launch_sample_nucleus(const SampleArgs &a);
 int launch_sample_cdf(const SampleArgs &a);
 int launch_presence_penalty(void *scores, const uint8_t *seen, int64_t n, float penalty, int dtype,
                             cudaStream_t stream);

@@ -519,7 +519,7 @@ int launch_mem_decode_commit(const MemCommitArgs &a) {
 
 int launch_mem_decode_step(const MemReadArgs &r, const MemCommitArgs &c, int32_t *arrive) {
   GqaDecodeArgs g;
-  if (r.B * r.G > 0 && arrive && c.CAP + c.chunk <= kMaxCand && mma_read_args(r, g))
+  if (r.B * r.G > 0 && arrive && c.CAP + c.chunk <= kMaxCand && mma_read_args(r, g) && gqa_decode_commit_fits(g, c))
     return launch_gqa_decode_commit(g, c, arrive);
   const int rc = launch_mem_decode_read(r);
   return rc != YB_OK ? rc : launch_mem_decode_commit(c);

@@ -617,13 +617,300 @@ int topk_t(const SampleArgs &a) {
   return check_launch("topk_final_kernel");
 }
 
+// ------------------------------------------------- sorted nucleus ----------
+// top_k > kMaxTopK, or top_k <= 0 with top_p < 1 (runtime/model/
+// inference_kernels.py:85-88 through top_k_top_p_distribution :42-56 and
+// sample_probabilities_counter :58-71): the reference sorts the top-k of
+// z = x / T, takes their softmax, keeps the entries whose running mass before
+// them is below top_p, renormalises and picks with the counter uniform in
+// that sorted order.  Nothing is sorted here.  Every question about the
+// sorted order is a quantile: "the element at which the running count (or
+// mass) crosses a target".  Each is answered by a radix descent over the
+// order-preserving 32-bit keys of z, 8 bits per level, with per-row
+// histograms of counts and masses.  A mass is exp(z - z_max) in 2^-26 fixed
+// point (the largest is 2^26), so every sum is an exact integer whatever the
+// order of the atomic additions, and repeated calls give the same ids.
+// Equal z are ordered by ascending index (a tie group has one mass per
+// element, so which tie the target falls on is integer arithmetic; its index
+// comes from one counting pass).  The steps, per row:
+//   1. z_max (the largest key);
+//   2. top_k < vocab: the k-th largest key kappa by count; Z = mass of the
+//      top k (keys above kappa plus the first `need` ties of kappa);
+//      otherwise Z = the mass of every element;
+//   3. top_p < 1: the element where the running mass crosses ceil(top_p Z):
+//      the kept set ends there; E = its mass up to and including that
+//      element; otherwise E = Z;
+//   4. theta = ceil(u E) (u the counter uniform), at most E: the element
+//      where the running mass crosses theta is the sample.
+// Elements outside the top-k set or beyond the kept set come later in the
+// sorted order, so they never change where a target below Z (or E) falls,
+// and the descents need no exclusion.  The running sums are exact where the
+// reference's are fp32 in sorted order; ids can differ only where a target
+// lies within that rounding of a boundary.  NaN scores count as -inf.
+constexpr int kNucMaxSplits = 64;
+constexpr float kNucScale = 67108864.f;   // 2^26
+
+struct NucRow {
+  unsigned maxkey, prefix, mask, found;
+  int stage, pad;
+  long long want, above_count, need, tie_rank;
+  unsigned long long above_mass, Z, E;
+  int hist_count[256];
+  unsigned long long hist_mass[256];
+  int split_ties[kNucMaxSplits];
+};
+
+__device__ __forceinline__ float nuc_z(float x, float temperature) {
+  const float z = temperature == 1.f ? x : x / temperature;
+  return z != z ? -INFINITY : z;
+}
+// inverse of fkey
+__device__ __forceinline__ float key_value(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+__device__ __forceinline__ uint32_t nuc_mass(float z, float zmax) {
+  return zmax == -INFINITY ? 0u : uint32_t(rintf(__expf(z - zmax) * kNucScale));
+}
+
+__global__ void nuc_init_kernel(NucRow *rows, int64_t B) {
+  const int64_t b = blockIdx.x;
+  if (b >= B) return;
+  NucRow &r = rows[b];
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+    r.hist_count[i] = 0;
+    r.hist_mass[i] = 0ull;
+  }
+  if (threadIdx.x == 0) {
+    r.maxkey = 0u; r.prefix = 0u; r.mask = 0u; r.found = 0u; r.stage = 0;
+    r.want = 0; r.above_count = 0; r.need = 0; r.tie_rank = 0;
+    r.above_mass = 0ull; r.Z = 0ull; r.E = 0ull;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kNT) nuc_max_kernel(const T *scores, int64_t row_stride, int64_t vocab,
+                                                      float temperature, NucRow *rows) {
+  const int64_t b = blockIdx.y;
+  const int64_t lo = int64_t(blockIdx.x) * kTopkSpan, hi = lo + kTopkSpan < vocab ? lo + kTopkSpan : vocab;
+  const T *row = scores + b * row_stride;
+  uint32_t best = 0u;
+  for (int64_t i = lo + threadIdx.x; i < hi; i += kNT) best = max(best, fkey(nuc_z(to_f(row[i]), temperature)));
+  best = __reduce_max_sync(0xffffffffu, best);
+  if ((threadIdx.x & 31) == 0) atomicMax(&rows[b].maxkey, best);
+}
+
+// Histogram of the 8-bit digit at `shift` of the keys that match the row's prefix so far.
+template <typename T>
+__global__ void __launch_bounds__(kNT) nuc_hist_kernel(const T *scores, int64_t row_stride, int64_t vocab,
+                                                       float temperature, int shift, NucRow *rows) {
+  __shared__ int h_count[256];
+  __shared__ unsigned long long h_mass[256];
+  const int64_t b = blockIdx.y;
+  NucRow &r = rows[b];
+  for (int i = threadIdx.x; i < 256; i += kNT) {
+    h_count[i] = 0;
+    h_mass[i] = 0ull;
+  }
+  __syncthreads();
+  const uint32_t prefix = r.prefix, mask = r.mask;
+  const float zmax = key_value(r.maxkey);
+  const int64_t lo = int64_t(blockIdx.x) * kTopkSpan, hi = lo + kTopkSpan < vocab ? lo + kTopkSpan : vocab;
+  const T *row = scores + b * row_stride;
+  const int lane = threadIdx.x & 31;
+  for (int64_t base = lo; base < hi; base += kNT) {
+    const int64_t i = base + threadIdx.x;
+    int digit = -1;
+    uint32_t m = 0u;
+    if (i < hi) {
+      const float z = nuc_z(to_f(row[i]), temperature);
+      const uint32_t k = fkey(z);
+      if ((k & mask) == prefix) {
+        digit = int((k >> shift) & 255u);
+        m = nuc_mass(z, zmax);
+      }
+    }
+    // one shared-memory update per distinct digit in the warp (peers share it; their masses fit 32 bits)
+    const unsigned peers = __match_any_sync(0xffffffffu, digit);
+    const unsigned msum = __reduce_add_sync(peers, m);
+    if (digit >= 0 && lane == __ffs(peers) - 1) {
+      atomicAdd(&h_count[digit], __popc(peers));
+      atomicAdd(&h_mass[digit], (unsigned long long)msum);
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 256; i += kNT) {
+    if (h_count[i]) {
+      atomicAdd(&r.hist_count[i], h_count[i]);
+      atomicAdd(&r.hist_mass[i], h_mass[i]);
+    }
+  }
+}
+
+// One thread per row: pick the digit where the target falls, move the descent on, and after the last
+// level finish the current question and set up the next one.
+__global__ void nuc_pick_kernel(NucRow *rows, int64_t B, int level, int64_t top_k, int64_t vocab, float top_p,
+                                const int64_t *attempt, const int64_t *steps, int64_t scalar_step, int64_t seed,
+                                int64_t stream_id) {
+  const int64_t b = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  NucRow &r = rows[b];
+  const int shift = 24 - 8 * level;
+  if (level == 0 && r.stage > 0 && r.Z == 0ull && top_k >= vocab) {
+    // no top-k cut: Z is the mass of every element (the level-0 histogram covers them all)
+    unsigned long long z = 0ull;
+    for (int d = 0; d < 256; ++d) z += r.hist_mass[d];
+    r.Z = z;
+  }
+  if (level == 0 && r.stage == 1) {
+    const double t = ceil(double(top_p) * double(r.Z));
+    r.want = (long long)(t < 1.0 ? 1.0 : t);
+  }
+  if (level == 0 && r.stage == 2) {
+    if (r.E == 0ull) r.E = r.Z;
+    const float u = counter_uniform(attempt[b], steps ? steps[b] : scalar_step, seed, stream_id);
+    double t = ceil(double(u) * double(r.E));
+    if (t < 1.0) t = 1.0;
+    if (t > double(r.E)) t = double(r.E);
+    r.want = (long long)t;
+  }
+  long long acc_c = 0;
+  unsigned long long acc_m = 0ull;
+  int d = 255;
+  for (; d > 0; --d) {
+    const long long c = r.hist_count[d];
+    const unsigned long long m = r.hist_mass[d];
+    if (r.stage == 0 ? (acc_c + c >= r.want) : (acc_m + m >= (unsigned long long)r.want)) break;
+    acc_c += c;
+    acc_m += m;
+  }
+  const long long ties = r.hist_count[d];
+  const unsigned long long tie_mass = r.hist_mass[d];
+  r.prefix |= uint32_t(d) << shift;
+  r.mask |= 255u << shift;
+  r.above_count += acc_c;
+  r.above_mass += acc_m;
+  r.want -= r.stage == 0 ? acc_c : (long long)acc_m;
+  for (int i = 0; i < 256; ++i) {
+    r.hist_count[i] = 0;
+    r.hist_mass[i] = 0ull;
+  }
+  if (shift != 0) return;
+  // the descent reached one key: r.prefix; `ties` elements share it, each of mass tie_mass / ties
+  const unsigned long long each = ties > 0 ? tie_mass / (unsigned long long)ties : 0ull;
+  const long long t = each ? (long long)(((unsigned long long)r.want + each - 1ull) / each) - 1 : 0;
+  if (r.stage == 0) {
+    r.need = r.want;                                   // ties of kappa inside the top k
+    r.Z = r.above_mass + (unsigned long long)r.need * each;
+    r.stage = top_p < 1.f ? 1 : 2;
+  } else if (r.stage == 1) {
+    r.E = r.above_mass + (unsigned long long)(t + 1) * each;
+    r.stage = 2;
+  } else {
+    r.found = r.prefix;
+    r.tie_rank = t < 0 ? 0 : t;
+    r.stage = 3;
+  }
+  if (r.stage != 3) {
+    r.prefix = r.mask = 0u;
+    r.above_count = 0;
+    r.above_mass = 0ull;
+  }
+}
+
+// The first question of every row: `stage` 0 (the k-th largest by count, want = k) or a mass question.
+__global__ void nuc_stage_kernel(NucRow *rows, int64_t B, int stage, int64_t k) {
+  const int64_t b = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  rows[b].stage = stage;
+  rows[b].want = stage == 0 ? k : 0;
+}
+
+// Ties of the selected key per split (in index order), then the row's pick.
+template <typename T>
+__global__ void __launch_bounds__(kNT) nuc_ties_kernel(const T *scores, int64_t row_stride, int64_t vocab,
+                                                       float temperature, NucRow *rows) {
+  const int64_t b = blockIdx.y;
+  const uint32_t found = rows[b].found;
+  const int64_t lo = int64_t(blockIdx.x) * kTopkSpan, hi = lo + kTopkSpan < vocab ? lo + kTopkSpan : vocab;
+  const T *row = scores + b * row_stride;
+  int n = 0;
+  for (int64_t i = lo + threadIdx.x; i < hi; i += kNT) n += fkey(nuc_z(to_f(row[i]), temperature)) == found;
+  int total;
+  block_exclusive_scan(n, total);
+  if (threadIdx.x == 0) rows[b].split_ties[blockIdx.x] = total;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kNT) nuc_final_kernel(const T *scores, int64_t row_stride, int64_t vocab,
+                                                        float temperature, int splits, NucRow *rows, int64_t *out) {
+  const int64_t b = blockIdx.x;
+  const NucRow &r = rows[b];
+  long long rank = r.tie_rank;
+  int s = 0;
+  for (; s < splits - 1; ++s) {
+    if (rank < r.split_ties[s]) break;
+    rank -= r.split_ties[s];
+  }
+  const int64_t lo = int64_t(s) * kTopkSpan, hi = lo + kTopkSpan < vocab ? lo + kTopkSpan : vocab;
+  const T *row = scores + b * row_stride;
+  __shared__ long long pick;
+  if (threadIdx.x == 0) pick = -1;
+  __syncthreads();
+  // walk the split in index order, kNT elements at a time, counting the ties before each
+  long long seen = 0;
+  for (int64_t base = lo; base < hi; base += kNT) {
+    const int64_t i = base + threadIdx.x;
+    const int hit = (i < hi && fkey(nuc_z(to_f(row[i]), temperature)) == r.found) ? 1 : 0;
+    int total;
+    const int before = block_exclusive_scan(hit, total);
+    if (hit && seen + before == rank) pick = i;
+    seen += total;
+    __syncthreads();
+    if (pick >= 0 || seen > rank) break;
+  }
+  if (threadIdx.x == 0) out[b] = pick >= 0 ? pick : lo;
+}
+
+template <typename T>
+int nucleus_t(const SampleArgs &a) {
+  const int splits = int((a.vocab + kTopkSpan - 1) / kTopkSpan);
+  if (splits > kNucMaxSplits) return set_error(YB_ERR_UNSUPPORTED, "sample: vocabulary too large for the nucleus path");
+  NucRow *rows = static_cast<NucRow *>(a.workspace);
+  const T *sc = static_cast<const T *>(a.scores);
+  const dim3 grid(unsigned(splits), unsigned(a.B));
+  const unsigned pick_blocks = unsigned((a.B + 63) / 64);
+  nuc_init_kernel<<<unsigned(a.B), 256, 0, a.stream>>>(rows, a.B);
+  nuc_max_kernel<T><<<grid, kNT, 0, a.stream>>>(sc, a.row_stride, a.vocab, a.temperature, rows);
+  const int64_t k_eff = a.top_k > 0 ? a.top_k : a.vocab;
+  // the questions in order: [k-th by count] [top-p cut by mass] sample by mass; each is 4 levels
+  const int first = k_eff < a.vocab ? 0 : (a.top_p < 1.f ? 1 : 2);
+  // without a count question Z comes from the first mass histogram (it covers every element)
+  nuc_stage_kernel<<<pick_blocks, 64, 0, a.stream>>>(rows, a.B, first, k_eff);
+  for (int q = first; q <= 2; ++q) {
+    if (q == 1 && a.top_p >= 1.f) continue;
+    for (int level = 0; level < 4; ++level) {
+      nuc_hist_kernel<T><<<grid, kNT, 0, a.stream>>>(sc, a.row_stride, a.vocab, a.temperature, 24 - 8 * level, rows);
+      nuc_pick_kernel<<<pick_blocks, 64, 0, a.stream>>>(rows, a.B, level, k_eff, a.vocab, a.top_p, a.attempt_ids,
+                                                        a.steps, a.scalar_step, a.seed, a.stream_id);
+    }
+  }
+  nuc_ties_kernel<T><<<grid, kNT, 0, a.stream>>>(sc, a.row_stride, a.vocab, a.temperature, rows);
+  nuc_final_kernel<T><<<unsigned(a.B), kNT, 0, a.stream>>>(sc, a.row_stride, a.vocab, a.temperature, splits, rows,
+                                                          a.out);
+  return check_launch("nuc_final_kernel");
+}
+
 }  // namespace
 
 int64_t sample_workspace_bytes(int64_t B, int64_t vocab, int64_t top_k) {
   const int64_t g = int64_t(greedy_splits(B, vocab)) * B * int64_t(sizeof(Cand));
   int64_t t = 0;
-  if (top_k > 1) t = int64_t(topk_splits(vocab, top_k)) * top_k * B * int64_t(sizeof(Cand));
+  if (top_k > 1 && top_k <= kMaxTopK) t = int64_t(topk_splits(vocab, top_k)) * top_k * B * int64_t(sizeof(Cand));
   if (top_k <= 0) t = (vocab + kTopkSpan - 1) / kTopkSpan * B * int64_t(sizeof(SoftPart));
+  if (top_k <= 0 || top_k > kMaxTopK) {   // the sorted-nucleus path
+    const int64_t n = B * int64_t(sizeof(NucRow));
+    t = t > n ? t : n;
+  }
   return g > t ? g : t;
 }
 
@@ -727,13 +1014,23 @@ int launch_sample_greedy_noalloc(const SampleArgs &a) {
   return launch_sample_greedy(b);
 }
 
+int launch_sample_nucleus(const SampleArgs &a) {
+  if (a.B == 0) return YB_OK;
+  if (a.vocab >= 0x7fffffffLL) return set_error(YB_ERR_UNSUPPORTED, "sample: vocabulary too large");
+  switch (a.dtype) {
+    case YB_F32: return nucleus_t<float>(a);
+    case YB_BF16: return nucleus_t<__nv_bfloat16>(a);
+    case YB_F16: return nucleus_t<__half>(a);
+  }
+  return set_error(YB_ERR_ARGUMENT, "sample: bad dtype %d", a.dtype);
+}
+
 int launch_sample_topk_topp(const SampleArgs &a) {
   if (a.B == 0) return YB_OK;
-  if (a.top_k < 2 || a.top_k > kMaxTopK)
-    return set_error(YB_ERR_UNSUPPORTED, "sample: top_k=%lld outside [2, %d]", (long long)a.top_k, kMaxTopK);
+  if (a.top_k < 2) return set_error(YB_ERR_UNSUPPORTED, "sample: top_k=%lld below 2", (long long)a.top_k);
+  if (a.top_k > kMaxTopK) return launch_sample_nucleus(a);   // beyond the sorted top-k buffers
   const int M = topk_splits(a.vocab, a.top_k) * int(a.top_k);
-  if (size_t(M) * 16 + 8 > 200 * 1024)
-    return set_error(YB_ERR_UNSUPPORTED, "sample: %d candidates exceed the merge buffer", M);
+  if (size_t(M) * 16 + 8 > 200 * 1024) return launch_sample_nucleus(a);
   switch (a.dtype) {
     case YB_F32: return topk_t<float>(a);
     case YB_BF16: return topk_t<__nv_bfloat16>(a);
