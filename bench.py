@@ -1149,6 +1149,94 @@ def cpu_decode_parallel(steps=2, B=64, warmup=0):
     return B * steps / dt, dt, workers
 
 
+def run_comparators(args):
+    """Context only (not the reference arm): the GPU kernels the reference itself uses for this path,
+    timed on the same B200 at the bench's shapes with CUDA events, beside this library's kernels.
+
+    * fla 0.5.1 (the third-party package the reference pins, requirements.txt:20):
+      chunk_gated_delta_rule at config 1 and fused_recurrent_gated_delta_rule for one decode layer at
+      B=64, as modeling_yanchor.py:397-406 binds them;
+    * the reference's Triton anchor-memory kernels from its install (runtime/model/independent_memory.py:
+      committed_gqa then commit_decode, 8 layers at B=64 with full banks and staggered pending counts).
+    Each runs once to compile, then is timed; a failure is reported, not raised."""
+    import torch
+    import yanchor_b200 as yb
+    dev = torch.device('cuda', 0)
+    stream = torch.cuda.current_stream(dev)
+    bf = torch.bfloat16
+    gen = torch.Generator(device=dev).manual_seed(7)
+    out = {}
+
+    def timed(name, fn, iters=5):
+        try:
+            fn()
+            torch.cuda.synchronize()
+            out[name] = round(time_events(torch, fn, iters, stream), 4)
+        except Exception as e:  # noqa: BLE001
+            out[name] = f'failed: {type(e).__name__}: {str(e)[:200]}'
+
+    B, T, H, K = 8, 8192, 32, 128
+    q, k, v = (torch.randn(B, T, H, K, generator=gen, device=dev).to(bf) for _ in range(3))
+    g = torch.nn.functional.logsigmoid(torch.randn(B, T, H, generator=gen, device=dev))
+    beta = torch.randn(B, T, H, generator=gen, device=dev).sigmoid().to(bf)
+    h0 = 0.02 * torch.randn(B, H, K, K, generator=gen, device=dev)
+    timed('yanchor_b200_chunk_config1_ms', lambda: yb.chunk_gated_delta_rule(
+        q, k, v, g, beta, initial_state=h0, output_final_state=True, use_qk_l2norm_in_kernel=True))
+    try:
+        from fla.ops.gated_delta_rule import chunk_gated_delta_rule as fla_chunk
+        from fla.ops.gated_delta_rule import fused_recurrent_gated_delta_rule as fla_rec
+        timed('fla_chunk_config1_ms', lambda: fla_chunk(q, k, v, g=g, beta=beta, initial_state=h0,
+                                                           output_final_state=True, use_qk_l2norm_in_kernel=True))
+    except Exception as e:  # noqa: BLE001
+        out['fla_chunk_config1_ms'] = f'failed: {type(e).__name__}: {str(e)[:200]}'
+        fla_rec = None
+    del q, k, v, g, beta, h0
+    Bd = 64
+    qd = torch.randn(Bd, 1, H_K, DK, generator=gen, device=dev).to(bf)
+    kd = torch.randn(Bd, 1, H_K, DK, generator=gen, device=dev).to(bf)
+    vd = torch.randn(Bd, 1, H_V, DV, generator=gen, device=dev).to(bf)
+    gd = torch.nn.functional.logsigmoid(torch.randn(Bd, 1, H_V, generator=gen, device=dev))
+    bd = torch.randn(Bd, 1, H_V, generator=gen, device=dev).sigmoid().to(bf)
+    sd = 0.02 * torch.randn(Bd, H_V, DK, DV, generator=gen, device=dev)
+    timed('yanchor_b200_recurrent_b64_layer_ms', lambda: yb.fused_recurrent_gated_delta_rule(
+        qd, kd, vd, g=gd, beta=bd, initial_state=sd, output_final_state=True, use_qk_l2norm_in_kernel=True,
+        inplace=True), iters=20)
+    if fla_rec is not None:
+        qr, kr = qd.repeat_interleave(H_V // H_K, dim=2), kd.repeat_interleave(H_V // H_K, dim=2)
+        timed('fla_recurrent_b64_layer_ms', lambda: fla_rec(qr, kr, vd, g=gd, beta=bd, initial_state=sd,
+                                                            output_final_state=True, use_qk_l2norm_in_kernel=True),
+              iters=20)
+    # anchor memory decode, 8 layers
+    mems = [yb.MemoryState.empty(Bd, MEM_G, MEM_CAP, MEM_CHUNK, MEM_D, dev, bf) for _ in range(L_MEM)]
+    mq = torch.randn(L_MEM, Bd, 1, MEM_H, MEM_D, generator=gen, device=dev).to(bf)
+    mk = torch.randn(L_MEM, Bd, 1, MEM_G, MEM_D, generator=gen, device=dev).to(bf)
+    ms = torch.randn(L_MEM, Bd, 1, MEM_G, generator=gen, device=dev)
+    act = torch.ones(Bd, device=dev, dtype=torch.bool)
+    for _ in range(MEM_CHUNK + 2):
+        for i, m in enumerate(mems):
+            yb.memory_decode_step(mq[i], mk[i], mk[i], ms[i], act, MEM_CHUNK, m)
+    for m in mems:
+        m.count.copy_(torch.arange(Bd, device=dev) % MEM_CHUNK)
+    timed('yanchor_b200_memory_8_layers_ms', lambda: [yb.memory_decode_step(mq[i], mk[i], mk[i], ms[i], act,
+                                                                            MEM_CHUNK, m) for i, m in enumerate(mems)],
+          iters=20)
+    if reference_installed():
+        try:
+            sys.path.append(os.path.join(REF_ROOT, 'runtime'))
+            import importlib
+            ref_mem = importlib.import_module('model.independent_memory')
+
+            def ref_layers():
+                for i, m in enumerate(mems):
+                    ref_mem.committed_gqa(mq[i], m, None)
+                    ref_mem.commit_decode(mk[i], mk[i], ms[i], act, MEM_CHUNK, m, None)
+            timed('reference_triton_memory_8_layers_ms', ref_layers, iters=20)
+        except Exception as e:  # noqa: BLE001
+            out['reference_triton_memory_8_layers_ms'] = f'failed: {type(e).__name__}: {str(e)[:200]}'
+    print(json.dumps({'comparators': out, 'how': 'CUDA events, eager launches (no CUDA graph) for every entry, '
+                      'same inputs per pair'}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
@@ -1166,6 +1254,8 @@ def main():
                                        'topk'], help='run one kernel family (small ncu captures)')
     ap.add_argument('--prefill-batch', type=int, default=8)
     ap.add_argument('--cpu-sample', nargs=3, type=int, metavar=('B', 'STEPS', 'WARMUP'), help=argparse.SUPPRESS)
+    ap.add_argument('--comparators', action='store_true',
+                    help='time the reference\'s own GPU kernels (fla, its Triton memory kernels) beside these')
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get('WORLD_SIZE', '1'))
@@ -1176,6 +1266,9 @@ def main():
     if args.cpu_sample:
         line, _ = cpu_sample_line(*args.cpu_sample)
         print(json.dumps(line), flush=True)
+        return
+    if args.comparators:
+        run_comparators(args)
         return
     if args.only:
         run_only(args)

@@ -124,20 +124,32 @@ __device__ void commit_after_read(const MemCommitArgs &a, int64_t row, int64_t s
     if (r0 + r1 < CAP) sel[r0 + r1] = c;
   }
   __syncthreads();   // sel complete; every thread's push is visible to the pending loads below
-  for (int e = tid; e < CAP * DV; e += nt) {
-    const int r = e / DV, d = (e % DV) * VEC;
-    const int c = sel[r];
-    const int src = c_pkey[c] == INT64_MAX ? 0 : c;   // an empty winner copies old bank slot 0, as the reference
-    uint4 kv, vv;
-    if (src < CAP) {
-      kv = *reinterpret_cast<const uint4 *>(sk + src * ROW + d);
-      vv = *reinterpret_cast<const uint4 *>(sv + src * ROW + d);
-    } else {
-      kv = *reinterpret_cast<const uint4 *>(pend_k + (src - CAP) * D + d);
-      vv = *reinterpret_cast<const uint4 *>(pend_v + (src - CAP) * D + d);
+  // the new bank, keys then values: each thread loads all its pieces first (old bank rows from shared
+  // memory, pending rows from global memory, all in flight together), then stores them
+  constexpr int PER = 16;
+  for (int half = 0; half < 2; ++half) {
+    const T *old_rows = half ? sv : sk;
+    const T *pend = half ? pend_v : pend_k;
+    T *bank = half ? bank_v : bank_k;
+    for (int base = 0; base < CAP * DV; base += nt * PER) {
+      uint4 buf[PER];
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int e = base + tid + i * nt;
+        if (e < CAP * DV) {
+          const int r = e / DV, d = (e % DV) * VEC;
+          const int c = sel[r];
+          const int src = c_pkey[c] == INT64_MAX ? 0 : c;   // an empty winner copies old bank slot 0, as the reference
+          buf[i] = src < CAP ? *reinterpret_cast<const uint4 *>(old_rows + src * ROW + d)
+                             : *reinterpret_cast<const uint4 *>(pend + (src - CAP) * D + d);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int e = base + tid + i * nt;
+        if (e < CAP * DV) *reinterpret_cast<uint4 *>(bank + (e / DV) * D + (e % DV) * VEC) = buf[i];
+      }
     }
-    *reinterpret_cast<uint4 *>(bank_k + r * D + d) = kv;
-    *reinterpret_cast<uint4 *>(bank_v + r * D + d) = vv;
   }
   for (int r = tid; r < CAP; r += nt) {
     const int c = sel[r];
