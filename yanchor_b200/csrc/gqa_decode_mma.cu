@@ -70,10 +70,59 @@ __device__ __forceinline__ void cp16(void *dst, const void *src) {
 // value rows are still in shared memory from the read (rows of ROW elements in sk / sv), so each new
 // slot is written in one pass straight from there or from the pending rows, with no staging copy.
 // Candidate arrays live over the query / P rows (`cand`, free once the read's MMAs are done).
+// What the commit needs that does not depend on the read, loaded by every thread at the start of the
+// kernel so that its memory latency hides behind the read: the row's flags and counters, this thread's
+// piece of the new key / value row and, when the chunk fills, this thread's merge candidate (the
+// pending rows are prefetched into L2 for the bank write).
+struct CommitPrefetch {
+  bool active;
+  int64_t count, total;
+  float new_score;
+  uint4 kpiece, vpiece;
+  float cand_score;
+  int64_t cand_key;
+};
+
+template <typename T, int D>
+__device__ CommitPrefetch commit_prefetch(const MemCommitArgs &a, int64_t row, int64_t s, int g) {
+  const int tid = threadIdx.x, nt = blockDim.x;
+  constexpr int VEC = 16 / int(sizeof(T));
+  constexpr int DV = D / VEC;
+  CommitPrefetch f{};
+  f.active = a.active[row] != 0;
+  if (!f.active) return f;
+  f.count = a.count[s * a.count_s0];
+  f.total = a.total[s * a.count_s0];
+  f.new_score = a.scores[row * a.G + g];
+  if (tid < DV) {
+    f.kpiece = *reinterpret_cast<const uint4 *>(static_cast<const T *>(a.key) + (row * a.G + g) * D + tid * VEC);
+    f.vpiece = *reinterpret_cast<const uint4 *>(static_cast<const T *>(a.value) + (row * a.G + g) * D + tid * VEC);
+  }
+  if (f.count + 1 != a.chunk) return f;
+  const int CAP = int(a.CAP);
+  if (tid < CAP) {
+    const int32_t pos = a.positions[s * a.meta_s0 + int64_t(g) * CAP + tid];
+    f.cand_score = a.bank_scores[s * a.meta_s0 + int64_t(g) * CAP + tid];
+    f.cand_key = pos < 0 ? INT64_MAX : int64_t(pos);
+  } else if (tid < CAP + a.chunk) {
+    const int i = tid - CAP;
+    f.cand_score = i == f.count ? f.new_score : a.pscores[s * a.pmeta_s0 + int64_t(g) * a.PC + i];
+    f.cand_key = f.total - f.count + i;
+  }
+  const char *pk = reinterpret_cast<const char *>(static_cast<const T *>(a.pkeys) + s * a.pkv_s0 + int64_t(g) * a.PC * D);
+  const char *pv = reinterpret_cast<const char *>(static_cast<const T *>(a.pvalues) + s * a.pkv_s0 + int64_t(g) * a.PC * D);
+  for (int64_t off = int64_t(tid) * 128; off < a.chunk * D * int64_t(sizeof(T)); off += int64_t(nt) * 128) {
+    prefetch_l2(pk + off);
+    prefetch_l2(pv + off);
+  }
+  return f;
+}
+
 template <typename T, int D, int ROW>
-__device__ void commit_after_read(const MemCommitArgs &a, int64_t row, int64_t s, int g, int64_t count, int64_t total,
+__device__ void commit_after_read(const MemCommitArgs &a, int64_t row, int64_t s, int g, const CommitPrefetch &f,
                                   const T *sk, const T *sv, unsigned char *cand) {
   const int tid = threadIdx.x, nt = blockDim.x;
+  const int64_t count = f.count, total = f.total;
   const int CAP = int(a.CAP), chunk = int(a.chunk), G = int(a.G), PC = int(a.PC);
   T *bank_k = static_cast<T *>(a.keys) + s * a.kv_s0 + int64_t(g) * CAP * D;
   T *bank_v = static_cast<T *>(a.values) + s * a.kv_s0 + int64_t(g) * CAP * D;
@@ -84,21 +133,23 @@ __device__ void commit_after_read(const MemCommitArgs &a, int64_t row, int64_t s
   float *pscore = a.pscores + s * a.pmeta_s0 + int64_t(g) * PC;
   constexpr int VEC = 16 / int(sizeof(T));
   constexpr int DV = D / VEC;
-  // push (16-byte pieces: row starts are 16-byte aligned for D % 8 == 0 and 16-byte aligned bases)
-  const T *key = static_cast<const T *>(a.key) + (row * G + g) * D;
-  const T *val = static_cast<const T *>(a.value) + (row * G + g) * D;
-  for (int e = tid; e < DV; e += nt) {
-    *reinterpret_cast<uint4 *>(pend_k + count * D + e * VEC) = *reinterpret_cast<const uint4 *>(key + e * VEC);
-    *reinterpret_cast<uint4 *>(pend_v + count * D + e * VEC) = *reinterpret_cast<const uint4 *>(val + e * VEC);
+  // push (16-byte pieces, loaded at the start: row starts are 16-byte aligned)
+  if (tid < DV) {
+    *reinterpret_cast<uint4 *>(pend_k + count * D + tid * VEC) = f.kpiece;
+    *reinterpret_cast<uint4 *>(pend_v + count * D + tid * VEC) = f.vpiece;
   }
-  const float new_score = a.scores[row * G + g];
+  const float new_score = f.new_score;
   if (tid == 0) pscore[count] = new_score;
   if (count + 1 != chunk) return;
   const int n = CAP + chunk;
   float *c_score = reinterpret_cast<float *>(cand);
   int64_t *c_pkey = reinterpret_cast<int64_t *>(cand + ((4 * n + 15) & ~15));
   int *sel = reinterpret_cast<int *>(reinterpret_cast<unsigned char *>(c_pkey) + 8 * n);
-  for (int c = tid; c < n; c += nt) {
+  if (tid < n) {   // this thread's candidate, loaded at the start
+    c_score[tid] = f.cand_score;
+    c_pkey[tid] = f.cand_key;
+  }
+  for (int c = nt + tid; c < n; c += nt) {   // any beyond one per thread
     if (c < CAP) {
       const int32_t pos = bpos[c];
       c_score[c] = bscore[c];
@@ -126,7 +177,7 @@ __device__ void commit_after_read(const MemCommitArgs &a, int64_t row, int64_t s
   __syncthreads();   // sel complete; every thread's push is visible to the pending loads below
   // the new bank, keys then values: each thread loads all its pieces first (old bank rows from shared
   // memory, pending rows from global memory, all in flight together), then stores them
-  constexpr int PER = 16;
+  constexpr int PER = 8;
   for (int half = 0; half < 2; ++half) {
     const T *old_rows = half ? sv : sk;
     const T *pend = half ? pend_v : pend_k;
@@ -193,6 +244,8 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_decode_mma_kernel(const GqaDe
     for (int e = tid; e < R * D; e += kGqaThreads) o[e] = from_f<T>(0.f);
     return;
   }
+  CommitPrefetch pre{};
+  if constexpr (COMMIT) pre = commit_prefetch<T, D>(ct.c, b, s, int(g));
   const T *kb = static_cast<const T *>(a.keys) + s * a.kv_bs + g * a.kv_gs + p0 * D;
   const T *vb = static_cast<const T *>(a.values) + s * a.kv_bs + g * a.kv_gs + p0 * D;
   constexpr int PIECES = D / 8;
@@ -346,11 +399,10 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_decode_mma_kernel(const GqaDe
       // arrival counter goes back to 0 for the next call.  The commit's buffers reuse the K / V
       // rows, which every warp is done with after the first barrier.
       const MemCommitArgs &c = ct.c;
-      if (c.active[b]) {   // the same for the row's G CTAs
-        const int64_t count = c.count[s * c.count_s0];
-        const int64_t total = c.total[s * c.count_s0];
+      if (pre.active) {   // the same for the row's G CTAs
+        const int64_t count = pre.count, total = pre.total;
         __syncthreads();   // every warp is done with the query / P rows and the V rows
-        commit_after_read<T, D, ROW>(c, b, s, int(g), count, total, sk, sv, reinterpret_cast<unsigned char *>(sq));
+        commit_after_read<T, D, ROW>(c, b, s, int(g), pre, sk, sv, reinterpret_cast<unsigned char *>(sq));
         __syncthreads();
         if (tid == 0) {
           __threadfence();
