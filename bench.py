@@ -1157,7 +1157,8 @@ def run_comparators(args):
       chunk_gated_delta_rule at config 1 and fused_recurrent_gated_delta_rule for one decode layer at
       B=64, as modeling_yanchor.py:397-406 binds them;
     * the reference's Triton anchor-memory kernels from its install (runtime/model/independent_memory.py:
-      committed_gqa then commit_decode, 8 layers at B=64 with full banks and staggered pending counts).
+      committed_gqa then commit_decode, 8 layers at B=64 with full banks and staggered pending counts;
+      indexed_gqa, the anchor prefill read, at config 1).
     Each runs once to compile, then is timed; a failure is reported, not raised."""
     import torch
     import yanchor_b200 as yb
@@ -1220,11 +1221,23 @@ def run_comparators(args):
     timed('yanchor_b200_memory_8_layers_ms', lambda: [yb.memory_decode_step(mq[i], mk[i], mk[i], ms[i], act,
                                                                             MEM_CHUNK, m) for i, m in enumerate(mems)],
           iters=20)
+    # anchor prefill read at config 1 (8 rows x 128 blocks x 4 groups, 64 referenced slots)
+    iq = torch.randn(8, 128, MEM_CHUNK, MEM_H, MEM_D, generator=gen, device=dev).to(bf)
+    ik = torch.randn(1, 4096, MEM_G, MEM_D, generator=gen, device=dev).to(bf)
+    irefs = torch.randint(0, 4096, (8, 128, MEM_G, MEM_CAP), generator=gen, device=dev)
+    timed('yanchor_b200_indexed_read_config1_ms', lambda: yb.indexed_gqa(iq, ik, ik, irefs), iters=20)
     if reference_installed():
         try:
-            sys.path.append(os.path.join(REF_ROOT, 'runtime'))
-            import importlib
-            ref_mem = importlib.import_module('model.independent_memory')
+            # the reference's module (it imports modeling_yanchor from the install root); loaded under
+            # its own name so that this package's drop-in module of the same name is not picked up
+            sys.path[:0] = [REF_ROOT, os.path.join(REF_ROOT, 'runtime')]
+            import importlib.util
+            spec = importlib.util.spec_from_file_location(
+                'reference_independent_memory', os.path.join(REF_ROOT, 'runtime', 'model', 'independent_memory.py'))
+            ref_mem = importlib.util.module_from_spec(spec)
+            spec.loader.exec_module(ref_mem)
+            timed('reference_triton_indexed_read_config1_ms', lambda: ref_mem.indexed_gqa(iq, ik, ik, irefs),
+                  iters=20)
 
             def ref_layers():
                 for i, m in enumerate(mems):
@@ -1233,6 +1246,8 @@ def run_comparators(args):
             timed('reference_triton_memory_8_layers_ms', ref_layers, iters=20)
         except Exception as e:  # noqa: BLE001
             out['reference_triton_memory_8_layers_ms'] = f'failed: {type(e).__name__}: {str(e)[:200]}'
+    else:
+        out['reference_triton'] = 'not installed'
     print(json.dumps({'comparators': out, 'how': 'CUDA events, eager launches (no CUDA graph) for every entry, '
                       'same inputs per pair'}), flush=True)
 
