@@ -10,7 +10,9 @@ Reference algorithms restated here (paths inside the reference project):
 * ``decode_attention``   runtime/model/inference_kernels.py:1881-1897: one
   query per row attends to every ring position (softmax over the positions
   whose ``valid`` is set), scale ``D ** -0.5``, grouped-query (query head
-  ``h`` reads KV head ``h // (QH / KVH)``);
+  ``h`` reads KV head ``h // (QH / KVH)``); a row with no valid position
+  gives zeros, as torch's SDPA does for a fully masked row (torch >= 2.5,
+  the version the reference runs on here);
 * ``prefill_attention``  modeling_yanchor.py:412-427 (``reference_swa``):
   causal sliding-window attention of a prompt, absolute positions, optional
   key validity and a query offset (keys of a cached window before the
@@ -48,10 +50,12 @@ def decode_attention(query, ring_key, ring_value, valid, dtype=np.float64):
     kk = np.repeat(k, R, axis=1)                          # [B, QH, W, D]
     vv = np.repeat(v, R, axis=1)
     logits = np.einsum('bhd,bhwd->bhw', q, kk) / np.sqrt(D)
+    any_valid = np.asarray(valid).any(-1)[:, None, None]
     logits = np.where(np.asarray(valid)[:, None, :], logits, -np.inf)
+    logits = np.where(any_valid, logits, 0.0)             # fully masked rows: weights 0 below
     m = logits.max(-1, keepdims=True)
     e = np.exp(logits - m)
-    w = e / e.sum(-1, keepdims=True)
+    w = np.where(any_valid, e / e.sum(-1, keepdims=True), 0.0)
     return np.einsum('bhw,bhwd->bhd', w, vv)[:, None]     # [B, 1, QH, D]
 
 

@@ -220,6 +220,29 @@ def test_swa_decode_attention(golden):
     close(swa.decode_attention(d['swa_q'], d['swa_k'], d['swa_v'], d['swa_valid']), d['swa_out'], 2e-6)
 
 
+def test_swa_decode_attention_empty_row_matches_reference():
+    """A ring row with no valid position: the reference's own decode attention
+    (runtime/model/inference_kernels.py:1881-1897, run here on the CPU from
+    its install) gives zeros for it under the installed torch; the oracle
+    does the same, and the other rows agree."""
+    import _reference
+    if not _reference.available():
+        pytest.skip('SKIPPED, NOT PASSED: the reference install (baseline/_ref) is absent')
+    import torch
+    from oracle import swa
+    ik = _reference.inference_kernels()
+    rng = np.random.default_rng(3)
+    B, QH, KVH, W, D = 3, 4, 2, 9, 16
+    q = rng.standard_normal((B, 1, QH, D))
+    k = rng.standard_normal((B, KVH, W, D))
+    v = rng.standard_normal((B, KVH, W, D))
+    valid = rng.random((B, W)) > 0.4
+    valid[1] = False
+    ref = ik.fixed_memory_physical_ring_decode_attention(*(torch.from_numpy(x) for x in (q, k, v, valid))).numpy()
+    assert np.all(ref[1] == 0)
+    close(swa.decode_attention(q, k, v, valid), ref, 1e-12)
+
+
 @pytest.mark.parametrize('case', ['a', 'b', 'c'])
 def test_swa_prefill_attention(golden, case):
     """reference_swa: plain causal window, left padding through key validity,

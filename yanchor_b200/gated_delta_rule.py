@@ -160,7 +160,18 @@ def fused_recurrent_gated_delta_rule(q, k, v, g=None, gk=None, gv=None, beta=Non
 def chunk_gated_delta_rule(q, k, v, g, beta, scale=None, initial_state=None, output_final_state=False,
                            use_qk_l2norm_in_kernel=False, cu_seqlens=None, cu_seqlens_cpu=None, cp_context=None,
                            transpose_state_layout=False, **kwargs):
-    """Chunked (64-token) gated delta rule (fla ``chunk_gated_delta_rule``)."""
+    """Chunked (64-token) gated delta rule (fla ``chunk_gated_delta_rule``).
+
+    Two CUDA kernels serve it, chosen by the inputs:
+
+    * bf16 q / k / v with K = V = 128 (the YANchor shape): the tcgen05
+      tensor-core kernel (``gdn_chunk_tc_kernel``), 1.5 ms at B=8, T=8192,
+      H=32 on a B200;
+    * anything else (fp16 or fp32 inputs, other head dimensions): the SIMT
+      kernel (``gdn_chunk_simt_kernel``), which does the same arithmetic on
+      the FP32 pipe, about 20x slower at the YANchor shape. Convert fp16
+      inputs to bf16 first where that precision is acceptable.
+    """
     if 'head_first' in kwargs:
         raise DeprecationWarning('head_first has been removed. Inputs must be in `[B, T, H, ...]` format.')
     if cp_context is not None:
