@@ -849,13 +849,21 @@ def run_only(args):
         mk = torch.randn(1, 4096, MEM_G, MEM_D, generator=gen, device=dev).to(bf)
         refs = torch.randint(0, 4096, (8, blocks, MEM_G, 64), generator=gen, device=dev)
         fn = lambda: yb.indexed_gqa(mq, mk, mk, refs)  # noqa: E731
-    elif args.only == 'swa':
+    elif args.only in ('swa', 'swa_layer'):
         rk = torch.randn(B, 4, 1024, 256, generator=gen, device=dev).to(bf)
         rv = torch.randn(B, 4, 1024, 256, generator=gen, device=dev).to(bf)
         rval = torch.ones(B, 1024, device=dev, dtype=torch.bool)
         sq = torch.randn(B, 1, 16, 256, generator=gen, device=dev).to(bf)
         sw = torch.empty(yb.swa.workspace_bytes(B, 4, 16, 1024, 256), device=dev, dtype=torch.uint8)
         fn = lambda: yb.physical_ring_decode_attention(sq, rk, rv, rval, workspace=sw)  # noqa: E731
+        if args.only == 'swa_layer':   # the whole SWA decode layer: ring write and advance, then attention
+            ridx = torch.zeros((), device=dev, dtype=torch.int64)
+            nk = torch.randn(B, 4, 1, 256, generator=gen, device=dev).to(bf)
+            nval = torch.ones(B, 1, device=dev, dtype=torch.bool)
+
+            def fn():
+                yb.physical_ring_update_(rk, rv, rval, ridx, nk, nk, nval)
+                yb.physical_ring_decode_attention(sq, rk, rv, rval, workspace=sw)
     elif args.only in ('mem_topk', 'mem_sequence'):
         blocks, T = 128, 8192
         psc = (torch.randn(8, blocks, MEM_G, 64, generator=gen, device=dev) * 2).round() / 2
@@ -1265,7 +1273,7 @@ def main():
     ap.add_argument('--no-b256', action='store_true', help='skip the config-2 batch (B=256)')
     ap.add_argument('--only', choices=['conv_update', 'gdn_decode', 'gdn_fused', 'gdn_chunk', 'mem_read', 'mem_commit',
                                        'mem_step', 'mem_step_merge', 'mem_layers', 'mem_indexed', 'mem_topk',
-                                       'mem_sequence', 'swa', 'swa_prefill', 'greedy',
+                                       'mem_sequence', 'swa', 'swa_layer', 'swa_prefill', 'greedy',
                                        'topk'], help='run one kernel family (small ncu captures)')
     ap.add_argument('--prefill-batch', type=int, default=8)
     ap.add_argument('--cpu-sample', nargs=3, type=int, metavar=('B', 'STEPS', 'WARMUP'), help=argparse.SUPPRESS)

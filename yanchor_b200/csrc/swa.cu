@@ -38,6 +38,8 @@ __device__ __forceinline__ int64_t ring_index_of(const SwaArgs &a) {
 template <typename T>
 __global__ void swa_ring_write_kernel(const SwaArgs a) {
   constexpr int VEC = 16 / int(sizeof(T));
+  pdl_wait();
+  pdl_release();
   const int64_t idx = ring_index_of(a);
   if (idx < 0 || idx >= a.W) return;   // a corrupt index writes nothing (the advance restarts it at 0)
   const int64_t pieces = a.B * a.KVH * (a.D / VEC);
@@ -56,6 +58,8 @@ __global__ void swa_ring_write_kernel(const SwaArgs a) {
 }
 
 __global__ void swa_ring_advance_kernel(const SwaArgs a) {
+  pdl_wait();   // every write of the previous kernel has read the index
+  pdl_release();
   const int64_t i = ring_index_of(a);
   const int64_t next = (i < 0 || i + 1 >= a.W) ? 0 : i + 1;
   if (a.index_i64) *static_cast<int64_t *>(a.ring_index) = next;
@@ -159,6 +163,8 @@ __global__ void swa_combine_kernel(const SwaArgs a, const float *part, int R, in
   const int64_t bh = blockIdx.x, b = bh / a.KVH, kvh = bh % a.KVH;
   const int r = blockIdx.y;
   const int D = int(a.D);
+  pdl_wait();   // the slices are written
+  pdl_release();
   const float *pb = part + bh * slices * (R * (D + 2)) + r * (D + 2);
   float M = -INFINITY;
   for (int s = 0; s < slices; ++s) M = fmaxf(M, pb[s * R * (D + 2) + D]);
@@ -228,15 +234,18 @@ int launch_swa_ring_write(const SwaArgs &a) {
   const int64_t elem = a.dtype == YB_F32 ? 4 : 2;
   const int64_t n = 2 * a.B * a.KVH * (a.D * elem / 16) + a.B;
   const unsigned blocks = unsigned((n + 255) / 256);
+  cudaError_t e;
   switch (a.dtype) {
-    case YB_F32: swa_ring_write_kernel<float><<<blocks, 256, 0, a.stream>>>(a); break;
-    case YB_BF16: swa_ring_write_kernel<__nv_bfloat16><<<blocks, 256, 0, a.stream>>>(a); break;
-    case YB_F16: swa_ring_write_kernel<__half><<<blocks, 256, 0, a.stream>>>(a); break;
+    case YB_F32: e = launch_pdl(swa_ring_write_kernel<float>, dim3(blocks), dim3(256), 0, a.stream, a); break;
+    case YB_BF16: e = launch_pdl(swa_ring_write_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, a.stream, a); break;
+    case YB_F16: e = launch_pdl(swa_ring_write_kernel<__half>, dim3(blocks), dim3(256), 0, a.stream, a); break;
     default: return set_error(YB_ERR_ARGUMENT, "swa ring: bad dtype %d", a.dtype);
   }
+  if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "swa_ring_write_kernel: %s", cudaGetErrorString(e));
   int rc = check_launch("swa_ring_write_kernel");
   if (rc) return rc;
-  swa_ring_advance_kernel<<<1, 1, 0, a.stream>>>(a);
+  e = launch_pdl(swa_ring_advance_kernel, dim3(1), dim3(1), 0, a.stream, a);
+  if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "swa_ring_advance_kernel: %s", cudaGetErrorString(e));
   return check_launch("swa_ring_advance_kernel");
 }
 
@@ -267,15 +276,11 @@ int launch_swa_decode_attention(const SwaArgs &a, void *workspace) {
     int rc = launch_gqa_decode_mma(g);
     if (rc) return rc;
     const int R = int(a.QH / a.KVH);
-    switch (a.dtype) {
-      case YB_BF16:
-        swa_combine_kernel<__nv_bfloat16><<<dim3(unsigned(a.B * a.KVH), unsigned(R)), a.D < 256 ? a.D : 256, 0,
-                                            a.stream>>>(a, part, R, slices);
-        break;
-      default:
-        swa_combine_kernel<__half><<<dim3(unsigned(a.B * a.KVH), unsigned(R)), a.D < 256 ? a.D : 256, 0, a.stream>>>(
-            a, part, R, slices);
-    }
+    const dim3 cgrid(unsigned(a.B * a.KVH), unsigned(R)), cblock(unsigned(a.D < 256 ? a.D : 256));
+    const cudaError_t e = a.dtype == YB_BF16
+                              ? launch_pdl(swa_combine_kernel<__nv_bfloat16>, cgrid, cblock, 0, a.stream, a, part, R, slices)
+                              : launch_pdl(swa_combine_kernel<__half>, cgrid, cblock, 0, a.stream, a, part, R, slices);
+    if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "swa_combine_kernel: %s", cudaGetErrorString(e));
     return check_launch("swa_combine_kernel");
   }
   switch (a.dtype) {
