@@ -67,8 +67,9 @@ __device__ __forceinline__ void cp16(void *dst, const void *src) {
 // slot `count`; when the chunk fills, rank the CAP bank slots and the `chunk` pending slots (score
 // descending, position ascending with empty slots last, then candidate index: the stable double
 // argsort of select_topk, modeling_yanchor.py:51-55) and write the new bank.  The old bank's key and
-// value rows are still in shared memory from the read (rows of ROW elements in sk / sv), so each new
-// slot is written in one pass straight from there or from the pending rows, with no staging copy.
+// value rows are still in shared memory from the read (rows of ROW elements in sk / sv): a new slot won
+// by an old row is one bulk copy from there to the bank; the slots won by pending rows are copied by
+// the threads, all their loads in flight together.
 // Candidate arrays live over the query / P rows (`cand`, free once the read's MMAs are done).
 // What the commit needs that does not depend on the read, loaded by every thread at the start of the
 // kernel so that its memory latency hides behind the read: the row's flags and counters, this thread's
@@ -174,31 +175,62 @@ __device__ void commit_after_read(const MemCommitArgs &a, int64_t row, int64_t s
     if (o < n) r0 += memcommit::cand_before(c_score[o], c_pkey[o], o, sc, pkc, c);
     if (r0 + r1 < CAP) sel[r0 + r1] = c;
   }
-  __syncthreads();   // sel complete; every thread's push is visible to the pending loads below
-  // the new bank, keys then values: each thread loads all its pieces first (old bank rows from shared
-  // memory, pending rows from global memory, all in flight together), then stores them
-  constexpr int PER = 8;
-  for (int half = 0; half < 2; ++half) {
-    const T *old_rows = half ? sv : sk;
-    const T *pend = half ? pend_v : pend_k;
-    T *bank = half ? bank_v : bank_k;
-    for (int base = 0; base < CAP * DV; base += nt * PER) {
-      uint4 buf[PER];
-#pragma unroll
-      for (int i = 0; i < PER; ++i) {
-        const int e = base + tid + i * nt;
-        if (e < CAP * DV) {
-          const int r = e / DV, d = (e % DV) * VEC;
-          const int c = sel[r];
-          const int src = c_pkey[c] == INT64_MAX ? 0 : c;   // an empty winner copies old bank slot 0, as the reference
-          buf[i] = src < CAP ? *reinterpret_cast<const uint4 *>(old_rows + src * ROW + d)
-                             : *reinterpret_cast<const uint4 *>(pend + (src - CAP) * D + d);
-        }
+  __syncthreads();   // sel complete
+  // the new slots whose winner is a pending row, in slot order (warp 0; CAP <= 64)
+  int *plist = sel + CAP;
+  int *npend = plist + CAP;
+  if (tid < 32) {
+    int base = 0;
+    for (int r0 = 0; r0 < CAP; r0 += 32) {
+      const int r = r0 + tid;
+      bool from_pend = false;
+      if (r < CAP) {
+        const int c = sel[r];
+        from_pend = c_pkey[c] != INT64_MAX && c >= CAP;
       }
+      const unsigned m = __ballot_sync(0xffffffffu, from_pend);
+      if (from_pend) plist[base + __popc(m & ((1u << tid) - 1u))] = r;
+      base += __popc(m);
+    }
+    if (tid == 0) *npend = base;
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the old bank rows are read below by bulk copies
+  __syncthreads();      // sel, plist complete; every thread's push is visible to the pending loads below
+  // (1) slots won by an old bank row (an empty winner copies old bank slot 0, as the reference): one
+  //     bulk copy per row straight from the shared-memory row the read used
+  if (tid < 2 * CAP) {
+    const int r = tid % CAP, half = tid / CAP;
+    const int c = sel[r];
+    const int src = c_pkey[c] == INT64_MAX ? 0 : c;
+    if (src < CAP) {
+      T *dst = (half ? bank_v : bank_k) + r * D;
+      const T *from = (half ? sv : sk) + src * ROW;
+      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+                   "r"(static_cast<uint32_t>(__cvta_generic_to_shared(from))), "r"(uint32_t(D * sizeof(T)))
+                   : "memory");
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    }
+  }
+  // (2) slots won by a pending row: each thread loads all its pieces (key and value rows together)
+  //     before it stores them
+  const int np = *npend;
+  constexpr int PER = 8;
+  for (int base = 0; base < np * 2 * DV; base += nt * PER) {
+    uint4 buf[PER];
 #pragma unroll
-      for (int i = 0; i < PER; ++i) {
-        const int e = base + tid + i * nt;
-        if (e < CAP * DV) *reinterpret_cast<uint4 *>(bank + (e / DV) * D + (e % DV) * VEC) = buf[i];
+    for (int i = 0; i < PER; ++i) {
+      const int e = base + tid + i * nt;
+      if (e < np * 2 * DV) {
+        const int r = plist[e / (2 * DV)], rem = e % (2 * DV), half = rem / DV, d = (rem % DV) * VEC;
+        buf[i] = *reinterpret_cast<const uint4 *>((half ? pend_v : pend_k) + (sel[r] - CAP) * D + d);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int e = base + tid + i * nt;
+      if (e < np * 2 * DV) {
+        const int r = plist[e / (2 * DV)], rem = e % (2 * DV), half = rem / DV, d = (rem % DV) * VEC;
+        *reinterpret_cast<uint4 *>((half ? bank_v : bank_k) + r * D + d) = buf[i];
       }
     }
   }
@@ -207,6 +239,8 @@ __device__ void commit_after_read(const MemCommitArgs &a, int64_t row, int64_t s
     bscore[r] = c_score[c];
     bpos[r] = c_pkey[c] == INT64_MAX ? -1 : int32_t(c_pkey[c]);
   }
+  // the bulk copies have read their rows and written the bank before the CTA goes on or exits
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 template <typename T, int R, int D, bool COMMIT>
@@ -472,7 +506,7 @@ int launch_gqa_decode_mma(const GqaDecodeArgs &a) {
 
 bool gqa_decode_commit_fits(const GqaDecodeArgs &a, const MemCommitArgs &c) {
   const int64_t n = c.CAP + c.chunk;
-  const int64_t cand_bytes = ((4 * n + 15) & ~int64_t(15)) + 8 * n + 4 * c.CAP;
+  const int64_t cand_bytes = ((4 * n + 15) & ~int64_t(15)) + 8 * n + 4 * c.CAP + 4 * c.CAP + 4;   // + plist, npend
   const int64_t room = 2 * (8 * (a.D + 8) + 2 * 8 * (kGqaSlice + 8));   // the query and P rows (16-bit)
   const uintptr_t al = reinterpret_cast<uintptr_t>(c.key) | reinterpret_cast<uintptr_t>(c.value) |
                        reinterpret_cast<uintptr_t>(c.keys) | reinterpret_cast<uintptr_t>(c.values) |
