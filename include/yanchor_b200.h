@@ -300,12 +300,17 @@ int yb_mem_indexed_read(const void *query, const void *key, const void *value, c
  * token_shift / write_lo / write_hi: device int64 [B].  Replaces the
  * reference's gather of the query onto the timeline and of the read back
  * (modeling_yanchor.py:196-198, 260-265) around `indexed_gqa`.
+ *   key_new, value_new (may be null, then S_new = 0): a second source of
+ *   rows [S_new, G, D], contiguous, for key batch KB = 1: reference S + i
+ *   reads row i there.  The prefill passes the state's old rows as key /
+ *   value and the writer's new rows here, instead of the reference's
+ *   concatenation of both (modeling_yanchor.py:238-241).
  */
-int yb_mem_indexed_read_timeline(const void *query, const void *key, const void *value, const int64_t *references,
-                                 void *out, int64_t B, int64_t T, int64_t blocks, int64_t chunk, int64_t H,
-                                 int64_t G, int64_t D, int64_t S, int64_t KB, int64_t CAP,
-                                 const int64_t *token_shift, const int64_t *write_lo, const int64_t *write_hi,
-                                 int dtype, void *stream);
+int yb_mem_indexed_read_timeline(const void *query, const void *key, const void *value, const void *key_new,
+                                 const void *value_new, const int64_t *references, void *out, int64_t B, int64_t T,
+                                 int64_t blocks, int64_t chunk, int64_t H, int64_t G, int64_t D, int64_t S,
+                                 int64_t S_new, int64_t KB, int64_t CAP, const int64_t *token_shift,
+                                 const int64_t *write_lo, const int64_t *write_hi, int dtype, void *stream);
 
 /*
  * Top-CAP selection of anchor candidates.  Order: score descending (NaN

@@ -45,8 +45,8 @@ SIGNATURES = {
     'yb_mem_decode_step': (_I, [_P, _P, _P, _P, _P, _P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64,
                                 _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I, _P]),
     'yb_mem_indexed_read': (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I, _P]),
-    'yb_mem_indexed_read_timeline': (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
-                                          _I64, _P, _P, _P, _I, _P]),
+    'yb_mem_indexed_read_timeline': (_I, [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
+                                          _I64, _I64, _I64, _P, _P, _P, _I, _P]),
     'yb_gdn_decode_fused': (_I, [_P, _I64, _P, _I64, _P, _P, _I64, _P, _I64, _I64, _P, _P, _I64, _P, _I, _P, _P, _P,
                                  _F, _P, _I64, _I64, _I64, _I64, _I64, _I64, _F, _I, _U32, _P]),
     'yb_swa_ring_write': (_I, [_P, _P, _I64, _I64, _P, _P, _P, _I64, _I64, _P, _I64, _P, _I, _I64, _I64, _I64, _I64,

@@ -223,19 +223,22 @@ int yb_mem_indexed_read(const void *query, const void *key, const void *value, c
   return launch_mem_indexed_read(a);
 }
 
-int yb_mem_indexed_read_timeline(const void *query, const void *key, const void *value, const int64_t *references,
-                                 void *out, int64_t B, int64_t T, int64_t blocks, int64_t chunk, int64_t H,
-                                 int64_t G, int64_t D, int64_t S, int64_t KB, int64_t CAP,
-                                 const int64_t *token_shift, const int64_t *write_lo, const int64_t *write_hi,
-                                 int dtype, void *stream) {
+int yb_mem_indexed_read_timeline(const void *query, const void *key, const void *value, const void *key_new,
+                                 const void *value_new, const int64_t *references, void *out, int64_t B, int64_t T,
+                                 int64_t blocks, int64_t chunk, int64_t H, int64_t G, int64_t D, int64_t S,
+                                 int64_t S_new, int64_t KB, int64_t CAP, const int64_t *token_shift,
+                                 const int64_t *write_lo, const int64_t *write_hi, int dtype, void *stream) {
   YB_REQUIRE(dtype_ok(dtype), "mem_indexed_read_timeline: bad dtype");
-  YB_REQUIRE(B >= 0 && T >= 0 && blocks >= 0 && chunk > 0 && H > 0 && G > 0 && D > 0 && S >= 0 && CAP > 0 &&
-                 H % G == 0 && blocks * chunk < 0x7fffffffLL && T < 0x7fffffffLL,
+  YB_REQUIRE(B >= 0 && T >= 0 && blocks >= 0 && chunk > 0 && H > 0 && G > 0 && D > 0 && S >= 0 && S_new >= 0 &&
+                 CAP > 0 && H % G == 0 && blocks * chunk < 0x7fffffffLL && T < 0x7fffffffLL,
              "mem_indexed_read_timeline: bad sizes");
   YB_REQUIRE(KB == 1 || KB == B, "mem_indexed_read_timeline: key batch must be 1 or B");
   YB_REQUIRE(query && key && value && references && out && token_shift && write_lo && write_hi,
              "mem_indexed_read_timeline: null tensor");
-  YB_REQUIRE(aligned(query, 16) && aligned(key, 16) && aligned(value, 16) && aligned(out, 16),
+  YB_REQUIRE(S_new == 0 || (key_new && value_new && KB == 1),
+             "mem_indexed_read_timeline: a second source needs both tensors and key batch 1");
+  YB_REQUIRE(aligned(query, 16) && aligned(key, 16) && aligned(value, 16) && aligned(out, 16) &&
+                 (S_new == 0 || (aligned(key_new, 16) && aligned(value_new, 16))),
              "mem_indexed_read_timeline: tensors must be 16-byte aligned");
   MemIndexedArgs a{query, key, value, references, out, B, blocks, chunk, H, G, D, S, KB, CAP, dtype,
                    static_cast<cudaStream_t>(stream)};
@@ -243,6 +246,11 @@ int yb_mem_indexed_read_timeline(const void *query, const void *key, const void 
   a.w_lo = write_lo;
   a.w_hi = write_hi;
   a.T = T;
+  if (S_new > 0) {
+    a.key2 = key_new;
+    a.value2 = value_new;
+    a.S2 = S_new;
+  }
   return launch_mem_indexed_read(a);
 }
 

@@ -82,6 +82,9 @@ struct MemIndexedArgs {
   // s + tok_shift[b]; only slots in [w_lo[b], w_hi[b]) are written
   const int64_t *tok_shift = nullptr, *w_lo = nullptr, *w_hi = nullptr;
   int64_t T = 0;
+  // optional second source (KB == 1): references S .. S + S2 - 1 are rows 0 .. S2 - 1 of key2 / value2
+  const void *key2 = nullptr, *value2 = nullptr;
+  int64_t S2 = 0;
 };
 int launch_mem_indexed_read(const MemIndexedArgs &a);
 bool mem_indexed_tc_supported(const MemIndexedArgs &a);

@@ -13,8 +13,9 @@
 //   (logit 0, value 0), masked where the reference is empty  ->  P as bf16
 //   hi + lo parts in TMEM  ->  O = (P_hi + P_lo) V (TMEM)  ->  O / den in
 //   bf16  ->  TMA store through two 16 KB staging tiles.
-// Warp roles: warp 0 loads (Q halves by TMA, K / V rows by cp.async), warp 1
-// issues the MMAs, warps 2-5 run the softmax and the output.  Each buffer is
+// Warp roles: warp 0 loads the Q halves (TMA) and the K rows (cp.async), warp
+// 6 the V rows (cp.async), warp 1 issues the MMAs, warps 2-5 run the softmax
+// and the output.  Each buffer is
 // refilled for the next unit as soon as its last reader is done: a Q half
 // after its S MMA, K after the second S MMA, V after the second O MMA, so
 // the next unit's loads overlap this unit's softmax and output.
@@ -38,7 +39,7 @@ namespace {
 
 using namespace tc;
 
-constexpr int D = 256, CAPS = 64, ROWS = 256, NT = 192;
+constexpr int D = 256, CAPS = 64, ROWS = 256, NT = 224;
 constexpr uint32_t OFF_Q = 0;           // two Q halves: 4 column blocks x 128 rows x 128 B each (64 KB)
 constexpr uint32_t OFF_K = 131072;      // K: 4 column blocks x 64 rows x 128 B
 constexpr uint32_t OFF_V = 163840;      // V: same
@@ -68,6 +69,9 @@ struct IdxParams {
   int64_t T;
   __nv_bfloat16 *out;
   int64_t units;
+  // second source: references S .. S + S2 - 1 are rows of key2 / value2 (key batch 1)
+  const __nv_bfloat16 *key2, *value2;
+  int64_t S2;
 };
 
 __device__ __forceinline__ void cp_async16(void *dst, const void *src, bool valid) {
@@ -162,9 +166,11 @@ __global__ void __launch_bounds__(NT, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_base_smem;
 
-  if (warp == 0) {
-    // ===================== loads: Q halves by TMA (lane 0), K / V rows by cp.async =====================
-    if (lane == 0 && !*abort_flag) prefetch_tensormap(&map_q);
+  if (warp == 0 || warp == 6) {
+    // ===================== loads: Q halves by TMA (warp 0, lane 0) and K rows by cp.async (warp 0);
+    //                       V rows by cp.async (warp 6), so the two gathers run side by side =====================
+    const bool kq = warp == 0;
+    if (kq && lane == 0 && !*abort_flag) prefetch_tensormap(&map_q);
     int issued = 0;
     int phases[4] = {0, 0, 0, 0};   // loads issued on Q half 0, Q half 1, K, V
     bool ok = !*abort_flag;
@@ -193,17 +199,29 @@ __global__ void __launch_bounds__(NT, 1)
       // K / V rows: 64 slots x 32 pieces of 16 bytes, lane = piece; the lane
       // waits for its own copies and makes them visible to the tensor core
       // before it arrives on the full barrier
-      auto gather = [&](int empty_bar, const __nv_bfloat16 *src, uint32_t off, int &phase) {
+      auto gather = [&](int empty_bar, const __nv_bfloat16 *src, const __nv_bfloat16 *src2, uint32_t off,
+                        int &phase) {
         if (n > 0) ok = ok && mbar_wait(&bars[empty_bar], (n - 1) & 1, abort_flag, ERR_WAIT_FREE);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) return;
         ++phase;
+        if (p.S2 == 0) {
 #pragma unroll 4
-        for (int slot = 0; slot < CAPS; ++slot) {
-          const int64_t ref = __shfl_sync(0xffffffffu, slot < 32 ? r0 : r1, slot & 31);
-          const bool ok_ref = ref >= 0 && ref < p.S;   // out-of-range references read as empty
-          const int64_t row = ((u.kb * p.S + (ok_ref ? ref : 0)) * p.G + u.g) * D + lane * 8;
-          cp_async16(smem + off + sw128_off(64, cb, slot, j), src + row, ok_ref);
+          for (int slot = 0; slot < CAPS; ++slot) {
+            const int64_t ref = __shfl_sync(0xffffffffu, slot < 32 ? r0 : r1, slot & 31);
+            const bool ok_ref = ref >= 0 && ref < p.S;   // out-of-range references read as empty
+            const int64_t row = ((u.kb * p.S + (ok_ref ? ref : 0)) * p.G + u.g) * D + lane * 8;
+            cp_async16(smem + off + sw128_off(64, cb, slot, j), src + row, ok_ref);
+          }
+        } else {   // references from S on read the second source (key batch 1)
+#pragma unroll 4
+          for (int slot = 0; slot < CAPS; ++slot) {
+            const int64_t ref = __shfl_sync(0xffffffffu, slot < 32 ? r0 : r1, slot & 31);
+            const bool ok_ref = ref >= 0 && ref < p.S + p.S2;
+            const bool second = ok_ref && ref >= p.S;
+            const int64_t row = ((second ? ref - p.S : (ok_ref ? ref : 0)) * p.G + u.g) * D + lane * 8;
+            cp_async16(smem + off + sw128_off(64, cb, slot, j), (second ? src2 : src) + row, ok_ref);
+          }
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
       };
@@ -212,12 +230,15 @@ __global__ void __launch_bounds__(NT, 1)
         fence_async_smem();
         mbar_arrive(&bars[full_bar]);
       };
-      load_q(0);
-      if (ok) gather(B_KEMPTY, p.key, OFF_K, phases[2]);
-      if (ok) load_q(1);
-      if (ok) publish(B_KFULL);
-      if (ok) gather(B_VEMPTY, p.value, OFF_V, phases[3]);
-      if (ok) publish(B_VFULL);
+      if (kq) {
+        load_q(0);
+        if (ok) gather(B_KEMPTY, p.key, p.key2, OFF_K, phases[2]);
+        if (ok) load_q(1);
+        if (ok) publish(B_KFULL);
+      } else {
+        gather(B_VEMPTY, p.value, p.value2, OFF_V, phases[3]);
+        if (ok) publish(B_VFULL);
+      }
     }
     // drain: every copy issued must have landed before the CTA may exit
     asm volatile("cp.async.wait_group 0;" ::: "memory");
@@ -286,8 +307,9 @@ __global__ void __launch_bounds__(NT, 1)
       // the valid slots as a 64-bit mask (bit s: reference s is in range)
       const int64_t *refs = p.refs + unit * CAPS;
       const int64_t r0 = refs[lane], r1 = refs[lane + 32];
-      const uint64_t mask = uint64_t(__ballot_sync(0xffffffffu, r0 >= 0 && r0 < p.S)) |
-                            (uint64_t(__ballot_sync(0xffffffffu, r1 >= 0 && r1 < p.S)) << 32);
+      const int64_t nrows = p.S + p.S2;
+      const uint64_t mask = uint64_t(__ballot_sync(0xffffffffu, r0 >= 0 && r0 < nrows)) |
+                            (uint64_t(__ballot_sync(0xffffffffu, r1 >= 0 && r1 < nrows)) << 32);
       float inv_den[2];
       for (int h = 0; h < 2; ++h) {
         ok = ok && mbar_wait(&bars[B_SFULL + h], n & 1, abort_flag, ERR_WAIT_S);
@@ -446,7 +468,8 @@ int idx_sm_count() {
 bool mem_indexed_tc_supported(const MemIndexedArgs &a) {
   // TMA needs 16-byte aligned global bases; cp.async moves 16-byte pieces.
   const bool aligned = ((reinterpret_cast<uintptr_t>(a.query) | reinterpret_cast<uintptr_t>(a.out) |
-                         reinterpret_cast<uintptr_t>(a.key) | reinterpret_cast<uintptr_t>(a.value)) & 15u) == 0;
+                         reinterpret_cast<uintptr_t>(a.key) | reinterpret_cast<uintptr_t>(a.value) |
+                         reinterpret_cast<uintptr_t>(a.key2) | reinterpret_cast<uintptr_t>(a.value2)) & 15u) == 0;
   return a.dtype == YB_BF16 && a.D == D && a.CAP == CAPS && a.chunk * (a.H / a.G) == ROWS && a.chunk == 64 &&
          a.B * a.blocks * a.G > 0 && aligned;
 }
@@ -472,6 +495,9 @@ int launch_mem_indexed_tc(const MemIndexedArgs &a) {
   p.scale = 1.0f / sqrtf(float(D));
   p.tok_shift = a.tok_shift; p.w_lo = a.w_lo; p.w_hi = a.w_hi; p.T = a.T;
   p.out = static_cast<__nv_bfloat16 *>(a.out);
+  p.key2 = static_cast<const __nv_bfloat16 *>(a.key2);
+  p.value2 = static_cast<const __nv_bfloat16 *>(a.value2);
+  p.S2 = a.key2 ? a.S2 : 0;
   cudaError_t e = cudaFuncSetAttribute(mem_indexed_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        int(SMEM_BYTES));
   if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "indexed read tc: smem attribute: %s", cudaGetErrorString(e));

@@ -330,11 +330,17 @@ __global__ void __launch_bounds__(kIdxThreads) mem_indexed_read_kernel(const Mem
     const int slot = e / (D / 8), d8 = (e % (D / 8)) * 8;
     const int64_t ref = refs[slot];
     float kx[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, vx[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    const bool ok_ref = ref >= 0 && ref < a.S;  // out-of-range references read as empty
+    const bool ok_ref = ref >= 0 && ref < a.S + a.S2;  // out-of-range references read as empty
     if (ok_ref) {
-      const int64_t off = ((kb * a.S + ref) * a.G + g) * D + d8;
-      load8(kbase + off, kx);
-      load8(vbase + off, vx);
+      if (ref < a.S) {
+        const int64_t off = ((kb * a.S + ref) * a.G + g) * D + d8;
+        load8(kbase + off, kx);
+        load8(vbase + off, vx);
+      } else {   // the second source (key batch 1)
+        const int64_t off = ((ref - a.S) * a.G + g) * D + d8;
+        load8(static_cast<const T *>(a.key2) + off, kx);
+        load8(static_cast<const T *>(a.value2) + off, vx);
+      }
     }
     store8(sk + slot * PITCH + d8, kx);
     store8(sv + slot * PITCH + d8, vx);

@@ -106,22 +106,36 @@ def exclusive_prefix_topk(scores, positions, references, capacity, initial=None)
     return out_s.to(scores.dtype), out_p, out_r.to(references.dtype)
 
 
-def _read_timeline(query, src_k, src_v, refs, shift, lo, hi, blocks, chunk, zero_fill):
+def _read_timeline(query, old_k, old_v, n_old, new_k, new_v, refs, shift, lo, hi, blocks, chunk, zero_fill):
     """indexed read of the prompt's ``[B, T, H, D]`` query through the
-    timeline (slot s of row b = token s + shift[b]), writing slots [lo, hi)."""
+    timeline (slot s of row b = token s + shift[b]), writing slots [lo, hi).
+    References below ``n_old`` read rows of ``old_k / old_v``, the others
+    rows of ``new_k / new_v`` (the writer's rows, read where they are)."""
     query = query.contiguous()
     B, T, H, D = query.shape
     G, CAP = refs.shape[-2:]
     out = torch.zeros_like(query) if zero_fill else torch.empty_like(query)
-    key, value = src_k[None].contiguous(), src_v[None].contiguous()
+    old_k, old_v, new_k, new_v = (x.contiguous() for x in (old_k, old_v, new_k, new_v))
     refs = refs.contiguous()
     shift, lo, hi = (x.to(torch.int64).contiguous() for x in (shift, lo, hi))
+    n_new = new_k.shape[0]
     rc = _lib.lib().yb_mem_indexed_read_timeline(
-        query.data_ptr(), key.data_ptr(), value.data_ptr(), refs.data_ptr(), out.data_ptr(), B, T, blocks, chunk, H,
-        G, D, key.shape[1], 1, CAP, shift.data_ptr(), lo.data_ptr(), hi.data_ptr(), dtype_code(query),
-        stream_ptr(query.device))
+        query.data_ptr(), old_k.data_ptr(), old_v.data_ptr(), new_k.data_ptr() if n_new else None,
+        new_v.data_ptr() if n_new else None, refs.data_ptr(), out.data_ptr(), B, T, blocks, chunk, H, G, D, n_old,
+        n_new, 1, CAP, shift.data_ptr(), lo.data_ptr(), hi.data_ptr(), dtype_code(query), stream_ptr(query.device))
     _lib.check(rc, 'indexed_gqa (timeline)')
     return out
+
+
+def _take(old, new, n_old, idx, *more):
+    """Rows ``idx`` (any shape) of the joint source [old rows 0 .. n_old - 1 |
+    new rows], each indexed further by ``more`` (broadcast with ``idx``)."""
+    from_old = old[(idx.clamp(max=max(n_old - 1, 0)),) + more]
+    if new.shape[0] == 0:
+        return from_old
+    from_new = new[((idx - n_old).clamp(min=0, max=new.shape[0] - 1),) + more]
+    cond = torch.broadcast_to(idx, torch.broadcast_shapes(idx.shape, *(m.shape for m in more))) < n_old
+    return torch.where(cond.reshape(cond.shape + (1,) * (from_old.dim() - cond.dim())), from_old, from_new)
 
 
 def sequence(query, scores, write_kv, valid, chunk, state=None, capacity=None, *, capture_safe=False,
@@ -226,22 +240,21 @@ def sequence(query, scores, write_kv, valid, chunk, state=None, capacity=None, *
     k_new = k_new.to(query.dtype).reshape(-1, G, D)
     v_new = v_new.to(query.dtype).reshape(-1, G, D)
 
-    # ---- source rows [old bank + pending rows | new rows | zero row] and the slot -> row table ----
+    # ---- source rows [old bank + pending rows | new rows] and the slot -> row table; the read and the
+    #      state update take the two parts where they are (the reference concatenates them) ----
     table = torch.full((B, shift + extent), -1, **i64)
-    zero = query.new_zeros(1, G, D)
     if state is not None:
         per = cap + chunk
         old_k = torch.cat((state.keys, state.pending_keys[:, :, :chunk]), 2).transpose(1, 2)
         old_v = torch.cat((state.values, state.pending_values[:, :, :chunk]), 2).transpose(1, 2)
-        src_k = torch.cat((old_k.reshape(-1, G, D).to(query.dtype), k_new, zero), 0)
-        src_v = torch.cat((old_v.reshape(-1, G, D).to(query.dtype), v_new, zero), 0)
+        old_k = old_k.reshape(-1, G, D).to(query.dtype)
+        old_v = old_v.reshape(-1, G, D).to(query.dtype)
         base = rows * per
         table[:, :shift] = base + torch.arange(shift, **i64)[None]
         table[:, shift:] = torch.where(~is_new, base + cap + slot, -1)
         offset = B * per
     else:
-        src_k = torch.cat((k_new, zero), 0)
-        src_v = torch.cat((v_new, zero), 0)
+        old_k = old_v = query.new_zeros(1, G, D)   # no old rows: a placeholder no reference reaches
         offset = 0
     if capture_safe:
         table[:, shift:] = torch.where(needed, offset + rows * extent + slot, table[:, shift:])
@@ -262,11 +275,14 @@ def sequence(query, scores, write_kv, valid, chunk, state=None, capacity=None, *
         # the read kernel addresses the prompt's own rows: slot s of row b is
         # token s - count + first valid token; only new, live slots are written
         first = torch.zeros(B, **i64) if order is None else valid.to(torch.int8).argmax(1)
-        out = _read_timeline(query, src_k, src_v, read_refs, first - c0, c0, fill, blocks, chunk, zero_fill=order
-                             is not None)
+        out = _read_timeline(query, old_k, old_v, offset, k_new, v_new, read_refs, first - c0, c0, fill, blocks,
+                             chunk, zero_fill=order is not None)
     else:
         # whole (token, all heads) rows move with index_select on flattened views
         q_slot = query.reshape(B * T, H * D).index_select(0, (rows * T + tok).flatten())
+        zero = query.new_zeros(1, G, D)                       # keeps the source non-empty; never referenced
+        src_k = torch.cat((old_k[:offset], k_new, zero), 0)
+        src_v = torch.cat((old_v[:offset], v_new, zero), 0)
         read = indexed_gqa(q_slot.view(B, blocks, chunk, H, D), src_k[None], src_v[None], read_refs)
         rank = torch.argsort(order, dim=1)                    # token -> its rank among the reordered tokens
         at = (c0[:, None] + rank).clamp(max=extent - 1)
@@ -279,8 +295,8 @@ def sequence(query, scores, write_kv, valid, chunk, state=None, capacity=None, *
         gi = torch.arange(G, **i64)[None, :, None]
         src_row = table[rows[:, :, None], bank_r.clamp(min=0)].clamp(min=0)
         hole = (bank_r < 0)[..., None]
-        state.keys.copy_(src_k[src_row, gi].masked_fill(hole, 0))
-        state.values.copy_(src_v[src_row, gi].masked_fill(hole, 0))
+        state.keys.copy_(_take(old_k, k_new, offset, src_row, gi).masked_fill(hole, 0))
+        state.values.copy_(_take(old_v, v_new, offset, src_row, gi).masked_fill(hole, 0))
         state.scores.copy_(bank_s)
         state.positions.copy_(bank_p)
         pc = state.pending_keys.shape[2]
@@ -288,8 +304,10 @@ def sequence(query, scores, write_kv, valid, chunk, state=None, capacity=None, *
         remaining = fill % chunk
         keep = torch.arange(pc, **i64)[None] < remaining[:, None]
         tail_row = table[rows, tail + shift].clamp(min=0)
-        state.pending_keys.copy_(src_k[tail_row].masked_fill(~keep[..., None, None], 0).transpose(1, 2))
-        state.pending_values.copy_(src_v[tail_row].masked_fill(~keep[..., None, None], 0).transpose(1, 2))
+        state.pending_keys.copy_(_take(old_k, k_new, offset, tail_row).masked_fill(~keep[..., None, None], 0)
+                                 .transpose(1, 2))
+        state.pending_values.copy_(_take(old_v, v_new, offset, tail_row).masked_fill(~keep[..., None, None], 0)
+                                   .transpose(1, 2))
         state.pending_scores.copy_(s_slot[rows, tail].masked_fill(~keep[..., None], float('-inf')).transpose(1, 2))
         state.count.copy_(remaining)
         state.total.copy_(t0 + n_new)
