@@ -864,7 +864,7 @@ def run_only(args):
             def fn():
                 yb.physical_ring_update_(rk, rv, rval, ridx, nk, nk, nval)
                 yb.physical_ring_decode_attention(sq, rk, rv, rval, workspace=sw)
-    elif args.only in ('mem_topk', 'mem_sequence'):
+    elif args.only in ('mem_topk', 'mem_sequence', 'mem_sequence_graph'):
         blocks, T = 128, 8192
         psc = (torch.randn(8, blocks, MEM_G, 64, generator=gen, device=dev) * 2).round() / 2
         ppos = torch.arange(T, device=dev).reshape(1, blocks, 1, 64).expand(8, blocks, MEM_G, 64).contiguous()
@@ -880,6 +880,18 @@ def run_only(args):
             st = yb.MemoryState.empty(8, MEM_G, MEM_CAP, MEM_CHUNK, MEM_D, dev, bf)
             yb.sequence(mq, msc, writer, None, MEM_CHUNK, st)
         fn = (lambda: yb.exclusive_prefix_topk(psc, ppos, ppos, 64)) if args.only == 'mem_topk' else seq
+        if args.only == 'mem_sequence_graph':   # the capture-safe form, replayed from a CUDA graph
+            st_g = yb.MemoryState.empty(8, MEM_G, MEM_CAP, MEM_CHUNK, MEM_D, dev, bf)
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                yb.sequence(mq, msc, writer, None, MEM_CHUNK, st_g, capture_safe=True)
+            torch.cuda.current_stream(dev).wait_stream(side)
+            torch.cuda.synchronize()
+            g_seq = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_seq):
+                yb.sequence(mq, msc, writer, None, MEM_CHUNK, st_g, capture_safe=True)
+            fn = g_seq.replay
     elif args.only == 'mem_layers':
         # the 8 memory layers' decode step in one CUDA graph, three bank states: empty banks, full banks
         # with no row merging during the timed replays (counts restarted at 0), and full banks with pending
@@ -1273,7 +1285,7 @@ def main():
     ap.add_argument('--no-b256', action='store_true', help='skip the config-2 batch (B=256)')
     ap.add_argument('--only', choices=['conv_update', 'gdn_decode', 'gdn_fused', 'gdn_chunk', 'mem_read', 'mem_commit',
                                        'mem_step', 'mem_step_merge', 'mem_layers', 'mem_indexed', 'mem_topk',
-                                       'mem_sequence', 'swa', 'swa_layer', 'swa_prefill', 'greedy',
+                                       'mem_sequence', 'mem_sequence_graph', 'swa', 'swa_layer', 'swa_prefill', 'greedy',
                                        'topk'], help='run one kernel family (small ncu captures)')
     ap.add_argument('--prefill-batch', type=int, default=8)
     ap.add_argument('--cpu-sample', nargs=3, type=int, metavar=('B', 'STEPS', 'WARMUP'), help=argparse.SUPPRESS)

@@ -346,6 +346,61 @@ int yb_mem_exclusive_prefix_topk(const float *scores, const void *positions, int
                                  void *stream);
 
 /*
+ * The prefill orchestration of one memory layer on the device, the index work
+ * of IndependentGQAMemory._sequence (modeling_yanchor.py:178-275) between the
+ * selection and the read, in four calls (every tensor contiguous unless a
+ * stride is given; shift = capacity with a state, 0 without).
+ *
+ * yb_mem_prefill_timeline (modeling_yanchor.py:186-205): each row's slots
+ *   [the state's pending tokens | new tokens, valid first], padded to extent
+ *   (a multiple of chunk).  scores [B, T, G] f32; order [B, T] int64 (the
+ *   stable valid-first order) or NULL; n_new [B] (valid tokens) or NULL (T);
+ *   count / total [B] at count_stride0 and pending_scores [B, G, PC] at
+ *   pmeta_stride0 (the state; ignored when shift = 0).  Writes snapshot
+ *   [3, B] (count, total, n_new before the call), slot scores / positions /
+ *   references [B, extent / chunk, G, chunk] (the selection's input) and the
+ *   token of every slot [B, extent].
+ */
+int yb_mem_prefill_timeline(const float *scores, const int64_t *order, const int64_t *n_new, const int64_t *count,
+                            const int64_t *total, int64_t count_stride0, const float *pending_scores,
+                            int64_t pmeta_stride0, int64_t B, int64_t T, int64_t G, int64_t chunk, int64_t extent,
+                            int64_t shift, int64_t PC, int64_t *snapshot, float *slot_scores,
+                            int64_t *slot_positions, int64_t *slot_references, int64_t *slot_tokens, void *stream);
+/*
+ * yb_mem_prefill_table (modeling_yanchor.py:206-244): from the prefix top-CAP
+ * references [B, blocks + 1, G, capacity], which new slots need a writer row
+ * (needed [B, extent] bytes) and the slot -> source-row table
+ * [B, shift + extent] (old rows b * (capacity + chunk) + s; -1 elsewhere).
+ * With capture_safe the writer ran on every slot (row b * extent + slot after
+ * the old rows), so the needed slots are filled in and read_references
+ * [B, blocks, G, capacity] is written too; otherwise the caller fills in the
+ * needed slots and calls yb_mem_prefill_read_references.
+ */
+int yb_mem_prefill_table(const int64_t *prefix_references, const int64_t *snapshot, int64_t B, int64_t G,
+                         int64_t chunk, int64_t extent, int64_t capacity, int has_state, int capture_safe,
+                         uint8_t *needed, int64_t *table, int64_t *read_references, void *stream);
+/* yb_mem_prefill_read_references: each block's prefix top-CAP as source rows (-1 = empty). */
+int yb_mem_prefill_read_references(const int64_t *prefix_references, const int64_t *table, int64_t B, int64_t G,
+                                   int64_t chunk, int64_t extent, int64_t capacity, int has_state,
+                                   int64_t *read_references, void *stream);
+/*
+ * yb_mem_prefill_state (modeling_yanchor.py:266-275): the new bank (the prefix
+ * entry after the last complete block) and pending chunk (the incomplete
+ * tail), their rows from old_keys / old_values [B * (capacity + chunk), G, D]
+ * (a copy of the bank and pending rows taken before the call) or new_keys /
+ * new_values [N, G, D] (the writer's rows), and count / total.  The state's
+ * fields at their batch strides (inner dimensions contiguous).
+ */
+int yb_mem_prefill_state(const float *prefix_scores, const int64_t *prefix_positions,
+                         const int64_t *prefix_references, const int64_t *table, const int64_t *snapshot,
+                         const float *slot_scores, const void *old_keys, const void *old_values, const void *new_keys,
+                         const void *new_values, void *keys, void *values, int64_t kv_stride0, float *bank_scores,
+                         int32_t *positions, int64_t meta_stride0, void *pending_keys, void *pending_values,
+                         int64_t pkv_stride0, float *pending_scores, int64_t pmeta_stride0, int64_t *count,
+                         int64_t *total, int64_t count_stride0, int64_t B, int64_t G, int64_t chunk, int64_t extent,
+                         int64_t capacity, int64_t PC, int64_t D, int dtype, void *stream);
+
+/*
  * Sampling.  scores [B, vocab] (row stride in elements) in dtype; out [B] int64.
  * Workspace: device scratch of at least yb_sample_workspace_bytes(B, vocab, top_k).
  *

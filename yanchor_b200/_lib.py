@@ -62,6 +62,12 @@ SIGNATURES = {
     'yb_mem_select_topk': (_I, [_P, _P, _I, _P, _I64, _I64, _I64, _P, _P, _P, _P]),
     'yb_mem_exclusive_prefix_topk': (_I, [_P, _P, _I, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _I, _P, _P, _P, _P,
                                           _P]),
+    'yb_mem_prefill_timeline': (_I, [_P, _P, _P, _P, _P, _I64, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
+                                     _P, _P, _P, _P, _P, _P]),
+    'yb_mem_prefill_table': (_I, [_P, _P, _I64, _I64, _I64, _I64, _I64, _I, _I, _P, _P, _P, _P]),
+    'yb_mem_prefill_read_references': (_I, [_P, _P, _I64, _I64, _I64, _I64, _I64, _I, _P, _P]),
+    'yb_mem_prefill_state': (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _P, _P, _I64, _P, _P, _I64,
+                                  _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I, _P]),
     'yb_sample_workspace_bytes': (_I64, [_I64, _I64, _I64]),
     'yb_sample_greedy': (_I, [_P, _I64, _I64, _I64, _I, _P, _P, _I64, _P]),
     'yb_sample_greedy_noalloc': (_I, [_P, _I64, _I64, _I64, _I, _P, _P]),

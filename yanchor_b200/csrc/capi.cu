@@ -425,6 +425,103 @@ int yb_mem_exclusive_prefix_topk(const float *scores, const void *positions, int
   return launch_exclusive_prefix_topk(a);
 }
 
+static bool glue_sizes_ok(int64_t B, int64_t G, int64_t chunk, int64_t extent, int64_t cap) {
+  return B >= 0 && G > 0 && chunk > 0 && extent >= 0 && extent % chunk == 0 && cap > 0 && B * extent < (1LL << 40);
+}
+
+int yb_mem_prefill_timeline(const float *scores, const int64_t *order, const int64_t *n_new, const int64_t *count,
+                            const int64_t *total, int64_t count_stride0, const float *pending_scores,
+                            int64_t pmeta_stride0, int64_t B, int64_t T, int64_t G, int64_t chunk, int64_t extent,
+                            int64_t shift, int64_t PC, int64_t *snapshot, float *slot_scores,
+                            int64_t *slot_positions, int64_t *slot_references, int64_t *slot_tokens, void *stream) {
+  YB_REQUIRE(glue_sizes_ok(B, G, chunk, extent, 1) && T > 0 && shift >= 0 && PC >= 0,
+             "mem_prefill_timeline: bad sizes");
+  YB_REQUIRE(scores && snapshot && slot_scores && slot_positions && slot_references && slot_tokens,
+             "mem_prefill_timeline: null tensor");
+  YB_REQUIRE(shift == 0 || (count && total && pending_scores && PC >= chunk),
+             "mem_prefill_timeline: a state needs its counters and pending scores");
+  PrefillGlueArgs a;
+  a.B = B; a.T = T; a.G = G; a.chunk = chunk; a.extent = extent; a.blocks = extent / chunk; a.shift = shift;
+  a.PC = PC; a.has_state = shift > 0;
+  a.count = count; a.total = total; a.count_s0 = count_stride0;
+  a.pend_scores = pending_scores; a.pmeta_s0 = pmeta_stride0;
+  a.order = order; a.n_new = n_new; a.scores = scores; a.snap = snapshot;
+  a.s_blk = slot_scores; a.pos_blk = slot_positions; a.ref_blk = slot_references; a.tok = slot_tokens;
+  a.stream = static_cast<cudaStream_t>(stream);
+  if (B * extent == 0) return YB_OK;
+  return launch_prefill_glue(a, 0);
+}
+
+int yb_mem_prefill_table(const int64_t *prefix_references, const int64_t *snapshot, int64_t B, int64_t G,
+                         int64_t chunk, int64_t extent, int64_t capacity, int has_state, int capture_safe,
+                         uint8_t *needed, int64_t *table, int64_t *read_references, void *stream) {
+  YB_REQUIRE(glue_sizes_ok(B, G, chunk, extent, capacity), "mem_prefill_table: bad sizes");
+  YB_REQUIRE(prefix_references && snapshot && needed && table, "mem_prefill_table: null tensor");
+  YB_REQUIRE(!capture_safe || read_references, "mem_prefill_table: capture_safe computes the read references");
+  PrefillGlueArgs a;
+  a.B = B; a.G = G; a.chunk = chunk; a.extent = extent; a.blocks = extent / chunk; a.cap = capacity;
+  a.has_state = has_state != 0; a.shift = has_state ? capacity : 0; a.capture_safe = capture_safe != 0;
+  a.pre_r = prefix_references; a.snap = const_cast<int64_t *>(snapshot); a.needed = needed; a.table = table;
+  a.read_refs = read_references;
+  a.stream = static_cast<cudaStream_t>(stream);
+  if (B * extent == 0) return YB_OK;
+  int rc = launch_prefill_glue(a, 1);
+  if (!rc && capture_safe) rc = launch_prefill_glue(a, 2);
+  return rc;
+}
+
+int yb_mem_prefill_read_references(const int64_t *prefix_references, const int64_t *table, int64_t B, int64_t G,
+                                   int64_t chunk, int64_t extent, int64_t capacity, int has_state,
+                                   int64_t *read_references, void *stream) {
+  YB_REQUIRE(glue_sizes_ok(B, G, chunk, extent, capacity), "mem_prefill_read_references: bad sizes");
+  YB_REQUIRE(prefix_references && table && read_references, "mem_prefill_read_references: null tensor");
+  PrefillGlueArgs a;
+  a.B = B; a.G = G; a.chunk = chunk; a.extent = extent; a.blocks = extent / chunk; a.cap = capacity;
+  a.has_state = has_state != 0; a.shift = has_state ? capacity : 0;
+  a.pre_r = prefix_references; a.table = const_cast<int64_t *>(table); a.read_refs = read_references;
+  a.stream = static_cast<cudaStream_t>(stream);
+  if (B * extent == 0) return YB_OK;
+  return launch_prefill_glue(a, 2);
+}
+
+int yb_mem_prefill_state(const float *prefix_scores, const int64_t *prefix_positions,
+                         const int64_t *prefix_references, const int64_t *table, const int64_t *snapshot,
+                         const float *slot_scores, const void *old_keys, const void *old_values, const void *new_keys,
+                         const void *new_values, void *keys, void *values, int64_t kv_stride0, float *bank_scores,
+                         int32_t *positions, int64_t meta_stride0, void *pending_keys, void *pending_values,
+                         int64_t pkv_stride0, float *pending_scores, int64_t pmeta_stride0, int64_t *count,
+                         int64_t *total, int64_t count_stride0, int64_t B, int64_t G, int64_t chunk, int64_t extent,
+                         int64_t capacity, int64_t PC, int64_t D, int dtype, void *stream) {
+  YB_REQUIRE(dtype_ok(dtype), "mem_prefill_state: bad dtype");
+  const int64_t vec = 16 / (dtype == YB_F32 ? 4 : 2);
+  YB_REQUIRE(glue_sizes_ok(B, G, chunk, extent, capacity) && PC >= chunk && D > 0 && D % vec == 0,
+             "mem_prefill_state: bad sizes");
+  YB_REQUIRE(prefix_scores && prefix_positions && prefix_references && table && snapshot && slot_scores &&
+                 old_keys && old_values && keys && values && bank_scores && positions && pending_keys &&
+                 pending_values && pending_scores && count && total,
+             "mem_prefill_state: null tensor");
+  YB_REQUIRE(aligned(old_keys, 16) && aligned(old_values, 16) && aligned(keys, 16) && aligned(values, 16) &&
+                 aligned(pending_keys, 16) && aligned(pending_values, 16) &&
+                 (!new_keys || (aligned(new_keys, 16) && aligned(new_values, 16))) && kv_stride0 % vec == 0 &&
+                 pkv_stride0 % vec == 0,
+             "mem_prefill_state: rows must be 16-byte aligned");
+  PrefillGlueArgs a;
+  a.B = B; a.G = G; a.chunk = chunk; a.extent = extent; a.blocks = extent / chunk; a.cap = capacity; a.PC = PC;
+  a.D = D; a.dtype = dtype; a.has_state = 1; a.shift = capacity;
+  a.pre_s = prefix_scores; a.pre_p = prefix_positions; a.pre_r = prefix_references;
+  a.table = const_cast<int64_t *>(table); a.snap = const_cast<int64_t *>(snapshot);
+  a.s_blk = const_cast<float *>(slot_scores);
+  a.old_k = old_keys; a.old_v = old_values; a.new_k = new_keys; a.new_v = new_values;
+  a.keys = keys; a.values = values; a.kv_s0 = kv_stride0;
+  a.bank_scores = bank_scores; a.positions = positions; a.meta_s0 = meta_stride0;
+  a.pkeys = pending_keys; a.pvalues = pending_values; a.pkv_s0 = pkv_stride0;
+  a.pscores = pending_scores; a.pmeta_s0 = pmeta_stride0;
+  a.count_out = count; a.total_out = total; a.count_s0 = count_stride0;
+  a.stream = static_cast<cudaStream_t>(stream);
+  if (B == 0) return YB_OK;
+  return launch_prefill_glue(a, 3);
+}
+
 int64_t yb_sample_workspace_bytes(int64_t B, int64_t vocab, int64_t top_k) {
   return sample_workspace_bytes(B, vocab, top_k);
 }

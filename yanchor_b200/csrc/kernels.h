@@ -91,6 +91,42 @@ bool mem_indexed_tc_supported(const MemIndexedArgs &a);
 int launch_mem_indexed_tc(const MemIndexedArgs &a);
 int read_device_error_idx(int clear);
 
+// Anchor-memory prefill orchestration (the index work around the selection and read kernels).
+struct PrefillGlueArgs {
+  int64_t B = 0, T = 0, G = 0, chunk = 0, extent = 0, blocks = 0, cap = 0, PC = 0, shift = 0, D = 0;
+  int has_state = 0, capture_safe = 0, dtype = 0;
+  const int64_t *count = nullptr, *total = nullptr;   // the state's counters (read by the timeline phase)
+  int64_t count_s0 = 0;
+  const float *pend_scores = nullptr;                  // [B, G, PC] at pmeta_s0
+  int64_t pmeta_s0 = 0;
+  const int64_t *order = nullptr, *n_new = nullptr;    // [B, T] / [B] or null
+  const float *scores = nullptr;                       // [B, T, G]
+  int64_t *snap = nullptr;                             // [3, B]: count, total, new tokens before the prefill
+  float *s_blk = nullptr;                              // [B, blocks, G, chunk]
+  int64_t *pos_blk = nullptr, *ref_blk = nullptr;
+  int64_t *tok = nullptr;                              // [B, extent]
+  const int64_t *pre_r = nullptr;                      // [B, blocks + 1, G, cap]
+  const float *pre_s = nullptr;
+  const int64_t *pre_p = nullptr;
+  uint8_t *needed = nullptr;                           // [B, extent]
+  int64_t *table = nullptr;                            // [B, shift + extent]
+  int64_t *read_refs = nullptr;                        // [B, blocks, G, cap]
+  const void *old_k = nullptr, *old_v = nullptr;       // [B * (cap + chunk), G, D]
+  const void *new_k = nullptr, *new_v = nullptr;       // [N, G, D]
+  void *keys = nullptr, *values = nullptr;             // the state, written by the state phase
+  int64_t kv_s0 = 0;
+  float *bank_scores = nullptr;
+  int32_t *positions = nullptr;
+  int64_t meta_s0 = 0;
+  void *pkeys = nullptr, *pvalues = nullptr;
+  int64_t pkv_s0 = 0;
+  float *pscores = nullptr;
+  int64_t *count_out = nullptr, *total_out = nullptr;
+  cudaStream_t stream = nullptr;
+};
+// phase 0: timeline; 1: needed + table; 2: read references; 3: the new state
+int launch_prefill_glue(const PrefillGlueArgs &a, int phase);
+
 struct TopkArgs {
   const float *scores;
   const void *positions;

@@ -10,8 +10,9 @@ read / write orchestration, with the reference's call signatures.
 
 The selections run on libyanchor_b200.so's sort / merge kernels and the read
 on its indexed-read kernel, which addresses the prompt's own query and output
-through the timeline; the orchestration between them is device-side torch
-indexing.  There is no CPU path.
+through the timeline; the index work between them (timeline, slot table,
+read references, new state) runs on its prefill orchestration kernels.
+There is no CPU path.
 """
 from __future__ import annotations
 
@@ -127,17 +128,6 @@ def _read_timeline(query, old_k, old_v, n_old, new_k, new_v, refs, shift, lo, hi
     return out
 
 
-def _take(old, new, n_old, idx, *more):
-    """Rows ``idx`` (any shape) of the joint source [old rows 0 .. n_old - 1 |
-    new rows], each indexed further by ``more`` (broadcast with ``idx``)."""
-    from_old = old[(idx.clamp(max=max(n_old - 1, 0)),) + more]
-    if new.shape[0] == 0:
-        return from_old
-    from_new = new[((idx - n_old).clamp(min=0, max=new.shape[0] - 1),) + more]
-    cond = torch.broadcast_to(idx, torch.broadcast_shapes(idx.shape, *(m.shape for m in more))) < n_old
-    return torch.where(cond.reshape(cond.shape + (1,) * (from_old.dim() - cond.dim())), from_old, from_new)
-
-
 def sequence(query, scores, write_kv, valid, chunk, state=None, capacity=None, *, capture_safe=False,
              mask_is_run=None):
     """Prefill anchor read and write (``IndependentGQAMemory._sequence``,
@@ -178,92 +168,76 @@ def sequence(query, scores, write_kv, valid, chunk, state=None, capacity=None, *
     if T == 0:
         return query.new_zeros(query.shape)                   # nothing to read or add
     i64 = dict(device=dev, dtype=torch.int64)
-    rows = torch.arange(B, **i64)[:, None]
+    L = _lib.lib()
+    stream = stream_ptr(dev)
+    ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
 
-    # ---- timeline: [the state's pending tokens | new tokens, valid first] ----
+    # ---- timeline: [the state's pending tokens | new tokens, valid first], on the device ----
     if valid is None:
-        order = None
-        n_new = torch.full((B,), T, **i64)
+        order = n_new = None
     else:
         valid = valid.to(device=dev, dtype=torch.bool)
-        order = torch.argsort((~valid).to(torch.int8), dim=1, stable=True)   # valid first, stable
-        n_new = valid.sum(1)
-    c0 = torch.zeros(B, **i64) if state is None else state.count.to(torch.int64).clone()
-    t0 = torch.zeros(B, **i64) if state is None else state.total.to(torch.int64).clone()
+        order = torch.argsort((~valid).to(torch.int8), dim=1, stable=True).contiguous()   # valid first, stable
+        n_new = valid.sum(1).to(torch.int64).contiguous()
     lead = 0 if state is None else chunk
     extent = -(-(T + lead) // chunk) * chunk
     blocks = extent // chunk
-    slot = torch.arange(extent, **i64)[None]
-    fill = c0 + n_new
-    live = slot < fill[:, None]
-    is_new = slot >= c0[:, None]
-    j = (slot - c0[:, None]).clamp(0, T - 1)                 # new-token rank of each slot
-    tok = j if order is None else order.gather(1, j)          # its token index
-    s_slot = scores.to(torch.float32).reshape(B * T, G).index_select(0, (rows * T + tok).flatten()).view(B, extent, G)
-    shift = 0
-    if state is not None:
-        pend = state.pending_scores[:, :, :chunk].transpose(1, 2).to(torch.float32)
-        s_slot = torch.where(is_new[..., None], s_slot, pend[rows, slot.clamp(max=chunk - 1)])
-        shift = cap
-    s_slot = s_slot.masked_fill(~live[..., None], float('-inf'))
-    pos_slot = (t0 - c0)[:, None] + slot
-    ref_slot = torch.where(live, slot + shift, -1)
-
-    def blocked(x):
-        if x.dim() == 2:
-            x = x[..., None].expand(B, extent, G)
-        return x.reshape(B, blocks, chunk, G).transpose(2, 3)
+    shift = 0 if state is None else cap
+    has_state = state is not None
+    if has_state:
+        _check_state_layout(state, chunk)
+        pc = int(state.pending_keys.shape[2])
+        count, total, pscores = state.count, state.total, state.pending_scores
+        count_s0, pmeta_s0 = count.stride(0), pscores.stride(0)
+    else:
+        pc, count, total, pscores, count_s0, pmeta_s0 = 0, None, None, None, 0, 0
+    snap = torch.empty(3, B, **i64)
+    s_blk = torch.empty(B, blocks, G, chunk, device=dev, dtype=torch.float32)
+    pos_blk = torch.empty(B, blocks, G, chunk, **i64)
+    ref_blk = torch.empty(B, blocks, G, chunk, **i64)
+    tok = torch.empty(B, extent, **i64)
+    s32 = scores.to(torch.float32).contiguous()
+    _lib.check(L.yb_mem_prefill_timeline(s32.data_ptr(), ptr(order), ptr(n_new), ptr(count), ptr(total), count_s0,
+                                         ptr(pscores), pmeta_s0, B, T, G, chunk, extent, shift, pc, snap.data_ptr(),
+                                         s_blk.data_ptr(), pos_blk.data_ptr(), ref_blk.data_ptr(), tok.data_ptr(),
+                                         stream), 'sequence (timeline)')
+    c0, fill = snap[0], snap[0] + snap[2]
 
     initial = None if state is None else (state.scores, state.positions)
-    pre_s, pre_p, pre_r = exclusive_prefix_topk(blocked(s_slot), blocked(pos_slot), blocked(ref_slot), cap,
-                                                initial=initial)
+    pre_s, pre_p, pre_r = exclusive_prefix_topk(s_blk, pos_blk, ref_blk, cap, initial=initial)
 
-    # ---- which new tokens get a key / value row ----
-    bound = (torch.arange(1, blocks + 1, **i64) * chunk)[None, :, None, None]
-    ent = pre_r[:, 1:] - shift                                # entrant slot of each block-end top-CAP
-    used = bound <= fill[:, None, None, None] if state is not None else bound < fill[:, None, None, None]
-    own = (ent >= bound - chunk) & (ent < bound) & used
-    needed = torch.zeros(B, extent + 1, device=dev, dtype=torch.bool)
-    needed.scatter_(1, torch.where(own, ent, extent).flatten(1), True)
-    needed = needed[:, :extent]
-    if state is not None:
-        full = fill // chunk
-        needed |= live & (slot >= (full * chunk)[:, None])    # the tail that stays pending
-    needed &= live & is_new
+    # ---- which new tokens get a key / value row, and the slot -> source-row table ----
+    needed = torch.empty(B, extent, device=dev, dtype=torch.uint8)
+    table = torch.empty(B, shift + extent, **i64)
+    read_refs = torch.empty(B, blocks, G, cap, **i64)
+    _lib.check(L.yb_mem_prefill_table(pre_r.data_ptr(), snap.data_ptr(), B, G, chunk, extent, cap, int(has_state),
+                                      int(capture_safe), needed.data_ptr(), table.data_ptr(), read_refs.data_ptr(),
+                                      stream), 'sequence (table)')
+    offset = B * (cap + chunk) if has_state else 0
     if capture_safe:
         # every slot of the timeline gets a writer row (row b * extent + slot); no list to size
-        sel_b = rows.expand(B, extent).reshape(-1)
+        sel_b = torch.arange(B, **i64)[:, None].expand(B, extent).reshape(-1)
         k_new, v_new = write_kv(sel_b, tok.reshape(-1))
     else:
         sel_b, sel_slot = needed.nonzero(as_tuple=True)
         k_new, v_new = write_kv(sel_b, tok[sel_b, sel_slot])
-    k_new = k_new.to(query.dtype).reshape(-1, G, D)
-    v_new = v_new.to(query.dtype).reshape(-1, G, D)
+        table[sel_b, shift + sel_slot] = offset + torch.arange(sel_b.numel(), **i64)
+        _lib.check(L.yb_mem_prefill_read_references(pre_r.data_ptr(), table.data_ptr(), B, G, chunk, extent, cap,
+                                                    int(has_state), read_refs.data_ptr(), stream),
+                   'sequence (read references)')
+    k_new = k_new.to(query.dtype).reshape(-1, G, D).contiguous()
+    v_new = v_new.to(query.dtype).reshape(-1, G, D).contiguous()
 
-    # ---- source rows [old bank + pending rows | new rows] and the slot -> row table; the read and the
-    #      state update take the two parts where they are (the reference concatenates them) ----
-    table = torch.full((B, shift + extent), -1, **i64)
-    if state is not None:
-        per = cap + chunk
+    # ---- the two row sources: [old bank + pending rows (a copy: the state is rewritten below) | new rows] ----
+    if has_state:
         old_k = torch.cat((state.keys, state.pending_keys[:, :, :chunk]), 2).transpose(1, 2)
         old_v = torch.cat((state.values, state.pending_values[:, :, :chunk]), 2).transpose(1, 2)
-        old_k = old_k.reshape(-1, G, D).to(query.dtype)
-        old_v = old_v.reshape(-1, G, D).to(query.dtype)
-        base = rows * per
-        table[:, :shift] = base + torch.arange(shift, **i64)[None]
-        table[:, shift:] = torch.where(~is_new, base + cap + slot, -1)
-        offset = B * per
+        old_k = old_k.reshape(-1, G, D).to(query.dtype).contiguous()
+        old_v = old_v.reshape(-1, G, D).to(query.dtype).contiguous()
     else:
         old_k = old_v = query.new_zeros(1, G, D)   # no old rows: a placeholder no reference reaches
-        offset = 0
-    if capture_safe:
-        table[:, shift:] = torch.where(needed, offset + rows * extent + slot, table[:, shift:])
-    else:
-        table[sel_b, shift + sel_slot] = offset + torch.arange(sel_b.numel(), **i64)
 
     # ---- read: block i attends to prefix entry i ----
-    reads = pre_r[:, :-1]
-    read_refs = torch.where(reads < 0, -1, table[rows[:, :, None, None], reads.clamp(min=0)])
     run = True                                                # each row's valid tokens are one run
     if order is not None:
         if mask_is_run is not None:
@@ -279,6 +253,7 @@ def sequence(query, scores, write_kv, valid, chunk, state=None, capacity=None, *
                              chunk, zero_fill=order is not None)
     else:
         # whole (token, all heads) rows move with index_select on flattened views
+        rows = torch.arange(B, **i64)[:, None]
         q_slot = query.reshape(B * T, H * D).index_select(0, (rows * T + tok).flatten())
         zero = query.new_zeros(1, G, D)                       # keeps the source non-empty; never referenced
         src_k = torch.cat((old_k[:offset], k_new, zero), 0)
@@ -290,25 +265,36 @@ def sequence(query, scores, write_kv, valid, chunk, state=None, capacity=None, *
         out.masked_fill_(~valid[..., None, None], 0)
 
     # ---- new state: bank = top-CAP over all complete blocks, tail = pending ----
-    if state is not None:
-        bank_s, bank_p, bank_r = (x[torch.arange(B, device=dev), full] for x in (pre_s, pre_p, pre_r))
-        gi = torch.arange(G, **i64)[None, :, None]
-        src_row = table[rows[:, :, None], bank_r.clamp(min=0)].clamp(min=0)
-        hole = (bank_r < 0)[..., None]
-        state.keys.copy_(_take(old_k, k_new, offset, src_row, gi).masked_fill(hole, 0))
-        state.values.copy_(_take(old_v, v_new, offset, src_row, gi).masked_fill(hole, 0))
-        state.scores.copy_(bank_s)
-        state.positions.copy_(bank_p)
-        pc = state.pending_keys.shape[2]
-        tail = (full[:, None] * chunk + torch.arange(pc, **i64)[None]).clamp(max=extent - 1)
-        remaining = fill % chunk
-        keep = torch.arange(pc, **i64)[None] < remaining[:, None]
-        tail_row = table[rows, tail + shift].clamp(min=0)
-        state.pending_keys.copy_(_take(old_k, k_new, offset, tail_row).masked_fill(~keep[..., None, None], 0)
-                                 .transpose(1, 2))
-        state.pending_values.copy_(_take(old_v, v_new, offset, tail_row).masked_fill(~keep[..., None, None], 0)
-                                   .transpose(1, 2))
-        state.pending_scores.copy_(s_slot[rows, tail].masked_fill(~keep[..., None], float('-inf')).transpose(1, 2))
-        state.count.copy_(remaining)
-        state.total.copy_(t0 + n_new)
+    if has_state:
+        n_rows = k_new.shape[0]
+        _lib.check(L.yb_mem_prefill_state(
+            pre_s.data_ptr(), pre_p.data_ptr(), pre_r.data_ptr(), table.data_ptr(), snap.data_ptr(),
+            s_blk.data_ptr(), old_k.data_ptr(), old_v.data_ptr(), k_new.data_ptr() if n_rows else None,
+            v_new.data_ptr() if n_rows else None, state.keys.data_ptr(), state.values.data_ptr(),
+            state.keys.stride(0), state.scores.data_ptr(), state.positions.data_ptr(), state.scores.stride(0),
+            state.pending_keys.data_ptr(), state.pending_values.data_ptr(), state.pending_keys.stride(0),
+            state.pending_scores.data_ptr(), state.pending_scores.stride(0), state.count.data_ptr(),
+            state.total.data_ptr(), state.count.stride(0), B, G, chunk, extent, cap, pc, D, dtype_code(query),
+            stream), 'sequence (state)')
     return out
+
+
+def _check_state_layout(state, chunk):
+    """The device orchestration reads and writes the state's fields at their
+    batch strides with every inner dimension contiguous (as the state's own
+    allocation and the vLLM page views are), in the query's dtype for the
+    rows, float32 scores, int32 positions and int64 counters."""
+    B, G, cap, D = state.keys.shape
+    pc = state.pending_keys.shape[2]
+    inner = lambda t, n: all(t.stride(i) == math.prod(t.shape[i + 1:]) for i in range(1, n))  # noqa: E731
+    ok = (state.values.shape == state.keys.shape and state.values.stride() == state.keys.stride()
+          and state.pending_values.shape == state.pending_keys.shape
+          and state.pending_values.stride() == state.pending_keys.stride() and pc >= chunk
+          and inner(state.keys, 4) and inner(state.pending_keys, 4) and inner(state.scores, 3)
+          and state.positions.stride() == state.scores.stride() and inner(state.pending_scores, 3)
+          and state.scores.dtype == torch.float32 and state.pending_scores.dtype == torch.float32
+          and state.positions.dtype == torch.int32 and state.count.dtype == torch.int64
+          and state.total.dtype == torch.int64 and state.count.stride() == state.total.stride())
+    if not ok:
+        raise ValueError('memory state: fields must be batch-strided with contiguous inner dimensions '
+                         '(float32 scores, int32 positions, int64 count / total)')
