@@ -1331,7 +1331,8 @@ def main():
         import torch
         import torch.distributed as tdist
         torch.cuda.set_device(local_rank)
-        tdist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120))
+        tdist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120),
+                                 device_id=torch.device('cuda', local_rank))
         dist = tdist
     result, _ = run_gpu(args, rank, world, local_rank, dist)
     import torch
