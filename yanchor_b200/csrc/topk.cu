@@ -12,13 +12,17 @@
 //
 // select: one CTA per row, bitonic sort of the keys in shared memory.
 // exclusive prefix: phase 1 selects each block's own top-CAP (sorted) into
-// output slot blk + 1 (only a block's top-CAP can survive any later merge);
-// phase 2 runs one CTA per (row, group) down the blocks, merging the running
-// top-CAP with the next block by binary-search ranks (both lists are sorted;
-// on equal keys the running list goes first, as it precedes the block in
-// the reference's concatenation) and writing each prefix back in place.  An
-// optional initial bank seeds the scan, which equals the reference's merge
-// of every prefix entry with the state's bank (modeling_yanchor.py:206-208).
+// output slot blk + 1 (only a block's top-CAP can survive any later merge).
+// Merging two sorted top-CAP lists (binary-search ranks; on equal keys the
+// earlier list goes first, as it precedes the later one in the reference's
+// concatenation) is associative, so the scan over the blocks runs as a
+// two-level scan: phase 2 merges, inside each segment of 1024 / (2 CAP)
+// blocks, the blocks' lists into local prefixes (one CTA per segment); phase
+// 3 runs one CTA per (row, group) down the segments, merging the running
+// prefix with all of a segment's local prefixes at once.  A sequential depth
+// of seg + blocks / seg merges instead of blocks.  An optional initial bank
+// seeds the running prefix, which equals the reference's merge of every
+// prefix entry with the state's bank (modeling_yanchor.py:206-208).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -124,16 +128,97 @@ struct Entry {
   int64_t p, r;
 };
 
-__global__ void prefix_scan_kernel(const ScanArgs a) {
+// Merge of two sorted top-cap lists into the first cap of their union (the
+// left list first on equal keys), by the group of 2 * cap threads t: thread
+// t < cap places left[t], thread cap + t places right[t], at their ranks.
+__device__ __forceinline__ void merge_place(const Key *lk, const Entry *le, const Key *rk, const Entry *re, Key *nk,
+                                            Entry *ne, int cap, int t) {
+  const bool from_left = t < cap;
+  const int i = from_left ? t : t - cap;
+  const Key mine = from_left ? lk[i] : rk[i];
+  const Key *other = from_left ? rk : lk;
+  // from the left: count other < mine;  from the right: count other <= mine
+  int lo = 0, hi = cap;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    const bool before = from_left ? key_less(other[mid], mine) : !key_less(mine, other[mid]);
+    if (before) lo = mid + 1; else hi = mid;
+  }
+  const int rank = i + lo;
+  if (rank < cap) {
+    nk[rank] = mine;
+    ne[rank] = from_left ? le[i] : re[i];
+  }
+}
+
+__device__ __forceinline__ Entry load_entry(const ScanArgs &a, int64_t o) {
+  return Entry{a.out_s[o], a.out_p[o], a.out_r[o]};
+}
+__device__ __forceinline__ void store_entry(const ScanArgs &a, int64_t o, const Entry &e) {
+  a.out_s[o] = e.s;
+  a.out_p[o] = e.p;
+  a.out_r[o] = e.r;
+}
+// keys of a list entry: the index bits stay 0, so equal keys keep list order
+__device__ __forceinline__ Key entry_key(const Entry &e) { return make_key(e.s, e.p, e.r, 0u); }
+
+// Phase A: within each segment of `seg` blocks, the inclusive prefix of the
+// blocks' own top-cap lists (slots blk + 1), written back in place.  One CTA
+// of 2 * cap threads per (row, group, segment).
+__global__ void prefix_segment_kernel(const ScanArgs a, int seg) {
   extern __shared__ __align__(16) unsigned char scan_raw[];
   const int cap = int(a.cap);
-  Key *acc_k = reinterpret_cast<Key *>(scan_raw);            // [cap]
-  Key *cand_k = acc_k + cap;                                  // [cap]
-  Key *new_k = cand_k + cap;                                  // [cap]
-  Entry *acc_e = reinterpret_cast<Entry *>(new_k + cap);      // [cap]
-  Entry *cand_e = acc_e + cap;                                // [cap]
-  Entry *new_e = cand_e + cap;                                // [cap]
+  Key *acc_k = reinterpret_cast<Key *>(scan_raw);
+  Key *cand_k = acc_k + cap;
+  Key *new_k = cand_k + cap;
+  Entry *acc_e = reinterpret_cast<Entry *>(new_k + cap);
+  Entry *cand_e = acc_e + cap;
+  Entry *new_e = cand_e + cap;
   const int tid = threadIdx.x;
+  const int64_t nseg = (a.blocks + seg - 1) / seg;
+  const int64_t bg = blockIdx.x / nseg, sg = blockIdx.x % nseg;
+  const int64_t b = bg / a.G, g = bg % a.G;
+  auto slot = [&](int64_t i) { return ((b * (a.blocks + 1) + i) * a.G + g) * a.cap; };
+  const int64_t first = sg * seg, last = (first + seg < a.blocks ? first + seg : a.blocks) - 1;
+  if (tid < cap) {
+    const Entry e = load_entry(a, slot(first + 1) + tid);
+    acc_e[tid] = e;
+    acc_k[tid] = entry_key(e);
+  }
+  for (int64_t blk = first + 1; blk <= last; ++blk) {
+    if (tid < cap) {
+      const Entry e = load_entry(a, slot(blk + 1) + tid);
+      cand_e[tid] = e;
+      cand_k[tid] = entry_key(e);
+    }
+    __syncthreads();
+    if (tid < 2 * cap) merge_place(acc_k, acc_e, cand_k, cand_e, new_k, new_e, cap, tid);
+    __syncthreads();
+    if (tid < cap) {
+      acc_k[tid] = new_k[tid];
+      acc_e[tid] = new_e[tid];
+      store_entry(a, slot(blk + 1) + tid, new_e[tid]);
+    }
+    __syncthreads();
+  }
+}
+
+// Phase B: one CTA per (row, group) walks the segments: the running prefix
+// (the sorted initial bank first, written to slot 0) is merged with every
+// local prefix of the segment at once (groups of 2 * cap threads, one block
+// each), which gives those blocks' exclusive prefixes; the segment's last
+// result carries on.  Every merge keeps the earlier blocks first on equal
+// keys, so the result is the sequential scan's.
+__global__ void prefix_carry_kernel(const ScanArgs a, int seg) {
+  extern __shared__ __align__(16) unsigned char scan_raw[];
+  const int cap = int(a.cap);
+  Key *acc_k = reinterpret_cast<Key *>(scan_raw);               // [cap]
+  Key *cand_k = acc_k + cap;                                     // [seg][cap]
+  Key *new_k = cand_k + seg * cap;                               // [seg][cap]
+  Entry *acc_e = reinterpret_cast<Entry *>(new_k + seg * cap);   // [cap]
+  Entry *cand_e = acc_e + cap;                                   // [seg][cap]
+  Entry *new_e = cand_e + seg * cap;                             // [seg][cap]
+  const int tid = threadIdx.x, q = tid / (2 * cap), t = tid % (2 * cap);
   const int64_t b = blockIdx.x / a.G, g = blockIdx.x % a.G;
   auto slot = [&](int64_t i) { return ((b * (a.blocks + 1) + i) * a.G + g) * a.cap; };
 
@@ -157,56 +242,26 @@ __global__ void prefix_scan_kernel(const ScanArgs a) {
     for (int j = 0; j < cap; ++j) rank += key_less(cand_k[j], mine);
     acc_e[rank] = cand_e[tid];
     acc_k[rank] = Key{mine.hi, mine.lo & ~0xffffffffull};   // index no longer needed: list order breaks ties
-    const int64_t o = slot(0) + rank;
-    a.out_s[o] = cand_e[tid].s;
-    a.out_p[o] = cand_e[tid].p;
-    a.out_r[o] = cand_e[tid].r;
-  }
-  // the first block's candidates
-  Entry next{-INFINITY, -1, -1};
-  if (tid < cap && a.blocks > 0) {
-    const int64_t o = slot(1) + tid;
-    next = Entry{a.out_s[o], a.out_p[o], a.out_r[o]};
+    store_entry(a, slot(0) + rank, cand_e[tid]);
   }
   __syncthreads();
-
-  for (int64_t blk = 0; blk < a.blocks; ++blk) {
-    if (tid < cap) {
-      cand_e[tid] = next;
-      cand_k[tid] = make_key(next.s, next.p, next.r, 0u);
-      if (blk + 1 < a.blocks) {                // prefetch the next block's candidates
-        const int64_t o = slot(blk + 2) + tid;
-        next = Entry{a.out_s[o], a.out_p[o], a.out_r[o]};
-      }
+  for (int64_t first = 0; first < a.blocks; first += seg) {
+    const int64_t blk = first + q;
+    const bool active = q < seg && blk < a.blocks;
+    if (active && t < cap) {
+      const Entry e = load_entry(a, slot(blk + 1) + t);   // the local prefix of the segment up to blk
+      cand_e[q * cap + t] = e;
+      cand_k[q * cap + t] = entry_key(e);
     }
     __syncthreads();
-    if (tid < 2 * cap) {
-      const bool from_acc = tid < cap;
-      const int t = from_acc ? tid : tid - cap;
-      const Key mine = from_acc ? acc_k[t] : cand_k[t];
-      const Key *other = from_acc ? cand_k : acc_k;
-      // from_acc: count other < mine;  from cand: count other <= mine
-      int lo = 0, hi = cap;
-      while (lo < hi) {
-        const int mid = (lo + hi) >> 1;
-        const bool before = from_acc ? key_less(other[mid], mine) : !key_less(mine, other[mid]);
-        if (before) lo = mid + 1; else hi = mid;
-      }
-      const int rank = t + lo;
-      if (rank < cap) {
-        new_k[rank] = mine;
-        new_e[rank] = from_acc ? acc_e[t] : cand_e[t];
-      }
-    }
+    if (active)
+      merge_place(acc_k, acc_e, cand_k + q * cap, cand_e + q * cap, new_k + q * cap, new_e + q * cap, cap, t);
     __syncthreads();
+    if (active && t < cap) store_entry(a, slot(blk + 1) + t, new_e[q * cap + t]);
+    const int64_t lastq = (first + seg < a.blocks ? seg : a.blocks - first) - 1;
     if (tid < cap) {
-      acc_k[tid] = new_k[tid];
-      const Entry e = new_e[tid];
-      acc_e[tid] = e;
-      const int64_t o = slot(blk + 1) + tid;
-      a.out_s[o] = e.s;
-      a.out_p[o] = e.p;
-      a.out_r[o] = e.r;
+      acc_k[tid] = new_k[lastq * cap + tid];
+      acc_e[tid] = new_e[lastq * cap + tid];
     }
     __syncthreads();
   }
@@ -254,12 +309,27 @@ int launch_exclusive_prefix_topk(const PrefixTopkArgs &t) {
     if (rc) return rc;
   }
   ScanArgs s{t.init_s, t.init_p, t.init_r, t.init_pos_dtype, t.B, t.blocks, t.G, t.cap, t.out_s, t.out_p, t.out_r};
-  const size_t smem = size_t(t.cap) * 3 * (sizeof(Key) + sizeof(Entry));
-  cudaError_t e = cudaFuncSetAttribute(prefix_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  // segments of `seg` blocks: as many merges side by side as fit in 1024 threads (8 at cap 64)
+  const int seg = int(1024 / (2 * t.cap) > 0 ? 1024 / (2 * t.cap) : 1);
+  const int64_t nseg = (t.blocks + seg - 1) / seg;
+  const int group = int((2 * t.cap + 31) / 32 * 32);
+  if (seg > 1 && t.blocks > 1) {
+    const size_t smem_a = size_t(t.cap) * 3 * (sizeof(Key) + sizeof(Entry));
+    cudaError_t e = cudaFuncSetAttribute(prefix_segment_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         int(smem_a));
+    if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "prefix scan: smem attribute: %s", cudaGetErrorString(e));
+    prefix_segment_kernel<<<unsigned(t.B * t.G * nseg), group, smem_a, t.stream>>>(s, seg);
+    const int rc = check_launch("prefix_segment_kernel");
+    if (rc) return rc;
+  }
+  const int seg_b = t.blocks > 1 ? seg : 1;   // one block per segment: phase A is the identity
+  const size_t smem_b = size_t(t.cap) * (1 + 2 * seg_b) * (sizeof(Key) + sizeof(Entry));
+  cudaError_t e = cudaFuncSetAttribute(prefix_carry_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(smem_b));
   if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "prefix scan: smem attribute: %s", cudaGetErrorString(e));
-  const int threads = int((2 * t.cap + 31) / 32 * 32);
-  prefix_scan_kernel<<<unsigned(t.B * t.G), threads, smem, t.stream>>>(s);
-  return check_launch("prefix_scan_kernel");
+  const int threads = int(((2 * t.cap * seg_b) + 31) / 32 * 32);
+  prefix_carry_kernel<<<unsigned(t.B * t.G), threads, smem_b, t.stream>>>(s, seg_b);
+  return check_launch("prefix_carry_kernel");
 }
 
 }  // namespace yb
