@@ -38,6 +38,13 @@ template <typename T>
 __global__ void __launch_bounds__(kConvThreads) conv_update4_kernel(const ConvArgs a) {
   const int64_t c = (int64_t(blockIdx.x) * kConvThreads + threadIdx.x) * 4;
   const int64_t b0 = int64_t(blockIdx.y) * kConvRows;
+  if (c < a.C && (threadIdx.x & 1) == 0) {
+    // warm L2 with this thread pair's state row pieces and weights before the wait (an L2 prefetch is
+    // safe even if the previous kernel writes them); the input comes from the previous kernel
+    for (int rr = 0; rr < kConvRows && b0 + rr < a.B; ++rr)
+      prefetch_l2(static_cast<const T *>(a.state) + (b0 + rr) * a.state_bs + c * 4);
+    prefetch_l2(a.weight + c * 4);
+  }
   pdl_wait();
   pdl_release();
   if (c >= a.C) return;
