@@ -295,7 +295,7 @@ __global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(const RecParams
 
 // One token per sequence, row-major state: the state is staged in shared
 // memory by four bulk copies (16 KB each for fp32, 8 KB for a 16-bit state)
-// rather than held in registers, so three (fp32) or four (16-bit) CTAs share
+// rather than held in registers, so three (fp32) or five (16-bit) CTAs share
 // an SM and more bytes are in flight per SM than with register-resident
 // CTAs; four copies instead of sixteen vector loads per thread.  The copies'
 // wait is bounded: on timeout the CTA records ERR_REC_STATE, skips the
@@ -323,7 +323,7 @@ __device__ __forceinline__ void bulk_load_state(void *dst, const void *src, uint
 }
 
 template <typename TIO, typename TS, bool NORM>
-__global__ void __launch_bounds__(kThreads, sizeof(TS) == 4 ? 3 : 4) gdn_recurrent_sst_kernel(const RecParams p) {
+__global__ void __launch_bounds__(kThreads, sizeof(TS) == 4 ? 3 : 5) gdn_recurrent_sst_kernel(const RecParams p) {
   constexpr int K = 128, V = 128, COLS = V, NCG = COLS / 4, RG = kThreads / NCG, RPT = K / RG;
   constexpr uint32_t kS32Bytes = staged_bytes<TS>();
   extern __shared__ __align__(128) unsigned char s32_dyn[];
@@ -516,7 +516,7 @@ int launch_kv(const GdnArgs &a, const RecParams &p) {
   const bool norm = a.z != nullptr;
   dim3 grid(unsigned(a.N * a.HV));
   if constexpr (K == 128 && V == 128) {
-    // one token per sequence: the state staged in shared memory, three (fp32) or four (16-bit)
+    // one token per sequence: the state staged in shared memory, three (fp32) or five (16-bit)
     // CTAs per SM
     if (!trans && a.T == 1 && !a.cu_seqlens && a.h0 && a.ht && (reinterpret_cast<uintptr_t>(a.h0) & 15u) == 0) {
       auto ks = norm ? gdn_recurrent_sst_kernel<TIO, TS, true> : gdn_recurrent_sst_kernel<TIO, TS, false>;
