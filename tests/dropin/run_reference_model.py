@@ -15,9 +15,9 @@ Same weights (B loads A's state dict), bf16, a 150-token prefill of two
 prompts then 49 decode steps.  A third run, the same weights in fp32 on the
 reference's torch path, is the yardstick: its greedy tokens feed all three
 runs, and each bf16 path's logits are compared with it.  The model shape
-(§8(c) of the task's survey: 4 layers, 3 GDN + 1 SWA layer with an
-IndependentGQAMemory of 16 slots, commit chunk 16, window 32) uses the
-YANchor head shapes (GDN K = V = 128, memory / SWA head_dim 256).
+(the smallest YANchorForCausalLM that has every layer kind: 4 layers, 3 GDN
++ 1 SWA layer with an IndependentGQAMemory of 16 slots, commit chunk 16,
+window 32) uses the YANchor head shapes (GDN K = V = 128, memory / SWA head_dim 256).
 
 fla is made unavailable in this process, so transformers builds the GDN
 layers of both models with the same torch modules (its gated RMSNorm
