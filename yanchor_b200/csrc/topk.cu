@@ -185,11 +185,13 @@ __global__ void prefix_segment_kernel(const ScanArgs a, int seg) {
     acc_e[tid] = e;
     acc_k[tid] = entry_key(e);
   }
+  Entry nxt{-INFINITY, -1, -1};   // the next block's entry, loaded one merge ahead
+  if (tid < cap && first + 1 <= last) nxt = load_entry(a, slot(first + 2) + tid);
   for (int64_t blk = first + 1; blk <= last; ++blk) {
     if (tid < cap) {
-      const Entry e = load_entry(a, slot(blk + 1) + tid);
-      cand_e[tid] = e;
-      cand_k[tid] = entry_key(e);
+      cand_e[tid] = nxt;
+      cand_k[tid] = entry_key(nxt);
+      if (blk + 1 <= last) nxt = load_entry(a, slot(blk + 2) + tid);
     }
     __syncthreads();
     if (tid < 2 * cap) merge_place(acc_k, acc_e, cand_k, cand_e, new_k, new_e, cap, tid);
@@ -245,13 +247,16 @@ __global__ void prefix_carry_kernel(const ScanArgs a, int seg) {
     store_entry(a, slot(0) + rank, cand_e[tid]);
   }
   __syncthreads();
+  // the local prefix of each segment up to block first + q, loaded one segment ahead
+  Entry nxt{-INFINITY, -1, -1};
+  if (q < seg && q < a.blocks && t < cap) nxt = load_entry(a, slot(q + 1) + t);
   for (int64_t first = 0; first < a.blocks; first += seg) {
     const int64_t blk = first + q;
     const bool active = q < seg && blk < a.blocks;
     if (active && t < cap) {
-      const Entry e = load_entry(a, slot(blk + 1) + t);   // the local prefix of the segment up to blk
-      cand_e[q * cap + t] = e;
-      cand_k[q * cap + t] = entry_key(e);
+      cand_e[q * cap + t] = nxt;
+      cand_k[q * cap + t] = entry_key(nxt);
+      if (blk + seg < a.blocks) nxt = load_entry(a, slot(blk + seg + 1) + t);
     }
     __syncthreads();
     if (active)
