@@ -155,28 +155,38 @@ def test_decode_16bit_state_storage(yb, sdtype, trans):
     assert rel(host(state), es) <= STATE_RTOL
 
 
-@pytest.mark.parametrize('sdtype', [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize('sdtype', [torch.float32, torch.float16, torch.bfloat16])
 @pytest.mark.parametrize('B,H,HV', [(6, 16, 32), (3, 1, 1)])
-def test_decode_16bit_packed_path_matches_generic(yb, sdtype, B, H, HV):
-    """One token per sequence with a 16-bit state in place runs the staged
-    kernel (the state copied into shared memory by bulk copies); the same
-    inputs laid out as varlen sequences of length 1 run the generic kernel.
-    Both do the same fp32 operations, so outputs and states agree bit for
-    bit, at the YANchor head counts and at one head."""
+@pytest.mark.parametrize('norm', [False, True])
+def test_decode_staged_path_matches_generic(yb, sdtype, B, H, HV, norm):
+    """One token per sequence with the state in place runs the staged kernel
+    (the state copied into shared memory by bulk copies); the same inputs
+    laid out as varlen sequences of length 1 run the generic kernel.  Both do
+    the same fp32 operations in the same order, so outputs and states agree
+    bit for bit, for fp32 and 16-bit states, at the YANchor head counts and
+    at one head, with and without the fused gates and gated RMSNorm."""
     rng = np.random.default_rng(91)
     K, V = 128, 128
     q, k, v, g, beta, h0 = make_inputs(rng, B, 1, H, HV, K, V, h0_std=0.05)
     bf = torch.bfloat16
     sa = cuda(h0).to(sdtype)
     sb = sa.clone()
+    extra = {}
+    if norm:
+        extra = dict(use_gate_in_kernel=True, A_log=cuda(np.log(rng.uniform(1, 16, HV)).astype(np.float32)),
+                     dt_bias=cuda(rng.standard_normal(HV).astype(np.float32)), use_beta_sigmoid_in_kernel=True,
+                     norm_weight=cuda((1 + 0.1 * rng.standard_normal(V)).astype(np.float32), bf))
+        z = rng.standard_normal((B, 1, HV, V)).astype(np.float32)
     oa, _ = yb.fused_recurrent_gated_delta_rule(cuda(q, bf), cuda(k, bf), cuda(v, bf), g=cuda(g), beta=cuda(beta),
                                                 initial_state=sa, output_final_state=True,
-                                                use_qk_l2norm_in_kernel=True, inplace=True)
+                                                use_qk_l2norm_in_kernel=True, inplace=True,
+                                                **(dict(extra, z=cuda(z, bf)) if norm else {}))
     cu = torch.arange(B + 1, device='cuda', dtype=torch.int64)
     flat = lambda x, dt=None: cuda(x, dt).reshape(1, B, *x.shape[2:]) if dt else cuda(x).reshape(1, B, *x.shape[2:])  # noqa: E731
     ob, _ = yb.fused_recurrent_gated_delta_rule(flat(q, bf), flat(k, bf), flat(v, bf), g=flat(g), beta=flat(beta),
                                                 initial_state=sb, output_final_state=True,
-                                                use_qk_l2norm_in_kernel=True, inplace=True, cu_seqlens=cu)
+                                                use_qk_l2norm_in_kernel=True, inplace=True, cu_seqlens=cu,
+                                                **(dict(extra, z=flat(z, bf)) if norm else {}))
     torch.cuda.synchronize()
     assert torch.equal(sa, sb)
     assert torch.equal(oa.reshape(-1), ob.reshape(-1))
