@@ -1,7 +1,9 @@
-"""GPU parity against the reference's own GPU kernels for the anchor memory:
-the Triton module runtime/model/independent_memory.py from the reference
-install (`committed_gqa` :177, `commit_decode` :190, `indexed_gqa` :38), run
-on the same inputs on the same GPU.
+"""GPU parity against the reference's own GPU kernels, run from its install
+on the same inputs on the same GPU: the anchor memory's Triton module
+runtime/model/independent_memory.py (`committed_gqa` :177, `commit_decode`
+:190, `indexed_gqa` :38), and from runtime/model/inference_kernels.py the
+fused top-20 sampler, the graph-safe conv update, the fused GDN gates and
+the decode loop's bookkeeping.
 
 The memory state is index and copy work, so after every decode step each
 state field must be equal bit for bit; the reads are bf16 outputs of two
@@ -106,3 +108,91 @@ def test_top20_sampler_matches_reference_triton(yb):
         ids = yb.sample_top_k_top_p_counter(logits, attempt, step, seed=1234, temperature=0.7, top_k=20, top_p=0.95)
         torch.cuda.synchronize()
         assert torch.equal(ids.view(-1).cpu(), ref_ids.view(-1).cpu()), step
+
+
+def _kernels():
+    if not os.path.exists(os.path.join(REF, 'runtime', 'model', 'inference_kernels.py')):
+        pytest.skip('SKIPPED, NOT PASSED: the reference install (baseline/_ref) is absent')
+    import _reference
+    return _reference.inference_kernels()
+
+
+def test_conv_update_matches_reference_triton(yb):
+    """The graph-safe decode convolution (inference_kernels.py:339-376) on the
+    cache's own [B, C, 4] state layout: the shifted state bit-identical, the
+    bf16 output within one rounding (the two sum the four taps in different
+    orders)."""
+    ik = _kernels()
+    B, C, KS = 64, 8192, 4
+    bf = torch.bfloat16
+    gen = torch.Generator(device='cuda').manual_seed(41)
+    state = torch.randn(B, C, KS, generator=gen, device='cuda').to(bf)
+    ref_state = state.clone()
+    w = torch.randn(C, KS, generator=gen, device='cuda') * 0.5
+    bias = torch.randn(C, generator=gen, device='cuda') * 0.1
+    for _ in range(3):
+        x = torch.randn(B, C, 1, generator=gen, device='cuda').to(bf)
+        y = yb.causal_conv1d_update(x, state, w, bias, 'silu')
+        ry = ik.triton_graph_safe_causal_conv1d_update(x, ref_state, w, bias, 'silu')
+        torch.cuda.synchronize()
+        assert torch.equal(state, ref_state)
+        d = (y.float() - ry.float()).abs()
+        assert (d <= ry.float().abs() * 2 ** -7 + 1e-6).all()
+
+
+def test_gates_match_reference_triton(yb):
+    """The fused decode gates (inference_kernels.py:668-691): beta = sigmoid(b)
+    in bf16 and g = -exp(A_log) softplus(a + dt_bias) in fp32."""
+    ik = _kernels()
+    B, HV = 64, 32
+    gen = torch.Generator(device='cuda').manual_seed(43)
+    b = torch.randn(B, 1, HV, generator=gen, device='cuda').to(torch.bfloat16)
+    a = (3 * torch.randn(B, 1, HV, generator=gen, device='cuda')).to(torch.bfloat16)
+    A_log = torch.log(torch.rand(HV, generator=gen, device='cuda') * 15 + 1)
+    dt_bias = torch.randn(HV, generator=gen, device='cuda')
+    beta, g = yb.gdn_gates(b, a, A_log, dt_bias)
+    rbeta, rg = ik.triton_qwen35_fused_gdn_gates(b, a, A_log, dt_bias)
+    torch.cuda.synchronize()
+    assert (beta.float() - rbeta.float()).abs().max().item() <= 2 ** -8
+    assert ((g - rg).abs() <= rg.abs() * 1e-5 + 1e-7).all()
+
+
+def test_decode_bookkeeping_matches_reference_triton(yb):
+    """The decode loop's per-step bookkeeping (inference_kernels.py:1169-1208)
+    over a 42-step trajectory with EOS ids, empty slots and per-row caps:
+    every table bit-identical."""
+    ik = _kernels()
+    slots, total, max_new, vocab, pad, eos = 96, 192, 40, 64, 1, (5, 9)
+    gen = torch.Generator(device='cuda').manual_seed(47)
+    i64 = dict(device='cuda', dtype=torch.int64)
+
+    def fresh():
+        perm = torch.randperm(total, generator=gen, device='cuda')[:slots]
+        rows = torch.where(torch.rand(slots, generator=gen, device='cuda') < 0.9, perm, torch.full_like(perm, -1))
+        return {
+            'storage': torch.full((total + slots, max_new + 1), pad, device='cuda', dtype=torch.int32),
+            'dense_seen': torch.zeros(slots, vocab, device='cuda', dtype=torch.bool),
+            'generated_lengths': torch.zeros(total + slots, **i64),
+            'finished_by_eos': torch.zeros(total + slots, device='cuda', dtype=torch.bool),
+            'finished': torch.rand(slots, generator=gen, device='cuda') < 0.1,
+            'slot_rows': rows,
+            'sink_rows': total + torch.arange(slots, **i64),
+            'slot_caps': torch.randint(1, max_new + 1, (slots,), generator=gen, **i64),
+            'row_steps': torch.ones(slots, **i64),
+            'row_positions': torch.randint(0, 5000, (slots,), generator=gen, **i64),
+            'decode_ids': torch.randint(0, vocab, (slots, 1), generator=gen, **i64),
+            'decode_useful_events': torch.zeros((), **i64),
+        }
+    ours = fresh()
+    theirs = {k: v.clone() for k, v in ours.items()}
+    order = ('storage', 'dense_seen', 'generated_lengths', 'finished_by_eos', 'finished', 'slot_rows', 'sink_rows',
+             'slot_caps', 'row_steps', 'row_positions', 'decode_ids', 'decode_useful_events')
+    for _ in range(max_new + 2):
+        tok = torch.randint(0, vocab, (slots, 1), generator=gen, **i64)
+        yb.update_fixed_decode_state_(tok, *(ours[k] for k in order), maximum_new_tokens=max_new,
+                                      pad_token_id=pad, eos_token_ids=eos)
+        ik._update_fixed_decode_state_(tok, *(theirs[k] for k in order), maximum_new_tokens=max_new,
+                                       pad_token_id=pad, eos_token_ids=eos)
+    torch.cuda.synchronize()
+    for k in order:
+        assert torch.equal(ours[k], theirs[k]), k
