@@ -30,6 +30,7 @@ graph of the whole model forward too).
 from __future__ import annotations
 
 import argparse
+import importlib.util
 import json
 import os
 import statistics
@@ -1169,6 +1170,78 @@ def cpu_decode_parallel(steps=2, B=64, warmup=0):
     return B * steps / dt, dt, workers
 
 
+def reference_gpu_decode_step(torch, yb, dev, ref_mem, fla_rec, B=64, reps=10):
+    """The headline decode step at B=64 composed from the GPU kernels the reference's own stack runs for
+    it, captured in one CUDA graph and replayed beside this library's graphed step on the same state:
+
+    * per GDN layer: the graph-safe conv update and the fused gates (runtime/model/inference_kernels.py:
+      358, :683), fla 0.5.1's fused_recurrent_gated_delta_rule (its native GQA indexing, no repeat of
+      q/k; a new final-state buffer, so the same bytes as the in-place form), and the gated RMSNorm
+      module modeling_yanchor.py:374 builds (transformers Qwen3_5RMSNormGated);
+    * per memory layer: committed_gqa then commit_decode (runtime/model/independent_memory.py:177, :190);
+    * greedy argmax (inference_kernels.py:83) and the decode loop's bookkeeping (:1206).
+
+    Both graphs replay over the steady-state memory of `fill_and_stagger`."""
+    spec = importlib.util.spec_from_file_location(
+        'reference_inference_kernels', os.path.join(REF_ROOT, 'runtime', 'model', 'inference_kernels.py'))
+    ik = importlib.util.module_from_spec(spec)
+    sys.modules[spec.name] = ik            # its dataclasses look their module up by name
+    spec.loader.exec_module(ik)
+    from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5RMSNormGated
+    stream = torch.cuda.current_stream(dev)
+    layers, mems, inputs, active, ws, table = build_decode(torch, yb, B, dev, n_inputs=1, seed=3)
+    x = inputs[0]
+    norms = []
+    for L in layers:
+        n = Qwen3_5RMSNormGated(DV, eps=1e-6).to(dev)
+        with torch.no_grad():
+            n.weight.copy_(L['norm_w'].float())
+        norms.append(n)
+    fill_and_stagger(torch, yb, layers, mems, inputs, active, ws, table)
+
+    def ref_step():
+        for i, L in enumerate(layers):
+            mix = ik.triton_graph_safe_causal_conv1d_update(x['mixed'][i].transpose(1, 2), L['conv_state'],
+                                                            L['conv_w'], None, 'silu').transpose(1, 2)
+            q = mix[..., :H_K * DK].unflatten(-1, (H_K, DK))
+            k = mix[..., H_K * DK:2 * H_K * DK].unflatten(-1, (H_K, DK))
+            v = mix[..., 2 * H_K * DK:].unflatten(-1, (H_V, DV))
+            beta, g = ik.triton_qwen35_fused_gdn_gates(x['b'][i], x['a'][i], L['A_log'], L['dt_bias'])
+            o, _ = fla_rec(q, k, v, g=g, beta=beta, initial_state=L['state'], output_final_state=True,
+                           use_qk_l2norm_in_kernel=True)
+            norms[i](o.reshape(-1, DV), x['z'][i].reshape(-1, DV))
+        for i, m in enumerate(mems):
+            ref_mem.committed_gqa(x['mq'][i], m, None)
+            ref_mem.commit_decode(x['mk'][i], x['mv'][i], x['ms'][i], active, MEM_CHUNK, m, None)
+        tok = x['logits'].argmax(dim=-1, keepdim=True)
+        ik._update_fixed_decode_state_(tok, *(table[f] for f in TABLE_FIELDS), maximum_new_tokens=GEN_TOKENS,
+                                       pad_token_id=PAD_ID, eos_token_ids=EOS_IDS)
+
+    def graph_of(fn):
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(stream)
+        with torch.cuda.stream(s), torch.no_grad():
+            fn()                                   # compiles the Triton kernels, then a pre-capture run
+            fn()
+        stream.wait_stream(s)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g), torch.no_grad():
+            fn()
+        return g
+
+    g_ref = graph_of(ref_step)
+    g_ours = graph_of(lambda: decode_step(yb, layers, mems, x, active, ws, table))
+    res = {}
+    for name, g in (('reference_gpu_decode_step_ms', g_ref), ('yanchor_b200_decode_step_ms', g_ours)):
+        g.replay()
+        res[name] = round(time_events(torch, g.replay, reps, stream), 4)
+    res['reference_gpu_decode_step_tok_s'] = round(B / res['reference_gpu_decode_step_ms'] * 1e3, 1)
+    res['yanchor_b200_decode_step_tok_s'] = round(B / res['yanchor_b200_decode_step_ms'] * 1e3, 1)
+    del g_ref, g_ours
+    return res
+
+
 def run_comparators(args):
     """Context only (not the reference arm): the GPU kernels the reference itself uses for this path,
     timed on the same B200 at the bench's shapes with CUDA events, beside this library's kernels.
@@ -1178,7 +1251,8 @@ def run_comparators(args):
       B=64, as modeling_yanchor.py:397-406 binds them;
     * the reference's Triton anchor-memory kernels from its install (runtime/model/independent_memory.py:
       committed_gqa then commit_decode, 8 layers at B=64 with full banks and staggered pending counts;
-      indexed_gqa, the anchor prefill read, at config 1).
+      indexed_gqa, the anchor prefill read, at config 1);
+    * the whole B=64 decode step composed from those kernels (`reference_gpu_decode_step`), graphed.
     Each runs once to compile, then is timed; a failure is reported, not raised."""
     import torch
     import yanchor_b200 as yb
@@ -1251,7 +1325,6 @@ def run_comparators(args):
             # the reference's module (it imports modeling_yanchor from the install root); loaded under
             # its own name so that this package's drop-in module of the same name is not picked up
             sys.path[:0] = [REF_ROOT, os.path.join(REF_ROOT, 'runtime')]
-            import importlib.util
             spec = importlib.util.spec_from_file_location(
                 'reference_independent_memory', os.path.join(REF_ROOT, 'runtime', 'model', 'independent_memory.py'))
             ref_mem = importlib.util.module_from_spec(spec)
@@ -1266,9 +1339,17 @@ def run_comparators(args):
             timed('reference_triton_memory_8_layers_ms', ref_layers, iters=20)
         except Exception as e:  # noqa: BLE001
             out['reference_triton_memory_8_layers_ms'] = f'failed: {type(e).__name__}: {str(e)[:200]}'
+            ref_mem = None
+        del mems, iq, ik, irefs
+        if ref_mem is not None and fla_rec is not None:
+            try:
+                out.update(reference_gpu_decode_step(torch, yb, dev, ref_mem, fla_rec))
+            except Exception as e:  # noqa: BLE001
+                out['reference_gpu_decode_step_ms'] = f'failed: {type(e).__name__}: {str(e)[:200]}'
     else:
         out['reference_triton'] = 'not installed'
-    print(json.dumps({'comparators': out, 'how': 'CUDA events, eager launches (no CUDA graph) for every entry, '
+    print(json.dumps({'comparators': out, 'how': 'CUDA events; eager launches (no CUDA graph) for every entry but '
+                      'the two *_decode_step entries, which replay one CUDA graph of the whole step each, '
                       'same inputs per pair'}), flush=True)
 
 
