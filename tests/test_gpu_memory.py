@@ -139,6 +139,40 @@ def test_memory_decode_step_matches_read_then_commit(yb, R, D, pool):
     assert yb.lib().yb_device_error(1) == 0
 
 
+@pytest.mark.parametrize('CAP,chunk', [(64, 64), (40, 24), (64, 96)])
+def test_memory_decode_step_nan_scores_match_oracle(yb, CAP, chunk):
+    """Merges with NaN admission scores among tied ones: NaN ranks ahead of
+    every number and NaNs tie with each other (torch's descending sort),
+    then position, then candidate index.  The one-launch step (which ranks
+    the candidates during its read when they are at most one per thread:
+    64 + 64 and 40 + 24 here, 64 + 96 after the read) against the read and
+    commit launches and the oracle, every state field bit for bit."""
+    rng = np.random.default_rng(7 * CAP + chunk)
+    B, G, H, D = 4, 4, 16, 256
+    bf = torch.bfloat16
+    st_a = yb.MemoryState.empty(B, G, CAP, chunk, D, 'cuda', bf)
+    st_b = yb.MemoryState.empty(B, G, CAP, chunk, D, 'cuda', bf)
+    st_np = omem.empty_state(B, G, CAP, chunk, D)
+    for t in range(2 * chunk + 5):
+        q = cuda(rng.standard_normal((B, 1, H, D)), bf)
+        k = cuda(rng.standard_normal((B, 1, G, D)), bf)
+        v = cuda(rng.standard_normal((B, 1, G, D)), bf)
+        sc = np.round(rng.standard_normal((B, 1, G)) * 2).astype(np.float32) / 2
+        sc[rng.random((B, 1, G)) < 0.1] = np.nan
+        act = rng.random(B) > 0.1
+        out_a = yb.memory_decode_step(q, k, v, cuda(sc), cuda(act), chunk, st_a)
+        out_b = yb.committed_gqa(q, st_b)
+        yb.commit_decode(k, v, cuda(sc), cuda(act), chunk, st_b)
+        omem.commit_decode(host(k), host(v), sc, act, chunk, st_np)
+        assert torch.equal(out_a, out_b), f'read @ {t}'
+    for f in FIELDS:
+        a, b = host(getattr(st_a, f)), host(getattr(st_b, f))
+        np.testing.assert_array_equal(a, b, err_msg=f)
+        np.testing.assert_array_equal(a, st_np[f].astype(a.dtype), err_msg=f)
+    assert np.isnan(host(st_a.scores)).any()   # NaN entries made it into the banks
+    assert yb.lib().yb_device_error(1) == 0
+
+
 def test_indexed_read_golden(yb, golden):
     d = golden('memory')
     out = yb.indexed_gqa(cuda(d['idx_q']), cuda(d['idx_k']), cuda(d['idx_v']), cuda(d['idx_refs']))

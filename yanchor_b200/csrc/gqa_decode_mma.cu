@@ -63,18 +63,32 @@ __device__ __forceinline__ void cp16(void *dst, const void *src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
 }
 
-// The commit of group g after its read, in the read's CTA.  Push (key, value, score) into pending
-// slot `count`; when the chunk fills, rank the CAP bank slots and the `chunk` pending slots (score
-// descending, position ascending with empty slots last, then candidate index: the stable double
-// argsort of select_topk, modeling_yanchor.py:51-55) and write the new bank.  The old bank's key and
-// value rows are still in shared memory from the read (rows of ROW elements in sk / sv): a new slot won
-// by an old row is one bulk copy from there to the bank; the slots won by pending rows are copied by
-// the threads, all their loads in flight together.
-// Candidate arrays live over the query / P rows (`cand`, free once the read's MMAs are done).
-// What the commit needs that does not depend on the read, loaded by every thread at the start of the
-// kernel so that its memory latency hides behind the read: the row's flags and counters, this thread's
-// piece of the new key / value row and, when the chunk fills, this thread's merge candidate (the
-// pending rows are prefetched into L2 for the bank write).
+// Named barriers of the memory step's CTA (barrier 0 is __syncthreads): the read warps (0-3) sync
+// among themselves on 1, the commit warps (4-7) on 2, and the read warps arrive on 3 once the K / V
+// rows have landed, where the commit warps wait for them.
+constexpr int kBarRead = 1, kBarCommit = 2, kBarLanded = 3;
+__device__ __forceinline__ void named_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+__device__ __forceinline__ void named_arrive(int id, int n) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+// The commit of group g, run by four warps of the read's CTA beside the read (the memory step:
+// committed_gqa then commit_decode in one launch).  Push (key, value, score) into pending slot
+// `count`; when the chunk fills, rank the CAP bank slots and the `chunk` pending slots (score
+// descending with NaN first, position ascending with empty slots last, then candidate index: the
+// stable double argsort of select_topk, modeling_yanchor.py:51-55) and write the new bank.
+//
+// The rank needs nothing from the read, so it runs while the read computes: each candidate's
+// (score, key) sits in the 16 spare bytes at the end of a K row (candidates 0..63) or V row
+// (64..127), which no load, MMA or copy touches.  The bank is rewritten once the read's K / V rows
+// have landed (so the read still sees the bank from before the commit): a new slot won by an old row
+// is one bulk copy from the row the read holds in shared memory, the slots won by pending rows are
+// copied by the threads, all their loads in flight together.  The read warps only read those rows,
+// and read the positions they mask with before they arrive, so nothing the read uses is written
+// under it.  The last of the row's G CTAs to finish updates count / total, which all of them read
+// first; its arrival counter goes back to 0 for the next call.
 struct CommitPrefetch {
   bool active;
   int64_t count, total;
@@ -84,47 +98,99 @@ struct CommitPrefetch {
   int64_t cand_key;
 };
 
+// What the commit reads before it can do anything else (thread `t` of `nt` commit threads): the
+// row's flags and counters, this thread's piece of the new key / value row and, when the chunk
+// fills, this thread's merge candidate (the pending rows are prefetched into L2 for the bank write).
 template <typename T, int D>
-__device__ CommitPrefetch commit_prefetch(const MemCommitArgs &a, int64_t row, int64_t s, int g) {
-  const int tid = threadIdx.x, nt = blockDim.x;
+__device__ CommitPrefetch commit_prefetch(const MemCommitArgs &a, int64_t row, int64_t s, int g, int t, int nt) {
   constexpr int VEC = 16 / int(sizeof(T));
   constexpr int DV = D / VEC;
   CommitPrefetch f{};
+  // every load in one round trip: the merge candidate is loaded before it is known whether the
+  // chunk fills (a few bytes per thread, every address valid for a stored row)
+  const int CAP = int(a.CAP);
   f.active = a.active[row] != 0;
-  if (!f.active) return f;
   f.count = a.count[s * a.count_s0];
   f.total = a.total[s * a.count_s0];
   f.new_score = a.scores[row * a.G + g];
-  if (tid < DV) {
-    f.kpiece = *reinterpret_cast<const uint4 *>(static_cast<const T *>(a.key) + (row * a.G + g) * D + tid * VEC);
-    f.vpiece = *reinterpret_cast<const uint4 *>(static_cast<const T *>(a.value) + (row * a.G + g) * D + tid * VEC);
+  if (t < DV) {
+    f.kpiece = *reinterpret_cast<const uint4 *>(static_cast<const T *>(a.key) + (row * a.G + g) * D + t * VEC);
+    f.vpiece = *reinterpret_cast<const uint4 *>(static_cast<const T *>(a.value) + (row * a.G + g) * D + t * VEC);
   }
-  if (f.count + 1 != a.chunk) return f;
-  const int CAP = int(a.CAP);
-  if (tid < CAP) {
-    const int32_t pos = a.positions[s * a.meta_s0 + int64_t(g) * CAP + tid];
-    f.cand_score = a.bank_scores[s * a.meta_s0 + int64_t(g) * CAP + tid];
-    f.cand_key = pos < 0 ? INT64_MAX : int64_t(pos);
-  } else if (tid < CAP + a.chunk) {
-    const int i = tid - CAP;
-    f.cand_score = i == f.count ? f.new_score : a.pscores[s * a.pmeta_s0 + int64_t(g) * a.PC + i];
+  int32_t bpos = -1;
+  float sc = 0.f;
+  if (t < CAP) {
+    bpos = a.positions[s * a.meta_s0 + int64_t(g) * CAP + t];
+    sc = a.bank_scores[s * a.meta_s0 + int64_t(g) * CAP + t];
+  } else if (t < CAP + a.chunk) {
+    sc = a.pscores[s * a.pmeta_s0 + int64_t(g) * a.PC + (t - CAP)];
+  }
+  if (!f.active || f.count + 1 != a.chunk) return f;
+  if (t < CAP) {
+    f.cand_score = sc;
+    f.cand_key = bpos < 0 ? INT64_MAX : int64_t(bpos);
+  } else if (t < CAP + a.chunk) {
+    const int i = t - CAP;
+    f.cand_score = i == f.count ? f.new_score : sc;
     f.cand_key = f.total - f.count + i;
   }
   const char *pk = reinterpret_cast<const char *>(static_cast<const T *>(a.pkeys) + s * a.pkv_s0 + int64_t(g) * a.PC * D);
   const char *pv = reinterpret_cast<const char *>(static_cast<const T *>(a.pvalues) + s * a.pkv_s0 + int64_t(g) * a.PC * D);
-  for (int64_t off = int64_t(tid) * 128; off < a.chunk * D * int64_t(sizeof(T)); off += int64_t(nt) * 128) {
+  for (int64_t off = int64_t(t) * 128; off < a.chunk * D * int64_t(sizeof(T)); off += int64_t(nt) * 128) {
     prefetch_l2(pk + off);
     prefetch_l2(pv + off);
   }
   return f;
 }
 
+// candidate c's (score, key): the spare bytes of K row c or V row c - 64
 template <typename T, int D, int ROW>
-__device__ void commit_after_read(const MemCommitArgs &a, int64_t row, int64_t s, int g, const CommitPrefetch &f,
-                                  const T *sk, const T *sv, unsigned char *cand) {
-  const int tid = threadIdx.x, nt = blockDim.x;
+__device__ __forceinline__ unsigned char *cand_pad(const T *sk, const T *sv, int c) {
+  return reinterpret_cast<unsigned char *>(const_cast<T *>((c < kGqaSlice ? sk + c * ROW : sv + (c - kGqaSlice) * ROW) + D));
+}
+
+// Shared memory of the commit warps beyond the rows: the candidates' order keys (padded to a
+// multiple of 32), sel (the candidate of each new slot), plist (the new slots won by pending rows, in
+// slot order) and their count.
+constexpr int kCommitBytes = 2 * kGqaSlice * 8 + (2 * kGqaSlice + 4) * 4;
+
+// One 64-bit key per candidate whose unsigned order is the merge order, up to the candidate index:
+// the score (NaN first, then descending, -0.0 with 0.0) above the position (empty slots last).  Exact
+// for positions below 2^32 - 1; `ok` is false otherwise, and the CTA then ranks by cand_before.
+__device__ __forceinline__ uint64_t order_key(float sc, int64_t pk, bool &ok) {
+  uint32_t ks = 0u;                                             // NaN
+  if (sc == sc) {
+    const uint32_t bits = __float_as_uint(sc == 0.f ? 0.f : sc);
+    ks = ~((bits & 0x80000000u) ? ~bits : (bits | 0x80000000u));   // larger score, smaller key; never 0
+  }
+  ok = pk == INT64_MAX || (pk >= 0 && pk < 0xFFFFFFFFll);
+  return (uint64_t(ks) << 32) | (pk == INT64_MAX ? 0xFFFFFFFFull : uint64_t(uint32_t(pk)));
+}
+__device__ __forceinline__ bool commit_red_and(bool p) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\tbar.red.and.pred po, %2, %3, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(r)
+      : "r"(uint32_t(p)), "r"(kBarCommit), "r"(kGqaThreads)
+      : "memory");
+  return r != 0;
+}
+
+// Every path through here reaches the landed barrier exactly once (the read warps arrive on it
+// exactly once) and the commit warps' own barriers the same number of times in every thread.
+template <typename T, int D, int ROW>
+__device__ void commit_group(const MemCommitTail &ct, int64_t row, int64_t s, int g, const T *sk, const T *sv,
+                             int *cm, int t) {
+  constexpr int NT = kGqaThreads;
+  const MemCommitArgs &a = ct.c;
+  const CommitPrefetch f = commit_prefetch<T, D>(a, row, s, g, t, NT);
+  if (!f.active) {   // the same for the row's G CTAs: no push, no arrival
+    named_sync(kBarLanded, 2 * NT);
+    return;
+  }
   const int64_t count = f.count, total = f.total;
-  const int CAP = int(a.CAP), chunk = int(a.chunk), G = int(a.G), PC = int(a.PC);
+  const int CAP = int(a.CAP), chunk = int(a.chunk), PC = int(a.PC);
   T *bank_k = static_cast<T *>(a.keys) + s * a.kv_s0 + int64_t(g) * CAP * D;
   T *bank_v = static_cast<T *>(a.values) + s * a.kv_s0 + int64_t(g) * CAP * D;
   T *pend_k = static_cast<T *>(a.pkeys) + s * a.pkv_s0 + int64_t(g) * PC * D;
@@ -134,117 +200,171 @@ __device__ void commit_after_read(const MemCommitArgs &a, int64_t row, int64_t s
   float *pscore = a.pscores + s * a.pmeta_s0 + int64_t(g) * PC;
   constexpr int VEC = 16 / int(sizeof(T));
   constexpr int DV = D / VEC;
-  // push (16-byte pieces, loaded at the start: row starts are 16-byte aligned)
-  if (tid < DV) {
-    *reinterpret_cast<uint4 *>(pend_k + count * D + tid * VEC) = f.kpiece;
-    *reinterpret_cast<uint4 *>(pend_v + count * D + tid * VEC) = f.vpiece;
+  // push (16-byte pieces: row starts are 16-byte aligned); the read does not look at pending rows
+  if (t < DV) {
+    *reinterpret_cast<uint4 *>(pend_k + count * D + t * VEC) = f.kpiece;
+    *reinterpret_cast<uint4 *>(pend_v + count * D + t * VEC) = f.vpiece;
   }
-  const float new_score = f.new_score;
-  if (tid == 0) pscore[count] = new_score;
-  if (count + 1 != chunk) return;
-  const int n = CAP + chunk;
-  float *c_score = reinterpret_cast<float *>(cand);
-  int64_t *c_pkey = reinterpret_cast<int64_t *>(cand + ((4 * n + 15) & ~15));
-  int *sel = reinterpret_cast<int *>(reinterpret_cast<unsigned char *>(c_pkey) + 8 * n);
-  if (tid < n) {   // this thread's candidate, loaded at the start
-    c_score[tid] = f.cand_score;
-    c_pkey[tid] = f.cand_key;
-  }
-  for (int c = nt + tid; c < n; c += nt) {   // any beyond one per thread
-    if (c < CAP) {
-      const int32_t pos = bpos[c];
-      c_score[c] = bscore[c];
-      c_pkey[c] = pos < 0 ? INT64_MAX : int64_t(pos);
-    } else {
-      const int i = c - CAP;   // every pending slot is filled when the chunk commits; slot `count` is new
-      c_score[c] = i == count ? new_score : pscore[i];
-      c_pkey[c] = total - count + i;
-    }
-  }
-  __syncthreads();
-  for (int c = tid; c < n; c += nt) {
-    const float sc = c_score[c];
-    const int64_t pkc = c_pkey[c];
-    int r0 = 0, r1 = 0;
-    int o = 0;
-#pragma unroll 4
-    for (; o + 1 < n; o += 2) {
-      r0 += memcommit::cand_before(c_score[o], c_pkey[o], o, sc, pkc, c);
-      r1 += memcommit::cand_before(c_score[o + 1], c_pkey[o + 1], o + 1, sc, pkc, c);
-    }
-    if (o < n) r0 += memcommit::cand_before(c_score[o], c_pkey[o], o, sc, pkc, c);
-    if (r0 + r1 < CAP) sel[r0 + r1] = c;
-  }
-  __syncthreads();   // sel complete
-  // the new slots whose winner is a pending row, in slot order (warp 0; CAP <= 64)
-  int *plist = sel + CAP;
-  int *npend = plist + CAP;
-  if (tid < 32) {
-    int base = 0;
-    for (int r0 = 0; r0 < CAP; r0 += 32) {
-      const int r = r0 + tid;
-      bool from_pend = false;
-      if (r < CAP) {
-        const int c = sel[r];
-        from_pend = c_pkey[c] != INT64_MAX && c >= CAP;
-      }
-      const unsigned m = __ballot_sync(0xffffffffu, from_pend);
-      if (from_pend) plist[base + __popc(m & ((1u << tid) - 1u))] = r;
-      base += __popc(m);
-    }
-    if (tid == 0) *npend = base;
-  }
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the old bank rows are read below by bulk copies
-  __syncthreads();      // sel, plist complete; every thread's push is visible to the pending loads below
-  // (1) slots won by an old bank row (an empty winner copies old bank slot 0, as the reference): one
-  //     bulk copy per row straight from the shared-memory row the read used
-  if (tid < 2 * CAP) {
-    const int r = tid % CAP, half = tid / CAP;
-    const int c = sel[r];
-    const int src = c_pkey[c] == INT64_MAX ? 0 : c;
-    if (src < CAP) {
-      T *dst = (half ? bank_v : bank_k) + r * D;
-      const T *from = (half ? sv : sk) + src * ROW;
-      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
-                   "r"(static_cast<uint32_t>(__cvta_generic_to_shared(from))), "r"(uint32_t(D * sizeof(T)))
-                   : "memory");
-      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-    }
-  }
-  // (2) slots won by a pending row: each thread loads all its pieces (key and value rows together)
-  //     before it stores them
-  const int np = *npend;
+  if (t == 0) pscore[count] = f.new_score;
+  const bool merge = count + 1 == chunk;   // the same for the whole CTA
+  const int n = CAP + chunk;                // at most 2 * kGqaSlice = NT (checked on the host)
+  uint64_t *okey = reinterpret_cast<uint64_t *>(cm);
+  int *sel = reinterpret_cast<int *>(okey + 2 * kGqaSlice), *plist = sel + kGqaSlice, *npend = plist + kGqaSlice;
   constexpr int PER = 8;
-  for (int base = 0; base < np * 2 * DV; base += nt * PER) {
-    uint4 buf[PER];
+  uint4 buf[PER];
+  int np = 0;
+  if (merge) {
+    bool key_ok = true;
+    const int n32 = (n + 31) & ~31;
+    if (t < n) {
+      unsigned char *pd = cand_pad<T, D, ROW>(sk, sv, t);
+      *reinterpret_cast<float *>(pd) = f.cand_score;
+      *reinterpret_cast<int64_t *>(pd + 8) = f.cand_key;
+      okey[t] = order_key(f.cand_score, f.cand_key, key_ok);
+    } else if (t < n32) {
+      okey[t] = ~0ull;   // padding: after every candidate
+    }
+    key_ok = commit_red_and(key_ok);   // also the barrier after the keys
+    if (key_ok && t < n) {
+      // rank = keys below this one + equal keys at a lower index; blocks of 32 candidates below (above)
+      // this warp's own compare with key + 1 (key), the warp's own block candidate by candidate
+      const uint64_t kc = okey[t], kc1 = kc + 1;   // no overflow: the score part is at most 0xFF800000
+      const int w = t >> 5;
+      int r0 = 0, r1 = 0;
+      for (int jb = 0; jb < n32 / 32; ++jb) {
+        const ulonglong2 *kp = reinterpret_cast<const ulonglong2 *>(okey + jb * 32);
+        if (jb != w) {
+          const uint64_t lim = jb < w ? kc1 : kc;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const ulonglong2 k2 = kp[i];
+            r0 += k2.x < lim;
+            r1 += k2.y < lim;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const ulonglong2 k2 = kp[i];
+            const int o = jb * 32 + 2 * i;
+            r0 += k2.x < (o < t ? kc1 : kc);
+            r1 += k2.y < (o + 1 < t ? kc1 : kc);
+          }
+        }
+      }
+      if (r0 + r1 < CAP) sel[r0 + r1] = t;   // the order is strict and total: the ranks are a permutation
+    } else if (t < n) {
+      const float sc = f.cand_score;
+      const int64_t pk = f.cand_key;
+      int r0 = 0, r1 = 0, o = 0;
+#pragma unroll 4
+      for (; o + 1 < n; o += 2) {
+        const unsigned char *q0 = cand_pad<T, D, ROW>(sk, sv, o), *q1 = cand_pad<T, D, ROW>(sk, sv, o + 1);
+        r0 += memcommit::cand_before(*reinterpret_cast<const float *>(q0), *reinterpret_cast<const int64_t *>(q0 + 8),
+                                     o, sc, pk, t);
+        r1 += memcommit::cand_before(*reinterpret_cast<const float *>(q1), *reinterpret_cast<const int64_t *>(q1 + 8),
+                                     o + 1, sc, pk, t);
+      }
+      if (o < n) {
+        const unsigned char *q0 = cand_pad<T, D, ROW>(sk, sv, o);
+        r0 += memcommit::cand_before(*reinterpret_cast<const float *>(q0), *reinterpret_cast<const int64_t *>(q0 + 8),
+                                     o, sc, pk, t);
+      }
+      if (r0 + r1 < CAP) sel[r0 + r1] = t;
+    }
+    named_sync(kBarCommit, NT);   // sel complete
+    // the new slots whose winner is a pending row, in slot order (first commit warp; CAP <= 64)
+    if (t < 32) {
+      int base = 0;
+      for (int r0 = 0; r0 < CAP; r0 += 32) {
+        const int r = r0 + t;
+        bool from_pend = false;
+        if (r < CAP) {
+          const int c = sel[r];
+          from_pend = c >= CAP;   // pending candidates are never empty
+        }
+        const unsigned m = __ballot_sync(0xffffffffu, from_pend);
+        if (from_pend) plist[base + __popc(m & ((1u << t) - 1u))] = r;
+        base += __popc(m);
+      }
+      if (t == 0) *npend = base;
+    }
+    named_sync(kBarCommit, NT);   // plist complete
+    np = *npend;
+    // the first round of pending-row loads (they read pending rows only, which the read never touches)
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
-      const int e = base + tid + i * nt;
+      const int e = t + i * NT;
       if (e < np * 2 * DV) {
         const int r = plist[e / (2 * DV)], rem = e % (2 * DV), half = rem / DV, d = (rem % DV) * VEC;
         buf[i] = *reinterpret_cast<const uint4 *>((half ? pend_v : pend_k) + (sel[r] - CAP) * D + d);
       }
     }
-#pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      const int e = base + tid + i * nt;
-      if (e < np * 2 * DV) {
-        const int r = plist[e / (2 * DV)], rem = e % (2 * DV), half = rem / DV, d = (rem % DV) * VEC;
-        *reinterpret_cast<uint4 *>((half ? bank_v : bank_k) + r * D + d) = buf[i];
+  }
+  // the read's K / V rows have landed (its warps arrive here after their last row wait and a proxy
+  // fence): the bank may be overwritten, and the rows in shared memory are final
+  named_sync(kBarLanded, 2 * NT);
+  if (merge) {
+    // (1) slots won by an old bank row (an empty winner copies old bank slot 0, as the reference):
+    //     one bulk copy per row straight from the shared-memory row the read holds
+    if (t < 2 * CAP) {
+      const int r = t % CAP, half = t / CAP;
+      const int c = sel[r];
+      const int src = *reinterpret_cast<const int64_t *>(cand_pad<T, D, ROW>(sk, sv, c) + 8) == INT64_MAX ? 0 : c;
+      if (src < CAP) {
+        T *dst = (half ? bank_v : bank_k) + r * D;
+        const T *from = (half ? sv : sk) + src * ROW;
+        asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+                     "r"(static_cast<uint32_t>(__cvta_generic_to_shared(from))), "r"(uint32_t(D * sizeof(T)))
+                     : "memory");
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
       }
     }
+    // (2) slots won by a pending row: each thread loads all its pieces of a round (key and value rows
+    //     together) before it stores them; the first round's loads were issued before the wait
+    for (int base = 0; base < np * 2 * DV; base += NT * PER) {
+      if (base > 0) {
+#pragma unroll
+        for (int i = 0; i < PER; ++i) {
+          const int e = base + t + i * NT;
+          if (e < np * 2 * DV) {
+            const int r = plist[e / (2 * DV)], rem = e % (2 * DV), half = rem / DV, d = (rem % DV) * VEC;
+            buf[i] = *reinterpret_cast<const uint4 *>((half ? pend_v : pend_k) + (sel[r] - CAP) * D + d);
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int e = base + t + i * NT;
+        if (e < np * 2 * DV) {
+          const int r = plist[e / (2 * DV)], rem = e % (2 * DV), half = rem / DV, d = (rem % DV) * VEC;
+          *reinterpret_cast<uint4 *>((half ? bank_v : bank_k) + r * D + d) = buf[i];
+        }
+      }
+    }
+    for (int r = t; r < CAP; r += NT) {
+      const int c = sel[r];
+      const unsigned char *pd = cand_pad<T, D, ROW>(sk, sv, c);
+      const int64_t key = *reinterpret_cast<const int64_t *>(pd + 8);
+      bscore[r] = *reinterpret_cast<const float *>(pd);
+      bpos[r] = key == INT64_MAX ? -1 : int32_t(key);
+    }
+    // the bulk copies have read their rows and written the bank before the CTA goes on or exits
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   }
-  for (int r = tid; r < CAP; r += nt) {
-    const int c = sel[r];
-    bscore[r] = c_score[c];
-    bpos[r] = c_pkey[c] == INT64_MAX ? -1 : int32_t(c_pkey[c]);
+  named_sync(kBarCommit, NT);   // every commit store of this CTA is issued
+  if (t == 0) {
+    __threadfence();
+    if (atomicAdd(ct.arrive + row, 1) == int(a.G) - 1) {
+      ct.arrive[row] = 0;
+      a.count[s * a.count_s0] = merge ? 0 : count + 1;
+      a.total[s * a.count_s0] = total + 1;
+    }
   }
-  // the bulk copies have read their rows and written the bank before the CTA goes on or exits
-  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 template <typename T, int R, int D, bool COMMIT>
-__global__ void __launch_bounds__(kGqaThreads) gqa_decode_mma_kernel(const GqaDecodeArgs a, const MemCommitTail ct) {
+__global__ void __launch_bounds__(COMMIT ? 2 * kGqaThreads : kGqaThreads, 3)
+    gqa_decode_mma_kernel(const GqaDecodeArgs a, const MemCommitTail ct) {
   static_assert(R <= 8 && D % 64 == 0, "R <= 8 heads, D a multiple of 64");
   constexpr int ROW = D + 8;          // padded K / V / Q row (elements)
   constexpr int PROW = kGqaSlice + 8; // padded P row
@@ -255,11 +375,12 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_decode_mma_kernel(const GqaDe
   T *sp = sq + 8 * ROW;                                   // [2][8][PROW]  P hi, P lo
   float *red = reinterpret_cast<float *>(sp + 2 * 8 * PROW);   // [4 warps][8] max, then [4][8] sums
   float *fin = red + 2 * 4 * 8;                                // [8] max, [8] 1 / denominator
+  int *cm = reinterpret_cast<int *>(fin + 16);                 // the commit warps' arrays (memory step)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g8 = lane >> 2, t4 = lane & 3;
   const int64_t unit = blockIdx.x;                        // (row, group)
   const int64_t slice = blockIdx.y, p0 = slice * kGqaSlice;
   const int64_t b = unit / a.G, g = unit % a.G;
-  if (!a.indices) {   // the slice's rows are known before the wait: warm L2 with them
+  if (!a.indices && tid < kGqaThreads) {   // the slice's rows are known before the wait: warm L2 with them
     const char *k0 = reinterpret_cast<const char *>(static_cast<const T *>(a.keys) + b * a.kv_bs + g * a.kv_gs + p0 * D);
     const char *v0 = reinterpret_cast<const char *>(static_cast<const T *>(a.values) + b * a.kv_bs + g * a.kv_gs + p0 * D);
     const int64_t nb = (a.P - p0 < kGqaSlice ? a.P - p0 : kGqaSlice) * D * int64_t(sizeof(T));
@@ -275,11 +396,17 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_decode_mma_kernel(const GqaDe
   const int np = int(a.P - p0 < kGqaSlice ? a.P - p0 : kGqaSlice);
   if (s < 0) {   // skipped request (memory read): zero output
     T *o = static_cast<T *>(a.out) + (b * a.QH + g * R) * D;
-    for (int e = tid; e < R * D; e += kGqaThreads) o[e] = from_f<T>(0.f);
+    if (tid < kGqaThreads)
+      for (int e = tid; e < R * D; e += kGqaThreads) o[e] = from_f<T>(0.f);
     return;
   }
-  CommitPrefetch pre{};
-  if constexpr (COMMIT) pre = commit_prefetch<T, D>(ct.c, b, s, int(g));
+  if constexpr (COMMIT) {
+    if (tid >= kGqaThreads) {   // warps 4-7: this group's commit, beside the read
+      commit_group<T, D, ROW>(ct, b, s, int(g), sk, sv, cm, tid - kGqaThreads);
+      return;
+    }
+  }
+  // warps 0-3: the read
   const T *kb = static_cast<const T *>(a.keys) + s * a.kv_bs + g * a.kv_gs + p0 * D;
   const T *vb = static_cast<const T *>(a.values) + s * a.kv_bs + g * a.kv_gs + p0 * D;
   constexpr int PIECES = D / 8;
@@ -299,7 +426,7 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_decode_mma_kernel(const GqaDe
         h < R ? *reinterpret_cast<const uint4 *>(qg + h * D + c) : make_uint4(0, 0, 0, 0);
   }
   asm volatile("cp.async.wait_group 1;" ::: "memory");
-  __syncthreads();
+  named_sync(kBarRead, kGqaThreads);
 
   // ---- S^T (16 positions x 8 heads per warp) ----
   float sc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -338,13 +465,13 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_decode_mma_kernel(const GqaDe
     red[warp * 8 + 2 * t4] = m2[0];
     red[warp * 8 + 2 * t4 + 1] = m2[1];
   }
-  __syncthreads();
+  named_sync(kBarRead, kGqaThreads);
   if (tid < 8) {
     float m = fmaxf(fmaxf(red[tid], red[8 + tid]), fmaxf(red[16 + tid], red[24 + tid]));
     if (a.null_slot) m = fmaxf(m, 0.f);
     fin[tid] = m;
   }
-  __syncthreads();
+  named_sync(kBarRead, kGqaThreads);
   // ---- P = exp(S - m) as bf16 hi + lo, and the exp-sums ----
   float l2[2] = {0.f, 0.f};
   T *phi = sp, *plo = sp + 8 * PROW;
@@ -368,13 +495,17 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_decode_mma_kernel(const GqaDe
     red[32 + warp * 8 + 2 * t4 + 1] = l2[1];
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
-  __syncthreads();
+  if constexpr (COMMIT) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the commit's bulk copies read these rows
+    named_arrive(kBarLanded, 2 * kGqaThreads);
+  }
+  named_sync(kBarRead, kGqaThreads);
   if (tid < 8) {
     float l = red[32 + tid] + red[40 + tid] + red[48 + tid] + red[56 + tid];
     if (a.null_slot) l += expf(-fin[tid]);         // the null slot: logit 0, value 0
     fin[8 + tid] = l;
   }
-  __syncthreads();
+  named_sync(kBarRead, kGqaThreads);
 
   // ---- O^T = V^T P^T: warp w owns D columns [w D/4, (w+1) D/4) ----
   constexpr int DW = D / 4, TILES = DW / 16;
@@ -425,42 +556,19 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_decode_mma_kernel(const GqaDe
           o[h * D + d] = from_f<T>(l > 0.f ? acc[t][j] / l : 0.f);
         }
       }
-    if constexpr (COMMIT) {
-      // This group's commit (push, and the merge when the chunk fills), right after its read: the
-      // group's bank is read by this CTA alone, so every read of the step still sees the bank
-      // from before the commit, as with a read launch followed by a commit launch.  The last of
-      // the row's G CTAs to finish updates count / total, which all of them read first; its
-      // arrival counter goes back to 0 for the next call.  The commit's buffers reuse the K / V
-      // rows, which every warp is done with after the first barrier.
-      const MemCommitArgs &c = ct.c;
-      if (pre.active) {   // the same for the row's G CTAs
-        const int64_t count = pre.count, total = pre.total;
-        __syncthreads();   // every warp is done with the query / P rows and the V rows
-        commit_after_read<T, D, ROW>(c, b, s, int(g), pre, sk, sv, reinterpret_cast<unsigned char *>(sq));
-        __syncthreads();
-        if (tid == 0) {
-          __threadfence();
-          if (atomicAdd(ct.arrive + b, 1) == int(a.G) - 1) {
-            ct.arrive[b] = 0;
-            c.count[s * c.count_s0] = count + 1 == c.chunk ? 0 : count + 1;
-            c.total[s * c.count_s0] = total + 1;
-          }
-        }
-      }
-    }
   }
 }
 
 template <typename T, int R, int D, bool COMMIT>
 int launch_gqa(const GqaDecodeArgs &a, const MemCommitTail &ct, unsigned slices) {
   constexpr int ROW = D + 8, PROW = kGqaSlice + 8;
-  static_assert(kGqaSlice * ROW * sizeof(T) >= (sizeof(float) + sizeof(int64_t) + sizeof(int)) * memcommit::kMaxCand,
-                "the commit's candidate arrays fit in the V rows");
-  const size_t smem = sizeof(T) * (2 * kGqaSlice * ROW + 8 * ROW + 2 * 8 * PROW) + sizeof(float) * (64 + 16);
+  const size_t smem = sizeof(T) * (2 * kGqaSlice * ROW + 8 * ROW + 2 * 8 * PROW) + sizeof(float) * (64 + 16) +
+                      (COMMIT ? kCommitBytes : 0);
   auto k = gqa_decode_mma_kernel<T, R, D, COMMIT>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "gqa decode: smem attribute: %s", cudaGetErrorString(e));
-  e = launch_pdl(k, dim3(unsigned(a.B * a.G), slices), dim3(kGqaThreads), smem, a.stream, a, ct);
+  e = launch_pdl(k, dim3(unsigned(a.B * a.G), slices), dim3(COMMIT ? 2 * kGqaThreads : kGqaThreads), smem, a.stream,
+                 a, ct);
   if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "gqa decode: %s", cudaGetErrorString(e));
   return check_launch("gqa_decode_mma_kernel");
 }
@@ -505,14 +613,12 @@ int launch_gqa_decode_mma(const GqaDecodeArgs &a) {
 }
 
 bool gqa_decode_commit_fits(const GqaDecodeArgs &a, const MemCommitArgs &c) {
-  const int64_t n = c.CAP + c.chunk;
-  const int64_t cand_bytes = ((4 * n + 15) & ~int64_t(15)) + 8 * n + 4 * c.CAP + 4 * c.CAP + 4;   // + plist, npend
-  const int64_t room = 2 * (8 * (a.D + 8) + 2 * 8 * (kGqaSlice + 8));   // the query and P rows (16-bit)
+  const int64_t n = c.CAP + c.chunk;   // one merge candidate per commit thread, in the rows' spare bytes
   const uintptr_t al = reinterpret_cast<uintptr_t>(c.key) | reinterpret_cast<uintptr_t>(c.value) |
                        reinterpret_cast<uintptr_t>(c.keys) | reinterpret_cast<uintptr_t>(c.values) |
                        reinterpret_cast<uintptr_t>(c.pkeys) | reinterpret_cast<uintptr_t>(c.pvalues);
   return !a.partial && a.P <= kGqaSlice && a.B == c.B && a.G == c.G && a.indices == c.indices &&
-         cand_bytes <= room && c.CAP == a.P && c.D == a.D && c.dtype == a.dtype && (al % 16) == 0 &&
+         n <= 2 * kGqaSlice && c.CAP == a.P && c.D == a.D && c.dtype == a.dtype && (al % 16) == 0 &&
          (c.kv_s0 % 8) == 0 && (c.pkv_s0 % 8) == 0;
 }
 

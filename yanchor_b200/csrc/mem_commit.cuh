@@ -7,8 +7,10 @@
 // chunk fills, merge the CAP bank slots and the `chunk` pending slots of each
 // group into the new top-CAP bank.  Groups are independent: commit_group does
 // one, so the read kernel's tail commits each group in its own CTA.  Order:
-// score descending, then position ascending (invalid last), then candidate
-// index — the stable double argsort of select_topk.  Invalid winners get
+// score descending with NaN first (NaNs tie with each other, as in torch's
+// descending sort), then position ascending (invalid last), then candidate
+// index — the stable double argsort of select_topk.  It is a strict total
+// order, so the ranks of the candidates are a permutation.  Invalid winners get
 // position -1 and copy bank slot 0, as the reference's gather with references
 // clamped at 0 does.  Every thread of the CTA calls these; loops stride by the
 // CTA's thread count.
@@ -22,7 +24,9 @@ namespace memcommit {
 constexpr int kMaxCand = 512;
 
 __device__ __forceinline__ bool cand_before(float sa, int64_t pa, int ia, float sb, int64_t pb, int ib) {
-  if (sa != sb) return sa > sb;  // -0.0 == 0.0, as in a float sort
+  const bool na = sa != sa, nb = sb != sb;
+  if (na != nb) return na;                 // NaN ahead of every number
+  if (!na && sa != sb) return sa > sb;     // -0.0 == 0.0, as in a float sort
   if (pa != pb) return pa < pb;
   return ia < ib;
 }
