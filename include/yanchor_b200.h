@@ -258,12 +258,14 @@ int yb_mem_decode_commit(const void *key, const void *value, const float *scores
 /*
  * Anchor memory, one decode step of a memory layer: yb_mem_decode_read, then
  * yb_mem_decode_commit on the same state, in one launch where the read takes
- * its tensor-core path (16-bit, CAP <= 64): each (row, group) CTA reads its
- * group and then commits that same group (push, and the merge when the chunk
- * fills).  Only that CTA reads the group's bank, so every read still sees the
- * bank from before this step's commit, as with the two calls in that order.
- * The last of the row's G CTAs to arrive updates count / total and sets the
- * row's arrival counter back to 0.  Otherwise it makes those two calls.
+ * its tensor-core path (16-bit, CAP <= 64, CAP + chunk <= 128): each
+ * (row, group) CTA reads its group in four warps and commits that same group
+ * (push, and the merge when the chunk fills) in four more beside them.  Only
+ * that CTA reads the group's bank, and the commit writes it only after the
+ * read holds its rows, so every read still sees the bank from before this
+ * step's commit, as with the two calls in that order.  The last of the row's
+ * G CTAs to finish its commit updates count / total and sets the row's
+ * arrival counter back to 0.  Otherwise it makes those two calls.
  * Results are identical to the two calls.
  * The sequence of runtime/model/independent_memory.py:177 `committed_gqa`
  * then :190 `commit_decode` in the reference's decode layer
