@@ -158,31 +158,71 @@ __global__ void __launch_bounds__(kSwaThreads) swa_partial_kernel(const SwaArgs 
   }
 }
 
+// The combine of one (row, KV head, query head): every slice's factor e^{m_s - M} once per CTA (a
+// slice with nothing valid is skipped), then one output feature per thread, with the slices' partial
+// sums for it loaded eight at a time before they are summed in slice order.
+constexpr int kCombineBatch = 8;
+__host__ __device__ constexpr size_t combine_smem(int slices) { return size_t(2) * slices * sizeof(float); }
+
 template <typename T>
 __global__ void swa_combine_kernel(const SwaArgs a, const float *part, int R, int slices) {
+  extern __shared__ float comb[];   // [slices] factor (-1: skip), [slices] exp-sum
+  __shared__ float wmax[8];
+  __shared__ float s_den;
   const int64_t bh = blockIdx.x, b = bh / a.KVH, kvh = bh % a.KVH;
   const int r = blockIdx.y;
-  const int D = int(a.D);
+  const int D = int(a.D), tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5;
   pdl_wait();   // the slices are written
   pdl_release();
-  const float *pb = part + bh * slices * (R * (D + 2)) + r * (D + 2);
+  const int64_t stride = int64_t(R) * (D + 2);
+  const float *pb = part + bh * slices * stride + r * (D + 2);
+  float *fac = comb, *lsum = comb + slices;
   float M = -INFINITY;
-  for (int s = 0; s < slices; ++s) M = fmaxf(M, pb[s * R * (D + 2) + D]);
+  for (int s = tid; s < slices; s += nt) {
+    const float m = pb[s * stride + D];
+    fac[s] = m;
+    lsum[s] = pb[s * stride + D + 1];
+    M = fmaxf(M, m);
+  }
+  M = warp_max(M);
+  if (lane == 0) wmax[warp] = M;
+  __syncthreads();
+  M = wmax[0];
+  for (int w = 1; w < (nt + 31) / 32; ++w) M = fmaxf(M, wmax[w]);
+  for (int s = tid; s < slices; s += nt) fac[s] = (M == -INFINITY || fac[s] == -INFINITY) ? -1.f : __expf(fac[s] - M);
+  __syncthreads();
+  if (tid == 0) {
+    float den = 0.f;
+    for (int s = 0; s < slices; ++s)
+      if (fac[s] >= 0.f) den = fmaf(lsum[s], fac[s], den);
+    s_den = den;
+  }
+  __syncthreads();
+  const float den = s_den;
   T *o = static_cast<T *>(a.out) + (b * a.QH + kvh * R + r) * D;
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    float num = 0.f, den = 0.f;
-    if (M != -INFINITY) {
-      for (int s = 0; s < slices; ++s) {
-        const float *ps = pb + s * R * (D + 2);
-        const float m = ps[D];
-        if (m == -INFINITY) continue;
-        const float f = __expf(m - M);
-        num = fmaf(ps[d], f, num);
-        den = fmaf(ps[D + 1], f, den);
-      }
+  for (int d = tid; d < D; d += nt) {
+    float num = 0.f;
+    for (int s0 = 0; s0 < slices; s0 += kCombineBatch) {
+      float x[kCombineBatch];
+#pragma unroll
+      for (int j = 0; j < kCombineBatch; ++j) x[j] = s0 + j < slices ? pb[(s0 + j) * stride + d] : 0.f;
+#pragma unroll
+      for (int j = 0; j < kCombineBatch; ++j)
+        if (s0 + j < slices && fac[s0 + j] >= 0.f) num = fmaf(x[j], fac[s0 + j], num);
     }
     o[d] = from_f<T>(den > 0.f ? num / den : 0.f);
   }
+}
+
+// the combine's dynamic shared memory beyond the default 48 KB (slices > 6144) needs the attribute
+template <typename T>
+int combine_prepare(int slices) {
+  const size_t smem = combine_smem(slices);
+  if (smem <= 48 * 1024) return YB_OK;
+  if (smem > 227 * 1024) return set_error(YB_ERR_UNSUPPORTED, "swa combine: %d slices exceed shared memory", slices);
+  const cudaError_t e = cudaFuncSetAttribute(swa_combine_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             int(smem));
+  return e == cudaSuccess ? YB_OK : set_error(YB_ERR_CUDA, "swa combine: smem attribute: %s", cudaGetErrorString(e));
 }
 
 template <typename T, int R, int D>
@@ -194,8 +234,10 @@ int attn_launch(const SwaArgs &a, float *part, int slices) {
   k<<<dim3(unsigned(a.B * a.KVH), unsigned(slices)), kSwaThreads, smem, a.stream>>>(a, part);
   int rc = check_launch("swa_partial_kernel");
   if (rc) return rc;
-  swa_combine_kernel<T><<<dim3(unsigned(a.B * a.KVH), unsigned(R)), D < 256 ? D : 256, 0, a.stream>>>(a, part, R,
-                                                                                                      slices);
+  rc = combine_prepare<T>(slices);
+  if (rc) return rc;
+  swa_combine_kernel<T><<<dim3(unsigned(a.B * a.KVH), unsigned(R)), D < 256 ? D : 256, combine_smem(slices),
+                          a.stream>>>(a, part, R, slices);
   return check_launch("swa_combine_kernel");
 }
 
@@ -277,9 +319,12 @@ int launch_swa_decode_attention(const SwaArgs &a, void *workspace) {
     if (rc) return rc;
     const int R = int(a.QH / a.KVH);
     const dim3 cgrid(unsigned(a.B * a.KVH), unsigned(R)), cblock(unsigned(a.D < 256 ? a.D : 256));
+    rc = a.dtype == YB_BF16 ? combine_prepare<__nv_bfloat16>(slices) : combine_prepare<__half>(slices);
+    if (rc) return rc;
+    const size_t csm = combine_smem(slices);
     const cudaError_t e = a.dtype == YB_BF16
-                              ? launch_pdl(swa_combine_kernel<__nv_bfloat16>, cgrid, cblock, 0, a.stream, a, part, R, slices)
-                              : launch_pdl(swa_combine_kernel<__half>, cgrid, cblock, 0, a.stream, a, part, R, slices);
+                              ? launch_pdl(swa_combine_kernel<__nv_bfloat16>, cgrid, cblock, csm, a.stream, a, part, R, slices)
+                              : launch_pdl(swa_combine_kernel<__half>, cgrid, cblock, csm, a.stream, a, part, R, slices);
     if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "swa_combine_kernel: %s", cudaGetErrorString(e));
     return check_launch("swa_combine_kernel");
   }
