@@ -107,17 +107,18 @@ def test_decode_strided_pool_view(yb):
         np.testing.assert_array_equal(host(getattr(st, f)), st_np[f].astype(host(getattr(st, f)).dtype))
 
 
-@pytest.mark.parametrize('R,D,pool', [(4, 256, False), (2, 128, True)])
-def test_memory_decode_step_matches_read_then_commit(yb, R, D, pool):
+@pytest.mark.parametrize('R,D,pool,dt', [(4, 256, False, torch.bfloat16), (2, 128, True, torch.bfloat16),
+                                         (8, 64, False, torch.float16), (1, 256, True, torch.float16)])
+def test_memory_decode_step_matches_read_then_commit(yb, R, D, pool, dt):
     """The one-launch decode step of a memory layer against committed_gqa
     then commit_decode on a copy of the same state, bit for bit, over 170
     steps (two commits at chunk 64 for rows active in 128 of them, the second
     merging a full bank with a full chunk): tied scores, inactive rows, and (pool)
     requests mapped into a larger slot pool with one skipped request."""
-    rng = np.random.default_rng(90 + D)
+    rng = np.random.default_rng(90 + D + R)
     B, G, CAP, chunk = 6, 4, 64, 64
     H = G * R
-    bf = torch.bfloat16
+    bf = dt
     rows = 9 if pool else B
     idx = cuda(np.array([3, 0, -1, 8, 5, 1], np.int64)) if pool else None
     st_a = yb.MemoryState.empty(rows, G, CAP, chunk, D, 'cuda', bf)
@@ -143,10 +144,11 @@ def test_memory_decode_step_matches_read_then_commit(yb, R, D, pool):
 def test_memory_decode_step_nan_scores_match_oracle(yb, CAP, chunk):
     """Merges with NaN admission scores among tied ones: NaN ranks ahead of
     every number and NaNs tie with each other (torch's descending sort),
-    then position, then candidate index.  The one-launch step (which ranks
-    the candidates during its read when they are at most one per thread:
-    64 + 64 and 40 + 24 here, 64 + 96 after the read) against the read and
-    commit launches and the oracle, every state field bit for bit."""
+    then position, then candidate index.  The one-launch step (its commit
+    warps rank one candidate each: 64 + 64 and 40 + 24 here; 64 + 96 has
+    more candidates than commit threads and takes the two launches) against
+    the read and commit launches and the oracle, every state field bit for
+    bit."""
     rng = np.random.default_rng(7 * CAP + chunk)
     B, G, H, D = 4, 4, 16, 256
     bf = torch.bfloat16
