@@ -1,12 +1,13 @@
-// Anchor-memory decode commit of one request row, shared by the commit kernel
-// (memory.cu) and the read kernel's commit tail (gqa_decode_mma.cu)
+// Anchor-memory decode commit of one request row, for the commit kernel
+// (memory.cu); the memory step's commit warps (gqa_decode_mma.cu) rank by
+// the same order (`cand_before`)
 // (runtime/model/independent_memory.py:190 `commit_decode`,
 // modeling_yanchor.py:186-216 `_commit`, :229-251 `select_topk`).
 //
 // Push (key, value, score) of every group into pending slot `count`; when the
 // chunk fills, merge the CAP bank slots and the `chunk` pending slots of each
 // group into the new top-CAP bank.  Groups are independent: commit_group does
-// one, so the read kernel's tail commits each group in its own CTA.  Order:
+// one.  Order:
 // score descending with NaN first (NaNs tie with each other, as in torch's
 // descending sort), then position ascending (invalid last), then candidate
 // index — the stable double argsort of select_topk.  It is a strict total

@@ -267,7 +267,7 @@ int launch_read_t(const MemReadArgs &a) {
 
 // ---------------------------------------------------------------------------
 // Decode commit: one CTA per request row (the row's work is
-// memcommit::commit_row, shared with the read kernel's commit tail).
+// memcommit::commit_row; the memory step's commit warps merge by the same order).
 // ---------------------------------------------------------------------------
 constexpr int kCommitThreads = 256;
 constexpr int kMaxCand = memcommit::kMaxCand;
