@@ -49,11 +49,13 @@ def test_attention_bf16_yanchor_shape(yb, W):
     assert np.abs(host(out) - ref).max() <= 2e-2
 
 
-def test_ring_update_wraps_and_feeds_attention(yb):
+@pytest.mark.parametrize('B,KVH,D', [(3, 2, 64), (128, 4, 256)])
+def test_ring_update_wraps_and_feeds_attention(yb, B, KVH, D):
     """Nine writes into a 4-wide ring (two wrap-arounds) with inactive rows,
-    each followed by an attention read, against the oracle."""
-    rng = np.random.default_rng(5)
-    B, QH, KVH, W, D = 3, 8, 2, 4, 64
+    each followed by an attention read, against the oracle: a small ring and
+    an fp32 one of 128 rows x 4 heads x 256 (1 MB per update)."""
+    rng = np.random.default_rng(5 + B)
+    QH, W = 4 * KVH, 4
     rk = np.zeros((B, KVH, W, D), np.float32)
     rv = np.zeros((B, KVH, W, D), np.float32)
     rval = np.zeros((B, W), bool)
