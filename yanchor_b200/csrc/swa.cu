@@ -158,71 +158,100 @@ __global__ void __launch_bounds__(kSwaThreads) swa_partial_kernel(const SwaArgs 
   }
 }
 
-// The combine of one (row, KV head, query head): every slice's factor e^{m_s - M} once per CTA (a
-// slice with nothing valid is skipped), then one output feature per thread, with the slices' partial
-// sums for it loaded eight at a time before they are summed in slice order.
-constexpr int kCombineBatch = 8;
-__host__ __device__ constexpr size_t combine_smem(int slices) { return size_t(2) * slices * sizeof(float); }
+// The combine of one (row, KV head): for each of its HN query heads, every slice's factor
+// e^{m_s - M} once per CTA (a slice with nothing valid is skipped), then one output feature per
+// thread for all HN heads, with the slices' partial sums for it loaded 16 at a time (16 / HN slices
+// of every head) before they are summed in slice order.
+__host__ __device__ constexpr size_t combine_smem(int slices, int R) { return size_t(2) * R * slices * sizeof(float); }
 
-template <typename T>
-__global__ void swa_combine_kernel(const SwaArgs a, const float *part, int R, int slices) {
-  extern __shared__ float comb[];   // [slices] factor (-1: skip), [slices] exp-sum
-  __shared__ float wmax[8];
-  __shared__ float s_den;
+template <typename T, int HN>
+__global__ void swa_combine_kernel(const SwaArgs a, const float *part, int slices) {
+  extern __shared__ float comb[];   // per head: [slices] factor (-1: skip), then per head: [slices] exp-sum
+  __shared__ float s_den[HN];
   const int64_t bh = blockIdx.x, b = bh / a.KVH, kvh = bh % a.KVH;
-  const int r = blockIdx.y;
-  const int D = int(a.D), tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5;
+  const int D = int(a.D), tid = threadIdx.x, nt = blockDim.x;
   pdl_wait();   // the slices are written
   pdl_release();
-  const int64_t stride = int64_t(R) * (D + 2);
-  const float *pb = part + bh * slices * stride + r * (D + 2);
-  float *fac = comb, *lsum = comb + slices;
-  float M = -INFINITY;
-  for (int s = tid; s < slices; s += nt) {
-    const float m = pb[s * stride + D];
-    fac[s] = m;
-    lsum[s] = pb[s * stride + D + 1];
-    M = fmaxf(M, m);
+  const int64_t stride = int64_t(HN) * (D + 2);
+  const float *pb = part + bh * slices * stride;
+  float *fac = comb, *lsum = comb + HN * slices;
+  for (int i = tid; i < HN * slices; i += nt) {
+    const int hr = i / slices, s = i - hr * slices;
+    fac[i] = pb[s * stride + hr * (D + 2) + D];
+    lsum[i] = pb[s * stride + hr * (D + 2) + D + 1];
   }
-  M = warp_max(M);
-  if (lane == 0) wmax[warp] = M;
   __syncthreads();
-  M = wmax[0];
-  for (int w = 1; w < (nt + 31) / 32; ++w) M = fmaxf(M, wmax[w]);
-  for (int s = tid; s < slices; s += nt) fac[s] = (M == -INFINITY || fac[s] == -INFINITY) ? -1.f : __expf(fac[s] - M);
-  __syncthreads();
-  if (tid == 0) {
+  if (tid < HN) {   // this head's max over the slices, its factors, and its denominator in slice order
+    float *fh = fac + tid * slices;
+    const float *lh = lsum + tid * slices;
+    float M = -INFINITY;
+    for (int s = 0; s < slices; ++s) M = fmaxf(M, fh[s]);
     float den = 0.f;
-    for (int s = 0; s < slices; ++s)
-      if (fac[s] >= 0.f) den = fmaf(lsum[s], fac[s], den);
-    s_den = den;
+    for (int s = 0; s < slices; ++s) {
+      const float f = (M == -INFINITY || fh[s] == -INFINITY) ? -1.f : __expf(fh[s] - M);
+      fh[s] = f;
+      if (f >= 0.f) den = fmaf(lh[s], f, den);
+    }
+    s_den[tid] = den;
   }
   __syncthreads();
-  const float den = s_den;
-  T *o = static_cast<T *>(a.out) + (b * a.QH + kvh * R + r) * D;
   for (int d = tid; d < D; d += nt) {
-    float num = 0.f;
-    for (int s0 = 0; s0 < slices; s0 += kCombineBatch) {
-      float x[kCombineBatch];
+    float num[HN];
 #pragma unroll
-      for (int j = 0; j < kCombineBatch; ++j) x[j] = s0 + j < slices ? pb[(s0 + j) * stride + d] : 0.f;
+    for (int hr = 0; hr < HN; ++hr) num[hr] = 0.f;
+    constexpr int BATCH = HN >= 8 ? 2 : 16 / HN;   // 16 loads in flight per thread
+    for (int s0 = 0; s0 < slices; s0 += BATCH) {
+      float x[HN][BATCH];
 #pragma unroll
-      for (int j = 0; j < kCombineBatch; ++j)
-        if (s0 + j < slices && fac[s0 + j] >= 0.f) num = fmaf(x[j], fac[s0 + j], num);
+      for (int hr = 0; hr < HN; ++hr)
+#pragma unroll
+        for (int j = 0; j < BATCH; ++j)
+          x[hr][j] = s0 + j < slices ? pb[(s0 + j) * stride + hr * (D + 2) + d] : 0.f;
+#pragma unroll
+      for (int hr = 0; hr < HN; ++hr)
+#pragma unroll
+        for (int j = 0; j < BATCH; ++j)
+          if (s0 + j < slices && fac[hr * slices + s0 + j] >= 0.f)
+            num[hr] = fmaf(x[hr][j], fac[hr * slices + s0 + j], num[hr]);
     }
-    o[d] = from_f<T>(den > 0.f ? num / den : 0.f);
+#pragma unroll
+    for (int hr = 0; hr < HN; ++hr) {
+      const float den = s_den[hr];
+      static_cast<T *>(a.out)[(b * a.QH + kvh * HN + hr) * D + d] = from_f<T>(den > 0.f ? num[hr] / den : 0.f);
+    }
   }
 }
 
-// the combine's dynamic shared memory beyond the default 48 KB (slices > 6144) needs the attribute
-template <typename T>
-int combine_prepare(int slices) {
-  const size_t smem = combine_smem(slices);
-  if (smem <= 48 * 1024) return YB_OK;
+// the combine of every (row, KV head), one CTA each; its dynamic shared memory beyond the default
+// 48 KB (R x slices > 6144) needs the attribute
+template <typename T, int HN>
+int combine_launch_hn(const SwaArgs &a, const float *part, int slices, bool pdl) {
+  const size_t smem = combine_smem(slices, HN);
+  auto k = swa_combine_kernel<T, HN>;
   if (smem > 227 * 1024) return set_error(YB_ERR_UNSUPPORTED, "swa combine: %d slices exceed shared memory", slices);
-  const cudaError_t e = cudaFuncSetAttribute(swa_combine_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             int(smem));
-  return e == cudaSuccess ? YB_OK : set_error(YB_ERR_CUDA, "swa combine: smem attribute: %s", cudaGetErrorString(e));
+  if (smem > 48 * 1024) {
+    const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "swa combine: smem attribute: %s", cudaGetErrorString(e));
+  }
+  const dim3 grid(unsigned(a.B * a.KVH)), block(unsigned(a.D < 256 ? a.D : 256));
+  if (pdl) {
+    const cudaError_t e = launch_pdl(k, grid, block, smem, a.stream, a, part, slices);
+    if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "swa_combine_kernel: %s", cudaGetErrorString(e));
+  } else {
+    k<<<grid, block, smem, a.stream>>>(a, part, slices);
+  }
+  return check_launch("swa_combine_kernel");
+}
+
+template <typename T>
+int combine_launch(const SwaArgs &a, const float *part, int R, int slices, bool pdl) {
+  switch (R) {
+    case 1: return combine_launch_hn<T, 1>(a, part, slices, pdl);
+    case 2: return combine_launch_hn<T, 2>(a, part, slices, pdl);
+    case 4: return combine_launch_hn<T, 4>(a, part, slices, pdl);
+    case 8: return combine_launch_hn<T, 8>(a, part, slices, pdl);
+  }
+  return set_error(YB_ERR_UNSUPPORTED, "swa combine: QH / KVH = %d not built (1/2/4/8)", R);
 }
 
 template <typename T, int R, int D>
@@ -234,11 +263,7 @@ int attn_launch(const SwaArgs &a, float *part, int slices) {
   k<<<dim3(unsigned(a.B * a.KVH), unsigned(slices)), kSwaThreads, smem, a.stream>>>(a, part);
   int rc = check_launch("swa_partial_kernel");
   if (rc) return rc;
-  rc = combine_prepare<T>(slices);
-  if (rc) return rc;
-  swa_combine_kernel<T><<<dim3(unsigned(a.B * a.KVH), unsigned(R)), D < 256 ? D : 256, combine_smem(slices),
-                          a.stream>>>(a, part, R, slices);
-  return check_launch("swa_combine_kernel");
+  return combine_launch<T>(a, part, R, slices, false);
 }
 
 template <typename T, int R>
@@ -318,15 +343,8 @@ int launch_swa_decode_attention(const SwaArgs &a, void *workspace) {
     int rc = launch_gqa_decode_mma(g);
     if (rc) return rc;
     const int R = int(a.QH / a.KVH);
-    const dim3 cgrid(unsigned(a.B * a.KVH), unsigned(R)), cblock(unsigned(a.D < 256 ? a.D : 256));
-    rc = a.dtype == YB_BF16 ? combine_prepare<__nv_bfloat16>(slices) : combine_prepare<__half>(slices);
-    if (rc) return rc;
-    const size_t csm = combine_smem(slices);
-    const cudaError_t e = a.dtype == YB_BF16
-                              ? launch_pdl(swa_combine_kernel<__nv_bfloat16>, cgrid, cblock, csm, a.stream, a, part, R, slices)
-                              : launch_pdl(swa_combine_kernel<__half>, cgrid, cblock, csm, a.stream, a, part, R, slices);
-    if (e != cudaSuccess) return set_error(YB_ERR_CUDA, "swa_combine_kernel: %s", cudaGetErrorString(e));
-    return check_launch("swa_combine_kernel");
+    return a.dtype == YB_BF16 ? combine_launch<__nv_bfloat16>(a, part, R, slices, true)
+                              : combine_launch<__half>(a, part, R, slices, true);
   }
   switch (a.dtype) {
     case YB_F32: return attn_t<float>(a, part, slices);
